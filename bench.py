@@ -1,0 +1,459 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 Q8_0 linear (BASELINE.json metric).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl madi|reference]
+
+Workload (N=1 is BASELINE config 1 at B=16, the largest single-GPU config):
+  step = encoder FFN pair over B=16 chunks of 30 s audio (M = 24000 frames):
+         H = GELU(X @ deq(fc1)^T + b1)   fc1 Q8 [5120 x 1280]
+         Y = H @ deq(fc2)^T + b2 + X     fc2 Q8 [1280 x 5120]
+  value = whole-job encoder Q8 GEMM TFLOP/s (2*M*N*K per GEMM, all ranks),
+          inputs resident in HBM; working set (X 61 MB + H 246 MB + Y 61 MB)
+          is larger than the 126 MB L2.
+  decode leg (M=8 token slots): one decoder token step's
+          Q8 projections (4 layers x {qkv, o, cq, co, fc1, fc2}) + vocab head,
+          replayed as a CUDA graph over two distinct weight sets (2 x 168 MB,
+          alternating, so every replay streams from HBM); reported in GB/s.
+          At N>1 the vocab head is column-split and its logits all-gathered
+          over NCCL.
+  e2e   = the same encoder metric through the public API (madi_b200.q8.linear)
+          with pinned HOST buffers: per step H2D of X and D2H of Y inside the
+          timed region.
+Multi-GPU: one process per GPU (torchrun), each rank runs its own B chunks
+(weak scaling, no data-path collective on the encoder); times are the max
+over ranks.  --impl reference times the reference's CPU computation of the
+same op (the C restatement in oracle/, all host threads) on a row sample.
+"""
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "encoder Q8 GEMM TFLOP/s + decode GEMV GB/s; 30s-chunks/sec at 1/2/4/8 B200"
+SEQ, D, F, V = 1500, 1280, 5120, 51866
+CLOCK_FIELDS = ["pci.bus_id", "clocks.sm", "clocks.max.sm", "power.draw", "clocks_event_reasons.hw_slowdown",
+                "clocks_event_reasons.hw_thermal_slowdown", "clocks_event_reasons.sw_thermal_slowdown",
+                "clocks_event_reasons.sw_power_cap"]
+REASONS = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["madi", "reference"], default="madi")
+    ap.add_argument("--batch", type=int, default=16, help="30 s chunks per GPU per step (config 1: 1, 4, 16)")
+    ap.add_argument("--decode-m", type=int, default=8)
+    ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    return ap.parse_args()
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            j = json.load(f)
+        return dict(hbm=j["hbm_gbs"], bf16=j["bf16_tflops"], bf16_sus=j["bf16_tflops_sustained"], src="measured")
+    return dict(hbm=6650.0, bf16=1590.0, bf16_sus=1400.0, src="fallback")
+
+
+def load_traffic(name):
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f).get(name)
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi samples every 200 ms while the timed region runs."""
+
+    def __init__(self, bus_id):
+        self.bus_id = (bus_id or "").lower()
+        self.rows, self.proc, self.thr = [], None, None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "--query-gpu=" + ",".join(CLOCK_FIELDS),
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            return self
+        self.thr = threading.Thread(target=self._read, daemon=True)
+        self.thr.start()
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) == len(CLOCK_FIELDS):
+                self.rows.append(parts)
+
+    def stop(self):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        if self.thr:
+            self.thr.join(timeout=5)
+        mine = [r for r in self.rows if not self.bus_id or r[0].lower().endswith(self.bus_id[-12:])] or self.rows
+        if not mine:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        sm = [float(r[1]) for r in mine if r[1].replace(".", "").isdigit()]
+        smax = [float(r[2]) for r in mine if r[2].replace(".", "").isdigit()]
+        reasons = sorted({REASONS[i] for r in mine for i in range(4) if r[4 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": reasons, "samples": len(mine)}
+
+
+# ----------------------------------------------------------------------------- distributed plumbing
+def dist_init():
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(world, v):
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ----------------------------------------------------------------------------- CPU (reference) timing
+def cpu_ffn_sample(rows, seconds, nthreads=None):
+    """The reference's CPU computation of the FFN pair (f32 dequant + accumulate,
+    oracle/q8_oracle.c madi_orc_linear_f32_baseline) on `rows` frames, repeated
+    for about `seconds`.  Returns (TFLOP/s, threads, passes)."""
+    import numpy as np
+    from madi_b200 import synth
+    from oracle import oracle
+    oracle.build()
+    w = synth.ffn_weights(0)
+    x = synth.activations(rows, D, 1)
+    nt = nthreads or oracle.max_threads()
+    flops = 2.0 * rows * F * D * 2
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        h = oracle.linear_f32_baseline(x, w["fc1_qs"], w["fc1_scales"], w["fc1_bias"], oracle.EPI_BIAS_GELU,
+                                       nthreads=nt)
+        oracle.linear_f32_baseline(h, w["fc2_qs"], w["fc2_scales"], w["fc2_bias"], oracle.EPI_BIAS_RES,
+                                   residual=x, nthreads=nt)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    return flops * n / el / 1e12, nt, n
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    from oracle import oracle
+    oracle.build()
+    rows = 96                      # bounded sample of the 24000-frame step
+    per = []
+    for i in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        tf, nt, _ = cpu_ffn_sample(rows, 0.0)
+        if i >= args.warmup:
+            per.append(time.perf_counter() - t0)
+    flops = 2.0 * rows * F * D * 2
+    value = flops * len(per) / sum(per) / 1e12
+    ms = 1e3 * sum(per) / len(per)
+    sample = f"FFN pair (fc1+GELU, fc2+residual) on {rows} of {args.batch * SEQ} frames per step"
+    line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "impl": "reference", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"config1 encoder FFN pair, B={args.batch} chunks (M={args.batch * SEQ})",
+                       "cpu_sample_rows": rows},
+            "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": oracle.max_threads(), "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- GPU arm
+def main_madi(args, world, rank, local):
+    import numpy as np
+    import torch
+
+    import madi_b200
+    from madi_b200 import q8, synth
+
+    torch.cuda.set_device(local)
+    madi_b200.init(local)
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.Stream(device=dev)
+    peaks = load_peaks()
+
+    def t(a):
+        return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+    # ---------------- encoder FFN pair (config 1)
+    M = args.batch * SEQ
+    w = synth.ffn_weights(0)
+    W1 = q8.Q8Weight(t(w["fc1_qs"]), t(w["fc1_scales"]))
+    W2 = q8.Q8Weight(t(w["fc2_qs"]), t(w["fc2_scales"]))
+    b1, b2 = t(w["fc1_bias"]), t(w["fc2_bias"])
+    X = t(synth.activations(M, D, 1000 + rank))
+    H = torch.empty((M, F), dtype=torch.float16, device=dev)
+    Y = torch.empty((M, D), dtype=torch.float16, device=dev)
+    torch.cuda.synchronize()
+
+    def step():
+        q8.linear(W1, X, bias=b1, epi=q8.EPI_BIAS_GELU, out=H, stream=stream)
+        q8.linear(W2, H, bias=b2, epi=q8.EPI_BIAS_RES, residual=X, out=Y, stream=stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    K = args.steps
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(2 * K + 1)]
+    bus = None
+    try:
+        bus = torch.cuda.get_device_properties(dev).pci_bus_id
+    except Exception:
+        pass
+    sampler = ClockSampler(bus).start()
+    time.sleep(0.3)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        evs[0].record(stream)
+        for i in range(K):
+            q8.linear(W1, X, bias=b1, epi=q8.EPI_BIAS_GELU, out=H, stream=stream)
+            evs[2 * i + 1].record(stream)
+            q8.linear(W2, H, bias=b2, epi=q8.EPI_BIAS_RES, residual=X, out=Y, stream=stream)
+            evs[2 * i + 2].record(stream)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    barrier(world)
+    total_ms = evs[0].elapsed_time(evs[2 * K])
+    launches = [evs[j].elapsed_time(evs[j + 1]) for j in range(2 * K)]
+    ms_step = max_over_ranks(world, total_ms / K)
+    gemm_flops = 2.0 * M * F * D                  # per launch (fc1 and fc2 alike)
+    value = 2 * gemm_flops * world / (ms_step / 1e3) / 1e12
+    avg_launch_ms = sum(launches) / len(launches)
+    achieved = gemm_flops / (avg_launch_ms / 1e3) / 1e12
+    peak = peaks["bf16_sus"] if total_ms > 1000 else peaks["bf16"]
+    roofline = {"bound": "tensor", "kernel": "q8_gemm_tc_kernel", "achieved": achieved, "peak": peak,
+                "peak_kind": ("sustained" if total_ms > 1000 else "burst") + " bf16, " + peaks["src"],
+                "unit": "TFLOP/s", "frac": achieved / peak, "traffic": load_traffic("q8_gemm_tc_ffn_b16"),
+                "flops_per_launch": gemm_flops,
+                "fc1_ms": statistics.mean(launches[0::2]), "fc2_ms": statistics.mean(launches[1::2])}
+    chunks_per_s = args.batch * world / (ms_step / 1e3)
+
+    # ---------------- e2e through the public API with host buffers
+    e2e = None
+    if not args.no_e2e:
+        Xh = torch.empty((M, D), dtype=torch.float16, pin_memory=True)
+        Xh.copy_(X.cpu())
+        Yh = torch.empty((M, D), dtype=torch.float16, pin_memory=True)
+        Ke = max(3, min(K, 20))
+        for _ in range(2):
+            X.copy_(Xh, non_blocking=True)
+        torch.cuda.synchronize()
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(Ke):
+                X.copy_(Xh, non_blocking=True)
+                q8.linear(W1, X, bias=b1, epi=q8.EPI_BIAS_GELU, out=H, stream=stream)
+                q8.linear(W2, H, bias=b2, epi=q8.EPI_BIAS_RES, residual=X, out=Y, stream=stream)
+                Yh.copy_(Y, non_blocking=True)
+            e1.record(stream)
+        torch.cuda.synchronize()
+        ms_e2e = max_over_ranks(world, e0.elapsed_time(e1) / Ke)
+        e2e = {"value": 2 * gemm_flops * world / (ms_e2e / 1e3) / 1e12, "unit": "TFLOP/s",
+               "h2d_bytes_per_step": M * D * 2, "d2h_bytes_per_step": M * D * 2, "ms_per_step": ms_e2e}
+        del Xh, Yh
+
+    del H
+    torch.cuda.empty_cache()
+
+    # ---------------- decode leg (config 2)
+    decode = None
+    if not args.no_decode:
+        decode = decode_leg(args, world, rank, dev, stream, peaks)
+
+    # ---------------- CPU baseline (rank 0, N=1 only)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rows = 256
+        tf, nt, n = cpu_ffn_sample(rows, args.cpu_seconds)
+        cpu = {"value": tf, "unit": "TFLOP/s", "cores": nt, "kind": "port",
+               "sample": f"FFN pair on {rows} of {M} frames, {n} passes (~{args.cpu_seconds:.0f} s), "
+                         f"f32 dequant+accumulate as test_q8gemm.zig:59-69"}
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": K,
+                "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+                "config": {"workload": f"config1 encoder FFN pair (fc1 Q8 5120x1280 +bias+GELU, fc2 Q8 1280x5120 "
+                                       f"+bias+residual), B={args.batch} chunks/GPU, M={M}",
+                           "parallelism": f"dp{world} (independent chunks, replicated weights)",
+                           "l2": "inputs larger than L2 (X 61 MB + H 246 MB + Y 61 MB per step)",
+                           "weights": "random-init Q8_0 (block-32 int8 + f16 scales)"},
+                "chunks_per_s": chunks_per_s,
+                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "decode": decode,
+                "clocks": clocks, "gpu_launches": 2 * K}
+        print(json.dumps(line), flush=True)
+
+
+def decode_leg(args, world, rank, dev, stream, peaks):
+    """One decoder token step's Q8 projections for M token slots, CUDA-graph replayed."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from madi_b200 import q8, synth
+
+    Md = args.decode_m
+    shard = (V + world - 1) // world
+    h0 = rank * shard
+    h1 = min(V, h0 + shard)
+
+    def t(a):
+        return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+    def make_set(seed):
+        layers = []
+        for l in range(4):
+            L = {}
+            for j, (name, n, k) in enumerate(synth.decoder_shapes()):
+                qs, sc = synth.q8_weight(n, k, seed * 1000 + l * 10 + j)
+                L[name] = (q8.Q8Weight(t(qs), t(sc)), t(synth.bias(n, seed * 1000 + l * 10 + j)))
+            layers.append(L)
+        hq, hs = synth.q8_weight(V, D, seed * 1000 + 999)
+        head = q8.Q8Weight(t(hq[h0:h1]), t(hs[h0:h1]))
+        return layers, head
+
+    sets = [make_set(s) for s in (1, 2)]
+    x = t(synth.activations(Md, D, 7, np.float32))
+    big = torch.empty((Md, F), dtype=torch.float32, device=dev)
+    outs = {n: torch.empty((Md, nn), dtype=torch.float32, device=dev) for n, nn, _ in synth.decoder_shapes()}
+    resid = torch.zeros((Md, D), dtype=torch.float32, device=dev)
+    logits = torch.empty((Md, h1 - h0), dtype=torch.float32, device=dev)
+
+    def token_step(layers, head):
+        for L in layers:
+            q8.linear(L["qkv"][0], x, out=outs["qkv"], stream=stream)
+            q8.linear(L["o"][0], x, out=outs["o"], stream=stream)
+            q8.linear(L["cq"][0], x, bias=L["cq"][1], out=outs["cq"], stream=stream)
+            q8.linear(L["co"][0], x, out=outs["co"], stream=stream)
+            q8.linear(L["fc1"][0], x, bias=L["fc1"][1], epi=q8.EPI_BIAS_GELU, out=big, stream=stream)
+            q8.linear(L["fc2"][0], big, bias=L["fc2"][1], epi=q8.EPI_BIAS_RES, residual=resid, out=resid,
+                      stream=stream)
+        q8.linear(head, x, out=logits, stream=stream)
+
+    bytes_step = 0
+    for name, n, k in synth.decoder_shapes():
+        b = n * k + n * k // 16 + Md * k * 4 + Md * n * 4
+        if name in ("cq", "fc1", "fc2"):
+            b += n * 4
+        if name == "fc2":
+            b += Md * n * 4
+        bytes_step += 4 * b
+    hn = h1 - h0
+    bytes_step += hn * D + hn * D // 16 + Md * D * 4 + Md * hn * 4
+
+    graphs = []
+    with torch.cuda.stream(stream):
+        for s in sets:
+            token_step(*s)           # eager warm-up (sets kernel attributes before capture)
+        torch.cuda.synchronize()
+        for s in sets:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream, capture_error_mode="thread_local"):
+                token_step(*s)
+            graphs.append(g)
+    gathered = torch.empty((world, Md, shard), dtype=torch.float32, device=dev) if world > 1 else None
+    K = max(10, args.steps)
+    for i in range(4):
+        graphs[i % 2].replay()
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for i in range(K):
+            graphs[i % 2].replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / K
+    ag_ms = None
+    if world > 1:
+        # column-split head: gather every rank's logit shard (NCCL over NVLink)
+        pad = torch.zeros((Md, shard), dtype=torch.float32, device=dev)
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record()
+        for i in range(K):
+            graphs[i % 2].replay()
+            pad[:, :hn].copy_(logits)
+            dist.all_gather_into_tensor(gathered, pad)
+        a1.record()
+        torch.cuda.synchronize()
+        ag_ms = max_over_ranks(world, a0.elapsed_time(a1) / K)
+    ms_max = max_over_ranks(world, ms)
+    gbs = bytes_step / (ms / 1e3) / 1e9
+    return {"value": bytes_step * world / (ms_max / 1e3) / 1e9, "unit": "GB/s", "m_tokens": Md,
+            "bytes_per_step_per_gpu": bytes_step, "ms_per_token_step": ms_max, "gpu_launches_per_step": 25,
+            "head_rows_per_gpu": hn, "step_with_logit_allgather_ms": ag_ms,
+            "roofline": {"bound": "hbm", "kernel": "q8_gemv_kernel (25 launches/step, CUDA graph)",
+                         "achieved": gbs, "peak": peaks["hbm"], "unit": "GB/s", "frac": gbs / peaks["hbm"],
+                         "traffic": load_traffic("q8_gemv_decode_step")},
+            "l2": "two 168 MB weight sets replayed alternately (> 126 MB L2)"}
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        run_reference(args, world, rank)
+        return 0
+    world, rank, local = dist_init()
+    try:
+        main_madi(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

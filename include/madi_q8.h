@@ -1,0 +1,182 @@
+/*
+ * madi_q8.h -- C ABI of the B200 (sm_100a) Q8_0 linear layer.
+ *
+ * Drop-in for the Q8 path of companyjupiter/madi's engine operator API
+ * (engine/metal/metal_backend.h + metal_backend.zig).  The reference's Zig host
+ * binds that header with `extern fn` declarations (metal_backend.zig:12-32); a
+ * Zig caller binds this one the same way or through @cImport.  Each entry point
+ * below names the reference interface it replaces.
+ *
+ * Conventions (same as the reference):
+ *   - Q8_0 weight: qs int8 [N][K] row-major (K contiguous) + scales f16 [N][K/32];
+ *     deq(n,k) = qs[n*K+k] * scales[n*(K/32) + k/32]   (q8_gemm.metal:2-3).
+ *     K must be a multiple of 32.
+ *   - Every pointer is a caller-owned DEVICE pointer unless stated; the library
+ *     never frees caller buffers (metal_backend.m:336-361 ownership rule).
+ *   - Every int-returning entry returns MADI_OK (0) on success and a negative
+ *     MADI_E* code on failure, so the reference's `!= 0 -> error` checks
+ *     (metal_backend.zig:34-41) keep working.  Argument checks happen before
+ *     any launch.
+ *   - Not thread-safe per process except madi_alloc/madi_free (the reference's
+ *     g_alloc_mutex rule, metal_backend.m:99).  One device per process.
+ */
+#ifndef MADI_Q8_H
+#define MADI_Q8_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------- */
+#define MADI_OK             0
+#define MADI_ERR           -1   /* generic failure (the reference's -1) */
+#define MADI_EINVAL        -2   /* bad argument: shape, alignment, null, dtype */
+#define MADI_ENOTFOUND     -3   /* unknown kernel name */
+#define MADI_ECUDA         -4   /* CUDA runtime error (see madi_last_error) */
+#define MADI_ETIMEDOUT     -5   /* madi_sync timed out; work still pending */
+#define MADI_ENOINIT       -6   /* madi_init not called / failed */
+#define MADI_EDEVICE       -7   /* a kernel's bounded wait expired (device error flag) */
+#define MADI_EUNSUPPORTED  -8   /* device is not sm_100 / feature unavailable */
+#define MADI_EBUSY         -9   /* command buffer already open / not open */
+
+/* ---- element types ------------------------------------------------------ */
+#define MADI_F32  0
+#define MADI_F16  1
+
+/* ---- epilogues (bias / GELU / residual flags of the reference kernels) ---- */
+#define MADI_EPI_NONE       0   /* y = acc                       gemv_q8, m4_gemm_nn, logit_gemv_q8 */
+#define MADI_EPI_BIAS       1   /* y = acc + b                   gemv_q8_bias, m4_gemm_bias */
+#define MADI_EPI_BIAS_GELU  2   /* y = gelu_erf(acc + b)         gemv_q8_bias_gelu, m4_gemm_bias_gelu */
+#define MADI_EPI_BIAS_RES   3   /* y = r + acc + b               gemv_q8_bias_res (r may alias y),
+                                   encoder residual of bias_res_ln_f16 (encoder_ops.metal:343) */
+
+/* Q8_0 weight handle.  Replaces `Q8 = struct { qs: [*]i8, scales: [*]f16 }`
+ * (encoder.zig:20-21, decoder.zig:22); carries its shape. */
+typedef struct madi_q8w {
+    const int8_t   *qs;       /* [n][k] */
+    const uint16_t *scales;   /* [n][k/32] f16 bit patterns */
+    int32_t n;                /* out features (rows) */
+    int32_t k;                /* in features, multiple of 32 */
+} madi_q8w;
+
+/* ======================= lifecycle / memory =============================== */
+
+/* mtl_init (metal_backend.h:15): bind `device`, create the stream, check sm_100. */
+int   madi_init(int device);
+/* mtl_cleanup (metal_backend.h:16): free library-owned state (never user buffers). */
+void  madi_cleanup(void);
+/* mtl_alloc / mtl_free (metal_backend.h:21-22): device memory, registered so
+ * madi_dispatch can bind base or interior pointers.  256-byte aligned. */
+void *madi_alloc(size_t size);
+void  madi_free(void *ptr);
+/* mtl_upload / mtl_download (metal_backend.h:30-31): host <-> device copies
+ * (synchronous with respect to the library stream). */
+int   madi_upload(void *dst_device, const void *src_host, size_t size);
+int   madi_download(void *dst_host, const void *src_device, size_t size);
+
+/* ======================= kernels by name ================================== */
+
+/* mtl_get_function (metal_backend.h:47).  Accepted names and argument orders
+ * are the reference kernels' buffer orders:
+ *   gemv_q8            (out f32, qs, scales, x f32, N u32, K u32)           graph_helpers.metal:390
+ *   gemv_q8_bias       (out, qs, scales, x, bias f32, N, K)                 graph_helpers.metal:424
+ *   gemv_q8_bias_gelu  (out, qs, scales, x, bias, N, K)                     graph_helpers.metal:475
+ *   gemv_q8_bias_res   (out, qs, scales, x, bias, N, K)   out += acc+bias   graph_helpers.metal:498
+ *   gemv_q8_qkv        (q_out, qs, scales, x, qb, vb, kc, vc, pos_ptr u32*, D u32)  graph_helpers.metal:527
+ *   logit_gemv_q8      (logits, qs, scales, x, vocab u32, dim u32)          graph_helpers.metal:320
+ *   dequant_q8_f16     (out f16 [K][N], qs, scales, N, K)                   q8_gemm.metal:12
+ *   mul_mm_q8          (C f16, A f16, qs, scales, M, N, K)                  q8_gemm.metal:29
+ *   m4_gemm_q8tg       (A f16, Wq, scales, C f16, bias f32, M, N, K, act_gelu u32)  m4_gemm.metal:196
+ *   m4_gemm_q8_bias_gelu (same arguments as m4_gemm_q8tg)                   m4_gemm.metal:131
+ * On success *out_id holds a handle for madi_dispatch. */
+int   madi_get_function(const char *name, int *out_id);
+
+/* mtl_dispatch (metal_backend.h:53-56): `args[i]` points at the i-th argument
+ * value and `arg_sizes[i]` is its size -- the cuLaunchKernel kernelParams
+ * convention the reference uses.  Pointer arguments must be device pointers
+ * (madi_alloc'd, base or interior, or any other device allocation).  The
+ * grid/block values are accepted for compatibility and ignored: each B200
+ * kernel picks its own launch shape.  Inside begin/commit the launch is
+ * recorded into the open command buffer, otherwise it is enqueued at once. */
+int   madi_dispatch(int func_id,
+                    uint32_t grid_x, uint32_t grid_y, uint32_t grid_z,
+                    uint32_t block_x, uint32_t block_y, uint32_t block_z,
+                    const void **args, const size_t *arg_sizes, int n_args);
+
+/* ======================= command buffers / sync =========================== */
+
+/* mtl_begin_command_buffer / mtl_commit_command_buffer (metal_backend.h:65-68):
+ * begin opens a CUDA stream capture; commit closes it into a CUDA graph and
+ * launches it (the graph executable is reused when the recorded work has the
+ * same shape).  Returns MADI_EBUSY on mismatched begin/commit. */
+int   madi_begin_command_buffer(void);
+int   madi_commit_command_buffer(void);
+/* mtl_flush (metal_backend.h:59): no-op (launches are already enqueued). */
+void  madi_flush(void);
+/* mtl_sync (metal_backend.h:62), with a bound: waits up to timeout_ms (<0 =
+ * no bound) for all enqueued work; MADI_ETIMEDOUT instead of hanging,
+ * MADI_EDEVICE if a kernel reported an expired wait, MADI_ECUDA on a CUDA error. */
+int   madi_sync(int timeout_ms);
+
+/* Stream binding (no reference counterpart: the reference owns one queue).
+ * stream = a cudaStream_t; NULL restores the library stream. */
+int   madi_set_stream(void *cuda_stream);
+void *madi_get_stream(void);
+
+/* ======================= diagnostics ====================================== */
+/* Last error message of this thread (never NULL). */
+const char *madi_last_error(void);
+/* mtl_set_verbose (metal_backend.h:91). */
+void  madi_set_verbose(int v);
+/* mtl_dump_profile (metal_backend.h:81): with MADI_PROFILE=1 each dispatch is
+ * timed with CUDA events; this writes an nsys cuda_gpu_kern_sum-style table
+ * (out_path NULL -> stdout). */
+void  madi_dump_profile(const char *out_path);
+/* Number of streaming multiprocessors of the bound device (0 before init). */
+int   madi_num_sms(void);
+
+/* ======================= typed Q8 API ===================================== */
+
+/* Y[m][n] = epi( sum_k X[m][k] * deq(n,k) ).  Replaces the reference's
+ * per-projection pairs (kDeq + m4_gemm_bias / _bias_gelu / _nn, encoder.zig:262-304;
+ * the gemv_q8* family, decoder.zig:155-200; the batched f16 projection,
+ * decoder.zig:337-341).  One call, no dequant scratch:
+ *   m > 8 : tcgen05 tensor-core GEMM, X f16, Y f16, residual f16;
+ *           f16 dequantised weights, f32 accumulation.
+ *   m <= 8: bandwidth-bound skinny GEMM, X f32 or f16, Y f32 or f16,
+ *           residual with Y's type and may alias Y; f32 semantics
+ *           (exact int8 weights, per-block f32 scale).
+ * bias: f32 or f16 per bias_dtype, required unless epi == MADI_EPI_NONE.
+ * x, y, residual: row-major, rows of k (x) / n (y, residual) elements, 16-byte
+ * aligned base pointers.  stream: cudaStream_t or NULL (library stream). */
+int madi_q8_linear(const madi_q8w *w, const void *x, int x_dtype, int m,
+                   const void *bias, int bias_dtype, int epi,
+                   const void *residual, void *y, int y_dtype, void *stream);
+
+/* Decoder self-attention QKV projection with the KV-cache store fused
+ * (gemv_q8_qkv, graph_helpers.metal:527-567) for m <= 8 token slots.
+ * w: stacked [3D][D]; x f32 [m][D].  For slot s: q_out[s][0..D) = q + qb;
+ * kc[s*cache_stride + pos[s]*D + j] = k_j;  vc[...] = v_j + vb[j].
+ * pos: device u32 [m] (read on the device, so a graph can replay it);
+ * cache_stride: elements between slots' caches (ignored for m == 1). */
+int madi_q8_qkv(const madi_q8w *w, const float *x, int m,
+                const float *qb, const float *vb, float *q_out,
+                float *kc, float *vc, const uint32_t *pos, int64_t cache_stride,
+                void *stream);
+
+/* dequant_q8_f16 (q8_gemm.metal:12-27): out f16 [K][N] = half(q*s), transposed. */
+int madi_q8_dequant_f16(const madi_q8w *w, uint16_t *out, void *stream);
+
+/* quantInto (transcribe.zig:309-327) on the device: w f16 [rows][dim] ->
+ * qs int8 [rows][dim], scales f16 [rows][dim/32].  Bit-identical to the
+ * reference's quantiser (round half away from zero on w * (1/s_f32)). */
+int madi_q8_quantize_f16(const uint16_t *w, int rows, int dim,
+                         int8_t *qs, uint16_t *scales, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MADI_Q8_H */

@@ -1,0 +1,194 @@
+// common.cuh -- device helpers shared by the sm_100a Q8 kernels.
+//
+//  * exact int8 -> f16 conversion (bias-exponent trick, see q8_to_half2x2)
+//  * Abramowitz & Stegun 7.1.26 GELU, the reference's epilogue formula
+//    (m4_gemm.metal:43-57, graph_helpers.metal:460-473)
+//  * thin inline-PTX wrappers: mbarrier, TMA (cp.async.bulk.tensor), tcgen05
+//  * bounded waits: every spin has a clock budget; on expiry it raises the
+//    CTA's abort flag and the library's device error word instead of hanging.
+#pragma once
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#define MADI_DEV __device__ __forceinline__
+
+namespace madi {
+
+// ~2 s at 1.9 GHz: far above any legitimate wait in these kernels.
+constexpr long long kWaitBudgetCycles = 4000000000LL;
+
+// Device error word codes (written with atomicCAS so the first cause sticks).
+enum : int { kDevErrNone = 0, kDevErrWaitTimeout = 1, kDevErrBadArgs = 2 };
+
+// ------------------------------------------------------------------ numerics
+
+// Four int8 (one 32-bit word, little-endian) -> two half2 holding q exactly:
+// lo = {q0, q1}, hi = {q2, q3}.  Flipping the sign bit turns q into the
+// unsigned byte q+128; placing that byte under the f16 exponent of 1024
+// (0x64xx) gives the half 1024 + q + 128 exactly; subtracting 1152 leaves q.
+MADI_DEV void q8_to_half2x2(uint32_t w, __half2 &lo, __half2 &hi) {
+    const uint32_t u = w ^ 0x80808080u;
+    uint32_t a, b;
+    asm("prmt.b32 %0, %1, %2, 0x4140;" : "=r"(a) : "r"(u), "r"(0x64646464u));
+    asm("prmt.b32 %0, %1, %2, 0x4342;" : "=r"(b) : "r"(u), "r"(0x64646464u));
+    const __half2 bias = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));  // 1152
+    lo = __hsub2(*reinterpret_cast<__half2 *>(&a), bias);
+    hi = __hsub2(*reinterpret_cast<__half2 *>(&b), bias);
+}
+
+MADI_DEV uint32_t h2_as_u32(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
+
+// 0.5 x (1 + erf(x / sqrt 2)), erf from A&S 7.1.26 (|eps| <= 1.5e-7) with
+// exp2(max(-z^2 log2 e, -80)): the reference's GELU formula, restated.
+// The reciprocal and exp2 use the hardware approximations; their error is
+// far below the 2e-3 x RMS output tolerance.
+MADI_DEV float gelu_erf(float xv) {
+    const float z = xv * 0.7071067811865476f;
+    const float az = fabsf(z);
+    const float t = __fdividef(1.0f, fmaf(az, 0.3275911f, 1.0f));
+    float poly = fmaf(1.061405429f, t, -1.453152027f);
+    poly = fmaf(poly, t, 1.421413741f);
+    poly = fmaf(poly, t, -0.284496736f);
+    poly = fmaf(poly, t, 0.254829592f);
+    poly = poly * t;
+    const float ex = exp2f(fmaxf(-az * az * 1.4426950408889634f, -80.0f));
+    const float e = 1.0f - poly * ex;
+    const float erf = z < 0.0f ? -e : e;
+    return 0.5f * xv * (1.0f + erf);
+}
+
+// ------------------------------------------------------------------ shared / mbarrier
+
+MADI_DEV uint32_t smem_u32(const void *p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+
+MADI_DEV void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+MADI_DEV void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+
+MADI_DEV void mbar_arrive(uint64_t *bar) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+MADI_DEV void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(
+                     smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+MADI_DEV bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Waits for `parity` on `bar`.  Gives up (returns false) when the CTA abort
+// flag is raised or the clock budget runs out; in the latter case it raises
+// the abort flag and records kDevErrWaitTimeout in *dev_err.
+MADI_DEV bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int *dev_err) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (true) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (*abort_flag) return false;
+        if (clock64() - t0 > kWaitBudgetCycles) {
+            *abort_flag = 1;
+            if (dev_err) atomicCAS(dev_err, kDevErrNone, kDevErrWaitTimeout);
+            return false;
+        }
+    }
+}
+
+// ------------------------------------------------------------------ TMA
+
+MADI_DEV void tma_prefetch_desc(const CUtensorMap *m) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
+}
+// 2-D tiled TMA load (no multicast) into this CTA's shared memory; completes
+// `bytes` of transaction on `bar`.  c0 = innermost coordinate (elements).
+MADI_DEV void tma_load_2d(void *smem_dst, const CUtensorMap *m, uint64_t *bar, int c0, int c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+            smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(m)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+        : "memory");
+}
+
+// ------------------------------------------------------------------ tcgen05
+
+MADI_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+MADI_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Warp-collective.  Writes the TMEM base address to *dst_smem.
+MADI_DEV void tmem_alloc(uint32_t *dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+                 "r"(ncols)
+                 : "memory");
+}
+MADI_DEV void tmem_relinquish() { asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory"); }
+MADI_DEV void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// D[tmem] (+)= A[tmem] * B[smem]; kind::f16, single CTA.  One thread issues.
+MADI_DEV void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Arrive on `bar` once every tcgen05 op issued so far by this thread completes.
+MADI_DEV void umma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+MADI_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+MADI_DEV void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// 32 lanes x 32 consecutive 32-bit columns (thread = lane, register i = column i).
+MADI_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
+
+MADI_DEV void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+        "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]),
+        "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]),
+        "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+
+// Shared-memory matrix descriptor for a K-major operand stored in the
+// 128-byte swizzle layout that TMA's SWIZZLE_128B writes: rows of 128 bytes,
+// 8-row groups 1024 bytes apart (SBO), LBO unused (1), descriptor version 1.
+MADI_DEV uint64_t smem_desc_sw128(uint32_t smem_addr) {
+    return (uint64_t)((smem_addr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor, kind::f16: A = B = f16, D = f32, both K-major.
+__host__ __device__ constexpr uint32_t idesc_f16_f32(int m, int n) {
+    return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+}  // namespace madi

@@ -1,0 +1,63 @@
+// internal.h -- launcher interfaces between the C-ABI layer (runtime.cu) and
+// the kernel translation units.  Not part of the public ABI.
+#pragma once
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace madi {
+
+enum : int { kEpiNone = 0, kEpiBias = 1, kEpiBiasGelu = 2, kEpiBiasRes = 3 };
+
+// ---------------------------------------------------------------- variant (b)
+struct GemvArgs {
+    const int8_t *qs;        // [N][K]
+    const __half *scales;    // [N][K/32]
+    const void *x;           // [M][K] f32 or f16
+    void *y;                 // [M][N] f32 or f16 (QKV: q_out f32 [M][D])
+    const void *residual;    // [M][N], y's type (EPI_BIAS_RES)
+    const void *bias;        // [N] f32 or f16
+    int N, K, M, ks;
+    int bias_f16;
+    // QKV fusion (gemv_q8_qkv)
+    const float *qb, *vb;
+    float *kc, *vc;
+    const uint32_t *pos;
+    long long cache_stride;
+    int D;
+};
+int gemv_pick_ks(int N, int K, int num_sms);
+size_t gemv_smem_bytes(int M, int K, bool x_f32);
+cudaError_t launch_gemv(const GemvArgs &a, bool x_f32, bool y_f32, int epi, bool qkv, cudaStream_t st, bool pdl);
+
+// ---------------------------------------------------------------- variant (a)
+struct GemmArgs {
+    const __half *x;         // [M][K] f16
+    const int8_t *qs;        // [N][K]
+    const __half *scales;    // [N][K/32]
+    const void *bias;        // [N] f32 or f16
+    const __half *residual;  // [M][N] f16
+    __half *y;               // [M][N] f16
+    int M, N, K;
+    int bias_f16;
+    int *dev_err;            // device error word (bounded-wait expiry)
+};
+// Returns cudaErrorNotSupported if the tensor-map encoder is unavailable.
+cudaError_t launch_gemm_tc(const GemmArgs &a, int epi, int num_sms, cudaStream_t st);
+// The smallest M routed to variant (a) by madi_q8_linear.
+constexpr int kGemmMinM = 9;
+
+// ---------------------------------------------------------------- misc kernels
+cudaError_t launch_dequant_f16(const int8_t *qs, const __half *scales, int N, int K, __half *out, cudaStream_t st);
+cudaError_t launch_quantize_f16(const __half *w, int rows, int dim, int8_t *qs, __half *scales, cudaStream_t st);
+
+// Driver entry point for cuTensorMapEncodeTiled (resolved lazily through the
+// runtime, so the library needs no link-time libcuda).
+typedef CUresult (*PFN_encodeTiled)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                    const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+PFN_encodeTiled tensor_map_encoder();
+
+}  // namespace madi

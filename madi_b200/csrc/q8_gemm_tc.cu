@@ -1,0 +1,359 @@
+// q8_gemm_tc.cu -- variant (a): Q8_0 linear on the 5th-generation tensor cores.
+//
+//   Y[m][n] = epi( sum_k X[m][k] * half(q[n][k] * s[n][k/32]) ),  f32 accumulate
+//
+// Semantics follow the reference's encoder path (kDeq + m4_gemm_*,
+// encoder.zig:262-304): weights are dequantised to f16 with ONE rounding
+// (q8_gemm.metal:25-26), products accumulate in f32, the epilogue adds the f32
+// bias, applies the A&S GELU or adds the residual, and rounds once to f16.
+//
+// Design (one persistent CTA per SM, warp-specialised):
+//   * the GEMM is computed transposed, Y^T = Wdq * X^T, so the DEQUANTISED
+//     WEIGHT TILE is the MMA's A operand and lives in tensor memory: dequant
+//     warps read int8 from shared memory, convert in registers and write f16
+//     pairs straight to TMEM with tcgen05.st.  f16 weights never touch shared
+//     memory or HBM.
+//   * X tiles are the B operand: TMA (SWIZZLE_128B, no multicast) into shared
+//     memory, read by tcgen05.mma through a K-major smem descriptor.
+//   * int8 weight tiles arrive by TMA too (SWIZZLE_64B, conflict-free rows).
+//   * the f32 accumulator (128 weight rows x BT tokens) sits in TMEM, double
+//     buffered so the epilogue of tile i overlaps the MMAs of tile i+1.
+//
+// Warp roles (384 threads): w0 TMA producer, w1 MMA issuer + TMEM owner,
+// w2-3 idle, w4-7 dequant (TMEM lane quarter = warp % 4), w8-11 epilogue.
+// TMEM columns: [0, 2*BT) accumulators, then STAGES x 32 columns of A.
+// Every mbarrier wait is bounded; on expiry the CTA raises its abort flag,
+// records the device error word, drains its in-flight copies and MMAs,
+// frees TMEM and returns.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace madi {
+namespace {
+
+constexpr int BN = 128;        // weight rows per tile = MMA M
+constexpr int BK = 64;         // K per pipeline stage
+constexpr int STAGES = 4;
+constexpr int W_STAGE = BN * BK;           // int8 bytes
+constexpr int A_STAGE_COLS = BK / 2;       // f16 pairs per TMEM column
+constexpr int TMEM_COLS = 512;
+constexpr int kThreads = 384;
+
+template <int BT> struct Cfg {
+    static constexpr int X_STAGE = BT * BK * 2;   // f16 bytes
+    static constexpr int ACC_COLS = BT;
+    static constexpr int A_COL0 = 2 * BT;
+    static_assert(A_COL0 + STAGES * A_STAGE_COLS <= TMEM_COLS, "TMEM budget");
+    static_assert(BT % 32 == 0 && BT >= 32 && BT <= 256, "MMA N");
+    static constexpr uint32_t IDESC = idesc_f16_f32(BN, BT);
+    static constexpr size_t SMEM = 1024 + (size_t)STAGES * (X_STAGE + W_STAGE) + 256;
+};
+
+struct __align__(8) Bars {
+    uint64_t full[STAGES];     // TMA bytes landed (X + W)
+    uint64_t aready[STAGES];   // dequantised A written to TMEM (128 arrivals)
+    uint64_t empty[STAGES];    // MMAs of the stage done (tcgen05.commit)
+    uint64_t accfull[2];       // accumulator ready (tcgen05.commit)
+    uint64_t accempty[2];      // epilogue drained the accumulator (128 arrivals)
+    uint64_t drain;            // final MMA drain
+    uint32_t tmem_base;
+    int abort;
+};
+
+// Warp-uniform bounded wait: every lane observes the barrier (so each has the
+// acquire ordering for the data it guards), then the warp agrees; a lane that
+// gave up makes the whole warp give up, keeping warp-collective tcgen05 ops
+// convergent.
+MADI_DEV bool warp_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int *dev_err) {
+    const bool ok = mbar_wait(bar, parity, abort_flag, dev_err);
+    return __all_sync(0xffffffffu, ok);
+}
+
+// Bounded wait that ignores the abort flag (used to drain in-flight work).
+MADI_DEV void mbar_wait_drain(uint64_t *bar, uint32_t parity) {
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity))
+        if (clock64() - t0 > kWaitBudgetCycles) return;
+}
+
+template <int BT, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    q8_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
+                      const GemmArgs p) {
+    using C = Cfg<BT>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *xs = smem;
+    uint8_t *ws = smem + STAGES * C::X_STAGE;
+    Bars *bars = reinterpret_cast<Bars *>(ws + STAGES * W_STAGE);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int M = p.M, N = p.N, K = p.K;
+    const int n_tiles = (N + BN - 1) / BN;
+    const int num_tiles = n_tiles * ((M + BT - 1) / BT);
+    const int KT = (K + BK - 1) / BK;
+    const int nkb = K / 32;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&bars->full[s], 1);
+            mbar_init(&bars->aready[s], 128);
+            mbar_init(&bars->empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&bars->accfull[b], 1);
+            mbar_init(&bars->accempty[b], 128);
+        }
+        mbar_init(&bars->drain, 1);
+        bars->abort = 0;
+        fence_mbar_init();
+        tma_prefetch_desc(&tmX);
+        tma_prefetch_desc(&tmW);
+    }
+    if (warp == 1) {
+        tmem_alloc(&bars->tmem_base, TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = bars->tmem_base;
+    volatile int *abort_flag = &bars->abort;
+    int *err = p.dev_err;
+
+    if (warp == 0) {
+        // ------------------------------------------------ TMA producer
+        if (lane == 0) {
+            int s = 0;
+            uint32_t ph = 0;
+            uint32_t issued_mask = 0, last_ph[STAGES];
+            for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+                const int m0 = (tile / n_tiles) * BT, n0 = (tile % n_tiles) * BN;
+                for (int kt = 0; kt < KT; ++kt) {
+                    if (!mbar_wait(&bars->empty[s], ph ^ 1, abort_flag, err)) goto producer_done;
+                    mbar_arrive_expect_tx(&bars->full[s], C::X_STAGE + W_STAGE);
+                    tma_load_2d(xs + s * C::X_STAGE, &tmX, &bars->full[s], kt * BK, m0);
+                    tma_load_2d(ws + s * W_STAGE, &tmW, &bars->full[s], kt * BK, n0);
+                    issued_mask |= 1u << s;
+                    last_ph[s] = ph;
+                    if (++s == STAGES) { s = 0; ph ^= 1; }
+                }
+            }
+        producer_done:
+            // the copies issued last must land before shared memory is released
+            for (int i = 0; i < STAGES; ++i)
+                if (issued_mask & (1u << i)) mbar_wait_drain(&bars->full[i], last_ph[i]);
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            int s = 0, lt = 0;
+            uint32_t ph = 0;
+            for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++lt) {
+                const int b = lt & 1;
+                const uint32_t aph = (lt >> 1) & 1;
+                if (!mbar_wait(&bars->accempty[b], aph ^ 1, abort_flag, err)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem + b * C::ACC_COLS;
+                bool ok = true;
+                for (int kt = 0; kt < KT; ++kt) {
+                    if (!mbar_wait(&bars->aready[s], ph, abort_flag, err)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t a_tmem = tmem + C::A_COL0 + s * A_STAGE_COLS;
+                    const uint32_t xaddr = smem_u32(xs + s * C::X_STAGE);
+#pragma unroll
+                    for (int j = 0; j < BK / 16; ++j)
+                        umma_f16_ts(d_tmem, a_tmem + j * 8, smem_desc_sw128(xaddr + j * 32), C::IDESC,
+                                    (kt | j) != 0);
+                    umma_commit(&bars->empty[s]);
+                    if (++s == STAGES) { s = 0; ph ^= 1; }
+                }
+                if (!ok) break;
+                umma_commit(&bars->accfull[b]);
+            }
+            // every MMA issued must finish before TMEM is released
+            umma_commit(&bars->drain);
+            mbar_wait_drain(&bars->drain, 0);
+        }
+        __syncwarp();
+    } else if (warp >= 4 && warp < 8) {
+        // ------------------------------------------------ dequant: int8 smem -> f16 TMEM
+        const int q = warp & 3;
+        const int r = q * 32 + lane;            // weight row within the tile = TMEM lane
+        const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+        const int swz = (r >> 1) & 3;           // SWIZZLE_64B: 16-byte chunk c lives at c ^ swz
+        int s = 0;
+        uint32_t ph = 0;
+        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+            const int n = (tile % n_tiles) * BN + r;
+            const bool nok = n < N;
+            const __half *srow = p.scales + (size_t)(nok ? n : 0) * nkb;
+            for (int kt = 0; kt < KT; ++kt) {
+                const int kb = kt * 2;
+                const __half sc0 = (nok && kb < nkb) ? srow[kb] : __ushort_as_half(0);
+                const __half sc1 = (nok && kb + 1 < nkb) ? srow[kb + 1] : __ushort_as_half(0);
+                if (!warp_wait(&bars->full[s], ph, abort_flag, err)) goto dequant_done;
+                {
+                    const uint8_t *wrow = ws + s * W_STAGE + r * 64;
+                    uint32_t a[32];
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        const uint4 v = *reinterpret_cast<const uint4 *>(wrow + ((c ^ swz) << 4));
+                        const __half2 sc = __half2half2(c < 2 ? sc0 : sc1);
+                        const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            __half2 lo, hi;
+                            q8_to_half2x2(wv[i], lo, hi);
+                            a[c * 8 + 2 * i] = h2_as_u32(__hmul2(lo, sc));
+                            a[c * 8 + 2 * i + 1] = h2_as_u32(__hmul2(hi, sc));
+                        }
+                    }
+                    tmem_st32(tmem + lane_addr + C::A_COL0 + s * A_STAGE_COLS, a);
+                    tmem_wait_st();
+                }
+                tc_fence_before();
+                mbar_arrive(&bars->aready[s]);
+                if (++s == STAGES) { s = 0; ph ^= 1; }
+            }
+        }
+    dequant_done:;
+    } else if (warp >= 8) {
+        // ------------------------------------------------ epilogue: TMEM -> bias/GELU/residual -> f16
+        const int q = warp & 3;
+        const int r = q * 32 + lane;
+        const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+        int lt = 0;
+        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++lt) {
+            const int b = lt & 1;
+            const uint32_t aph = (lt >> 1) & 1;
+            if (!warp_wait(&bars->accfull[b], aph, abort_flag, err)) break;
+            tc_fence_after();
+            const int m0 = (tile / n_tiles) * BT;
+            const int n = (tile % n_tiles) * BN + r;
+            const bool nok = n < N;
+            float bias = 0.f;
+            if constexpr (EPI != kEpiNone) {
+                if (nok)
+                    bias = p.bias_f16 ? __half2float(reinterpret_cast<const __half *>(p.bias)[n])
+                                      : reinterpret_cast<const float *>(p.bias)[n];
+            }
+#pragma unroll 1
+            for (int c = 0; c < BT / 32; ++c) {
+                uint32_t v[32];
+                tmem_ld32(tmem + lane_addr + b * C::ACC_COLS + c * 32, v);
+                tmem_wait_ld();
+                const int mb = m0 + c * 32;
+                if (nok) {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        const int m = mb + i;
+                        if (m < M) {
+                            float y = __uint_as_float(v[i]);
+                            if constexpr (EPI == kEpiBias) y += bias;
+                            if constexpr (EPI == kEpiBiasGelu) y = gelu_erf(y + bias);
+                            if constexpr (EPI == kEpiBiasRes)
+                                y = y + bias + __half2float(p.residual[(size_t)m * N + n]);
+                            p.y[(size_t)m * N + n] = __float2half_rn(y);
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&bars->accempty[b]);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, TMEM_COLS);
+    }
+}
+
+template <int BT, int EPI>
+cudaError_t launch_bt(const GemmArgs &a, const CUtensorMap &tmX, const CUtensorMap &tmW, int num_sms,
+                      cudaStream_t st) {
+    using C = Cfg<BT>;
+    auto fn = q8_gemm_tc_kernel<BT, EPI>;
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
+    if (e != cudaSuccess) return e;
+    const int tiles = ((a.N + BN - 1) / BN) * ((a.M + BT - 1) / BT);
+    const int grid = tiles < num_sms ? tiles : num_sms;
+    fn<<<grid, kThreads, C::SMEM, st>>>(tmX, tmW, a);
+    return cudaGetLastError();
+}
+
+bool make_map(CUtensorMap *m, CUtensorMapDataType dt, const void *base, uint64_t inner, uint64_t outer,
+              uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz) {
+    PFN_encodeTiled enc = tensor_map_encoder();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = {inner, outer};
+    const cuuint64_t strides[1] = {row_bytes};
+    const cuuint32_t box[2] = {box_inner, box_outer};
+    const cuuint32_t es[2] = {1, 1};
+    return enc(m, dt, 2, const_cast<void *>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Token-tile width: the candidate with the fewest waves x tile length wins,
+// the wider tile on ties (it amortises the weight dequant over more tokens).
+int pick_bt(int M, int N, int num_sms) {
+    const int n_tiles = (N + BN - 1) / BN;
+    long best_cost = -1;
+    int best = 192;
+    for (int bt : {192, 128}) {
+        const long tiles = (long)n_tiles * ((M + bt - 1) / bt);
+        const long waves = (tiles + num_sms - 1) / num_sms;
+        const long cost = waves * bt;
+        if (best_cost < 0 || cost < best_cost) { best_cost = cost; best = bt; }
+    }
+    return best;
+}
+
+}  // namespace
+
+PFN_encodeTiled tensor_map_encoder() {
+    static PFN_encodeTiled fn = nullptr;
+    static bool tried = false;
+    if (!tried) {
+        tried = true;
+        void *ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_encodeTiled>(ptr);
+    }
+    return fn;
+}
+
+cudaError_t launch_gemm_tc(const GemmArgs &a, int epi, int num_sms, cudaStream_t st) {
+    const int bt = pick_bt(a.M, a.N, num_sms);
+    CUtensorMap tmX, tmW;
+    if (!make_map(&tmX, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.x, (uint64_t)a.K, (uint64_t)a.M, (uint64_t)a.K * 2, BK,
+                  (uint32_t)bt, CU_TENSOR_MAP_SWIZZLE_128B))
+        return cudaErrorNotSupported;
+    if (!make_map(&tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.qs, (uint64_t)a.K, (uint64_t)a.N, (uint64_t)a.K, BK, BN,
+                  CU_TENSOR_MAP_SWIZZLE_64B))
+        return cudaErrorNotSupported;
+#define MADI_GEMM_EPI(BT)                                                          \
+    switch (epi) {                                                                 \
+        case kEpiNone: return launch_bt<BT, kEpiNone>(a, tmX, tmW, num_sms, st);   \
+        case kEpiBias: return launch_bt<BT, kEpiBias>(a, tmX, tmW, num_sms, st);   \
+        case kEpiBiasGelu: return launch_bt<BT, kEpiBiasGelu>(a, tmX, tmW, num_sms, st); \
+        case kEpiBiasRes: return launch_bt<BT, kEpiBiasRes>(a, tmX, tmW, num_sms, st);   \
+        default: return cudaErrorInvalidValue;                                     \
+    }
+    if (bt == 192) { MADI_GEMM_EPI(192) }
+    MADI_GEMM_EPI(128)
+#undef MADI_GEMM_EPI
+}
+
+}  // namespace madi

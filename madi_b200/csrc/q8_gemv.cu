@@ -1,0 +1,259 @@
+// q8_gemv.cu -- variant (b): bandwidth-bound Q8_0 GEMV / skinny GEMM, M <= 8.
+//
+// Semantics (reference graph_helpers.metal:320-567, f32 throughout):
+//   y[m][n] = epi( sum_kb s[n][kb] * sum_{k in kb} x[m][k] * q[n][k] )
+// The int8 weights are converted to f16 EXACTLY (no scale folded in), the
+// per-32-block scale is applied in f32 to each block's partial sum, and f32
+// activations are split into two f16 halves (hi = f16(x), lo = f16(x - hi))
+// so the products keep ~22 mantissa bits.  Accumulation is f32.
+//
+// Mapping onto the tensor cores (mma.sync m16n8k16, f16 in, f32 accumulate):
+// the MMA "M" dimension is 16 weight rows, "N" is the 8 token slots, "K" walks
+// one Q8 block (32) in two k16 steps.  Because a dot product does not care in
+// which order its terms are summed, the MMA's k-slots are bound to physical k
+// so that each lane reads 8 CONTIGUOUS int8 of a row per block:
+//   lane (g = lane/4, t = lane%4) owns physical k = 8t .. 8t+7 of the block;
+//   step s uses 8t+4s .. 8t+4s+3; A slots {2t,2t+1} <- k+0,1 and {2t+8,2t+9} <- k+2,3.
+// The activations are staged once per CTA in shared memory already permuted
+// into that fragment order, so every B-fragment read is one conflict-free
+// 8-byte load.
+//
+// Work split: a CTA is 8 warps; `ks` warps share one 16-row tile and split
+// its K blocks (ks in {1,2,4,8}); partial sums meet in shared memory and are
+// added in a fixed order (deterministic, no atomics, no global scratch).
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace madi {
+namespace {
+
+constexpr int kWarps = 8;
+constexpr int kThreads = kWarps * 32;
+constexpr int kUnroll = 4;   // Q8 blocks in flight per warp iteration
+
+MADI_DEV uint2 ldg_stream_u2(const void *p) {
+    uint2 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+    return v;
+}
+MADI_DEV float ldg_half(const __half *p) { return __half2float(__ldg(p)); }
+
+MADI_DEV void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+template <typename T> MADI_DEV float to_f32(T v);
+template <> MADI_DEV float to_f32<float>(float v) { return v; }
+template <> MADI_DEV float to_f32<__half>(__half v) { return __half2float(v); }
+template <typename T> MADI_DEV T from_f32(float v);
+template <> MADI_DEV float from_f32<float>(float v) { return v; }
+template <> MADI_DEV __half from_f32<__half>(float v) { return __float2half_rn(v); }
+
+// Stage x [M][K] into shared memory in fragment order.  Slot for (kb, s, m, t)
+// holds x[m][kb*32 + 8t + 4s + 0..3] as four f16.
+template <typename XT, bool kSplit>
+MADI_DEV void stage_x(const XT *__restrict__ x, int M, int K, uint2 *xf_hi, uint2 *xf_lo) {
+    const int nquads = M * K / 4;
+    for (int i = threadIdx.x; i < nquads; i += kThreads) {
+        const int m = (4 * i) / K, k = (4 * i) % K;
+        const int kb = k >> 5, t = (k & 31) >> 3, s = (k & 7) >> 2;
+        const int slot = ((kb * 2 + s) * M + m) * 4 + t;
+        float v[4];
+        if constexpr (sizeof(XT) == 4) {
+            const float4 f = __ldg(reinterpret_cast<const float4 *>(x) + i);
+            v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
+        } else {
+            const uint2 u = __ldg(reinterpret_cast<const uint2 *>(x) + i);
+            const __half2 h0 = *reinterpret_cast<const __half2 *>(&u.x), h1 = *reinterpret_cast<const __half2 *>(&u.y);
+            v[0] = __low2float(h0); v[1] = __high2float(h0); v[2] = __low2float(h1); v[3] = __high2float(h1);
+        }
+        __half2 h01 = __floats2half2_rn(v[0], v[1]), h23 = __floats2half2_rn(v[2], v[3]);
+        xf_hi[slot] = make_uint2(h2_as_u32(h01), h2_as_u32(h23));
+        if constexpr (kSplit) {
+            __half2 l01 = __floats2half2_rn(v[0] - __low2float(h01), v[1] - __high2float(h01));
+            __half2 l23 = __floats2half2_rn(v[2] - __low2float(h23), v[3] - __high2float(h23));
+            xf_lo[slot] = make_uint2(h2_as_u32(l01), h2_as_u32(l23));
+        }
+    }
+}
+
+// out-of-range rows read as zero weights and zero scales
+template <typename XT, typename YT, int EPI, bool kQKV>
+__global__ void __launch_bounds__(kThreads) q8_gemv_kernel(const GemvArgs p) {
+    constexpr bool kSplit = sizeof(XT) == 4;
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int M = p.M, K = p.K, N = p.N, ks = p.ks;
+    const int nkb = K >> 5;
+    uint2 *xf_hi = reinterpret_cast<uint2 *>(smem);
+    uint2 *xf_lo = xf_hi + (size_t)M * K / 4;
+    float4 *red = reinterpret_cast<float4 *>(smem + (size_t)M * K * (kSplit ? 4 : 2));
+
+    // griddepcontrol: the weights do not depend on the previous kernel, so
+    // with programmatic dependent launch only the activation read waits.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    stage_x<XT, kSplit>(reinterpret_cast<const XT *>(p.x), M, K, xf_hi, xf_lo);
+    __syncthreads();
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, t = lane & 3;
+    const int rt = kWarps / ks;
+    const int tile = blockIdx.x * rt + warp / ks;
+    const int slice = warp % ks;
+    const int row0 = tile * 16 + g, row1 = row0 + 8;
+    const bool ok0 = row0 < N, ok1 = row1 < N;
+    const int kb_per = (nkb + ks - 1) / ks;
+    const int kb_begin = slice * kb_per;
+    const int kb_end = min(nkb, kb_begin + kb_per);
+
+    const int8_t *w0 = p.qs + (size_t)(ok0 ? row0 : 0) * K + 8 * t;
+    const int8_t *w1 = p.qs + (size_t)(ok1 ? row1 : 0) * K + 8 * t;
+    const __half *s0p = p.scales + (size_t)(ok0 ? row0 : 0) * nkb;
+    const __half *s1p = p.scales + (size_t)(ok1 ? row1 : 0) * nkb;
+    const bool gval = g < M;
+
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int kb0 = kb_begin; kb0 < kb_end; kb0 += kUnroll) {
+        uint2 wa[kUnroll], wb[kUnroll];
+        float sa[kUnroll], sb[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+            const int kb = kb0 + u;
+            const bool in = kb < kb_end;
+            wa[u] = (in && ok0) ? ldg_stream_u2(w0 + (size_t)kb * 32) : make_uint2(0u, 0u);
+            wb[u] = (in && ok1) ? ldg_stream_u2(w1 + (size_t)kb * 32) : make_uint2(0u, 0u);
+            sa[u] = (in && ok0) ? ldg_half(s0p + kb) : 0.f;
+            sb[u] = (in && ok1) ? ldg_half(s1p + kb) : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+            const int kb = kb0 + u;
+            if (kb >= kb_end) break;
+            float blk[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int s = 0; s < 2; ++s) {
+                __half2 a_lo0, a_hi0, a_lo1, a_hi1;
+                q8_to_half2x2(s == 0 ? wa[u].x : wa[u].y, a_lo0, a_hi0);
+                q8_to_half2x2(s == 0 ? wb[u].x : wb[u].y, a_lo1, a_hi1);
+                const uint32_t a[4] = {h2_as_u32(a_lo0), h2_as_u32(a_lo1), h2_as_u32(a_hi0), h2_as_u32(a_hi1)};
+                const int slot = ((kb * 2 + s) * M + g) * 4 + t;
+                uint2 bh = gval ? xf_hi[slot] : make_uint2(0u, 0u);
+                mma16816(blk, a, bh.x, bh.y);
+                if constexpr (kSplit) {
+                    uint2 bl = gval ? xf_lo[slot] : make_uint2(0u, 0u);
+                    mma16816(blk, a, bl.x, bl.y);
+                }
+            }
+            acc[0] = fmaf(blk[0], sa[u], acc[0]);
+            acc[1] = fmaf(blk[1], sa[u], acc[1]);
+            acc[2] = fmaf(blk[2], sb[u], acc[2]);
+            acc[3] = fmaf(blk[3], sb[u], acc[3]);
+        }
+    }
+
+    if (ks > 1) {
+        red[warp * 32 + lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        __syncthreads();
+        if (slice != 0) return;
+        for (int j = 1; j < ks; ++j) {
+            const float4 o = red[(warp + j) * 32 + lane];
+            acc[0] += o.x; acc[1] += o.y; acc[2] += o.z; acc[3] += o.w;
+        }
+    }
+    // allow the next kernel in the stream to start its weight prefetch
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
+    // C fragment: acc[0..1] = (row0, tokens 2t, 2t+1), acc[2..3] = (row1, ...)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int row = (i < 2) ? row0 : row1;
+        const int tok = 2 * t + (i & 1);
+        if (row >= N || tok >= M) continue;
+        float v = acc[i];
+        if constexpr (kQKV) {
+            const int D = p.D;
+            if (row < D) {
+                reinterpret_cast<float *>(p.y)[(size_t)tok * D + row] = v + p.qb[row];
+            } else {
+                const size_t base = (size_t)tok * p.cache_stride + (size_t)p.pos[tok] * D;
+                if (row < 2 * D) p.kc[base + (row - D)] = v;
+                else p.vc[base + (row - 2 * D)] = v + p.vb[row - 2 * D];
+            }
+        } else {
+            float b = 0.f;
+            if constexpr (EPI != kEpiNone)
+                b = p.bias_f16 ? __half2float(reinterpret_cast<const __half *>(p.bias)[row])
+                               : reinterpret_cast<const float *>(p.bias)[row];
+            const size_t o = (size_t)tok * N + row;
+            if constexpr (EPI == kEpiBias) v = v + b;
+            if constexpr (EPI == kEpiBiasGelu) v = gelu_erf(v + b);
+            if constexpr (EPI == kEpiBiasRes) v = to_f32(reinterpret_cast<const YT *>(p.residual)[o]) + v + b;
+            reinterpret_cast<YT *>(p.y)[o] = from_f32<YT>(v);
+        }
+    }
+}
+
+template <typename XT, typename YT, int EPI, bool kQKV>
+cudaError_t launch_one(const GemvArgs &a, cudaStream_t st, bool pdl) {
+    const size_t xbytes = (size_t)a.M * a.K * (sizeof(XT) == 4 ? 4 : 2);
+    const size_t smem = xbytes + (size_t)kThreads * 16;
+    auto fn = q8_gemv_kernel<XT, YT, EPI, kQKV>;
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    const int tiles = (a.N + 15) / 16;
+    const int rt = kWarps / a.ks;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((tiles + rt - 1) / rt);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, fn, a);
+}
+
+}  // namespace
+
+int gemv_pick_ks(int N, int K, int num_sms) {
+    const int tiles = (N + 15) / 16;
+    const int nkb = K / 32;
+    const int want = num_sms * 16;   // warps in flight we aim for
+    int ks = 1;
+    while (ks < 8 && tiles * ks < want && (nkb / (ks * 2)) >= 2) ks *= 2;
+    return ks;
+}
+
+size_t gemv_smem_bytes(int M, int K, bool x_f32) {
+    return (size_t)M * K * (x_f32 ? 4 : 2) + (size_t)kThreads * 16;
+}
+
+cudaError_t launch_gemv(const GemvArgs &a, bool x_f32, bool y_f32, int epi, bool qkv, cudaStream_t st, bool pdl) {
+    if (qkv) return x_f32 ? launch_one<float, float, kEpiNone, true>(a, st, pdl)
+                          : launch_one<__half, float, kEpiNone, true>(a, st, pdl);
+#define MADI_GEMV_CASE(XT, YT)                                                  \
+    switch (epi) {                                                              \
+        case kEpiNone: return launch_one<XT, YT, kEpiNone, false>(a, st, pdl);  \
+        case kEpiBias: return launch_one<XT, YT, kEpiBias, false>(a, st, pdl);  \
+        case kEpiBiasGelu: return launch_one<XT, YT, kEpiBiasGelu, false>(a, st, pdl); \
+        case kEpiBiasRes: return launch_one<XT, YT, kEpiBiasRes, false>(a, st, pdl);   \
+        default: return cudaErrorInvalidValue;                                  \
+    }
+    if (x_f32 && y_f32) { MADI_GEMV_CASE(float, float) }
+    if (x_f32 && !y_f32) { MADI_GEMV_CASE(float, __half) }
+    if (!x_f32 && y_f32) { MADI_GEMV_CASE(__half, float) }
+    MADI_GEMV_CASE(__half, __half)
+#undef MADI_GEMV_CASE
+}
+
+}  // namespace madi

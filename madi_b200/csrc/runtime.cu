@@ -1,0 +1,548 @@
+// runtime.cu -- the C ABI declared in include/madi_q8.h.
+//
+// Re-expresses the reference's Metal bridge (engine/metal/metal_backend.m) for
+// CUDA on B200:
+//   mtl_init / cleanup            -> device bind, library stream, sm_100 check
+//   mtl_alloc registry (:136-230) -> cudaMalloc + an ordered registry so base
+//                                    and interior pointers resolve (:756-790)
+//   mtl_get_function (:607-666)   -> name table of the reference Q8 kernels
+//   mtl_dispatch (:669-797)       -> argument unpacking in kernelParams style,
+//                                    validation, B200 launch (own grid/block)
+//   command buffers (:861-917)    -> CUDA stream capture -> CUDA graph replay
+//   mtl_sync (:816-859)           -> bounded event poll (+ device error word)
+//   per-kernel profiler (:107-132, :717-747) -> CUDA events, kern_sum table
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "../../include/madi_q8.h"
+#include "internal.h"
+
+namespace {
+
+using namespace madi;
+
+thread_local std::string g_last_error = "ok";
+
+int fail(int code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+int cuda_fail(cudaError_t e, const char *what) {
+    return fail(MADI_ECUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+struct State {
+    bool ready = false;
+    int device = -1;
+    int num_sms = 0;
+    int max_smem_optin = 0;
+    cudaStream_t own_stream = nullptr;
+    cudaStream_t stream = nullptr;   // current (own or caller's)
+    int *dev_err = nullptr;          // device error word (bounded-wait expiry)
+    bool capturing = false;
+    cudaGraphExec_t exec = nullptr;
+    cudaEvent_t done = nullptr;
+    int verbose = 0;
+    bool profile = false;
+    bool pdl = true;
+    std::map<std::string, std::pair<long long, double>> prof;   // name -> (instances, total ms)
+} S;
+
+std::mutex g_alloc_mu;
+std::map<uintptr_t, size_t> g_allocs;   // base -> size
+
+bool in_registry(const void *p) {
+    std::lock_guard<std::mutex> lk(g_alloc_mu);
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    auto it = g_allocs.upper_bound(a);
+    if (it == g_allocs.begin()) return false;
+    --it;
+    return a < it->first + it->second;
+}
+
+bool is_device_ptr(const void *p) {
+    if (!p) return false;
+    if (in_registry(p)) return true;
+    cudaPointerAttributes at;
+    if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return at.type == cudaMemoryTypeDevice || at.type == cudaMemoryTypeManaged;
+}
+
+bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+cudaStream_t pick_stream(void *s) { return s ? static_cast<cudaStream_t>(s) : S.stream; }
+
+// ---------------------------------------------------------------- Q8 linear core
+
+int q8_linear_impl(const madi_q8w *w, const void *x, int x_dtype, int m, const void *bias, int bias_dtype, int epi,
+                   const void *residual, void *y, int y_dtype, cudaStream_t st, const char *who) {
+    if (!S.ready) return fail(MADI_ENOINIT, "%s: madi_init has not succeeded", who);
+    if (!w || !w->qs || !w->scales) return fail(MADI_EINVAL, "%s: null weight", who);
+    const int N = w->n, K = w->k;
+    if (N <= 0 || K <= 0 || (K % 32) != 0) return fail(MADI_EINVAL, "%s: bad weight shape N=%d K=%d (K %% 32 == 0)", who, N, K);
+    if (m <= 0) return fail(MADI_EINVAL, "%s: m=%d must be > 0", who, m);
+    if (!x || !y) return fail(MADI_EINVAL, "%s: null x or y", who);
+    if (epi < MADI_EPI_NONE || epi > MADI_EPI_BIAS_RES) return fail(MADI_EINVAL, "%s: bad epilogue %d", who, epi);
+    if (epi != MADI_EPI_NONE && !bias) return fail(MADI_EINVAL, "%s: epilogue %d needs a bias", who, epi);
+    if (epi == MADI_EPI_BIAS_RES && !residual) return fail(MADI_EINVAL, "%s: residual epilogue needs a residual", who);
+    if ((x_dtype != MADI_F32 && x_dtype != MADI_F16) || (y_dtype != MADI_F32 && y_dtype != MADI_F16) ||
+        (bias && bias_dtype != MADI_F32 && bias_dtype != MADI_F16))
+        return fail(MADI_EINVAL, "%s: bad dtype", who);
+    if ((size_t)m * (size_t)std::max(N, K) >= (1ull << 31) || (size_t)N * K >= (1ull << 40))
+        return fail(MADI_EINVAL, "%s: problem too large (m=%d N=%d K=%d)", who, m, N, K);
+    if (!aligned(w->qs, 16) || !aligned(w->scales, 2)) return fail(MADI_EINVAL, "%s: qs must be 16-byte aligned", who);
+
+    if (m >= kGemmMinM) {
+        if (x_dtype != MADI_F16 || y_dtype != MADI_F16)
+            return fail(MADI_EINVAL, "%s: the tensor-core path (m > 8) takes f16 x and f16 y", who);
+        if (!aligned(x, 16)) return fail(MADI_EINVAL, "%s: x must be 16-byte aligned", who);
+        if (!aligned(y, 2) || (residual && !aligned(residual, 2))) return fail(MADI_EINVAL, "%s: misaligned y", who);
+        GemmArgs a{};
+        a.x = static_cast<const __half *>(x);
+        a.qs = w->qs;
+        a.scales = reinterpret_cast<const __half *>(w->scales);
+        a.bias = bias;
+        a.bias_f16 = bias_dtype == MADI_F16;
+        a.residual = static_cast<const __half *>(residual);
+        a.y = static_cast<__half *>(y);
+        a.M = m; a.N = N; a.K = K;
+        a.dev_err = S.dev_err;
+        cudaError_t e = launch_gemm_tc(a, epi, S.num_sms, st);
+        if (e == cudaErrorNotSupported) return fail(MADI_EUNSUPPORTED, "%s: cuTensorMapEncodeTiled unavailable", who);
+        if (e != cudaSuccess) return cuda_fail(e, who);
+        return MADI_OK;
+    }
+    const bool xf32 = x_dtype == MADI_F32;
+    if (!aligned(x, xf32 ? 16 : 8)) return fail(MADI_EINVAL, "%s: x must be %d-byte aligned", who, xf32 ? 16 : 8);
+    const size_t smem = gemv_smem_bytes(m, K, xf32);
+    if (smem > (size_t)S.max_smem_optin)
+        return fail(MADI_EINVAL, "%s: K=%d too large for the decode path at m=%d", who, K, m);
+    GemvArgs a{};
+    a.qs = w->qs;
+    a.scales = reinterpret_cast<const __half *>(w->scales);
+    a.x = x; a.y = y; a.residual = residual; a.bias = bias;
+    a.bias_f16 = bias_dtype == MADI_F16;
+    a.N = N; a.K = K; a.M = m;
+    a.ks = gemv_pick_ks(N, K, S.num_sms);
+    cudaError_t e = launch_gemv(a, xf32, y_dtype == MADI_F32, epi, false, st, S.pdl);
+    if (e != cudaSuccess) return cuda_fail(e, who);
+    return MADI_OK;
+}
+
+int q8_qkv_impl(const madi_q8w *w, const float *x, int m, const float *qb, const float *vb, float *q_out, float *kc,
+                float *vc, const uint32_t *pos, long long cache_stride, cudaStream_t st, const char *who) {
+    if (!S.ready) return fail(MADI_ENOINIT, "%s: madi_init has not succeeded", who);
+    if (!w || !w->qs || !w->scales || !x || !qb || !vb || !q_out || !kc || !vc || !pos)
+        return fail(MADI_EINVAL, "%s: null argument", who);
+    const int D = w->k;
+    if (D <= 0 || D % 32 != 0 || w->n != 3 * D) return fail(MADI_EINVAL, "%s: qkv weight must be [3D][D], D %% 32 == 0", who);
+    if (m <= 0 || m > 8) return fail(MADI_EINVAL, "%s: m=%d outside 1..8", who, m);
+    if (!aligned(x, 16) || !aligned(w->qs, 16)) return fail(MADI_EINVAL, "%s: misaligned x or qs", who);
+    if (gemv_smem_bytes(m, D, true) > (size_t)S.max_smem_optin) return fail(MADI_EINVAL, "%s: D too large", who);
+    GemvArgs a{};
+    a.qs = w->qs;
+    a.scales = reinterpret_cast<const __half *>(w->scales);
+    a.x = x; a.y = q_out;
+    a.N = 3 * D; a.K = D; a.M = m;
+    a.ks = gemv_pick_ks(3 * D, D, S.num_sms);
+    a.qb = qb; a.vb = vb; a.kc = kc; a.vc = vc; a.pos = pos;
+    a.cache_stride = m > 1 ? cache_stride : 0;
+    a.D = D;
+    cudaError_t e = launch_gemv(a, true, true, MADI_EPI_NONE, true, st, S.pdl);
+    if (e != cudaSuccess) return cuda_fail(e, who);
+    return MADI_OK;
+}
+
+// ---------------------------------------------------------------- name table
+
+enum ArgKind { kPtr, kU32, kF32 };
+struct ArgVal {
+    const void *p;
+    uint32_t u;
+    float f;
+};
+using Handler = int (*)(const ArgVal *a, cudaStream_t st);
+
+struct Op {
+    const char *name;
+    std::vector<ArgKind> kinds;
+    Handler fn;
+};
+
+madi_q8w mkw(const ArgVal &qs, const ArgVal &sc, uint32_t n, uint32_t k) {
+    return madi_q8w{static_cast<const int8_t *>(qs.p), static_cast<const uint16_t *>(sc.p), (int32_t)n, (int32_t)k};
+}
+
+// gemv_q8(out, qs, scales, x, N, K)  graph_helpers.metal:390-422
+int h_gemv(const ArgVal *a, cudaStream_t st) {
+    madi_q8w w = mkw(a[1], a[2], a[4].u, a[5].u);
+    return q8_linear_impl(&w, a[3].p, MADI_F32, 1, nullptr, MADI_F32, MADI_EPI_NONE, nullptr, const_cast<void *>(a[0].p),
+                          MADI_F32, st, "gemv_q8");
+}
+// gemv_q8_bias / _bias_gelu / _bias_res(out, qs, scales, x, bias, N, K)  graph_helpers.metal:424-519
+template <int EPI>
+int h_gemv_bias(const ArgVal *a, cudaStream_t st) {
+    madi_q8w w = mkw(a[1], a[2], a[5].u, a[6].u);
+    return q8_linear_impl(&w, a[3].p, MADI_F32, 1, a[4].p, MADI_F32, EPI, EPI == MADI_EPI_BIAS_RES ? a[0].p : nullptr,
+                          const_cast<void *>(a[0].p), MADI_F32, st, "gemv_q8_bias*");
+}
+// gemv_q8_qkv(q_out, qs, scales, x, qb, vb, kc, vc, pos_ptr, D)  graph_helpers.metal:527-567
+int h_qkv(const ArgVal *a, cudaStream_t st) {
+    madi_q8w w = mkw(a[1], a[2], 3 * a[9].u, a[9].u);
+    return q8_qkv_impl(&w, static_cast<const float *>(a[3].p), 1, static_cast<const float *>(a[4].p),
+                       static_cast<const float *>(a[5].p), (float *)a[0].p, (float *)a[6].p, (float *)a[7].p,
+                       static_cast<const uint32_t *>(a[8].p), 0, st, "gemv_q8_qkv");
+}
+// logit_gemv_q8(logits, qs, scales, x, vocab, dim)  graph_helpers.metal:320-352
+int h_logit(const ArgVal *a, cudaStream_t st) {
+    madi_q8w w = mkw(a[1], a[2], a[4].u, a[5].u);
+    return q8_linear_impl(&w, a[3].p, MADI_F32, 1, nullptr, MADI_F32, MADI_EPI_NONE, nullptr, const_cast<void *>(a[0].p),
+                          MADI_F32, st, "logit_gemv_q8");
+}
+// dequant_q8_f16(out, qs, scales, N, K)  q8_gemm.metal:12-27
+int h_dequant(const ArgVal *a, cudaStream_t st) {
+    madi_q8w w = mkw(a[1], a[2], a[3].u, a[4].u);
+    return madi_q8_dequant_f16(&w, (uint16_t *)a[0].p, st);
+}
+// mul_mm_q8(C, A, qs, scales, M, N, K)  q8_gemm.metal:29-102
+int h_mul_mm(const ArgVal *a, cudaStream_t st) {
+    madi_q8w w = mkw(a[2], a[3], a[5].u, a[6].u);
+    return q8_linear_impl(&w, a[1].p, MADI_F16, (int)a[4].u, nullptr, MADI_F32, MADI_EPI_NONE, nullptr,
+                          const_cast<void *>(a[0].p), MADI_F16, st, "mul_mm_q8");
+}
+// m4_gemm_q8tg / m4_gemm_q8_bias_gelu(A, Wq, scales, C, bias, M, N, K, act_gelu)  m4_gemm.metal:131-266
+int h_m4_q8(const ArgVal *a, cudaStream_t st) {
+    madi_q8w w = mkw(a[1], a[2], a[6].u, a[7].u);
+    return q8_linear_impl(&w, a[0].p, MADI_F16, (int)a[5].u, a[4].p, MADI_F32,
+                          a[8].u ? MADI_EPI_BIAS_GELU : MADI_EPI_BIAS, nullptr, const_cast<void *>(a[3].p), MADI_F16, st,
+                          "m4_gemm_q8");
+}
+
+const std::vector<Op> &ops() {
+    static const std::vector<Op> table = {
+        {"gemv_q8", {kPtr, kPtr, kPtr, kPtr, kU32, kU32}, h_gemv},
+        {"gemv_q8_bias", {kPtr, kPtr, kPtr, kPtr, kPtr, kU32, kU32}, h_gemv_bias<MADI_EPI_BIAS>},
+        {"gemv_q8_bias_gelu", {kPtr, kPtr, kPtr, kPtr, kPtr, kU32, kU32}, h_gemv_bias<MADI_EPI_BIAS_GELU>},
+        {"gemv_q8_bias_res", {kPtr, kPtr, kPtr, kPtr, kPtr, kU32, kU32}, h_gemv_bias<MADI_EPI_BIAS_RES>},
+        {"gemv_q8_qkv", {kPtr, kPtr, kPtr, kPtr, kPtr, kPtr, kPtr, kPtr, kPtr, kU32}, h_qkv},
+        {"logit_gemv_q8", {kPtr, kPtr, kPtr, kPtr, kU32, kU32}, h_logit},
+        {"dequant_q8_f16", {kPtr, kPtr, kPtr, kU32, kU32}, h_dequant},
+        {"mul_mm_q8", {kPtr, kPtr, kPtr, kPtr, kU32, kU32, kU32}, h_mul_mm},
+        {"m4_gemm_q8tg", {kPtr, kPtr, kPtr, kPtr, kPtr, kU32, kU32, kU32, kU32}, h_m4_q8},
+        {"m4_gemm_q8_bias_gelu", {kPtr, kPtr, kPtr, kPtr, kPtr, kU32, kU32, kU32, kU32}, h_m4_q8},
+    };
+    return table;
+}
+
+void prof_add(const char *name, double ms) {
+    auto &e = S.prof[name];
+    e.first += 1;
+    e.second += ms;
+}
+
+}  // namespace
+
+// ======================================================================= C ABI
+extern "C" {
+
+int madi_init(int device) {
+    if (S.ready) {
+        if (device == S.device) return MADI_OK;
+        return fail(MADI_EBUSY, "madi_init: already bound to device %d", S.device);
+    }
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess) { cudaGetLastError(); return cuda_fail(e, "madi_init: cudaGetDeviceCount"); }
+    if (device < 0 || device >= n) return fail(MADI_EINVAL, "madi_init: device %d of %d", device, n);
+    if ((e = cudaSetDevice(device)) != cudaSuccess) return cuda_fail(e, "madi_init: cudaSetDevice");
+    cudaDeviceProp prop;
+    if ((e = cudaGetDeviceProperties(&prop, device)) != cudaSuccess) return cuda_fail(e, "madi_init: properties");
+    if (prop.major != 10 || prop.minor != 0)
+        return fail(MADI_EUNSUPPORTED, "madi_init: %s is sm_%d%d; this library is built for sm_100a", prop.name,
+                    prop.major, prop.minor);
+    S.device = device;
+    S.num_sms = prop.multiProcessorCount;
+    cudaDeviceGetAttribute(&S.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
+    // a BLOCKING stream: it orders against the legacy default stream, so work
+    // a caller (e.g. torch) queued there is visible to our kernels and vice versa
+    if ((e = cudaStreamCreateWithFlags(&S.own_stream, cudaStreamDefault)) != cudaSuccess)
+        return cuda_fail(e, "madi_init: stream");
+    S.stream = S.own_stream;
+    if ((e = cudaMalloc(&S.dev_err, 256)) != cudaSuccess) return cuda_fail(e, "madi_init: error word");
+    cudaMemset(S.dev_err, 0, 256);
+    if ((e = cudaEventCreateWithFlags(&S.done, cudaEventDisableTiming)) != cudaSuccess)
+        return cuda_fail(e, "madi_init: event");
+    const char *pv = getenv("MADI_PROFILE");
+    S.profile = pv && pv[0] == '1';
+    const char *pd = getenv("MADI_PDL");
+    S.pdl = !(pd && pd[0] == '0');
+    const char *dv = getenv("MADI_DEBUG");
+    if (dv && dv[0] == '1') S.verbose = 1;
+    if (!tensor_map_encoder()) return fail(MADI_EUNSUPPORTED, "madi_init: cuTensorMapEncodeTiled unavailable");
+    cudaDeviceSynchronize();
+    S.ready = true;
+    if (S.verbose) fprintf(stderr, "[madi] device %d %s, %d SMs\n", device, prop.name, S.num_sms);
+    return MADI_OK;
+}
+
+void madi_cleanup(void) {
+    if (!S.ready) return;
+    if (S.capturing) {
+        cudaGraph_t g = nullptr;
+        cudaStreamEndCapture(S.stream, &g);
+        if (g) cudaGraphDestroy(g);
+        S.capturing = false;
+    }
+    cudaStreamSynchronize(S.stream);
+    if (S.exec) cudaGraphExecDestroy(S.exec);
+    if (S.done) cudaEventDestroy(S.done);
+    if (S.dev_err) cudaFree(S.dev_err);
+    if (S.own_stream) cudaStreamDestroy(S.own_stream);
+    {
+        std::lock_guard<std::mutex> lk(g_alloc_mu);
+        for (auto &kv : g_allocs) cudaFree(reinterpret_cast<void *>(kv.first));
+        g_allocs.clear();
+    }
+    S = State();
+}
+
+void *madi_alloc(size_t size) {
+    if (!S.ready) { fail(MADI_ENOINIT, "madi_alloc: not initialised"); return nullptr; }
+    if (size == 0) size = 1;
+    void *p = nullptr;
+    cudaError_t e = cudaMalloc(&p, (size + 255) & ~size_t(255));
+    if (e != cudaSuccess) { cuda_fail(e, "madi_alloc"); return nullptr; }
+    std::lock_guard<std::mutex> lk(g_alloc_mu);
+    g_allocs[reinterpret_cast<uintptr_t>(p)] = size;
+    return p;
+}
+
+void madi_free(void *ptr) {
+    if (!ptr) return;
+    {
+        std::lock_guard<std::mutex> lk(g_alloc_mu);
+        auto it = g_allocs.find(reinterpret_cast<uintptr_t>(ptr));
+        if (it == g_allocs.end()) { fail(MADI_EINVAL, "madi_free: %p was not returned by madi_alloc", ptr); return; }
+        g_allocs.erase(it);
+    }
+    cudaFree(ptr);
+}
+
+int madi_upload(void *dst, const void *src, size_t size) {
+    if (!S.ready) return fail(MADI_ENOINIT, "madi_upload: not initialised");
+    if (!dst || !src) return fail(MADI_EINVAL, "madi_upload: null pointer");
+    cudaError_t e = cudaMemcpyAsync(dst, src, size, cudaMemcpyHostToDevice, S.stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(S.stream);
+    return e == cudaSuccess ? MADI_OK : cuda_fail(e, "madi_upload");
+}
+
+int madi_download(void *dst, const void *src, size_t size) {
+    if (!S.ready) return fail(MADI_ENOINIT, "madi_download: not initialised");
+    if (!dst || !src) return fail(MADI_EINVAL, "madi_download: null pointer");
+    cudaError_t e = cudaMemcpyAsync(dst, src, size, cudaMemcpyDeviceToHost, S.stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(S.stream);
+    return e == cudaSuccess ? MADI_OK : cuda_fail(e, "madi_download");
+}
+
+int madi_get_function(const char *name, int *out_id) {
+    if (!name || !out_id) return fail(MADI_EINVAL, "madi_get_function: null argument");
+    const auto &t = ops();
+    for (size_t i = 0; i < t.size(); ++i)
+        if (strcmp(t[i].name, name) == 0) { *out_id = (int)i; return MADI_OK; }
+    return fail(MADI_ENOTFOUND, "madi_get_function: no kernel named '%s'", name);
+}
+
+int madi_dispatch(int func_id, uint32_t gx, uint32_t gy, uint32_t gz, uint32_t bx, uint32_t by, uint32_t bz,
+                  const void **args, const size_t *arg_sizes, int n_args) {
+    (void)gx; (void)gy; (void)gz; (void)bx; (void)by; (void)bz;
+    if (!S.ready) return fail(MADI_ENOINIT, "madi_dispatch: not initialised");
+    const auto &t = ops();
+    if (func_id < 0 || func_id >= (int)t.size()) return fail(MADI_EINVAL, "madi_dispatch: bad function id %d", func_id);
+    const Op &op = t[func_id];
+    if (n_args != (int)op.kinds.size())
+        return fail(MADI_EINVAL, "madi_dispatch(%s): %d arguments, expected %zu", op.name, n_args, op.kinds.size());
+    if (!args || !arg_sizes) return fail(MADI_EINVAL, "madi_dispatch(%s): null argument arrays", op.name);
+    ArgVal v[16];
+    for (int i = 0; i < n_args; ++i) {
+        if (!args[i]) return fail(MADI_EINVAL, "madi_dispatch(%s): argument %d is null", op.name, i);
+        switch (op.kinds[i]) {
+            case kPtr:
+                if (arg_sizes[i] != sizeof(void *))
+                    return fail(MADI_EINVAL, "madi_dispatch(%s): argument %d must be a buffer pointer", op.name, i);
+                memcpy(&v[i].p, args[i], sizeof(void *));
+                if (!is_device_ptr(v[i].p))
+                    return fail(MADI_EINVAL, "madi_dispatch(%s): argument %d (%p) is not device memory", op.name, i,
+                                v[i].p);
+                break;
+            case kU32:
+                if (arg_sizes[i] != 4) return fail(MADI_EINVAL, "madi_dispatch(%s): argument %d must be u32", op.name, i);
+                memcpy(&v[i].u, args[i], 4);
+                break;
+            case kF32:
+                if (arg_sizes[i] != 4) return fail(MADI_EINVAL, "madi_dispatch(%s): argument %d must be f32", op.name, i);
+                memcpy(&v[i].f, args[i], 4);
+                break;
+        }
+    }
+    if (S.profile && !S.capturing) {
+        cudaEvent_t e0, e1;
+        cudaEventCreate(&e0);
+        cudaEventCreate(&e1);
+        cudaEventRecord(e0, S.stream);
+        int rc = op.fn(v, S.stream);
+        cudaEventRecord(e1, S.stream);
+        cudaEventSynchronize(e1);
+        float ms = 0.f;
+        cudaEventElapsedTime(&ms, e0, e1);
+        cudaEventDestroy(e0);
+        cudaEventDestroy(e1);
+        if (rc == MADI_OK) prof_add(op.name, ms);
+        return rc;
+    }
+    return op.fn(v, S.stream);
+}
+
+int madi_begin_command_buffer(void) {
+    if (!S.ready) return fail(MADI_ENOINIT, "madi_begin_command_buffer: not initialised");
+    if (S.capturing) return fail(MADI_EBUSY, "madi_begin_command_buffer: a command buffer is already open");
+    cudaError_t e = cudaStreamBeginCapture(S.stream, cudaStreamCaptureModeThreadLocal);
+    if (e != cudaSuccess) return cuda_fail(e, "madi_begin_command_buffer");
+    S.capturing = true;
+    return MADI_OK;
+}
+
+int madi_commit_command_buffer(void) {
+    if (!S.ready) return fail(MADI_ENOINIT, "madi_commit_command_buffer: not initialised");
+    if (!S.capturing) return fail(MADI_EBUSY, "madi_commit_command_buffer: no command buffer open");
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamEndCapture(S.stream, &g);
+    S.capturing = false;
+    if (e != cudaSuccess) return cuda_fail(e, "madi_commit_command_buffer: end capture");
+    if (S.exec) {
+        cudaGraphExecUpdateResultInfo info;
+        if (cudaGraphExecUpdate(S.exec, g, &info) != cudaSuccess) {
+            cudaGetLastError();
+            cudaGraphExecDestroy(S.exec);
+            S.exec = nullptr;
+        }
+    }
+    if (!S.exec && (e = cudaGraphInstantiate(&S.exec, g, 0)) != cudaSuccess) {
+        cudaGraphDestroy(g);
+        return cuda_fail(e, "madi_commit_command_buffer: instantiate");
+    }
+    cudaGraphDestroy(g);
+    if ((e = cudaGraphLaunch(S.exec, S.stream)) != cudaSuccess) return cuda_fail(e, "madi_commit_command_buffer: launch");
+    return MADI_OK;
+}
+
+void madi_flush(void) {}
+
+int madi_sync(int timeout_ms) {
+    if (!S.ready) return fail(MADI_ENOINIT, "madi_sync: not initialised");
+    if (S.capturing) return fail(MADI_EBUSY, "madi_sync: a command buffer is open (commit it first)");
+    cudaError_t e = cudaEventRecord(S.done, S.stream);
+    if (e != cudaSuccess) return cuda_fail(e, "madi_sync: record");
+    const auto t0 = std::chrono::steady_clock::now();
+    while (true) {
+        e = cudaEventQuery(S.done);
+        if (e == cudaSuccess) break;
+        if (e != cudaErrorNotReady) return cuda_fail(e, "madi_sync");
+        if (timeout_ms >= 0 &&
+            std::chrono::steady_clock::now() - t0 > std::chrono::milliseconds(timeout_ms))
+            return fail(MADI_ETIMEDOUT, "madi_sync: work still pending after %d ms", timeout_ms);
+        std::this_thread::sleep_for(std::chrono::microseconds(20));
+    }
+    int word = 0;
+    if ((e = cudaMemcpy(&word, S.dev_err, sizeof(int), cudaMemcpyDeviceToHost)) != cudaSuccess)
+        return cuda_fail(e, "madi_sync: error word");
+    if (word != 0) {
+        cudaMemset(S.dev_err, 0, sizeof(int));
+        return fail(MADI_EDEVICE, "madi_sync: a kernel reported device error %d (bounded wait expired)", word);
+    }
+    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "madi_sync");
+    return MADI_OK;
+}
+
+int madi_set_stream(void *cuda_stream) {
+    if (!S.ready) return fail(MADI_ENOINIT, "madi_set_stream: not initialised");
+    if (S.capturing) return fail(MADI_EBUSY, "madi_set_stream: a command buffer is open");
+    S.stream = cuda_stream ? static_cast<cudaStream_t>(cuda_stream) : S.own_stream;
+    return MADI_OK;
+}
+
+void *madi_get_stream(void) { return S.stream; }
+
+const char *madi_last_error(void) { return g_last_error.c_str(); }
+
+void madi_set_verbose(int v) { S.verbose = v; }
+
+int madi_num_sms(void) { return S.num_sms; }
+
+void madi_dump_profile(const char *out_path) {
+    FILE *f = out_path ? fopen(out_path, "w") : stdout;
+    if (!f) return;
+    double total = 0;
+    std::vector<std::pair<std::string, std::pair<long long, double>>> rows(S.prof.begin(), S.prof.end());
+    for (auto &r : rows) total += r.second.second;
+    std::sort(rows.begin(), rows.end(), [](auto &a, auto &b) { return a.second.second > b.second.second; });
+    fprintf(f, " Time (%%)  Total Time (ns)  Instances  Avg (ns)  Name\n");
+    for (auto &r : rows) {
+        const double ns = r.second.second * 1e6;
+        fprintf(f, " %7.1f  %15.0f  %9lld  %8.0f  %s\n", total > 0 ? 100.0 * r.second.second / total : 0.0, ns,
+                r.second.first, ns / (double)r.second.first, r.first.c_str());
+    }
+    if (f != stdout) fclose(f);
+}
+
+int madi_q8_linear(const madi_q8w *w, const void *x, int x_dtype, int m, const void *bias, int bias_dtype, int epi,
+                   const void *residual, void *y, int y_dtype, void *stream) {
+    return q8_linear_impl(w, x, x_dtype, m, bias, bias_dtype, epi, residual, y, y_dtype, pick_stream(stream),
+                          "madi_q8_linear");
+}
+
+int madi_q8_qkv(const madi_q8w *w, const float *x, int m, const float *qb, const float *vb, float *q_out, float *kc,
+                float *vc, const uint32_t *pos, int64_t cache_stride, void *stream) {
+    return q8_qkv_impl(w, x, m, qb, vb, q_out, kc, vc, pos, (long long)cache_stride, pick_stream(stream), "madi_q8_qkv");
+}
+
+int madi_q8_dequant_f16(const madi_q8w *w, uint16_t *out, void *stream) {
+    if (!S.ready) return fail(MADI_ENOINIT, "madi_q8_dequant_f16: not initialised");
+    if (!w || !w->qs || !w->scales || !out) return fail(MADI_EINVAL, "madi_q8_dequant_f16: null argument");
+    if (w->n <= 0 || w->k <= 0 || w->k % 32) return fail(MADI_EINVAL, "madi_q8_dequant_f16: bad shape");
+    if (!aligned(w->qs, 16) || !aligned(out, 16)) return fail(MADI_EINVAL, "madi_q8_dequant_f16: misaligned buffer");
+    cudaError_t e = launch_dequant_f16(w->qs, reinterpret_cast<const __half *>(w->scales), w->n, w->k,
+                                       reinterpret_cast<__half *>(out), pick_stream(stream));
+    return e == cudaSuccess ? MADI_OK : cuda_fail(e, "madi_q8_dequant_f16");
+}
+
+int madi_q8_quantize_f16(const uint16_t *w, int rows, int dim, int8_t *qs, uint16_t *scales, void *stream) {
+    if (!S.ready) return fail(MADI_ENOINIT, "madi_q8_quantize_f16: not initialised");
+    if (!w || !qs || !scales) return fail(MADI_EINVAL, "madi_q8_quantize_f16: null argument");
+    if (rows <= 0 || dim <= 0 || dim % 32) return fail(MADI_EINVAL, "madi_q8_quantize_f16: bad shape (dim %% 32)");
+    cudaError_t e = launch_quantize_f16(reinterpret_cast<const __half *>(w), rows, dim, qs,
+                                        reinterpret_cast<__half *>(scales), pick_stream(stream));
+    return e == cudaSuccess ? MADI_OK : cuda_fail(e, "madi_q8_quantize_f16");
+}
+
+}  // extern "C"

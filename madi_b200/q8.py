@@ -1,0 +1,119 @@
+"""Typed Q8_0 linear API over torch CUDA tensors.
+
+Thin wrappers of the C ABI's typed entry points (madi_q8_linear, madi_q8_qkv,
+madi_q8_dequant_f16, madi_q8_quantize_f16).  torch supplies device memory and
+streams only: every call runs this library's sm_100a kernels on the caller's
+current torch stream.
+"""
+import ctypes
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+from . import _lib
+from ._lib import EPI_BIAS, EPI_BIAS_GELU, EPI_BIAS_RES, EPI_NONE, MADI_F16, MADI_F32  # noqa: F401
+
+_DT = {torch.float32: MADI_F32, torch.float16: MADI_F16}
+
+
+@dataclass
+class Q8Weight:
+    """Q8_0 weight: qs int8 [n][k] + scales f16 [n][k/32] (the reference's `Q8`,
+    encoder.zig:20-21).  Both CUDA tensors, contiguous."""
+    qs: torch.Tensor
+    scales: torch.Tensor
+
+    def __post_init__(self):
+        if self.qs.dtype != torch.int8 or self.scales.dtype != torch.float16:
+            raise TypeError("Q8Weight wants qs int8 and scales float16")
+        if self.qs.dim() != 2 or self.scales.shape != (self.qs.shape[0], self.qs.shape[1] // 32):
+            raise ValueError(f"Q8Weight shapes {tuple(self.qs.shape)} / {tuple(self.scales.shape)}")
+        if not (self.qs.is_contiguous() and self.scales.is_contiguous()):
+            raise ValueError("Q8Weight tensors must be contiguous")
+
+    @property
+    def n(self) -> int:
+        return self.qs.shape[0]
+
+    @property
+    def k(self) -> int:
+        return self.qs.shape[1]
+
+    def handle(self) -> _lib.madi_q8w:
+        return _lib.madi_q8w(self.qs.data_ptr(), self.scales.data_ptr(), self.n, self.k)
+
+    def rows(self, r0: int, r1: int) -> "Q8Weight":
+        """Rows [r0, r1) -- e.g. the q / k / v thirds of a stacked [3D][D] weight."""
+        return Q8Weight(self.qs[r0:r1], self.scales[r0:r1])
+
+
+def _stream(stream) -> Optional[int]:
+    if stream is None:
+        return torch.cuda.current_stream().cuda_stream
+    return getattr(stream, "cuda_stream", stream)
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def linear(w: Q8Weight, x: torch.Tensor, bias: Optional[torch.Tensor] = None, epi: Optional[int] = None,
+           residual: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+           out_dtype: Optional[torch.dtype] = None, stream=None) -> torch.Tensor:
+    """y[m][n] = epi(x @ deq(w)^T).  x [m][k] (f16; f32 also allowed for m <= 8).
+    epi defaults to BIAS when a bias is given, BIAS_RES when a residual is given.
+    m > 8 runs the tcgen05 GEMM, m <= 8 the decode skinny GEMM."""
+    if x.dim() != 2 or x.shape[1] != w.k:
+        raise ValueError(f"x {tuple(x.shape)} vs weight k={w.k}")
+    if not x.is_contiguous():
+        raise ValueError("x must be contiguous")
+    m = x.shape[0]
+    if epi is None:
+        epi = EPI_BIAS_RES if residual is not None else (EPI_BIAS if bias is not None else EPI_NONE)
+    if out is None:
+        od = out_dtype or x.dtype
+        out = torch.empty((m, w.n), dtype=od, device=x.device)
+    if residual is not None and residual.dtype != out.dtype:
+        raise TypeError("residual must have the output's dtype")
+    bias_dt = _DT[bias.dtype] if bias is not None else MADI_F32
+    h = w.handle()
+    rc = _lib.load().madi_q8_linear(ctypes.byref(h), x.data_ptr(), _DT[x.dtype], m, _ptr(bias), bias_dt, epi,
+                                    _ptr(residual), out.data_ptr(), _DT[out.dtype], _stream(stream))
+    _lib.check(rc, "madi_q8_linear")
+    return out
+
+
+def qkv(w: Q8Weight, x: torch.Tensor, qb: torch.Tensor, vb: torch.Tensor, kc: torch.Tensor, vc: torch.Tensor,
+        pos: torch.Tensor, q_out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+    """Fused decoder QKV (gemv_q8_qkv).  x f32 [m][D]; kc/vc f32 [m][max_tok][D]
+    (or [max_tok][D] for m == 1); pos u32/int32 [m] on the device."""
+    m, D = x.shape
+    if q_out is None:
+        q_out = torch.empty((m, D), dtype=torch.float32, device=x.device)
+    stride = kc.stride(0) if kc.dim() == 3 else 0
+    h = w.handle()
+    rc = _lib.load().madi_q8_qkv(ctypes.byref(h), x.data_ptr(), m, qb.data_ptr(), vb.data_ptr(), q_out.data_ptr(),
+                                 kc.data_ptr(), vc.data_ptr(), pos.data_ptr(), stride, _stream(stream))
+    _lib.check(rc, "madi_q8_qkv")
+    return q_out
+
+
+def dequant_f16(w: Q8Weight, out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+    """dequant_q8_f16: f16 [k][n] = half(q * s), transposed."""
+    if out is None:
+        out = torch.empty((w.k, w.n), dtype=torch.float16, device=w.qs.device)
+    h = w.handle()
+    _lib.check(_lib.load().madi_q8_dequant_f16(ctypes.byref(h), out.data_ptr(), _stream(stream)),
+               "madi_q8_dequant_f16")
+    return out
+
+
+def quantize_f16(w: torch.Tensor, stream=None) -> Q8Weight:
+    """quantInto on the device: f16 [rows][dim] -> Q8Weight."""
+    rows, dim = w.shape
+    qs = torch.empty((rows, dim), dtype=torch.int8, device=w.device)
+    sc = torch.empty((rows, dim // 32), dtype=torch.float16, device=w.device)
+    _lib.check(_lib.load().madi_q8_quantize_f16(w.data_ptr(), rows, dim, qs.data_ptr(), sc.data_ptr(),
+                                                _stream(stream)), "madi_q8_quantize_f16")
+    return Q8Weight(qs, sc)

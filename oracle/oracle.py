@@ -1,0 +1,155 @@
+"""numpy front-end for the C oracle (oracle/q8_oracle.c).
+
+TEST INFRASTRUCTURE ONLY: the checker for the CUDA path.  Only tests/,
+__graft_entry__.smoke() and bench.py's CPU legs may import this module;
+madi_b200 never does.  See q8_oracle.c's header for what each function
+restates (reference file:line) and for the parity status (quantiser pinned to
+the reference's quantize_q8.py outputs; linear / GEMV arithmetic unpinned
+restatements, because the reference's Metal kernels cannot run here).
+"""
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "_build", "libmadi_oracle.so")
+
+EPI_NONE, EPI_BIAS, EPI_BIAS_GELU, EPI_BIAS_RES = 0, 1, 2, 3
+
+_lib = None
+
+
+def build() -> str:
+    """Compile the oracle with its Makefile (idempotent)."""
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+    return LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            build()
+        L = ctypes.CDLL(LIB_PATH)
+        P, I, F = ctypes.c_void_p, ctypes.c_int, ctypes.c_float
+        L.madi_orc_h2f.argtypes, L.madi_orc_h2f.restype = [ctypes.c_uint16], F
+        L.madi_orc_f2h.argtypes, L.madi_orc_f2h.restype = [F], ctypes.c_uint16
+        L.madi_orc_quantize_q8.argtypes = [P, I, I, P, P]
+        L.madi_orc_dequant_q8_f16.argtypes = [P, P, I, I, P]
+        L.madi_orc_gelu_erf.argtypes, L.madi_orc_gelu_erf.restype = [F], F
+        L.madi_orc_linear_f16.argtypes = [P, I, I, P, P, I, P, I, P, P, P]
+        L.madi_orc_gemv_q8.argtypes = [P, I, P, P, I, I, P, I, P, P, P]
+        L.madi_orc_gemv_q8_qkv.argtypes = [P, I, P, P, I, P, P, P, P, P, P]
+        L.madi_orc_argmax.argtypes, L.madi_orc_argmax.restype = [P, I], I
+        L.madi_orc_linear_f32_baseline.argtypes = [P, I, I, P, P, I, P, I, P, P, I]
+        L.madi_orc_linear_f32_baseline.restype = I
+        L.madi_orc_max_threads.restype = I
+        _lib = L
+    return _lib
+
+
+def _p(a):
+    return None if a is None else a.ctypes.data_as(ctypes.c_void_p)
+
+
+def _c(a, dt):
+    return None if a is None else np.ascontiguousarray(a, dtype=dt)
+
+
+def quantize_q8(w_f16: np.ndarray):
+    """transcribe.zig:309-327 quantInto.  w f16 [rows][dim] -> (qs int8, scales f16)."""
+    w = _c(w_f16, np.float16)
+    rows, dim = w.shape
+    assert dim % 32 == 0
+    qs = np.empty((rows, dim), np.int8)
+    sc = np.empty((rows, dim // 32), np.uint16)
+    lib().madi_orc_quantize_q8(_p(w.view(np.uint16)), rows, dim, _p(qs), _p(sc))
+    return qs, sc.view(np.float16)
+
+
+def dequant_q8_f16(qs, scales):
+    """q8_gemm.metal:12-27: -> f16 [K][N] (transposed)."""
+    qs = _c(qs, np.int8)
+    sc = _c(scales, np.float16)
+    N, K = qs.shape
+    out = np.empty((K, N), np.uint16)
+    lib().madi_orc_dequant_q8_f16(_p(qs), _p(sc.view(np.uint16)), N, K, _p(out))
+    return out.view(np.float16)
+
+
+def gelu_erf(x: float) -> float:
+    return lib().madi_orc_gelu_erf(float(x))
+
+
+def linear_f16(X, qs, scales, bias=None, epi=EPI_NONE, residual=None, want_ref=False):
+    """Encoder linear.  Returns y_exact f64 [M][N] (and y_ref f16 if want_ref)."""
+    X = _c(X, np.float16)
+    qs = _c(qs, np.int8)
+    sc = _c(scales, np.float16)
+    M, K = X.shape
+    N = qs.shape[0]
+    b = _c(bias, np.float32)
+    r = _c(residual, np.float16)
+    y = np.empty((M, N), np.float64)
+    yr = np.empty((M, N), np.uint16) if want_ref else None
+    lib().madi_orc_linear_f16(_p(X.view(np.uint16)), M, K, _p(qs), _p(sc.view(np.uint16)), N, _p(b), epi,
+                              None if r is None else _p(r.view(np.uint16)), _p(y), _p(yr))
+    return (y, yr.view(np.float16)) if want_ref else y
+
+
+def gemv_q8(x, qs, scales, bias=None, epi=EPI_NONE, res_in=None, want_ref=False):
+    """Decode GEMV family in f32 semantics.  x f32 [M][K] -> f64 [M][N] (+ f32 ref)."""
+    x = _c(np.atleast_2d(x), np.float32)
+    qs = _c(qs, np.int8)
+    sc = _c(scales, np.float16)
+    M, K = x.shape
+    N = qs.shape[0]
+    b = _c(bias, np.float32)
+    r = _c(res_in, np.float32)
+    y = np.empty((M, N), np.float64)
+    yr = np.empty((M, N), np.float32) if want_ref else None
+    lib().madi_orc_gemv_q8(_p(x), M, _p(qs), _p(sc.view(np.uint16)), N, K, _p(b), epi, _p(r), _p(y), _p(yr))
+    return (y, yr) if want_ref else y
+
+
+def gemv_q8_qkv(x, qs, scales, qb, vb, pos, cache_rows):
+    """graph_helpers.metal:527-567.  Returns (q f64 [M][D], kc f64 [rows][D], vc f64 [rows][D]);
+    cache rows not written stay NaN."""
+    x = _c(np.atleast_2d(x), np.float32)
+    qs = _c(qs, np.int8)
+    sc = _c(scales, np.float16)
+    M, D = x.shape
+    pos = _c(pos, np.uint32)
+    q = np.empty((M, D), np.float64)
+    kc = np.full((cache_rows, D), np.nan)
+    vc = np.full((cache_rows, D), np.nan)
+    lib().madi_orc_gemv_q8_qkv(_p(x), M, _p(qs), _p(sc.view(np.uint16)), D, _p(_c(qb, np.float32)),
+                               _p(_c(vb, np.float32)), _p(pos), _p(q), _p(kc), _p(vc))
+    return q, kc, vc
+
+
+def argmax(logits) -> int:
+    l = _c(logits, np.float32)
+    return lib().madi_orc_argmax(_p(l), l.size)
+
+
+def linear_f32_baseline(X, qs, scales, bias=None, epi=EPI_NONE, residual=None, nthreads=None):
+    """The reference's CPU loop (f32 dequant + accumulate) -- the timed CPU baseline."""
+    X = _c(X, np.float16)
+    qs = _c(qs, np.int8)
+    sc = _c(scales, np.float16)
+    M, K = X.shape
+    N = qs.shape[0]
+    y = np.empty((M, N), np.uint16)
+    nt = nthreads or lib().madi_orc_max_threads()
+    r = _c(residual, np.float16)
+    lib().madi_orc_linear_f32_baseline(_p(X.view(np.uint16)), M, K, _p(qs), _p(sc.view(np.uint16)), N,
+                                       _p(_c(bias, np.float32)), epi,
+                                       None if r is None else _p(r.view(np.uint16)), _p(y), nt)
+    return y.view(np.float16)
+
+
+def max_threads() -> int:
+    return lib().madi_orc_max_threads()
