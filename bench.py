@@ -80,8 +80,8 @@ def load_traffic(name):
 class ClockSampler:
     """nvidia-smi samples every 200 ms while the timed region runs."""
 
-    def __init__(self, bus_id):
-        self.bus_id = (bus_id or "").lower()
+    def __init__(self, bus_num):
+        self.bus_num = bus_num          # PCI bus number of this rank's GPU (torch device property)
         self.rows, self.proc, self.thr = [], None, None
 
     def start(self):
@@ -110,7 +110,12 @@ class ClockSampler:
                 self.proc.kill()
         if self.thr:
             self.thr.join(timeout=5)
-        mine = [r for r in self.rows if not self.bus_id or r[0].lower().endswith(self.bus_id[-12:])] or self.rows
+        def bus(r):
+            try:
+                return int(r[0].split(":")[1], 16)
+            except (IndexError, ValueError):
+                return None
+        mine = [r for r in self.rows if self.bus_num is None or bus(r) == self.bus_num] or self.rows
         if not mine:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
         sm = [float(r[1]) for r in mine if r[1].replace(".", "").isdigit()]
@@ -244,7 +249,7 @@ def main_madi(args, world, rank, local):
     evs = [torch.cuda.Event(enable_timing=True) for _ in range(2 * K + 1)]
     bus = None
     try:
-        bus = torch.cuda.get_device_properties(dev).pci_bus_id
+        bus = int(torch.cuda.get_device_properties(dev).pci_bus_id)
     except Exception:
         pass
     sampler = ClockSampler(bus).start()
@@ -337,14 +342,10 @@ def decode_leg(args, world, rank, dev, stream, peaks):
     """One decoder token step's Q8 projections for M token slots, CUDA-graph replayed."""
     import numpy as np
     import torch
-    import torch.distributed as dist
-
-    from madi_b200 import q8, synth
+    from madi_b200 import q8, shard, synth
 
     Md = args.decode_m
-    shard = (V + world - 1) // world
-    h0 = rank * shard
-    h1 = min(V, h0 + shard)
+    h0, h1 = shard.vocab_shard(V, world, rank)
 
     def t(a):
         return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
@@ -400,7 +401,6 @@ def decode_leg(args, world, rank, dev, stream, peaks):
             with torch.cuda.graph(g, stream=stream, capture_error_mode="thread_local"):
                 token_step(*s)
             graphs.append(g)
-    gathered = torch.empty((world, Md, shard), dtype=torch.float32, device=dev) if world > 1 else None
     K = max(10, args.steps)
     for i in range(4):
         graphs[i % 2].replay()
@@ -416,14 +416,14 @@ def decode_leg(args, world, rank, dev, stream, peaks):
     ms = e0.elapsed_time(e1) / K
     ag_ms = None
     if world > 1:
-        # column-split head: gather every rank's logit shard (NCCL over NVLink)
-        pad = torch.zeros((Md, shard), dtype=torch.float32, device=dev)
+        # column-split head: gather every rank's logit shard (NCCL over NVLink) and
+        # take the greedy tokens, as the multi-GPU decode step does
         a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a0.record()
         for i in range(K):
             graphs[i % 2].replay()
-            pad[:, :hn].copy_(logits)
-            dist.all_gather_into_tensor(gathered, pad)
+            full = shard.allgather_logits(logits, V, world)
+            shard.greedy_tokens(full)
         a1.record()
         torch.cuda.synchronize()
         ag_ms = max_over_ranks(world, a0.elapsed_time(a1) / K)

@@ -95,12 +95,14 @@ class Arg:
     """One kernel argument: a pointer to its value plus the value's size.
 
     Arg.buf(device_ptr) boxes a pointer-sized value; Arg.u32(n) / Arg.f32(v)
-    box scalars.  The box is kept alive by the Arg object."""
+    box scalars.  The box -- and, for Arg.buf(tensor), the tensor that owns the
+    memory -- is kept alive by the Arg object, so a temporary tensor cannot be
+    freed (and its memory reused) before the dispatch."""
 
-    __slots__ = ("box", "size")
+    __slots__ = ("box", "size", "owner")
 
-    def __init__(self, box, size):
-        self.box, self.size = box, size
+    def __init__(self, box, size, owner=None):
+        self.box, self.size, self.owner = box, size, owner
 
     @property
     def ptr(self):
@@ -109,7 +111,7 @@ class Arg:
     @classmethod
     def buf(cls, p) -> "Arg":
         v = p.data_ptr() if hasattr(p, "data_ptr") else int(p)
-        return cls(ctypes.c_void_p(v), ctypes.sizeof(ctypes.c_void_p))
+        return cls(ctypes.c_void_p(v), ctypes.sizeof(ctypes.c_void_p), owner=p)
 
     @classmethod
     def u32(cls, v: int) -> "Arg":

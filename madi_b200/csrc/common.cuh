@@ -41,21 +41,30 @@ MADI_DEV uint32_t h2_as_u32(__half2 h) { return *reinterpret_cast<uint32_t *>(&h
 
 // 0.5 x (1 + erf(x / sqrt 2)), erf from A&S 7.1.26 (|eps| <= 1.5e-7) with
 // exp2(max(-z^2 log2 e, -80)): the reference's GELU formula, restated.
-// The reciprocal and exp2 use the hardware approximations; their error is
-// far below the 2e-3 x RMS output tolerance.
+// Written as 0.5 x + 0.5 |x| erf(|z|) (erf is odd, so sign(x) x = |x|).  The
+// reciprocal and exp2 are the single hardware approximations (rcp.approx,
+// ex2.approx); their error is far below the 2e-3 x RMS output tolerance.
+MADI_DEV float rcp_approx(float v) {
+    float r;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(v));
+    return r;
+}
+MADI_DEV float ex2_approx(float v) {
+    float r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(v));
+    return r;
+}
 MADI_DEV float gelu_erf(float xv) {
-    const float z = xv * 0.7071067811865476f;
-    const float az = fabsf(z);
-    const float t = __fdividef(1.0f, fmaf(az, 0.3275911f, 1.0f));
+    const float az = fabsf(xv) * 0.7071067811865476f;
+    const float t = rcp_approx(fmaf(az, 0.3275911f, 1.0f));
     float poly = fmaf(1.061405429f, t, -1.453152027f);
     poly = fmaf(poly, t, 1.421413741f);
     poly = fmaf(poly, t, -0.284496736f);
     poly = fmaf(poly, t, 0.254829592f);
     poly = poly * t;
-    const float ex = exp2f(fmaxf(-az * az * 1.4426950408889634f, -80.0f));
-    const float e = 1.0f - poly * ex;
-    const float erf = z < 0.0f ? -e : e;
-    return 0.5f * xv * (1.0f + erf);
+    const float ex = ex2_approx(fmaxf(az * az * -1.4426950408889634f, -80.0f));
+    const float erf_abs = fmaf(-poly, ex, 1.0f);
+    return fmaf(0.5f * fabsf(xv), erf_abs, 0.5f * xv);
 }
 
 // ------------------------------------------------------------------ shared / mbarrier

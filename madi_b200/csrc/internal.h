@@ -19,7 +19,7 @@ struct GemvArgs {
     void *y;                 // [M][N] f32 or f16 (QKV: q_out f32 [M][D])
     const void *residual;    // [M][N], y's type (EPI_BIAS_RES)
     const void *bias;        // [N] f32 or f16
-    int N, K, M, ks;
+    int N, K, M, ks;         // ks = thread-block cluster size along K (1, 2, 4, 8)
     int bias_f16;
     // QKV fusion (gemv_q8_qkv)
     const float *qb, *vb;
@@ -29,7 +29,7 @@ struct GemvArgs {
     int D;
 };
 int gemv_pick_ks(int N, int K, int num_sms);
-size_t gemv_smem_bytes(int M, int K, bool x_f32);
+size_t gemv_smem_bytes(int M, int K, int cs, bool x_f32);
 cudaError_t launch_gemv(const GemvArgs &a, bool x_f32, bool y_f32, int epi, bool qkv, cudaStream_t st, bool pdl);
 
 // ---------------------------------------------------------------- variant (a)

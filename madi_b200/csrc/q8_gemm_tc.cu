@@ -19,8 +19,9 @@
 //   * the f32 accumulator (128 weight rows x BT tokens) sits in TMEM, double
 //     buffered so the epilogue of tile i overlaps the MMAs of tile i+1.
 //
-// Warp roles (384 threads): w0 TMA producer, w1 MMA issuer + TMEM owner,
-// w2-3 idle, w4-7 dequant (TMEM lane quarter = warp % 4), w8-11 epilogue.
+// Warp roles (512 threads): w0 TMA producer, w1 MMA issuer + TMEM owner,
+// w2-3 idle, w4-11 dequant in two groups of four that take alternate stages
+// (TMEM lane quarter = warp % 4), w12-15 epilogue.
 // TMEM columns: [0, 2*BT) accumulators, then STAGES x 32 columns of A.
 // Every mbarrier wait is bounded; on expiry the CTA raises its abort flag,
 // records the device error word, drains its in-flight copies and MMAs,
@@ -41,7 +42,9 @@ constexpr int STAGES = 4;
 constexpr int W_STAGE = BN * BK;           // int8 bytes
 constexpr int A_STAGE_COLS = BK / 2;       // f16 pairs per TMEM column
 constexpr int TMEM_COLS = 512;
-constexpr int kThreads = 384;
+constexpr int kDqWarp0 = 4;                // warps 4..11: dequant (two groups of four)
+constexpr int kEpiWarp0 = 12;              // warps 12..15: epilogue
+constexpr int kThreads = 512;
 
 template <int BT> struct Cfg {
     static constexpr int X_STAGE = BT * BK * 2;   // f16 bytes
@@ -55,7 +58,7 @@ template <int BT> struct Cfg {
 
 struct __align__(8) Bars {
     uint64_t full[STAGES];     // TMA bytes landed (X + W)
-    uint64_t aready[STAGES];   // dequantised A written to TMEM (128 arrivals)
+    uint64_t aready[STAGES];   // dequantised A written to TMEM (128 arrivals: one dequant group)
     uint64_t empty[STAGES];    // MMAs of the stage done (tcgen05.commit)
     uint64_t accfull[2];       // accumulator ready (tcgen05.commit)
     uint64_t accempty[2];      // epilogue drained the accumulator (128 arrivals)
@@ -78,6 +81,39 @@ MADI_DEV void mbar_wait_drain(uint64_t *bar, uint32_t parity) {
     const long long t0 = clock64();
     while (!mbar_try_wait(bar, parity))
         if (clock64() - t0 > kWaitBudgetCycles) return;
+}
+
+// 32 consecutive tokens (m) of one output feature (n): y[m][n] for m in [mb, mb+32).
+template <int EPI>
+MADI_DEV void epilogue_chunk(const GemmArgs &p, const uint32_t (&v)[32], int mb, int n, float bias) {
+    const int N = p.N;
+    const size_t base = (size_t)mb * N + n;
+    if (mb + 32 <= p.M) {
+        float res[32];
+        if constexpr (EPI == kEpiBiasRes) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) res[i] = __half2float(p.residual[base + (size_t)i * N]);
+        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            float y = __uint_as_float(v[i]);
+            if constexpr (EPI == kEpiBias) y += bias;
+            if constexpr (EPI == kEpiBiasGelu) y = gelu_erf(y + bias);
+            if constexpr (EPI == kEpiBiasRes) y = y + bias + res[i];
+            p.y[base + (size_t)i * N] = __float2half_rn(y);
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            if (mb + i < p.M) {
+                float y = __uint_as_float(v[i]);
+                if constexpr (EPI == kEpiBias) y += bias;
+                if constexpr (EPI == kEpiBiasGelu) y = gelu_erf(y + bias);
+                if constexpr (EPI == kEpiBiasRes) y = y + bias + __half2float(p.residual[base + (size_t)i * N]);
+                p.y[base + (size_t)i * N] = __float2half_rn(y);
+            }
+        }
+    }
 }
 
 template <int BT, int EPI>
@@ -181,49 +217,75 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_wait_drain(&bars->drain, 0);
         }
         __syncwarp();
-    } else if (warp >= 4 && warp < 8) {
+    } else if (warp >= kDqWarp0 && warp < kEpiWarp0) {
         // ------------------------------------------------ dequant: int8 smem -> f16 TMEM
+        // Two groups of four warps take alternate pipeline stages; within a
+        // group, warp % 4 selects the TMEM lane quarter and lane = weight row.
+        const int grp = (warp - kDqWarp0) >> 2;
         const int q = warp & 3;
         const int r = q * 32 + lane;            // weight row within the tile = TMEM lane
         const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
         const int swz = (r >> 1) & 3;           // SWIZZLE_64B: 16-byte chunk c lives at c ^ swz
-        int s = 0;
-        uint32_t ph = 0;
-        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+        const bool pair_ok = (nkb & 1) == 0;    // both block scales of a stage in one aligned word
+
+        // f16 scale pair (blocks 2kt, 2kt+1) of this thread's row at global stage `it`
+        auto scale_word = [&](int it) -> uint32_t {
+            const int lt = it / KT, kt = it - lt * KT;
+            const int tile = blockIdx.x + lt * gridDim.x;
+            if (tile >= num_tiles) return 0u;
             const int n = (tile % n_tiles) * BN + r;
-            const bool nok = n < N;
-            const __half *srow = p.scales + (size_t)(nok ? n : 0) * nkb;
-            for (int kt = 0; kt < KT; ++kt) {
-                const int kb = kt * 2;
-                const __half sc0 = (nok && kb < nkb) ? srow[kb] : __ushort_as_half(0);
-                const __half sc1 = (nok && kb + 1 < nkb) ? srow[kb + 1] : __ushort_as_half(0);
-                if (!warp_wait(&bars->full[s], ph, abort_flag, err)) goto dequant_done;
-                {
-                    const uint8_t *wrow = ws + s * W_STAGE + r * 64;
-                    uint32_t a[32];
+            if (n >= N) return 0u;
+            const int kb = 2 * kt;
+            const __half *sp = p.scales + (size_t)n * nkb + kb;
+            if (pair_ok) return __ldg(reinterpret_cast<const unsigned int *>(sp));
+            const uint32_t lo = kb < nkb ? __half_as_ushort(__ldg(sp)) : 0u;
+            const uint32_t hi = kb + 1 < nkb ? __half_as_ushort(__ldg(sp + 1)) : 0u;
+            return lo | (hi << 16);
+        };
+        // dequantise global stage `it` with scale pair `sw`; false when done or aborted
+        auto visit = [&](int it, uint32_t sw) -> bool {
+            const int lt = it / KT;
+            if (blockIdx.x + lt * gridDim.x >= num_tiles) return false;
+            const int s = it % STAGES;
+            const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
+            if (!warp_wait(&bars->full[s], ph, abort_flag, err)) return false;
+            const __half2 sw2 = *reinterpret_cast<const __half2 *>(&sw);
+            const __half2 sc_lo = __low2half2(sw2), sc_hi = __high2half2(sw2);
+            const uint8_t *wrow = ws + s * W_STAGE + r * 64;
+            uint32_t a[32];
 #pragma unroll
-                    for (int c = 0; c < 4; ++c) {
-                        const uint4 v = *reinterpret_cast<const uint4 *>(wrow + ((c ^ swz) << 4));
-                        const __half2 sc = __half2half2(c < 2 ? sc0 : sc1);
-                        const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+            for (int c = 0; c < 4; ++c) {
+                const uint4 v = *reinterpret_cast<const uint4 *>(wrow + ((c ^ swz) << 4));
+                const __half2 sc = c < 2 ? sc_lo : sc_hi;
+                const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-                        for (int i = 0; i < 4; ++i) {
-                            __half2 lo, hi;
-                            q8_to_half2x2(wv[i], lo, hi);
-                            a[c * 8 + 2 * i] = h2_as_u32(__hmul2(lo, sc));
-                            a[c * 8 + 2 * i + 1] = h2_as_u32(__hmul2(hi, sc));
-                        }
-                    }
-                    tmem_st32(tmem + lane_addr + C::A_COL0 + s * A_STAGE_COLS, a);
-                    tmem_wait_st();
+                for (int i = 0; i < 4; ++i) {
+                    __half2 lo, hi;
+                    q8_to_half2x2(wv[i], lo, hi);
+                    a[c * 8 + 2 * i] = h2_as_u32(__hmul2(lo, sc));      // half(q*s): one rounding
+                    a[c * 8 + 2 * i + 1] = h2_as_u32(__hmul2(hi, sc));
                 }
-                tc_fence_before();
-                mbar_arrive(&bars->aready[s]);
-                if (++s == STAGES) { s = 0; ph ^= 1; }
             }
+            tmem_st32(tmem + lane_addr + C::A_COL0 + s * A_STAGE_COLS, a);
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(&bars->aready[s]);
+            return true;
+        };
+        // this group visits stages grp, grp+2, ...; scales are fetched two
+        // visits (four stages) ahead so their L2 latency is off the critical path
+        int it = grp;
+        uint32_t sA = scale_word(it), sB = scale_word(it + 2);
+        while (true) {
+            uint32_t use = sA;
+            sA = scale_word(it + 4);
+            if (!visit(it, use)) break;
+            use = sB;
+            sB = scale_word(it + 6);
+            if (!visit(it + 2, use)) break;
+            it += 4;
         }
-    dequant_done:;
-    } else if (warp >= 8) {
+    } else if (warp >= kEpiWarp0) {
         // ------------------------------------------------ epilogue: TMEM -> bias/GELU/residual -> f16
         const int q = warp & 3;
         const int r = q * 32 + lane;
@@ -243,26 +305,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                     bias = p.bias_f16 ? __half2float(reinterpret_cast<const __half *>(p.bias)[n])
                                       : reinterpret_cast<const float *>(p.bias)[n];
             }
+            const uint32_t acc_addr = tmem + lane_addr + b * C::ACC_COLS;
+            // load -> wait -> use: no register written by an in-flight tcgen05.ld is
+            // ever live across compiler-scheduled code
 #pragma unroll 1
             for (int c = 0; c < BT / 32; ++c) {
                 uint32_t v[32];
-                tmem_ld32(tmem + lane_addr + b * C::ACC_COLS + c * 32, v);
+                tmem_ld32(acc_addr + c * 32, v);
                 tmem_wait_ld();
-                const int mb = m0 + c * 32;
-                if (nok) {
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        const int m = mb + i;
-                        if (m < M) {
-                            float y = __uint_as_float(v[i]);
-                            if constexpr (EPI == kEpiBias) y += bias;
-                            if constexpr (EPI == kEpiBiasGelu) y = gelu_erf(y + bias);
-                            if constexpr (EPI == kEpiBiasRes)
-                                y = y + bias + __half2float(p.residual[(size_t)m * N + n]);
-                            p.y[(size_t)m * N + n] = __float2half_rn(y);
-                        }
-                    }
-                }
+                if (nok) epilogue_chunk<EPI>(p, v, m0 + c * 32, n, bias);
             }
             tc_fence_before();
             mbar_arrive(&bars->accempty[b]);
@@ -282,8 +333,12 @@ cudaError_t launch_bt(const GemmArgs &a, const CUtensorMap &tmX, const CUtensorM
                       cudaStream_t st) {
     using C = Cfg<BT>;
     auto fn = q8_gemm_tc_kernel<BT, EPI>;
-    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
-    if (e != cudaSuccess) return e;
+    static bool attr_set = false;   // once per instantiation: launches inside a capture stay pure launches
+    if (!attr_set) {
+        cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
+        if (e != cudaSuccess) return e;
+        attr_set = true;
+    }
     const int tiles = ((a.N + BN - 1) / BN) * ((a.M + BT - 1) / BT);
     const int grid = tiles < num_sms ? tiles : num_sms;
     fn<<<grid, kThreads, C::SMEM, st>>>(tmX, tmW, a);

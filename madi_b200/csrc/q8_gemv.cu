@@ -14,36 +14,51 @@
 // so that each lane reads 8 CONTIGUOUS int8 of a row per block:
 //   lane (g = lane/4, t = lane%4) owns physical k = 8t .. 8t+7 of the block;
 //   step s uses 8t+4s .. 8t+4s+3; A slots {2t,2t+1} <- k+0,1 and {2t+8,2t+9} <- k+2,3.
-// The activations are staged once per CTA in shared memory already permuted
-// into that fragment order, so every B-fragment read is one conflict-free
-// 8-byte load.
+// The activations are staged per CTA in shared memory already permuted into
+// that fragment order, so every B-fragment read is one conflict-free 8-byte load.
 //
-// Work split: a CTA is 8 warps; `ks` warps share one 16-row tile and split
-// its K blocks (ks in {1,2,4,8}); partial sums meet in shared memory and are
-// added in a fixed order (deterministic, no atomics, no global scratch).
+// Work split: a CTA is 8 warps, one 16-row tile each (128 rows).  A thread-
+// block cluster of `cs` CTAs (1..16) shares the same 128 rows and splits K:
+// CTA rank r streams K blocks [r*bpw, (r+1)*bpw) and stages only that slice of
+// x.  The partial sums meet in the rank-0 CTA through distributed shared
+// memory and are added in rank order (deterministic, no atomics, no global
+// scratch).
+//
+// Streaming: a decode GEMV moves only a few MB, so it is latency-bound unless
+// the whole matrix is in flight at once.  Each warp therefore requests ALL of
+// its slice (bpw <= kMaxB blocks: 16 rows x bpw x 32 bytes) in one round, and
+// does so before griddepcontrol.wait: the weights do not depend on the
+// previous kernel, so under programmatic dependent launch they stream while
+// that kernel drains.
+#include <cooperative_groups.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
 
 #include "common.cuh"
 #include "internal.h"
 
+namespace cg = cooperative_groups;
+
 namespace madi {
 namespace {
 
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
-constexpr int kUnroll = 4;   // Q8 blocks in flight per warp iteration
+constexpr int kRows = 16 * kWarps;   // weight rows per CTA
+constexpr int kMaxB = 10;            // Q8 blocks a warp keeps in flight (one round)
+constexpr int kMaxCluster = 16;      // non-portable cluster size, allowed on sm_100
 
 MADI_DEV uint2 ldg_stream_u2(const void *p) {
     uint2 v;
-    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+    // not volatile: the weights are read-only for the kernel's lifetime, so the
+    // compiler may schedule these loads freely around the MMA chains
+    asm("ld.global.nc.L1::no_allocate.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
     return v;
 }
 MADI_DEV float ldg_half(const __half *p) { return __half2float(__ldg(p)); }
 
 MADI_DEV void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
@@ -56,74 +71,86 @@ template <typename T> MADI_DEV T from_f32(float v);
 template <> MADI_DEV float from_f32<float>(float v) { return v; }
 template <> MADI_DEV __half from_f32<__half>(float v) { return __float2half_rn(v); }
 
-// Stage x [M][K] into shared memory in fragment order.  Slot for (kb, s, m, t)
-// holds x[m][kb*32 + 8t + 4s + 0..3] as four f16.
+// Stage x[m][k] for k in this CTA's slice [kb_begin*32, kb_end*32) into shared
+// memory in fragment order: slot (lkb, s, m, t) holds x[m][(kb_begin+lkb)*32 +
+// 8t + 4s + 0..3] as four f16.  Loads are issued in batches of 8 per thread so
+// the L2 round trips overlap.
 template <typename XT, bool kSplit>
-MADI_DEV void stage_x(const XT *__restrict__ x, int M, int K, uint2 *xf_hi, uint2 *xf_lo) {
-    const int nquads = M * K / 4;
-    for (int i = threadIdx.x; i < nquads; i += kThreads) {
-        const int m = (4 * i) / K, k = (4 * i) % K;
-        const int kb = k >> 5, t = (k & 31) >> 3, s = (k & 7) >> 2;
-        const int slot = ((kb * 2 + s) * M + m) * 4 + t;
-        float v[4];
-        if constexpr (sizeof(XT) == 4) {
-            const float4 f = __ldg(reinterpret_cast<const float4 *>(x) + i);
-            v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
-        } else {
-            const uint2 u = __ldg(reinterpret_cast<const uint2 *>(x) + i);
-            const __half2 h0 = *reinterpret_cast<const __half2 *>(&u.x), h1 = *reinterpret_cast<const __half2 *>(&u.y);
-            v[0] = __low2float(h0); v[1] = __high2float(h0); v[2] = __low2float(h1); v[3] = __high2float(h1);
+MADI_DEV void stage_x(const XT *__restrict__ x, int M, int K, int kb_begin, int kb_end, uint2 *xf_hi,
+                      uint2 *xf_lo) {
+    constexpr int B = 8;
+    const int qrow = (kb_end - kb_begin) * 8;   // quads of 4 elements per token row
+    const int nq = M * qrow;
+    for (int base = threadIdx.x; base < nq; base += B * kThreads) {
+        float v[B][4];
+#pragma unroll
+        for (int j = 0; j < B; ++j) {
+            const int i = base + j * kThreads;
+            if (i < nq) {
+                const int m = i / qrow, kq = i - m * qrow;
+                const size_t off = (size_t)m * K + (size_t)kb_begin * 32 + 4 * kq;
+                if constexpr (sizeof(XT) == 4) {
+                    const float4 f = __ldg(reinterpret_cast<const float4 *>(x + off));
+                    v[j][0] = f.x; v[j][1] = f.y; v[j][2] = f.z; v[j][3] = f.w;
+                } else {
+                    const uint2 u = __ldg(reinterpret_cast<const uint2 *>(x + off));
+                    const __half2 h0 = *reinterpret_cast<const __half2 *>(&u.x);
+                    const __half2 h1 = *reinterpret_cast<const __half2 *>(&u.y);
+                    v[j][0] = __low2float(h0); v[j][1] = __high2float(h0);
+                    v[j][2] = __low2float(h1); v[j][3] = __high2float(h1);
+                }
+            }
         }
-        __half2 h01 = __floats2half2_rn(v[0], v[1]), h23 = __floats2half2_rn(v[2], v[3]);
-        xf_hi[slot] = make_uint2(h2_as_u32(h01), h2_as_u32(h23));
-        if constexpr (kSplit) {
-            __half2 l01 = __floats2half2_rn(v[0] - __low2float(h01), v[1] - __high2float(h01));
-            __half2 l23 = __floats2half2_rn(v[2] - __low2float(h23), v[3] - __high2float(h23));
-            xf_lo[slot] = make_uint2(h2_as_u32(l01), h2_as_u32(l23));
+#pragma unroll
+        for (int j = 0; j < B; ++j) {
+            const int i = base + j * kThreads;
+            if (i < nq) {
+                const int m = i / qrow, kq = i - m * qrow;
+                const int lkb = kq >> 3, t = (kq & 7) >> 1, s = kq & 1;
+                const int slot = ((lkb * 2 + s) * M + m) * 4 + t;
+                const __half2 h01 = __floats2half2_rn(v[j][0], v[j][1]), h23 = __floats2half2_rn(v[j][2], v[j][3]);
+                xf_hi[slot] = make_uint2(h2_as_u32(h01), h2_as_u32(h23));
+                if constexpr (kSplit) {
+                    const __half2 l01 = __floats2half2_rn(v[j][0] - __low2float(h01), v[j][1] - __high2float(h01));
+                    const __half2 l23 = __floats2half2_rn(v[j][2] - __low2float(h23), v[j][3] - __high2float(h23));
+                    xf_lo[slot] = make_uint2(h2_as_u32(l01), h2_as_u32(l23));
+                }
+            }
         }
     }
 }
 
-// out-of-range rows read as zero weights and zero scales
 template <typename XT, typename YT, int EPI, bool kQKV>
-__global__ void __launch_bounds__(kThreads) q8_gemv_kernel(const GemvArgs p) {
+__global__ void __launch_bounds__(kThreads, 2) q8_gemv_kernel(const GemvArgs p) {
     constexpr bool kSplit = sizeof(XT) == 4;
     extern __shared__ __align__(16) uint8_t smem[];
-    const int M = p.M, K = p.K, N = p.N, ks = p.ks;
+    const int M = p.M, K = p.K, N = p.N, cs = p.ks;
     const int nkb = K >> 5;
+    const int bpw = (nkb + cs - 1) / cs;                          // blocks per CTA (and per warp)
+    const int rank = cs > 1 ? (int)(blockIdx.x % cs) : 0;        // cluster rank along x
+    const int group = cs > 1 ? (int)(blockIdx.x / cs) : (int)blockIdx.x;
+    const int kb_begin = min(nkb, rank * bpw);
+    const int kb_end = min(nkb, kb_begin + bpw);
+    const size_t slot_count = (size_t)(kb_end - kb_begin) * 8 * M;   // uint2 slots per half
     uint2 *xf_hi = reinterpret_cast<uint2 *>(smem);
-    uint2 *xf_lo = xf_hi + (size_t)M * K / 4;
-    float4 *red = reinterpret_cast<float4 *>(smem + (size_t)M * K * (kSplit ? 4 : 2));
-
-    // griddepcontrol: the weights do not depend on the previous kernel, so
-    // with programmatic dependent launch only the activation read waits.
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    stage_x<XT, kSplit>(reinterpret_cast<const XT *>(p.x), M, K, xf_hi, xf_lo);
-    __syncthreads();
+    uint2 *xf_lo = xf_hi + slot_count;
+    float4 *red = reinterpret_cast<float4 *>(smem + (size_t)bpw * 8 * 8 * (kSplit ? 16 : 8));
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, t = lane & 3;
-    const int rt = kWarps / ks;
-    const int tile = blockIdx.x * rt + warp / ks;
-    const int slice = warp % ks;
-    const int row0 = tile * 16 + g, row1 = row0 + 8;
+    const int row0 = group * kRows + warp * 16 + g, row1 = row0 + 8;
     const bool ok0 = row0 < N, ok1 = row1 < N;
-    const int kb_per = (nkb + ks - 1) / ks;
-    const int kb_begin = slice * kb_per;
-    const int kb_end = min(nkb, kb_begin + kb_per);
 
     const int8_t *w0 = p.qs + (size_t)(ok0 ? row0 : 0) * K + 8 * t;
     const int8_t *w1 = p.qs + (size_t)(ok1 ? row1 : 0) * K + 8 * t;
     const __half *s0p = p.scales + (size_t)(ok0 ? row0 : 0) * nkb;
     const __half *s1p = p.scales + (size_t)(ok1 ? row1 : 0) * nkb;
-    const bool gval = g < M;
 
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int kb0 = kb_begin; kb0 < kb_end; kb0 += kUnroll) {
-        uint2 wa[kUnroll], wb[kUnroll];
-        float sa[kUnroll], sb[kUnroll];
+    uint2 wa[kMaxB], wb[kMaxB];
+    float sa[kMaxB], sb[kMaxB];
+    auto load_round = [&](int kb0) {
 #pragma unroll
-        for (int u = 0; u < kUnroll; ++u) {
+        for (int u = 0; u < kMaxB; ++u) {
             const int kb = kb0 + u;
             const bool in = kb < kb_end;
             wa[u] = (in && ok0) ? ldg_stream_u2(w0 + (size_t)kb * 32) : make_uint2(0u, 0u);
@@ -131,8 +158,21 @@ __global__ void __launch_bounds__(kThreads) q8_gemv_kernel(const GemvArgs p) {
             sa[u] = (in && ok0) ? ldg_half(s0p + kb) : 0.f;
             sb[u] = (in && ok1) ? ldg_half(s1p + kb) : 0.f;
         }
+    };
+
+    // the whole slice of weights first, before waiting on the kernel that produced x
+    load_round(kb_begin);
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    stage_x<XT, kSplit>(reinterpret_cast<const XT *>(p.x), M, K, kb_begin, kb_end, xf_hi, xf_lo);
+    __syncthreads();
+
+    const bool gval = g < M;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int kb0 = kb_begin; kb0 < kb_end; kb0 += kMaxB) {
+        if (kb0 != kb_begin) load_round(kb0);   // only when a slice exceeds kMaxB blocks
 #pragma unroll
-        for (int u = 0; u < kUnroll; ++u) {
+        for (int u = 0; u < kMaxB; ++u) {
             const int kb = kb0 + u;
             if (kb >= kb_end) break;
             float blk[4] = {0.f, 0.f, 0.f, 0.f};
@@ -142,11 +182,11 @@ __global__ void __launch_bounds__(kThreads) q8_gemv_kernel(const GemvArgs p) {
                 q8_to_half2x2(s == 0 ? wa[u].x : wa[u].y, a_lo0, a_hi0);
                 q8_to_half2x2(s == 0 ? wb[u].x : wb[u].y, a_lo1, a_hi1);
                 const uint32_t a[4] = {h2_as_u32(a_lo0), h2_as_u32(a_lo1), h2_as_u32(a_hi0), h2_as_u32(a_hi1)};
-                const int slot = ((kb * 2 + s) * M + g) * 4 + t;
-                uint2 bh = gval ? xf_hi[slot] : make_uint2(0u, 0u);
+                const int slot = (((kb - kb_begin) * 2 + s) * M + g) * 4 + t;
+                const uint2 bh = gval ? xf_hi[slot] : make_uint2(0u, 0u);
                 mma16816(blk, a, bh.x, bh.y);
                 if constexpr (kSplit) {
-                    uint2 bl = gval ? xf_lo[slot] : make_uint2(0u, 0u);
+                    const uint2 bl = gval ? xf_lo[slot] : make_uint2(0u, 0u);
                     mma16816(blk, a, bl.x, bl.y);
                 }
             }
@@ -157,17 +197,20 @@ __global__ void __launch_bounds__(kThreads) q8_gemv_kernel(const GemvArgs p) {
         }
     }
 
-    if (ks > 1) {
+    if (cs > 1) {
+        // cross-CTA split-K: partials meet in the rank-0 CTA through DSMEM
         red[warp * 32 + lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-        __syncthreads();
-        if (slice != 0) return;
-        for (int j = 1; j < ks; ++j) {
-            const float4 o = red[(warp + j) * 32 + lane];
-            acc[0] += o.x; acc[1] += o.y; acc[2] += o.z; acc[3] += o.w;
+        cg::cluster_group cluster = cg::this_cluster();
+        cluster.sync();
+        if (rank == 0) {
+            for (int j = 1; j < cs; ++j) {
+                const float4 o = cluster.map_shared_rank(red, j)[warp * 32 + lane];
+                acc[0] += o.x; acc[1] += o.y; acc[2] += o.z; acc[3] += o.w;
+            }
         }
+        cluster.sync();   // remote shared memory stays alive until it has been read
+        if (rank != 0) return;
     }
-    // allow the next kernel in the stream to start its weight prefetch
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     // C fragment: acc[0..1] = (row0, tokens 2t, 2t+1), acc[2..3] = (row1, ...)
 #pragma unroll
@@ -201,41 +244,69 @@ __global__ void __launch_bounds__(kThreads) q8_gemv_kernel(const GemvArgs p) {
 
 template <typename XT, typename YT, int EPI, bool kQKV>
 cudaError_t launch_one(const GemvArgs &a, cudaStream_t st, bool pdl) {
-    const size_t xbytes = (size_t)a.M * a.K * (sizeof(XT) == 4 ? 4 : 2);
-    const size_t smem = xbytes + (size_t)kThreads * 16;
+    const size_t smem = gemv_smem_bytes(a.M, a.K, a.ks, sizeof(XT) == 4);
     auto fn = q8_gemv_kernel<XT, YT, EPI, kQKV>;
-    if (smem > 48 * 1024) {
+    // raise the dynamic shared-memory cap once per instantiation (to the
+    // largest ever needed), so a launch inside a graph capture is only a launch
+    static size_t smem_cap = 48 * 1024;
+    static bool cluster_attr = false;
+    if (smem > smem_cap) {
         cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
+        smem_cap = smem;
     }
-    const int tiles = (a.N + 15) / 16;
-    const int rt = kWarps / a.ks;
+    if (!cluster_attr && a.ks > 8) {
+        cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        if (e != cudaSuccess) return e;
+        cluster_attr = true;
+    }
+    const int groups = (a.N + kRows - 1) / kRows;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((tiles + rt - 1) / rt);
+    cfg.gridDim = dim3(groups * a.ks);
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cudaLaunchAttribute attr[2];
+    int na = 0;
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    ++na;
+    if (a.ks > 1) {
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = a.ks;
+        attr[na].val.clusterDim.y = 1;
+        attr[na].val.clusterDim.z = 1;
+        ++na;
+    }
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = na;
     return cudaLaunchKernelEx(&cfg, fn, a);
 }
 
 }  // namespace
 
+// Cluster size (cross-CTA K split): about kMaxB Q8 blocks per warp so a slice
+// is one round of loads, at most 16 CTAs per cluster -- then halved while the
+// grid would exceed ~6 CTAs per SM (large N has parallelism in rows already).
+// Measured on B200 (decode shapes, M = 1 and 8, under PDL): K = 1280 -> 4,
+// K = 5120 -> 16, vocab head (N = 51866) -> 2.
 int gemv_pick_ks(int N, int K, int num_sms) {
-    const int tiles = (N + 15) / 16;
+    const int groups = (N + kRows - 1) / kRows;
     const int nkb = K / 32;
-    const int want = num_sms * 16;   // warps in flight we aim for
-    int ks = 1;
-    while (ks < 8 && tiles * ks < want && (nkb / (ks * 2)) >= 2) ks *= 2;
-    return ks;
+    int cs = (nkb + kMaxB - 1) / kMaxB;
+    if (cs < 1) cs = 1;
+    if (cs > kMaxCluster) cs = kMaxCluster;
+    while (cs > 1 && groups * cs > 6 * num_sms) cs = (cs + 1) / 2;
+    return cs;
 }
 
-size_t gemv_smem_bytes(int M, int K, bool x_f32) {
-    return (size_t)M * K * (x_f32 ? 4 : 2) + (size_t)kThreads * 16;
+size_t gemv_smem_bytes(int M, int K, int cs, bool x_f32) {
+    const int nkb = K / 32;
+    const int bpw = (nkb + cs - 1) / cs;
+    (void)M;
+    // x slice sized for the maximum 8 token slots so every launch of an
+    // instantiation fits the same cap, plus the partial-sum exchange area
+    return (size_t)bpw * 8 * 8 * (x_f32 ? 16 : 8) + (size_t)kThreads * 16;
 }
 
 cudaError_t launch_gemv(const GemvArgs &a, bool x_f32, bool y_f32, int epi, bool qkv, cudaStream_t st, bool pdl) {

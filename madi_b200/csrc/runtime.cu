@@ -135,8 +135,8 @@ int q8_linear_impl(const madi_q8w *w, const void *x, int x_dtype, int m, const v
     }
     const bool xf32 = x_dtype == MADI_F32;
     if (!aligned(x, xf32 ? 16 : 8)) return fail(MADI_EINVAL, "%s: x must be %d-byte aligned", who, xf32 ? 16 : 8);
-    const size_t smem = gemv_smem_bytes(m, K, xf32);
-    if (smem > (size_t)S.max_smem_optin)
+    const int ks = gemv_pick_ks(N, K, S.num_sms);
+    if (gemv_smem_bytes(m, K, ks, xf32) > (size_t)S.max_smem_optin)
         return fail(MADI_EINVAL, "%s: K=%d too large for the decode path at m=%d", who, K, m);
     GemvArgs a{};
     a.qs = w->qs;
@@ -144,7 +144,7 @@ int q8_linear_impl(const madi_q8w *w, const void *x, int x_dtype, int m, const v
     a.x = x; a.y = y; a.residual = residual; a.bias = bias;
     a.bias_f16 = bias_dtype == MADI_F16;
     a.N = N; a.K = K; a.M = m;
-    a.ks = gemv_pick_ks(N, K, S.num_sms);
+    a.ks = ks;
     cudaError_t e = launch_gemv(a, xf32, y_dtype == MADI_F32, epi, false, st, S.pdl);
     if (e != cudaSuccess) return cuda_fail(e, who);
     return MADI_OK;
@@ -159,13 +159,14 @@ int q8_qkv_impl(const madi_q8w *w, const float *x, int m, const float *qb, const
     if (D <= 0 || D % 32 != 0 || w->n != 3 * D) return fail(MADI_EINVAL, "%s: qkv weight must be [3D][D], D %% 32 == 0", who);
     if (m <= 0 || m > 8) return fail(MADI_EINVAL, "%s: m=%d outside 1..8", who, m);
     if (!aligned(x, 16) || !aligned(w->qs, 16)) return fail(MADI_EINVAL, "%s: misaligned x or qs", who);
-    if (gemv_smem_bytes(m, D, true) > (size_t)S.max_smem_optin) return fail(MADI_EINVAL, "%s: D too large", who);
+    const int ks = gemv_pick_ks(3 * D, D, S.num_sms);
+    if (gemv_smem_bytes(m, D, ks, true) > (size_t)S.max_smem_optin) return fail(MADI_EINVAL, "%s: D too large", who);
     GemvArgs a{};
     a.qs = w->qs;
     a.scales = reinterpret_cast<const __half *>(w->scales);
     a.x = x; a.y = q_out;
     a.N = 3 * D; a.K = D; a.M = m;
-    a.ks = gemv_pick_ks(3 * D, D, S.num_sms);
+    a.ks = ks;
     a.qb = qb; a.vb = vb; a.kc = kc; a.vc = vc; a.pos = pos;
     a.cache_stride = m > 1 ? cache_stride : 0;
     a.D = D;

@@ -1,0 +1,63 @@
+"""Multi-GPU partitioning of the Q8 path (one process per GPU).
+
+* Chunks: independent 30 s audio chunks are split into contiguous blocks, one per rank
+  (weights replicated).  No collective touches the encoder data path.
+* Vocab head: column-split by output rows -- rank g owns rows [g*S, min(V, (g+1)*S))
+  with S = ceil(V / world).  Each rank computes logits for its rows for every token
+  slot; the shards are all-gathered (NCCL over NVLink on B200, gloo on CPU) and the
+  greedy token is the global argmax with ties broken toward the lowest vocab index.
+
+Only torch.distributed is used for the exchange; the per-rank logits come from
+madi_b200.q8.linear on the rank's own head shard.
+"""
+from typing import Tuple
+
+import torch
+
+
+def chunk_range(n_chunks: int, world: int, rank: int) -> range:
+    """Contiguous block of chunk indices owned by `rank` (sizes differ by at most 1)."""
+    base, extra = divmod(n_chunks, world)
+    start = rank * base + min(rank, extra)
+    return range(start, start + base + (1 if rank < extra else 0))
+
+
+def vocab_shard(vocab: int, world: int, rank: int) -> Tuple[int, int]:
+    """Rows [h0, h1) of the [vocab][dim] head owned by `rank`."""
+    size = (vocab + world - 1) // world
+    h0 = min(vocab, rank * size)
+    return h0, min(vocab, h0 + size)
+
+
+def allgather_logits(local: torch.Tensor, vocab: int, world: int, group=None) -> torch.Tensor:
+    """local [m][h1-h0] float32 of this rank's shard -> full logits [m][vocab] on every rank."""
+    import torch.distributed as dist
+    if world == 1:
+        return local
+    m = local.shape[0]
+    size = (vocab + world - 1) // world
+    pad = torch.zeros((m, size), dtype=local.dtype, device=local.device)
+    pad[:, :local.shape[1]] = local
+    out = torch.empty((world * m, size), dtype=local.dtype, device=local.device)   # rank-major concat
+    dist.all_gather_into_tensor(out, pad, group=group)
+    full = out.view(world, m, size).permute(1, 0, 2).reshape(m, world * size)
+    return full[:, :vocab].contiguous()
+
+
+def greedy_tokens(logits: torch.Tensor) -> torch.Tensor:
+    """Greedy token per row, lowest index on ties (torch.argmax returns the first maximum)."""
+    return torch.argmax(logits, dim=-1)
+
+
+def shard_argmax(local: torch.Tensor, h0: int) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Per-row (max value, global index) of a shard -- the cheap alternative to gathering
+    whole logit rows: gather these pairs and merge with merge_shard_argmax."""
+    v, i = torch.max(local, dim=-1)
+    return v, i + h0
+
+
+def merge_shard_argmax(values: torch.Tensor, indices: torch.Tensor) -> torch.Tensor:
+    """values/indices [world][m] -> global greedy index per row; ties -> lowest index."""
+    best = values.max(dim=0, keepdim=True).values
+    cand = torch.where(values == best, indices, torch.full_like(indices, torch.iinfo(indices.dtype).max))
+    return cand.min(dim=0).values
