@@ -64,7 +64,8 @@ MADI_DEV float gelu_erf(float xv) {
     poly = poly * t;
     const float ex = ex2_approx(fmaxf(az * az * -1.4426950408889634f, -80.0f));
     const float erf_abs = fmaf(-poly, ex, 1.0f);
-    return fmaf(0.5f * fabsf(xv), erf_abs, 0.5f * xv);
+    const float h = 0.5f * xv;
+    return fmaf(fabsf(h), erf_abs, h);
 }
 
 // ------------------------------------------------------------------ shared / mbarrier
@@ -113,6 +114,30 @@ MADI_DEV bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag
     }
 }
 
+// Warp-uniform bounded wait: every lane observes the barrier (so each has the
+// acquire ordering for the data it guards), then the warp agrees; a lane that
+// gave up makes the whole warp give up, keeping warp-collective ops convergent.
+MADI_DEV bool warp_wait_all(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int *dev_err) {
+    const bool ok = mbar_wait(bar, parity, abort_flag, dev_err);
+    return __all_sync(0xffffffffu, ok);
+}
+
+// ------------------------------------------------------------------ prefetching loads
+
+// Read-only predicated loads into a register the caller pre-set (kept when the
+// predicate is false).  Nothing consumes the value inside the asm, so the
+// thread only waits for it at its first real use: a register prefetch.
+MADI_DEV void ldg_nc_u32_pred(uint32_t &dst, const void *p, bool pred) {
+    asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %2, 0;\n\t@q ld.global.nc.b32 %0, [%1];\n\t}"
+                 : "+r"(dst)
+                 : "l"(p), "r"((int)pred));
+}
+MADI_DEV void ldg_nc_u16_pred(uint32_t &dst, const void *p, bool pred) {
+    asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %2, 0;\n\t@q ld.global.nc.u16 %0, [%1];\n\t}"
+                 : "+r"(dst)
+                 : "l"(p), "r"((int)pred));
+}
+
 // ------------------------------------------------------------------ TMA
 
 MADI_DEV void tma_prefetch_desc(const CUtensorMap *m) {
@@ -125,6 +150,15 @@ MADI_DEV void tma_load_2d(void *smem_dst, const CUtensorMap *m, uint64_t *bar, i
         "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
             smem_u32(smem_dst)),
         "l"(reinterpret_cast<uint64_t>(m)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+        : "memory");
+}
+
+// 3-D tiled TMA load (no multicast); c0 = innermost coordinate (elements).
+MADI_DEV void tma_load_3d(void *smem_dst, const CUtensorMap *m, uint64_t *bar, int c0, int c1, int c2) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], "
+        "[%2];" ::"r"(smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(m)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
         : "memory");
 }
 

@@ -22,7 +22,10 @@
 // Warp roles (512 threads): w0 TMA producer, w1 MMA issuer + TMEM owner,
 // w2-3 idle, w4-11 dequant in two groups of four that take alternate stages
 // (TMEM lane quarter = warp % 4), w12-15 epilogue.
-// TMEM columns: [0, 2*BT) accumulators, then STAGES x 32 columns of A.
+// TMEM columns: [0, 2*BT) accumulators, then A_STAGES x 32 columns of A.  The
+// shared-memory ring (X + int8 W per 64-K stage) is decoupled from the TMEM A
+// ring and as deep as ~192 KB allows (6 stages at BT=192, 8 at BT=128), so TMA
+// latency from L2/HBM is covered by bytes in flight.
 // Every mbarrier wait is bounded; on expiry the CTA raises its abort flag,
 // records the device error word, drains its in-flight copies and MMAs,
 // frees TMEM and returns.
@@ -38,7 +41,9 @@ namespace {
 
 constexpr int BN = 128;        // weight rows per tile = MMA M
 constexpr int BK = 64;         // K per pipeline stage
-constexpr int STAGES = 4;
+constexpr int A_STAGES = 4;    // TMEM ring of dequantised A stages
+constexpr int MAX_STAGES = 8;  // shared-memory ring depth upper bound
+constexpr int RING_BYTES = 192 * 1024;      // shared-memory ring budget (X + W stages)
 constexpr int W_STAGE = BN * BK;           // int8 bytes
 constexpr int A_STAGE_COLS = BK / 2;       // f16 pairs per TMEM column
 constexpr int TMEM_COLS = 512;
@@ -48,33 +53,30 @@ constexpr int kThreads = 512;
 
 template <int BT> struct Cfg {
     static constexpr int X_STAGE = BT * BK * 2;   // f16 bytes
+    // as many shared-memory stages as the ring budget holds: DRAM/L2 latency is
+    // covered by bytes in flight, so the ring is as deep as shared memory allows
+    static constexpr int STAGES = RING_BYTES / (X_STAGE + W_STAGE) < MAX_STAGES
+                                      ? RING_BYTES / (X_STAGE + W_STAGE) : MAX_STAGES;
     static constexpr int ACC_COLS = BT;
     static constexpr int A_COL0 = 2 * BT;
-    static_assert(A_COL0 + STAGES * A_STAGE_COLS <= TMEM_COLS, "TMEM budget");
+    static_assert(A_COL0 + A_STAGES * A_STAGE_COLS <= TMEM_COLS, "TMEM budget");
     static_assert(BT % 32 == 0 && BT >= 32 && BT <= 256, "MMA N");
+    static_assert(STAGES >= 2, "ring depth");
     static constexpr uint32_t IDESC = idesc_f16_f32(BN, BT);
     static constexpr size_t SMEM = 1024 + (size_t)STAGES * (X_STAGE + W_STAGE) + 256;
 };
 
 struct __align__(8) Bars {
-    uint64_t full[STAGES];     // TMA bytes landed (X + W)
-    uint64_t aready[STAGES];   // dequantised A written to TMEM (128 arrivals: one dequant group)
-    uint64_t empty[STAGES];    // MMAs of the stage done (tcgen05.commit)
+    uint64_t full[MAX_STAGES];   // TMA bytes landed (X + W)
+    uint64_t empty[MAX_STAGES];  // MMAs of the stage done (tcgen05.commit): X and W both consumed
+    uint64_t aready[A_STAGES];   // dequantised A written to TMEM (128 arrivals: one dequant group)
+    uint64_t aempty[A_STAGES];   // MMAs reading the TMEM A stage done (tcgen05.commit)
     uint64_t accfull[2];       // accumulator ready (tcgen05.commit)
     uint64_t accempty[2];      // epilogue drained the accumulator (128 arrivals)
     uint64_t drain;            // final MMA drain
     uint32_t tmem_base;
     int abort;
 };
-
-// Warp-uniform bounded wait: every lane observes the barrier (so each has the
-// acquire ordering for the data it guards), then the warp agrees; a lane that
-// gave up makes the whole warp give up, keeping warp-collective tcgen05 ops
-// convergent.
-MADI_DEV bool warp_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int *dev_err) {
-    const bool ok = mbar_wait(bar, parity, abort_flag, dev_err);
-    return __all_sync(0xffffffffu, ok);
-}
 
 // Bounded wait that ignores the abort flag (used to drain in-flight work).
 MADI_DEV void mbar_wait_drain(uint64_t *bar, uint32_t parity) {
@@ -121,6 +123,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     q8_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
                       const GemmArgs p) {
     using C = Cfg<BT>;
+    constexpr int STAGES = C::STAGES;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *xs = smem;
@@ -137,8 +140,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(&bars->full[s], 1);
-            mbar_init(&bars->aready[s], 128);
             mbar_init(&bars->empty[s], 1);
+        }
+        for (int a = 0; a < A_STAGES; ++a) {
+            mbar_init(&bars->aready[a], 128);
+            mbar_init(&bars->aempty[a], 1);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&bars->accfull[b], 1);
@@ -188,8 +194,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == 1) {
         // ------------------------------------------------ MMA issuer
         if (lane == 0) {
-            int s = 0, lt = 0;
-            uint32_t ph = 0;
+            int s = 0, a = 0, lt = 0;
+            uint32_t ph = 0, pha = 0;
             for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++lt) {
                 const int b = lt & 1;
                 const uint32_t aph = (lt >> 1) & 1;
@@ -198,16 +204,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t d_tmem = tmem + b * C::ACC_COLS;
                 bool ok = true;
                 for (int kt = 0; kt < KT; ++kt) {
-                    if (!mbar_wait(&bars->aready[s], ph, abort_flag, err)) { ok = false; break; }
+                    if (!mbar_wait(&bars->aready[a], pha, abort_flag, err)) { ok = false; break; }
                     tc_fence_after();
-                    const uint32_t a_tmem = tmem + C::A_COL0 + s * A_STAGE_COLS;
+                    const uint32_t a_tmem = tmem + C::A_COL0 + a * A_STAGE_COLS;
                     const uint32_t xaddr = smem_u32(xs + s * C::X_STAGE);
 #pragma unroll
                     for (int j = 0; j < BK / 16; ++j)
                         umma_f16_ts(d_tmem, a_tmem + j * 8, smem_desc_sw128(xaddr + j * 32), C::IDESC,
                                     (kt | j) != 0);
-                    umma_commit(&bars->empty[s]);
+                    umma_commit(&bars->empty[s]);     // X (MMA) and W (dequant, earlier) consumed
+                    umma_commit(&bars->aempty[a]);    // TMEM A stage reusable
                     if (++s == STAGES) { s = 0; ph ^= 1; }
+                    if (++a == A_STAGES) { a = 0; pha ^= 1; }
                 }
                 if (!ok) break;
                 umma_commit(&bars->accfull[b]);
@@ -228,27 +236,37 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int swz = (r >> 1) & 3;           // SWIZZLE_64B: 16-byte chunk c lives at c ^ swz
         const bool pair_ok = (nkb & 1) == 0;    // both block scales of a stage in one aligned word
 
-        // f16 scale pair (blocks 2kt, 2kt+1) of this thread's row at global stage `it`
-        auto scale_word = [&](int it) -> uint32_t {
+        // f16 scale pair (blocks 2kt, 2kt+1) of this thread's row at global stage
+        // `it`.  The loads are predicated PTX loads whose destinations nothing
+        // reads until the stage that uses them, so their L2 latency overlaps the
+        // two visits in between (a select on the loaded value here would stall).
+        auto scale_word = [&](int it) -> uint2 {
             const int lt = it / KT, kt = it - lt * KT;
             const int tile = blockIdx.x + lt * gridDim.x;
-            if (tile >= num_tiles) return 0u;
             const int n = (tile % n_tiles) * BN + r;
-            if (n >= N) return 0u;
             const int kb = 2 * kt;
-            const __half *sp = p.scales + (size_t)n * nkb + kb;
-            if (pair_ok) return __ldg(reinterpret_cast<const unsigned int *>(sp));
-            const uint32_t lo = kb < nkb ? __half_as_ushort(__ldg(sp)) : 0u;
-            const uint32_t hi = kb + 1 < nkb ? __half_as_ushort(__ldg(sp + 1)) : 0u;
-            return lo | (hi << 16);
+            const bool rowok = tile < num_tiles && n < N;
+            const __half *sp = p.scales + (size_t)(rowok ? n : 0) * nkb + (rowok ? kb : 0);
+            uint2 v = make_uint2(0u, 0u);
+            if (pair_ok) {
+                ldg_nc_u32_pred(v.x, sp, rowok);
+            } else {
+                ldg_nc_u16_pred(v.x, sp, rowok && kb < nkb);
+                ldg_nc_u16_pred(v.y, sp + 1, rowok && kb + 1 < nkb);
+            }
+            return v;
         };
         // dequantise global stage `it` with scale pair `sw`; false when done or aborted
-        auto visit = [&](int it, uint32_t sw) -> bool {
+        auto visit = [&](int it, uint2 swv) -> bool {
             const int lt = it / KT;
             if (blockIdx.x + lt * gridDim.x >= num_tiles) return false;
             const int s = it % STAGES;
             const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
-            if (!warp_wait(&bars->full[s], ph, abort_flag, err)) return false;
+            const int as = it % A_STAGES;
+            const uint32_t pha = (uint32_t)(it / A_STAGES) & 1u;
+            if (!warp_wait_all(&bars->aempty[as], pha ^ 1u, abort_flag, err)) return false;
+            if (!warp_wait_all(&bars->full[s], ph, abort_flag, err)) return false;
+            const uint32_t sw = pair_ok ? swv.x : (swv.x | (swv.y << 16));
             const __half2 sw2 = *reinterpret_cast<const __half2 *>(&sw);
             const __half2 sc_lo = __low2half2(sw2), sc_hi = __high2half2(sw2);
             const uint8_t *wrow = ws + s * W_STAGE + r * 64;
@@ -266,18 +284,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                     a[c * 8 + 2 * i + 1] = h2_as_u32(__hmul2(hi, sc));
                 }
             }
-            tmem_st32(tmem + lane_addr + C::A_COL0 + s * A_STAGE_COLS, a);
+            tmem_st32(tmem + lane_addr + C::A_COL0 + as * A_STAGE_COLS, a);
             tmem_wait_st();
             tc_fence_before();
-            mbar_arrive(&bars->aready[s]);
+            mbar_arrive(&bars->aready[as]);
             return true;
         };
         // this group visits stages grp, grp+2, ...; scales are fetched two
         // visits (four stages) ahead so their L2 latency is off the critical path
         int it = grp;
-        uint32_t sA = scale_word(it), sB = scale_word(it + 2);
+        uint2 sA = scale_word(it), sB = scale_word(it + 2);
         while (true) {
-            uint32_t use = sA;
+            uint2 use = sA;
             sA = scale_word(it + 4);
             if (!visit(it, use)) break;
             use = sB;
@@ -294,7 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++lt) {
             const int b = lt & 1;
             const uint32_t aph = (lt >> 1) & 1;
-            if (!warp_wait(&bars->accfull[b], aph, abort_flag, err)) break;
+            if (!warp_wait_all(&bars->accfull[b], aph, abort_flag, err)) break;
             tc_fence_after();
             const int m0 = (tile / n_tiles) * BT;
             const int n = (tile % n_tiles) * BN + r;
@@ -357,8 +375,9 @@ bool make_map(CUtensorMap *m, CUtensorMapDataType dt, const void *base, uint64_t
                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// Token-tile width: the candidate with the fewest waves x tile length wins,
-// the wider tile on ties (it amortises the weight dequant over more tokens).
+// Token-tile width: the candidate with the lowest waves x (tile length + a fixed
+// per-tile cost of 32 token columns) wins, the wider tile on ties (it amortises
+// the weight dequant over more tokens).
 int pick_bt(int M, int N, int num_sms) {
     const int n_tiles = (N + BN - 1) / BN;
     long best_cost = -1;
@@ -366,7 +385,7 @@ int pick_bt(int M, int N, int num_sms) {
     for (int bt : {192, 128}) {
         const long tiles = (long)n_tiles * ((M + bt - 1) / bt);
         const long waves = (tiles + num_sms - 1) / num_sms;
-        const long cost = waves * bt;
+        const long cost = waves * (bt + 32);
         if (best_cost < 0 || cost < best_cost) { best_cost = cost; best = bt; }
     }
     return best;

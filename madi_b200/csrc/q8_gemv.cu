@@ -48,14 +48,16 @@ constexpr int kRows = 16 * kWarps;   // weight rows per CTA
 constexpr int kMaxB = 10;            // Q8 blocks a warp keeps in flight (one round)
 constexpr int kMaxCluster = 16;      // non-portable cluster size, allowed on sm_100
 
-MADI_DEV uint2 ldg_stream_u2(const void *p) {
-    uint2 v;
-    // not volatile: the weights are read-only for the kernel's lifetime, so the
-    // compiler may schedule these loads freely around the MMA chains
-    asm("ld.global.nc.L1::no_allocate.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
-    return v;
+// Predicated streaming load into registers the caller pre-set to zero.  No
+// instruction consumes the value inside the asm, so all of a warp's loads are
+// in flight together and the thread waits only at the MMA that uses them.
+MADI_DEV void ldg_stream_u2_pred(uint2 &v, const void *p, bool pred) {
+    asm volatile(
+        "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %3, 0;\n\t"
+        "@q ld.global.nc.L1::no_allocate.v2.u32 {%0, %1}, [%2];\n\t}"
+        : "+r"(v.x), "+r"(v.y)
+        : "l"(p), "r"((int)pred));
 }
-MADI_DEV float ldg_half(const __half *p) { return __half2float(__ldg(p)); }
 
 MADI_DEV void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
     asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
@@ -147,16 +149,21 @@ __global__ void __launch_bounds__(kThreads, 2) q8_gemv_kernel(const GemvArgs p) 
     const __half *s1p = p.scales + (size_t)(ok1 ? row1 : 0) * nkb;
 
     uint2 wa[kMaxB], wb[kMaxB];
-    float sa[kMaxB], sb[kMaxB];
+    uint32_t sa[kMaxB], sb[kMaxB];     // raw f16 scale bits, converted at use
     auto load_round = [&](int kb0) {
 #pragma unroll
         for (int u = 0; u < kMaxB; ++u) {
             const int kb = kb0 + u;
             const bool in = kb < kb_end;
-            wa[u] = (in && ok0) ? ldg_stream_u2(w0 + (size_t)kb * 32) : make_uint2(0u, 0u);
-            wb[u] = (in && ok1) ? ldg_stream_u2(w1 + (size_t)kb * 32) : make_uint2(0u, 0u);
-            sa[u] = (in && ok0) ? ldg_half(s0p + kb) : 0.f;
-            sb[u] = (in && ok1) ? ldg_half(s1p + kb) : 0.f;
+            const int kbc = in ? kb : kb_begin;     // a valid address even when predicated off
+            wa[u] = make_uint2(0u, 0u);
+            wb[u] = make_uint2(0u, 0u);
+            sa[u] = 0u;
+            sb[u] = 0u;
+            ldg_stream_u2_pred(wa[u], w0 + (size_t)kbc * 32, in && ok0);
+            ldg_stream_u2_pred(wb[u], w1 + (size_t)kbc * 32, in && ok1);
+            ldg_nc_u16_pred(sa[u], s0p + kbc, in && ok0);
+            ldg_nc_u16_pred(sb[u], s1p + kbc, in && ok1);
         }
     };
 
@@ -190,10 +197,12 @@ __global__ void __launch_bounds__(kThreads, 2) q8_gemv_kernel(const GemvArgs p) 
                     mma16816(blk, a, bl.x, bl.y);
                 }
             }
-            acc[0] = fmaf(blk[0], sa[u], acc[0]);
-            acc[1] = fmaf(blk[1], sa[u], acc[1]);
-            acc[2] = fmaf(blk[2], sb[u], acc[2]);
-            acc[3] = fmaf(blk[3], sb[u], acc[3]);
+            const float s0 = __half2float(__ushort_as_half((unsigned short)sa[u]));
+            const float s1 = __half2float(__ushort_as_half((unsigned short)sb[u]));
+            acc[0] = fmaf(blk[0], s0, acc[0]);
+            acc[1] = fmaf(blk[1], s0, acc[1]);
+            acc[2] = fmaf(blk[2], s1, acc[2]);
+            acc[3] = fmaf(blk[3], s1, acc[3]);
         }
     }
 

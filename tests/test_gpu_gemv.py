@@ -154,3 +154,12 @@ def test_qkv_kv_store(madi, oracle):
         _check(qo[s], q_ex[0], f"slot {s} q")
         _check(kcb[s, posb[s]], k_ex[posb[s]], f"slot {s} k")
         _check(vcb[s, posb[s]], v_ex[posb[s]], f"slot {s} v")
+
+
+@pytest.mark.parametrize("M,epi,x_dt,y_dt", [(8, 1, np.float32, np.float32), (3, 2, np.float32, np.float32),
+                                             (8, 3, np.float32, np.float32), (5, 0, np.float16, np.float32),
+                                             (2, 1, np.float32, np.float16), (1, 3, np.float16, np.float16)])
+def test_large_n_streaming_path(madi, oracle, M, epi, x_dt, y_dt):
+    """N >= 16 x 16 x SMs with K % 256 == 0 takes the persistent bulk-copy streamed
+    kernel; N = 40010 leaves a ragged last 16-row tile (10 rows)."""
+    _case(madi, oracle, M, 40010, 1536, epi, x_dt=x_dt, y_dt=y_dt, seed=M * 13 + epi)
