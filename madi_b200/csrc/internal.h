@@ -31,11 +31,12 @@ struct GemvArgs {
 int gemv_pick_ks(int N, int K, int num_sms);
 size_t gemv_smem_bytes(int M, int K, int cs, bool x_f32);
 cudaError_t launch_gemv(const GemvArgs &a, bool x_f32, bool y_f32, int epi, bool qkv, cudaStream_t st, bool pdl);
-// Large-N path (vocab head): persistent, TMA-streamed weights.  Valid when
-// gemv_stream_ok(); same arithmetic and epilogues as launch_gemv (no QKV).
-bool gemv_stream_ok(int M, int N, int K, bool x_f32, int num_sms);
-cudaError_t launch_gemv_stream(const GemvArgs &a, bool x_f32, bool y_f32, int epi, int num_sms, int *dev_err,
-                               cudaStream_t st, bool pdl);
+// TMA-streamed tile kernel (q8_gemv_tile.cu): every shape with K % 256 == 0 whose
+// x slice and one weight stage fit in shared memory, QKV included; same
+// arithmetic and epilogues as launch_gemv.  Needs 16-byte aligned qs and scales.
+bool gemv_tile_ok(int M, int N, int K, bool x_f32, int num_sms);
+cudaError_t launch_gemv_tile(const GemvArgs &a, bool x_f32, bool y_f32, int epi, bool qkv, int num_sms, int *dev_err,
+                             cudaStream_t st, bool pdl);
 
 // ---------------------------------------------------------------- variant (a)
 struct GemmArgs {

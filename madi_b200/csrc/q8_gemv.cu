@@ -76,7 +76,9 @@ template <> MADI_DEV __half from_f32<__half>(float v) { return __float2half_rn(v
 // Stage x[m][k] for k in this CTA's slice [kb_begin*32, kb_end*32) into shared
 // memory in fragment order: slot (lkb, s, m, t) holds x[m][(kb_begin+lkb)*32 +
 // 8t + 4s + 0..3] as four f16.  Loads are issued in batches of 8 per thread so
-// the L2 round trips overlap.
+// the L2 round trips overlap; they use the coherent L2 path (ld.global.cg)
+// because under programmatic dependent launch x is written by a kernel whose
+// lifetime overlaps this one's.
 template <typename XT, bool kSplit>
 MADI_DEV void stage_x(const XT *__restrict__ x, int M, int K, int kb_begin, int kb_end, uint2 *xf_hi,
                       uint2 *xf_lo) {
@@ -92,10 +94,10 @@ MADI_DEV void stage_x(const XT *__restrict__ x, int M, int K, int kb_begin, int 
                 const int m = i / qrow, kq = i - m * qrow;
                 const size_t off = (size_t)m * K + (size_t)kb_begin * 32 + 4 * kq;
                 if constexpr (sizeof(XT) == 4) {
-                    const float4 f = __ldg(reinterpret_cast<const float4 *>(x + off));
+                    const float4 f = __ldcg(reinterpret_cast<const float4 *>(x + off));
                     v[j][0] = f.x; v[j][1] = f.y; v[j][2] = f.z; v[j][3] = f.w;
                 } else {
-                    const uint2 u = __ldg(reinterpret_cast<const uint2 *>(x + off));
+                    const uint2 u = __ldcg(reinterpret_cast<const uint2 *>(x + off));
                     const __half2 h0 = *reinterpret_cast<const __half2 *>(&u.x);
                     const __half2 h1 = *reinterpret_cast<const __half2 *>(&u.y);
                     v[j][0] = __low2float(h0); v[j][1] = __high2float(h0);

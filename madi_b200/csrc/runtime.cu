@@ -136,8 +136,8 @@ int q8_linear_impl(const madi_q8w *w, const void *x, int x_dtype, int m, const v
     const bool xf32 = x_dtype == MADI_F32;
     if (!aligned(x, xf32 ? 16 : 8)) return fail(MADI_EINVAL, "%s: x must be %d-byte aligned", who, xf32 ? 16 : 8);
     const int ks = gemv_pick_ks(N, K, S.num_sms);
-    const bool stream_path = gemv_stream_ok(m, N, K, xf32, S.num_sms) && aligned(w->qs, 16) && aligned(w->scales, 16);
-    if (!stream_path && gemv_smem_bytes(m, K, ks, xf32) > (size_t)S.max_smem_optin)
+    const bool tile_path = aligned(w->qs, 16) && aligned(w->scales, 16) && gemv_tile_ok(m, N, K, xf32, S.num_sms);
+    if (!tile_path && gemv_smem_bytes(m, K, ks, xf32) > (size_t)S.max_smem_optin)
         return fail(MADI_EINVAL, "%s: K=%d too large for the decode path at m=%d", who, K, m);
     GemvArgs a{};
     a.qs = w->qs;
@@ -146,8 +146,8 @@ int q8_linear_impl(const madi_q8w *w, const void *x, int x_dtype, int m, const v
     a.bias_f16 = bias_dtype == MADI_F16;
     a.N = N; a.K = K; a.M = m;
     a.ks = ks;
-    cudaError_t e = stream_path
-                        ? launch_gemv_stream(a, xf32, y_dtype == MADI_F32, epi, S.num_sms, S.dev_err, st, S.pdl)
+    cudaError_t e = tile_path
+                        ? launch_gemv_tile(a, xf32, y_dtype == MADI_F32, epi, false, S.num_sms, S.dev_err, st, S.pdl)
                         : launch_gemv(a, xf32, y_dtype == MADI_F32, epi, false, st, S.pdl);
     if (e == cudaErrorNotSupported) return fail(MADI_EUNSUPPORTED, "%s: cuTensorMapEncodeTiled unavailable", who);
     if (e != cudaSuccess) return cuda_fail(e, who);
@@ -164,7 +164,9 @@ int q8_qkv_impl(const madi_q8w *w, const float *x, int m, const float *qb, const
     if (m <= 0 || m > 8) return fail(MADI_EINVAL, "%s: m=%d outside 1..8", who, m);
     if (!aligned(x, 16) || !aligned(w->qs, 16)) return fail(MADI_EINVAL, "%s: misaligned x or qs", who);
     const int ks = gemv_pick_ks(3 * D, D, S.num_sms);
-    if (gemv_smem_bytes(m, D, ks, true) > (size_t)S.max_smem_optin) return fail(MADI_EINVAL, "%s: D too large", who);
+    const bool tile_path = aligned(w->scales, 16) && gemv_tile_ok(m, 3 * D, D, true, S.num_sms);
+    if (!tile_path && gemv_smem_bytes(m, D, ks, true) > (size_t)S.max_smem_optin)
+        return fail(MADI_EINVAL, "%s: D too large", who);
     GemvArgs a{};
     a.qs = w->qs;
     a.scales = reinterpret_cast<const __half *>(w->scales);
@@ -174,7 +176,9 @@ int q8_qkv_impl(const madi_q8w *w, const float *x, int m, const float *qb, const
     a.qb = qb; a.vb = vb; a.kc = kc; a.vc = vc; a.pos = pos;
     a.cache_stride = m > 1 ? cache_stride : 0;
     a.D = D;
-    cudaError_t e = launch_gemv(a, true, true, MADI_EPI_NONE, true, st, S.pdl);
+    cudaError_t e = tile_path ? launch_gemv_tile(a, true, true, MADI_EPI_NONE, true, S.num_sms, S.dev_err, st, S.pdl)
+                              : launch_gemv(a, true, true, MADI_EPI_NONE, true, st, S.pdl);
+    if (e == cudaErrorNotSupported) return fail(MADI_EUNSUPPORTED, "%s: cuTensorMapEncodeTiled unavailable", who);
     if (e != cudaSuccess) return cuda_fail(e, who);
     return MADI_OK;
 }

@@ -160,6 +160,22 @@ def test_qkv_kv_store(madi, oracle):
                                              (8, 3, np.float32, np.float32), (5, 0, np.float16, np.float32),
                                              (2, 1, np.float32, np.float16), (1, 3, np.float16, np.float16)])
 def test_large_n_streaming_path(madi, oracle, M, epi, x_dt, y_dt):
-    """N >= 16 x 16 x SMs with K % 256 == 0 takes the persistent bulk-copy streamed
-    kernel; N = 40010 leaves a ragged last 16-row tile (10 rows)."""
+    """Many more 16-row tiles than CTA slots: the TMA tile kernel runs persistent
+    (two CTAs per SM, a ring of stages each); N = 40010 leaves a ragged last tile
+    (10 rows) that the TMA unit zero-fills."""
     _case(madi, oracle, M, 40010, 1536, epi, x_dt=x_dt, y_dt=y_dt, seed=M * 13 + epi)
+
+
+@pytest.mark.parametrize("M,N,K,epi,x_dt,y_dt", [
+    (3, 300, 1024, 1, np.float32, np.float32),     # 19 tiles: 4-CTA clusters split K (256 each)
+    (5, 37, 2048, 2, np.float32, np.float32),      # 3 tiles, the last ragged, 4-way split
+    (2, 1280, 5120, 3, np.float32, np.float32),    # fc2 shape, 2-way split
+    (8, 1280, 5120, 3, np.float16, np.float32),    # fc2 with f16 activations, 2-way split
+    (7, 1280, 5120, 0, np.float16, np.float16),
+    (4, 4000, 4096, 1, np.float32, np.float32),    # persistent, one CTA per SM (x slice too big for two)
+    (1, 2048, 256, 0, np.float32, np.float32),     # K = 256: one box, one block per warp
+])
+def test_tile_kernel_plans(madi, oracle, M, N, K, epi, x_dt, y_dt):
+    """The tile kernel's launch plans: thread-block clusters splitting K (partial
+    sums pushed into rank 0), one unit per CTA, persistent rings."""
+    _case(madi, oracle, M, N, K, epi, x_dt=x_dt, y_dt=y_dt, seed=N + K + M)
