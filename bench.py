@@ -10,12 +10,13 @@ Workload (N=1 is BASELINE config 1 at B=16, the largest single-GPU config):
   value = whole-job encoder Q8 GEMM TFLOP/s (2*M*N*K per GEMM, all ranks),
           inputs resident in HBM; working set (X 61 MB + H 246 MB + Y 61 MB)
           is larger than the 126 MB L2.
-  decode leg (M=8 token slots): one decoder token step's
-          Q8 projections (4 layers x {qkv, o, cq, co, fc1, fc2}) + vocab head,
-          replayed as a CUDA graph over two distinct weight sets (2 x 168 MB,
-          alternating, so every replay streams from HBM); reported in GB/s.
-          At N>1 the vocab head is column-split and its logits all-gathered
-          over NCCL.
+  decode leg (M=8 token slots, fp16 activations): one
+          decoder token step's Q8 projections (4 layers x {qkv, o, cq, co, fc1,
+          fc2}) + vocab head, replayed as a CUDA graph over two distinct weight
+          sets (2 x 168 MB, alternating, so every replay streams from HBM);
+          reported in GB/s, with each shape also timed alone (back-to-back
+          launches over > 300 MB of weight copies).  At N>1 the vocab head is
+          column-split and its logits all-gathered over NCCL.
   e2e   = the same encoder metric through the public API (madi_b200.q8.linear)
           with pinned HOST buffers: per step H2D of X and D2H of Y inside the
           timed region.
@@ -53,6 +54,8 @@ def parse():
     ap.add_argument("--impl", choices=["madi", "reference"], default="madi")
     ap.add_argument("--batch", type=int, default=16, help="30 s chunks per GPU per step (config 1: 1, 4, 16)")
     ap.add_argument("--decode-m", type=int, default=8)
+    ap.add_argument("--decode-x", choices=["f16", "f32"], default="f16",
+                    help="decode activations (config 2: fp16; the reference decoder's own GEMVs take f32)")
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -339,13 +342,20 @@ def main_madi(args, world, rank, local):
 
 
 def decode_leg(args, world, rank, dev, stream, peaks):
-    """One decoder token step's Q8 projections for M token slots, CUDA-graph replayed."""
+    """one decoder token step's Q8 projections for M token slots
+    (fp16 activations), CUDA-graph replayed; plus each projection shape on its own,
+    back to back in a graph over enough weight copies that every launch streams its
+    weights from HBM (the vocab head is the roofline kernel)."""
     import numpy as np
     import torch
     from madi_b200 import q8, shard, synth
 
     Md = args.decode_m
+    xdt = torch.float16 if args.decode_x == "f16" else torch.float32
+    sx = 2 if xdt == torch.float16 else 4
     h0, h1 = shard.vocab_shard(V, world, rank)
+    epis = {"qkv": q8.EPI_NONE, "o": q8.EPI_NONE, "cq": q8.EPI_BIAS, "co": q8.EPI_NONE,
+            "fc1": q8.EPI_BIAS_GELU, "fc2": q8.EPI_BIAS_RES}
 
     def t(a):
         return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
@@ -363,8 +373,8 @@ def decode_leg(args, world, rank, dev, stream, peaks):
         return layers, head
 
     sets = [make_set(s) for s in (1, 2)]
-    x = t(synth.activations(Md, D, 7, np.float32))
-    big = torch.empty((Md, F), dtype=torch.float32, device=dev)
+    x = t(synth.activations(Md, D, 7, np.float32)).to(xdt)
+    big = torch.empty((Md, F), dtype=xdt, device=dev)        # fc1 output = fc2 input
     outs = {n: torch.empty((Md, nn), dtype=torch.float32, device=dev) for n, nn, _ in synth.decoder_shapes()}
     resid = torch.zeros((Md, D), dtype=torch.float32, device=dev)
     logits = torch.empty((Md, h1 - h0), dtype=torch.float32, device=dev)
@@ -380,16 +390,22 @@ def decode_leg(args, world, rank, dev, stream, peaks):
                       stream=stream)
         q8.linear(head, x, out=logits, stream=stream)
 
-    bytes_step = 0
-    for name, n, k in synth.decoder_shapes():
-        b = n * k + n * k // 16 + Md * k * 4 + Md * n * 4
-        if name in ("cq", "fc1", "fc2"):
+    def op_bytes(name, n, k):
+        """Algorithmic bytes of one projection at M = Md: weights, scales, x, y
+        (+ bias, + the residual read of fc2)."""
+        ysz = sx if name == "fc1" else 4
+        xsz = sx
+        b = n * k + n * k // 16 + Md * k * xsz + Md * n * ysz
+        if epis.get(name, 0) != q8.EPI_NONE:
             b += n * 4
         if name == "fc2":
             b += Md * n * 4
-        bytes_step += 4 * b
+        return b
+
+    bytes_step = 4 * sum(op_bytes(name, n, k) for name, n, k in synth.decoder_shapes())
     hn = h1 - h0
-    bytes_step += hn * D + hn * D // 16 + Md * D * 4 + Md * hn * 4
+    bytes_head = op_bytes("head", hn, D)
+    bytes_step += bytes_head
 
     graphs = []
     with torch.cuda.stream(stream):
@@ -428,14 +444,67 @@ def decode_leg(args, world, rank, dev, stream, peaks):
         torch.cuda.synchronize()
         ag_ms = max_over_ranks(world, a0.elapsed_time(a1) / K)
     ms_max = max_over_ranks(world, ms)
+    del graphs
+
+    # ---- each shape alone: `copies` distinct weights (> 300 MB in all) launched back
+    # to back in one graph; us per launch = graph time / copies
+    per_shape = {}
+    shapes = [(name, n, k) for name, n, k in synth.decoder_shapes()] + [("head", hn, D)]
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1234 + rank)
+    for name, n, k in shapes:
+        nb = n * k + n * k // 16
+        copies = max(4, int(300e6 // nb) + 1)
+        Ws = [q8.Q8Weight(torch.randint(-127, 128, (n, k), dtype=torch.int8, device=dev, generator=gen),
+                          (torch.rand((n, k // 32), device=dev, generator=gen) * 2e-3 + 1e-4).half())
+              for _ in range(copies)]
+        xi = big if name == "fc2" else x
+        bias = torch.zeros(n, dtype=torch.float32, device=dev)
+        yo = torch.empty((Md, n), dtype=xdt if name == "fc1" else torch.float32, device=dev)
+        epi = epis.get(name, q8.EPI_NONE)
+
+        def run():
+            for W in Ws:
+                q8.linear(W, xi, bias=bias if epi != q8.EPI_NONE else None, epi=epi,
+                          residual=yo if epi == q8.EPI_BIAS_RES else None, out=yo, stream=stream)
+        with torch.cuda.stream(stream):
+            run()
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream, capture_error_mode="thread_local"):
+                run()
+            for _ in range(2):
+                g.replay()
+            torch.cuda.synchronize()
+            best = None
+            for _ in range(3):
+                a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a0.record(stream)
+                g.replay()
+                a1.record(stream)
+                a1.synchronize()
+                us = a0.elapsed_time(a1) * 1e3 / copies
+                best = us if best is None else min(best, us)
+        us = max_over_ranks(world, best)
+        b = op_bytes(name, n, k)
+        per_shape[name] = {"N": n, "K": k, "us_per_launch": us, "GBps": b / us / 1e3,
+                           "frac_of_hbm": b / us / 1e3 / peaks["hbm"]}
+        del g, Ws
+        torch.cuda.empty_cache()
+
+    head = per_shape["head"]
     gbs = bytes_step / (ms / 1e3) / 1e9
     return {"value": bytes_step * world / (ms_max / 1e3) / 1e9, "unit": "GB/s", "m_tokens": Md,
-            "bytes_per_step_per_gpu": bytes_step, "ms_per_token_step": ms_max, "gpu_launches_per_step": 25,
-            "head_rows_per_gpu": hn, "step_with_logit_allgather_ms": ag_ms,
-            "roofline": {"bound": "hbm", "kernel": "q8_gemv_kernel (25 launches/step, CUDA graph)",
-                         "achieved": gbs, "peak": peaks["hbm"], "unit": "GB/s", "frac": gbs / peaks["hbm"],
-                         "traffic": load_traffic("q8_gemv_decode_step")},
-            "l2": "two 168 MB weight sets replayed alternately (> 126 MB L2)"}
+            "activations": args.decode_x, "bytes_per_step_per_gpu": bytes_step, "ms_per_token_step": ms_max,
+            "step_GBps_per_gpu": gbs, "gpu_launches_per_step": 25, "head_rows_per_gpu": hn,
+            "step_with_logit_allgather_ms": ag_ms, "per_shape": per_shape,
+            "roofline": {"bound": "hbm", "kernel": f"q8_gemv_tile_kernel (vocab head {hn}x{D}, M={Md}, "
+                                                  "back-to-back launches in a CUDA graph)",
+                         "achieved": head["GBps"], "peak": peaks["hbm"], "unit": "GB/s",
+                         "frac": head["GBps"] / peaks["hbm"],
+                         "traffic": load_traffic(f"q8_gemv_tile_head_m{Md}")},
+            "l2": "step: two 168 MB weight sets replayed alternately (> 126 MB L2); per shape: > 300 MB of "
+                  "distinct weight copies per graph"}
 
 
 def main():

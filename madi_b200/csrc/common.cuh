@@ -187,6 +187,29 @@ MADI_DEV void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uin
         : "memory");
 }
 
+// One 64-wide K stage of a TS MMA chain in a single asm block: four K=16 MMAs
+// (A columns advance by 8, the B descriptor's start address by 32 bytes = 2 in
+// its 16-byte units) followed by two commits.  `desc_lo`/`desc_hi` are the two
+// words of the K-major SWIZZLE_128B smem descriptor of the stage's first MMA;
+// `accumulate` = 0 starts a new accumulation with the first MMA.
+MADI_DEV void umma_stage4_ts(uint32_t d_tmem, uint32_t a_tmem, uint32_t desc_lo, uint32_t desc_hi, uint32_t idesc,
+                             uint32_t accumulate, uint32_t bar0, uint32_t bar1) {
+    asm volatile(
+        "{\n\t.reg .pred p, t;\n\t.reg .b32 a1, a2, a3, l1, l2, l3;\n\t.reg .b64 d0, d1, d2, d3;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\tsetp.eq.b32 t, %4, %4;\n\t"
+        "add.u32 a1, %1, 8;\n\tadd.u32 a2, %1, 16;\n\tadd.u32 a3, %1, 24;\n\t"
+        "add.u32 l1, %2, 2;\n\tadd.u32 l2, %2, 4;\n\tadd.u32 l3, %2, 6;\n\t"
+        "mov.b64 d0, {%2, %3};\n\tmov.b64 d1, {l1, %3};\n\tmov.b64 d2, {l2, %3};\n\tmov.b64 d3, {l3, %3};\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], d0, %5, p;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [a1], d1, %5, t;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [a2], d2, %5, t;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [a3], d3, %5, t;\n\t"
+        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%6];\n\t"
+        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%7];\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "r"(desc_lo), "r"(desc_hi), "r"(accumulate), "r"(idesc), "r"(bar0), "r"(bar1)
+        : "memory");
+}
+
 // Arrive on `bar` once every tcgen05 op issued so far by this thread completes.
 MADI_DEV void umma_commit(uint64_t *bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))

@@ -19,9 +19,10 @@
 //   * the f32 accumulator (128 weight rows x BT tokens) sits in TMEM, double
 //     buffered so the epilogue of tile i overlaps the MMAs of tile i+1.
 //
-// Warp roles (512 threads): w0 TMA producer, w1 MMA issuer + TMEM owner,
+// Warp roles (640 threads): w0 TMA producer, w1 MMA issuer + TMEM owner,
 // w2-3 idle, w4-11 dequant in two groups of four that take alternate stages
-// (TMEM lane quarter = warp % 4), w12-15 epilogue.
+// (TMEM lane quarter = warp % 4), w12-19 epilogue (two warps per lane quarter,
+// each taking every second 32-token chunk of the accumulator).
 // TMEM columns: [0, 2*BT) accumulators, then A_STAGES x 32 columns of A.  The
 // shared-memory ring (X + int8 W per 64-K stage) is decoupled from the TMEM A
 // ring and as deep as ~192 KB allows (6 stages at BT=192, 8 at BT=128), so TMA
@@ -48,8 +49,11 @@ constexpr int W_STAGE = BN * BK;           // int8 bytes
 constexpr int A_STAGE_COLS = BK / 2;       // f16 pairs per TMEM column
 constexpr int TMEM_COLS = 512;
 constexpr int kDqWarp0 = 4;                // warps 4..11: dequant (two groups of four)
-constexpr int kEpiWarp0 = 12;              // warps 12..15: epilogue
-constexpr int kThreads = 512;
+constexpr int kEpiWarp0 = 12;              // warps 12..19: epilogue
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 32 * (kEpiWarp0 + kEpiWarps);
+
+static_assert(BK == 64, "umma_stage4_ts issues four K=16 MMAs per stage");
 
 template <int BT> struct Cfg {
     static constexpr int X_STAGE = BT * BK * 2;   // f16 bytes
@@ -72,7 +76,7 @@ struct __align__(8) Bars {
     uint64_t aready[A_STAGES];   // dequantised A written to TMEM (128 arrivals: one dequant group)
     uint64_t aempty[A_STAGES];   // MMAs reading the TMEM A stage done (tcgen05.commit)
     uint64_t accfull[2];       // accumulator ready (tcgen05.commit)
-    uint64_t accempty[2];      // epilogue drained the accumulator (128 arrivals)
+    uint64_t accempty[2];      // epilogue drained the accumulator (one arrival per epilogue thread)
     uint64_t drain;            // final MMA drain
     uint32_t tmem_base;
     int abort;
@@ -148,7 +152,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&bars->accfull[b], 1);
-            mbar_init(&bars->accempty[b], 128);
+            mbar_init(&bars->accempty[b], kEpiWarps * 32);
         }
         mbar_init(&bars->drain, 1);
         bars->abort = 0;
@@ -196,6 +200,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             int s = 0, a = 0, lt = 0;
             uint32_t ph = 0, pha = 0;
+            // Everything a stage's MMAs need is advanced by adds: the B descriptor's
+            // low word (start address in 16-byte units), the A columns and the two
+            // commit barriers.  The MMA thread shares its scheduler with four busy
+            // warps, so its per-stage instruction count bounds the MMA issue rate.
+            const uint64_t desc0 = smem_desc_sw128(smem_u32(xs));
+            const uint32_t desc_hi = (uint32_t)(desc0 >> 32);
+            const uint32_t desc_lo0 = (uint32_t)desc0;
+            constexpr uint32_t kDescStep = C::X_STAGE >> 4;
+            const uint32_t empty0 = smem_u32(&bars->empty[0]), aempty0 = smem_u32(&bars->aempty[0]);
+            const uint32_t a_tmem0 = tmem + C::A_COL0;
             for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++lt) {
                 const int b = lt & 1;
                 const uint32_t aph = (lt >> 1) & 1;
@@ -206,14 +220,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int kt = 0; kt < KT; ++kt) {
                     if (!mbar_wait(&bars->aready[a], pha, abort_flag, err)) { ok = false; break; }
                     tc_fence_after();
-                    const uint32_t a_tmem = tmem + C::A_COL0 + a * A_STAGE_COLS;
-                    const uint32_t xaddr = smem_u32(xs + s * C::X_STAGE);
-#pragma unroll
-                    for (int j = 0; j < BK / 16; ++j)
-                        umma_f16_ts(d_tmem, a_tmem + j * 8, smem_desc_sw128(xaddr + j * 32), C::IDESC,
-                                    (kt | j) != 0);
-                    umma_commit(&bars->empty[s]);     // X (MMA) and W (dequant, earlier) consumed
-                    umma_commit(&bars->aempty[a]);    // TMEM A stage reusable
+                    // X (MMA) and W (dequant, earlier) of smem stage s consumed; TMEM A stage a reusable
+                    umma_stage4_ts(d_tmem, a_tmem0 + a * A_STAGE_COLS, desc_lo0 + (uint32_t)s * kDescStep, desc_hi,
+                                   C::IDESC, kt != 0, empty0 + 8u * s, aempty0 + 8u * a);
                     if (++s == STAGES) { s = 0; ph ^= 1; }
                     if (++a == A_STAGES) { a = 0; pha ^= 1; }
                 }
@@ -235,17 +244,30 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
         const int swz = (r >> 1) & 3;           // SWIZZLE_64B: 16-byte chunk c lives at c ^ swz
         const bool pair_ok = (nkb & 1) == 0;    // both block scales of a stage in one aligned word
+        const int gstep = (int)(gridDim.x % (unsigned)n_tiles);
 
-        // f16 scale pair (blocks 2kt, 2kt+1) of this thread's row at global stage
-        // `it`.  The loads are predicated PTX loads whose destinations nothing
-        // reads until the stage that uses them, so their L2 latency overlaps the
-        // two visits in between (a select on the loaded value here would stall).
-        auto scale_word = [&](int it) -> uint2 {
-            const int lt = it / KT, kt = it - lt * KT;
-            const int tile = blockIdx.x + lt * gridDim.x;
-            const int n = (tile % n_tiles) * BN + r;
-            const int kb = 2 * kt;
-            const bool rowok = tile < num_tiles && n < N;
+        // A cursor over this group's stages (every second one): the tile, its
+        // row-block index and the k-step, advanced without divisions.
+        struct Cur {
+            int kt, tile, nt;
+        };
+        auto adv = [&](Cur &c) {
+            c.kt += 2;
+            while (c.kt >= KT) {
+                c.kt -= KT;
+                c.tile += gridDim.x;
+                c.nt += gstep;
+                if (c.nt >= n_tiles) c.nt -= n_tiles;
+            }
+        };
+        // f16 scale pair (blocks 2kt, 2kt+1) of this thread's row at cursor c.  The
+        // loads are predicated PTX loads whose destinations nothing reads until the
+        // stage that uses them, so their L2 latency overlaps the two visits in
+        // between (a select on the loaded value here would stall).
+        auto scale_at = [&](const Cur &c) -> uint2 {
+            const int n = c.nt * BN + r;
+            const int kb = 2 * c.kt;
+            const bool rowok = c.tile < num_tiles && n < N;
             const __half *sp = p.scales + (size_t)(rowok ? n : 0) * nkb + (rowok ? kb : 0);
             uint2 v = make_uint2(0u, 0u);
             if (pair_ok) {
@@ -256,14 +278,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             return v;
         };
-        // dequantise global stage `it` with scale pair `sw`; false when done or aborted
-        auto visit = [&](int it, uint2 swv) -> bool {
-            const int lt = it / KT;
-            if (blockIdx.x + lt * gridDim.x >= num_tiles) return false;
-            const int s = it % STAGES;
-            const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
-            const int as = it % A_STAGES;
-            const uint32_t pha = (uint32_t)(it / A_STAGES) & 1u;
+        // ring positions of the stage being visited (smem ring s/ph, TMEM A ring as/pha)
+        int s = grp % STAGES, as = grp % A_STAGES;
+        uint32_t ph = (uint32_t)(grp / STAGES) & 1u, pha = (uint32_t)(grp / A_STAGES) & 1u;
+        // dequantise the visited stage (tile `tile`) with scale pair `swv`; false when
+        // done or aborted
+        auto visit = [&](int tile, uint2 swv) -> bool {
+            if (tile >= num_tiles) return false;
             if (!warp_wait_all(&bars->aempty[as], pha ^ 1u, abort_flag, err)) return false;
             if (!warp_wait_all(&bars->full[s], ph, abort_flag, err)) return false;
             const uint32_t sw = pair_ok ? swv.x : (swv.x | (swv.y << 16));
@@ -288,24 +309,36 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(&bars->aready[as]);
+            s += 2;
+            if (s >= STAGES) { s -= STAGES; ph ^= 1u; }
+            as += 2;
+            if (as >= A_STAGES) { as -= A_STAGES; pha ^= 1u; }
             return true;
         };
-        // this group visits stages grp, grp+2, ...; scales are fetched two
-        // visits (four stages) ahead so their L2 latency is off the critical path
-        int it = grp;
-        uint2 sA = scale_word(it), sB = scale_word(it + 2);
+        // this group visits stages grp, grp+2, ...; scales are fetched two visits
+        // (four stages) ahead so their L2 latency is off the critical path
+        Cur vc{grp % KT, (int)blockIdx.x + (grp / KT) * (int)gridDim.x, 0};
+        vc.nt = vc.tile % n_tiles;
+        Cur pc = vc;
+        adv(pc);
+        uint2 sA = scale_at(vc), sB = scale_at(pc);
+        adv(pc);                                // prefetch cursor: four stages ahead
         while (true) {
             uint2 use = sA;
-            sA = scale_word(it + 4);
-            if (!visit(it, use)) break;
+            sA = scale_at(pc);
+            adv(pc);
+            if (!visit(vc.tile, use)) break;
+            adv(vc);
             use = sB;
-            sB = scale_word(it + 6);
-            if (!visit(it + 2, use)) break;
-            it += 4;
+            sB = scale_at(pc);
+            adv(pc);
+            if (!visit(vc.tile, use)) break;
+            adv(vc);
         }
     } else if (warp >= kEpiWarp0) {
         // ------------------------------------------------ epilogue: TMEM -> bias/GELU/residual -> f16
         const int q = warp & 3;
+        const int half = (warp - kEpiWarp0) >> 2;   // which of the two warps of lane quarter q
         const int r = q * 32 + lane;
         const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
         int lt = 0;
@@ -327,7 +360,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // load -> wait -> use: no register written by an in-flight tcgen05.ld is
             // ever live across compiler-scheduled code
 #pragma unroll 1
-            for (int c = 0; c < BT / 32; ++c) {
+            for (int c = half; c < BT / 32; c += 2) {
                 uint32_t v[32];
                 tmem_ld32(acc_addr + c * 32, v);
                 tmem_wait_ld();
