@@ -162,6 +162,27 @@ MADI_DEV void tma_load_3d(void *smem_dst, const CUtensorMap *m, uint64_t *bar, i
         : "memory");
 }
 
+// 2-D tiled TMA store shared::cta -> global (bulk-group completion); the tensor
+// map clips rows and columns outside the tensor.  c0 = innermost coordinate.
+MADI_DEV void tma_store_2d(const CUtensorMap *m, const void *smem_src, int c0, int c1) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(m)),
+                 "r"(smem_u32(smem_src)), "r"(c0), "r"(c1)
+                 : "memory");
+}
+MADI_DEV void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until at most N committed bulk groups still read their shared-memory source.
+template <int N> MADI_DEV void bulk_wait_group_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+MADI_DEV void bulk_wait_group_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Generic-proxy shared-memory writes before this fence are visible to later
+// async-proxy (TMA) reads once a barrier orders them.
+MADI_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+MADI_DEV void named_bar_sync(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
 // ------------------------------------------------------------------ tcgen05
 
 MADI_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -207,6 +228,39 @@ MADI_DEV void umma_stage4_ts(uint32_t d_tmem, uint32_t a_tmem, uint32_t desc_lo,
         "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%6];\n\t"
         "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%7];\n\t}" ::"r"(d_tmem),
         "r"(a_tmem), "r"(desc_lo), "r"(desc_hi), "r"(accumulate), "r"(idesc), "r"(bar0), "r"(bar1)
+        : "memory");
+}
+
+// Two consecutive 64-wide K stages in one asm block: the second stage's A
+// columns follow the first's (+32) and its B tile is `desc_step` 16-byte units
+// further; eight MMAs, then four commits (bar0..bar3).
+MADI_DEV void umma_stage8_ts(uint32_t d_tmem, uint32_t a_tmem, uint32_t desc_lo, uint32_t desc_hi, uint32_t desc_step,
+                             uint32_t idesc, uint32_t accumulate, uint32_t bar0, uint32_t bar1, uint32_t bar2,
+                             uint32_t bar3) {
+    asm volatile(
+        "{\n\t.reg .pred p, t;\n\t.reg .b32 a1, a2, a3, a4, a5, a6, a7, l1, l2, l3, l4, l5, l6, l7;\n\t"
+        ".reg .b64 d0, d1, d2, d3, d4, d5, d6, d7;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\tsetp.eq.b32 t, %4, %4;\n\t"
+        "add.u32 a1, %1, 8;\n\tadd.u32 a2, %1, 16;\n\tadd.u32 a3, %1, 24;\n\t"
+        "add.u32 a4, %1, 32;\n\tadd.u32 a5, %1, 40;\n\tadd.u32 a6, %1, 48;\n\tadd.u32 a7, %1, 56;\n\t"
+        "add.u32 l1, %2, 2;\n\tadd.u32 l2, %2, 4;\n\tadd.u32 l3, %2, 6;\n\t"
+        "add.u32 l4, %2, %6;\n\tadd.u32 l5, l4, 2;\n\tadd.u32 l6, l4, 4;\n\tadd.u32 l7, l4, 6;\n\t"
+        "mov.b64 d0, {%2, %3};\n\tmov.b64 d1, {l1, %3};\n\tmov.b64 d2, {l2, %3};\n\tmov.b64 d3, {l3, %3};\n\t"
+        "mov.b64 d4, {l4, %3};\n\tmov.b64 d5, {l5, %3};\n\tmov.b64 d6, {l6, %3};\n\tmov.b64 d7, {l7, %3};\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], d0, %5, p;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [a1], d1, %5, t;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [a2], d2, %5, t;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [a3], d3, %5, t;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [a4], d4, %5, t;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [a5], d5, %5, t;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [a6], d6, %5, t;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [a7], d7, %5, t;\n\t"
+        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%7];\n\t"
+        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%8];\n\t"
+        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%9];\n\t"
+        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%10];\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "r"(desc_lo), "r"(desc_hi), "r"(accumulate), "r"(idesc), "r"(desc_step), "r"(bar0), "r"(bar1),
+        "r"(bar2), "r"(bar3)
         : "memory");
 }
 

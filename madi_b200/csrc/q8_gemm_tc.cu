@@ -33,6 +33,7 @@
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
+#include <string.h>
 
 #include "common.cuh"
 #include "internal.h"
@@ -45,6 +46,9 @@ constexpr int BK = 64;         // K per pipeline stage
 constexpr int A_STAGES = 4;    // TMEM ring of dequantised A stages
 constexpr int MAX_STAGES = 8;  // shared-memory ring depth upper bound
 constexpr int RING_BYTES = 192 * 1024;      // shared-memory ring budget (X + W stages)
+constexpr int Y_ROWS = 32;                 // tokens per epilogue chunk
+constexpr int Y_BUF = Y_ROWS * 128 * 2;    // one f16 [32 tokens][128 features] staging tile
+constexpr int Y_STAGE_BYTES = 2 * 2 * Y_BUF;   // two epilogue halves x double buffer
 constexpr int W_STAGE = BN * BK;           // int8 bytes
 constexpr int A_STAGE_COLS = BK / 2;       // f16 pairs per TMEM column
 constexpr int TMEM_COLS = 512;
@@ -67,7 +71,8 @@ template <int BT> struct Cfg {
     static_assert(BT % 32 == 0 && BT >= 32 && BT <= 256, "MMA N");
     static_assert(STAGES >= 2, "ring depth");
     static constexpr uint32_t IDESC = idesc_f16_f32(BN, BT);
-    static constexpr size_t SMEM = 1024 + (size_t)STAGES * (X_STAGE + W_STAGE) + 256;
+    static constexpr size_t SMEM_BASE = 1024 + (size_t)STAGES * (X_STAGE + W_STAGE) + 256;
+    static_assert(SMEM_BASE + Y_STAGE_BYTES <= 227 * 1024, "shared memory");
 };
 
 struct __align__(8) Bars {
@@ -122,17 +127,50 @@ MADI_DEV void epilogue_chunk(const GemmArgs &p, const uint32_t (&v)[32], int mb,
     }
 }
 
+// 32 consecutive tokens of one feature into the staging tile: col[i * 128] =
+// y[mb + i][n].  Rows past M / features past N are computed from zero-filled
+// operands and clipped by the TMA store; residual reads stay in bounds.
+template <int EPI>
+MADI_DEV void epilogue_chunk_stage(const GemmArgs &p, const uint32_t (&v)[32], int mb, int n, float bias, bool nok,
+                                   __half *col) {
+    float res[32];
+    if constexpr (EPI == kEpiBiasRes) {
+        const size_t base = (size_t)mb * p.N + n;
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+            res[i] = (nok && mb + i < p.M) ? __half2float(p.residual[base + (size_t)i * p.N]) : 0.f;
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        float y = __uint_as_float(v[i]);
+        if constexpr (EPI == kEpiBias) y += bias;
+        if constexpr (EPI == kEpiBiasGelu) y = gelu_erf(y + bias);
+        if constexpr (EPI == kEpiBiasRes) y = y + bias + res[i];
+        col[i * BN] = __float2half_rn(y);
+    }
+}
+
+// Output staging (shared memory + TMA store) for the epilogues without a residual
+// read.  The residual epilogue keeps direct stores and the smaller shared-memory
+// footprint: measured faster for fc2, whose scale reads profit from the larger
+// L1 left beside it.
+template <int EPI> constexpr bool kStagedY = EPI != kEpiBiasRes;
+template <int BT, int EPI> constexpr size_t gemm_smem() {
+    return Cfg<BT>::SMEM_BASE + (kStagedY<EPI> ? Y_STAGE_BYTES : 0);
+}
+
 template <int BT, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     q8_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
-                      const GemmArgs p) {
+                      const __grid_constant__ CUtensorMap tmY, const GemmArgs p, int ystore) {
     using C = Cfg<BT>;
     constexpr int STAGES = C::STAGES;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *xs = smem;
     uint8_t *ws = smem + STAGES * C::X_STAGE;
-    Bars *bars = reinterpret_cast<Bars *>(ws + STAGES * W_STAGE);
+    uint8_t *ystage = ws + STAGES * W_STAGE;
+    Bars *bars = reinterpret_cast<Bars *>(ystage + (kStagedY<EPI> ? Y_STAGE_BYTES : 0));
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int M = p.M, N = p.N, K = p.K;
@@ -210,6 +248,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             constexpr uint32_t kDescStep = C::X_STAGE >> 4;
             const uint32_t empty0 = smem_u32(&bars->empty[0]), aempty0 = smem_u32(&bars->aempty[0]);
             const uint32_t a_tmem0 = tmem + C::A_COL0;
+            const bool pairs = (KT & 1) == 0 && (STAGES & 1) == 0 && (A_STAGES & 1) == 0;
             for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++lt) {
                 const int b = lt & 1;
                 const uint32_t aph = (lt >> 1) & 1;
@@ -217,14 +256,29 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_fence_after();
                 const uint32_t d_tmem = tmem + b * C::ACC_COLS;
                 bool ok = true;
-                for (int kt = 0; kt < KT; ++kt) {
-                    if (!mbar_wait(&bars->aready[a], pha, abort_flag, err)) { ok = false; break; }
-                    tc_fence_after();
-                    // X (MMA) and W (dequant, earlier) of smem stage s consumed; TMEM A stage a reusable
-                    umma_stage4_ts(d_tmem, a_tmem0 + a * A_STAGE_COLS, desc_lo0 + (uint32_t)s * kDescStep, desc_hi,
-                                   C::IDESC, kt != 0, empty0 + 8u * s, aempty0 + 8u * a);
-                    if (++s == STAGES) { s = 0; ph ^= 1; }
-                    if (++a == A_STAGES) { a = 0; pha ^= 1; }
+                if (pairs) {
+                    // two stages per iteration: with KT, STAGES and A_STAGES even, s and a
+                    // stay even and a pair never wraps a ring
+                    for (int kt = 0; kt < KT; kt += 2) {
+                        if (!mbar_wait(&bars->aready[a], pha, abort_flag, err) ||
+                            !mbar_wait(&bars->aready[a + 1], pha, abort_flag, err)) { ok = false; break; }
+                        tc_fence_after();
+                        umma_stage8_ts(d_tmem, a_tmem0 + a * A_STAGE_COLS, desc_lo0 + (uint32_t)s * kDescStep, desc_hi,
+                                       kDescStep, C::IDESC, kt != 0, empty0 + 8u * s, empty0 + 8u * (s + 1),
+                                       aempty0 + 8u * a, aempty0 + 8u * (a + 1));
+                        if ((s += 2) == STAGES) { s = 0; ph ^= 1; }
+                        if ((a += 2) == A_STAGES) { a = 0; pha ^= 1; }
+                    }
+                } else {
+                    for (int kt = 0; kt < KT; ++kt) {
+                        if (!mbar_wait(&bars->aready[a], pha, abort_flag, err)) { ok = false; break; }
+                        tc_fence_after();
+                        // X (MMA) and W (dequant, earlier) of smem stage s consumed; TMEM A stage a reusable
+                        umma_stage4_ts(d_tmem, a_tmem0 + a * A_STAGE_COLS, desc_lo0 + (uint32_t)s * kDescStep, desc_hi,
+                                       C::IDESC, kt != 0, empty0 + 8u * s, aempty0 + 8u * a);
+                        if (++s == STAGES) { s = 0; ph ^= 1; }
+                        if (++a == A_STAGES) { a = 0; pha ^= 1; }
+                    }
                 }
                 if (!ok) break;
                 umma_commit(&bars->accfull[b]);
@@ -341,6 +395,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int half = (warp - kEpiWarp0) >> 2;   // which of the two warps of lane quarter q
         const int r = q * 32 + lane;
         const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+        // With ystore, each half stages its 32-token chunks (all 128 features: the
+        // four warps of the half) in shared memory and one thread writes the chunk
+        // with a TMA store; the two staging tiles of a half alternate.
+        const bool leader = q == 0 && lane == 0;
+        const int bar_id = 1 + half;
+        uint8_t *ybuf = ystage + half * 2 * Y_BUF;
+        int ycnt = 0;
         int lt = 0;
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++lt) {
             const int b = lt & 1;
@@ -348,7 +409,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!warp_wait_all(&bars->accfull[b], aph, abort_flag, err)) break;
             tc_fence_after();
             const int m0 = (tile / n_tiles) * BT;
-            const int n = (tile % n_tiles) * BN + r;
+            const int n0 = (tile % n_tiles) * BN;
+            const int n = n0 + r;
             const bool nok = n < N;
             float bias = 0.f;
             if constexpr (EPI != kEpiNone) {
@@ -364,11 +426,26 @@ __global__ void __launch_bounds__(kThreads, 1)
                 uint32_t v[32];
                 tmem_ld32(acc_addr + c * 32, v);
                 tmem_wait_ld();
-                if (nok) epilogue_chunk<EPI>(p, v, m0 + c * 32, n, bias);
+                if (kStagedY<EPI> && ystore) {
+                    __half *buf = reinterpret_cast<__half *>(ybuf + (ycnt & 1) * Y_BUF);
+                    if (leader) bulk_wait_group_read<1>();   // the store that last used buf has read it
+                    named_bar_sync(bar_id, 128);
+                    epilogue_chunk_stage<EPI>(p, v, m0 + c * 32, n, bias, nok, buf + r);
+                    fence_proxy_async_smem();
+                    named_bar_sync(bar_id, 128);
+                    if (leader) {
+                        tma_store_2d(&tmY, buf, n0, m0 + c * 32);
+                        bulk_commit_group();
+                    }
+                    ++ycnt;
+                } else if (nok) {
+                    epilogue_chunk<EPI>(p, v, m0 + c * 32, n, bias);
+                }
             }
             tc_fence_before();
             mbar_arrive(&bars->accempty[b]);
         }
+        if (leader) bulk_wait_group_all();   // stores complete before shared memory goes away
     }
 
     tc_fence_before();
@@ -380,19 +457,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 template <int BT, int EPI>
-cudaError_t launch_bt(const GemmArgs &a, const CUtensorMap &tmX, const CUtensorMap &tmW, int num_sms,
-                      cudaStream_t st) {
+cudaError_t launch_bt(const GemmArgs &a, const CUtensorMap &tmX, const CUtensorMap &tmW, const CUtensorMap &tmY,
+                      int ystore, int num_sms, cudaStream_t st) {
     using C = Cfg<BT>;
     auto fn = q8_gemm_tc_kernel<BT, EPI>;
     static bool attr_set = false;   // once per instantiation: launches inside a capture stay pure launches
     if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
+        cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem<BT, EPI>());
         if (e != cudaSuccess) return e;
         attr_set = true;
     }
     const int tiles = ((a.N + BN - 1) / BN) * ((a.M + BT - 1) / BT);
     const int grid = tiles < num_sms ? tiles : num_sms;
-    fn<<<grid, kThreads, C::SMEM, st>>>(tmX, tmW, a);
+    fn<<<grid, kThreads, gemm_smem<BT, EPI>(), st>>>(tmX, tmW, tmY, a, ystore);
     return cudaGetLastError();
 }
 
@@ -450,13 +527,20 @@ cudaError_t launch_gemm_tc(const GemmArgs &a, int epi, int num_sms, cudaStream_t
     if (!make_map(&tmW, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.qs, (uint64_t)a.K, (uint64_t)a.N, (uint64_t)a.K, BK, BN,
                   CU_TENSOR_MAP_SWIZZLE_64B))
         return cudaErrorNotSupported;
-#define MADI_GEMM_EPI(BT)                                                          \
-    switch (epi) {                                                                 \
-        case kEpiNone: return launch_bt<BT, kEpiNone>(a, tmX, tmW, num_sms, st);   \
-        case kEpiBias: return launch_bt<BT, kEpiBias>(a, tmX, tmW, num_sms, st);   \
-        case kEpiBiasGelu: return launch_bt<BT, kEpiBiasGelu>(a, tmX, tmW, num_sms, st); \
-        case kEpiBiasRes: return launch_bt<BT, kEpiBiasRes>(a, tmX, tmW, num_sms, st);   \
-        default: return cudaErrorInvalidValue;                                     \
+    // Output through staged TMA stores when the row pitch allows a tensor map
+    // (N * 2 bytes a multiple of 16); otherwise the epilogue stores directly.
+    CUtensorMap tmY;
+    int ystore = a.N % 8 == 0 && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0 &&
+                 make_map(&tmY, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.y, (uint64_t)a.N, (uint64_t)a.M,
+                          (uint64_t)a.N * 2, BN, Y_ROWS, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (!ystore) memset(&tmY, 0, sizeof(tmY));
+#define MADI_GEMM_EPI(BT)                                                                         \
+    switch (epi) {                                                                                \
+        case kEpiNone: return launch_bt<BT, kEpiNone>(a, tmX, tmW, tmY, ystore, num_sms, st);     \
+        case kEpiBias: return launch_bt<BT, kEpiBias>(a, tmX, tmW, tmY, ystore, num_sms, st);     \
+        case kEpiBiasGelu: return launch_bt<BT, kEpiBiasGelu>(a, tmX, tmW, tmY, ystore, num_sms, st); \
+        case kEpiBiasRes: return launch_bt<BT, kEpiBiasRes>(a, tmX, tmW, tmY, ystore, num_sms, st);   \
+        default: return cudaErrorInvalidValue;                                                    \
     }
     if (bt == 192) { MADI_GEMM_EPI(192) }
     MADI_GEMM_EPI(128)
