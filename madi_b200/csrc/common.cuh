@@ -264,6 +264,34 @@ MADI_DEV void umma_stage8_ts(uint32_t d_tmem, uint32_t a_tmem, uint32_t desc_lo,
         : "memory");
 }
 
+// As umma_stage8_ts with two commits (both stages' resources released through
+// one barrier each).
+MADI_DEV void umma_stage8_ts_2c(uint32_t d_tmem, uint32_t a_tmem, uint32_t desc_lo, uint32_t desc_hi,
+                                uint32_t desc_step, uint32_t idesc, uint32_t accumulate, uint32_t bar0, uint32_t bar1) {
+    asm volatile(
+        "{\n\t.reg .pred p, t;\n\t.reg .b32 a1, a2, a3, a4, a5, a6, a7, l1, l2, l3, l4, l5, l6, l7;\n\t"
+        ".reg .b64 d0, d1, d2, d3, d4, d5, d6, d7;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\tsetp.eq.b32 t, %4, %4;\n\t"
+        "add.u32 a1, %1, 8;\n\tadd.u32 a2, %1, 16;\n\tadd.u32 a3, %1, 24;\n\t"
+        "add.u32 a4, %1, 32;\n\tadd.u32 a5, %1, 40;\n\tadd.u32 a6, %1, 48;\n\tadd.u32 a7, %1, 56;\n\t"
+        "add.u32 l1, %2, 2;\n\tadd.u32 l2, %2, 4;\n\tadd.u32 l3, %2, 6;\n\t"
+        "add.u32 l4, %2, %6;\n\tadd.u32 l5, l4, 2;\n\tadd.u32 l6, l4, 4;\n\tadd.u32 l7, l4, 6;\n\t"
+        "mov.b64 d0, {%2, %3};\n\tmov.b64 d1, {l1, %3};\n\tmov.b64 d2, {l2, %3};\n\tmov.b64 d3, {l3, %3};\n\t"
+        "mov.b64 d4, {l4, %3};\n\tmov.b64 d5, {l5, %3};\n\tmov.b64 d6, {l6, %3};\n\tmov.b64 d7, {l7, %3};\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], d0, %5, p;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [a1], d1, %5, t;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [a2], d2, %5, t;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [a3], d3, %5, t;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [a4], d4, %5, t;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [a5], d5, %5, t;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [a6], d6, %5, t;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [a7], d7, %5, t;\n\t"
+        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%7];\n\t"
+        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%8];\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "r"(desc_lo), "r"(desc_hi), "r"(accumulate), "r"(idesc), "r"(desc_step), "r"(bar0), "r"(bar1)
+        : "memory");
+}
+
 // Arrive on `bar` once every tcgen05 op issued so far by this thread completes.
 MADI_DEV void umma_commit(uint64_t *bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))

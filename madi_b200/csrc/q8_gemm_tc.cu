@@ -59,6 +59,8 @@ constexpr int kThreads = 32 * (kEpiWarp0 + kEpiWarps);
 
 static_assert(BK == 64, "umma_stage4_ts issues four K=16 MMAs per stage");
 
+constexpr size_t kBarsBytes = 512;          // shared memory reserved for struct Bars (checked below)
+
 template <int BT> struct Cfg {
     static constexpr int X_STAGE = BT * BK * 2;   // f16 bytes
     // as many shared-memory stages as the ring budget holds: DRAM/L2 latency is
@@ -71,7 +73,7 @@ template <int BT> struct Cfg {
     static_assert(BT % 32 == 0 && BT >= 32 && BT <= 256, "MMA N");
     static_assert(STAGES >= 2, "ring depth");
     static constexpr uint32_t IDESC = idesc_f16_f32(BN, BT);
-    static constexpr size_t SMEM_BASE = 1024 + (size_t)STAGES * (X_STAGE + W_STAGE) + 256;
+    static constexpr size_t SMEM_BASE = 1024 + (size_t)STAGES * (X_STAGE + W_STAGE) + kBarsBytes;
     static_assert(SMEM_BASE + Y_STAGE_BYTES <= 227 * 1024, "shared memory");
 };
 
@@ -80,12 +82,20 @@ struct __align__(8) Bars {
     uint64_t empty[MAX_STAGES];  // MMAs of the stage done (tcgen05.commit): X and W both consumed
     uint64_t aready[A_STAGES];   // dequantised A written to TMEM (128 arrivals: one dequant group)
     uint64_t aempty[A_STAGES];   // MMAs reading the TMEM A stage done (tcgen05.commit)
+    // Pair mode (even KT): the MMA thread takes two stages at a time, so readiness
+    // and release are tracked per pair of stages -- half the barrier traffic on
+    // the single MMA-issuing thread.
+    uint64_t empty2[MAX_STAGES / 2];  // both smem stages of a pair consumed (tcgen05.commit)
+    uint64_t aready2[A_STAGES / 2];   // both A stages of a pair written (256 arrivals: both dequant groups)
+    uint64_t aempty2[A_STAGES / 2];   // both A stages of a pair reusable (tcgen05.commit)
     uint64_t accfull[2];       // accumulator ready (tcgen05.commit)
     uint64_t accempty[2];      // epilogue drained the accumulator (one arrival per epilogue thread)
     uint64_t drain;            // final MMA drain
     uint32_t tmem_base;
     int abort;
 };
+
+static_assert(sizeof(Bars) <= kBarsBytes, "Bars must fit the shared memory reserved for it");
 
 // Bounded wait that ignores the abort flag (used to drain in-flight work).
 MADI_DEV void mbar_wait_drain(uint64_t *bar, uint32_t parity) {
@@ -178,6 +188,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int num_tiles = n_tiles * ((M + BT - 1) / BT);
     const int KT = (K + BK - 1) / BK;
     const int nkb = K / 32;
+    // pair mode: KT, STAGES and A_STAGES even, so a pair of stages never wraps a
+    // ring or spans two tiles
+    const bool pairs = (KT & 1) == 0 && (STAGES & 1) == 0 && (A_STAGES & 1) == 0;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -187,6 +200,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int a = 0; a < A_STAGES; ++a) {
             mbar_init(&bars->aready[a], 128);
             mbar_init(&bars->aempty[a], 1);
+        }
+        for (int i = 0; i < MAX_STAGES / 2; ++i) mbar_init(&bars->empty2[i], 1);
+        for (int i = 0; i < A_STAGES / 2; ++i) {
+            mbar_init(&bars->aready2[i], 256);
+            mbar_init(&bars->aempty2[i], 1);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&bars->accfull[b], 1);
@@ -218,7 +236,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
                 const int m0 = (tile / n_tiles) * BT, n0 = (tile % n_tiles) * BN;
                 for (int kt = 0; kt < KT; ++kt) {
-                    if (!mbar_wait(&bars->empty[s], ph ^ 1, abort_flag, err)) goto producer_done;
+                    if (!mbar_wait(pairs ? &bars->empty2[s >> 1] : &bars->empty[s], ph ^ 1, abort_flag, err))
+                        goto producer_done;
                     mbar_arrive_expect_tx(&bars->full[s], C::X_STAGE + W_STAGE);
                     tma_load_2d(xs + s * C::X_STAGE, &tmX, &bars->full[s], kt * BK, m0);
                     tma_load_2d(ws + s * W_STAGE, &tmW, &bars->full[s], kt * BK, n0);
@@ -248,7 +267,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             constexpr uint32_t kDescStep = C::X_STAGE >> 4;
             const uint32_t empty0 = smem_u32(&bars->empty[0]), aempty0 = smem_u32(&bars->aempty[0]);
             const uint32_t a_tmem0 = tmem + C::A_COL0;
-            const bool pairs = (KT & 1) == 0 && (STAGES & 1) == 0 && (A_STAGES & 1) == 0;
+            const uint32_t empty2_0 = smem_u32(&bars->empty2[0]), aempty2_0 = smem_u32(&bars->aempty2[0]);
             for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++lt) {
                 const int b = lt & 1;
                 const uint32_t aph = (lt >> 1) & 1;
@@ -257,15 +276,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t d_tmem = tmem + b * C::ACC_COLS;
                 bool ok = true;
                 if (pairs) {
-                    // two stages per iteration: with KT, STAGES and A_STAGES even, s and a
-                    // stay even and a pair never wraps a ring
+                    // two stages per iteration (s and a stay even): one readiness wait and
+                    // two release commits per pair; pair slot a / 2, phase pha
                     for (int kt = 0; kt < KT; kt += 2) {
-                        if (!mbar_wait(&bars->aready[a], pha, abort_flag, err) ||
-                            !mbar_wait(&bars->aready[a + 1], pha, abort_flag, err)) { ok = false; break; }
+                        if (!mbar_wait(&bars->aready2[a >> 1], pha, abort_flag, err)) { ok = false; break; }
                         tc_fence_after();
-                        umma_stage8_ts(d_tmem, a_tmem0 + a * A_STAGE_COLS, desc_lo0 + (uint32_t)s * kDescStep, desc_hi,
-                                       kDescStep, C::IDESC, kt != 0, empty0 + 8u * s, empty0 + 8u * (s + 1),
-                                       aempty0 + 8u * a, aempty0 + 8u * (a + 1));
+                        umma_stage8_ts_2c(d_tmem, a_tmem0 + a * A_STAGE_COLS, desc_lo0 + (uint32_t)s * kDescStep,
+                                          desc_hi, kDescStep, C::IDESC, kt != 0, empty2_0 + 8u * (s >> 1),
+                                          aempty2_0 + 8u * (a >> 1));
                         if ((s += 2) == STAGES) { s = 0; ph ^= 1; }
                         if ((a += 2) == A_STAGES) { a = 0; pha ^= 1; }
                     }
@@ -339,7 +357,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         // done or aborted
         auto visit = [&](int tile, uint2 swv) -> bool {
             if (tile >= num_tiles) return false;
-            if (!warp_wait_all(&bars->aempty[as], pha ^ 1u, abort_flag, err)) return false;
+            if (!warp_wait_all(pairs ? &bars->aempty2[as >> 1] : &bars->aempty[as], pha ^ 1u, abort_flag, err))
+                return false;
             if (!warp_wait_all(&bars->full[s], ph, abort_flag, err)) return false;
             const uint32_t sw = pair_ok ? swv.x : (swv.x | (swv.y << 16));
             const __half2 sw2 = *reinterpret_cast<const __half2 *>(&sw);
@@ -362,7 +381,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_st32(tmem + lane_addr + C::A_COL0 + as * A_STAGE_COLS, a);
             tmem_wait_st();
             tc_fence_before();
-            mbar_arrive(&bars->aready[as]);
+            mbar_arrive(pairs ? &bars->aready2[as >> 1] : &bars->aready[as]);
             s += 2;
             if (s >= STAGES) { s -= STAGES; ph ^= 1u; }
             as += 2;
