@@ -1,0 +1,60 @@
+"""Run one Q8 linear shape a few times on cuda:0 -- a fixed workload to time or to
+put under a profiler (ncu -k regex:<kernel> -s <skip> -c <count> ...).
+
+    python -m madi_b200.cases gemv --n 51866 --k 1280 --m 8 --x f16 --iters 6
+    python -m madi_b200.cases gemm --m 24000 --n 5120 --k 1280 --epi gelu --iters 3
+
+Inputs are seeded random tensors of the given shape (int8 weights in [-127, 127],
+f16 scales in [1e-4, 2.1e-3], N(0,1) activations); the script prints the mean
+device time per call from CUDA events, between an L2-evicting read of a 256 MB
+buffer and each call.
+"""
+import argparse
+
+import torch
+
+from . import init, q8
+
+EPIS = {"none": q8.EPI_NONE, "bias": q8.EPI_BIAS, "gelu": q8.EPI_BIAS_GELU, "res": q8.EPI_BIAS_RES}
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("kind", choices=["gemv", "gemm"])
+    ap.add_argument("--m", type=int, required=True)
+    ap.add_argument("--n", type=int, required=True)
+    ap.add_argument("--k", type=int, required=True)
+    ap.add_argument("--x", choices=["f16", "f32"], default="f16")
+    ap.add_argument("--epi", choices=sorted(EPIS), default="none")
+    ap.add_argument("--iters", type=int, default=6)
+    a = ap.parse_args(argv)
+    init(0)
+    dev = torch.device("cuda:0")
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234)
+    W = q8.Q8Weight(torch.randint(-127, 128, (a.n, a.k), dtype=torch.int8, device=dev, generator=g),
+                    (torch.rand((a.n, a.k // 32), device=dev, generator=g) * 2e-3 + 1e-4).half())
+    xdt = torch.float32 if a.x == "f32" else torch.float16
+    if a.kind == "gemm":
+        xdt = torch.float16
+    x = torch.randn((a.m, a.k), device=dev, generator=g).to(xdt)
+    ydt = xdt if a.kind == "gemm" else torch.float32
+    bias = torch.randn(a.n, device=dev, generator=g) * 0.02
+    epi = EPIS[a.epi]
+    y = torch.zeros((a.m, a.n), dtype=ydt, device=dev)
+    flush = torch.zeros(64 << 20, dtype=torch.int32, device=dev)
+    ts = []
+    for _ in range(a.iters):
+        flush.sum()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        q8.linear(W, x, bias=bias if epi != q8.EPI_NONE else None, epi=epi,
+                  residual=y if epi == q8.EPI_BIAS_RES else None, out=y)
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1) * 1e3)
+    print(f"{a.kind} M={a.m} N={a.n} K={a.k} x={a.x} epi={a.epi}: mean {sum(ts) / len(ts):.2f} us over {len(ts)} calls")
+
+
+if __name__ == "__main__":
+    main()
