@@ -159,6 +159,15 @@ def max_over_ranks(world, v):
 
 
 # ----------------------------------------------------------------------------- CPU (reference) timing
+def host_threads() -> int:
+    """Host threads this process may use (its CPU affinity mask).  torchrun sets
+    OMP_NUM_THREADS=1 per rank, so the OpenMP default is not used."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def cpu_ffn_sample(rows, seconds, nthreads=None):
     """The reference's CPU computation of the FFN pair (f32 dequant + accumulate,
     oracle/q8_oracle.c madi_orc_linear_f32_baseline) on `rows` frames, repeated
@@ -169,7 +178,7 @@ def cpu_ffn_sample(rows, seconds, nthreads=None):
     oracle.build()
     w = synth.ffn_weights(0)
     x = synth.activations(rows, D, 1)
-    nt = nthreads or oracle.max_threads()
+    nt = nthreads or host_threads()
     flops = 2.0 * rows * F * D * 2
     t0 = time.perf_counter()
     n = 0
@@ -191,10 +200,11 @@ def run_reference(args, world, rank):
     from oracle import oracle
     oracle.build()
     rows = 96                      # bounded sample of the 24000-frame step
+    nt = host_threads()
     per = []
     for i in range(args.warmup + args.steps):
         t0 = time.perf_counter()
-        tf, nt, _ = cpu_ffn_sample(rows, 0.0)
+        tf, _, _ = cpu_ffn_sample(rows, 0.0, nthreads=nt)
         if i >= args.warmup:
             per.append(time.perf_counter() - t0)
     flops = 2.0 * rows * F * D * 2
@@ -206,7 +216,7 @@ def run_reference(args, world, rank):
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": f"config1 encoder FFN pair, B={args.batch} chunks (M={args.batch * SEQ})",
                        "cpu_sample_rows": rows},
-            "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": oracle.max_threads(), "kind": "port",
+            "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": nt, "kind": "port",
                              "sample": sample},
             "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -430,19 +440,48 @@ def decode_leg(args, world, rank, dev, stream, peaks):
         e1.record(stream)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / K
-    ag_ms = None
+    ag = {}
     if world > 1:
-        # column-split head: gather every rank's logit shard (NCCL over NVLink) and
-        # take the greedy tokens, as the multi-GPU decode step does
-        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a0.record()
-        for i in range(K):
-            graphs[i % 2].replay()
-            full = shard.allgather_logits(logits, V, world)
-            shard.greedy_tokens(full)
-        a1.record()
-        torch.cuda.synchronize()
-        ag_ms = max_over_ranks(world, a0.elapsed_time(a1) / K)
+        # column-split head: the greedy token needs every rank's shard.  Two equal-
+        # result exchanges over NCCL, each captured in the step's graph (every rank
+        # captures and replays the same sequence): the whole logit shards, or only
+        # each shard's per-row (max, argmax) pair.
+        def make_step(kind):
+            def step(s):
+                token_step(*s)
+                if kind == "logits":
+                    return shard.greedy_tokens(shard.allgather_logits(logits, V, world))
+                return shard.allgather_greedy(logits, V, world, rank)
+            return step
+
+        for kind in ("logits", "argmax_pairs"):
+            step = make_step(kind)
+            ag_graphs, how = [], "CUDA graph (NCCL all-gather captured)"
+            try:
+                with torch.cuda.stream(stream):
+                    for s in sets:
+                        step(s)
+                    torch.cuda.synchronize()
+                    for s in sets:
+                        g = torch.cuda.CUDAGraph()
+                        with torch.cuda.graph(g, stream=stream, capture_error_mode="thread_local"):
+                            step(s)
+                        ag_graphs.append(g)
+            except Exception as e:                 # capture refused: eager exchange
+                ag_graphs, how = [], f"eager all-gather ({type(e).__name__})"
+            barrier(world)
+            a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(stream):
+                a0.record(stream)
+                for i in range(K):
+                    if ag_graphs:
+                        ag_graphs[i % 2].replay()
+                    else:
+                        step(sets[i % 2])
+                a1.record(stream)
+            torch.cuda.synchronize()
+            ag[kind] = {"ms": max_over_ranks(world, a0.elapsed_time(a1) / K), "timing": how}
+            del ag_graphs
     ms_max = max_over_ranks(world, ms)
     del graphs
 
@@ -497,7 +536,9 @@ def decode_leg(args, world, rank, dev, stream, peaks):
     return {"value": bytes_step * world / (ms_max / 1e3) / 1e9, "unit": "GB/s", "m_tokens": Md,
             "activations": args.decode_x, "bytes_per_step_per_gpu": bytes_step, "ms_per_token_step": ms_max,
             "step_GBps_per_gpu": gbs, "gpu_launches_per_step": 25, "head_rows_per_gpu": hn,
-            "step_with_logit_allgather_ms": ag_ms, "per_shape": per_shape,
+            "step_with_logit_allgather_ms": ag.get("logits", {}).get("ms"),
+            "step_with_argmax_pair_allgather_ms": ag.get("argmax_pairs", {}).get("ms"),
+            "allgather_timing": ag.get("logits", {}).get("timing"), "per_shape": per_shape,
             "roofline": {"bound": "hbm", "kernel": f"q8_gemv_tile_kernel (vocab head {hn}x{D}, M={Md}, "
                                                   "back-to-back launches in a CUDA graph)",
                          "achieved": head["GBps"], "peak": peaks["hbm"], "unit": "GB/s",

@@ -51,9 +51,10 @@ def greedy_tokens(logits: torch.Tensor) -> torch.Tensor:
 
 def shard_argmax(local: torch.Tensor, h0: int) -> Tuple[torch.Tensor, torch.Tensor]:
     """Per-row (max value, global index) of a shard -- the cheap alternative to gathering
-    whole logit rows: gather these pairs and merge with merge_shard_argmax."""
-    v, i = torch.max(local, dim=-1)
-    return v, i + h0
+    whole logit rows: gather these pairs and merge with merge_shard_argmax.  argmax
+    returns the first maximal index, so ties inside a shard go to the lowest index."""
+    i = torch.argmax(local, dim=-1, keepdim=True)
+    return torch.gather(local, -1, i).squeeze(-1), i.squeeze(-1) + h0
 
 
 def merge_shard_argmax(values: torch.Tensor, indices: torch.Tensor) -> torch.Tensor:
@@ -61,3 +62,20 @@ def merge_shard_argmax(values: torch.Tensor, indices: torch.Tensor) -> torch.Ten
     best = values.max(dim=0, keepdim=True).values
     cand = torch.where(values == best, indices, torch.full_like(indices, torch.iinfo(indices.dtype).max))
     return cand.min(dim=0).values
+
+
+def allgather_greedy(local: torch.Tensor, vocab: int, world: int, rank: int, group=None) -> torch.Tensor:
+    """Greedy tokens of the column-split head without gathering whole logit rows:
+    each rank contributes its shard's per-row (max, argmax) and the pairs are merged
+    with the lowest-index tie rule -- the same tokens as greedy_tokens(allgather_logits(...))."""
+    import torch.distributed as dist
+    h0, _ = vocab_shard(vocab, world, rank)
+    v, i = shard_argmax(local, h0)
+    if world == 1:
+        return i
+    m = v.shape[0]
+    vs = torch.empty((world * m,), dtype=v.dtype, device=v.device)     # rank-major concatenation
+    is_ = torch.empty((world * m,), dtype=i.dtype, device=i.device)
+    dist.all_gather_into_tensor(vs, v.contiguous(), group=group)
+    dist.all_gather_into_tensor(is_, i.contiguous(), group=group)
+    return merge_shard_argmax(vs.view(world, m), is_.view(world, m))

@@ -65,7 +65,9 @@ def _worker(rank, world, port, mode, q):
         dist.all_gather(vs, v)
         dist.all_gather(is_, i)
         merged = shard.merge_shard_argmax(torch.stack(vs), torch.stack(is_))
-        q.put((rank, ok_gather, tok.tolist(), merged.tolist(), int(np.argmax(full[1])), int(np.argmax(full[2]))))
+        pairs = shard.allgather_greedy(local, V, world, rank)      # (max, argmax) pairs only
+        q.put((rank, ok_gather, tok.tolist(), merged.tolist(), int(np.argmax(full[1])), int(np.argmax(full[2])),
+               pairs.tolist()))
     except Exception as e:  # reported to the parent, never hangs
         q.put((rank, "error", repr(e)))
     finally:
@@ -95,6 +97,7 @@ def test_vocab_allgather_and_greedy_merge_two_ranks():
         assert r[2][0] == 5 and r[3][0] == 5           # tie across shards -> lowest index
         assert r[2][1] == r[4] and r[2][2] == r[5]
         assert r[3] == r[2]
+        assert r[6] == r[2]                             # pair gather = full-row gather
 
 
 def test_a_failing_rank_is_reported_not_hung():
