@@ -91,6 +91,10 @@ int   madi_download(void *dst_host, const void *src_device, size_t size);
  *   mul_mm_q8          (C f16, A f16, qs, scales, M, N, K)                  q8_gemm.metal:29
  *   m4_gemm_q8tg       (A f16, Wq, scales, C f16, bias f32, M, N, K, act_gelu u32)  m4_gemm.metal:196
  *   m4_gemm_q8_bias_gelu (same arguments as m4_gemm_q8tg)                   m4_gemm.metal:131
+ *   bias_res_ln_f16    (X f32, MO f16, bias f32, Y f16, gamma f32, beta f32, D u32, eps f32)
+ *                      rows = grid_x, as the reference's grid                encoder_ops.metal:333
+ *   layer_norm_f16     (X f32, Y f16, gamma f32, beta f32, D u32, eps f32)
+ *                      rows = grid_x                                        encoder_ops.metal:305
  * On success *out_id holds a handle for madi_dispatch. */
 int   madi_get_function(const char *name, int *out_id);
 
@@ -98,8 +102,9 @@ int   madi_get_function(const char *name, int *out_id);
  * value and `arg_sizes[i]` is its size -- the cuLaunchKernel kernelParams
  * convention the reference uses.  Pointer arguments must be device pointers
  * (madi_alloc'd, base or interior, or any other device allocation).  The
- * grid/block values are accepted for compatibility and ignored: each B200
- * kernel picks its own launch shape.  Inside begin/commit the launch is
+ * grid/block values are accepted for compatibility and ignored -- each B200
+ * kernel picks its own launch shape -- except grid_x of the two LayerNorm
+ * kernels, which is their row count as in the reference.  Inside begin/commit the launch is
  * recorded into the open command buffer, otherwise it is enqueued at once. */
 int   madi_dispatch(int func_id,
                     uint32_t grid_x, uint32_t grid_y, uint32_t grid_z,
@@ -175,6 +180,24 @@ int madi_q8_dequant_f16(const madi_q8w *w, uint16_t *out, void *stream);
  * reference's quantiser (round half away from zero on w * (1/s_f32)). */
 int madi_q8_quantize_f16(const uint16_t *w, int rows, int dim,
                          int8_t *qs, uint16_t *scales, void *stream);
+
+/* ======================= residual + LayerNorm beside the linear ============ */
+
+/* bias_res_ln_f16 (encoder_ops.metal:333-364), the encoder's step after the
+ * out-projection / fc2: for each of `rows` rows of width d,
+ *   x[r][i] += float(mo[r][i]) + bias[i]      (f32 residual stream, in place)
+ *   y[r][i]  = half((x[r][i] - mean) * rsqrt(var + eps) * gamma[i] + beta[i])
+ * with mean and var over the updated row (two passes).  x is updated exactly as
+ * the reference does ((x + mo) + bias in f32).  128 <= d <= 2048, d % 128 == 0;
+ * f32 buffers 16-byte and f16 buffers 8-byte aligned. */
+int madi_bias_res_ln_f16(float *x, const uint16_t *mo, const float *bias, uint16_t *y,
+                         const float *gamma, const float *beta, int rows, int d, float eps,
+                         void *stream);
+
+/* layer_norm_f16 (encoder_ops.metal:305-331): y = half(LN(x) * gamma + beta),
+ * x f32 [rows][d] unchanged.  Same shape and alignment rules. */
+int madi_layer_norm_f16(const float *x, uint16_t *y, const float *gamma, const float *beta,
+                        int rows, int d, float eps, void *stream);
 
 #ifdef __cplusplus
 }

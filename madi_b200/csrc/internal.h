@@ -55,6 +55,12 @@ cudaError_t launch_gemm_tc(const GemmArgs &a, int epi, int num_sms, cudaStream_t
 // The smallest M routed to variant (a) by madi_q8_linear.
 constexpr int kGemmMinM = 9;
 
+// ---------------------------------------------------------------- residual + LayerNorm (res_ln.cu)
+constexpr int kLnMaxD = 2048;   // row width limit of the register-resident row kernel (D % 128 == 0)
+// MO == nullptr: layer_norm_f16; else bias_res_ln_f16 (X updated in place).
+cudaError_t launch_res_ln(float *X, const __half *MO, const float *bias, __half *Y, const float *gamma,
+                          const float *beta, int rows, int D, float eps, cudaStream_t st);
+
 // ---------------------------------------------------------------- misc kernels
 cudaError_t launch_dequant_f16(const int8_t *qs, const __half *scales, int N, int K, __half *out, cudaStream_t st);
 cudaError_t launch_quantize_f16(const __half *w, int rows, int dim, int8_t *qs, __half *scales, cudaStream_t st);

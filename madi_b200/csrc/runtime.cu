@@ -191,7 +191,7 @@ struct ArgVal {
     uint32_t u;
     float f;
 };
-using Handler = int (*)(const ArgVal *a, cudaStream_t st);
+using Handler = int (*)(const ArgVal *a, uint32_t gx, cudaStream_t st);   // gx: dispatch grid x
 
 struct Op {
     const char *name;
@@ -204,48 +204,60 @@ madi_q8w mkw(const ArgVal &qs, const ArgVal &sc, uint32_t n, uint32_t k) {
 }
 
 // gemv_q8(out, qs, scales, x, N, K)  graph_helpers.metal:390-422
-int h_gemv(const ArgVal *a, cudaStream_t st) {
+int h_gemv(const ArgVal *a, uint32_t gx, cudaStream_t st) {
     madi_q8w w = mkw(a[1], a[2], a[4].u, a[5].u);
     return q8_linear_impl(&w, a[3].p, MADI_F32, 1, nullptr, MADI_F32, MADI_EPI_NONE, nullptr, const_cast<void *>(a[0].p),
                           MADI_F32, st, "gemv_q8");
 }
 // gemv_q8_bias / _bias_gelu / _bias_res(out, qs, scales, x, bias, N, K)  graph_helpers.metal:424-519
 template <int EPI>
-int h_gemv_bias(const ArgVal *a, cudaStream_t st) {
+int h_gemv_bias(const ArgVal *a, uint32_t gx, cudaStream_t st) {
     madi_q8w w = mkw(a[1], a[2], a[5].u, a[6].u);
     return q8_linear_impl(&w, a[3].p, MADI_F32, 1, a[4].p, MADI_F32, EPI, EPI == MADI_EPI_BIAS_RES ? a[0].p : nullptr,
                           const_cast<void *>(a[0].p), MADI_F32, st, "gemv_q8_bias*");
 }
 // gemv_q8_qkv(q_out, qs, scales, x, qb, vb, kc, vc, pos_ptr, D)  graph_helpers.metal:527-567
-int h_qkv(const ArgVal *a, cudaStream_t st) {
+int h_qkv(const ArgVal *a, uint32_t gx, cudaStream_t st) {
     madi_q8w w = mkw(a[1], a[2], 3 * a[9].u, a[9].u);
     return q8_qkv_impl(&w, static_cast<const float *>(a[3].p), 1, static_cast<const float *>(a[4].p),
                        static_cast<const float *>(a[5].p), (float *)a[0].p, (float *)a[6].p, (float *)a[7].p,
                        static_cast<const uint32_t *>(a[8].p), 0, st, "gemv_q8_qkv");
 }
 // logit_gemv_q8(logits, qs, scales, x, vocab, dim)  graph_helpers.metal:320-352
-int h_logit(const ArgVal *a, cudaStream_t st) {
+int h_logit(const ArgVal *a, uint32_t gx, cudaStream_t st) {
     madi_q8w w = mkw(a[1], a[2], a[4].u, a[5].u);
     return q8_linear_impl(&w, a[3].p, MADI_F32, 1, nullptr, MADI_F32, MADI_EPI_NONE, nullptr, const_cast<void *>(a[0].p),
                           MADI_F32, st, "logit_gemv_q8");
 }
 // dequant_q8_f16(out, qs, scales, N, K)  q8_gemm.metal:12-27
-int h_dequant(const ArgVal *a, cudaStream_t st) {
+int h_dequant(const ArgVal *a, uint32_t gx, cudaStream_t st) {
     madi_q8w w = mkw(a[1], a[2], a[3].u, a[4].u);
     return madi_q8_dequant_f16(&w, (uint16_t *)a[0].p, st);
 }
 // mul_mm_q8(C, A, qs, scales, M, N, K)  q8_gemm.metal:29-102
-int h_mul_mm(const ArgVal *a, cudaStream_t st) {
+int h_mul_mm(const ArgVal *a, uint32_t gx, cudaStream_t st) {
     madi_q8w w = mkw(a[2], a[3], a[5].u, a[6].u);
     return q8_linear_impl(&w, a[1].p, MADI_F16, (int)a[4].u, nullptr, MADI_F32, MADI_EPI_NONE, nullptr,
                           const_cast<void *>(a[0].p), MADI_F16, st, "mul_mm_q8");
 }
 // m4_gemm_q8tg / m4_gemm_q8_bias_gelu(A, Wq, scales, C, bias, M, N, K, act_gelu)  m4_gemm.metal:131-266
-int h_m4_q8(const ArgVal *a, cudaStream_t st) {
+int h_m4_q8(const ArgVal *a, uint32_t gx, cudaStream_t st) {
     madi_q8w w = mkw(a[1], a[2], a[6].u, a[7].u);
     return q8_linear_impl(&w, a[0].p, MADI_F16, (int)a[5].u, a[4].p, MADI_F32,
                           a[8].u ? MADI_EPI_BIAS_GELU : MADI_EPI_BIAS, nullptr, const_cast<void *>(a[3].p), MADI_F16, st,
                           "m4_gemm_q8");
+}
+
+// bias_res_ln_f16(X, MO, bias, Y, gamma, beta, D, eps), rows = grid x   encoder_ops.metal:333-364
+int h_bias_res_ln(const ArgVal *a, uint32_t gx, cudaStream_t st) {
+    return madi_bias_res_ln_f16((float *)a[0].p, static_cast<const uint16_t *>(a[1].p), static_cast<const float *>(a[2].p),
+                                (uint16_t *)a[3].p, static_cast<const float *>(a[4].p), static_cast<const float *>(a[5].p),
+                                (int)gx, (int)a[6].u, a[7].f, st);
+}
+// layer_norm_f16(X, Y, gamma, beta, D, eps), rows = grid x   encoder_ops.metal:305-331
+int h_layer_norm(const ArgVal *a, uint32_t gx, cudaStream_t st) {
+    return madi_layer_norm_f16(static_cast<const float *>(a[0].p), (uint16_t *)a[1].p, static_cast<const float *>(a[2].p),
+                               static_cast<const float *>(a[3].p), (int)gx, (int)a[4].u, a[5].f, st);
 }
 
 const std::vector<Op> &ops() {
@@ -260,6 +272,8 @@ const std::vector<Op> &ops() {
         {"mul_mm_q8", {kPtr, kPtr, kPtr, kPtr, kU32, kU32, kU32}, h_mul_mm},
         {"m4_gemm_q8tg", {kPtr, kPtr, kPtr, kPtr, kPtr, kU32, kU32, kU32, kU32}, h_m4_q8},
         {"m4_gemm_q8_bias_gelu", {kPtr, kPtr, kPtr, kPtr, kPtr, kU32, kU32, kU32, kU32}, h_m4_q8},
+        {"bias_res_ln_f16", {kPtr, kPtr, kPtr, kPtr, kPtr, kPtr, kU32, kF32}, h_bias_res_ln},
+        {"layer_norm_f16", {kPtr, kPtr, kPtr, kPtr, kU32, kF32}, h_layer_norm},
     };
     return table;
 }
@@ -384,7 +398,7 @@ int madi_get_function(const char *name, int *out_id) {
 
 int madi_dispatch(int func_id, uint32_t gx, uint32_t gy, uint32_t gz, uint32_t bx, uint32_t by, uint32_t bz,
                   const void **args, const size_t *arg_sizes, int n_args) {
-    (void)gx; (void)gy; (void)gz; (void)bx; (void)by; (void)bz;
+    (void)gy; (void)gz; (void)bx; (void)by; (void)bz;   // gx: row count of the LayerNorm kernels
     if (!S.ready) return fail(MADI_ENOINIT, "madi_dispatch: not initialised");
     const auto &t = ops();
     if (func_id < 0 || func_id >= (int)t.size()) return fail(MADI_EINVAL, "madi_dispatch: bad function id %d", func_id);
@@ -419,7 +433,7 @@ int madi_dispatch(int func_id, uint32_t gx, uint32_t gy, uint32_t gz, uint32_t b
         cudaEventCreate(&e0);
         cudaEventCreate(&e1);
         cudaEventRecord(e0, S.stream);
-        int rc = op.fn(v, S.stream);
+        int rc = op.fn(v, gx, S.stream);
         cudaEventRecord(e1, S.stream);
         cudaEventSynchronize(e1);
         float ms = 0.f;
@@ -429,7 +443,7 @@ int madi_dispatch(int func_id, uint32_t gx, uint32_t gy, uint32_t gz, uint32_t b
         if (rc == MADI_OK) prof_add(op.name, ms);
         return rc;
     }
-    return op.fn(v, S.stream);
+    return op.fn(v, gx, S.stream);
 }
 
 int madi_begin_command_buffer(void) {
@@ -552,6 +566,37 @@ int madi_q8_quantize_f16(const uint16_t *w, int rows, int dim, int8_t *qs, uint1
     cudaError_t e = launch_quantize_f16(reinterpret_cast<const __half *>(w), rows, dim, qs,
                                         reinterpret_cast<__half *>(scales), pick_stream(stream));
     return e == cudaSuccess ? MADI_OK : cuda_fail(e, "madi_q8_quantize_f16");
+}
+
+namespace {
+int res_ln_impl(float *x, const uint16_t *mo, const float *bias, uint16_t *y, const float *gamma, const float *beta,
+                int rows, int d, float eps, void *stream, const char *who) {
+    if (!S.ready) return fail(MADI_ENOINIT, "%s: not initialised", who);
+    if (!x || !y || !gamma || !beta || (mo && !bias)) return fail(MADI_EINVAL, "%s: null argument", who);
+    if (rows < 0 || d < 128 || d > kLnMaxD || d % 128)
+        return fail(MADI_EINVAL, "%s: rows=%d, D=%d (need 128 <= D <= %d, D %% 128 == 0)", who, rows, d, kLnMaxD);
+    if (!(eps >= 0.f) || eps > 1.f) return fail(MADI_EINVAL, "%s: eps=%g", who, (double)eps);
+    if (!aligned(x, 16) || !aligned(gamma, 16) || !aligned(beta, 16) || !aligned(y, 8) || (mo && !aligned(mo, 8)) ||
+        (bias && !aligned(bias, 16)))
+        return fail(MADI_EINVAL, "%s: misaligned buffer (f32 rows 16-byte, f16 rows 8-byte aligned)", who);
+    if ((size_t)rows * (size_t)d >= (1ull << 31)) return fail(MADI_EINVAL, "%s: too large", who);
+    if (rows == 0) return MADI_OK;
+    cudaError_t e = launch_res_ln(x, reinterpret_cast<const __half *>(mo), bias, reinterpret_cast<__half *>(y), gamma,
+                                  beta, rows, d, eps, pick_stream(stream));
+    return e == cudaSuccess ? MADI_OK : cuda_fail(e, who);
+}
+}  // namespace
+
+int madi_bias_res_ln_f16(float *x, const uint16_t *mo, const float *bias, uint16_t *y, const float *gamma,
+                         const float *beta, int rows, int d, float eps, void *stream) {
+    if (!mo) return fail(MADI_EINVAL, "madi_bias_res_ln_f16: null MO");
+    return res_ln_impl(x, mo, bias, y, gamma, beta, rows, d, eps, stream, "madi_bias_res_ln_f16");
+}
+
+int madi_layer_norm_f16(const float *x, uint16_t *y, const float *gamma, const float *beta, int rows, int d, float eps,
+                        void *stream) {
+    return res_ln_impl(const_cast<float *>(x), nullptr, nullptr, y, gamma, beta, rows, d, eps, stream,
+                       "madi_layer_norm_f16");
 }
 
 }  // extern "C"

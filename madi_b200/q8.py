@@ -117,3 +117,42 @@ def quantize_f16(w: torch.Tensor, stream=None) -> Q8Weight:
     _lib.check(_lib.load().madi_q8_quantize_f16(w.data_ptr(), rows, dim, qs.data_ptr(), sc.data_ptr(),
                                                 _stream(stream)), "madi_q8_quantize_f16")
     return Q8Weight(qs, sc)
+
+
+def _ln_check(x, gamma, beta):
+    if x.dim() != 2 or x.dtype != torch.float32 or not x.is_contiguous():
+        raise ValueError("x must be a contiguous f32 [rows][d] tensor")
+    d = x.shape[1]
+    for t, nm in ((gamma, "gamma"), (beta, "beta")):
+        if t.dtype != torch.float32 or t.shape != (d,) or not t.is_contiguous():
+            raise ValueError(f"{nm} must be a contiguous f32 [{d}] tensor")
+    return x.shape[0], d
+
+
+def bias_res_ln_f16(x: torch.Tensor, mo: torch.Tensor, bias: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor,
+                    eps: float = 1e-5, out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+    """bias_res_ln_f16 (encoder_ops.metal:333-364): x (f32, updated in place) +=
+    mo (f16) + bias (f32); returns LayerNorm(x) * gamma + beta as f16."""
+    rows, d = _ln_check(x, gamma, beta)
+    if mo.dtype != torch.float16 or mo.shape != x.shape or not mo.is_contiguous():
+        raise ValueError("mo must be a contiguous f16 tensor shaped like x")
+    if bias.dtype != torch.float32 or bias.shape != (d,):
+        raise ValueError("bias must be f32 [d]")
+    if out is None:
+        out = torch.empty((rows, d), dtype=torch.float16, device=x.device)
+    rc = _lib.load().madi_bias_res_ln_f16(x.data_ptr(), mo.data_ptr(), bias.data_ptr(), out.data_ptr(),
+                                          gamma.data_ptr(), beta.data_ptr(), rows, d, float(eps), _stream(stream))
+    _lib.check(rc, "madi_bias_res_ln_f16")
+    return out
+
+
+def layer_norm_f16(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, eps: float = 1e-5,
+                   out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+    """layer_norm_f16 (encoder_ops.metal:305-331): f16 LayerNorm(x) * gamma + beta of f32 x."""
+    rows, d = _ln_check(x, gamma, beta)
+    if out is None:
+        out = torch.empty((rows, d), dtype=torch.float16, device=x.device)
+    rc = _lib.load().madi_layer_norm_f16(x.data_ptr(), out.data_ptr(), gamma.data_ptr(), beta.data_ptr(), rows, d,
+                                         float(eps), _stream(stream))
+    _lib.check(rc, "madi_layer_norm_f16")
+    return out

@@ -44,6 +44,7 @@ def lib():
         L.madi_orc_gemv_q8_qkv.argtypes = [P, I, P, P, I, P, P, P, P, P, P]
         L.madi_orc_argmax.argtypes, L.madi_orc_argmax.restype = [P, I], I
         L.madi_orc_linear_f32_baseline.argtypes = [P, I, I, P, P, I, P, I, P, P, I]
+        L.madi_orc_bias_res_ln.argtypes = [P, P, P, P, P, I, I, F, P]
         L.madi_orc_linear_f32_baseline.restype = I
         L.madi_orc_max_threads.restype = I
         _lib = L
@@ -153,3 +154,17 @@ def linear_f32_baseline(X, qs, scales, bias=None, epi=EPI_NONE, residual=None, n
 
 def max_threads() -> int:
     return lib().madi_orc_max_threads()
+
+
+def bias_res_ln(x, mo=None, bias=None, gamma=None, beta=None, eps=1e-5):
+    """bias_res_ln_f16 / layer_norm_f16 restated (encoder_ops.metal:305-364).
+    x f32 [rows][d] (not modified here); mo f16 [rows][d] or None.  Returns
+    (x updated in f32, y exact in f64)."""
+    x2 = _c(x, np.float32).copy()
+    rows, d = x2.shape
+    y = np.empty((rows, d), dtype=np.float64)
+    mo_c = None if mo is None else _c(mo, np.float16).view(np.uint16)
+    lib().madi_orc_bias_res_ln(_p(x2), None if mo_c is None else _p(mo_c),
+                               None if bias is None else _p(_c(bias, np.float32)),
+                               _p(_c(gamma, np.float32)), _p(_c(beta, np.float32)), rows, d, float(eps), _p(y))
+    return x2, y

@@ -324,6 +324,33 @@ int madi_orc_linear_f32_baseline(const uint16_t *X, int M, int K, const int8_t *
     return 0;
 }
 
+/* bias_res_ln_f16 (encoder_ops.metal:333-364) / layer_norm_f16 (:305-331).
+ * x[r][i] += float(mo[r][i]) + bias[i] in f32 in the reference's order
+ * ((x + mo) + bias: encoder_ops.metal:347), then the LayerNorm of the updated
+ * row -- mean, two-pass variance, rsqrt(var + eps), * gamma + beta -- in double:
+ * y_exact is the unrounded value the f16 output is checked against.  mo == NULL
+ * restates layer_norm_f16 (x unchanged). */
+void madi_orc_bias_res_ln(float *x, const uint16_t *mo, const float *bias, const float *gamma, const float *beta,
+                          int rows, int d, float eps, double *y_exact) {
+    #pragma omp parallel for schedule(static)
+    for (int r = 0; r < rows; ++r) {
+        float *xr = x + (size_t)r * d;
+        if (mo) {
+            const uint16_t *mr = mo + (size_t)r * d;
+            for (int i = 0; i < d; ++i) xr[i] = (xr[i] + madi_orc_h2f(mr[i])) + bias[i];
+        }
+        double mean = 0.0;
+        for (int i = 0; i < d; ++i) mean += (double)xr[i];
+        mean /= d;
+        double var = 0.0;
+        for (int i = 0; i < d; ++i) { const double t = (double)xr[i] - mean; var += t * t; }
+        var /= d;
+        const double inv = 1.0 / sqrt(var + (double)eps);
+        double *yr = y_exact + (size_t)r * d;
+        for (int i = 0; i < d; ++i) yr[i] = ((double)xr[i] - mean) * inv * (double)gamma[i] + (double)beta[i];
+    }
+}
+
 int madi_orc_max_threads(void) {
 #ifdef _OPENMP
     return omp_get_max_threads();

@@ -134,3 +134,22 @@ def test_cpu_baseline_kernel_matches_exact(oracle):
     y = oracle.linear_f32_baseline(x, qs, sc, b, oracle.EPI_BIAS_GELU, nthreads=2)
     ex = oracle.linear_f16(x, qs, sc, b, oracle.EPI_BIAS_GELU)
     assert np.abs(y.astype(np.float64) - ex).max() <= 2e-3 * np.sqrt(np.mean(ex ** 2)) + np.abs(ex).max() * 2 ** -11
+
+
+def test_oracle_bias_res_ln_restatement(oracle):
+    """The residual + LayerNorm restatement (encoder_ops.metal:305-364): the f32
+    residual update in the reference's order, and the LayerNorm against numpy."""
+    g = np.random.default_rng(3)
+    x = g.standard_normal((9, 384)).astype(np.float32)
+    mo = g.standard_normal((9, 384)).astype(np.float16)
+    b = (0.05 * g.standard_normal(384)).astype(np.float32)
+    gamma = (1 + 0.1 * g.standard_normal(384)).astype(np.float32)
+    beta = (0.1 * g.standard_normal(384)).astype(np.float32)
+    x2, y = oracle.bias_res_ln(x, mo, b, gamma, beta, 1e-5)
+    xe = (x + mo.astype(np.float32)) + b
+    assert np.array_equal(x2, xe)
+    m = xe.astype(np.float64).mean(1, keepdims=True)
+    v = ((xe - m) ** 2).mean(1, keepdims=True)
+    assert np.abs(y - ((xe - m) / np.sqrt(v + 1e-5) * gamma + beta)).max() < 1e-9
+    x3, y3 = oracle.bias_res_ln(x, None, None, gamma, beta, 1e-5)
+    assert np.array_equal(x3, x)
