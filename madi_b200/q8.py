@@ -119,6 +119,21 @@ def quantize_f16(w: torch.Tensor, stream=None) -> Q8Weight:
     return Q8Weight(qs, sc)
 
 
+def quantize_f16_into(w: torch.Tensor, qs: torch.Tensor, scales: torch.Tensor, stream=None) -> None:
+    """quantInto on the device into caller-provided buffers (e.g. a third of a
+    stacked QKV weight, as quantInto's row offset does): w f16 [rows][dim] ->
+    qs int8 [rows][dim], scales f16 [rows][dim/32], all contiguous on w's device."""
+    rows, dim = w.shape
+    if w.dtype != torch.float16 or not w.is_contiguous():
+        raise ValueError("w must be a contiguous f16 tensor")
+    if qs.dtype != torch.int8 or tuple(qs.shape) != (rows, dim) or not qs.is_contiguous():
+        raise ValueError(f"qs must be a contiguous int8 [{rows}][{dim}] tensor")
+    if scales.dtype != torch.float16 or tuple(scales.shape) != (rows, dim // 32) or not scales.is_contiguous():
+        raise ValueError(f"scales must be a contiguous f16 [{rows}][{dim // 32}] tensor")
+    _lib.check(_lib.load().madi_q8_quantize_f16(w.data_ptr(), rows, dim, qs.data_ptr(), scales.data_ptr(),
+                                                _stream(stream)), "madi_q8_quantize_f16")
+
+
 def _ln_check(x, gamma, beta):
     if x.dim() != 2 or x.dtype != torch.float32 or not x.is_contiguous():
         raise ValueError("x must be a contiguous f32 [rows][d] tensor")
