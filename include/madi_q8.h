@@ -95,6 +95,19 @@ int   madi_download(void *dst_host, const void *src_device, size_t size);
  *                      rows = grid_x, as the reference's grid                encoder_ops.metal:333
  *   layer_norm_f16     (X f32, Y f16, gamma f32, beta f32, D u32, eps f32)
  *                      rows = grid_x                                        encoder_ops.metal:305
+ * GPU-resident decode-step primitives (VOCAB = 51866 as in the reference; the
+ * lengths of buffers read through device-held indices are taken from their
+ * allocations, so out-of-range positions / tokens never read out of bounds):
+ *   emb_lookup_indirect_q8 (out f32, qs, scales, tokens u32*, pos_ptr u32*, dim)  graph_helpers.metal:354
+ *   gpu_emb_lookup_q8      (out f32, qs, scales, tok_ptr u32*, dim)           graph_helpers.metal:370
+ *   emb_lookup_indirect    (out f32, emb f16, tokens, pos_ptr, dim)           graph_helpers.metal:12
+ *   pos_embed_add_indirect (out f32, pos_emb f32, pos_ptr, dim)               graph_helpers.metal:48
+ *   step_advance           (pos_ptr)                                          graph_helpers.metal:60
+ *   argmax_no_inc          (logits, tokens, pos_ptr, max_len u32)             graph_helpers.metal:64
+ *   argmax_conf            (logits, tokens, conf f32*, pos_ptr, max_len)      graph_helpers.metal:785
+ *   suppress_list          (logits, ids u32*, n u32)                          graph_helpers.metal:97
+ *   logit_filter_indirect  (logits, past_tokens, num_suppress u32, step_ptr, sample_begin u32,
+ *                           no_repeat_ngram u32)                              graph_helpers.metal:109
  * On success *out_id holds a handle for madi_dispatch. */
 int   madi_get_function(const char *name, int *out_id);
 
@@ -198,6 +211,33 @@ int madi_bias_res_ln_f16(float *x, const uint16_t *mo, const float *bias, uint16
  * x f32 [rows][d] unchanged.  Same shape and alignment rules. */
 int madi_layer_norm_f16(const float *x, uint16_t *y, const float *gamma, const float *beta,
                         int rows, int d, float eps, void *stream);
+
+/* ======================= GPU-resident greedy decode step ==================== */
+
+/* Q8 token-embedding lookup for m slots (emb_lookup_indirect_q8 / gpu_emb_lookup_q8,
+ * graph_helpers.metal:354-383): out[s][i] = float(qs[tok][i]) * float(scales[tok][i/32]),
+ * tok = tokens[s*tok_stride + pos[s]] (pos != NULL) or tokens[s] (pos == NULL).
+ * A position >= tok_len or a token >= emb->n gives a zero row.  out f32 [m][emb->k]. */
+int madi_emb_lookup_q8(const madi_q8w *emb, const uint32_t *tokens, const uint32_t *pos, int m,
+                       int64_t tok_stride, int tok_len, float *out, void *stream);
+
+/* Greedy token per slot (argmax_conf, graph_helpers.metal:785-821): for slot s,
+ * tokens[s*stride + pos[s]] = argmax(logits[s][0..vocab)) and, if conf != NULL,
+ * conf[s*stride + pos[s]] = 1 / sum_i exp(logits[s][i] - max), when pos[s] < max_len.
+ * Ties resolve exactly as the reference's 1024-thread reduction does. */
+int madi_argmax_conf(const float *logits, int m, int vocab, uint32_t *tokens, float *conf,
+                     const uint32_t *pos, int max_len, int64_t stride, void *stream);
+
+/* logit_filter_indirect (graph_helpers.metal:109-160) on one logits row: bans
+ * tokens >= 50258, a token repeated three times, a repeated n-gram completion
+ * (no_repeat_ngram >= 2, last 16 tokens), and space / EOT during the first four
+ * generated steps; *step is read on the device; past holds past_len tokens. */
+int madi_logit_filter(float *logits, int vocab, const uint32_t *past, int past_len,
+                      const uint32_t *step, uint32_t sample_begin, uint32_t no_repeat_ngram,
+                      void *stream);
+
+/* step_advance (graph_helpers.metal:60-62) for m <= 32 slots: pos[s] += 1. */
+int madi_step_advance(uint32_t *pos, int m, void *stream);
 
 #ifdef __cplusplus
 }

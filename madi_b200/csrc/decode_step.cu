@@ -1,0 +1,214 @@
+// decode_step.cu -- the GPU-resident greedy decode-step primitives around the
+// Q8 projections (graph_helpers.metal:12-178, :354-388, :785-821), so a whole
+// token step -- embedding, projections, vocab head, logit filter, argmax -- runs
+// on the device with no host round trip between tokens and can be replayed as a
+// CUDA graph (the position / step counters live in device memory).
+//
+//   emb_lookup_indirect_q8  out[i] = float(qs[tok*dim+i]) * float(scales[tok*nb+i/32]),
+//                           tok = tokens[*pos]                             (:354-367)
+//   gpu_emb_lookup_q8       same, tok = *tok_ptr                           (:370-383)
+//   emb_lookup_indirect     out[i] = float(emb_f16[tok*dim+i])             (:12-23)
+//   pos_embed_add_indirect  out[i] += pos_emb[*pos*dim+i]                  (:48-57)
+//   step_advance            *pos += 1                                      (:60-62)
+//   argmax_no_inc           tokens[*pos] = argmax(logits)                  (:64-95)
+//   argmax_conf             + conf[*pos] = 1 / sum exp(z - zmax)           (:785-821)
+//   suppress_list           logits[ids[j]] = -3.4e38                       (:97-107)
+//   logit_filter_indirect   special / anti-loop / n-gram / begin-window bans (:109-160)
+//
+// The argmax keeps the reference's reduction structure exactly -- 1024 threads,
+// each scanning indices t, t+1024, ... with a strict '>', then a halving tree in
+// shared memory that takes the upper slot only when strictly greater -- so ties
+// resolve as the reference's do (the first index of the winning thread, the
+// winning thread being the one whose 10-bit index is smallest when bit-reversed).
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace madi {
+namespace {
+
+constexpr float kNeg = -3.4e38f;
+
+// Every index that comes from device memory (a position, a token) is checked
+// against the length the host derived for its buffer before it is used.
+__global__ void emb_q8_kernel(float *__restrict__ out, const int8_t *__restrict__ qs, const __half *__restrict__ scales,
+                              const uint32_t *__restrict__ tokens, const uint32_t *__restrict__ pos, int dim,
+                              int rows, int m, long long tok_stride, long long tok_len) {
+    const int s = blockIdx.y;                       // token slot
+    if (s >= m) return;
+    const uint32_t p = pos ? pos[s] : 0u;
+    const uint32_t tok = (long long)p < tok_len ? tokens[(size_t)s * tok_stride + p] : 0xffffffffu;
+    const int nb = dim >> 5;
+    float *o = out + (size_t)s * dim;
+    if (tok >= (uint32_t)rows) {                    // out-of-range position or token: zeros, no stray read
+        for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < dim; i += gridDim.x * blockDim.x) o[i] = 0.f;
+        return;
+    }
+    const int8_t *qr = qs + (size_t)tok * dim;
+    const __half *sr = scales + (size_t)tok * nb;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < dim; i += gridDim.x * blockDim.x)
+        o[i] = (float)qr[i] * __half2float(sr[i >> 5]);
+}
+
+__global__ void emb_f16_kernel(float *__restrict__ out, const __half *__restrict__ emb,
+                               const uint32_t *__restrict__ tokens, const uint32_t *__restrict__ pos, int dim, int rows,
+                               long long tok_len) {
+    const uint32_t p = pos[0];
+    const uint32_t tok = (long long)p < tok_len ? tokens[p] : 0xffffffffu;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < dim; i += gridDim.x * blockDim.x)
+        out[i] = tok < (uint32_t)rows ? __half2float(emb[(size_t)tok * dim + i]) : 0.f;
+}
+
+__global__ void pos_add_kernel(float *__restrict__ out, const float *__restrict__ pos_emb,
+                               const uint32_t *__restrict__ pos, int dim, int max_pos) {
+    const uint32_t p = pos[0];
+    if (p >= (uint32_t)max_pos) return;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < dim; i += gridDim.x * blockDim.x)
+        out[i] += pos_emb[(size_t)p * dim + i];
+}
+
+__global__ void step_advance_kernel(uint32_t *pos, int m) {
+    const int s = threadIdx.x;
+    if (s < m) pos[s] += 1;
+}
+
+// One CTA of 1024 threads per token slot (blockIdx.x): logits row blockIdx.x.
+template <bool kConf>
+__global__ void __launch_bounds__(1024) argmax_kernel(const float *__restrict__ logits, uint32_t *__restrict__ tokens,
+                                                      float *__restrict__ conf, const uint32_t *__restrict__ pos,
+                                                      int V, int max_len, long long stride) {
+    __shared__ float sv[1024];
+    __shared__ uint32_t si[1024];
+    const int t = threadIdx.x, s = blockIdx.x;
+    const float *lg = logits + (size_t)s * V;
+    float lm = -INFINITY;
+    uint32_t li = 0;
+    for (int i = t; i < V; i += 1024) {
+        const float v = lg[i];
+        if (v > lm) { lm = v; li = (uint32_t)i; }
+    }
+    sv[t] = lm;
+    si[t] = li;
+    __syncthreads();
+    for (int st = 512; st > 0; st >>= 1) {
+        if (t < st && sv[t + st] > sv[t]) { sv[t] = sv[t + st]; si[t] = si[t + st]; }
+        __syncthreads();
+    }
+    const float zmax = sv[0];
+    const uint32_t amax = si[0];
+    float inv_sum = 0.f;
+    if constexpr (kConf) {
+        __syncthreads();
+        float ls = 0.f;
+        for (int i = t; i < V; i += 1024) ls += expf(lg[i] - zmax);
+        sv[t] = ls;
+        __syncthreads();
+        for (int st = 512; st > 0; st >>= 1) {
+            if (t < st) sv[t] += sv[t + st];
+            __syncthreads();
+        }
+        inv_sum = 1.0f / sv[0];
+    }
+    if (t == 0) {
+        const uint32_t cur = pos[s];
+        if (cur < (uint32_t)max_len) {
+            tokens[(size_t)s * stride + cur] = amax;
+            if constexpr (kConf) conf[(size_t)s * stride + cur] = inv_sum;
+        }
+    }
+}
+
+__global__ void suppress_kernel(float *__restrict__ logits, const uint32_t *__restrict__ ids, int n, int V) {
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= n) return;
+    const uint32_t t = ids[j];
+    if (t < (uint32_t)V) logits[t] = kNeg;
+}
+
+// logit_filter_indirect (graph_helpers.metal:109-160): one CTA of 256 threads.
+__global__ void __launch_bounds__(256) logit_filter_kernel(float *__restrict__ logits,
+                                                           const uint32_t *__restrict__ past,
+                                                           const uint32_t *__restrict__ step_ptr, uint32_t sample_begin,
+                                                           uint32_t no_repeat_ngram, int V, int past_len) {
+    const uint32_t i = threadIdx.x;
+    const uint32_t step = step_ptr[0];
+    // the history reads below stay inside past[0 .. past_len)
+    const bool hist_ok = step <= (uint32_t)past_len;
+    if (i == 0 && hist_ok && step >= 3 && step >= sample_begin + 3) {
+        const uint32_t t1 = past[step - 1], t2 = past[step - 2], t3 = past[step - 3];
+        if (t1 == t2 && t2 == t3 && t1 < (uint32_t)V) logits[t1] = kNeg;
+    }
+    // (sample_begin <= step keeps the window start below step even if the sums wrap)
+    if (i == 0 && hist_ok && no_repeat_ngram >= 2 && step >= no_repeat_ngram && sample_begin <= step &&
+        step >= sample_begin + no_repeat_ngram) {
+        const uint32_t kWin = 16;
+        const uint32_t n = no_repeat_ngram;
+        const uint32_t suf = step - (n - 1);
+        const uint32_t j0 = (step > sample_begin + kWin) ? (step - kWin) : sample_begin;
+        for (uint32_t j = j0; j + n <= step; ++j) {
+            bool match = true;
+            for (uint32_t k = 0; k + 1 < n; ++k)
+                if (past[j + k] != past[suf + k]) { match = false; break; }
+            if (match) {
+                const uint32_t c = past[j + n - 1];
+                if (c < (uint32_t)V) logits[c] = kNeg;
+            }
+        }
+    }
+    for (uint32_t t = i + 50258; t < (uint32_t)V; t += 256) logits[t] = kNeg;
+    if (step < sample_begin + 4) {
+        if (i == 0 && 220 < V) logits[220] = kNeg;
+        if (i == 1 && 50257 < V) logits[50257] = kNeg;
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_emb_q8(float *out, const int8_t *qs, const __half *scales, const uint32_t *tokens,
+                          const uint32_t *pos, int dim, int rows, int m, long long tok_stride, long long tok_len,
+                          cudaStream_t st) {
+    emb_q8_kernel<<<dim3((dim + 255) / 256, m), 256, 0, st>>>(out, qs, scales, tokens, pos, dim, rows, m, tok_stride,
+                                                             tok_len);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_emb_f16(float *out, const __half *emb, const uint32_t *tokens, const uint32_t *pos, int dim,
+                           int rows, long long tok_len, cudaStream_t st) {
+    emb_f16_kernel<<<(dim + 255) / 256, 256, 0, st>>>(out, emb, tokens, pos, dim, rows, tok_len);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_pos_add(float *out, const float *pos_emb, const uint32_t *pos, int dim, int max_pos,
+                           cudaStream_t st) {
+    pos_add_kernel<<<(dim + 255) / 256, 256, 0, st>>>(out, pos_emb, pos, dim, max_pos);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_step_advance(uint32_t *pos, int m, cudaStream_t st) {
+    step_advance_kernel<<<1, 32, 0, st>>>(pos, m);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_argmax(const float *logits, uint32_t *tokens, float *conf, const uint32_t *pos, int V,
+                          int max_len, int m, long long stride, cudaStream_t st) {
+    if (conf)
+        argmax_kernel<true><<<m, 1024, 0, st>>>(logits, tokens, conf, pos, V, max_len, stride);
+    else
+        argmax_kernel<false><<<m, 1024, 0, st>>>(logits, tokens, nullptr, pos, V, max_len, stride);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_suppress(float *logits, const uint32_t *ids, int n, int V, cudaStream_t st) {
+    if (n > 0) suppress_kernel<<<(n + 255) / 256, 256, 0, st>>>(logits, ids, n, V);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_logit_filter(float *logits, const uint32_t *past, const uint32_t *step_ptr, uint32_t sample_begin,
+                                uint32_t no_repeat_ngram, int V, int past_len, cudaStream_t st) {
+    logit_filter_kernel<<<1, 256, 0, st>>>(logits, past, step_ptr, sample_begin, no_repeat_ngram, V, past_len);
+    return cudaGetLastError();
+}
+
+}  // namespace madi

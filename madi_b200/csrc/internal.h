@@ -61,6 +61,22 @@ constexpr int kLnMaxD = 2048;   // row width limit of the register-resident row 
 cudaError_t launch_res_ln(float *X, const __half *MO, const float *bias, __half *Y, const float *gamma,
                           const float *beta, int rows, int D, float eps, cudaStream_t st);
 
+// ---------------------------------------------------------------- decode-step primitives (decode_step.cu)
+constexpr int kWhisperVocab = 51866;   // VOCAB of graph_helpers.metal:9 (the by-name kernels assume it)
+// tok_len: entries readable per slot row of `tokens`; rows: embedding rows.
+cudaError_t launch_emb_q8(float *out, const int8_t *qs, const __half *scales, const uint32_t *tokens,
+                          const uint32_t *pos, int dim, int rows, int m, long long tok_stride, long long tok_len,
+                          cudaStream_t st);
+cudaError_t launch_emb_f16(float *out, const __half *emb, const uint32_t *tokens, const uint32_t *pos, int dim,
+                           int rows, long long tok_len, cudaStream_t st);
+cudaError_t launch_pos_add(float *out, const float *pos_emb, const uint32_t *pos, int dim, int max_pos, cudaStream_t st);
+cudaError_t launch_step_advance(uint32_t *pos, int m, cudaStream_t st);
+cudaError_t launch_argmax(const float *logits, uint32_t *tokens, float *conf, const uint32_t *pos, int V, int max_len,
+                          int m, long long stride, cudaStream_t st);
+cudaError_t launch_suppress(float *logits, const uint32_t *ids, int n, int V, cudaStream_t st);
+cudaError_t launch_logit_filter(float *logits, const uint32_t *past, const uint32_t *step_ptr, uint32_t sample_begin,
+                                uint32_t no_repeat_ngram, int V, int past_len, cudaStream_t st);
+
 // ---------------------------------------------------------------- misc kernels
 cudaError_t launch_dequant_f16(const int8_t *qs, const __half *scales, int N, int K, __half *out, cudaStream_t st);
 cudaError_t launch_quantize_f16(const __half *w, int rows, int dim, int8_t *qs, __half *scales, cudaStream_t st);

@@ -91,6 +91,29 @@ bool is_device_ptr(const void *p) {
 
 bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
+// Bytes from p to the end of the device allocation that contains it (0 if
+// unknown): the bound for indices the by-name decode-step kernels read from
+// device memory (positions, tokens), whose reference signatures carry no
+// buffer lengths.
+size_t bytes_after(const void *p) {
+    typedef CUresult (*PFN_range)(CUdeviceptr *, size_t *, CUdeviceptr);
+    static PFN_range fn = nullptr;
+    static bool tried = false;
+    if (!tried) {
+        tried = true;
+        void *ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuMemGetAddressRange", &ptr, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_range>(ptr);
+    }
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    if (!fn || !p || fn(&base, &size, reinterpret_cast<CUdeviceptr>(p)) != CUDA_SUCCESS) return 0;
+    return (size_t)(base + size - reinterpret_cast<CUdeviceptr>(p));
+}
+
 cudaStream_t pick_stream(void *s) { return s ? static_cast<cudaStream_t>(s) : S.stream; }
 
 // ---------------------------------------------------------------- Q8 linear core
@@ -248,6 +271,87 @@ int h_m4_q8(const ArgVal *a, uint32_t gx, cudaStream_t st) {
                           "m4_gemm_q8");
 }
 
+// ---- decode-step primitives by name (graph_helpers.metal); VOCAB = 51866 as in the reference
+
+// Rows of a Q8 table [rows][dim] (+ scales [rows][dim/32]) that both allocations hold.
+size_t q8_rows_in(const void *qs, const void *scales, int dim) {
+    return std::min(bytes_after(qs) / (size_t)dim, bytes_after(scales) / ((size_t)(dim / 32) * 2));
+}
+int h_emb_q8_indirect(const ArgVal *a, uint32_t, cudaStream_t st) {      // (out, qs, scales, tokens, pos_ptr, dim)
+    const int dim = (int)a[5].u;
+    if (dim <= 0 || dim % 32) return fail(MADI_EINVAL, "emb_lookup_indirect_q8: dim %d (multiple of 32)", dim);
+    const size_t rows = q8_rows_in(a[1].p, a[2].p, dim), tok_len = bytes_after(a[3].p) / 4;
+    if (!rows || !tok_len || bytes_after(a[0].p) < (size_t)dim * 4)
+        return fail(MADI_EINVAL, "emb_lookup_indirect_q8: buffer extents unknown or too small");
+    cudaError_t e = launch_emb_q8((float *)a[0].p, static_cast<const int8_t *>(a[1].p),
+                                  static_cast<const __half *>(a[2].p), static_cast<const uint32_t *>(a[3].p),
+                                  static_cast<const uint32_t *>(a[4].p), dim, (int)std::min<size_t>(rows, 1u << 30), 1,
+                                  0, (long long)tok_len, st);
+    return e == cudaSuccess ? MADI_OK : cuda_fail(e, "emb_lookup_indirect_q8");
+}
+int h_emb_q8_direct(const ArgVal *a, uint32_t, cudaStream_t st) {        // (out, qs, scales, tok_ptr, dim)
+    const int dim = (int)a[4].u;
+    if (dim <= 0 || dim % 32) return fail(MADI_EINVAL, "gpu_emb_lookup_q8: dim %d (multiple of 32)", dim);
+    const size_t rows = q8_rows_in(a[1].p, a[2].p, dim);
+    if (!rows || bytes_after(a[0].p) < (size_t)dim * 4) return fail(MADI_EINVAL, "gpu_emb_lookup_q8: buffer extents");
+    cudaError_t e = launch_emb_q8((float *)a[0].p, static_cast<const int8_t *>(a[1].p),
+                                  static_cast<const __half *>(a[2].p), static_cast<const uint32_t *>(a[3].p), nullptr,
+                                  dim, (int)std::min<size_t>(rows, 1u << 30), 1, 0, 1, st);
+    return e == cudaSuccess ? MADI_OK : cuda_fail(e, "gpu_emb_lookup_q8");
+}
+int h_emb_f16_indirect(const ArgVal *a, uint32_t, cudaStream_t st) {     // (out, emb, tokens, pos_ptr, dim)
+    const int dim = (int)a[4].u;
+    if (dim <= 0) return fail(MADI_EINVAL, "emb_lookup_indirect: dim %d", dim);
+    const size_t rows = bytes_after(a[1].p) / ((size_t)dim * 2), tok_len = bytes_after(a[2].p) / 4;
+    if (!rows || !tok_len || bytes_after(a[0].p) < (size_t)dim * 4)
+        return fail(MADI_EINVAL, "emb_lookup_indirect: buffer extents unknown or too small");
+    cudaError_t e = launch_emb_f16((float *)a[0].p, static_cast<const __half *>(a[1].p),
+                                   static_cast<const uint32_t *>(a[2].p), static_cast<const uint32_t *>(a[3].p), dim,
+                                   (int)std::min<size_t>(rows, 1u << 30), (long long)tok_len, st);
+    return e == cudaSuccess ? MADI_OK : cuda_fail(e, "emb_lookup_indirect");
+}
+int h_pos_add(const ArgVal *a, uint32_t, cudaStream_t st) {              // (out, pos_emb, pos_ptr, dim)
+    const int dim = (int)a[3].u;
+    if (dim <= 0) return fail(MADI_EINVAL, "pos_embed_add_indirect: dim %d", dim);
+    const size_t max_pos = bytes_after(a[1].p) / ((size_t)dim * 4);
+    if (!max_pos || bytes_after(a[0].p) < (size_t)dim * 4) return fail(MADI_EINVAL, "pos_embed_add_indirect: extents");
+    cudaError_t e = launch_pos_add((float *)a[0].p, static_cast<const float *>(a[1].p),
+                                   static_cast<const uint32_t *>(a[2].p), dim, (int)std::min<size_t>(max_pos, 1u << 30),
+                                   st);
+    return e == cudaSuccess ? MADI_OK : cuda_fail(e, "pos_embed_add_indirect");
+}
+int h_step_advance(const ArgVal *a, uint32_t, cudaStream_t st) {         // (pos_ptr)
+    cudaError_t e = launch_step_advance((uint32_t *)a[0].p, 1, st);
+    return e == cudaSuccess ? MADI_OK : cuda_fail(e, "step_advance");
+}
+template <bool kConf>
+int h_argmax(const ArgVal *a, uint32_t, cudaStream_t st) {   // (logits, tokens, [conf,] pos_ptr, max_len)
+    const int i_pos = kConf ? 3 : 2;
+    const uint32_t max_len = a[i_pos + 1].u;
+    if (bytes_after(a[0].p) < (size_t)kWhisperVocab * 4) return fail(MADI_EINVAL, "argmax: logits shorter than VOCAB");
+    if (bytes_after(a[1].p) < (size_t)max_len * 4 || (kConf && bytes_after(a[2].p) < (size_t)max_len * 4))
+        return fail(MADI_EINVAL, "argmax: tokens / conf shorter than max_len");
+    cudaError_t e = launch_argmax(static_cast<const float *>(a[0].p), (uint32_t *)a[1].p, kConf ? (float *)a[2].p : nullptr,
+                                  static_cast<const uint32_t *>(a[i_pos].p), kWhisperVocab, (int)max_len, 1, 0, st);
+    return e == cudaSuccess ? MADI_OK : cuda_fail(e, "argmax");
+}
+int h_suppress(const ArgVal *a, uint32_t, cudaStream_t st) {             // (logits, ids, n)
+    const uint32_t n = a[2].u;
+    if (bytes_after(a[0].p) < (size_t)kWhisperVocab * 4 || bytes_after(a[1].p) < (size_t)n * 4)
+        return fail(MADI_EINVAL, "suppress_list: buffer extents");
+    cudaError_t e = launch_suppress((float *)a[0].p, static_cast<const uint32_t *>(a[1].p), (int)n, kWhisperVocab, st);
+    return e == cudaSuccess ? MADI_OK : cuda_fail(e, "suppress_list");
+}
+// (logits, past_tokens, num_suppress, step_ptr, sample_begin, no_repeat_ngram)
+int h_logit_filter(const ArgVal *a, uint32_t, cudaStream_t st) {
+    if (bytes_after(a[0].p) < (size_t)kWhisperVocab * 4) return fail(MADI_EINVAL, "logit_filter_indirect: logits");
+    const size_t past_len = bytes_after(a[1].p) / 4;
+    cudaError_t e = launch_logit_filter((float *)a[0].p, static_cast<const uint32_t *>(a[1].p),
+                                        static_cast<const uint32_t *>(a[3].p), a[4].u, a[5].u, kWhisperVocab,
+                                        (int)std::min<size_t>(past_len, 1u << 30), st);
+    return e == cudaSuccess ? MADI_OK : cuda_fail(e, "logit_filter_indirect");
+}
+
 // bias_res_ln_f16(X, MO, bias, Y, gamma, beta, D, eps), rows = grid x   encoder_ops.metal:333-364
 int h_bias_res_ln(const ArgVal *a, uint32_t gx, cudaStream_t st) {
     return madi_bias_res_ln_f16((float *)a[0].p, static_cast<const uint16_t *>(a[1].p), static_cast<const float *>(a[2].p),
@@ -274,6 +378,15 @@ const std::vector<Op> &ops() {
         {"m4_gemm_q8_bias_gelu", {kPtr, kPtr, kPtr, kPtr, kPtr, kU32, kU32, kU32, kU32}, h_m4_q8},
         {"bias_res_ln_f16", {kPtr, kPtr, kPtr, kPtr, kPtr, kPtr, kU32, kF32}, h_bias_res_ln},
         {"layer_norm_f16", {kPtr, kPtr, kPtr, kPtr, kU32, kF32}, h_layer_norm},
+        {"emb_lookup_indirect_q8", {kPtr, kPtr, kPtr, kPtr, kPtr, kU32}, h_emb_q8_indirect},
+        {"gpu_emb_lookup_q8", {kPtr, kPtr, kPtr, kPtr, kU32}, h_emb_q8_direct},
+        {"emb_lookup_indirect", {kPtr, kPtr, kPtr, kPtr, kU32}, h_emb_f16_indirect},
+        {"pos_embed_add_indirect", {kPtr, kPtr, kPtr, kU32}, h_pos_add},
+        {"step_advance", {kPtr}, h_step_advance},
+        {"argmax_no_inc", {kPtr, kPtr, kPtr, kU32}, h_argmax<false>},
+        {"argmax_conf", {kPtr, kPtr, kPtr, kPtr, kU32}, h_argmax<true>},
+        {"suppress_list", {kPtr, kPtr, kU32}, h_suppress},
+        {"logit_filter_indirect", {kPtr, kPtr, kU32, kPtr, kU32, kU32}, h_logit_filter},
     };
     return table;
 }
@@ -591,6 +704,46 @@ int madi_bias_res_ln_f16(float *x, const uint16_t *mo, const float *bias, uint16
                          const float *beta, int rows, int d, float eps, void *stream) {
     if (!mo) return fail(MADI_EINVAL, "madi_bias_res_ln_f16: null MO");
     return res_ln_impl(x, mo, bias, y, gamma, beta, rows, d, eps, stream, "madi_bias_res_ln_f16");
+}
+
+int madi_emb_lookup_q8(const madi_q8w *emb, const uint32_t *tokens, const uint32_t *pos, int m, int64_t tok_stride,
+                       int tok_len, float *out, void *stream) {
+    if (!S.ready) return fail(MADI_ENOINIT, "madi_emb_lookup_q8: not initialised");
+    if (!emb || !emb->qs || !emb->scales || !tokens || !out) return fail(MADI_EINVAL, "madi_emb_lookup_q8: null argument");
+    if (emb->n <= 0 || emb->k <= 0 || emb->k % 32 || m <= 0 || m > 65535 || tok_len <= 0 ||
+        (m > 1 && pos && tok_stride < tok_len))
+        return fail(MADI_EINVAL, "madi_emb_lookup_q8: bad shape (rows=%d dim=%d m=%d tok_len=%d)", emb->n, emb->k, m,
+                    tok_len);
+    cudaError_t e = launch_emb_q8(out, emb->qs, reinterpret_cast<const __half *>(emb->scales), tokens, pos, emb->k,
+                                  emb->n, m, pos ? (long long)tok_stride : 1, pos ? (long long)tok_len : 1,
+                                  pick_stream(stream));
+    return e == cudaSuccess ? MADI_OK : cuda_fail(e, "madi_emb_lookup_q8");
+}
+
+int madi_argmax_conf(const float *logits, int m, int vocab, uint32_t *tokens, float *conf, const uint32_t *pos,
+                     int max_len, int64_t stride, void *stream) {
+    if (!S.ready) return fail(MADI_ENOINIT, "madi_argmax_conf: not initialised");
+    if (!logits || !tokens || !pos) return fail(MADI_EINVAL, "madi_argmax_conf: null argument");
+    if (m <= 0 || vocab <= 0 || max_len <= 0 || (m > 1 && stride < max_len))
+        return fail(MADI_EINVAL, "madi_argmax_conf: bad shape (m=%d vocab=%d max_len=%d)", m, vocab, max_len);
+    cudaError_t e = launch_argmax(logits, tokens, conf, pos, vocab, max_len, m, stride, pick_stream(stream));
+    return e == cudaSuccess ? MADI_OK : cuda_fail(e, "madi_argmax_conf");
+}
+
+int madi_logit_filter(float *logits, int vocab, const uint32_t *past, int past_len, const uint32_t *step,
+                      uint32_t sample_begin, uint32_t no_repeat_ngram, void *stream) {
+    if (!S.ready) return fail(MADI_ENOINIT, "madi_logit_filter: not initialised");
+    if (!logits || !past || !step || vocab <= 0 || past_len < 0) return fail(MADI_EINVAL, "madi_logit_filter: bad argument");
+    cudaError_t e = launch_logit_filter(logits, past, step, sample_begin, no_repeat_ngram, vocab, past_len,
+                                        pick_stream(stream));
+    return e == cudaSuccess ? MADI_OK : cuda_fail(e, "madi_logit_filter");
+}
+
+int madi_step_advance(uint32_t *pos, int m, void *stream) {
+    if (!S.ready) return fail(MADI_ENOINIT, "madi_step_advance: not initialised");
+    if (!pos || m <= 0 || m > 32) return fail(MADI_EINVAL, "madi_step_advance: m=%d (1..32)", m);
+    cudaError_t e = launch_step_advance(pos, m, pick_stream(stream));
+    return e == cudaSuccess ? MADI_OK : cuda_fail(e, "madi_step_advance");
 }
 
 int madi_layer_norm_f16(const float *x, uint16_t *y, const float *gamma, const float *beta, int rows, int d, float eps,

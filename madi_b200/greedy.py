@@ -1,0 +1,71 @@
+"""GPU-resident greedy decode-step primitives around the Q8 projections
+(graph_helpers.metal:12-178, :354-388, :785-821): with the token history, the
+position counters and the logits in device memory, a whole token step runs with
+no host round trip and replays as a CUDA graph.
+
+Thin wrappers of the C ABI (madi_emb_lookup_q8, madi_argmax_conf,
+madi_logit_filter, madi_step_advance) on torch CUDA tensors.
+"""
+import ctypes
+from typing import Optional
+
+import torch
+
+from . import _lib
+from .q8 import Q8Weight, _stream
+
+
+def emb_lookup_q8(emb: Q8Weight, tokens: torch.Tensor, pos: Optional[torch.Tensor] = None,
+                  out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+    """Token embeddings from a Q8 table: tokens u32 [m][len] with positions pos u32 [m]
+    (row s uses tokens[s][pos[s]]), or tokens u32 [m] directly when pos is None.
+    Returns f32 [m][dim]."""
+    if tokens.dtype != torch.int32 and tokens.dtype != torch.uint32:
+        raise TypeError("tokens must be 32-bit")
+    if pos is None:
+        m, tok_stride, tok_len = tokens.numel(), 1, 1
+    else:
+        if tokens.dim() != 2 or not tokens.is_contiguous():
+            raise ValueError("tokens must be a contiguous [m][len] tensor when pos is given")
+        m, tok_len = tokens.shape
+        tok_stride = tok_len
+        if pos.numel() != m:
+            raise ValueError("pos must have one entry per slot")
+    if out is None:
+        out = torch.empty((m, emb.k), dtype=torch.float32, device=tokens.device)
+    h = emb.handle()
+    rc = _lib.load().madi_emb_lookup_q8(ctypes.byref(h), tokens.data_ptr(), None if pos is None else pos.data_ptr(), m,
+                                        tok_stride, tok_len, out.data_ptr(), _stream(stream))
+    _lib.check(rc, "madi_emb_lookup_q8")
+    return out
+
+
+def argmax_conf(logits: torch.Tensor, tokens: torch.Tensor, pos: torch.Tensor, conf: Optional[torch.Tensor] = None,
+                stream=None) -> None:
+    """tokens[s][pos[s]] = argmax(logits[s]) (and conf[s][pos[s]] = its softmax
+    probability) for every slot with pos[s] < tokens.shape[1]."""
+    if logits.dim() != 2 or logits.dtype != torch.float32 or not logits.is_contiguous():
+        raise ValueError("logits must be a contiguous f32 [m][vocab] tensor")
+    m, vocab = logits.shape
+    if tokens.dim() != 2 or tokens.shape[0] != m or not tokens.is_contiguous():
+        raise ValueError("tokens must be a contiguous [m][max_len] tensor")
+    max_len = tokens.shape[1]
+    if conf is not None and (conf.shape != tokens.shape or conf.dtype != torch.float32 or not conf.is_contiguous()):
+        raise ValueError("conf must be f32 shaped like tokens")
+    rc = _lib.load().madi_argmax_conf(logits.data_ptr(), m, vocab, tokens.data_ptr(),
+                                      None if conf is None else conf.data_ptr(), pos.data_ptr(), max_len, max_len,
+                                      _stream(stream))
+    _lib.check(rc, "madi_argmax_conf")
+
+
+def logit_filter(logits: torch.Tensor, past: torch.Tensor, step: torch.Tensor, sample_begin: int,
+                 no_repeat_ngram: int = 0, stream=None) -> None:
+    """logit_filter_indirect on one f32 logits row, in place; step is a device u32 [1]."""
+    rc = _lib.load().madi_logit_filter(logits.data_ptr(), logits.numel(), past.data_ptr(), past.numel(),
+                                       step.data_ptr(), int(sample_begin), int(no_repeat_ngram), _stream(stream))
+    _lib.check(rc, "madi_logit_filter")
+
+
+def step_advance(pos: torch.Tensor, stream=None) -> None:
+    """pos[s] += 1 on the device."""
+    _lib.check(_lib.load().madi_step_advance(pos.data_ptr(), pos.numel(), _stream(stream)), "madi_step_advance")

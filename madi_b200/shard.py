@@ -5,7 +5,11 @@
 * Vocab head: column-split by output rows -- rank g owns rows [g*S, min(V, (g+1)*S))
   with S = ceil(V / world).  Each rank computes logits for its rows for every token
   slot; the shards are all-gathered (NCCL over NVLink on B200, gloo on CPU) and the
-  greedy token is the global argmax with ties broken toward the lowest vocab index.
+  greedy token is the global argmax with ties broken as the reference's single-GPU
+  argmax breaks them (graph_helpers.metal:64-95): its 1024-lane scan + halving tree
+  prefers, among tied indices, the one whose lane (index mod 1024) is smallest when
+  its 10 bits are reversed, then the lowest index in that lane.  That preference is
+  a total order on indices (tie_key), so per-shard winners merge exactly.
 
 Only torch.distributed is used for the exchange; the per-rank logits come from
 madi_b200.q8.linear on the rank's own head shard.
@@ -44,30 +48,49 @@ def allgather_logits(local: torch.Tensor, vocab: int, world: int, group=None) ->
     return full[:, :vocab].contiguous()
 
 
+_REV10 = {}
+
+
+def tie_key(idx: torch.Tensor) -> torch.Tensor:
+    """Order among tied maxima: (bit-reversed lane, index) packed in int64; smaller wins."""
+    rev = _REV10.get(idx.device)
+    if rev is None:
+        rev = torch.tensor([int(format(t, "010b")[::-1], 2) for t in range(1024)], dtype=torch.int64,
+                           device=idx.device)
+        _REV10[idx.device] = rev
+    idx = idx.to(torch.int64)
+    return (rev[idx & 1023] << 32) | idx
+
+
+def _pick(values: torch.Tensor, indices: torch.Tensor, dim: int) -> Tuple[torch.Tensor, torch.Tensor]:
+    best = values.max(dim=dim, keepdim=True).values
+    keys = torch.where(values == best, tie_key(indices), torch.full_like(indices, torch.iinfo(torch.int64).max,
+                                                                         dtype=torch.int64))
+    return best.squeeze(dim), keys.min(dim=dim).values & 0xFFFFFFFF
+
+
 def greedy_tokens(logits: torch.Tensor) -> torch.Tensor:
-    """Greedy token per row, lowest index on ties (torch.argmax returns the first maximum)."""
-    return torch.argmax(logits, dim=-1)
+    """Greedy token per row of full logits [m][vocab], the reference's tie rule."""
+    idx = torch.arange(logits.shape[-1], device=logits.device).expand_as(logits)
+    return _pick(logits, idx, -1)[1]
 
 
 def shard_argmax(local: torch.Tensor, h0: int) -> Tuple[torch.Tensor, torch.Tensor]:
     """Per-row (max value, global index) of a shard -- the cheap alternative to gathering
-    whole logit rows: gather these pairs and merge with merge_shard_argmax.  argmax
-    returns the first maximal index, so ties inside a shard go to the lowest index."""
-    i = torch.argmax(local, dim=-1, keepdim=True)
-    return torch.gather(local, -1, i).squeeze(-1), i.squeeze(-1) + h0
+    whole logit rows: gather these pairs and merge with merge_shard_argmax."""
+    idx = torch.arange(h0, h0 + local.shape[-1], device=local.device).expand_as(local)
+    return _pick(local, idx, -1)
 
 
 def merge_shard_argmax(values: torch.Tensor, indices: torch.Tensor) -> torch.Tensor:
-    """values/indices [world][m] -> global greedy index per row; ties -> lowest index."""
-    best = values.max(dim=0, keepdim=True).values
-    cand = torch.where(values == best, indices, torch.full_like(indices, torch.iinfo(indices.dtype).max))
-    return cand.min(dim=0).values
+    """values/indices [world][m] -> global greedy index per row (the reference's tie rule)."""
+    return _pick(values, indices, 0)[1]
 
 
 def allgather_greedy(local: torch.Tensor, vocab: int, world: int, rank: int, group=None) -> torch.Tensor:
     """Greedy tokens of the column-split head without gathering whole logit rows:
     each rank contributes its shard's per-row (max, argmax) and the pairs are merged
-    with the lowest-index tie rule -- the same tokens as greedy_tokens(allgather_logits(...))."""
+    with the same tie order -- the same tokens as greedy_tokens(allgather_logits(...))."""
     import torch.distributed as dist
     h0, _ = vocab_shard(vocab, world, rank)
     v, i = shard_argmax(local, h0)

@@ -43,6 +43,10 @@ def lib():
         L.madi_orc_gemv_q8.argtypes = [P, I, P, P, I, I, P, I, P, P, P]
         L.madi_orc_gemv_q8_qkv.argtypes = [P, I, P, P, I, P, P, P, P, P, P]
         L.madi_orc_argmax.argtypes, L.madi_orc_argmax.restype = [P, I], I
+        L.madi_orc_argmax_conf.argtypes, L.madi_orc_argmax_conf.restype = [P, I, P], I
+        L.madi_orc_emb_q8.argtypes = [P, P, I, ctypes.c_uint32, P]
+        L.madi_orc_suppress.argtypes = [P, I, P, I]
+        L.madi_orc_logit_filter.argtypes = [P, I, P, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32]
         L.madi_orc_linear_f32_baseline.argtypes = [P, I, I, P, P, I, P, I, P, P, I]
         L.madi_orc_bias_res_ln.argtypes = [P, P, P, P, P, I, I, F, P]
         L.madi_orc_linear_f32_baseline.restype = I
@@ -132,8 +136,44 @@ def gemv_q8_qkv(x, qs, scales, qb, vb, pos, cache_rows):
 
 
 def argmax(logits) -> int:
+    """Greedy token with the reference's 1024-lane tree tie rule (argmax_no_inc)."""
     l = _c(logits, np.float32)
     return lib().madi_orc_argmax(_p(l), l.size)
+
+
+def argmax_conf(logits):
+    """(token, confidence) as argmax_conf computes them (graph_helpers.metal:785-821)."""
+    l = _c(logits, np.float32)
+    c = ctypes.c_float()
+    tok = lib().madi_orc_argmax_conf(_p(l), l.size, ctypes.byref(c))
+    return tok, c.value
+
+
+def emb_q8(qs, scales, tok: int):
+    """One dequantised Q8 embedding row as f32 (emb_lookup_indirect_q8)."""
+    qs = _c(qs, np.int8)
+    sc = _c(scales, np.float16)
+    out = np.empty(qs.shape[1], np.float32)
+    lib().madi_orc_emb_q8(_p(qs), _p(sc.view(np.uint16)), qs.shape[1], int(tok), _p(out))
+    return out
+
+
+def suppress(logits, ids):
+    """suppress_list on a copy of one logits row."""
+    l = _c(logits, np.float32).copy()
+    i = _c(ids, np.uint32)
+    lib().madi_orc_suppress(_p(l), l.size, _p(i), i.size)
+    return l
+
+
+def logit_filter(logits, past, step: int, sample_begin: int, no_repeat_ngram: int = 0):
+    """logit_filter_indirect on a copy of one logits row (graph_helpers.metal:109-160)."""
+    l = _c(logits, np.float32).copy()
+    p = _c(past, np.uint32)
+    if step > p.size:
+        raise ValueError("step beyond the token history")
+    lib().madi_orc_logit_filter(_p(l), l.size, _p(p), int(step), int(sample_begin), int(no_repeat_ngram))
+    return l
 
 
 def linear_f32_baseline(X, qs, scales, bias=None, epi=EPI_NONE, residual=None, nthreads=None):

@@ -276,13 +276,92 @@ void madi_orc_gemv_q8_qkv(const float *x, int M, const int8_t *qs, const uint16_
         }
 }
 
-/* graph_helpers.metal:785-821 argmax_conf (token part): greedy argmax over
- * logits[0..V).  Ties resolve to the LOWEST index (the Metal tree keeps the
- * lower thread on ties; this restatement states the tie rule explicitly). */
+/* graph_helpers.metal:64-95 (argmax_no_inc) and :785-821 (argmax_conf), restated
+ * with the reference's own reduction structure: 1024 lanes, lane t scanning
+ * t, t+1024, ... with a strict '>', then a halving tree (s = 512 .. 1) in which
+ * slot t takes slot t+s only when strictly greater.  On ties this picks the
+ * first index of the winning lane, the winning lane being the tied lane whose
+ * 10-bit id is smallest when bit-reversed (NOT simply the lowest index).  When
+ * conf != NULL, *conf = 1 / sum_i exp(z_i - zmax) with the same lane sums and
+ * the same tree (f32, libm expf).  Returns the token. */
+int madi_orc_argmax_conf(const float *logits, int V, float *conf);
+
 int madi_orc_argmax(const float *logits, int V) {
-    int best = 0;
-    for (int i = 1; i < V; ++i) if (logits[i] > logits[best]) best = i;
-    return best;
+    return madi_orc_argmax_conf(logits, V, NULL);
+}
+
+int madi_orc_argmax_conf(const float *logits, int V, float *conf) {
+    float sv[1024];
+    uint32_t si[1024];
+    for (int t = 0; t < 1024; ++t) {
+        float lm = -INFINITY;
+        uint32_t li = 0;
+        for (int i = t; i < V; i += 1024)
+            if (logits[i] > lm) { lm = logits[i]; li = (uint32_t)i; }
+        sv[t] = lm;
+        si[t] = li;
+    }
+    for (int st = 512; st > 0; st >>= 1)
+        for (int t = 0; t < st; ++t)
+            if (sv[t + st] > sv[t]) { sv[t] = sv[t + st]; si[t] = si[t + st]; }
+    const float zmax = sv[0];
+    const uint32_t amax = si[0];
+    if (conf) {
+        for (int t = 0; t < 1024; ++t) {
+            float ls = 0.f;
+            for (int i = t; i < V; i += 1024) ls += expf(logits[i] - zmax);
+            sv[t] = ls;
+        }
+        for (int st = 512; st > 0; st >>= 1)
+            for (int t = 0; t < st; ++t) sv[t] += sv[t + st];
+        *conf = 1.0f / sv[0];
+    }
+    return (int)amax;
+}
+
+/* graph_helpers.metal:354-383 (emb_lookup_indirect_q8 / gpu_emb_lookup_q8):
+ * out[i] = float(qs[tok][i]) * float(scales[tok][i/32]) -- an exact f32 product
+ * (8-bit integer times 11-bit significand).  out [dim]. */
+void madi_orc_emb_q8(const int8_t *qs, const uint16_t *scales, int dim, uint32_t tok, float *out) {
+    const int nb = dim / 32;
+    for (int i = 0; i < dim; ++i)
+        out[i] = (float)qs[(size_t)tok * dim + i] * madi_orc_h2f(scales[(size_t)tok * nb + i / 32]);
+}
+
+/* graph_helpers.metal:97-107 suppress_list: logits[ids[j]] = -3.4e38 for ids < V. */
+void madi_orc_suppress(float *logits, int V, const uint32_t *ids, int n) {
+    for (int j = 0; j < n; ++j)
+        if (ids[j] < (uint32_t)V) logits[ids[j]] = -3.4e38f;
+}
+
+/* graph_helpers.metal:109-160 logit_filter_indirect, as one sequential pass:
+ * anti-loop (three equal trailing tokens ban that token, step >= sample_begin+3),
+ * windowed no-repeat-n-gram (n >= 2, last 16 tokens, a trailing (n-1)-gram seen
+ * before bans the token that completed it), tokens >= 50258 banned, and space
+ * (220) / EOT (50257) banned while step < sample_begin + 4.  The three bans
+ * write the same constant, so their order does not change the result. */
+void madi_orc_logit_filter(float *logits, int V, const uint32_t *past, uint32_t step, uint32_t sample_begin,
+                           uint32_t nrng) {
+    const float NEG = -3.4e38f;
+    if (step >= sample_begin + 3) {
+        const uint32_t t1 = past[step - 1], t2 = past[step - 2], t3 = past[step - 3];
+        if (t1 == t2 && t2 == t3 && t1 < (uint32_t)V) logits[t1] = NEG;
+    }
+    if (nrng >= 2 && step >= sample_begin + nrng) {
+        const uint32_t win = 16, suf = step - (nrng - 1);
+        const uint32_t j0 = step > sample_begin + win ? step - win : sample_begin;
+        for (uint32_t j = j0; j + nrng <= step; ++j) {
+            int match = 1;
+            for (uint32_t k = 0; k + 1 < nrng; ++k)
+                if (past[j + k] != past[suf + k]) { match = 0; break; }
+            if (match && past[j + nrng - 1] < (uint32_t)V) logits[past[j + nrng - 1]] = NEG;
+        }
+    }
+    for (int t = 50258; t < V; ++t) logits[t] = NEG;
+    if (step < sample_begin + 4) {
+        if (220 < V) logits[220] = NEG;
+        if (50257 < V) logits[50257] = NEG;
+    }
 }
 
 /* ------------------------------------------------------ CPU baseline kernel

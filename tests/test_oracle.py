@@ -119,9 +119,85 @@ def test_qkv_split(oracle):
     assert np.isnan(kc[0]).all()
 
 
-def test_argmax_lowest_index_on_ties(oracle):
-    l = np.array([0.0, 3.0, 1.0, 3.0, -1.0], np.float32)
-    assert oracle.argmax(l) == 1
+def _bitrev10(t):
+    return int(format(t, "010b")[::-1], 2)
+
+
+def _tree_argmax_py(l):
+    """argmax_no_inc (graph_helpers.metal:64-95) as plain Python loops."""
+    sv, si = [], []
+    for t in range(1024):
+        m, k = -np.inf, 0
+        for i in range(t, len(l), 1024):
+            if l[i] > m:
+                m, k = l[i], i
+        sv.append(m)
+        si.append(k)
+    s = 512
+    while s:
+        for t in range(s):
+            if sv[t + s] > sv[t]:
+                sv[t], si[t] = sv[t + s], si[t + s]
+        s >>= 1
+    return si[0]
+
+
+def test_argmax_tree_tie_rule(oracle):
+    """Ties resolve as the reference's 1024-lane tree does: the first index of
+    the tied lane whose 10-bit id is smallest bit-reversed -- not the lowest index."""
+    assert oracle.argmax(np.array([0.0, 3.0, 1.0, 3.0, -1.0], np.float32)) == 1
+    assert oracle.argmax(np.array([0.0, 5.0, 5.0], np.float32)) == 2          # lane 2 (rev 256) beats lane 1 (rev 512)
+    l = np.zeros(51866, np.float32)
+    l[[5, 1029]] = 7.0                                                          # same lane: first index
+    assert oracle.argmax(l) == 5
+    rng = np.random.default_rng(11)
+    for trial in range(6):
+        l = rng.integers(-3, 4, 51866).astype(np.float32)                       # many ties at the max
+        ties = np.flatnonzero(l == l.max())
+        want = min(ties, key=lambda i: (_bitrev10(i % 1024), i))
+        assert oracle.argmax(l) == want == _tree_argmax_py(l.tolist())
+    assert oracle.argmax(np.full(51866, -np.inf, np.float32)) == 0
+
+
+def test_argmax_conf_restatement(oracle):
+    rng = np.random.default_rng(3)
+    l = (rng.standard_normal(51866) * 4).astype(np.float32)
+    tok, conf = oracle.argmax_conf(l)
+    assert tok == int(np.argmax(l))
+    p = 1.0 / np.exp(l.astype(np.float64) - l.max()).sum()
+    assert abs(conf - p) <= 1e-5 * p
+
+
+def test_emb_q8_restatement(oracle):
+    rng = np.random.default_rng(4)
+    qs = rng.integers(-127, 128, (10, 96), dtype=np.int8)
+    sc = rng.uniform(1e-4, 2e-2, (10, 3)).astype(np.float16)
+    out = oracle.emb_q8(qs, sc, 7)
+    want = qs[7].astype(np.float64) * np.repeat(sc[7].astype(np.float64), 32)
+    assert np.array_equal(out.astype(np.float64), want)      # exact: int8 x f16 fits f32
+
+
+def test_logit_filter_restatement(oracle):
+    NEG = np.float32(-3.4e38)
+    V = 51866
+    base = np.zeros(V, np.float32)
+
+    def banned(out):
+        return set(np.flatnonzero(out == NEG).tolist()) - set(range(50258, V))
+
+    past = np.array([50258, 10, 20, 30, 40, 50, 60], np.uint32)
+    out = oracle.logit_filter(base, past, 7, 1, 0)
+    assert (out[50258:] == NEG).all() and banned(out) == set()
+    assert banned(oracle.logit_filter(base, past, 4, 1, 0)) == {220, 50257}       # step < sample_begin + 4
+    loop = np.array([50258, 7, 9, 9, 9], np.uint32)
+    assert banned(oracle.logit_filter(base, loop, 5, 1, 0)) == {9}                 # anti-loop
+    assert banned(oracle.logit_filter(base, loop, 5, 3, 0)) == {220, 50257}       # history before sample_begin
+    ng = np.array([50258, 1, 2, 3, 1, 2, 3, 1], np.uint32)
+    assert banned(oracle.logit_filter(base, ng, 8, 1, 2)) == {2}                   # bigram "1 2" seen -> ban 2
+    assert banned(oracle.logit_filter(base, ng, 8, 1, 3)) == {2}                   # "3 1" was followed by 2
+    ng3 = np.array([50258, 5, 6, 7, 5, 6], np.uint32)
+    assert banned(oracle.logit_filter(base, ng3, 6, 1, 3)) == {7}                  # "5 6 7" then "5 6" -> ban 7
+    assert banned(oracle.suppress(base, np.array([3, 99999, 11], np.uint32))) == {3, 11}   # out-of-range id skipped
 
 
 def test_cpu_baseline_kernel_matches_exact(oracle):

@@ -49,9 +49,12 @@ def _worker(rank, world, port, mode, q):
         head = g.standard_normal((V, D)).astype(np.float32)
         x = g.standard_normal((M, D)).astype(np.float32)
         full = x @ head.T
-        # planted ties: row 0 maximum appears at 5 (rank 0) and 900 (last rank) -> 5 wins
+        # planted ties.  Row 0: maximum at 5 (lane 5, reversed 640, rank 0) and 900 (lane
+        # 900, reversed 135, last rank) -> 900 wins, as the reference's 1024-lane tree picks.
+        # Row 1: 2 and 1 inside rank 0's shard -> 2 (reversed 256 < 512).
         full[0, :] = -1.0
         full[0, 5] = full[0, 900] = 7.0
+        full[1, 1] = full[1, 2] = full[1].max() + 1.0
         h0, h1 = shard.vocab_shard(V, world, rank)
         local = torch.from_numpy(full[:, h0:h1].copy())
         if mode == "fail" and rank == 1:
@@ -66,8 +69,7 @@ def _worker(rank, world, port, mode, q):
         dist.all_gather(is_, i)
         merged = shard.merge_shard_argmax(torch.stack(vs), torch.stack(is_))
         pairs = shard.allgather_greedy(local, V, world, rank)      # (max, argmax) pairs only
-        q.put((rank, ok_gather, tok.tolist(), merged.tolist(), int(np.argmax(full[1])), int(np.argmax(full[2])),
-               pairs.tolist()))
+        q.put((rank, ok_gather, tok.tolist(), merged.tolist(), 2, int(np.argmax(full[2])), pairs.tolist()))
     except Exception as e:  # reported to the parent, never hangs
         q.put((rank, "error", repr(e)))
     finally:
@@ -94,7 +96,7 @@ def test_vocab_allgather_and_greedy_merge_two_ranks():
     res = _run("ok")
     for r in res:
         assert r[1] is True, r
-        assert r[2][0] == 5 and r[3][0] == 5           # tie across shards -> lowest index
+        assert r[2][0] == 900 and r[3][0] == 900       # tie across shards -> the reference's lane order
         assert r[2][1] == r[4] and r[2][2] == r[5]
         assert r[3] == r[2]
         assert r[6] == r[2]                             # pair gather = full-row gather
