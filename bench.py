@@ -286,9 +286,11 @@ def main_madi(args, world, rank, local):
     avg_launch_ms = sum(launches) / len(launches)
     achieved = gemm_flops / (avg_launch_ms / 1e3) / 1e12
     peak = peaks["bf16_sus"] if total_ms > 1000 else peaks["bf16"]
-    roofline = {"bound": "tensor", "kernel": "q8_gemm_tc_kernel", "achieved": achieved, "peak": peak,
+    # the library runs the CTA-pair kernel unless MADI_GEMM_PAIR=0 selects the one-CTA kernel
+    kname = "q8_gemm_tc" if os.environ.get("MADI_GEMM_PAIR", "1")[:1] == "0" else "q8_gemm_pair"
+    roofline = {"bound": "tensor", "kernel": kname + "_kernel", "achieved": achieved, "peak": peak,
                 "peak_kind": ("sustained" if total_ms > 1000 else "burst") + " bf16, " + peaks["src"],
-                "unit": "TFLOP/s", "frac": achieved / peak, "traffic": load_traffic("q8_gemm_tc_ffn_b16"),
+                "unit": "TFLOP/s", "frac": achieved / peak, "traffic": load_traffic(kname + "_ffn_b16"),
                 "flops_per_launch": gemm_flops,
                 "fc1_ms": statistics.mean(launches[0::2]), "fc2_ms": statistics.mean(launches[1::2])}
     chunks_per_s = args.batch * world / (ms_step / 1e3)

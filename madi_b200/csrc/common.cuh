@@ -292,6 +292,140 @@ MADI_DEV void umma_stage8_ts_2c(uint32_t d_tmem, uint32_t a_tmem, uint32_t desc_
         : "memory");
 }
 
+// ------------------------------------------------------------------ CTA pairs (cta_group::2)
+//
+// A cluster of two CTAs on neighbouring SMs shares each MMA: the even CTA's
+// thread issues tcgen05.mma.cta_group::2 with M = 256; rows 0-127 of A and D
+// live in the even CTA's tensor memory, rows 128-255 in the odd CTA's, and B's
+// N columns are the two CTAs' shared-memory tiles side by side (first half in
+// the even CTA).  Every tcgen05 instruction that names a CTA group uses ::2.
+
+MADI_DEV uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// All threads of both CTAs; orders shared-memory state across the pair.
+MADI_DEV void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+// Address of the same shared-memory object in CTA `rank` of the cluster.
+MADI_DEV uint32_t mapa_u32(const void *p, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+    return r;
+}
+// Arrive on the barrier at cluster address `cbar` (possibly in the peer CTA),
+// with the instruction's default semantics (release at CTA scope).  The data
+// these arrivals publish lives in tensor memory and is ordered by the
+// tcgen05.fence::before_thread_sync / after_thread_sync pair around them; a
+// cluster-scope release would add a cluster-wide fence to every arrival.
+MADI_DEV void mbar_arrive_cluster(uint32_t cbar) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cbar) : "memory");
+}
+MADI_DEV void st_cluster_u32(uint32_t caddr, uint32_t v) {
+    asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(caddr), "r"(v) : "memory");
+}
+// mbar_wait for CTA pairs: on budget expiry it raises this CTA's abort flag and
+// the peer's (cluster address `peer_abort`), so both stop promptly.  Waits are
+// at CTA scope, as the arrivals they pair with (see mbar_arrive_cluster).
+MADI_DEV bool mbar_wait_cl(uint64_t *bar, uint32_t parity, volatile int *abort_flag, uint32_t peer_abort,
+                           int *dev_err) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (true) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (*abort_flag) return false;
+        if (clock64() - t0 > kWaitBudgetCycles) {
+            *abort_flag = 1;
+            st_cluster_u32(peer_abort, 1u);
+            if (dev_err) atomicCAS(dev_err, kDevErrNone, kDevErrWaitTimeout);
+            return false;
+        }
+    }
+}
+MADI_DEV bool warp_wait_all_cl(uint64_t *bar, uint32_t parity, volatile int *abort_flag, uint32_t peer_abort,
+                               int *dev_err) {
+    const bool ok = mbar_wait_cl(bar, parity, abort_flag, peer_abort, dev_err);
+    return __all_sync(0xffffffffu, ok);
+}
+
+// Warp-collective, executed by the same warp in both CTAs of the pair.
+MADI_DEV void tmem_alloc2(uint32_t *dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+                 "r"(ncols)
+                 : "memory");
+}
+MADI_DEV void tmem_relinquish2() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+MADI_DEV void tmem_dealloc2(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// Arrive on `bar` in both CTAs of the pair once the pair's tcgen05 ops issued so
+// far by this thread complete.
+MADI_DEV void umma2_commit_both(uint64_t *bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+            smem_u32(bar)),
+        "h"((uint16_t)3)
+        : "memory");
+}
+
+// Pair form of umma_stage4_ts: four K=16 MMAs of M = 256, then two commits, each
+// arriving on its barrier in both CTAs.
+MADI_DEV void umma2_stage4_ts(uint32_t d_tmem, uint32_t a_tmem, uint32_t desc_lo, uint32_t desc_hi, uint32_t idesc,
+                              uint32_t accumulate, uint32_t bar0, uint32_t bar1) {
+    asm volatile(
+        "{\n\t.reg .pred p, t;\n\t.reg .b32 a1, a2, a3, l1, l2, l3;\n\t.reg .b64 d0, d1, d2, d3;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\tsetp.eq.b32 t, %4, %4;\n\t"
+        "add.u32 a1, %1, 8;\n\tadd.u32 a2, %1, 16;\n\tadd.u32 a3, %1, 24;\n\t"
+        "add.u32 l1, %2, 2;\n\tadd.u32 l2, %2, 4;\n\tadd.u32 l3, %2, 6;\n\t"
+        "mov.b64 d0, {%2, %3};\n\tmov.b64 d1, {l1, %3};\n\tmov.b64 d2, {l2, %3};\n\tmov.b64 d3, {l3, %3};\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], d0, %5, p;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [a1], d1, %5, t;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [a2], d2, %5, t;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [a3], d3, %5, t;\n\t"
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%6], %8;\n\t"
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%7], %8;\n\t}" ::"r"(
+            d_tmem),
+        "r"(a_tmem), "r"(desc_lo), "r"(desc_hi), "r"(accumulate), "r"(idesc), "r"(bar0), "r"(bar1),
+        "h"((uint16_t)3)
+        : "memory");
+}
+
+// Pair form of umma_stage8_ts_2c: two consecutive K stages (eight MMAs of M = 256),
+// then two commits arriving in both CTAs.
+MADI_DEV void umma2_stage8_ts_2c(uint32_t d_tmem, uint32_t a_tmem, uint32_t desc_lo, uint32_t desc_hi,
+                                 uint32_t desc_step, uint32_t idesc, uint32_t accumulate, uint32_t bar0,
+                                 uint32_t bar1) {
+    asm volatile(
+        "{\n\t.reg .pred p, t;\n\t.reg .b32 a1, a2, a3, a4, a5, a6, a7, l1, l2, l3, l4, l5, l6, l7;\n\t"
+        ".reg .b64 d0, d1, d2, d3, d4, d5, d6, d7;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\tsetp.eq.b32 t, %4, %4;\n\t"
+        "add.u32 a1, %1, 8;\n\tadd.u32 a2, %1, 16;\n\tadd.u32 a3, %1, 24;\n\t"
+        "add.u32 a4, %1, 32;\n\tadd.u32 a5, %1, 40;\n\tadd.u32 a6, %1, 48;\n\tadd.u32 a7, %1, 56;\n\t"
+        "add.u32 l1, %2, 2;\n\tadd.u32 l2, %2, 4;\n\tadd.u32 l3, %2, 6;\n\t"
+        "add.u32 l4, %2, %6;\n\tadd.u32 l5, l4, 2;\n\tadd.u32 l6, l4, 4;\n\tadd.u32 l7, l4, 6;\n\t"
+        "mov.b64 d0, {%2, %3};\n\tmov.b64 d1, {l1, %3};\n\tmov.b64 d2, {l2, %3};\n\tmov.b64 d3, {l3, %3};\n\t"
+        "mov.b64 d4, {l4, %3};\n\tmov.b64 d5, {l5, %3};\n\tmov.b64 d6, {l6, %3};\n\tmov.b64 d7, {l7, %3};\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], d0, %5, p;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [a1], d1, %5, t;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [a2], d2, %5, t;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [a3], d3, %5, t;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [a4], d4, %5, t;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [a5], d5, %5, t;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [a6], d6, %5, t;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], [a7], d7, %5, t;\n\t"
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%7], %9;\n\t"
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%8], %9;\n\t}" ::"r"(
+            d_tmem),
+        "r"(a_tmem), "r"(desc_lo), "r"(desc_hi), "r"(accumulate), "r"(idesc), "r"(desc_step), "r"(bar0), "r"(bar1),
+        "h"((uint16_t)3)
+        : "memory");
+}
+
 // Arrive on `bar` once every tcgen05 op issued so far by this thread completes.
 MADI_DEV void umma_commit(uint64_t *bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))

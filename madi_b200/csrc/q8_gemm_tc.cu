@@ -33,6 +33,7 @@
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include "common.cuh"
@@ -43,7 +44,8 @@ namespace {
 
 constexpr int BN = 128;        // weight rows per tile = MMA M
 constexpr int BK = 64;         // K per pipeline stage
-constexpr int A_STAGES = 4;    // TMEM ring of dequantised A stages
+constexpr int A_STAGES = 4;    // TMEM ring of dequantised A stages (one-CTA kernel)
+constexpr int MAX_A_STAGES = 8;
 constexpr int MAX_STAGES = 8;  // shared-memory ring depth upper bound
 constexpr int RING_BYTES = 192 * 1024;      // shared-memory ring budget (X + W stages)
 constexpr int Y_ROWS = 32;                 // tokens per epilogue chunk
@@ -60,6 +62,7 @@ constexpr int kThreads = 32 * (kEpiWarp0 + kEpiWarps);
 static_assert(BK == 64, "umma_stage4_ts issues four K=16 MMAs per stage");
 
 constexpr size_t kBarsBytes = 512;          // shared memory reserved for struct Bars (checked below)
+
 
 template <int BT> struct Cfg {
     static constexpr int X_STAGE = BT * BK * 2;   // f16 bytes
@@ -80,14 +83,14 @@ template <int BT> struct Cfg {
 struct __align__(8) Bars {
     uint64_t full[MAX_STAGES];   // TMA bytes landed (X + W)
     uint64_t empty[MAX_STAGES];  // MMAs of the stage done (tcgen05.commit): X and W both consumed
-    uint64_t aready[A_STAGES];   // dequantised A written to TMEM (128 arrivals: one dequant group)
-    uint64_t aempty[A_STAGES];   // MMAs reading the TMEM A stage done (tcgen05.commit)
+    uint64_t aready[MAX_A_STAGES];   // dequantised A written to TMEM (one dequant group)
+    uint64_t aempty[MAX_A_STAGES];   // MMAs reading the TMEM A stage done (tcgen05.commit)
     // Pair mode (even KT): the MMA thread takes two stages at a time, so readiness
     // and release are tracked per pair of stages -- half the barrier traffic on
     // the single MMA-issuing thread.
     uint64_t empty2[MAX_STAGES / 2];  // both smem stages of a pair consumed (tcgen05.commit)
-    uint64_t aready2[A_STAGES / 2];   // both A stages of a pair written (256 arrivals: both dequant groups)
-    uint64_t aempty2[A_STAGES / 2];   // both A stages of a pair reusable (tcgen05.commit)
+    uint64_t aready2[MAX_A_STAGES / 2];   // both A stages of a pair written (both dequant groups)
+    uint64_t aempty2[MAX_A_STAGES / 2];   // both A stages of a pair reusable (tcgen05.commit)
     uint64_t accfull[2];       // accumulator ready (tcgen05.commit)
     uint64_t accempty[2];      // epilogue drained the accumulator (one arrival per epilogue thread)
     uint64_t drain;            // final MMA drain
@@ -357,8 +360,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         // done or aborted
         auto visit = [&](int tile, uint2 swv) -> bool {
             if (tile >= num_tiles) return false;
-            if (!warp_wait_all(pairs ? &bars->aempty2[as >> 1] : &bars->aempty[as], pha ^ 1u, abort_flag, err))
-                return false;
+            // convert as soon as the int8 stage has landed, then wait for the TMEM
+            // slot: the conversion stays off the MMA -> dequant -> MMA round trip
             if (!warp_wait_all(&bars->full[s], ph, abort_flag, err)) return false;
             const uint32_t sw = pair_ok ? swv.x : (swv.x | (swv.y << 16));
             const __half2 sw2 = *reinterpret_cast<const __half2 *>(&sw);
@@ -378,6 +381,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     a[c * 8 + 2 * i + 1] = h2_as_u32(__hmul2(hi, sc));
                 }
             }
+            if (!warp_wait_all(pairs ? &bars->aempty2[as >> 1] : &bars->aempty[as], pha ^ 1u, abort_flag, err))
+                return false;
+            tc_fence_after();
             tmem_st32(tmem + lane_addr + C::A_COL0 + as * A_STAGE_COLS, a);
             tmem_wait_st();
             tc_fence_before();
@@ -492,6 +498,386 @@ cudaError_t launch_bt(const GemmArgs &a, const CUtensorMap &tmX, const CUtensorM
     return cudaGetLastError();
 }
 
+// ================================================================ CTA-pair kernel
+//
+// The same pipeline on a cluster of two CTAs sharing every MMA (cta_group::2,
+// M = 256): a pair tile is 256 weight rows x 192 tokens.  Each CTA dequantises
+// its own 128 weight rows into its own tensor memory (A rows 0-127 in the even
+// CTA, 128-255 in the odd one) and stages its own 96-token half of the X tile
+// (B columns 0-95 in the even CTA, 96-191 in the odd one); the even CTA's MMA
+// thread issues the pair's MMAs, and each CTA's accumulator holds its 128
+// weight rows x all 192 tokens, which its own epilogue warps write out.
+// Compared with one CTA per tile this halves, per SM, the MMA instructions,
+// barrier waits and commits the single issuing thread handles, and the X bytes
+// each SM stages from L2.
+//
+// Synchronisation across the pair:
+//   * full[s]   (each CTA): its own TMA bytes (X half + int8 W) landed;
+//   * aready*   (even CTA): both CTAs' dequant warps wrote the A stage(s) --
+//               one arrival per warp, after tcgen05.wait::st and
+//               tcgen05.fence::before_thread_sync (a cluster-scope release on
+//               these arrivals was measured to cost 40 % of the kernel time);
+//   * empty*, aempty*, accfull, drain (each CTA): tcgen05.commit multicast to
+//               both CTAs by the even CTA's MMA thread;
+//   * accempty  (even CTA): both CTAs' epilogue warps drained the accumulator.
+// Both CTAs pass a cluster barrier after initialising their barriers and
+// before the first remote arrival, and again before tensor memory is freed and
+// the CTAs exit, so no arrival or MMA ever targets a CTA that has left.  A
+// bounded wait that expires raises the abort flag of both CTAs.
+constexpr int PBN = 2 * BN;       // weight rows per pair tile (MMA M)
+
+// PBT tokens per pair tile (MMA N; each CTA stages PBT / 2 of them).  The A
+// ring takes the tensor-memory columns the two accumulators leave: 4 stages at
+// PBT = 192.  Narrower tiles (deeper A rings: 6 stages at 160, 8 at 128) were
+// measured slower, 941 and 830 TFLOP/s against 1035 on the encoder FFN pair.
+constexpr int kPairTokens = 192;
+template <int PBT> struct PCfg {
+    static constexpr int PHALF = PBT / 2;
+    static constexpr int X_STAGE = PHALF * BK * 2;   // f16 bytes of one CTA's X half
+    static constexpr int STAGES = RING_BYTES / (X_STAGE + W_STAGE) < MAX_STAGES
+                                      ? RING_BYTES / (X_STAGE + W_STAGE) : MAX_STAGES;
+    static constexpr int ACC_COLS = PBT;
+    static constexpr int A_COL0 = 2 * PBT;
+    static constexpr int A_ST_RAW = (TMEM_COLS - A_COL0) / A_STAGE_COLS;
+    static constexpr int A_ST = (A_ST_RAW > MAX_A_STAGES ? MAX_A_STAGES : A_ST_RAW) & ~1;
+    static_assert(A_ST >= 2 && A_COL0 + A_ST * A_STAGE_COLS <= TMEM_COLS, "TMEM budget");
+    static_assert(STAGES % 2 == 0, "pair mode needs an even ring");
+    static_assert(X_STAGE % 1024 == 0, "SWIZZLE_128B atoms");
+    static_assert(PBT % 32 == 0 && PBT >= 64 && PBT <= 256, "MMA N");
+    static constexpr uint32_t IDESC = idesc_f16_f32(PBN, PBT);
+    static constexpr size_t SMEM_BASE = 1024 + (size_t)STAGES * (X_STAGE + W_STAGE) + kBarsBytes;
+    static_assert(SMEM_BASE + Y_STAGE_BYTES <= 227 * 1024, "shared memory");
+};
+constexpr int kPairDqArrivals = 2 * 4;         // dequant warps of one stage, both CTAs
+constexpr int kPairEpiArrivals = 2 * kEpiWarps; // epilogue warps, both CTAs
+
+template <int PBT, int EPI> constexpr size_t pair_smem() {
+    return PCfg<PBT>::SMEM_BASE + (kStagedY<EPI> ? Y_STAGE_BYTES : 0);
+}
+
+template <int PBT, int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    q8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
+                        const __grid_constant__ CUtensorMap tmY, const GemmArgs p, int ystore) {
+    using C = PCfg<PBT>;
+    constexpr int STAGES = C::STAGES;
+    constexpr int A_STAGES = C::A_ST;
+    constexpr int PHALF = C::PHALF;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *xs = smem;
+    uint8_t *ws = smem + STAGES * C::X_STAGE;
+    uint8_t *ystage = ws + STAGES * W_STAGE;
+    Bars *bars = reinterpret_cast<Bars *>(ystage + (kStagedY<EPI> ? Y_STAGE_BYTES : 0));
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();        // 0: issues the pair's MMAs
+    const int pair = (int)(blockIdx.x >> 1), npairs = (int)(gridDim.x >> 1);
+    const int M = p.M, N = p.N, K = p.K;
+    const int n_tiles = (N + PBN - 1) / PBN;
+    const int num_tiles = n_tiles * ((M + PBT - 1) / PBT);
+    const int KT = (K + BK - 1) / BK;
+    const int nkb = K / 32;
+    const bool pairs = (KT & 1) == 0;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&bars->full[s], 1);
+            mbar_init(&bars->empty[s], 1);
+        }
+        for (int a = 0; a < A_STAGES; ++a) {
+            mbar_init(&bars->aready[a], kPairDqArrivals);
+            mbar_init(&bars->aempty[a], 1);
+        }
+        for (int i = 0; i < MAX_STAGES / 2; ++i) mbar_init(&bars->empty2[i], 1);
+        for (int i = 0; i < A_STAGES / 2; ++i) {
+            mbar_init(&bars->aready2[i], 2 * kPairDqArrivals);
+            mbar_init(&bars->aempty2[i], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&bars->accfull[b], 1);
+            mbar_init(&bars->accempty[b], kPairEpiArrivals);
+        }
+        mbar_init(&bars->drain, 1);
+        bars->abort = 0;
+        fence_mbar_init();
+        tma_prefetch_desc(&tmX);
+        tma_prefetch_desc(&tmW);
+    }
+    if (warp == 1) {
+        tmem_alloc2(&bars->tmem_base, TMEM_COLS);
+        tmem_relinquish2();
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync_all();      // the peer's barriers are initialised before any arrival reaches them
+    tc_fence_after();
+    const uint32_t tmem = bars->tmem_base;
+    volatile int *abort_flag = &bars->abort;
+    const uint32_t peer_abort = mapa_u32(&bars->abort, rank ^ 1u);
+    int *err = p.dev_err;
+
+    if (warp == 0) {
+        // ------------------------------------------------ TMA producer (each CTA: its X half + its W rows)
+        if (lane == 0) {
+            int s = 0;
+            uint32_t ph = 0;
+            uint32_t issued_mask = 0, last_ph[STAGES];
+            for (int tile = pair; tile < num_tiles; tile += npairs) {
+                const int m0 = (tile / n_tiles) * PBT + (int)rank * PHALF;
+                const int n0 = (tile % n_tiles) * PBN + (int)rank * BN;
+                for (int kt = 0; kt < KT; ++kt) {
+                    if (!mbar_wait_cl(pairs ? &bars->empty2[s >> 1] : &bars->empty[s], ph ^ 1, abort_flag, peer_abort,
+                                      err))
+                        goto producer_done;
+                    mbar_arrive_expect_tx(&bars->full[s], C::X_STAGE + W_STAGE);
+                    tma_load_2d(xs + s * C::X_STAGE, &tmX, &bars->full[s], kt * BK, m0);
+                    tma_load_2d(ws + s * W_STAGE, &tmW, &bars->full[s], kt * BK, n0);
+                    issued_mask |= 1u << s;
+                    last_ph[s] = ph;
+                    if (++s == STAGES) { s = 0; ph ^= 1; }
+                }
+            }
+        producer_done:
+            for (int i = 0; i < STAGES; ++i)
+                if (issued_mask & (1u << i)) mbar_wait_drain(&bars->full[i], last_ph[i]);
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ------------------------------------------------ MMA issuer (even CTA only)
+        if (rank == 0 && lane == 0) {
+            int s = 0, a = 0, lt = 0;
+            uint32_t pha = 0;
+            const uint64_t desc0 = smem_desc_sw128(smem_u32(xs));
+            const uint32_t desc_hi = (uint32_t)(desc0 >> 32);
+            const uint32_t desc_lo0 = (uint32_t)desc0;
+            constexpr uint32_t kDescStep = C::X_STAGE >> 4;
+            const uint32_t empty0 = smem_u32(&bars->empty[0]), aempty0 = smem_u32(&bars->aempty[0]);
+            const uint32_t empty2_0 = smem_u32(&bars->empty2[0]), aempty2_0 = smem_u32(&bars->aempty2[0]);
+            const uint32_t a_tmem0 = tmem + C::A_COL0;
+            for (int tile = pair; tile < num_tiles; tile += npairs, ++lt) {
+                const int b = lt & 1;
+                const uint32_t aph = (lt >> 1) & 1;
+                if (!mbar_wait_cl(&bars->accempty[b], aph ^ 1, abort_flag, peer_abort, err)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem + b * C::ACC_COLS;
+                bool ok = true;
+                if (pairs) {
+                    for (int kt = 0; kt < KT; kt += 2) {
+                        if (!mbar_wait_cl(&bars->aready2[a >> 1], pha, abort_flag, peer_abort, err)) { ok = false; break; }
+                        tc_fence_after();
+                        umma2_stage8_ts_2c(d_tmem, a_tmem0 + a * A_STAGE_COLS, desc_lo0 + (uint32_t)s * kDescStep,
+                                           desc_hi, kDescStep, C::IDESC, kt != 0, empty2_0 + 8u * (s >> 1),
+                                           aempty2_0 + 8u * (a >> 1));
+                        if ((s += 2) == STAGES) s = 0;
+                        if ((a += 2) == A_STAGES) { a = 0; pha ^= 1; }
+                    }
+                } else {
+                    for (int kt = 0; kt < KT; ++kt) {
+                        if (!mbar_wait_cl(&bars->aready[a], pha, abort_flag, peer_abort, err)) { ok = false; break; }
+                        tc_fence_after();
+                        umma2_stage4_ts(d_tmem, a_tmem0 + a * A_STAGE_COLS, desc_lo0 + (uint32_t)s * kDescStep, desc_hi,
+                                        C::IDESC, kt != 0, empty0 + 8u * s, aempty0 + 8u * a);
+                        if (++s == STAGES) s = 0;
+                        if (++a == A_STAGES) { a = 0; pha ^= 1; }
+                    }
+                }
+                if (!ok) break;
+                umma2_commit_both(&bars->accfull[b]);
+            }
+            // every MMA issued must finish before either CTA releases tensor memory
+            umma2_commit_both(&bars->drain);
+            mbar_wait_drain(&bars->drain, 0);
+        }
+        __syncwarp();
+    } else if (warp >= kDqWarp0 && warp < kEpiWarp0) {
+        // ------------------------------------------------ dequant: int8 smem -> f16 TMEM (this CTA's rows)
+        const int grp = (warp - kDqWarp0) >> 2;
+        const int q = warp & 3;
+        const int r = q * 32 + lane;
+        const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+        const int swz = (r >> 1) & 3;
+        const bool pair_ok = (nkb & 1) == 0;
+        const int gstep = npairs % n_tiles;
+        const int rbase = (int)rank * BN + r;       // row within the pair tile
+        const uint32_t aready0 = mapa_u32(&bars->aready[0], 0), aready2_0 = mapa_u32(&bars->aready2[0], 0);
+        struct Cur {
+            int kt, tile, nt;
+        };
+        auto adv = [&](Cur &c) {
+            c.kt += 2;
+            while (c.kt >= KT) {
+                c.kt -= KT;
+                c.tile += npairs;
+                c.nt += gstep;
+                if (c.nt >= n_tiles) c.nt -= n_tiles;
+            }
+        };
+        auto scale_at = [&](const Cur &c) -> uint2 {
+            const int n = c.nt * PBN + rbase;
+            const int kb = 2 * c.kt;
+            const bool rowok = c.tile < num_tiles && n < N;
+            const __half *sp = p.scales + (size_t)(rowok ? n : 0) * nkb + (rowok ? kb : 0);
+            uint2 v = make_uint2(0u, 0u);
+            if (pair_ok) {
+                ldg_nc_u32_pred(v.x, sp, rowok);
+            } else {
+                ldg_nc_u16_pred(v.x, sp, rowok && kb < nkb);
+                ldg_nc_u16_pred(v.y, sp + 1, rowok && kb + 1 < nkb);
+            }
+            return v;
+        };
+        int s = grp % STAGES, as = grp % A_STAGES;
+        uint32_t ph = (uint32_t)(grp / STAGES) & 1u, pha = (uint32_t)(grp / A_STAGES) & 1u;
+        auto visit = [&](int tile, uint2 swv) -> bool {
+            if (tile >= num_tiles) return false;
+            if (!warp_wait_all_cl(&bars->full[s], ph, abort_flag, peer_abort, err)) return false;
+            const uint32_t sw = pair_ok ? swv.x : (swv.x | (swv.y << 16));
+            const __half2 sw2 = *reinterpret_cast<const __half2 *>(&sw);
+            const __half2 sc_lo = __low2half2(sw2), sc_hi = __high2half2(sw2);
+            const uint8_t *wrow = ws + s * W_STAGE + r * 64;
+            uint32_t a[32];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const uint4 v = *reinterpret_cast<const uint4 *>(wrow + ((c ^ swz) << 4));
+                const __half2 sc = c < 2 ? sc_lo : sc_hi;
+                const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    __half2 lo, hi;
+                    q8_to_half2x2(wv[i], lo, hi);
+                    a[c * 8 + 2 * i] = h2_as_u32(__hmul2(lo, sc));
+                    a[c * 8 + 2 * i + 1] = h2_as_u32(__hmul2(hi, sc));
+                }
+            }
+            if (!warp_wait_all_cl(pairs ? &bars->aempty2[as >> 1] : &bars->aempty[as], pha ^ 1u, abort_flag, peer_abort,
+                                  err))
+                return false;
+            tc_fence_after();
+            tmem_st32(tmem + lane_addr + C::A_COL0 + as * A_STAGE_COLS, a);
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(pairs ? aready2_0 + 8u * (as >> 1) : aready0 + 8u * as);
+            s += 2;
+            if (s >= STAGES) { s -= STAGES; ph ^= 1u; }
+            as += 2;
+            if (as >= A_STAGES) { as -= A_STAGES; pha ^= 1u; }
+            return true;
+        };
+        Cur vc{grp % KT, pair + (grp / KT) * npairs, 0};
+        vc.nt = vc.tile % n_tiles;
+        Cur pc = vc;
+        adv(pc);
+        uint2 sA = scale_at(vc), sB = scale_at(pc);
+        adv(pc);
+        while (true) {
+            uint2 use = sA;
+            sA = scale_at(pc);
+            adv(pc);
+            if (!visit(vc.tile, use)) break;
+            adv(vc);
+            use = sB;
+            sB = scale_at(pc);
+            adv(pc);
+            if (!visit(vc.tile, use)) break;
+            adv(vc);
+        }
+    } else if (warp >= kEpiWarp0) {
+        // ------------------------------------------------ epilogue: this CTA's 128 rows x 192 tokens
+        const int q = warp & 3;
+        const int half = (warp - kEpiWarp0) >> 2;
+        const int r = q * 32 + lane;
+        const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+        const bool leader = q == 0 && lane == 0;
+        const int bar_id = 1 + half;
+        uint8_t *ybuf = ystage + half * 2 * Y_BUF;
+        const uint32_t accempty0 = mapa_u32(&bars->accempty[0], 0);
+        int ycnt = 0;
+        int lt = 0;
+        for (int tile = pair; tile < num_tiles; tile += npairs, ++lt) {
+            const int b = lt & 1;
+            const uint32_t aph = (lt >> 1) & 1;
+            if (!warp_wait_all_cl(&bars->accfull[b], aph, abort_flag, peer_abort, err)) break;
+            tc_fence_after();
+            const int m0 = (tile / n_tiles) * PBT;
+            const int n0 = (tile % n_tiles) * PBN + (int)rank * BN;
+            const int n = n0 + r;
+            const bool nok = n < N;
+            float bias = 0.f;
+            if constexpr (EPI != kEpiNone) {
+                if (nok)
+                    bias = p.bias_f16 ? __half2float(reinterpret_cast<const __half *>(p.bias)[n])
+                                      : reinterpret_cast<const float *>(p.bias)[n];
+            }
+            const uint32_t acc_addr = tmem + lane_addr + b * C::ACC_COLS;
+#pragma unroll 1
+            for (int c = half; c < PBT / 32; c += 2) {
+                uint32_t v[32];
+                tmem_ld32(acc_addr + c * 32, v);
+                tmem_wait_ld();
+                if (kStagedY<EPI> && ystore) {
+                    __half *buf = reinterpret_cast<__half *>(ybuf + (ycnt & 1) * Y_BUF);
+                    if (leader) bulk_wait_group_read<1>();
+                    named_bar_sync(bar_id, 128);
+                    epilogue_chunk_stage<EPI>(p, v, m0 + c * 32, n, bias, nok, buf + r);
+                    fence_proxy_async_smem();
+                    named_bar_sync(bar_id, 128);
+                    if (leader) {
+                        tma_store_2d(&tmY, buf, n0, m0 + c * 32);
+                        bulk_commit_group();
+                    }
+                    ++ycnt;
+                } else if (nok) {
+                    epilogue_chunk<EPI>(p, v, m0 + c * 32, n, bias);
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(accempty0 + 8u * b);
+        }
+        if (leader) bulk_wait_group_all();
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync_all();      // no MMA, commit or arrival targets either CTA past this point
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc2(tmem, TMEM_COLS);
+    }
+}
+
+template <int PBT, int EPI>
+cudaError_t launch_pair(const GemmArgs &a, const CUtensorMap &tmX, const CUtensorMap &tmW, const CUtensorMap &tmY,
+                        int ystore, int num_sms, cudaStream_t st) {
+    auto fn = q8_gemm_pair_kernel<PBT, EPI>;
+    static int max_pairs = -1;     // once per instantiation: co-resident clusters on this device
+    if (max_pairs < 0) {
+        cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pair_smem<PBT, EPI>());
+        if (e != cudaSuccess) return e;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * (num_sms / 2));
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = pair_smem<PBT, EPI>();
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = 2;
+        at[0].val.clusterDim.y = 1;
+        at[0].val.clusterDim.z = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        int n = 0;
+        e = cudaOccupancyMaxActiveClusters(&n, fn, &cfg);
+        if (e != cudaSuccess) return e;
+        max_pairs = n > 0 ? n : 1;
+    }
+    const int tiles = ((a.N + PBN - 1) / PBN) * ((a.M + PBT - 1) / PBT);
+    const int pairs = tiles < max_pairs ? tiles : max_pairs;
+    fn<<<2 * pairs, kThreads, pair_smem<PBT, EPI>(), st>>>(tmX, tmW, tmY, a, ystore);
+    return cudaGetLastError();
+}
+
 bool make_map(CUtensorMap *m, CUtensorMapDataType dt, const void *base, uint64_t inner, uint64_t outer,
               uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz) {
     PFN_encodeTiled enc = tensor_map_encoder();
@@ -537,8 +923,19 @@ PFN_encodeTiled tensor_map_encoder() {
     return fn;
 }
 
+// CTA-pair kernel by default; MADI_GEMM_PAIR=0 in the environment selects the
+// one-CTA kernel (kept for comparison and for devices without cluster support).
+static bool use_pair_kernel() {
+    static int v = -1;
+    if (v < 0) {
+        const char *e = getenv("MADI_GEMM_PAIR");
+        v = (e && e[0] == '0') ? 0 : 1;
+    }
+    return v == 1;
+}
 cudaError_t launch_gemm_tc(const GemmArgs &a, int epi, int num_sms, cudaStream_t st) {
-    const int bt = pick_bt(a.M, a.N, num_sms);
+    const bool pair = use_pair_kernel() && num_sms >= 2;
+    const int bt = pair ? kPairTokens / 2 : pick_bt(a.M, a.N, num_sms);   // X box rows
     CUtensorMap tmX, tmW;
     if (!make_map(&tmX, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.x, (uint64_t)a.K, (uint64_t)a.M, (uint64_t)a.K * 2, BK,
                   (uint32_t)bt, CU_TENSOR_MAP_SWIZZLE_128B))
@@ -553,6 +950,15 @@ cudaError_t launch_gemm_tc(const GemmArgs &a, int epi, int num_sms, cudaStream_t
                  make_map(&tmY, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.y, (uint64_t)a.N, (uint64_t)a.M,
                           (uint64_t)a.N * 2, BN, Y_ROWS, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (!ystore) memset(&tmY, 0, sizeof(tmY));
+    if (pair) {
+        switch (epi) {
+            case kEpiNone: return launch_pair<kPairTokens, kEpiNone>(a, tmX, tmW, tmY, ystore, num_sms, st);
+            case kEpiBias: return launch_pair<kPairTokens, kEpiBias>(a, tmX, tmW, tmY, ystore, num_sms, st);
+            case kEpiBiasGelu: return launch_pair<kPairTokens, kEpiBiasGelu>(a, tmX, tmW, tmY, ystore, num_sms, st);
+            case kEpiBiasRes: return launch_pair<kPairTokens, kEpiBiasRes>(a, tmX, tmW, tmY, ystore, num_sms, st);
+            default: return cudaErrorInvalidValue;
+        }
+    }
 #define MADI_GEMM_EPI(BT)                                                                         \
     switch (epi) {                                                                                \
         case kEpiNone: return launch_bt<BT, kEpiNone>(a, tmX, tmW, tmY, ystore, num_sms, st);     \
