@@ -545,7 +545,9 @@ def decode_leg(args, world, rank, dev, stream, peaks):
                                                   "back-to-back launches in a CUDA graph)",
                          "achieved": head["GBps"], "peak": peaks["hbm"], "unit": "GB/s",
                          "frac": head["GBps"] / peaks["hbm"],
-                         "traffic": load_traffic(f"q8_gemv_tile_head_m{Md}")},
+                         # captured on the full 51866-row head; a column shard moves its rows' share
+                         "traffic": (None if load_traffic(f"q8_gemv_tile_head_m{Md}") is None
+                                     else int(load_traffic(f"q8_gemv_tile_head_m{Md}") * hn / 51866))},
             "l2": "step: two 168 MB weight sets replayed alternately (> 126 MB L2); per shape: > 300 MB of "
                   "distinct weight copies per graph"}
 

@@ -236,6 +236,21 @@ int madi_logit_filter(float *logits, int vocab, const uint32_t *past, int past_l
                       const uint32_t *step, uint32_t sample_begin, uint32_t no_repeat_ngram,
                       void *stream);
 
+/* Greedy token of each of m full logit rows (tokens[s], no position), the
+ * reference's argmax including its tie order (graph_helpers.metal:64-95). */
+int madi_argmax_rows(const float *logits, int m, int vocab, uint32_t *tokens, void *stream);
+
+/* Column-split vocab head (one shard per GPU; no reference counterpart: the
+ * reference engine runs the head on one device).  madi_shard_argmax reduces
+ * each of m rows of this shard's logits (n columns, global index h0 + column)
+ * to a (value, global index) pair, ties ordered as the reference's argmax
+ * orders them; madi_merge_shard_argmax takes the all-gathered pairs (rank-major,
+ * vals[r * m + row]) and writes the greedy token of each row.  Together they give
+ * the same tokens as madi_argmax_rows over the gathered full rows. */
+int madi_shard_argmax(const float *logits, int m, int n, int64_t row_stride, uint32_t h0, float *vals, uint32_t *idx,
+                      void *stream);
+int madi_merge_shard_argmax(const float *vals, const uint32_t *idx, int world, int m, uint32_t *tokens, void *stream);
+
 /* step_advance (graph_helpers.metal:60-62) for m <= 32 slots: pos[s] += 1. */
 int madi_step_advance(uint32_t *pos, int m, void *stream);
 

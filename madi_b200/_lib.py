@@ -61,6 +61,9 @@ SIGNATURES = {
     "madi_argmax_conf": ([P, I, I, P, P, P, I, ctypes.c_int64, P], I),
     "madi_logit_filter": ([P, I, P, I, P, U32, U32, P], I),
     "madi_step_advance": ([P, I, P], I),
+    "madi_argmax_rows": ([P, I, I, P, P], I),
+    "madi_shard_argmax": ([P, I, I, ctypes.c_int64, U32, P, P, P], I),
+    "madi_merge_shard_argmax": ([P, P, I, I, P, P], I),
 }
 
 _lib = None

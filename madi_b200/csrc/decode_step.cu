@@ -112,7 +112,7 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float *__restrict__ 
         inv_sum = 1.0f / sv[0];
     }
     if (t == 0) {
-        const uint32_t cur = pos[s];
+        const uint32_t cur = pos ? pos[s] : 0u;
         if (cur < (uint32_t)max_len) {
             tokens[(size_t)s * stride + cur] = amax;
             if constexpr (kConf) conf[(size_t)s * stride + cur] = inv_sum;
@@ -164,6 +164,60 @@ __global__ void __launch_bounds__(256) logit_filter_kernel(float *__restrict__ l
     }
 }
 
+// ---- greedy token over a column-split vocab head (one shard per GPU)
+//
+// The reference's tree (argmax_kernel above) prefers, among tied maxima, the
+// index g whose lane g mod 1024 is smallest when its 10 bits are reversed, then
+// the smallest g.  That is a total order on g, so a shard can reduce with the
+// key (bitrev10(g & 1023), g) and the shards' winners merge exactly.
+MADI_DEV uint64_t tie_key(uint32_t g) { return ((uint64_t)(__brev(g & 1023u) >> 22) << 32) | g; }
+MADI_DEV bool better(float v, uint64_t k, float bv, uint64_t bk) { return v > bv || (v == bv && k < bk); }
+
+// One CTA of 1024 threads per row: (max, global index) of logits[row][0..n),
+// global index = h0 + local index.
+__global__ void __launch_bounds__(1024) shard_argmax_kernel(const float *__restrict__ logits, long long row_stride,
+                                                            int n, uint32_t h0, float *__restrict__ vals,
+                                                            uint32_t *__restrict__ idx) {
+    __shared__ float sv[1024];
+    __shared__ uint64_t sk[1024];
+    const int t = threadIdx.x, row = blockIdx.x;
+    const float *lg = logits + (size_t)row * row_stride;
+    float bv = -INFINITY;
+    uint64_t bk = ~0ull;
+    for (int i = t; i < n; i += 1024) {
+        const float v = lg[i];
+        const uint64_t k = tie_key(h0 + (uint32_t)i);
+        if (better(v, k, bv, bk)) { bv = v; bk = k; }
+    }
+    sv[t] = bv;
+    sk[t] = bk;
+    __syncthreads();
+    for (int st = 512; st > 0; st >>= 1) {
+        if (t < st && better(sv[t + st], sk[t + st], sv[t], sk[t])) { sv[t] = sv[t + st]; sk[t] = sk[t + st]; }
+        __syncthreads();
+    }
+    if (t == 0) {
+        vals[row] = sv[0];
+        idx[row] = (uint32_t)sk[0];
+    }
+}
+
+// tokens[row] = the best of the `world` (value, index) pairs of the row; pairs
+// are rank-major: vals[r * m + row].
+__global__ void merge_argmax_kernel(const float *__restrict__ vals, const uint32_t *__restrict__ idx, int world, int m,
+                                    uint32_t *__restrict__ tokens) {
+    const int row = blockIdx.x * blockDim.x + threadIdx.x;
+    if (row >= m) return;
+    float bv = vals[row];
+    uint32_t bi = idx[row];
+    for (int r = 1; r < world; ++r) {
+        const float v = vals[(size_t)r * m + row];
+        const uint32_t i = idx[(size_t)r * m + row];
+        if (better(v, tie_key(i), bv, tie_key(bi))) { bv = v; bi = i; }
+    }
+    tokens[row] = bi;
+}
+
 }  // namespace
 
 cudaError_t launch_emb_q8(float *out, const int8_t *qs, const __half *scales, const uint32_t *tokens,
@@ -208,6 +262,18 @@ cudaError_t launch_suppress(float *logits, const uint32_t *ids, int n, int V, cu
 cudaError_t launch_logit_filter(float *logits, const uint32_t *past, const uint32_t *step_ptr, uint32_t sample_begin,
                                 uint32_t no_repeat_ngram, int V, int past_len, cudaStream_t st) {
     logit_filter_kernel<<<1, 256, 0, st>>>(logits, past, step_ptr, sample_begin, no_repeat_ngram, V, past_len);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_shard_argmax(const float *logits, long long row_stride, int n, uint32_t h0, int m, float *vals,
+                                uint32_t *idx, cudaStream_t st) {
+    shard_argmax_kernel<<<m, 1024, 0, st>>>(logits, row_stride, n, h0, vals, idx);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_merge_argmax(const float *vals, const uint32_t *idx, int world, int m, uint32_t *tokens,
+                                cudaStream_t st) {
+    merge_argmax_kernel<<<(m + 127) / 128, 128, 0, st>>>(vals, idx, world, m, tokens);
     return cudaGetLastError();
 }
 

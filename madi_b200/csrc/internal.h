@@ -76,6 +76,10 @@ cudaError_t launch_argmax(const float *logits, uint32_t *tokens, float *conf, co
 cudaError_t launch_suppress(float *logits, const uint32_t *ids, int n, int V, cudaStream_t st);
 cudaError_t launch_logit_filter(float *logits, const uint32_t *past, const uint32_t *step_ptr, uint32_t sample_begin,
                                 uint32_t no_repeat_ngram, int V, int past_len, cudaStream_t st);
+cudaError_t launch_shard_argmax(const float *logits, long long row_stride, int n, uint32_t h0, int m, float *vals,
+                                uint32_t *idx, cudaStream_t st);
+cudaError_t launch_merge_argmax(const float *vals, const uint32_t *idx, int world, int m, uint32_t *tokens,
+                                cudaStream_t st);
 
 // ---------------------------------------------------------------- misc kernels
 cudaError_t launch_dequant_f16(const int8_t *qs, const __half *scales, int N, int K, __half *out, cudaStream_t st);

@@ -739,6 +739,30 @@ int madi_logit_filter(float *logits, int vocab, const uint32_t *past, int past_l
     return e == cudaSuccess ? MADI_OK : cuda_fail(e, "madi_logit_filter");
 }
 
+int madi_argmax_rows(const float *logits, int m, int vocab, uint32_t *tokens, void *stream) {
+    if (!S.ready) return fail(MADI_ENOINIT, "madi_argmax_rows: not initialised");
+    if (!logits || !tokens || m <= 0 || vocab <= 0) return fail(MADI_EINVAL, "madi_argmax_rows: bad argument");
+    cudaError_t e = launch_argmax(logits, tokens, nullptr, nullptr, vocab, 1, m, 1, pick_stream(stream));
+    return e == cudaSuccess ? MADI_OK : cuda_fail(e, "madi_argmax_rows");
+}
+
+int madi_shard_argmax(const float *logits, int m, int n, int64_t row_stride, uint32_t h0, float *vals, uint32_t *idx,
+                      void *stream) {
+    if (!S.ready) return fail(MADI_ENOINIT, "madi_shard_argmax: not initialised");
+    if (!logits || !vals || !idx || m <= 0 || n <= 0 || row_stride < n)
+        return fail(MADI_EINVAL, "madi_shard_argmax: bad argument (m=%d n=%d)", m, n);
+    cudaError_t e = launch_shard_argmax(logits, (long long)row_stride, n, h0, m, vals, idx, pick_stream(stream));
+    return e == cudaSuccess ? MADI_OK : cuda_fail(e, "madi_shard_argmax");
+}
+
+int madi_merge_shard_argmax(const float *vals, const uint32_t *idx, int world, int m, uint32_t *tokens, void *stream) {
+    if (!S.ready) return fail(MADI_ENOINIT, "madi_merge_shard_argmax: not initialised");
+    if (!vals || !idx || !tokens || world <= 0 || m <= 0)
+        return fail(MADI_EINVAL, "madi_merge_shard_argmax: bad argument");
+    cudaError_t e = launch_merge_argmax(vals, idx, world, m, tokens, pick_stream(stream));
+    return e == cudaSuccess ? MADI_OK : cuda_fail(e, "madi_merge_shard_argmax");
+}
+
 int madi_step_advance(uint32_t *pos, int m, void *stream) {
     if (!S.ready) return fail(MADI_ENOINIT, "madi_step_advance: not initialised");
     if (!pos || m <= 0 || m > 32) return fail(MADI_EINVAL, "madi_step_advance: m=%d (1..32)", m);

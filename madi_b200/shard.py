@@ -12,7 +12,10 @@
   a total order on indices (tie_key), so per-shard winners merge exactly.
 
 Only torch.distributed is used for the exchange; the per-rank logits come from
-madi_b200.q8.linear on the rank's own head shard.
+madi_b200.q8.linear on the rank's own head shard.  On CUDA tensors the greedy
+reductions run as the library's kernels (madi_argmax_rows, madi_shard_argmax,
+madi_merge_shard_argmax); the torch formulation below is the host-side version
+the CPU (gloo) tests run and check the kernels against.
 """
 from typing import Tuple
 
@@ -69,21 +72,56 @@ def _pick(values: torch.Tensor, indices: torch.Tensor, dim: int) -> Tuple[torch.
     return best.squeeze(dim), keys.min(dim=dim).values & 0xFFFFFFFF
 
 
+def _lib():
+    from . import _lib as L
+    return L
+
+
+def _stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
 def greedy_tokens(logits: torch.Tensor) -> torch.Tensor:
-    """Greedy token per row of full logits [m][vocab], the reference's tie rule."""
+    """Greedy token per row of full logits [m][vocab], the reference's tie rule (int64)."""
+    if logits.is_cuda:
+        lg = logits.float().contiguous()
+        m, v = lg.shape
+        tok = torch.empty(m, dtype=torch.int32, device=lg.device)
+        L = _lib()
+        L.check(L.load().madi_argmax_rows(lg.data_ptr(), m, v, tok.data_ptr(), _stream()), "madi_argmax_rows")
+        return tok.long()
     idx = torch.arange(logits.shape[-1], device=logits.device).expand_as(logits)
     return _pick(logits, idx, -1)[1]
 
 
 def shard_argmax(local: torch.Tensor, h0: int) -> Tuple[torch.Tensor, torch.Tensor]:
     """Per-row (max value, global index) of a shard -- the cheap alternative to gathering
-    whole logit rows: gather these pairs and merge with merge_shard_argmax."""
+    whole logit rows: gather these pairs and merge with merge_shard_argmax.  Values are
+    f32; indices int32 on CUDA, int64 on the host."""
+    if local.is_cuda:
+        lg = local if local.dtype == torch.float32 and local.stride(-1) == 1 else local.float().contiguous()
+        m, n = lg.shape
+        vals = torch.empty(m, dtype=torch.float32, device=lg.device)
+        idx = torch.empty(m, dtype=torch.int32, device=lg.device)
+        L = _lib()
+        L.check(L.load().madi_shard_argmax(lg.data_ptr(), m, n, lg.stride(0), int(h0), vals.data_ptr(), idx.data_ptr(),
+                                           _stream()), "madi_shard_argmax")
+        return vals, idx
     idx = torch.arange(h0, h0 + local.shape[-1], device=local.device).expand_as(local)
     return _pick(local, idx, -1)
 
 
 def merge_shard_argmax(values: torch.Tensor, indices: torch.Tensor) -> torch.Tensor:
     """values/indices [world][m] -> global greedy index per row (the reference's tie rule)."""
+    if values.is_cuda:
+        vals = values.float().contiguous()
+        idx = indices.to(torch.int32).contiguous()
+        world, m = vals.shape
+        tok = torch.empty(m, dtype=torch.int32, device=vals.device)
+        L = _lib()
+        L.check(L.load().madi_merge_shard_argmax(vals.data_ptr(), idx.data_ptr(), world, m, tok.data_ptr(), _stream()),
+                "madi_merge_shard_argmax")
+        return tok.long()
     return _pick(values, indices, 0)[1]
 
 

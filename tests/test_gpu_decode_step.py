@@ -302,3 +302,31 @@ def test_greedy_loop_cuda_graph(madi, oracle):
     cf = conf[0, 1:steps + 1].cpu().numpy()
     np.testing.assert_allclose(cf, want_conf, rtol=1e-4)
     del graph
+
+
+def test_column_split_greedy_kernels(madi, oracle):
+    """madi_shard_argmax per vocab shard + madi_merge_shard_argmax give the
+    reference's greedy token (its tie order included), equal to madi_argmax_rows
+    on the full rows and to the host formulation the gloo tests use."""
+    import torch
+    from madi_b200 import shard
+    g = np.random.default_rng(77)
+    m = 5
+    L = g.integers(-6, 7, (m, VOCAB)).astype(np.float32)      # thousands of ties at each row's max
+    L[3] = g.standard_normal(VOCAB).astype(np.float32)        # one row without ties
+    L[4, :] = -np.inf                                          # all -inf: token 0, as the reference
+    want = [oracle.argmax(L[r]) for r in range(m)]
+    full = _t(L)
+    assert shard.greedy_tokens(full).cpu().tolist() == want
+    for world in (2, 3, 8):
+        vs, is_ = [], []
+        for rank in range(world):
+            h0, h1 = shard.vocab_shard(VOCAB, world, rank)
+            v, i = shard.shard_argmax(full[:, h0:h1], h0)     # strided view: row stride VOCAB
+            vs.append(v)
+            is_.append(i)
+        tok = shard.merge_shard_argmax(torch.stack(vs), torch.stack(is_))
+        torch.cuda.synchronize()
+        assert tok.cpu().tolist() == want, f"world {world}"
+        host = shard.merge_shard_argmax(torch.stack([v.cpu() for v in vs]), torch.stack([i.cpu().long() for i in is_]))
+        assert host.tolist() == want
