@@ -444,33 +444,66 @@ def decode_leg(args, world, rank, dev, stream, peaks):
     ms = e0.elapsed_time(e1) / K
     ag = {}
     if world > 1:
-        # column-split head: the greedy token needs every rank's shard.  Two equal-
-        # result exchanges over NCCL, each captured in the step's graph (every rank
-        # captures and replays the same sequence): the whole logit shards, or only
-        # each shard's per-row (max, argmax) pair.
+        # Column-split vocab head across the ranks' chunks: rank r serves its own Md
+        # slots but owns only vocab rows [h0, h1).  One token step = the rank's
+        # decoder projections on its slots, an all-gather of every rank's hidden
+        # states, this rank's shard logits for ALL world * Md slots (M > 8: the
+        # tcgen05 GEMM), then the greedy exchange -- either the whole logit shards
+        # or only each shard's per-row (max, argmax) pair -- and the tokens of the
+        # rank's own slots.  Timed beside it: the replicated head (every rank holds
+        # all 51866 rows and needs no exchange).  Every rank captures and replays the
+        # same sequence; NCCL calls are captured in the step's graph.
+        import torch.distributed as dist
+        X_all = torch.empty((world * Md, D), dtype=torch.float16, device=dev)
+        x16 = x if x.dtype == torch.float16 else x.half()
+        logits_all = torch.empty((world * Md, hn), dtype=torch.float32, device=dev)
+        logits_full = torch.empty((Md, V), dtype=torch.float32, device=dev)
+        full_heads = []
+        for seed in (1, 2):
+            hq, hs = synth.q8_weight(V, D, seed * 1000 + 999)
+            full_heads.append(q8.Q8Weight(t(hq), t(hs)))
+
+        def layers_only(layers):
+            for L in layers:
+                q8.linear(L["qkv"][0], x, out=outs["qkv"], stream=stream)
+                q8.linear(L["o"][0], x, out=outs["o"], stream=stream)
+                q8.linear(L["cq"][0], x, bias=L["cq"][1], out=outs["cq"], stream=stream)
+                q8.linear(L["co"][0], x, out=outs["co"], stream=stream)
+                q8.linear(L["fc1"][0], x, bias=L["fc1"][1], epi=q8.EPI_BIAS_GELU, out=big, stream=stream)
+                q8.linear(L["fc2"][0], big, bias=L["fc2"][1], epi=q8.EPI_BIAS_RES, residual=resid, out=resid,
+                          stream=stream)
+
         def make_step(kind):
-            def step(s):
-                token_step(*s)
+            def step(i):
+                layers, head = sets[i]
+                layers_only(layers)
+                if kind == "replicated":
+                    q8.linear(full_heads[i], x, out=logits_full, stream=stream)
+                    return shard.greedy_tokens(logits_full)
+                dist.all_gather_into_tensor(X_all, x16)                 # hidden states of all slots
+                q8.linear(head, X_all, out=logits_all, stream=stream)   # this shard, all slots
                 if kind == "logits":
-                    return shard.greedy_tokens(shard.allgather_logits(logits, V, world))
-                return shard.allgather_greedy(logits, V, world, rank)
+                    tok = shard.greedy_tokens(shard.allgather_logits(logits_all, V, world))
+                else:
+                    tok = shard.allgather_greedy(logits_all, V, world, rank)
+                return tok[rank * Md:(rank + 1) * Md]                   # this rank's slots
             return step
 
-        for kind in ("logits", "argmax_pairs"):
+        for kind in ("logits", "argmax_pairs", "replicated"):
             step = make_step(kind)
-            ag_graphs, how = [], "CUDA graph (NCCL all-gather captured)"
+            ag_graphs, how = [], "CUDA graph (NCCL collectives captured)"
             try:
                 with torch.cuda.stream(stream):
-                    for s in sets:
-                        step(s)
+                    for i in range(2):
+                        step(i)
                     torch.cuda.synchronize()
-                    for s in sets:
+                    for i in range(2):
                         g = torch.cuda.CUDAGraph()
                         with torch.cuda.graph(g, stream=stream, capture_error_mode="thread_local"):
-                            step(s)
+                            step(i)
                         ag_graphs.append(g)
             except Exception as e:                 # capture refused: eager exchange
-                ag_graphs, how = [], f"eager all-gather ({type(e).__name__})"
+                ag_graphs, how = [], f"eager collectives ({type(e).__name__})"
             barrier(world)
             a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             with torch.cuda.stream(stream):
@@ -479,11 +512,12 @@ def decode_leg(args, world, rank, dev, stream, peaks):
                     if ag_graphs:
                         ag_graphs[i % 2].replay()
                     else:
-                        step(sets[i % 2])
+                        step(i % 2)
                 a1.record(stream)
             torch.cuda.synchronize()
             ag[kind] = {"ms": max_over_ranks(world, a0.elapsed_time(a1) / K), "timing": how}
             del ag_graphs
+        del full_heads
     ms_max = max_over_ranks(world, ms)
     del graphs
 
@@ -538,9 +572,14 @@ def decode_leg(args, world, rank, dev, stream, peaks):
     return {"value": bytes_step * world / (ms_max / 1e3) / 1e9, "unit": "GB/s", "m_tokens": Md,
             "activations": args.decode_x, "bytes_per_step_per_gpu": bytes_step, "ms_per_token_step": ms_max,
             "step_GBps_per_gpu": gbs, "gpu_launches_per_step": 25, "head_rows_per_gpu": hn,
-            "step_with_logit_allgather_ms": ag.get("logits", {}).get("ms"),
-            "step_with_argmax_pair_allgather_ms": ag.get("argmax_pairs", {}).get("ms"),
-            "allgather_timing": ag.get("logits", {}).get("timing"), "per_shape": per_shape,
+            # N > 1: whole token steps with the split head (hidden-state all-gather, shard
+            # logits for all world * Md slots, then the greedy exchange) and with the
+            # head replicated on every rank; ms_per_token_step is the rank-local
+            # projections alone (this rank's slots, this rank's head shard)
+            "split_head_step_logit_gather_ms": ag.get("logits", {}).get("ms"),
+            "split_head_step_pair_gather_ms": ag.get("argmax_pairs", {}).get("ms"),
+            "replicated_head_step_ms": ag.get("replicated", {}).get("ms"),
+            "collective_timing": ag.get("logits", {}).get("timing"), "per_shape": per_shape,
             "roofline": {"bound": "hbm", "kernel": f"q8_gemv_tile_kernel (vocab head {hn}x{D}, M={Md}, "
                                                   "back-to-back launches in a CUDA graph)",
                          "achieved": head["GBps"], "peak": peaks["hbm"], "unit": "GB/s",

@@ -162,8 +162,10 @@ int   madi_num_sms(void);
  * per-projection pairs (kDeq + m4_gemm_bias / _bias_gelu / _nn, encoder.zig:262-304;
  * the gemv_q8* family, decoder.zig:155-200; the batched f16 projection,
  * decoder.zig:337-341).  One call, no dequant scratch:
- *   m > 8 : tcgen05 tensor-core GEMM, X f16, Y f16, residual f16;
- *           f16 dequantised weights, f32 accumulation.
+ *   m > 8 : tcgen05 tensor-core GEMM, X f16, Y f16, residual f16 (Y f32 is
+ *           accepted with MADI_EPI_NONE: unrounded f32 sums, e.g. the logits of
+ *           a vocab head over more than 8 token slots); f16 dequantised
+ *           weights, f32 accumulation.
  *   m <= 8: bandwidth-bound skinny GEMM, X f32 or f16, Y f32 or f16,
  *           residual with Y's type and may alias Y; f32 semantics
  *           (exact int8 weights, per-block f32 scale).

@@ -10,6 +10,9 @@
 namespace madi {
 
 enum : int { kEpiNone = 0, kEpiBias = 1, kEpiBiasGelu = 2, kEpiBiasRes = 3 };
+// Tensor-core path only: no epilogue, f32 output (logits of a vocab head with
+// more than 8 token slots).
+constexpr int kEpiNoneF32 = 4;
 
 // ---------------------------------------------------------------- variant (b)
 struct GemvArgs {
@@ -45,7 +48,7 @@ struct GemmArgs {
     const __half *scales;    // [N][K/32]
     const void *bias;        // [N] f32 or f16
     const __half *residual;  // [M][N] f16
-    __half *y;               // [M][N] f16
+    __half *y;               // [M][N] f16 (f32 for kEpiNoneF32)
     int M, N, K;
     int bias_f16;
     int *dev_err;            // device error word (bounded-wait expiry)

@@ -112,6 +112,13 @@ template <int EPI>
 MADI_DEV void epilogue_chunk(const GemmArgs &p, const uint32_t (&v)[32], int mb, int n, float bias) {
     const int N = p.N;
     const size_t base = (size_t)mb * N + n;
+    if constexpr (EPI == kEpiNoneF32) {
+        float *yf = reinterpret_cast<float *>(p.y);
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+            if (mb + i < p.M) yf[base + (size_t)i * N] = __uint_as_float(v[i]);
+        return;
+    }
     if (mb + 32 <= p.M) {
         float res[32];
         if constexpr (EPI == kEpiBiasRes) {
@@ -167,7 +174,7 @@ MADI_DEV void epilogue_chunk_stage(const GemmArgs &p, const uint32_t (&v)[32], i
 // read.  The residual epilogue keeps direct stores and the smaller shared-memory
 // footprint: measured faster for fc2, whose scale reads profit from the larger
 // L1 left beside it.
-template <int EPI> constexpr bool kStagedY = EPI != kEpiBiasRes;
+template <int EPI> constexpr bool kStagedY = EPI != kEpiBiasRes && EPI != kEpiNoneF32;
 template <int BT, int EPI> constexpr size_t gemm_smem() {
     return Cfg<BT>::SMEM_BASE + (kStagedY<EPI> ? Y_STAGE_BYTES : 0);
 }
@@ -438,7 +445,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int n = n0 + r;
             const bool nok = n < N;
             float bias = 0.f;
-            if constexpr (EPI != kEpiNone) {
+            if constexpr (EPI != kEpiNone && EPI != kEpiNoneF32) {
                 if (nok)
                     bias = p.bias_f16 ? __half2float(reinterpret_cast<const __half *>(p.bias)[n])
                                       : reinterpret_cast<const float *>(p.bias)[n];
@@ -805,7 +812,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const int n = n0 + r;
             const bool nok = n < N;
             float bias = 0.f;
-            if constexpr (EPI != kEpiNone) {
+            if constexpr (EPI != kEpiNone && EPI != kEpiNoneF32) {
                 if (nok)
                     bias = p.bias_f16 ? __half2float(reinterpret_cast<const __half *>(p.bias)[n])
                                       : reinterpret_cast<const float *>(p.bias)[n];
@@ -946,7 +953,7 @@ cudaError_t launch_gemm_tc(const GemmArgs &a, int epi, int num_sms, cudaStream_t
     // Output through staged TMA stores when the row pitch allows a tensor map
     // (N * 2 bytes a multiple of 16); otherwise the epilogue stores directly.
     CUtensorMap tmY;
-    int ystore = a.N % 8 == 0 && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0 &&
+    int ystore = epi != kEpiNoneF32 && a.N % 8 == 0 && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0 &&
                  make_map(&tmY, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.y, (uint64_t)a.N, (uint64_t)a.M,
                           (uint64_t)a.N * 2, BN, Y_ROWS, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (!ystore) memset(&tmY, 0, sizeof(tmY));
@@ -956,6 +963,7 @@ cudaError_t launch_gemm_tc(const GemmArgs &a, int epi, int num_sms, cudaStream_t
             case kEpiBias: return launch_pair<kPairTokens, kEpiBias>(a, tmX, tmW, tmY, ystore, num_sms, st);
             case kEpiBiasGelu: return launch_pair<kPairTokens, kEpiBiasGelu>(a, tmX, tmW, tmY, ystore, num_sms, st);
             case kEpiBiasRes: return launch_pair<kPairTokens, kEpiBiasRes>(a, tmX, tmW, tmY, ystore, num_sms, st);
+            case kEpiNoneF32: return launch_pair<kPairTokens, kEpiNoneF32>(a, tmX, tmW, tmY, 0, num_sms, st);
             default: return cudaErrorInvalidValue;
         }
     }
@@ -965,6 +973,7 @@ cudaError_t launch_gemm_tc(const GemmArgs &a, int epi, int num_sms, cudaStream_t
         case kEpiBias: return launch_bt<BT, kEpiBias>(a, tmX, tmW, tmY, ystore, num_sms, st);     \
         case kEpiBiasGelu: return launch_bt<BT, kEpiBiasGelu>(a, tmX, tmW, tmY, ystore, num_sms, st); \
         case kEpiBiasRes: return launch_bt<BT, kEpiBiasRes>(a, tmX, tmW, tmY, ystore, num_sms, st);   \
+        case kEpiNoneF32: return launch_bt<BT, kEpiNoneF32>(a, tmX, tmW, tmY, 0, num_sms, st);       \
         default: return cudaErrorInvalidValue;                                                    \
     }
     if (bt == 192) { MADI_GEMM_EPI(192) }

@@ -173,6 +173,49 @@ MADI_DEV void store_unit(const GemvArgs &p, int tile, int g8, int t, const float
     }
 }
 
+// Stage the x slice [M][kb0*32, kb0*32 + KS) once in fragment order: slot
+// (lkb, s, m, t) holds x[m][(kb0 + lkb)*32 + 8t + 4s + 0..3] as f16 hi (and, for
+// f32 x, f16 lo) pairs.  Thread `tid` of `nthr` owns the quads kq = tid, tid +
+// nthr, ... and fetches that quad of all M token rows at once (one L2 round trip
+// per quad column), then converts and stores.  x may have been written by the
+// kernel this one overlaps under programmatic dependent launch, so it is read on
+// the coherent L2 path (ld.global.cg), never through the non-coherent one.
+template <typename XT>
+MADI_DEV void stage_x(const GemvArgs &p, uint8_t *xs, int kb0, int KS, int tid, int nthr) {
+    constexpr bool kSplit = sizeof(XT) == 4;
+    const int M = p.M, K = p.K;
+    const int qrow = KS >> 2;
+    const XT *xrow = reinterpret_cast<const XT *>(p.x) + (size_t)kb0 * 32;
+    for (int kq = tid; kq < qrow; kq += nthr) {
+        const int kl = kq << 2;
+        const int slot0 = ((kl >> 5) * 2 + ((kl & 7) >> 2)) * M * 4 + ((kl & 31) >> 3);
+        if constexpr (kSplit) {
+            float4 f[8];
+#pragma unroll
+            for (int m = 0; m < 8; ++m)
+                if (m < M) f[m] = __ldcg(reinterpret_cast<const float4 *>(xrow + (size_t)m * K + kl));
+#pragma unroll
+            for (int m = 0; m < 8; ++m)
+                if (m < M) {
+                    const __half2 h01 = __floats2half2_rn(f[m].x, f[m].y);
+                    const __half2 h23 = __floats2half2_rn(f[m].z, f[m].w);
+                    const __half2 l01 = __floats2half2_rn(f[m].x - __low2float(h01), f[m].y - __high2float(h01));
+                    const __half2 l23 = __floats2half2_rn(f[m].z - __low2float(h23), f[m].w - __high2float(h23));
+                    reinterpret_cast<uint4 *>(xs)[slot0 + m * 4] =
+                        make_uint4(h2_as_u32(h01), h2_as_u32(h23), h2_as_u32(l01), h2_as_u32(l23));
+                }
+        } else {
+            uint2 u[8];
+#pragma unroll
+            for (int m = 0; m < 8; ++m)
+                if (m < M) u[m] = __ldcg(reinterpret_cast<const uint2 *>(xrow + (size_t)m * K + kl));
+#pragma unroll
+            for (int m = 0; m < 8; ++m)
+                if (m < M) reinterpret_cast<uint2 *>(xs)[slot0 + m * 4] = u[m];
+        }
+    }
+}
+
 template <typename XT, typename YT, int EPI, bool kQKV>
 __global__ void __launch_bounds__(kThreads, 2)
     q8_gemv_tile_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tms,
@@ -252,47 +295,8 @@ __global__ void __launch_bounds__(kThreads, 2)
         // ------------------------------------------------ consumers
         asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
         asm volatile("griddepcontrol.wait;" ::: "memory");
-        // stage the x slice once in fragment order: slot (lkb, s, m, t) holds
-        // x[m][(kb0 + lkb)*32 + 8t + 4s + 0..3] as f16 hi (and, for f32 x, f16 lo)
-        // pairs.  Thread c owns the quads kq = c, c + 256, ... of the slice and
-        // fetches that quad of all M token rows at once (one L2 round trip per quad
-        // column), then converts and stores.  x may have been written by the kernel
-        // this one overlaps under programmatic dependent launch, so it is read on
-        // the coherent L2 path (ld.global.cg), never through the non-coherent one.
-        {
-            const int ct = threadIdx.x - 32;
-            const int qrow = KS >> 2;
-            const XT *xrow = reinterpret_cast<const XT *>(p.x) + (size_t)kb0 * 32;
-            for (int kq = ct; kq < qrow; kq += kConsumers * 32) {
-                const int kl = kq << 2;
-                const int slot0 = ((kl >> 5) * 2 + ((kl & 7) >> 2)) * M * 4 + ((kl & 31) >> 3);
-                if constexpr (kSplit) {
-                    float4 f[8];
-#pragma unroll
-                    for (int m = 0; m < 8; ++m)
-                        if (m < M) f[m] = __ldcg(reinterpret_cast<const float4 *>(xrow + (size_t)m * K + kl));
-#pragma unroll
-                    for (int m = 0; m < 8; ++m)
-                        if (m < M) {
-                            const __half2 h01 = __floats2half2_rn(f[m].x, f[m].y);
-                            const __half2 h23 = __floats2half2_rn(f[m].z, f[m].w);
-                            const __half2 l01 = __floats2half2_rn(f[m].x - __low2float(h01), f[m].y - __high2float(h01));
-                            const __half2 l23 = __floats2half2_rn(f[m].z - __low2float(h23), f[m].w - __high2float(h23));
-                            reinterpret_cast<uint4 *>(xs)[slot0 + m * 4] =
-                                make_uint4(h2_as_u32(h01), h2_as_u32(h23), h2_as_u32(l01), h2_as_u32(l23));
-                        }
-                } else {
-                    uint2 u[8];
-#pragma unroll
-                    for (int m = 0; m < 8; ++m)
-                        if (m < M) u[m] = __ldcg(reinterpret_cast<const uint2 *>(xrow + (size_t)m * K + kl));
-#pragma unroll
-                    for (int m = 0; m < 8; ++m)
-                        if (m < M) reinterpret_cast<uint2 *>(xs)[slot0 + m * 4] = u[m];
-                }
-            }
-            asm volatile("bar.sync 1, %0;" ::"r"(kConsumers * 32) : "memory");   // consumers only
-        }
+        stage_x<XT>(p, xs, kb0, KS, (int)threadIdx.x - 32, kConsumers * 32);
+        asm volatile("bar.sync 1, %0;" ::"r"(kConsumers * 32) : "memory");   // consumers only
 
         const int cw = warp - 1;
         const bool gval = g8 < M;

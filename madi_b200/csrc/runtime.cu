@@ -137,10 +137,13 @@ int q8_linear_impl(const madi_q8w *w, const void *x, int x_dtype, int m, const v
     if (!aligned(w->qs, 16) || !aligned(w->scales, 2)) return fail(MADI_EINVAL, "%s: qs must be 16-byte aligned", who);
 
     if (m >= kGemmMinM) {
-        if (x_dtype != MADI_F16 || y_dtype != MADI_F16)
-            return fail(MADI_EINVAL, "%s: the tensor-core path (m > 8) takes f16 x and f16 y", who);
+        const bool y32 = y_dtype == MADI_F32;
+        if (x_dtype != MADI_F16 || (y32 && epi != MADI_EPI_NONE))
+            return fail(MADI_EINVAL, "%s: the tensor-core path (m > 8) takes f16 x, and f16 y (f32 y without an "
+                                     "epilogue)", who);
         if (!aligned(x, 16)) return fail(MADI_EINVAL, "%s: x must be 16-byte aligned", who);
-        if (!aligned(y, 2) || (residual && !aligned(residual, 2))) return fail(MADI_EINVAL, "%s: misaligned y", who);
+        if (!aligned(y, y32 ? 4 : 2) || (residual && !aligned(residual, 2)))
+            return fail(MADI_EINVAL, "%s: misaligned y", who);
         GemmArgs a{};
         a.x = static_cast<const __half *>(x);
         a.qs = w->qs;
@@ -151,7 +154,7 @@ int q8_linear_impl(const madi_q8w *w, const void *x, int x_dtype, int m, const v
         a.y = static_cast<__half *>(y);
         a.M = m; a.N = N; a.K = K;
         a.dev_err = S.dev_err;
-        cudaError_t e = launch_gemm_tc(a, epi, S.num_sms, st);
+        cudaError_t e = launch_gemm_tc(a, y32 ? kEpiNoneF32 : epi, S.num_sms, st);
         if (e == cudaErrorNotSupported) return fail(MADI_EUNSUPPORTED, "%s: cuTensorMapEncodeTiled unavailable", who);
         if (e != cudaSuccess) return cuda_fail(e, who);
         return MADI_OK;

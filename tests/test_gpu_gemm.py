@@ -129,3 +129,23 @@ def test_deterministic_repeat(madi):
     y2 = q8.linear(W, X)
     torch.cuda.synchronize()
     assert torch.equal(y1, y2)
+
+
+@pytest.mark.parametrize("M,N", [(16, 6483), (64, 6483), (200, 1312), (160, 25933)])
+def test_f32_output_without_epilogue(madi, oracle, M, N):
+    """The tensor-core path with f32 y and no epilogue (a vocab-head shard over
+    more than 8 token slots): f32 accumulation written without rounding, so the
+    error against the exact result is held to 1e-4 x RMS, far inside the gate."""
+    import torch
+    from madi_b200 import q8
+    K = 1280
+    qs, sc = synth.q8_weight(N, K, M + N)
+    x = synth.activations(M, K, M + N + 1)
+    W = q8.Q8Weight(_t(qs), _t(sc))
+    y = q8.linear(W, _t(x), out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert y.dtype == torch.float32
+    y_exact = oracle.linear_f16(x, qs, sc, epi=oracle.EPI_NONE)
+    err = np.abs(y.cpu().numpy().astype(np.float64) - y_exact).max()
+    rms = np.sqrt(np.mean(y_exact ** 2))
+    assert err <= 1e-4 * rms, f"M={M} N={N}: max err {err:.3e} vs rms {rms:.3e}"
