@@ -108,6 +108,16 @@ int   madi_download(void *dst_host, const void *src_device, size_t size);
  *   suppress_list          (logits, ids u32*, n u32)                          graph_helpers.metal:97
  *   logit_filter_indirect  (logits, past_tokens, num_suppress u32, step_ptr, sample_begin u32,
  *                           no_repeat_ngram u32)                              graph_helpers.metal:109
+ * Decoder attention (head_dim 64; extents taken from the allocations):
+ *   gpu_attention          (out, q, kc f32, vc f32, pos_ptr, hdd, kvd, nkv, nh) decoder_ops.metal:85
+ *   flash_cross_attn       (out, q, kc f32, vc f32, seqlen, hdd, kvd, nkv, nh)  decoder_ops.metal:194
+ *   flash_cross_attn_f16kv (out, q, kc f16, vc f16, seqlen, hdd, kvd, nkv, nh, sc_out f32*,
+ *                           write_sc u32)                                      decoder_ops.metal:254
+ *   flash_cross_attn_f16kv_batched (same first nine; slots = grid_x / nh)      decoder_ops.metal:466
+ *   flash_cross_attn_split (part f32*, q, kc, vc, seqlen, hdd, kvd, nkv, nh, nsplit, sc_raw, write_sc)
+ *                                                                              decoder_ops.metal:338
+ *   flash_cross_attn_reduce (out, part, hdd, nsplit, sc_out, seqlen, write_sc), heads = grid_x
+ *                                                                              decoder_ops.metal:416
  * On success *out_id holds a handle for madi_dispatch. */
 int   madi_get_function(const char *name, int *out_id);
 
@@ -237,6 +247,24 @@ int madi_argmax_conf(const float *logits, int m, int vocab, uint32_t *tokens, fl
 int madi_logit_filter(float *logits, int vocab, const uint32_t *past, int past_len,
                       const uint32_t *step, uint32_t sample_begin, uint32_t no_repeat_ngram,
                       void *stream);
+
+/* ============================ decoder attention ============================== */
+
+/* Cross-attention of one query token per slot over `seqlen` encoder positions
+ * (flash_cross_attn / _f16kv / _f16kv_batched, decoder_ops.metal:191-531):
+ * q f32 [slots][heads*64]; kc, vc [slots][seqlen][kv_dim] (MADI_F16 or MADI_F32);
+ * head h reads kv head h * kv_heads / heads; out f32 [slots][heads*64];
+ * scores (nullable) f32 [slots][heads][seqlen] normalised.  head_dim 64,
+ * seqlen <= 2048; one thread-block cluster per (slot, head). */
+int madi_cross_attn(const float *q, const void *kc, const void *vc, int kv_dtype, int slots, int seqlen, int heads,
+                    int kv_heads, int kv_dim, float *out, float *scores, void *stream);
+
+/* Self-attention of one query token per slot over its cache rows 0..pos[slot]
+ * (gpu_attention, decoder_ops.metal:81-149): kc, vc [slots][max_tok][kv_dim]
+ * (MADI_F32 as the reference, or MADI_F16); pos u32 [slots] on the device
+ * (positions >= max_tok attend max_tok rows); max_tok <= 512. */
+int madi_self_attn(const float *q, const void *kc, const void *vc, int kv_dtype, const uint32_t *pos, int slots,
+                   int heads, int kv_heads, int kv_dim, int max_tok, float *out, void *stream);
 
 /* Greedy token of each of m full logit rows (tokens[s], no position), the
  * reference's argmax including its tie order (graph_helpers.metal:64-95). */

@@ -64,6 +64,8 @@ SIGNATURES = {
     "madi_argmax_rows": ([P, I, I, P, P], I),
     "madi_shard_argmax": ([P, I, I, ctypes.c_int64, U32, P, P, P], I),
     "madi_merge_shard_argmax": ([P, P, I, I, P, P], I),
+    "madi_cross_attn": ([P, P, P, I, I, I, I, I, I, P, P, P], I),
+    "madi_self_attn": ([P, P, P, I, P, I, I, I, I, I, P, P], I),
 }
 
 _lib = None

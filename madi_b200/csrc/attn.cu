@@ -1,0 +1,407 @@
+// attn.cu -- decoder attention beside the Q8 projections (decoder_ops.metal:81-530).
+//
+//   gpu_attention                   self-attention of one query token per slot over
+//                                   the f32 KV cache rows 0..pos (pos read on the
+//                                   device)                                        (:81-149)
+//   flash_cross_attn[_f16kv]        cross-attention of one query token per slot over
+//                                   `seqlen` encoder positions, f32 or f16 K/V,
+//                                   optional normalised scores                     (:191-325)
+//   flash_cross_attn_f16kv_batched  the same for B slots, each with its own K/V    (:459-531)
+//   flash_cross_attn_split/_reduce  the two-pass form with caller-owned partials   (:327-457)
+//
+// Scores are q.k * rsqrt(head_dim); softmax as exp2((s - max) * log2 e); head_dim 64.
+//
+// B200 layout of the fused cross-attention: one thread-block cluster of `ns` CTAs
+// (<= 8) per (slot, head).  CTA c takes keys [c*csz, (c+1)*csz), computes its
+// partial flash result -- local max m, exp-sum s and unnormalised o = sum e*v --
+// and pushes (m, s, o) into rank 0's shared memory; rank 0 recombines them by
+// log-sum-exp (the reference's flash_cross_attn_reduce arithmetic) and writes the
+// output.  No global scratch and one launch, with (slots x heads x ns) CTAs
+// streaming K/V in parallel.  Key reads are coalesced: a half-warp reads one key
+// row's 64 elements (16 lanes x 4), a warp reads one value row (32 lanes x 2).
+// The cross-attention K/V is the decode step's largest read at 8 slots (2 x 1500
+// x 1280 f16 per slot per layer), so the kernel is HBM-bound.
+#include <cooperative_groups.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace cg = cooperative_groups;
+
+namespace madi {
+namespace {
+
+constexpr int kHd = 64;
+constexpr int kThr = 256;
+constexpr float kLog2e = 1.4426950408889634f;
+
+MADI_DEV float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+MADI_DEV float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+// Block-wide max / sum over 256 threads, result in every thread.  `s8` holds
+// the 8 warp partials; the trailing barrier lets the caller reuse it.
+MADI_DEV float block_max(float v, float *s8) {
+    v = warp_max(v);
+    if ((threadIdx.x & 31) == 0) s8[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float r = s8[0];
+#pragma unroll
+    for (int i = 1; i < 8; ++i) r = fmaxf(r, s8[i]);
+    __syncthreads();
+    return r;
+}
+MADI_DEV float block_sum(float v, float *s8) {
+    v = warp_sum(v);
+    if ((threadIdx.x & 31) == 0) s8[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float r = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) r += s8[i];
+    __syncthreads();
+    return r;
+}
+
+template <typename T> MADI_DEV float4 ld4(const T *p);
+template <> MADI_DEV float4 ld4<float>(const float *p) { return *reinterpret_cast<const float4 *>(p); }
+template <> MADI_DEV float4 ld4<__half>(const __half *p) {
+    const uint2 u = *reinterpret_cast<const uint2 *>(p);
+    const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&u.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&u.y));
+    return make_float4(a.x, a.y, b.x, b.y);
+}
+template <typename T> MADI_DEV float2 ld2(const T *p);
+template <> MADI_DEV float2 ld2<float>(const float *p) { return *reinterpret_cast<const float2 *>(p); }
+template <> MADI_DEV float2 ld2<__half>(const __half *p) {
+    return __half22float2(*reinterpret_cast<const __half2 *>(p));
+}
+
+// raw[k] = q_h . K[k] * rsqrt(64) for k in [0, n); a half-warp per key.
+template <typename KV>
+MADI_DEV void scores_of(const float *qh, const KV *kb, int kvd, int n, float *raw) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int hw = lane >> 4, li = lane & 15;
+    const float4 qv = make_float4(qh[4 * li], qh[4 * li + 1], qh[4 * li + 2], qh[4 * li + 3]);
+    const float rsq = rsqrtf((float)kHd);
+    for (int k0 = warp * 2; k0 < n; k0 += 16) {      // warp-uniform bound: all lanes shuffle
+        const int k = k0 + hw;
+        float d = 0.f;
+        if (k < n) {
+            const float4 kv = ld4(kb + (size_t)k * kvd + 4 * li);
+            d = qv.x * kv.x + qv.y * kv.y + qv.z * kv.z + qv.w * kv.w;
+        }
+        d += __shfl_xor_sync(0xffffffffu, d, 8);
+        d += __shfl_xor_sync(0xffffffffu, d, 4);
+        d += __shfl_xor_sync(0xffffffffu, d, 2);
+        d += __shfl_xor_sync(0xffffffffu, d, 1);
+        if (li == 0 && k < n) raw[k] = d * rsq;
+    }
+}
+
+// o[d] = sum_k w[k] * V[k][d] for d < 64, returned in threads 0..63 (a warp per
+// key, lanes over dims; the 8 warp sums are added in warp order).
+template <typename KV>
+MADI_DEV float pv_of(const float *w, const KV *vb, int kvd, int n, float (*red)[kHd]) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float a0 = 0.f, a1 = 0.f;
+    for (int k = warp; k < n; k += 8) {
+        const float2 v = ld2(vb + (size_t)k * kvd + 2 * lane);
+        a0 = fmaf(w[k], v.x, a0);
+        a1 = fmaf(w[k], v.y, a1);
+    }
+    red[warp][2 * lane] = a0;
+    red[warp][2 * lane + 1] = a1;
+    __syncthreads();
+    float o = 0.f;
+    if (threadIdx.x < kHd) {
+#pragma unroll
+        for (int w8 = 0; w8 < 8; ++w8) o += red[w8][threadIdx.x];
+    }
+    return o;
+}
+
+// ---------------------------------------------------------------- cross-attention
+// grid (ns, heads, slots), cluster (ns, 1, 1) when ns > 1.  kc / vc: [slot][seqlen][kvd].
+template <typename KV, bool kScores>
+__global__ void __launch_bounds__(kThr) cross_attn_kernel(float *__restrict__ out, const float *__restrict__ q,
+                                                          const KV *__restrict__ kc, const KV *__restrict__ vc,
+                                                          float *__restrict__ sc_out, int seqlen, int kvd, int nkv,
+                                                          int nh, int ns) {
+    __shared__ float qh[kHd];
+    __shared__ float raw[kAttnMaxChunk];
+    __shared__ float ew[kAttnMaxChunk];
+    __shared__ float s8[8];
+    __shared__ float red[8][kHd];
+    __shared__ float part[8][2 + kHd];          // rank 0: the cluster's partials
+    __shared__ float stats[2];                  // global (max, 1/sum), for the scores
+    const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    const int tid = threadIdx.x;
+    const int D = nh * kHd;
+    const int kvh = h * nkv / nh;
+    const int csz = (seqlen + ns - 1) / ns;
+    const int t0 = c * csz;
+    const int n = t0 < seqlen ? min(csz, seqlen - t0) : 0;
+    const size_t slot_off = (size_t)b * seqlen * kvd;
+    const KV *kb = kc + slot_off + (size_t)min(t0, seqlen) * kvd + kvh * kHd;
+    const KV *vb = vc + slot_off + (size_t)min(t0, seqlen) * kvd + kvh * kHd;
+    // every CTA of the cluster runs before rank 0's shared memory is written
+    if (ns > 1) asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
+
+    if (tid < kHd) qh[tid] = q[(size_t)b * D + h * kHd + tid];
+    __syncthreads();
+    scores_of(qh, kb, kvd, n, raw);
+    __syncthreads();
+    float lm = -INFINITY;
+    for (int t = tid; t < n; t += kThr) lm = fmaxf(lm, raw[t]);
+    const float mx = block_max(lm, s8);
+    float ls = 0.f;
+    for (int t = tid; t < n; t += kThr) {
+        const float e = exp2f((raw[t] - mx) * kLog2e);
+        ew[t] = e;
+        ls += e;
+    }
+    const float ssum = block_sum(ls, s8);      // its barriers also publish ew[]
+    const float o = pv_of(ew, vb, kvd, n, red);
+
+    float *p0 = &part[0][0];
+    if (ns > 1) {
+        asm volatile("barrier.cluster.wait;" ::: "memory");
+        p0 = cg::this_cluster().map_shared_rank(&part[0][0], 0);
+    }
+    if (tid < kHd) p0[c * (2 + kHd) + 2 + tid] = o;
+    if (tid == 0) {
+        p0[c * (2 + kHd)] = mx;
+        p0[c * (2 + kHd) + 1] = ssum;
+    }
+    if (ns > 1) {
+        asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+    } else {
+        __syncthreads();
+    }
+    if (c == 0) {
+        // log-sum-exp recombination (flash_cross_attn_reduce, decoder_ops.metal:416-457)
+        float gm = -INFINITY;
+        for (int r = 0; r < ns; ++r) gm = fmaxf(gm, part[r][0]);
+        float gs = 0.f;
+        for (int r = 0; r < ns; ++r)
+            if (part[r][0] > -INFINITY) gs += part[r][1] * exp2f((part[r][0] - gm) * kLog2e);
+        const float inv = 1.0f / gs;
+        if (tid < kHd) {
+            float acc = 0.f;
+            for (int r = 0; r < ns; ++r)
+                if (part[r][0] > -INFINITY) acc += part[r][2 + tid] * exp2f((part[r][0] - gm) * kLog2e);
+            out[(size_t)b * D + h * kHd + tid] = acc * inv;
+        }
+        if constexpr (kScores) {
+            if (tid < ns) {
+                float *st = ns > 1 ? cg::this_cluster().map_shared_rank(stats, tid) : stats;
+                st[0] = gm;
+                st[1] = inv;
+            }
+        }
+    }
+    if constexpr (kScores) {
+        if (ns > 1) asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+        else __syncthreads();
+        const float gm = stats[0], inv = stats[1];
+        float *sr = sc_out + ((size_t)b * nh + h) * seqlen + t0;
+        for (int t = tid; t < n; t += kThr) sr[t] = exp2f((raw[t] - gm) * kLog2e) * inv;
+    }
+}
+
+// Two-pass form with caller-owned partials part[head][nsplit][2 + 64] (m, s, o):
+// pass 1, grid (nsplit, heads); raw scores to sc_raw[head][seqlen] when asked.
+template <typename KV>
+__global__ void __launch_bounds__(kThr) cross_attn_part_kernel(float *__restrict__ part, const float *__restrict__ q,
+                                                               const KV *__restrict__ kc, const KV *__restrict__ vc,
+                                                               float *__restrict__ sc_raw, int write_sc, int seqlen,
+                                                               int kvd, int nkv, int nh, int nsplit) {
+    __shared__ float qh[kHd];
+    __shared__ float raw[kAttnMaxChunk];
+    __shared__ float s8[8];
+    __shared__ float red[8][kHd];
+    const int c = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+    const int kvh = h * nkv / nh;
+    const int csz = (seqlen + nsplit - 1) / nsplit;
+    const int t0 = c * csz;
+    const int n = t0 < seqlen ? min(csz, seqlen - t0) : 0;
+    float *my = part + ((size_t)h * nsplit + c) * (2 + kHd);
+    if (n == 0) {                               // empty tail chunk
+        if (tid == 0) { my[0] = -INFINITY; my[1] = 0.f; }
+        if (tid < kHd) my[2 + tid] = 0.f;
+        return;
+    }
+    const KV *kb = kc + (size_t)t0 * kvd + kvh * kHd;
+    const KV *vb = vc + (size_t)t0 * kvd + kvh * kHd;
+    if (tid < kHd) qh[tid] = q[h * kHd + tid];
+    __syncthreads();
+    scores_of(qh, kb, kvd, n, raw);
+    __syncthreads();
+    if (write_sc)
+        for (int t = tid; t < n; t += kThr) sc_raw[(size_t)h * seqlen + t0 + t] = raw[t];
+    float lm = -INFINITY;
+    for (int t = tid; t < n; t += kThr) lm = fmaxf(lm, raw[t]);
+    const float mx = block_max(lm, s8);
+    float ls = 0.f;
+    for (int t = tid; t < n; t += kThr) {
+        const float e = exp2f((raw[t] - mx) * kLog2e);
+        raw[t] = e;
+        ls += e;
+    }
+    const float ssum = block_sum(ls, s8);
+    const float o = pv_of(raw, vb, kvd, n, red);
+    if (tid < kHd) my[2 + tid] = o;
+    if (tid == 0) { my[0] = mx; my[1] = ssum; }
+}
+
+// pass 2, grid (heads): recombine and normalise the raw scores in place.
+__global__ void __launch_bounds__(kThr) cross_attn_reduce_kernel(float *__restrict__ out, const float *__restrict__ part,
+                                                                 int nsplit, float *__restrict__ sc, int seqlen,
+                                                                 int write_sc) {
+    const int h = blockIdx.x, tid = threadIdx.x;
+    const float *hp = part + (size_t)h * nsplit * (2 + kHd);
+    float gm = -INFINITY;
+    for (int c = 0; c < nsplit; ++c) gm = fmaxf(gm, hp[c * (2 + kHd)]);
+    float gs = 0.f;
+    for (int c = 0; c < nsplit; ++c) {
+        const float m = hp[c * (2 + kHd)];
+        if (m > -INFINITY) gs += hp[c * (2 + kHd) + 1] * exp2f((m - gm) * kLog2e);
+    }
+    const float inv = 1.0f / gs;
+    if (tid < kHd) {
+        float acc = 0.f;
+        for (int c = 0; c < nsplit; ++c) {
+            const float m = hp[c * (2 + kHd)];
+            if (m > -INFINITY) acc += hp[c * (2 + kHd) + 2 + tid] * exp2f((m - gm) * kLog2e);
+        }
+        out[h * kHd + tid] = acc * inv;
+    }
+    if (write_sc) {
+        float *sr = sc + (size_t)h * seqlen;
+        for (int t = tid; t < seqlen; t += kThr) sr[t] = exp2f((sr[t] - gm) * kLog2e) * inv;
+    }
+}
+
+// ---------------------------------------------------------------- self-attention
+// grid (heads, slots): keys 0..pos[slot] (bounded by max_tok) of the slot's cache
+// rows kc[slot * cache_stride + t * kvd + ...].
+template <typename KV>
+__global__ void __launch_bounds__(kThr) self_attn_kernel(float *__restrict__ out, const float *__restrict__ q,
+                                                         const KV *__restrict__ kc, const KV *__restrict__ vc,
+                                                         const uint32_t *__restrict__ pos, int kvd, int nkv, int nh,
+                                                         long long cache_stride, int max_tok) {
+    __shared__ float qh[kHd];
+    __shared__ float sc[kAttnMaxTok];
+    __shared__ float s8[8];
+    __shared__ float red[8][kHd];
+    const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
+    const int D = nh * kHd;
+    const int kvh = h * nkv / nh;
+    const uint32_t p = pos[b];
+    const int n = p < (uint32_t)max_tok ? (int)p + 1 : max_tok;
+    const KV *kb = kc + (size_t)b * cache_stride + kvh * kHd;
+    const KV *vb = vc + (size_t)b * cache_stride + kvh * kHd;
+    if (tid < kHd) qh[tid] = q[(size_t)b * D + h * kHd + tid];
+    __syncthreads();
+    scores_of(qh, kb, kvd, n, sc);
+    __syncthreads();
+    float lm = -INFINITY;
+    for (int t = tid; t < n; t += kThr) lm = fmaxf(lm, sc[t]);
+    const float mx = block_max(lm, s8);
+    float ls = 0.f;
+    for (int t = tid; t < n; t += kThr) {
+        const float e = exp2f((sc[t] - mx) * kLog2e);
+        sc[t] = e;
+        ls += e;
+    }
+    const float inv = 1.0f / block_sum(ls, s8);
+    for (int t = tid; t < n; t += kThr) sc[t] *= inv;     // normalised before P.V, as the reference
+    __syncthreads();
+    const float o = pv_of(sc, vb, kvd, n, red);
+    if (tid < kHd) out[(size_t)b * D + h * kHd + tid] = o;
+}
+
+template <typename KV, bool kScores>
+cudaError_t launch_cross_t(float *out, const float *q, const KV *kc, const KV *vc, float *sc, int slots, int seqlen,
+                           int kvd, int nkv, int nh, int ns, cudaStream_t st) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(ns, nh, slots);
+    cfg.blockDim = dim3(kThr);
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = ns;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = ns > 1 ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, cross_attn_kernel<KV, kScores>, out, q, kc, vc, sc, seqlen, kvd, nkv, nh, ns);
+}
+
+}  // namespace
+
+int attn_cluster_size(int seqlen) {
+    int ns = 1;
+    while (ns < 8 && (seqlen + ns - 1) / ns > 192) ns *= 2;
+    return (seqlen + ns - 1) / ns <= kAttnMaxChunk ? ns : 0;
+}
+
+cudaError_t launch_cross_attn(float *out, const float *q, const void *kc, const void *vc, bool kv_f16, float *scores,
+                              int slots, int seqlen, int kvd, int nkv, int nh, cudaStream_t st) {
+    const int ns = attn_cluster_size(seqlen);
+    if (ns == 0) return cudaErrorInvalidValue;
+    if (kv_f16) {
+        const __half *k = static_cast<const __half *>(kc), *v = static_cast<const __half *>(vc);
+        return scores ? launch_cross_t<__half, true>(out, q, k, v, scores, slots, seqlen, kvd, nkv, nh, ns, st)
+                      : launch_cross_t<__half, false>(out, q, k, v, nullptr, slots, seqlen, kvd, nkv, nh, ns, st);
+    }
+    const float *k = static_cast<const float *>(kc), *v = static_cast<const float *>(vc);
+    return scores ? launch_cross_t<float, true>(out, q, k, v, scores, slots, seqlen, kvd, nkv, nh, ns, st)
+                  : launch_cross_t<float, false>(out, q, k, v, nullptr, slots, seqlen, kvd, nkv, nh, ns, st);
+}
+
+cudaError_t launch_cross_attn_part(float *part, const float *q, const void *kc, const void *vc, bool kv_f16,
+                                   float *sc_raw, int write_sc, int seqlen, int kvd, int nkv, int nh, int nsplit,
+                                   cudaStream_t st) {
+    const dim3 grid(nsplit, nh);
+    if (kv_f16)
+        cross_attn_part_kernel<__half><<<grid, kThr, 0, st>>>(part, q, static_cast<const __half *>(kc),
+                                                              static_cast<const __half *>(vc), sc_raw, write_sc,
+                                                              seqlen, kvd, nkv, nh, nsplit);
+    else
+        cross_attn_part_kernel<float><<<grid, kThr, 0, st>>>(part, q, static_cast<const float *>(kc),
+                                                             static_cast<const float *>(vc), sc_raw, write_sc, seqlen,
+                                                             kvd, nkv, nh, nsplit);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_cross_attn_reduce(float *out, const float *part, int nsplit, float *sc, int seqlen, int write_sc,
+                                     int nh, cudaStream_t st) {
+    cross_attn_reduce_kernel<<<nh, kThr, 0, st>>>(out, part, nsplit, sc, seqlen, write_sc);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_self_attn(float *out, const float *q, const void *kc, const void *vc, bool kv_f16,
+                             const uint32_t *pos, int slots, int kvd, int nkv, int nh, long long cache_stride,
+                             int max_tok, cudaStream_t st) {
+    const dim3 grid(nh, slots);
+    if (kv_f16)
+        self_attn_kernel<__half><<<grid, kThr, 0, st>>>(out, q, static_cast<const __half *>(kc),
+                                                        static_cast<const __half *>(vc), pos, kvd, nkv, nh,
+                                                        cache_stride, max_tok);
+    else
+        self_attn_kernel<float><<<grid, kThr, 0, st>>>(out, q, static_cast<const float *>(kc),
+                                                       static_cast<const float *>(vc), pos, kvd, nkv, nh,
+                                                       cache_stride, max_tok);
+    return cudaGetLastError();
+}
+
+}  // namespace madi

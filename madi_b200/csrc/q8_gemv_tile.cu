@@ -223,7 +223,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     constexpr bool kSplit = sizeof(XT) == 4;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    const int M = p.M, K = p.K, N = p.N;
+    const int M = p.M, N = p.N;
     const int cs = plan.cs, KS = plan.kslice, stages = plan.stages, clusters = plan.clusters;
     const int nkbs = KS >> 5;                                   // 32-blocks in this CTA's slice
     const int rank = (int)(blockIdx.x % (unsigned)cs);          // cluster rank (clusters run along x)

@@ -355,6 +355,81 @@ int h_logit_filter(const ArgVal *a, uint32_t, cudaStream_t st) {
     return e == cudaSuccess ? MADI_OK : cuda_fail(e, "logit_filter_indirect");
 }
 
+// ---- decoder attention by name (decoder_ops.metal:81-531); head_dim 64, K/V rows
+// of kvd elements, head h reading the kv head h * nkv / nh.  Buffer extents come
+// from the allocations (the reference signatures carry none) and bound every read.
+int attn_shape_ok(const char *who, uint32_t hdd, uint32_t kvd, uint32_t nkv, uint32_t nh) {
+    if (hdd != 64) return fail(MADI_EINVAL, "%s: head_dim %u (64 supported)", who, hdd);
+    if (nh == 0 || nh > 1024 || nkv == 0 || nkv > nh || (size_t)kvd < (size_t)nkv * 64 || kvd % 4)
+        return fail(MADI_EINVAL, "%s: heads %u, kv heads %u, kv_dim %u", who, nh, nkv, kvd);
+    return MADI_OK;
+}
+bool extent_ok(const void *p, size_t bytes) { return p && aligned(p, 16) && bytes_after(p) >= bytes; }
+
+// gpu_attention(out, q, kc, vc, pos_ptr, hdd, kvd, nkv, nh): f32 cache, one slot
+int h_self_attn(const ArgVal *a, uint32_t, cudaStream_t st) {
+    const uint32_t hdd = a[5].u, kvd = a[6].u, nkv = a[7].u, nh = a[8].u;
+    if (int rc = attn_shape_ok("gpu_attention", hdd, kvd, nkv, nh)) return rc;
+    const size_t row = (size_t)kvd * 4, qb = (size_t)nh * 64 * 4;
+    const size_t rows = std::min(bytes_after(a[2].p), bytes_after(a[3].p)) / row;
+    if (!rows || !extent_ok(a[0].p, qb) || !extent_ok(a[1].p, qb) || !aligned(a[2].p, 16) || !aligned(a[3].p, 16))
+        return fail(MADI_EINVAL, "gpu_attention: buffer extents");
+    const int max_tok = (int)std::min<size_t>(rows, kAttnMaxTok);
+    cudaError_t e = launch_self_attn((float *)a[0].p, static_cast<const float *>(a[1].p), a[2].p, a[3].p, false,
+                                     static_cast<const uint32_t *>(a[4].p), 1, (int)kvd, (int)nkv, (int)nh, 0, max_tok,
+                                     st);
+    return e == cudaSuccess ? MADI_OK : cuda_fail(e, "gpu_attention");
+}
+// flash_cross_attn (f32 K/V) / flash_cross_attn_f16kv (+ sc_out, write_sc) /
+// flash_cross_attn_f16kv_batched (slots = grid x / nh)
+template <bool kF16, int kMode>   // kMode 0: one slot; 1: with scores; 2: batched
+int h_cross_attn(const ArgVal *a, uint32_t gx, cudaStream_t st) {
+    const char *who = kMode == 2 ? "flash_cross_attn_f16kv_batched" : kF16 ? "flash_cross_attn_f16kv" : "flash_cross_attn";
+    const uint32_t seqlen = a[4].u, hdd = a[5].u, kvd = a[6].u, nkv = a[7].u, nh = a[8].u;
+    if (int rc = attn_shape_ok(who, hdd, kvd, nkv, nh)) return rc;
+    if (seqlen == 0 || attn_cluster_size((int)seqlen) == 0) return fail(MADI_EINVAL, "%s: seqlen %u", who, seqlen);
+    const uint32_t slots = kMode == 2 ? gx / nh : 1;
+    if (slots == 0 || (kMode == 2 && gx % nh)) return fail(MADI_EINVAL, "%s: grid x %u is not slots x %u heads", who, gx, nh);
+    const size_t kvb = (size_t)slots * seqlen * kvd * (kF16 ? 2 : 4), qb = (size_t)slots * nh * 64 * 4;
+    if (!extent_ok(a[0].p, qb) || !extent_ok(a[1].p, qb) || !extent_ok(a[2].p, kvb) || !extent_ok(a[3].p, kvb))
+        return fail(MADI_EINVAL, "%s: buffer extents", who);
+    float *scores = nullptr;
+    if (kMode == 1 && a[10].u) {
+        if (!extent_ok(a[9].p, (size_t)nh * seqlen * 4)) return fail(MADI_EINVAL, "%s: sc_out extent", who);
+        scores = (float *)a[9].p;
+    }
+    cudaError_t e = launch_cross_attn((float *)a[0].p, static_cast<const float *>(a[1].p), a[2].p, a[3].p, kF16, scores,
+                                      (int)slots, (int)seqlen, (int)kvd, (int)nkv, (int)nh, st);
+    return e == cudaSuccess ? MADI_OK : cuda_fail(e, who);
+}
+// flash_cross_attn_split(part, q, kc, vc, seqlen, hdd, kvd, nkv, nh, nsplit, sc_raw, write_sc), grid nh * nsplit
+int h_cross_split(const ArgVal *a, uint32_t, cudaStream_t st) {
+    const uint32_t seqlen = a[4].u, hdd = a[5].u, kvd = a[6].u, nkv = a[7].u, nh = a[8].u, nsplit = a[9].u;
+    if (int rc = attn_shape_ok("flash_cross_attn_split", hdd, kvd, nkv, nh)) return rc;
+    if (seqlen == 0 || nsplit == 0 || nsplit > 1024 || (seqlen + nsplit - 1) / nsplit > (uint32_t)kAttnMaxChunk)
+        return fail(MADI_EINVAL, "flash_cross_attn_split: seqlen %u over %u splits", seqlen, nsplit);
+    const size_t kvb = (size_t)seqlen * kvd * 2;
+    if (!extent_ok(a[0].p, (size_t)nh * nsplit * 66 * 4) || !extent_ok(a[1].p, (size_t)nh * 256) ||
+        !extent_ok(a[2].p, kvb) || !extent_ok(a[3].p, kvb) || (a[11].u && !extent_ok(a[10].p, (size_t)nh * seqlen * 4)))
+        return fail(MADI_EINVAL, "flash_cross_attn_split: buffer extents");
+    cudaError_t e = launch_cross_attn_part((float *)a[0].p, static_cast<const float *>(a[1].p), a[2].p, a[3].p, true,
+                                           (float *)a[10].p, (int)(a[11].u != 0), (int)seqlen, (int)kvd, (int)nkv,
+                                           (int)nh, (int)nsplit, st);
+    return e == cudaSuccess ? MADI_OK : cuda_fail(e, "flash_cross_attn_split");
+}
+// flash_cross_attn_reduce(out, part, hdd, nsplit, sc_out, seqlen, write_sc), heads = grid x
+int h_cross_reduce(const ArgVal *a, uint32_t gx, cudaStream_t st) {
+    const uint32_t hdd = a[2].u, nsplit = a[3].u, seqlen = a[5].u, nh = gx;
+    if (hdd != 64 || nh == 0 || nh > 1024 || nsplit == 0 || nsplit > 1024)
+        return fail(MADI_EINVAL, "flash_cross_attn_reduce: head_dim %u, heads %u, splits %u", hdd, nh, nsplit);
+    if (!extent_ok(a[0].p, (size_t)nh * 256) || !extent_ok(a[1].p, (size_t)nh * nsplit * 66 * 4) ||
+        (a[6].u && !extent_ok(a[4].p, (size_t)nh * seqlen * 4)))
+        return fail(MADI_EINVAL, "flash_cross_attn_reduce: buffer extents");
+    cudaError_t e = launch_cross_attn_reduce((float *)a[0].p, static_cast<const float *>(a[1].p), (int)nsplit,
+                                             (float *)a[4].p, (int)seqlen, (int)(a[6].u != 0), (int)nh, st);
+    return e == cudaSuccess ? MADI_OK : cuda_fail(e, "flash_cross_attn_reduce");
+}
+
 // bias_res_ln_f16(X, MO, bias, Y, gamma, beta, D, eps), rows = grid x   encoder_ops.metal:333-364
 int h_bias_res_ln(const ArgVal *a, uint32_t gx, cudaStream_t st) {
     return madi_bias_res_ln_f16((float *)a[0].p, static_cast<const uint16_t *>(a[1].p), static_cast<const float *>(a[2].p),
@@ -390,6 +465,15 @@ const std::vector<Op> &ops() {
         {"argmax_conf", {kPtr, kPtr, kPtr, kPtr, kU32}, h_argmax<true>},
         {"suppress_list", {kPtr, kPtr, kU32}, h_suppress},
         {"logit_filter_indirect", {kPtr, kPtr, kU32, kPtr, kU32, kU32}, h_logit_filter},
+        {"gpu_attention", {kPtr, kPtr, kPtr, kPtr, kPtr, kU32, kU32, kU32, kU32}, h_self_attn},
+        {"flash_cross_attn", {kPtr, kPtr, kPtr, kPtr, kU32, kU32, kU32, kU32, kU32}, h_cross_attn<false, 0>},
+        {"flash_cross_attn_f16kv", {kPtr, kPtr, kPtr, kPtr, kU32, kU32, kU32, kU32, kU32, kPtr, kU32},
+         h_cross_attn<true, 1>},
+        {"flash_cross_attn_f16kv_batched", {kPtr, kPtr, kPtr, kPtr, kU32, kU32, kU32, kU32, kU32},
+         h_cross_attn<true, 2>},
+        {"flash_cross_attn_split", {kPtr, kPtr, kPtr, kPtr, kU32, kU32, kU32, kU32, kU32, kU32, kPtr, kU32},
+         h_cross_split},
+        {"flash_cross_attn_reduce", {kPtr, kPtr, kU32, kU32, kPtr, kU32, kU32}, h_cross_reduce},
     };
     return table;
 }
@@ -764,6 +848,36 @@ int madi_merge_shard_argmax(const float *vals, const uint32_t *idx, int world, i
         return fail(MADI_EINVAL, "madi_merge_shard_argmax: bad argument");
     cudaError_t e = launch_merge_argmax(vals, idx, world, m, tokens, pick_stream(stream));
     return e == cudaSuccess ? MADI_OK : cuda_fail(e, "madi_merge_shard_argmax");
+}
+
+int madi_cross_attn(const float *q, const void *kc, const void *vc, int kv_dtype, int slots, int seqlen, int heads,
+                    int kv_heads, int kv_dim, float *out, float *scores, void *stream) {
+    if (!S.ready) return fail(MADI_ENOINIT, "madi_cross_attn: not initialised");
+    if (!q || !kc || !vc || !out || (kv_dtype != MADI_F16 && kv_dtype != MADI_F32))
+        return fail(MADI_EINVAL, "madi_cross_attn: bad argument");
+    if (int rc = attn_shape_ok("madi_cross_attn", 64, (uint32_t)kv_dim, (uint32_t)kv_heads, (uint32_t)heads)) return rc;
+    if (slots <= 0 || slots > 65535 || seqlen <= 0 || attn_cluster_size(seqlen) == 0)
+        return fail(MADI_EINVAL, "madi_cross_attn: slots %d, seqlen %d (<= %d)", slots, seqlen, 8 * kAttnMaxChunk);
+    if (!aligned(q, 16) || !aligned(kc, 16) || !aligned(vc, 16) || !aligned(out, 16))
+        return fail(MADI_EINVAL, "madi_cross_attn: buffers must be 16-byte aligned");
+    cudaError_t e = launch_cross_attn(out, q, kc, vc, kv_dtype == MADI_F16, scores, slots, seqlen, kv_dim, kv_heads,
+                                      heads, pick_stream(stream));
+    return e == cudaSuccess ? MADI_OK : cuda_fail(e, "madi_cross_attn");
+}
+
+int madi_self_attn(const float *q, const void *kc, const void *vc, int kv_dtype, const uint32_t *pos, int slots,
+                   int heads, int kv_heads, int kv_dim, int max_tok, float *out, void *stream) {
+    if (!S.ready) return fail(MADI_ENOINIT, "madi_self_attn: not initialised");
+    if (!q || !kc || !vc || !pos || !out || (kv_dtype != MADI_F16 && kv_dtype != MADI_F32))
+        return fail(MADI_EINVAL, "madi_self_attn: bad argument");
+    if (int rc = attn_shape_ok("madi_self_attn", 64, (uint32_t)kv_dim, (uint32_t)kv_heads, (uint32_t)heads)) return rc;
+    if (slots <= 0 || slots > 65535 || max_tok <= 0 || max_tok > kAttnMaxTok)
+        return fail(MADI_EINVAL, "madi_self_attn: slots %d, max_tok %d (<= %d)", slots, max_tok, kAttnMaxTok);
+    if (!aligned(q, 16) || !aligned(kc, 16) || !aligned(vc, 16) || !aligned(out, 16))
+        return fail(MADI_EINVAL, "madi_self_attn: buffers must be 16-byte aligned");
+    cudaError_t e = launch_self_attn(out, q, kc, vc, kv_dtype == MADI_F16, pos, slots, kv_dim, kv_heads, heads,
+                                     (long long)max_tok * kv_dim, max_tok, pick_stream(stream));
+    return e == cudaSuccess ? MADI_OK : cuda_fail(e, "madi_self_attn");
 }
 
 int madi_step_advance(uint32_t *pos, int m, void *stream) {

@@ -208,3 +208,45 @@ def bias_res_ln(x, mo=None, bias=None, gamma=None, beta=None, eps=1e-5):
                                None if bias is None else _p(_c(bias, np.float32)),
                                _p(_c(gamma, np.float32)), _p(_c(beta, np.float32)), rows, d, float(eps), _p(y))
     return x2, y
+
+
+def _head_kv(kc, vc, h, nh, nkv, hdd):
+    kvh = h * nkv // nh
+    return kc[..., kvh * hdd:(kvh + 1) * hdd], vc[..., kvh * hdd:(kvh + 1) * hdd]
+
+
+def cross_attn(q, kc, vc, nh, nkv=None, hdd=64):
+    """flash_cross_attn / _f16kv / _f16kv_batched (decoder_ops.metal:194-325, 459-531)
+    restated in f64: per slot and head, s_t = q_h . k_t * rsqrt(hdd), p = softmax(s)
+    (the reference's exp2((s - max) * log2 e) / sum), out_h = sum_t p_t v_t.
+    q [slots][nh*hdd]; kc, vc [slots][seqlen][kvd].  Returns (out [slots][nh*hdd],
+    scores [slots][nh][seqlen])."""
+    nkv = nkv or nh
+    q = np.asarray(q, np.float64)
+    kc = np.asarray(kc, np.float64)
+    vc = np.asarray(vc, np.float64)
+    slots, seqlen, _ = kc.shape
+    out = np.empty((slots, nh * hdd))
+    sc = np.empty((slots, nh, seqlen))
+    for h in range(nh):
+        K, V = _head_kv(kc, vc, h, nh, nkv, hdd)
+        s = np.einsum("bd,btd->bt", q[:, h * hdd:(h + 1) * hdd], K) / np.sqrt(hdd)
+        e = np.exp(s - s.max(axis=1, keepdims=True))
+        p = e / e.sum(axis=1, keepdims=True)
+        sc[:, h] = p
+        out[:, h * hdd:(h + 1) * hdd] = np.einsum("bt,btd->bd", p, V)
+    return out, sc
+
+
+def self_attn(q, kc, vc, pos, nh, nkv=None, hdd=64):
+    """gpu_attention (decoder_ops.metal:81-149) restated in f64: slot b attends its
+    cache rows 0..pos[b] (at most the cache length).  kc, vc [slots][max_tok][kvd]."""
+    nkv = nkv or nh
+    kc = np.asarray(kc, np.float64)
+    vc = np.asarray(vc, np.float64)
+    out = np.empty((kc.shape[0], nh * hdd))
+    for b, p in enumerate(np.asarray(pos).tolist()):
+        n = min(int(p) + 1, kc.shape[1])
+        o, _ = cross_attn(np.asarray(q, np.float64)[b:b + 1], kc[b:b + 1, :n], vc[b:b + 1, :n], nh, nkv, hdd)
+        out[b] = o[0]
+    return out
