@@ -568,6 +568,51 @@ def decode_leg(args, world, rank, dev, stream, peaks):
         del g, Ws
         torch.cuda.empty_cache()
 
+    # ---- decoder attention at Md slots: cross-attention over 1500 encoder positions
+    # (f16 K/V per slot, as the reference's decoder keeps them) and self-attention
+    # over a full 448-row f32 KV cache; distinct K/V copies (> L2 in all) launched
+    # back to back in one graph; bytes = K + V + q + out
+    from madi_b200 import attn as attn_ops
+    attention = {}
+    H = D // 64
+    for kind, rows, kv_dt, esz in (("cross", 1500, torch.float16, 2), ("self", 448, torch.float32, 4)):
+        nbytes = 2 * Md * rows * D * esz + 2 * Md * D * 4
+        copies = max(3, int(300e6 // nbytes) + 1)
+        KV = [(torch.randn((Md, rows, D), device=dev, generator=gen).to(kv_dt),
+               torch.randn((Md, rows, D), device=dev, generator=gen).to(kv_dt)) for _ in range(copies)]
+        qa = torch.randn((Md, D), device=dev, generator=gen) * 0.5
+        oa = torch.empty_like(qa)
+        posa = torch.full((Md,), rows - 1, dtype=torch.int32, device=dev)
+
+        def run_attn():
+            for kc_, vc_ in KV:
+                if kind == "cross":
+                    attn_ops.cross_attn(qa, kc_, vc_, H, out=oa, stream=stream)
+                else:
+                    attn_ops.self_attn(qa, kc_, vc_, posa, H, out=oa, stream=stream)
+        with torch.cuda.stream(stream):
+            run_attn()
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream, capture_error_mode="thread_local"):
+                run_attn()
+            g.replay()
+            torch.cuda.synchronize()
+            best = None
+            for _ in range(3):
+                a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a0.record(stream)
+                g.replay()
+                a1.record(stream)
+                a1.synchronize()
+                us = a0.elapsed_time(a1) * 1e3 / copies
+                best = us if best is None else min(best, us)
+        us = max_over_ranks(world, best)
+        attention[kind] = {"slots": Md, "keys": rows, "kv_dtype": "f16" if esz == 2 else "f32",
+                           "us_per_launch": us, "GBps": nbytes / us / 1e3, "frac_of_hbm": nbytes / us / 1e3 / peaks["hbm"]}
+        del g, KV
+        torch.cuda.empty_cache()
+
     head = per_shape["head"]
     gbs = bytes_step / (ms / 1e3) / 1e9
     return {"value": bytes_step * world / (ms_max / 1e3) / 1e9, "unit": "GB/s", "m_tokens": Md,
@@ -581,6 +626,7 @@ def decode_leg(args, world, rank, dev, stream, peaks):
             "split_head_step_pair_gather_ms": ag.get("argmax_pairs", {}).get("ms"),
             "replicated_head_step_ms": ag.get("replicated", {}).get("ms"),
             "collective_timing": ag.get("logits", {}).get("timing"), "per_shape": per_shape,
+            "attention": attention,
             "roofline": {"bound": "hbm", "kernel": f"q8_gemv_tile_kernel (vocab head {hn}x{D}, M={Md}, "
                                                   "back-to-back launches in a CUDA graph)",
                          "achieved": head["GBps"], "peak": peaks["hbm"], "unit": "GB/s",

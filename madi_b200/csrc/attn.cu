@@ -11,16 +11,15 @@
 //
 // Scores are q.k * rsqrt(head_dim); softmax as exp2((s - max) * log2 e); head_dim 64.
 //
-// B200 layout of the fused cross-attention: one thread-block cluster of `ns` CTAs
-// (<= 8) per (slot, head).  CTA c takes keys [c*csz, (c+1)*csz), computes its
-// partial flash result -- local max m, exp-sum s and unnormalised o = sum e*v --
-// and pushes (m, s, o) into rank 0's shared memory; rank 0 recombines them by
+// B200 layout of the fused attention (cross- and self-): one thread-block cluster
+// of `ns` CTAs (<= 8) per (slot, head).  CTA c TMA-loads its chunk of keys and
+// values ([csz][64] boxes of its kv head) into shared memory, computes its partial
+// flash result -- local max m, exp-sum s and unnormalised o = sum e*v -- and
+// pushes (m, s, o) into rank 0's shared memory; rank 0 recombines them by
 // log-sum-exp (the reference's flash_cross_attn_reduce arithmetic) and writes the
 // output.  No global scratch and one launch, with (slots x heads x ns) CTAs
-// streaming K/V in parallel.  Key reads are coalesced: a half-warp reads one key
-// row's 64 elements (16 lanes x 4), a warp reads one value row (32 lanes x 2).
-// The cross-attention K/V is the decode step's largest read at 8 slots (2 x 1500
-// x 1280 f16 per slot per layer), so the kernel is HBM-bound.
+// streaming K/V in parallel.  The cross-attention K/V is the decode step's largest
+// read at 8 slots (2 x 1500 x 1280 f16 per slot per layer): the kernel is HBM-bound.
 #include <cooperative_groups.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
@@ -128,13 +127,23 @@ MADI_DEV float pv_of(const float *w, const KV *vb, int kvd, int n, float (*red)[
     return o;
 }
 
-// ---------------------------------------------------------------- cross-attention
-// grid (ns, heads, slots), cluster (ns, 1, 1) when ns > 1.  kc / vc: [slot][seqlen][kvd].
+// ---------------------------------------------------------------- fused attention
+// grid (ns, heads, slots), cluster (ns, 1, 1) when ns > 1.  K and V are viewed as
+// [slots * rows][kvd] tensors; slot b's keys are rows b * rows + t.  Cross-
+// attention: rows = seqlen and every slot attends all of them; self-attention:
+// rows = the cache length and slot b attends min(pos[b] + 1, rows) keys.  CTA c
+// loads rows [c * csz, c * csz + csz) of its kv head -- one [csz][64] TMA box for
+// K and one for V -- into shared memory before any compute, so the whole chunk is
+// in flight at once.
 template <typename KV, bool kScores>
-__global__ void __launch_bounds__(kThr) cross_attn_kernel(float *__restrict__ out, const float *__restrict__ q,
-                                                          const KV *__restrict__ kc, const KV *__restrict__ vc,
-                                                          float *__restrict__ sc_out, int seqlen, int kvd, int nkv,
-                                                          int nh, int ns) {
+__global__ void __launch_bounds__(kThr) attn_kernel(const __grid_constant__ CUtensorMap tmK,
+                                                    const __grid_constant__ CUtensorMap tmV, float *__restrict__ out,
+                                                    const float *__restrict__ q, float *__restrict__ sc_out,
+                                                    const uint32_t *__restrict__ pos, int rows, int nkv, int nh, int ns,
+                                                    int csz, int *dev_err) {
+    extern __shared__ uint8_t attn_smem[];
+    KV *ks = reinterpret_cast<KV *>((reinterpret_cast<uintptr_t>(attn_smem) + 127) & ~uintptr_t(127));
+    KV *vs = ks + (size_t)csz * kHd;
     __shared__ float qh[kHd];
     __shared__ float raw[kAttnMaxChunk];
     __shared__ float ew[kAttnMaxChunk];
@@ -142,22 +151,33 @@ __global__ void __launch_bounds__(kThr) cross_attn_kernel(float *__restrict__ ou
     __shared__ float red[8][kHd];
     __shared__ float part[8][2 + kHd];          // rank 0: the cluster's partials
     __shared__ float stats[2];                  // global (max, 1/sum), for the scores
+    __shared__ __align__(8) uint64_t full;
+    __shared__ int abort_flag;
     const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const int tid = threadIdx.x;
     const int D = nh * kHd;
     const int kvh = h * nkv / nh;
-    const int csz = (seqlen + ns - 1) / ns;
+    const int len = pos ? (pos[b] < (uint32_t)rows ? (int)pos[b] + 1 : rows) : rows;
     const int t0 = c * csz;
-    const int n = t0 < seqlen ? min(csz, seqlen - t0) : 0;
-    const size_t slot_off = (size_t)b * seqlen * kvd;
-    const KV *kb = kc + slot_off + (size_t)min(t0, seqlen) * kvd + kvh * kHd;
-    const KV *vb = vc + slot_off + (size_t)min(t0, seqlen) * kvd + kvh * kHd;
-    // every CTA of the cluster runs before rank 0's shared memory is written
+    int n = t0 < len ? min(csz, len - t0) : 0;
     if (ns > 1) asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
-
-    if (tid < kHd) qh[tid] = q[(size_t)b * D + h * kHd + tid];
+    if (tid == 0) {
+        abort_flag = 0;
+        mbar_init(&full, 1);
+        fence_mbar_init();
+    }
     __syncthreads();
-    scores_of(qh, kb, kvd, n, raw);
+    if (tid == 0 && n > 0) {
+        mbar_arrive_expect_tx(&full, (uint32_t)(2 * csz * kHd * sizeof(KV)));
+        tma_load_2d(ks, &tmK, &full, kvh * kHd, b * rows + t0);
+        tma_load_2d(vs, &tmV, &full, kvh * kHd, b * rows + t0);
+    }
+    if (tid < kHd) qh[tid] = q[(size_t)b * D + h * kHd + tid];
+    bool landed = true;
+    if (n > 0) landed = mbar_wait(&full, 0, &abort_flag, dev_err);
+    __syncthreads();
+    if (n > 0 && !__syncthreads_and(landed)) n = 0;     // a copy that never landed: contribute nothing
+    scores_of(qh, ks, kHd, n, raw);
     __syncthreads();
     float lm = -INFINITY;
     for (int t = tid; t < n; t += kThr) lm = fmaxf(lm, raw[t]);
@@ -169,7 +189,7 @@ __global__ void __launch_bounds__(kThr) cross_attn_kernel(float *__restrict__ ou
         ls += e;
     }
     const float ssum = block_sum(ls, s8);      // its barriers also publish ew[]
-    const float o = pv_of(ew, vb, kvd, n, red);
+    const float o = pv_of(ew, vs, kHd, n, red);
 
     float *p0 = &part[0][0];
     if (ns > 1) {
@@ -212,7 +232,7 @@ __global__ void __launch_bounds__(kThr) cross_attn_kernel(float *__restrict__ ou
         if (ns > 1) asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
         else __syncthreads();
         const float gm = stats[0], inv = stats[1];
-        float *sr = sc_out + ((size_t)b * nh + h) * seqlen + t0;
+        float *sr = sc_out + ((size_t)b * nh + h) * rows + t0;
         for (int t = tid; t < n; t += kThr) sr[t] = exp2f((raw[t] - gm) * kLog2e) * inv;
     }
 }
@@ -290,51 +310,44 @@ __global__ void __launch_bounds__(kThr) cross_attn_reduce_kernel(float *__restri
     }
 }
 
-// ---------------------------------------------------------------- self-attention
-// grid (heads, slots): keys 0..pos[slot] (bounded by max_tok) of the slot's cache
-// rows kc[slot * cache_stride + t * kvd + ...].
-template <typename KV>
-__global__ void __launch_bounds__(kThr) self_attn_kernel(float *__restrict__ out, const float *__restrict__ q,
-                                                         const KV *__restrict__ kc, const KV *__restrict__ vc,
-                                                         const uint32_t *__restrict__ pos, int kvd, int nkv, int nh,
-                                                         long long cache_stride, int max_tok) {
-    __shared__ float qh[kHd];
-    __shared__ float sc[kAttnMaxTok];
-    __shared__ float s8[8];
-    __shared__ float red[8][kHd];
-    const int h = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
-    const int D = nh * kHd;
-    const int kvh = h * nkv / nh;
-    const uint32_t p = pos[b];
-    const int n = p < (uint32_t)max_tok ? (int)p + 1 : max_tok;
-    const KV *kb = kc + (size_t)b * cache_stride + kvh * kHd;
-    const KV *vb = vc + (size_t)b * cache_stride + kvh * kHd;
-    if (tid < kHd) qh[tid] = q[(size_t)b * D + h * kHd + tid];
-    __syncthreads();
-    scores_of(qh, kb, kvd, n, sc);
-    __syncthreads();
-    float lm = -INFINITY;
-    for (int t = tid; t < n; t += kThr) lm = fmaxf(lm, sc[t]);
-    const float mx = block_max(lm, s8);
-    float ls = 0.f;
-    for (int t = tid; t < n; t += kThr) {
-        const float e = exp2f((sc[t] - mx) * kLog2e);
-        sc[t] = e;
-        ls += e;
-    }
-    const float inv = 1.0f / block_sum(ls, s8);
-    for (int t = tid; t < n; t += kThr) sc[t] *= inv;     // normalised before P.V, as the reference
-    __syncthreads();
-    const float o = pv_of(sc, vb, kvd, n, red);
-    if (tid < kHd) out[(size_t)b * D + h * kHd + tid] = o;
+// K / V as [slots * rows][kvd] with [csz][64] boxes (no swizzle: rows of 64
+// elements, read conflict-free by half-warps).
+bool attn_map(CUtensorMap *m, const void *base, bool f16, uint64_t total_rows, int kvd, int csz) {
+    PFN_encodeTiled enc = tensor_map_encoder();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)kvd, total_rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)kvd * (f16 ? 2 : 4)};
+    const cuuint32_t box[2] = {(cuuint32_t)kHd, (cuuint32_t)csz};
+    const cuuint32_t es[2] = {1, 1};
+    return enc(m, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void *>(base),
+               dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 template <typename KV, bool kScores>
-cudaError_t launch_cross_t(float *out, const float *q, const KV *kc, const KV *vc, float *sc, int slots, int seqlen,
-                           int kvd, int nkv, int nh, int ns, cudaStream_t st) {
+cudaError_t launch_attn_t(const void *kc, const void *vc, float *out, const float *q, float *sc, const uint32_t *pos,
+                          int slots, int rows, int kvd, int nkv, int nh, int *dev_err, cudaStream_t st) {
+    const int ns = attn_cluster_size(rows);
+    if (ns == 0) return cudaErrorInvalidValue;
+    const int csz = (rows + ns - 1) / ns;
+    const bool f16 = sizeof(KV) == 2;
+    CUtensorMap tmK, tmV;
+    if (!attn_map(&tmK, kc, f16, (uint64_t)slots * rows, kvd, csz) ||
+        !attn_map(&tmV, vc, f16, (uint64_t)slots * rows, kvd, csz))
+        return cudaErrorNotSupported;
+    auto fn = attn_kernel<KV, kScores>;
+    const size_t smem = 128 + 2 * (size_t)csz * kHd * sizeof(KV);
+    static bool attr = false;
+    if (!attr) {
+        cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)(128 + 2 * kAttnMaxChunk * kHd * sizeof(KV)));
+        if (e != cudaSuccess) return e;
+        attr = true;
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(ns, nh, slots);
     cfg.blockDim = dim3(kThr);
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute at[1];
     at[0].id = cudaLaunchAttributeClusterDimension;
@@ -343,7 +356,7 @@ cudaError_t launch_cross_t(float *out, const float *q, const KV *kc, const KV *v
     at[0].val.clusterDim.z = 1;
     cfg.attrs = at;
     cfg.numAttrs = ns > 1 ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, cross_attn_kernel<KV, kScores>, out, q, kc, vc, sc, seqlen, kvd, nkv, nh, ns);
+    return cudaLaunchKernelEx(&cfg, fn, tmK, tmV, out, q, sc, pos, rows, nkv, nh, ns, csz, dev_err);
 }
 
 }  // namespace
@@ -355,17 +368,14 @@ int attn_cluster_size(int seqlen) {
 }
 
 cudaError_t launch_cross_attn(float *out, const float *q, const void *kc, const void *vc, bool kv_f16, float *scores,
-                              int slots, int seqlen, int kvd, int nkv, int nh, cudaStream_t st) {
-    const int ns = attn_cluster_size(seqlen);
-    if (ns == 0) return cudaErrorInvalidValue;
-    if (kv_f16) {
-        const __half *k = static_cast<const __half *>(kc), *v = static_cast<const __half *>(vc);
-        return scores ? launch_cross_t<__half, true>(out, q, k, v, scores, slots, seqlen, kvd, nkv, nh, ns, st)
-                      : launch_cross_t<__half, false>(out, q, k, v, nullptr, slots, seqlen, kvd, nkv, nh, ns, st);
-    }
-    const float *k = static_cast<const float *>(kc), *v = static_cast<const float *>(vc);
-    return scores ? launch_cross_t<float, true>(out, q, k, v, scores, slots, seqlen, kvd, nkv, nh, ns, st)
-                  : launch_cross_t<float, false>(out, q, k, v, nullptr, slots, seqlen, kvd, nkv, nh, ns, st);
+                              int slots, int seqlen, int kvd, int nkv, int nh, int *dev_err, cudaStream_t st) {
+    if (kv_f16)
+        return scores ? launch_attn_t<__half, true>(kc, vc, out, q, scores, nullptr, slots, seqlen, kvd, nkv, nh, dev_err, st)
+                      : launch_attn_t<__half, false>(kc, vc, out, q, nullptr, nullptr, slots, seqlen, kvd, nkv, nh,
+                                                     dev_err, st);
+    return scores ? launch_attn_t<float, true>(kc, vc, out, q, scores, nullptr, slots, seqlen, kvd, nkv, nh, dev_err, st)
+                  : launch_attn_t<float, false>(kc, vc, out, q, nullptr, nullptr, slots, seqlen, kvd, nkv, nh, dev_err,
+                                                st);
 }
 
 cudaError_t launch_cross_attn_part(float *part, const float *q, const void *kc, const void *vc, bool kv_f16,
@@ -390,18 +400,10 @@ cudaError_t launch_cross_attn_reduce(float *out, const float *part, int nsplit, 
 }
 
 cudaError_t launch_self_attn(float *out, const float *q, const void *kc, const void *vc, bool kv_f16,
-                             const uint32_t *pos, int slots, int kvd, int nkv, int nh, long long cache_stride,
-                             int max_tok, cudaStream_t st) {
-    const dim3 grid(nh, slots);
-    if (kv_f16)
-        self_attn_kernel<__half><<<grid, kThr, 0, st>>>(out, q, static_cast<const __half *>(kc),
-                                                        static_cast<const __half *>(vc), pos, kvd, nkv, nh,
-                                                        cache_stride, max_tok);
-    else
-        self_attn_kernel<float><<<grid, kThr, 0, st>>>(out, q, static_cast<const float *>(kc),
-                                                       static_cast<const float *>(vc), pos, kvd, nkv, nh,
-                                                       cache_stride, max_tok);
-    return cudaGetLastError();
+                             const uint32_t *pos, int slots, int kvd, int nkv, int nh, int max_tok, int *dev_err,
+                             cudaStream_t st) {
+    return kv_f16 ? launch_attn_t<__half, false>(kc, vc, out, q, nullptr, pos, slots, max_tok, kvd, nkv, nh, dev_err, st)
+                  : launch_attn_t<float, false>(kc, vc, out, q, nullptr, pos, slots, max_tok, kvd, nkv, nh, dev_err, st);
 }
 
 }  // namespace madi

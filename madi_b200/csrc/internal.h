@@ -84,15 +84,15 @@ constexpr int kAttnMaxChunk = 256;   // keys per CTA of a cross-attention cluste
 constexpr int kAttnMaxTok = 512;     // self-attention keys per slot
 int attn_cluster_size(int seqlen);   // CTAs per (slot, head); 0 if seqlen is too long
 cudaError_t launch_cross_attn(float *out, const float *q, const void *kc, const void *vc, bool kv_f16, float *scores,
-                              int slots, int seqlen, int kvd, int nkv, int nh, cudaStream_t st);
+                              int slots, int seqlen, int kvd, int nkv, int nh, int *dev_err, cudaStream_t st);
 cudaError_t launch_cross_attn_part(float *part, const float *q, const void *kc, const void *vc, bool kv_f16,
                                    float *sc_raw, int write_sc, int seqlen, int kvd, int nkv, int nh, int nsplit,
                                    cudaStream_t st);
 cudaError_t launch_cross_attn_reduce(float *out, const float *part, int nsplit, float *sc, int seqlen, int write_sc,
                                      int nh, cudaStream_t st);
 cudaError_t launch_self_attn(float *out, const float *q, const void *kc, const void *vc, bool kv_f16,
-                             const uint32_t *pos, int slots, int kvd, int nkv, int nh, long long cache_stride,
-                             int max_tok, cudaStream_t st);
+                             const uint32_t *pos, int slots, int kvd, int nkv, int nh, int max_tok, int *dev_err,
+                             cudaStream_t st);
 cudaError_t launch_shard_argmax(const float *logits, long long row_stride, int n, uint32_t h0, int m, float *vals,
                                 uint32_t *idx, cudaStream_t st);
 cudaError_t launch_merge_argmax(const float *vals, const uint32_t *idx, int world, int m, uint32_t *tokens,

@@ -360,7 +360,7 @@ int h_logit_filter(const ArgVal *a, uint32_t, cudaStream_t st) {
 // from the allocations (the reference signatures carry none) and bound every read.
 int attn_shape_ok(const char *who, uint32_t hdd, uint32_t kvd, uint32_t nkv, uint32_t nh) {
     if (hdd != 64) return fail(MADI_EINVAL, "%s: head_dim %u (64 supported)", who, hdd);
-    if (nh == 0 || nh > 1024 || nkv == 0 || nkv > nh || (size_t)kvd < (size_t)nkv * 64 || kvd % 4)
+    if (nh == 0 || nh > 1024 || nkv == 0 || nkv > nh || (size_t)kvd < (size_t)nkv * 64 || kvd % 8)
         return fail(MADI_EINVAL, "%s: heads %u, kv heads %u, kv_dim %u", who, nh, nkv, kvd);
     return MADI_OK;
 }
@@ -376,8 +376,8 @@ int h_self_attn(const ArgVal *a, uint32_t, cudaStream_t st) {
         return fail(MADI_EINVAL, "gpu_attention: buffer extents");
     const int max_tok = (int)std::min<size_t>(rows, kAttnMaxTok);
     cudaError_t e = launch_self_attn((float *)a[0].p, static_cast<const float *>(a[1].p), a[2].p, a[3].p, false,
-                                     static_cast<const uint32_t *>(a[4].p), 1, (int)kvd, (int)nkv, (int)nh, 0, max_tok,
-                                     st);
+                                     static_cast<const uint32_t *>(a[4].p), 1, (int)kvd, (int)nkv, (int)nh, max_tok,
+                                     S.dev_err, st);
     return e == cudaSuccess ? MADI_OK : cuda_fail(e, "gpu_attention");
 }
 // flash_cross_attn (f32 K/V) / flash_cross_attn_f16kv (+ sc_out, write_sc) /
@@ -399,7 +399,7 @@ int h_cross_attn(const ArgVal *a, uint32_t gx, cudaStream_t st) {
         scores = (float *)a[9].p;
     }
     cudaError_t e = launch_cross_attn((float *)a[0].p, static_cast<const float *>(a[1].p), a[2].p, a[3].p, kF16, scores,
-                                      (int)slots, (int)seqlen, (int)kvd, (int)nkv, (int)nh, st);
+                                      (int)slots, (int)seqlen, (int)kvd, (int)nkv, (int)nh, S.dev_err, st);
     return e == cudaSuccess ? MADI_OK : cuda_fail(e, who);
 }
 // flash_cross_attn_split(part, q, kc, vc, seqlen, hdd, kvd, nkv, nh, nsplit, sc_raw, write_sc), grid nh * nsplit
@@ -861,7 +861,7 @@ int madi_cross_attn(const float *q, const void *kc, const void *vc, int kv_dtype
     if (!aligned(q, 16) || !aligned(kc, 16) || !aligned(vc, 16) || !aligned(out, 16))
         return fail(MADI_EINVAL, "madi_cross_attn: buffers must be 16-byte aligned");
     cudaError_t e = launch_cross_attn(out, q, kc, vc, kv_dtype == MADI_F16, scores, slots, seqlen, kv_dim, kv_heads,
-                                      heads, pick_stream(stream));
+                                      heads, S.dev_err, pick_stream(stream));
     return e == cudaSuccess ? MADI_OK : cuda_fail(e, "madi_cross_attn");
 }
 
@@ -875,8 +875,8 @@ int madi_self_attn(const float *q, const void *kc, const void *vc, int kv_dtype,
         return fail(MADI_EINVAL, "madi_self_attn: slots %d, max_tok %d (<= %d)", slots, max_tok, kAttnMaxTok);
     if (!aligned(q, 16) || !aligned(kc, 16) || !aligned(vc, 16) || !aligned(out, 16))
         return fail(MADI_EINVAL, "madi_self_attn: buffers must be 16-byte aligned");
-    cudaError_t e = launch_self_attn(out, q, kc, vc, kv_dtype == MADI_F16, pos, slots, kv_dim, kv_heads, heads,
-                                     (long long)max_tok * kv_dim, max_tok, pick_stream(stream));
+    cudaError_t e = launch_self_attn(out, q, kc, vc, kv_dtype == MADI_F16, pos, slots, kv_dim, kv_heads, heads, max_tok,
+                                     S.dev_err, pick_stream(stream));
     return e == cudaSuccess ? MADI_OK : cuda_fail(e, "madi_self_attn");
 }
 
