@@ -95,6 +95,9 @@ int   madi_download(void *dst_host, const void *src_device, size_t size);
  *                      rows = grid_x, as the reference's grid                encoder_ops.metal:333
  *   layer_norm_f16     (X f32, Y f16, gamma f32, beta f32, D u32, eps f32)
  *                      rows = grid_x                                        encoder_ops.metal:305
+ *   bias_res_ln        (X f32, MO f32, bias f32, Y f32, gamma, beta, D, eps), rows = grid_x
+ *                                                                           encoder_ops.metal:69
+ *   layer_norm         (X f32, Y f32, gamma, beta, D, eps), rows = grid_x   encoder_ops.metal:14
  * GPU-resident decode-step primitives (VOCAB = 51866 as in the reference; the
  * lengths of buffers read through device-held indices are taken from their
  * allocations, so out-of-range positions / tokens never read out of bounds):
@@ -223,6 +226,14 @@ int madi_bias_res_ln_f16(float *x, const uint16_t *mo, const float *bias, uint16
  * x f32 [rows][d] unchanged.  Same shape and alignment rules. */
 int madi_layer_norm_f16(const float *x, uint16_t *y, const float *gamma, const float *beta,
                         int rows, int d, float eps, void *stream);
+
+/* bias_res_ln / layer_norm (encoder_ops.metal:14-120), the decoder's f32 forms:
+ * x f32 [rows][d] += mo f32 + bias (in place), y f32 = LN(x) * gamma + beta.
+ * Same shape and alignment rules as the f16 forms (f32 rows 16-byte aligned). */
+int madi_bias_res_ln(float *x, const float *mo, const float *bias, float *y, const float *gamma, const float *beta,
+                     int rows, int d, float eps, void *stream);
+int madi_layer_norm(const float *x, float *y, const float *gamma, const float *beta, int rows, int d, float eps,
+                    void *stream);
 
 /* ======================= GPU-resident greedy decode step ==================== */
 

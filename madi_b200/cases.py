@@ -3,6 +3,8 @@ put under a profiler (ncu -k regex:<kernel> -s <skip> -c <count> ...).
 
     python -m madi_b200.cases gemv --n 51866 --k 1280 --m 8 --x f16 --iters 6
     python -m madi_b200.cases gemm --m 24000 --n 5120 --k 1280 --epi gelu --iters 3
+    python -m madi_b200.cases cross --m 8 --n 1500 --k 1280 --iters 6   (slots, keys, kv_dim)
+    python -m madi_b200.cases self --m 8 --n 448 --k 1280 --iters 6     (slots, cache rows, kv_dim)
 
 Inputs are seeded random tensors of the given shape (int8 weights in [-127, 127],
 f16 scales in [1e-4, 2.1e-3], N(0,1) activations); the script prints the mean
@@ -20,7 +22,7 @@ EPIS = {"none": q8.EPI_NONE, "bias": q8.EPI_BIAS, "gelu": q8.EPI_BIAS_GELU, "res
 
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    ap.add_argument("kind", choices=["gemv", "gemm"])
+    ap.add_argument("kind", choices=["gemv", "gemm", "cross", "self"])
     ap.add_argument("--m", type=int, required=True)
     ap.add_argument("--n", type=int, required=True)
     ap.add_argument("--k", type=int, required=True)
@@ -32,6 +34,8 @@ def main(argv=None):
     dev = torch.device("cuda:0")
     g = torch.Generator(device=dev)
     g.manual_seed(1234)
+    if a.kind in ("cross", "self"):
+        return attention_case(a, dev, g)
     W = q8.Q8Weight(torch.randint(-127, 128, (a.n, a.k), dtype=torch.int8, device=dev, generator=g),
                     (torch.rand((a.n, a.k // 32), device=dev, generator=g) * 2e-3 + 1e-4).half())
     xdt = torch.float32 if a.x == "f32" else torch.float16
@@ -59,6 +63,40 @@ def main(argv=None):
         torch.cuda.synchronize()
         ts.append(e0.elapsed_time(e1) * 1e3)
     print(f"{a.kind} M={a.m} N={a.n} K={a.k} x={a.x} epi={a.epi}: mean {sum(ts) / len(ts):.2f} us, "
+          f"min {min(ts):.2f} us over {len(ts)} calls (after one untimed call)")
+
+
+def attention_case(a, dev, g):
+    """Decoder attention: --m slots, --n keys (cross) or cache rows (self), --k kv_dim
+    (heads = kv_dim / 64); f16 K/V for cross, f32 for self, as the reference keeps them."""
+    from . import attn
+    heads = a.k // 64
+    kv_dt = torch.float16 if a.kind == "cross" else torch.float32
+    kc = torch.randn((a.m, a.n, a.k), device=dev, generator=g).to(kv_dt)
+    vc = torch.randn((a.m, a.n, a.k), device=dev, generator=g).to(kv_dt)
+    q = torch.randn((a.m, a.k), device=dev, generator=g) * 0.5
+    out = torch.empty_like(q)
+    pos = torch.full((a.m,), a.n - 1, dtype=torch.int32, device=dev)
+
+    def call():
+        if a.kind == "cross":
+            attn.cross_attn(q, kc, vc, heads, out=out)
+        else:
+            attn.self_attn(q, kc, vc, pos, heads, out=out)
+
+    call()
+    torch.cuda.synchronize()
+    flush = torch.zeros(64 << 20, dtype=torch.int32, device=dev)
+    ts = []
+    for _ in range(a.iters):
+        flush.sum()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        call()
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1) * 1e3)
+    print(f"{a.kind} attention slots={a.m} keys={a.n} kv_dim={a.k}: mean {sum(ts) / len(ts):.2f} us, "
           f"min {min(ts):.2f} us over {len(ts)} calls (after one untimed call)")
 
 

@@ -63,6 +63,8 @@ constexpr int kLnMaxD = 2048;   // row width limit of the register-resident row 
 // MO == nullptr: layer_norm_f16; else bias_res_ln_f16 (X updated in place).
 cudaError_t launch_res_ln(float *X, const __half *MO, const float *bias, __half *Y, const float *gamma,
                           const float *beta, int rows, int D, float eps, cudaStream_t st);
+cudaError_t launch_res_ln_f32(float *X, const float *MO, const float *bias, float *Y, const float *gamma,
+                              const float *beta, int rows, int D, float eps, cudaStream_t st);
 
 // ---------------------------------------------------------------- decode-step primitives (decode_step.cu)
 constexpr int kWhisperVocab = 51866;   // VOCAB of graph_helpers.metal:9 (the by-name kernels assume it)

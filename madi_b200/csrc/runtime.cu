@@ -355,6 +355,18 @@ int h_logit_filter(const ArgVal *a, uint32_t, cudaStream_t st) {
     return e == cudaSuccess ? MADI_OK : cuda_fail(e, "logit_filter_indirect");
 }
 
+// bias_res_ln(X, MO, bias, Y, gamma, beta, D, eps) / layer_norm(X, Y, gamma, beta, D, eps), f32, rows = grid x
+//   encoder_ops.metal:14-120 (the decoder's LayerNorms)
+int h_bias_res_ln_f32(const ArgVal *a, uint32_t gx, cudaStream_t st) {
+    return madi_bias_res_ln((float *)a[0].p, static_cast<const float *>(a[1].p), static_cast<const float *>(a[2].p),
+                            (float *)a[3].p, static_cast<const float *>(a[4].p), static_cast<const float *>(a[5].p),
+                            (int)gx, (int)a[6].u, a[7].f, st);
+}
+int h_layer_norm_f32(const ArgVal *a, uint32_t gx, cudaStream_t st) {
+    return madi_layer_norm(static_cast<const float *>(a[0].p), (float *)a[1].p, static_cast<const float *>(a[2].p),
+                           static_cast<const float *>(a[3].p), (int)gx, (int)a[4].u, a[5].f, st);
+}
+
 // ---- decoder attention by name (decoder_ops.metal:81-531); head_dim 64, K/V rows
 // of kvd elements, head h reading the kv head h * nkv / nh.  Buffer extents come
 // from the allocations (the reference signatures carry none) and bound every read.
@@ -456,6 +468,8 @@ const std::vector<Op> &ops() {
         {"m4_gemm_q8_bias_gelu", {kPtr, kPtr, kPtr, kPtr, kPtr, kU32, kU32, kU32, kU32}, h_m4_q8},
         {"bias_res_ln_f16", {kPtr, kPtr, kPtr, kPtr, kPtr, kPtr, kU32, kF32}, h_bias_res_ln},
         {"layer_norm_f16", {kPtr, kPtr, kPtr, kPtr, kU32, kF32}, h_layer_norm},
+        {"bias_res_ln", {kPtr, kPtr, kPtr, kPtr, kPtr, kPtr, kU32, kF32}, h_bias_res_ln_f32},
+        {"layer_norm", {kPtr, kPtr, kPtr, kPtr, kU32, kF32}, h_layer_norm_f32},
         {"emb_lookup_indirect_q8", {kPtr, kPtr, kPtr, kPtr, kPtr, kU32}, h_emb_q8_indirect},
         {"gpu_emb_lookup_q8", {kPtr, kPtr, kPtr, kPtr, kU32}, h_emb_q8_direct},
         {"emb_lookup_indirect", {kPtr, kPtr, kPtr, kPtr, kU32}, h_emb_f16_indirect},
@@ -769,23 +783,40 @@ int madi_q8_quantize_f16(const uint16_t *w, int rows, int dim, int8_t *qs, uint1
 }
 
 namespace {
-int res_ln_impl(float *x, const uint16_t *mo, const float *bias, uint16_t *y, const float *gamma, const float *beta,
-                int rows, int d, float eps, void *stream, const char *who) {
+// f32 = false: MO and Y f16 (the encoder's *_f16 forms); true: MO and Y f32 (the decoder's).
+int res_ln_impl(float *x, const void *mo, const float *bias, void *y, const float *gamma, const float *beta, int rows,
+                int d, float eps, void *stream, const char *who, bool f32 = false) {
     if (!S.ready) return fail(MADI_ENOINIT, "%s: not initialised", who);
     if (!x || !y || !gamma || !beta || (mo && !bias)) return fail(MADI_EINVAL, "%s: null argument", who);
     if (rows < 0 || d < 128 || d > kLnMaxD || d % 128)
         return fail(MADI_EINVAL, "%s: rows=%d, D=%d (need 128 <= D <= %d, D %% 128 == 0)", who, rows, d, kLnMaxD);
     if (!(eps >= 0.f) || eps > 1.f) return fail(MADI_EINVAL, "%s: eps=%g", who, (double)eps);
-    if (!aligned(x, 16) || !aligned(gamma, 16) || !aligned(beta, 16) || !aligned(y, 8) || (mo && !aligned(mo, 8)) ||
+    const size_t ya = f32 ? 16 : 8;
+    if (!aligned(x, 16) || !aligned(gamma, 16) || !aligned(beta, 16) || !aligned(y, ya) || (mo && !aligned(mo, ya)) ||
         (bias && !aligned(bias, 16)))
         return fail(MADI_EINVAL, "%s: misaligned buffer (f32 rows 16-byte, f16 rows 8-byte aligned)", who);
     if ((size_t)rows * (size_t)d >= (1ull << 31)) return fail(MADI_EINVAL, "%s: too large", who);
     if (rows == 0) return MADI_OK;
-    cudaError_t e = launch_res_ln(x, reinterpret_cast<const __half *>(mo), bias, reinterpret_cast<__half *>(y), gamma,
-                                  beta, rows, d, eps, pick_stream(stream));
+    cudaError_t e =
+        f32 ? launch_res_ln_f32(x, static_cast<const float *>(mo), bias, static_cast<float *>(y), gamma, beta, rows, d,
+                                eps, pick_stream(stream))
+            : launch_res_ln(x, static_cast<const __half *>(mo), bias, static_cast<__half *>(y), gamma, beta, rows, d,
+                            eps, pick_stream(stream));
     return e == cudaSuccess ? MADI_OK : cuda_fail(e, who);
 }
 }  // namespace
+
+int madi_bias_res_ln(float *x, const float *mo, const float *bias, float *y, const float *gamma, const float *beta,
+                     int rows, int d, float eps, void *stream) {
+    if (!mo) return fail(MADI_EINVAL, "madi_bias_res_ln: null MO");
+    return res_ln_impl(x, mo, bias, y, gamma, beta, rows, d, eps, stream, "madi_bias_res_ln", true);
+}
+
+int madi_layer_norm(const float *x, float *y, const float *gamma, const float *beta, int rows, int d, float eps,
+                    void *stream) {
+    return res_ln_impl(const_cast<float *>(x), nullptr, nullptr, y, gamma, beta, rows, d, eps, stream, "madi_layer_norm",
+                       true);
+}
 
 int madi_bias_res_ln_f16(float *x, const uint16_t *mo, const float *bias, uint16_t *y, const float *gamma,
                          const float *beta, int rows, int d, float eps, void *stream) {

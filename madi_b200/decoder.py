@@ -1,0 +1,159 @@
+"""A Whisper large-v3-turbo-shaped greedy decoder step on the library's kernels --
+the synthetic end-to-end configuration of the Q8 path.
+
+One token step per slot follows the reference's decodeBlock (decoder.zig:255-330):
+
+    x   = emb_q8(tokens[pos]) + pos_emb[pos]                       (f32 residual stream)
+    per layer:  xb = LN(x);  q, K[pos], V[pos] = qkv(xb)           gemv_q8_qkv (KV cache store)
+                ao = self_attn(q, K, V, 0..pos);  x += o(ao) + ob;  xb = LN(x)
+                q = cq(xb) + cqb;  ao = cross_attn(q, cross K/V);  x += co(ao) + cob;  xb = LN(x)
+                x += fc2(gelu(fc1(xb) + m0b)) + m2b                 gemv_q8_bias_gelu / _bias_res
+    logits = emb_q8 . LN_post(x)  (tied head);  pos += 1;  logit filter;  tokens[pos] = argmax
+
+Every operation is a library kernel (Q8 GEMVs for the projections at M = slots <= 8,
+the tcgen05 GEMM for the one-time cross K/V projection of the encoder states, the
+cluster attention kernels, the f32 LayerNorms, the decode-step helpers), all on one
+stream and capturable as one CUDA graph per token step.  Weights are seeded random
+Q8 (no checkpoint); the encoder states are seeded random f16 [1500][1280] per slot.
+"""
+from dataclasses import dataclass
+from typing import List
+
+import numpy as np
+import torch
+
+from . import attn, greedy, q8, synth
+
+D, F, V, HEADS, LAYERS, MAX_TOK, ENC = 1280, 5120, 51866, 20, 4, 448, 1500
+EPS = 1e-5
+
+
+@dataclass
+class Layer:
+    aln: tuple
+    qkv: q8.Q8Weight
+    qb: torch.Tensor
+    vb: torch.Tensor
+    o: q8.Q8Weight
+    ob: torch.Tensor
+    caln: tuple
+    cq: q8.Q8Weight
+    cqb: torch.Tensor
+    ck: q8.Q8Weight          # cross K projection (no bias) of the encoder states
+    cv: q8.Q8Weight          # cross V projection (+ cvb)
+    cvb: torch.Tensor
+    co: q8.Q8Weight
+    cob: torch.Tensor
+    mln: tuple
+    fc1: q8.Q8Weight
+    m0b: torch.Tensor
+    fc2: q8.Q8Weight
+    m2b: torch.Tensor
+
+
+def host_weights(seed: int = 1) -> dict:
+    """The synthetic decoder as host numpy arrays (the oracle's copy)."""
+    def ln(i):
+        g = synth.rng(seed, 900 + i)
+        return ((1.0 + 0.1 * g.standard_normal(D)).astype(np.float32), (0.1 * g.standard_normal(D)).astype(np.float32))
+
+    w = {"layers": []}
+    for l in range(LAYERS):
+        b = seed * 100 + l * 20
+        L = {"aln": ln(3 * l), "caln": ln(3 * l + 1), "mln": ln(3 * l + 2),
+             "qkv": synth.q8_weight(3 * D, D, b + 1), "qb": synth.bias(D, b + 2), "vb": synth.bias(D, b + 3),
+             "o": synth.q8_weight(D, D, b + 4), "ob": synth.bias(D, b + 5),
+             "cq": synth.q8_weight(D, D, b + 6), "cqb": synth.bias(D, b + 7),
+             "ck": synth.q8_weight(D, D, b + 8), "cv": synth.q8_weight(D, D, b + 9), "cvb": synth.bias(D, b + 10),
+             "co": synth.q8_weight(D, D, b + 11), "cob": synth.bias(D, b + 12),
+             "fc1": synth.q8_weight(F, D, b + 13), "m0b": synth.bias(F, b + 14),
+             "fc2": synth.q8_weight(D, F, b + 15), "m2b": synth.bias(D, b + 16)}
+        w["layers"].append(L)
+    w["emb"] = synth.q8_weight(V, D, seed * 100 + 99)
+    w["pos_emb"] = (synth.rng(seed, 950).standard_normal((MAX_TOK, D)) * 0.1).astype(np.float32)
+    w["ln_post"] = ln(99)
+    return w
+
+
+class Decoder:
+    """Device copy of the synthetic decoder plus the per-slot decode state."""
+
+    def __init__(self, w: dict, slots: int, device="cuda"):
+        if not 1 <= slots <= 8:
+            raise ValueError("1..8 token slots")
+        t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(device)
+        qw = lambda p: q8.Q8Weight(t(p[0]), t(p[1]))
+        self.slots, self.dev = slots, device
+        self.layers: List[Layer] = []
+        for L in w["layers"]:
+            self.layers.append(Layer(
+                aln=(t(L["aln"][0]), t(L["aln"][1])), qkv=qw(L["qkv"]), qb=t(L["qb"]), vb=t(L["vb"]), o=qw(L["o"]),
+                ob=t(L["ob"]), caln=(t(L["caln"][0]), t(L["caln"][1])), cq=qw(L["cq"]), cqb=t(L["cqb"]),
+                ck=qw(L["ck"]), cv=qw(L["cv"]), cvb=t(L["cvb"]), co=qw(L["co"]), cob=t(L["cob"]),
+                mln=(t(L["mln"][0]), t(L["mln"][1])), fc1=qw(L["fc1"]), m0b=t(L["m0b"]), fc2=qw(L["fc2"]),
+                m2b=t(L["m2b"])))
+        self.emb = qw(w["emb"])
+        self.pos_emb = t(w["pos_emb"])
+        self.ln_post = (t(w["ln_post"][0]), t(w["ln_post"][1]))
+        S = slots
+        f32 = dict(dtype=torch.float32, device=device)
+        self.x, self.xb, self.q, self.ao, self.mo = (torch.zeros((S, D), **f32) for _ in range(5))
+        self.mh = torch.zeros((S, F), **f32)
+        self.logits = torch.zeros((S, V), **f32)
+        self.kc = [torch.zeros((S, MAX_TOK, D), **f32) for _ in range(LAYERS)]
+        self.vc = [torch.zeros((S, MAX_TOK, D), **f32) for _ in range(LAYERS)]
+        self.ck = [None] * LAYERS
+        self.cv = [None] * LAYERS
+        self.tokens = torch.zeros((S, MAX_TOK), dtype=torch.int32, device=device)
+        self.conf = torch.zeros((S, MAX_TOK), **f32)
+        self.pos = torch.zeros(S, dtype=torch.int32, device=device)
+
+    def set_encoder(self, enc_states: torch.Tensor, stream=None):
+        """Cross K / V of every layer from the encoder states f16 [slots][1500][1280]
+        (the tcgen05 GEMM, once per audio chunk); kept f16 as the reference's decoder does."""
+        S, T, _ = enc_states.shape
+        flat = enc_states.reshape(S * T, D).contiguous()
+        for l, L in enumerate(self.layers):
+            self.ck[l] = q8.linear(L.ck, flat, stream=stream).view(S, T, D)
+            self.cv[l] = q8.linear(L.cv, flat, bias=L.cvb, stream=stream).view(S, T, D)
+
+    def reset(self, seed_token: int = 50258):
+        self.tokens.zero_()
+        self.tokens[:, 0] = seed_token
+        self.conf.zero_()
+        self.pos.zero_()
+        for c in self.kc + self.vc:
+            c.zero_()
+
+    def step(self, sample_begin: int = 1, no_repeat_ngram: int = 0, stream=None):
+        """One greedy token for every slot; all state on the device."""
+        s = dict(stream=stream)
+        greedy.emb_lookup_q8(self.emb, self.tokens, self.pos, out=self.x, **s)
+        self.x.add_(self.pos_emb.index_select(0, self.pos.long()))
+        for l, L in enumerate(self.layers):
+            q8.layer_norm(self.x, *L.aln, eps=EPS, out=self.xb, **s)
+            q8.qkv(L.qkv, self.xb, L.qb, L.vb, self.kc[l], self.vc[l], self.pos, q_out=self.q, **s)
+            attn.self_attn(self.q, self.kc[l], self.vc[l], self.pos, HEADS, out=self.ao, **s)
+            q8.linear(L.o, self.ao, out=self.mo, **s)
+            q8.bias_res_ln(self.x, self.mo, L.ob, *L.caln, eps=EPS, out=self.xb, **s)
+            q8.linear(L.cq, self.xb, bias=L.cqb, out=self.q, **s)
+            attn.cross_attn(self.q, self.ck[l], self.cv[l], HEADS, out=self.ao, **s)
+            q8.linear(L.co, self.ao, out=self.mo, **s)
+            q8.bias_res_ln(self.x, self.mo, L.cob, *L.mln, eps=EPS, out=self.xb, **s)
+            q8.linear(L.fc1, self.xb, bias=L.m0b, epi=q8.EPI_BIAS_GELU, out=self.mh, **s)
+            q8.linear(L.fc2, self.mh, bias=L.m2b, epi=q8.EPI_BIAS_RES, residual=self.x, out=self.x, **s)
+        q8.layer_norm(self.x, *self.ln_post, eps=EPS, out=self.xb, **s)
+        q8.linear(self.emb, self.xb, out=self.logits, **s)
+        greedy.step_advance(self.pos, **s)
+        for b in range(self.slots):
+            greedy.logit_filter(self.logits[b], self.tokens[b], self.pos[b:b + 1], sample_begin, no_repeat_ngram, **s)
+        greedy.argmax_conf(self.logits, self.tokens, self.pos, self.conf, **s)
+
+    def step_bytes(self) -> int:
+        """HBM bytes one token step must read: every Q8 weight and scale once, the
+        self K/V rows 0..pos (counted at a full 448-row cache), the cross K/V."""
+        per_layer = (3 * D * D + 3 * D * D + 2 * F * D) * (1 + 1 / 16)
+        kv_self = 2 * self.slots * MAX_TOK * D * 4
+        kv_cross = 2 * self.slots * ENC * D * 2
+        head = V * D * (1 + 1 / 16)
+        return int(LAYERS * (per_layer + kv_self + kv_cross) + head)

@@ -171,3 +171,32 @@ def layer_norm_f16(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, eps
                                          float(eps), _stream(stream))
     _lib.check(rc, "madi_layer_norm_f16")
     return out
+
+
+def bias_res_ln(x: torch.Tensor, mo: torch.Tensor, bias: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor,
+                eps: float = 1e-5, out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+    """bias_res_ln (encoder_ops.metal:69-120), the decoder's f32 form: x (updated in
+    place) += mo + bias; returns LayerNorm(x) * gamma + beta as f32."""
+    rows, d = _ln_check(x, gamma, beta)
+    if mo.dtype != torch.float32 or mo.shape != x.shape or not mo.is_contiguous():
+        raise ValueError("mo must be a contiguous f32 tensor shaped like x")
+    if bias.dtype != torch.float32 or bias.shape != (d,):
+        raise ValueError("bias must be f32 [d]")
+    if out is None:
+        out = torch.empty((rows, d), dtype=torch.float32, device=x.device)
+    rc = _lib.load().madi_bias_res_ln(x.data_ptr(), mo.data_ptr(), bias.data_ptr(), out.data_ptr(), gamma.data_ptr(),
+                                      beta.data_ptr(), rows, d, float(eps), _stream(stream))
+    _lib.check(rc, "madi_bias_res_ln")
+    return out
+
+
+def layer_norm(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, eps: float = 1e-5,
+               out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+    """layer_norm (encoder_ops.metal:14-67): f32 LayerNorm(x) * gamma + beta."""
+    rows, d = _ln_check(x, gamma, beta)
+    if out is None:
+        out = torch.empty((rows, d), dtype=torch.float32, device=x.device)
+    rc = _lib.load().madi_layer_norm(x.data_ptr(), out.data_ptr(), gamma.data_ptr(), beta.data_ptr(), rows, d,
+                                     float(eps), _stream(stream))
+    _lib.check(rc, "madi_layer_norm")
+    return out

@@ -210,6 +210,21 @@ def bias_res_ln(x, mo=None, bias=None, gamma=None, beta=None, eps=1e-5):
     return x2, y
 
 
+def bias_res_ln_f32(x, mo=None, bias=None, gamma=None, beta=None, eps=1e-5):
+    """bias_res_ln / layer_norm, the decoder's f32 forms (encoder_ops.metal:14-120):
+    x + mo + bias in the reference's f32 order ((x + mo) + bias), then the LayerNorm
+    in f64.  Returns (x updated in f32, y exact in f64)."""
+    x2 = np.array(x, dtype=np.float32, copy=True)
+    if mo is not None:
+        x2 = (x2 + np.asarray(mo, np.float32)) + np.asarray(bias, np.float32)
+    xd = x2.astype(np.float64)
+    mean = xd.mean(axis=1, keepdims=True)
+    var = ((xd - mean) ** 2).mean(axis=1, keepdims=True)
+    y = (xd - mean) / np.sqrt(var + float(np.float32(eps))) * np.asarray(gamma, np.float64) + np.asarray(beta,
+                                                                                                      np.float64)
+    return x2, y
+
+
 def _head_kv(kc, vc, h, nh, nkv, hdd):
     kvh = h * nkv // nh
     return kc[..., kvh * hdd:(kvh + 1) * hdd], vc[..., kvh * hdd:(kvh + 1) * hdd]

@@ -1,0 +1,107 @@
+"""The synthetic end-to-end configuration: a Whisper large-v3-turbo-shaped 4-layer
+decoder (madi_b200/decoder.py: Q8 projections, KV-cache self-attention,
+cross-attention over tcgen05-projected encoder states, f32 LayerNorms, tied Q8
+vocab head, logit filter, argmax) decoding greedily for 2 slots, one token step
+per CUDA-graph replay, against the same loop restated on the CPU from the
+oracle's primitives (f64 arithmetic, the reference's rounding points: f32
+residual stream and KV cache, f16 cross K/V).
+
+The greedy token streams must be bit-identical; the oracle's top-2 logit margin
+at every step is asserted far above the f32-vs-f64 difference, so equality is
+a decisive check.
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+STEPS, SLOTS, SEED_TOKEN, SAMPLE_BEGIN = 8, 2, 50258, 1
+
+
+def _t(a, dev="cuda"):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+
+def _oracle_decode(oracle, w, ck, cv, dec):
+    D, HEADS, MAX_TOK = dec.D, dec.HEADS, dec.MAX_TOK
+    f32 = lambda a: np.asarray(a, np.float32)
+    S = ck[0].shape[0]
+    tokens = np.zeros((S, MAX_TOK), np.uint32)
+    tokens[:, 0] = SEED_TOKEN
+    pos = np.zeros(S, np.int64)
+    kc = [np.zeros((S, MAX_TOK, D), np.float32) for _ in w["layers"]]
+    vc = [np.zeros((S, MAX_TOK, D), np.float32) for _ in w["layers"]]
+    eq, es = w["emb"]
+    margins, confs = [], []
+    for _ in range(STEPS):
+        x = np.stack([oracle.emb_q8(eq, es, tokens[b, pos[b]]) + w["pos_emb"][pos[b]] for b in range(S)])
+        for l, L in enumerate(w["layers"]):
+            _, xb = oracle.bias_res_ln_f32(x, None, None, *L["aln"], dec.EPS)
+            full = oracle.gemv_q8(f32(xb), *L["qkv"])
+            q = f32(full[:, :D] + L["qb"])
+            for b in range(S):
+                kc[l][b, pos[b]] = f32(full[b, D:2 * D])
+                vc[l][b, pos[b]] = f32(full[b, 2 * D:] + L["vb"])
+            ao = f32(oracle.self_attn(q, kc[l], vc[l], pos, HEADS))
+            mo = f32(oracle.gemv_q8(ao, *L["o"]))
+            x, xb = oracle.bias_res_ln_f32(x, mo, L["ob"], *L["caln"], dec.EPS)
+            q = f32(oracle.gemv_q8(f32(xb), *L["cq"], bias=L["cqb"], epi=oracle.EPI_BIAS))
+            ao = f32(oracle.cross_attn(q, ck[l], cv[l], HEADS)[0])
+            mo = f32(oracle.gemv_q8(ao, *L["co"]))
+            x, xb = oracle.bias_res_ln_f32(x, mo, L["cob"], *L["mln"], dec.EPS)
+            mh = f32(oracle.gemv_q8(f32(xb), *L["fc1"], bias=L["m0b"], epi=oracle.EPI_BIAS_GELU))
+            x = f32(oracle.gemv_q8(mh, *L["fc2"], bias=L["m2b"], epi=oracle.EPI_BIAS_RES, res_in=x))
+        _, xb = oracle.bias_res_ln_f32(x, None, None, *w["ln_post"], dec.EPS)
+        logits = oracle.gemv_q8(f32(xb), eq, es)
+        pos += 1
+        for b in range(S):
+            lg = oracle.logit_filter(f32(logits[b]), tokens[b], int(pos[b]), SAMPLE_BEGIN, 0)
+            tok, conf = oracle.argmax_conf(lg)
+            top2 = np.sort(lg.astype(np.float64))[-2:]
+            margins.append((top2[1] - top2[0]) / np.sqrt(np.mean(logits[b] ** 2)))
+            tokens[b, pos[b]] = tok
+            confs.append(conf)
+    return tokens, np.array(confs).reshape(STEPS, S), min(margins)
+
+
+def test_greedy_decoder_end_to_end(madi, oracle):
+    import torch
+    from madi_b200 import decoder as dec
+    w = dec.host_weights(seed=1)
+    model = dec.Decoder(w, SLOTS)
+    g = np.random.default_rng(5)
+    enc = g.standard_normal((SLOTS, dec.ENC, dec.D)).astype(np.float16)
+    model.set_encoder(_t(enc))
+    torch.cuda.synchronize()
+    ck = [c.cpu().numpy() for c in model.ck]
+    cv = [c.cpu().numpy() for c in model.cv]
+
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    model.reset(SEED_TOKEN)
+    with torch.cuda.stream(s):
+        model.step(SAMPLE_BEGIN)                 # warm-up outside the graph
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    first = model.tokens[:, 1].cpu().numpy().view(np.uint32).copy()
+    graph = torch.cuda.CUDAGraph()
+    model.reset(SEED_TOKEN)
+    torch.cuda.synchronize()
+    with torch.cuda.graph(graph):
+        model.step(SAMPLE_BEGIN)
+    model.reset(SEED_TOKEN)
+    torch.cuda.synchronize()
+    for _ in range(STEPS):
+        graph.replay()
+    torch.cuda.synchronize()
+    got = model.tokens[:, :STEPS + 1].cpu().numpy().view(np.uint32)
+    conf = model.conf[:, 1:STEPS + 1].cpu().numpy()
+    del graph
+
+    want, want_conf, margin = _oracle_decode(oracle, w, ck, cv, dec)
+    assert margin > 1e-3, f"synthetic data too close to a tie (margin {margin:.2e})"
+    assert np.array_equal(first, want[:, 1])
+    assert np.array_equal(got, want[:, :STEPS + 1]), f"GPU {got.tolist()}\noracle {want[:, :STEPS + 1].tolist()}"
+    assert int(model.pos[0].item()) == STEPS
+    np.testing.assert_allclose(conf.T, want_conf, rtol=1e-3)

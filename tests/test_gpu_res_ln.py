@@ -88,3 +88,39 @@ def test_rejects_unsupported_widths(madi):
         with pytest.raises(MadiError) as e:
             q8.layer_norm_f16(x, g, g)
         assert e.value.code == MADI_EINVAL
+
+
+@pytest.mark.parametrize("rows,d", [(1, 1280), (8, 1280), (300, 384)])
+def test_decoder_f32_forms(madi, oracle, rows, d):
+    """bias_res_ln / layer_norm (encoder_ops.metal:14-120): f32 MO and f32 Y, typed
+    and by name; the residual stream bit-exact, Y within 1e-5 x max|Y|."""
+    import torch
+    from madi_b200 import q8
+    from madi_b200 import backend as mtl
+    g = np.random.default_rng(rows + d)
+    x = (g.standard_normal((rows, d)) * 3.0).astype(np.float32)
+    mo = g.standard_normal((rows, d)).astype(np.float32)
+    b = (g.standard_normal(d) * 0.02).astype(np.float32)
+    gamma = (1.0 + 0.1 * g.standard_normal(d)).astype(np.float32)
+    beta = (0.1 * g.standard_normal(d)).astype(np.float32)
+    X = _t(x)
+    y = q8.bias_res_ln(X, _t(mo), _t(b), _t(gamma), _t(beta), eps=1e-5)
+    torch.cuda.synchronize()
+    x_ex, y_ex = oracle.bias_res_ln_f32(x, mo, b, gamma, beta, 1e-5)
+    assert np.array_equal(X.cpu().numpy(), x_ex)
+    assert np.abs(y.cpu().numpy() - y_ex).max() <= 1e-5 * np.abs(y_ex).max()
+    Y2 = torch.empty((rows, d), dtype=torch.float32, device="cuda")
+    mtl.dispatch(mtl.get_function("layer_norm"), (rows, 1, 1), (256, 1, 1),
+                 [mtl.Arg.buf(X), mtl.Arg.buf(Y2), mtl.Arg.buf(_t(gamma)), mtl.Arg.buf(_t(beta)), mtl.Arg.u32(d),
+                  mtl.Arg.f32(1e-5)])
+    mtl.sync(10000)
+    _, y2_ex = oracle.bias_res_ln_f32(x_ex, None, None, gamma, beta, 1e-5)
+    assert np.abs(Y2.cpu().numpy() - y2_ex).max() <= 1e-5 * np.abs(y2_ex).max()
+    X3 = _t(x)
+    Y3 = torch.empty((rows, d), dtype=torch.float32, device="cuda")
+    mtl.dispatch(mtl.get_function("bias_res_ln"), (rows, 1, 1), (256, 1, 1),
+                 [mtl.Arg.buf(X3), mtl.Arg.buf(_t(mo)), mtl.Arg.buf(_t(b)), mtl.Arg.buf(Y3), mtl.Arg.buf(_t(gamma)),
+                  mtl.Arg.buf(_t(beta)), mtl.Arg.u32(d), mtl.Arg.f32(1e-5)])
+    mtl.sync(10000)
+    assert np.array_equal(X3.cpu().numpy(), x_ex)
+    assert np.abs(Y3.cpu().numpy() - y_ex).max() <= 1e-5 * np.abs(y_ex).max()
