@@ -613,6 +613,43 @@ def decode_leg(args, world, rank, dev, stream, peaks):
         del g, KV
         torch.cuda.empty_cache()
 
+    # ---- the synthetic end-to-end decoder (madi_b200.decoder: 4 Whisper-shaped layers
+    # with attention, LayerNorms, the tied Q8 head and the greedy step), one token
+    # step per graph replay, at 1 and Md slots; cross K/V from seeded encoder
+    # states through the tcgen05 GEMM (untimed, once per chunk)
+    from madi_b200 import decoder as dec_mod
+    e2e_dec = {}
+    wts = dec_mod.host_weights(seed=1)
+    for S in sorted({1, Md}):
+        model = dec_mod.Decoder(wts, S, device=dev)
+        enc = torch.randn((S, dec_mod.ENC, D), device=dev, generator=gen).half()
+        with torch.cuda.stream(stream):
+            model.set_encoder(enc, stream=stream)
+            model.reset()
+            model.step(stream=stream)                    # eager warm-up
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream, capture_error_mode="thread_local"):
+                model.step(stream=stream)
+            model.reset()
+            torch.cuda.synchronize()
+            for _ in range(3):
+                g.replay()
+            n_tok = 48
+            a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a0.record(stream)
+            for _ in range(n_tok):
+                g.replay()
+            a1.record(stream)
+            torch.cuda.synchronize()
+        ms_tok = max_over_ranks(world, a0.elapsed_time(a1) / n_tok)
+        e2e_dec[f"slots_{S}"] = {"ms_per_token_step": ms_tok, "tokens_per_s": S * world / (ms_tok / 1e3),
+                                 "step_GBps_per_gpu": model.step_bytes() / (ms_tok / 1e3) / 1e9,
+                                 "step_bytes_per_gpu": model.step_bytes()}
+        del g, model, enc
+        torch.cuda.empty_cache()
+    del wts
+
     head = per_shape["head"]
     gbs = bytes_step / (ms / 1e3) / 1e9
     return {"value": bytes_step * world / (ms_max / 1e3) / 1e9, "unit": "GB/s", "m_tokens": Md,
@@ -627,6 +664,8 @@ def decode_leg(args, world, rank, dev, stream, peaks):
             "replicated_head_step_ms": ag.get("replicated", {}).get("ms"),
             "collective_timing": ag.get("logits", {}).get("timing"), "per_shape": per_shape,
             "attention": attention,
+            # whole decoder token steps (all layers, attention, head, greedy selection), tokens/s for the job
+            "end_to_end_decoder": e2e_dec,
             "roofline": {"bound": "hbm", "kernel": f"q8_gemv_tile_kernel (vocab head {hn}x{D}, M={Md}, "
                                                   "back-to-back launches in a CUDA graph)",
                          "achieved": head["GBps"], "peak": peaks["hbm"], "unit": "GB/s",
