@@ -121,6 +121,7 @@ int   madi_download(void *dst_host, const void *src_device, size_t size);
  *                                                                              decoder_ops.metal:338
  *   flash_cross_attn_reduce (out, part, hdd, nsplit, sc_out, seqlen, write_sc), heads = grid_x
  *                                                                              decoder_ops.metal:416
+ *   m4_flash_enc           (out, q, k, v, seq_len, nh): packed [seq][nh*64] f16 m4_gemm.metal:268
  * On success *out_id holds a handle for madi_dispatch. */
 int   madi_get_function(const char *name, int *out_id);
 
@@ -269,6 +270,16 @@ int madi_logit_filter(float *logits, int vocab, const uint32_t *past, int past_l
  * seqlen <= 2048; one thread-block cluster per (slot, head). */
 int madi_cross_attn(const float *q, const void *kc, const void *vc, int kv_dtype, int slots, int seqlen, int heads,
                     int kv_heads, int kv_dim, float *out, float *scores, void *stream);
+
+/* Encoder self-attention, bidirectional (m4_flash_enc, m4_gemm.metal:255-407) on
+ * the tensor cores: for each of `chunks` sequences of `seq` rows and each head h,
+ * out[t][h*64..] = softmax(Q K^T * 0.125) V over the sequence, P rounded to f16,
+ * f32 accumulation, out = half(O / (l + 1e-6)).  q / k / v / out: f16 rows of
+ * `stride` / `out_stride` elements (multiples of 8; the packed [q | k | v] rows of
+ * the QKV projection work with k = q + heads*64, v = q + 2*heads*64), chunk c at
+ * rows c*seq .. c*seq + seq - 1; head_dim 64; 16-byte aligned. */
+int madi_flash_attn_enc(const uint16_t *q, const uint16_t *k, const uint16_t *v, int stride, uint16_t *out,
+                        int out_stride, int seq, int heads, int chunks, void *stream);
 
 /* Self-attention of one query token per slot over its cache rows 0..pos[slot]
  * (gpu_attention, decoder_ops.metal:81-149): kc, vc [slots][max_tok][kv_dim]

@@ -68,6 +68,7 @@ SIGNATURES = {
     "madi_merge_shard_argmax": ([P, P, I, I, P, P], I),
     "madi_cross_attn": ([P, P, P, I, I, I, I, I, I, P, P, P], I),
     "madi_self_attn": ([P, P, P, I, P, I, I, I, I, I, P, P], I),
+    "madi_flash_attn_enc": ([P, P, P, I, P, I, I, I, I, P], I),
 }
 
 _lib = None

@@ -51,3 +51,23 @@ def self_attn(q: torch.Tensor, kc: torch.Tensor, vc: torch.Tensor, pos: torch.Te
                                     heads, kv_heads, kv_dim, max_tok, out.data_ptr(), _stream(stream))
     _lib.check(rc, "madi_self_attn")
     return out
+
+
+def flash_attn_enc(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, seq: int,
+                   out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+    """Encoder self-attention (m4_flash_enc) on the tensor cores.  q / k / v: f16 row
+    views [chunks * seq][>= heads*64] with a common row stride (e.g. column slices
+    of the packed [M][3 * heads * 64] QKV projection output); returns f16
+    [chunks * seq][heads * 64]."""
+    rows = q.shape[0]
+    if rows % seq or any(t.shape[0] != rows or t.dtype != torch.float16 or t.stride(1) != 1 for t in (q, k, v)):
+        raise ValueError("q / k / v must be f16 [chunks * seq][heads * 64] row views")
+    if not (q.stride(0) == k.stride(0) == v.stride(0)):
+        raise ValueError("q / k / v must share one row stride")
+    if out is None:
+        out = torch.empty((rows, heads * 64), dtype=torch.float16, device=q.device)
+    rc = _lib.load().madi_flash_attn_enc(q.data_ptr(), k.data_ptr(), v.data_ptr(), q.stride(0), out.data_ptr(),
+                                         out.stride(0), seq, heads, rows // seq, _stream(stream))
+    _lib.check(rc, "madi_flash_attn_enc")
+    return out
+

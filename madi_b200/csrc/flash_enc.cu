@@ -1,0 +1,316 @@
+// flash_enc.cu -- encoder self-attention (bidirectional) on the 5th-generation tensor
+// cores: m4_flash_enc (m4_gemm.metal:255-407) restated for sm_100a.
+//
+//   S = Q K^T * 0.125 (f32);  online softmax per query row: m' = max(m, max_j S),
+//   alpha = exp(m - m'), P = exp(S - m') rounded to f16, l = l * alpha + sum(P unrounded),
+//   O = O * alpha + P V (f32);  out = half(O / (l + 1e-6)).
+//   q / k / v: f16 rows of `stride` elements, head h at columns h*64..h*64+63;
+//   `chunks` independent sequences of `seq` rows each, back to back.
+//
+// One CTA per (128-query tile, head, chunk); 256 threads:
+//   warp 0   TMA producer: the Q tile, then K / V tiles of 128 keys through a
+//            2-stage ring (SWIZZLE_128B boxes [128 rows][64 dims]);
+//   warp 1   MMA issuer + TMEM owner: S_j = Q K_j^T (M = 128 queries, N = 128 keys,
+//            K = 64 dims, both operands K-major in shared memory) into one of two
+//            TMEM S buffers, issued one tile ahead so the tensor cores compute
+//            S_{j+1} while the softmax of tile j runs; then O += P_j V_j (TS form:
+//            P from TMEM as A, V from shared memory as an N-contiguous B operand);
+//   warps 4-7 softmax (thread = query row = TMEM lane): read the S row from TMEM,
+//            update the running max / sum, write P as f16 pairs back over S, and
+//            rescale O in TMEM by alpha before P_j V_j is issued; finally O / l.
+// TMEM columns: S0 [0, 128), S1 [128, 256), O [256, 320).  Every wait is bounded.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace madi {
+namespace {
+
+constexpr int kQT = 128;                 // queries per CTA
+constexpr int kKT = 128;                 // keys per tile
+constexpr int kHD = 64;                  // head dim
+constexpr int kNS = 2;                   // K / V ring stages
+constexpr int kTile = kQT * kHD * 2;     // bytes of one [128][64] f16 tile
+constexpr int kFaThreads = 256;
+constexpr int kSmWarp0 = 4;              // warps 4..7: softmax
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kOCol = 256;
+constexpr float kScale = 0.125f;
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct __align__(8) FaBars {
+    uint64_t q_full;
+    uint64_t kv_full[kNS];
+    uint64_t kv_empty[kNS];
+    uint64_t s_full[2];
+    uint64_t s_free[2];
+    uint64_t p_ready[2];
+    uint64_t o_done;
+    uint64_t drain;
+    uint32_t tmem_base;
+    int abort;
+};
+
+// The CTA allocates all 512 TMEM columns, so it asks for more than half of the
+// SM's shared memory: a second CTA never lands on the SM to wait in tcgen05.alloc.
+constexpr size_t kFaSmemUsed = 1024 + (size_t)(1 + 2 * kNS) * kTile + sizeof(FaBars) + 64;
+constexpr size_t kFaSmem = kFaSmemUsed > 120 * 1024 ? kFaSmemUsed : 120 * 1024;
+
+// PV: A = P (TMEM, K-major), B = V (shared memory, N-contiguous: bit 16 transposes B).
+constexpr uint32_t kIdescS = idesc_f16_f32(kQT, kKT);
+constexpr uint32_t kIdescPV = idesc_f16_f32(kQT, kHD) | (1u << 16);
+
+// Bounded wait that ignores the abort flag (to drain work in flight before exit).
+MADI_DEV void mbar_wait_drain_fa(uint64_t *bar, uint32_t parity) {
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity))
+        if (clock64() - t0 > kWaitBudgetCycles) return;
+}
+
+MADI_DEV void mma_ss(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc)
+        : "memory");
+}
+MADI_DEV void mma_ts(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
+        "r"(a), "l"(b), "r"(idesc), "r"(acc)
+        : "memory");
+}
+
+__global__ void __launch_bounds__(kFaThreads, 1)
+    flash_enc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmV, __half *__restrict__ out, int out_stride, int seq,
+                     int *dev_err) {
+    extern __shared__ uint8_t fa_smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(fa_smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *qs = smem;
+    uint8_t *ks = qs + kTile;                    // kNS tiles
+    uint8_t *vs = ks + kNS * kTile;              // kNS tiles
+    FaBars *bars = reinterpret_cast<FaBars *>(vs + kNS * kTile);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int q0 = blockIdx.x * kQT, h = blockIdx.y, chunk = blockIdx.z;
+    const int row0 = chunk * seq;                // first row of this chunk
+    const int nkv = (seq + kKT - 1) / kKT;
+
+    if (threadIdx.x == 0) {
+        mbar_init(&bars->q_full, 1);
+        for (int s = 0; s < kNS; ++s) {
+            mbar_init(&bars->kv_full[s], 1);
+            mbar_init(&bars->kv_empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&bars->s_full[b], 1);
+            mbar_init(&bars->s_free[b], 1);
+            mbar_init(&bars->p_ready[b], 128);
+        }
+        mbar_init(&bars->o_done, 1);
+        mbar_init(&bars->drain, 1);
+        bars->abort = 0;
+        fence_mbar_init();
+        tma_prefetch_desc(&tmQ);
+        tma_prefetch_desc(&tmK);
+        tma_prefetch_desc(&tmV);
+    }
+    if (warp == 1) {
+        tmem_alloc(&bars->tmem_base, kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = bars->tmem_base;
+    volatile int *abort_flag = &bars->abort;
+
+    if (warp == 0) {
+        // ------------------------------------------------ TMA producer
+        if (lane == 0) {
+            mbar_arrive_expect_tx(&bars->q_full, kTile);
+            tma_load_2d(qs, &tmQ, &bars->q_full, h * kHD, row0 + q0);
+            int issued = 0;
+            for (int j = 0; j < nkv; ++j) {
+                const int s = j % kNS;
+                if (!mbar_wait(&bars->kv_empty[s], ((j / kNS) & 1) ^ 1, abort_flag, dev_err)) break;
+                mbar_arrive_expect_tx(&bars->kv_full[s], 2 * kTile);
+                tma_load_2d(ks + s * kTile, &tmK, &bars->kv_full[s], h * kHD, row0 + j * kKT);
+                tma_load_2d(vs + s * kTile, &tmV, &bars->kv_full[s], h * kHD, row0 + j * kKT);
+                issued = j + 1;
+            }
+            // copies issued last must land before shared memory is released
+            mbar_wait_drain_fa(&bars->q_full, 0);
+            for (int j = issued > kNS ? issued - kNS : 0; j < issued; ++j)
+                mbar_wait_drain_fa(&bars->kv_full[j % kNS], (j / kNS) & 1);
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            const uint64_t qd = smem_desc_sw128(smem_u32(qs));
+            const uint64_t kd0 = smem_desc_sw128(smem_u32(ks));
+            const uint64_t vd0 = smem_desc_sw128(smem_u32(vs));
+            constexpr uint64_t kTileU = kTile >> 4;          // descriptor units per tile
+            bool ok = mbar_wait(&bars->q_full, 0, abort_flag, dev_err);
+            auto issue_s = [&](int j) -> bool {
+                const int s = j % kNS, b = j & 1;
+                if (!mbar_wait(&bars->kv_full[s], (j / kNS) & 1, abort_flag, dev_err)) return false;
+                if (j >= 2 && !mbar_wait(&bars->s_free[b], ((j - 2) >> 1) & 1, abort_flag, dev_err)) return false;
+                tc_fence_after();
+#pragma unroll
+                for (int k = 0; k < kHD / 16; ++k)       // K = 64 dims: 4 MMAs, descriptors +32 bytes each
+                    mma_ss(tmem + b * kKT, qd + 2 * k, kd0 + s * kTileU + 2 * k, kIdescS, k != 0);
+                umma_commit(&bars->s_full[b]);
+                return true;
+            };
+            if (ok) ok = issue_s(0);
+            for (int j = 0; ok && j < nkv; ++j) {
+                const int s = j % kNS, b = j & 1;
+                if (j + 1 < nkv && !issue_s(j + 1)) { ok = false; break; }
+                if (!mbar_wait(&bars->p_ready[b], (j >> 1) & 1, abort_flag, dev_err)) { ok = false; break; }
+                tc_fence_after();
+                // O += P_j V_j: K = 128 keys in 8 steps; P columns +8 (16 f16), V rows +16 = 2048 bytes
+#pragma unroll
+                for (int k = 0; k < kKT / 16; ++k)
+                    mma_ts(tmem + kOCol, tmem + b * kKT + 8 * k, vd0 + s * kTileU + 128 * k, kIdescPV, (j | k) != 0);
+                umma_commit(&bars->kv_empty[s]);
+                umma_commit(&bars->s_free[b]);
+                umma_commit(&bars->o_done);
+            }
+            umma_commit(&bars->drain);
+            mbar_wait_drain_fa(&bars->drain, 0);
+        }
+        __syncwarp();
+    } else if (warp >= kSmWarp0) {
+        // ------------------------------------------------ softmax, one query row per thread
+        const int qw = warp & 3;
+        const uint32_t lane_addr = (uint32_t)(qw * 32) << 16;
+        const int qrow = qw * 32 + lane;         // row of the tile
+        float m = -INFINITY, l = 0.f;
+        bool alive = true;
+        for (int j = 0; j < nkv && alive; ++j) {
+            const int b = j & 1;
+            alive = warp_wait_all(&bars->s_full[b], (j >> 1) & 1, abort_flag, dev_err);
+            if (!alive) break;
+            tc_fence_after();
+            const int kcur = min(seq - j * kKT, kKT);   // valid keys of this tile
+            const uint32_t sa = tmem + lane_addr + b * kKT;
+            uint32_t sv[kKT];
+#pragma unroll
+            for (int c = 0; c < kKT / 32; ++c) tmem_ld32(sa + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&sv[32 * c]));
+            tmem_wait_ld();
+            float mx = -INFINITY;
+#pragma unroll
+            for (int i = 0; i < kKT; ++i) {
+                const float v = i < kcur ? __uint_as_float(sv[i]) * kScale : -INFINITY;
+                sv[i] = __float_as_uint(v);
+                mx = fmaxf(mx, v);
+            }
+            const float mn = fmaxf(m, mx);
+            const float alpha = (m == -INFINITY) ? 0.f : exp2f((m - mn) * kLog2e);
+            float bs = 0.f;
+            uint32_t pp[kKT / 2];
+#pragma unroll
+            for (int i = 0; i < kKT; i += 2) {
+                const float e0 = exp2f((__uint_as_float(sv[i]) - mn) * kLog2e);
+                const float e1 = exp2f((__uint_as_float(sv[i + 1]) - mn) * kLog2e);
+                bs += e0 + e1;
+                pp[i >> 1] = h2_as_u32(__floats2half2_rn(e0, e1));
+            }
+            l = l * alpha + bs;
+            m = mn;
+            // P_j over the first 64 columns of S_j (f16 pairs, K-major for the TS MMA)
+            tmem_st32(sa, *reinterpret_cast<uint32_t(*)[32]>(&pp[0]));
+            tmem_st32(sa + 32, *reinterpret_cast<uint32_t(*)[32]>(&pp[32]));
+            if (j > 0) {
+                // O *= alpha, once P_{j-1} V_{j-1} has landed in TMEM
+                alive = warp_wait_all(&bars->o_done, (j - 1) & 1, abort_flag, dev_err);
+                if (!alive) break;
+                tc_fence_after();
+                const uint32_t oa = tmem + lane_addr + kOCol;
+                uint32_t ov[kHD];
+                tmem_ld32(oa, *reinterpret_cast<uint32_t(*)[32]>(&ov[0]));
+                tmem_ld32(oa + 32, *reinterpret_cast<uint32_t(*)[32]>(&ov[32]));
+                tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < kHD; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
+                tmem_st32(oa, *reinterpret_cast<uint32_t(*)[32]>(&ov[0]));
+                tmem_st32(oa + 32, *reinterpret_cast<uint32_t(*)[32]>(&ov[32]));
+            }
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(&bars->p_ready[b]);
+        }
+        if (alive) alive = warp_wait_all(&bars->o_done, (nkv - 1) & 1, abort_flag, dev_err);
+        if (alive) {
+            tc_fence_after();
+            const uint32_t oa = tmem + lane_addr + kOCol;
+            uint32_t ov[kHD];
+            tmem_ld32(oa, *reinterpret_cast<uint32_t(*)[32]>(&ov[0]));
+            tmem_ld32(oa + 32, *reinterpret_cast<uint32_t(*)[32]>(&ov[32]));
+            tmem_wait_ld();
+            const int q = q0 + qrow;
+            if (q < seq) {
+                const float inv = 1.0f / (l + 1e-6f);
+                __half *orow = out + (size_t)(row0 + q) * out_stride + h * kHD;
+#pragma unroll
+                for (int c = 0; c < kHD / 8; ++c) {
+                    uint4 w;
+                    w.x = h2_as_u32(__floats2half2_rn(__uint_as_float(ov[8 * c]) * inv, __uint_as_float(ov[8 * c + 1]) * inv));
+                    w.y = h2_as_u32(__floats2half2_rn(__uint_as_float(ov[8 * c + 2]) * inv, __uint_as_float(ov[8 * c + 3]) * inv));
+                    w.z = h2_as_u32(__floats2half2_rn(__uint_as_float(ov[8 * c + 4]) * inv, __uint_as_float(ov[8 * c + 5]) * inv));
+                    w.w = h2_as_u32(__floats2half2_rn(__uint_as_float(ov[8 * c + 6]) * inv, __uint_as_float(ov[8 * c + 7]) * inv));
+                    *reinterpret_cast<uint4 *>(orow + 8 * c) = w;
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+bool fa_map(CUtensorMap *m, const void *base, uint64_t rows, int stride, int cols) {
+    PFN_encodeTiled enc = tensor_map_encoder();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)stride * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)kHD, (cuuint32_t)kQT};
+    const cuuint32_t es[2] = {1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims, strides, box, es,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+cudaError_t launch_flash_enc(const __half *q, const __half *k, const __half *v, int stride, __half *out,
+                             int out_stride, int seq, int heads, int chunks, int *dev_err, cudaStream_t st) {
+    CUtensorMap tmQ, tmK, tmV;
+    const uint64_t rows = (uint64_t)chunks * seq;
+    const int cols = heads * kHD;
+    if (!fa_map(&tmQ, q, rows, stride, cols) || !fa_map(&tmK, k, rows, stride, cols) ||
+        !fa_map(&tmV, v, rows, stride, cols))
+        return cudaErrorNotSupported;
+    static bool attr = false;
+    if (!attr) {
+        cudaError_t e = cudaFuncSetAttribute(flash_enc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kFaSmem);
+        if (e != cudaSuccess) return e;
+        attr = true;
+    }
+    const dim3 grid((seq + kQT - 1) / kQT, heads, chunks);
+    flash_enc_kernel<<<grid, kFaThreads, kFaSmem, st>>>(tmQ, tmK, tmV, out, out_stride, seq, dev_err);
+    return cudaGetLastError();
+}
+
+}  // namespace madi

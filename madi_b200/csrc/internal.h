@@ -95,6 +95,9 @@ cudaError_t launch_cross_attn_reduce(float *out, const float *part, int nsplit, 
 cudaError_t launch_self_attn(float *out, const float *q, const void *kc, const void *vc, bool kv_f16,
                              const uint32_t *pos, int slots, int kvd, int nkv, int nh, int max_tok, int *dev_err,
                              cudaStream_t st);
+// ---- encoder self-attention on the tensor cores (flash_enc.cu); head_dim 64
+cudaError_t launch_flash_enc(const __half *q, const __half *k, const __half *v, int stride, __half *out,
+                             int out_stride, int seq, int heads, int chunks, int *dev_err, cudaStream_t st);
 cudaError_t launch_shard_argmax(const float *logits, long long row_stride, int n, uint32_t h0, int m, float *vals,
                                 uint32_t *idx, cudaStream_t st);
 cudaError_t launch_merge_argmax(const float *vals, const uint32_t *idx, int world, int m, uint32_t *tokens,

@@ -355,6 +355,19 @@ int h_logit_filter(const ArgVal *a, uint32_t, cudaStream_t st) {
     return e == cudaSuccess ? MADI_OK : cuda_fail(e, "logit_filter_indirect");
 }
 
+// m4_flash_enc(out, q, k, v, seq_len, nh): packed [seq][nh*64] f16 buffers   m4_gemm.metal:268-407
+int h_flash_enc(const ArgVal *a, uint32_t, cudaStream_t st) {
+    const uint32_t seq = a[4].u, nh = a[5].u;
+    if (seq == 0 || seq > (1u << 20) || nh == 0 || nh > 1024) return fail(MADI_EINVAL, "m4_flash_enc: seq %u, heads %u", seq, nh);
+    const size_t bytes = (size_t)seq * nh * 64 * 2;
+    for (int i = 0; i < 4; ++i)
+        if (!a[i].p || !aligned(a[i].p, 16) || bytes_after(a[i].p) < bytes)
+            return fail(MADI_EINVAL, "m4_flash_enc: buffer %d extent / alignment", i);
+    return madi_flash_attn_enc(static_cast<const uint16_t *>(a[1].p), static_cast<const uint16_t *>(a[2].p),
+                               static_cast<const uint16_t *>(a[3].p), (int)nh * 64, (uint16_t *)a[0].p, (int)nh * 64,
+                               (int)seq, (int)nh, 1, st);
+}
+
 // bias_res_ln(X, MO, bias, Y, gamma, beta, D, eps) / layer_norm(X, Y, gamma, beta, D, eps), f32, rows = grid x
 //   encoder_ops.metal:14-120 (the decoder's LayerNorms)
 int h_bias_res_ln_f32(const ArgVal *a, uint32_t gx, cudaStream_t st) {
@@ -488,6 +501,7 @@ const std::vector<Op> &ops() {
         {"flash_cross_attn_split", {kPtr, kPtr, kPtr, kPtr, kU32, kU32, kU32, kU32, kU32, kU32, kPtr, kU32},
          h_cross_split},
         {"flash_cross_attn_reduce", {kPtr, kPtr, kU32, kU32, kPtr, kU32, kU32}, h_cross_reduce},
+        {"m4_flash_enc", {kPtr, kPtr, kPtr, kPtr, kU32, kU32}, h_flash_enc},
     };
     return table;
 }
@@ -894,6 +908,23 @@ int madi_cross_attn(const float *q, const void *kc, const void *vc, int kv_dtype
     cudaError_t e = launch_cross_attn(out, q, kc, vc, kv_dtype == MADI_F16, scores, slots, seqlen, kv_dim, kv_heads,
                                       heads, S.dev_err, pick_stream(stream));
     return e == cudaSuccess ? MADI_OK : cuda_fail(e, "madi_cross_attn");
+}
+
+int madi_flash_attn_enc(const uint16_t *q, const uint16_t *k, const uint16_t *v, int stride, uint16_t *out,
+                        int out_stride, int seq, int heads, int chunks, void *stream) {
+    if (!S.ready) return fail(MADI_ENOINIT, "madi_flash_attn_enc: not initialised");
+    if (!q || !k || !v || !out) return fail(MADI_EINVAL, "madi_flash_attn_enc: null argument");
+    if (seq <= 0 || heads <= 0 || heads > 1024 || chunks <= 0 || chunks > 65535 || stride < heads * 64 ||
+        out_stride < heads * 64 || stride % 8 || out_stride % 8 || (size_t)chunks * seq >= (1ull << 31))
+        return fail(MADI_EINVAL, "madi_flash_attn_enc: seq %d heads %d chunks %d stride %d out_stride %d", seq, heads,
+                    chunks, stride, out_stride);
+    if (!aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) || !aligned(out, 16))
+        return fail(MADI_EINVAL, "madi_flash_attn_enc: buffers must be 16-byte aligned");
+    cudaError_t e = launch_flash_enc(reinterpret_cast<const __half *>(q), reinterpret_cast<const __half *>(k),
+                                     reinterpret_cast<const __half *>(v), stride, reinterpret_cast<__half *>(out),
+                                     out_stride, seq, heads, chunks, S.dev_err, pick_stream(stream));
+    if (e == cudaErrorNotSupported) return fail(MADI_EUNSUPPORTED, "madi_flash_attn_enc: tensor maps unavailable");
+    return e == cudaSuccess ? MADI_OK : cuda_fail(e, "madi_flash_attn_enc");
 }
 
 int madi_self_attn(const float *q, const void *kc, const void *vc, int kv_dtype, const uint32_t *pos, int slots,

@@ -265,3 +265,23 @@ def self_attn(q, kc, vc, pos, nh, nkv=None, hdd=64):
         o, _ = cross_attn(np.asarray(q, np.float64)[b:b + 1], kc[b:b + 1, :n], vc[b:b + 1, :n], nh, nkv, hdd)
         out[b] = o[0]
     return out
+
+
+def flash_attn_enc(q, k, v, heads, seq, hdd=64):
+    """m4_flash_enc (m4_gemm.metal:255-407) restated without tiling in f64: per chunk
+    and head, softmax(Q K^T * 0.125) V.  The unrounded result (the reference's
+    kernel rounds P to f16 inside its online softmax; the parity gate is measured
+    against this exact value).  q / k / v [chunks * seq][heads * hdd]."""
+    q = np.asarray(q, np.float64)
+    k = np.asarray(k, np.float64)
+    v = np.asarray(v, np.float64)
+    out = np.empty((q.shape[0], heads * hdd))
+    for c in range(q.shape[0] // seq):
+        r = slice(c * seq, (c + 1) * seq)
+        for h in range(heads):
+            cs = slice(h * hdd, (h + 1) * hdd)
+            s = (q[r, cs] @ k[r, cs].T) * 0.125
+            e = np.exp(s - s.max(axis=1, keepdims=True))
+            out[r, cs] = (e @ v[r, cs]) / e.sum(axis=1, keepdims=True)
+    return out
+
