@@ -5,6 +5,7 @@ put under a profiler (ncu -k regex:<kernel> -s <skip> -c <count> ...).
     python -m madi_b200.cases gemm --m 24000 --n 5120 --k 1280 --epi gelu --iters 3
     python -m madi_b200.cases cross --m 8 --n 1500 --k 1280 --iters 6   (slots, keys, kv_dim)
     python -m madi_b200.cases self --m 8 --n 448 --k 1280 --iters 6     (slots, cache rows, kv_dim)
+    python -m madi_b200.cases flash --m 8 --n 1500 --k 1280 --iters 6    (chunks, seq, heads*64)
 
 Inputs are seeded random tensors of the given shape (int8 weights in [-127, 127],
 f16 scales in [1e-4, 2.1e-3], N(0,1) activations); the script prints the mean
@@ -22,7 +23,7 @@ EPIS = {"none": q8.EPI_NONE, "bias": q8.EPI_BIAS, "gelu": q8.EPI_BIAS_GELU, "res
 
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    ap.add_argument("kind", choices=["gemv", "gemm", "cross", "self"])
+    ap.add_argument("kind", choices=["gemv", "gemm", "cross", "self", "flash"])
     ap.add_argument("--m", type=int, required=True)
     ap.add_argument("--n", type=int, required=True)
     ap.add_argument("--k", type=int, required=True)
@@ -36,6 +37,8 @@ def main(argv=None):
     g.manual_seed(1234)
     if a.kind in ("cross", "self"):
         return attention_case(a, dev, g)
+    if a.kind == "flash":
+        return flash_case(a, dev, g)
     W = q8.Q8Weight(torch.randint(-127, 128, (a.n, a.k), dtype=torch.int8, device=dev, generator=g),
                     (torch.rand((a.n, a.k // 32), device=dev, generator=g) * 2e-3 + 1e-4).half())
     xdt = torch.float32 if a.x == "f32" else torch.float16
@@ -98,6 +101,29 @@ def attention_case(a, dev, g):
         ts.append(e0.elapsed_time(e1) * 1e3)
     print(f"{a.kind} attention slots={a.m} keys={a.n} kv_dim={a.k}: mean {sum(ts) / len(ts):.2f} us, "
           f"min {min(ts):.2f} us over {len(ts)} calls (after one untimed call)")
+
+
+def flash_case(a, dev, g):
+    """Encoder self-attention: --m chunks, --n sequence length, --k heads * 64; q / k / v
+    as column slices of one packed [chunks * seq][3 * k] f16 QKV buffer."""
+    from . import attn
+    heads = a.k // 64
+    qkv = torch.randn((a.m * a.n, 3 * a.k), device=dev, generator=g).half()
+    q, k, v = qkv[:, :a.k], qkv[:, a.k:2 * a.k], qkv[:, 2 * a.k:]
+    out = torch.empty((a.m * a.n, a.k), dtype=torch.float16, device=dev)
+    attn.flash_attn_enc(q, k, v, heads, a.n, out=out)
+    torch.cuda.synchronize()
+    flops = 4.0 * a.n * a.n * 64 * heads * a.m
+    ts = []
+    for _ in range(a.iters):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        attn.flash_attn_enc(q, k, v, heads, a.n, out=out)
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1) * 1e3)
+    print(f"flash attention chunks={a.m} seq={a.n} heads={heads}: mean {sum(ts) / len(ts):.2f} us, min {min(ts):.2f} us, "
+          f"{flops / min(ts) / 1e6:.1f} TFLOP/s at the min over {len(ts)} calls (after one untimed call)")
 
 
 if __name__ == "__main__":

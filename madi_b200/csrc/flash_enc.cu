@@ -205,33 +205,38 @@ __global__ void __launch_bounds__(kFaThreads, 1)
 #pragma unroll
             for (int c = 0; c < kKT / 32; ++c) tmem_ld32(sa + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&sv[32 * c]));
             tmem_wait_ld();
-            float mx = -INFINITY;
+            // row max of the raw scores (scale > 0 commutes with max); keys >= kcur masked
+            float mxr = -INFINITY;
 #pragma unroll
-            for (int i = 0; i < kKT; ++i) {
-                const float v = i < kcur ? __uint_as_float(sv[i]) * kScale : -INFINITY;
-                sv[i] = __float_as_uint(v);
-                mx = fmaxf(mx, v);
-            }
-            const float mn = fmaxf(m, mx);
-            const float alpha = (m == -INFINITY) ? 0.f : exp2f((m - mn) * kLog2e);
+            for (int i = 0; i < kKT; ++i)
+                if (i < kcur) mxr = fmaxf(mxr, __uint_as_float(sv[i]));
+            const float mn = fmaxf(m, mxr * kScale);
+            // exp(s * scale - m') = 2^(s * scale * log2 e - m' * log2 e): one FFMA and the
+            // hardware base-2 exponential per element (P is rounded to f16 after it)
+            const float ml = mn * kLog2e;
+            const float alpha = (m == -INFINITY) ? 0.f : ex2_approx(fmaf(m, kLog2e, -ml));
             float bs = 0.f;
             uint32_t pp[kKT / 2];
 #pragma unroll
             for (int i = 0; i < kKT; i += 2) {
-                const float e0 = exp2f((__uint_as_float(sv[i]) - mn) * kLog2e);
-                const float e1 = exp2f((__uint_as_float(sv[i + 1]) - mn) * kLog2e);
+                const float e0 = i < kcur ? ex2_approx(fmaf(__uint_as_float(sv[i]), kScale * kLog2e, -ml)) : 0.f;
+                const float e1 = i + 1 < kcur ? ex2_approx(fmaf(__uint_as_float(sv[i + 1]), kScale * kLog2e, -ml)) : 0.f;
                 bs += e0 + e1;
                 pp[i >> 1] = h2_as_u32(__floats2half2_rn(e0, e1));
             }
             l = l * alpha + bs;
+            const bool grew = mn != m;
             m = mn;
             // P_j over the first 64 columns of S_j (f16 pairs, K-major for the TS MMA)
             tmem_st32(sa, *reinterpret_cast<uint32_t(*)[32]>(&pp[0]));
             tmem_st32(sa + 32, *reinterpret_cast<uint32_t(*)[32]>(&pp[32]));
             if (j > 0) {
-                // O *= alpha, once P_{j-1} V_{j-1} has landed in TMEM
+                // O *= alpha, once P_{j-1} V_{j-1} has landed in TMEM; skipped when no
+                // row of the warp has a new maximum (alpha == 1 for all of them)
                 alive = warp_wait_all(&bars->o_done, (j - 1) & 1, abort_flag, dev_err);
                 if (!alive) break;
+            }
+            if (j > 0 && __any_sync(0xffffffffu, grew)) {
                 tc_fence_after();
                 const uint32_t oa = tmem + lane_addr + kOCol;
                 uint32_t ov[kHD];
