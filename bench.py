@@ -59,6 +59,7 @@ def parse():
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-encoder-layer", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     return ap.parse_args()
 
@@ -295,6 +296,44 @@ def main_madi(args, world, rank, local):
                 "fc1_ms": statistics.mean(launches[0::2]), "fc2_ms": statistics.mean(launches[1::2])}
     chunks_per_s = args.batch * world / (ms_step / 1e3)
 
+    # ---------------- one whole encoder layer at config 3's batch (8 chunks per GPU):
+    # LN, QKV / out / fc1 / fc2 Q8 GEMMs, tcgen05 flash attention, residual LNs;
+    # inputs resident, one CUDA graph per layer; the full 32-layer encoder's chunk
+    # rate is derived from it (conv stem and positional embedding not included)
+    enc_layer = None
+    if not args.no_encoder_layer:
+        from madi_b200 import encoder as enc_mod
+        EB = 8
+        layer = enc_mod.EncoderLayer(enc_mod.host_layer(seed=1), device=dev)
+        gx = torch.Generator(device=dev)
+        gx.manual_seed(55 + rank)
+        xl = torch.randn((EB * enc_mod.SEQ, D), device=dev, generator=gx)
+        pf = (torch.randn((EB * enc_mod.SEQ, D), device=dev, generator=gx) * 0.5).half()
+        with torch.cuda.stream(stream):
+            for _ in range(2):
+                layer.forward(xl, pf, layer.b2, stream=stream)
+            torch.cuda.synchronize()
+            gl = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gl, stream=stream, capture_error_mode="thread_local"):
+                layer.forward(xl, pf, layer.b2, stream=stream)
+            gl.replay()
+            torch.cuda.synchronize()
+            nl = 10
+            l0, l1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            l0.record(stream)
+            for _ in range(nl):
+                gl.replay()
+            l1.record(stream)
+            torch.cuda.synchronize()
+        ms_layer = max_over_ranks(world, l0.elapsed_time(l1) / nl)
+        fl = enc_mod.EncoderLayer.flops(EB)
+        enc_layer = {"chunks_per_gpu": EB, "ms_per_layer": ms_layer, "TFLOPs": fl / (ms_layer / 1e3) / 1e12,
+                     "flops_per_layer": fl,
+                     "encoder_32_layers_chunks_per_s": EB * world / (32 * ms_layer / 1e3),
+                     "note": "derived: 32 x one measured layer; conv stem and positional embedding not included"}
+        del gl, layer, xl, pf
+        torch.cuda.empty_cache()
+
     # ---------------- e2e through the public API with host buffers
     e2e = None
     if not args.no_e2e:
@@ -350,6 +389,7 @@ def main_madi(args, world, rank, local):
                 # 30 s chunks through one fc1 + fc2 pair per second (not the whole encoder)
                 "ffn_pair_chunks_per_s": chunks_per_s,
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "decode": decode,
+                "encoder_layer": enc_layer,
                 "clocks": clocks, "gpu_launches": 2 * K}
         print(json.dumps(line), flush=True)
 
