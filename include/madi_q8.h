@@ -245,6 +245,13 @@ int madi_layer_norm(const float *x, float *y, const float *gamma, const float *b
 int madi_emb_lookup_q8(const madi_q8w *emb, const uint32_t *tokens, const uint32_t *pos, int m,
                        int64_t tok_stride, int tok_len, float *out, void *stream);
 
+/* madi_emb_lookup_q8 followed by pos_embed_add_indirect (graph_helpers.metal:48-57)
+ * for m slots in one launch: out[s][i] = emb(tok)[i] + pos_emb[pos[s]][i] when
+ * pos[s] < max_pos (else the embedding alone).  pos_emb f32 [max_pos][emb->k]. */
+int madi_emb_pos_q8(const madi_q8w *emb, const uint32_t *tokens, const uint32_t *pos, int m,
+                    int64_t tok_stride, int tok_len, const float *pos_emb, int max_pos, float *out,
+                    void *stream);
+
 /* Greedy token per slot (argmax_conf, graph_helpers.metal:785-821): for slot s,
  * tokens[s*stride + pos[s]] = argmax(logits[s][0..vocab)) and, if conf != NULL,
  * conf[s*stride + pos[s]] = 1 / sum_i exp(logits[s][i] - max), when pos[s] < max_len.
@@ -259,6 +266,12 @@ int madi_argmax_conf(const float *logits, int m, int vocab, uint32_t *tokens, fl
 int madi_logit_filter(float *logits, int vocab, const uint32_t *past, int past_len,
                       const uint32_t *step, uint32_t sample_begin, uint32_t no_repeat_ngram,
                       void *stream);
+
+/* madi_logit_filter on m rows in one launch: row r filters logits + r*vocab with
+ * history past + r*past_stride (past_len tokens) and step[r]. */
+int madi_logit_filter_rows(float *logits, int m, int vocab, const uint32_t *past, int past_len,
+                           int64_t past_stride, const uint32_t *step, uint32_t sample_begin,
+                           uint32_t no_repeat_ngram, void *stream);
 
 /* ============================ decoder attention ============================== */
 

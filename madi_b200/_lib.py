@@ -60,8 +60,10 @@ SIGNATURES = {
     "madi_bias_res_ln": ([P, P, P, P, P, P, I, I, ctypes.c_float, P], I),
     "madi_layer_norm": ([P, P, P, P, I, I, ctypes.c_float, P], I),
     "madi_emb_lookup_q8": ([ctypes.POINTER(madi_q8w), P, P, I, ctypes.c_int64, I, P, P], I),
+    "madi_emb_pos_q8": ([ctypes.POINTER(madi_q8w), P, P, I, ctypes.c_int64, I, P, I, P, P], I),
     "madi_argmax_conf": ([P, I, I, P, P, P, I, ctypes.c_int64, P], I),
     "madi_logit_filter": ([P, I, P, I, P, U32, U32, P], I),
+    "madi_logit_filter_rows": ([P, I, I, P, I, ctypes.c_int64, P, U32, U32, P], I),
     "madi_step_advance": ([P, I, P], I),
     "madi_argmax_rows": ([P, I, I, P, P], I),
     "madi_shard_argmax": ([P, I, I, ctypes.c_int64, U32, P, P, P], I),

@@ -6,6 +6,7 @@ put under a profiler (ncu -k regex:<kernel> -s <skip> -c <count> ...).
     python -m madi_b200.cases cross --m 8 --n 1500 --k 1280 --iters 6   (slots, keys, kv_dim)
     python -m madi_b200.cases self --m 8 --n 448 --k 1280 --iters 6     (slots, cache rows, kv_dim)
     python -m madi_b200.cases flash --m 8 --n 1500 --k 1280 --iters 6    (chunks, seq, heads*64)
+    python -m madi_b200.cases decoder --m 8 --n 64 --k 1280 --iters 6    (slots, tokens decoded first, d)
 
 Inputs are seeded random tensors of the given shape (int8 weights in [-127, 127],
 f16 scales in [1e-4, 2.1e-3], N(0,1) activations); the script prints the mean
@@ -23,7 +24,7 @@ EPIS = {"none": q8.EPI_NONE, "bias": q8.EPI_BIAS, "gelu": q8.EPI_BIAS_GELU, "res
 
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    ap.add_argument("kind", choices=["gemv", "gemm", "cross", "self", "flash"])
+    ap.add_argument("kind", choices=["gemv", "gemm", "cross", "self", "flash", "decoder"])
     ap.add_argument("--m", type=int, required=True)
     ap.add_argument("--n", type=int, required=True)
     ap.add_argument("--k", type=int, required=True)
@@ -39,6 +40,8 @@ def main(argv=None):
         return attention_case(a, dev, g)
     if a.kind == "flash":
         return flash_case(a, dev, g)
+    if a.kind == "decoder":
+        return decoder_case(a, dev)
     W = q8.Q8Weight(torch.randint(-127, 128, (a.n, a.k), dtype=torch.int8, device=dev, generator=g),
                     (torch.rand((a.n, a.k // 32), device=dev, generator=g) * 2e-3 + 1e-4).half())
     xdt = torch.float32 if a.x == "f32" else torch.float16
@@ -124,6 +127,44 @@ def flash_case(a, dev, g):
         ts.append(e0.elapsed_time(e1) * 1e3)
     print(f"flash attention chunks={a.m} seq={a.n} heads={heads}: mean {sum(ts) / len(ts):.2f} us, min {min(ts):.2f} us, "
           f"{flops / min(ts) / 1e6:.1f} TFLOP/s at the min over {len(ts)} calls (after one untimed call)")
+
+
+def decoder_case(a, dev):
+    """The synthetic 4-layer greedy decoder (madi_b200/decoder.py) with --m slots: one
+    token step captured as a CUDA graph, replayed --n times untimed (the positions
+    reach n), then --iters timed replays."""
+    from . import decoder as dec
+    model = dec.Decoder(dec.host_weights(seed=1), a.m, device=dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    model.set_encoder(torch.randn((a.m, dec.ENC, dec.D), device=dev, generator=g).half())
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    model.reset()
+    with torch.cuda.stream(s):
+        model.step()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    model.reset()
+    torch.cuda.synchronize()
+    with torch.cuda.graph(graph):
+        model.step()
+    model.reset()
+    for _ in range(a.n):
+        graph.replay()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(a.iters):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1) * 1e3)
+    del graph
+    print(f"decoder slots={a.m} from position {a.n}: mean {sum(ts) / len(ts):.2f} us, min {min(ts):.2f} us per token "
+          f"step over {len(ts)} replays")
 
 
 if __name__ == "__main__":

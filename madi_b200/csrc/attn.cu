@@ -157,6 +157,8 @@ __global__ void __launch_bounds__(kThr) attn_kernel(const __grid_constant__ CUte
     const int tid = threadIdx.x;
     const int D = nh * kHd;
     const int kvh = h * nkv / nh;
+    pdl_trigger();
+    pdl_wait();                 // q, pos and the cache row at pos come from earlier kernels
     const int len = pos ? (pos[b] < (uint32_t)rows ? (int)pos[b] + 1 : rows) : rows;
     const int t0 = c * csz;
     int n = t0 < len ? min(csz, len - t0) : 0;
@@ -237,6 +239,234 @@ __global__ void __launch_bounds__(kThr) attn_kernel(const __grid_constant__ CUte
     }
 }
 
+// ---------------------------------------------------------------- streamed attention
+// The same (slot, head) clusters without the scores output, for any chunk size.
+// CTA c walks its rows [c * csz, c * csz + n) in stages of kR rows (64 for f16
+// K / V, 32 for f32: 16 KB of K and V per stage): a producer warp keeps a ring of
+// `stages` TMA slots in flight ([kR][64] K and V boxes), and each of the 8
+// consumer warps runs its own online softmax over its kR / 8 keys of every stage
+// -- running max m_w, sum l_w and the partial output over the 64 dims (2 per
+// lane), rescaled by exp2((m_old - m_new) log2 e) when m_w grows -- with no
+// block-wide barrier per stage.  8 lanes form a key's score (4 keys per pass).
+// At the end the warps' (m, l, o) and then the cluster's CTAs are recombined by
+// log-sum-exp, as flash_cross_attn_reduce does.
+constexpr int kMaxStages = 8;
+constexpr int kThrS = 288;                                 // 8 consumer warps + 1 producer warp
+
+template <typename KV>
+MADI_DEV float dot8(const KV *kr, int li, const float (&qv)[8]);
+template <>
+MADI_DEV float dot8<__half>(const __half *kr, int li, const float (&qv)[8]) {
+    const uint4 u = *reinterpret_cast<const uint4 *>(kr + 8 * li);           // dims 8li .. 8li+7
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+    float d = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&w[i]));
+        d = fmaf(qv[2 * i], f.x, d);
+        d = fmaf(qv[2 * i + 1], f.y, d);
+    }
+    return d;
+}
+template <>
+MADI_DEV float dot8<float>(const float *kr, int li, const float (&qv)[8]) {
+    const float4 a = *reinterpret_cast<const float4 *>(kr + 4 * li);         // dims 4li .. 4li+3
+    const float4 b = *reinterpret_cast<const float4 *>(kr + 32 + 4 * li);    // dims 32+4li .. 32+4li+3
+    float d = qv[0] * a.x;
+    d = fmaf(qv[1], a.y, d);
+    d = fmaf(qv[2], a.z, d);
+    d = fmaf(qv[3], a.w, d);
+    d = fmaf(qv[4], b.x, d);
+    d = fmaf(qv[5], b.y, d);
+    d = fmaf(qv[6], b.z, d);
+    d = fmaf(qv[7], b.w, d);
+    return d;
+}
+// The q dims lane li multiplies in dot8.
+template <typename KV> MADI_DEV int q_dim(int li, int i);
+template <> MADI_DEV int q_dim<__half>(int li, int i) { return 8 * li + i; }
+template <> MADI_DEV int q_dim<float>(int li, int i) { return i < 4 ? 4 * li + i : 32 + 4 * li + (i - 4); }
+
+template <typename KV> struct StreamRows { static constexpr int kR = sizeof(KV) == 2 ? 64 : 32; };
+
+template <typename KV>
+__global__ void __launch_bounds__(kThrS, 4) attn_stream_kernel(const __grid_constant__ CUtensorMap tmK,
+                                                            const __grid_constant__ CUtensorMap tmV,
+                                                            float *__restrict__ out, const float *__restrict__ q,
+                                                            const uint32_t *__restrict__ pos, int rows, int nkv,
+                                                            int nh, int ns, int csz, int stages, int *dev_err) {
+    constexpr int kR = StreamRows<KV>::kR;
+    constexpr int kBox = kR * kHd;                        // elements per K (or V) box
+    constexpr int kPasses = kR / 32;                      // 4 keys per warp per pass, 8 warps
+    extern __shared__ uint8_t attn_smem[];
+    KV *ring = reinterpret_cast<KV *>((reinterpret_cast<uintptr_t>(attn_smem) + 127) & ~uintptr_t(127));
+    __shared__ float qh[kHd];
+    __shared__ float wm[8], wl[8];
+    __shared__ float wo[8][kHd];
+    __shared__ float part[8][2 + kHd];
+    __shared__ __align__(8) uint64_t full[kMaxStages];
+    __shared__ __align__(8) uint64_t empty[kMaxStages];
+    __shared__ int abort_flag;
+    const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int D = nh * kHd;
+    const int kvh = h * nkv / nh;
+    pdl_trigger();
+    pdl_wait();                 // q, pos and the cache row at pos come from earlier kernels
+    const int len = pos ? (pos[b] < (uint32_t)rows ? (int)pos[b] + 1 : rows) : rows;
+    const int t0 = c * csz;
+    const int n = t0 < len ? min(csz, len - t0) : 0;
+    const int nsub = (n + kR - 1) / kR;
+    if (ns > 1) asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
+    if (tid == 0) {
+        abort_flag = 0;
+        for (int i = 0; i < stages; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 8);
+        }
+        fence_mbar_init();
+    }
+    if (tid < kHd) qh[tid] = q[(size_t)b * D + h * kHd + tid];
+    __syncthreads();
+
+    float m_w = -INFINITY, l_w = 0.f, o0 = 0.f, o1 = 0.f;
+    if (warp == 8) {
+        // ------------------------------------------------ producer
+        if (lane == 0) {
+            const uint32_t tx = 2u * kBox * (uint32_t)sizeof(KV);
+            int issued = 0;
+            for (int j = 0; j < nsub; ++j) {
+                const int s = j % stages;
+                if (j >= stages && !mbar_wait(&empty[s], (uint32_t)(j / stages - 1) & 1u, &abort_flag, dev_err)) break;
+                KV *ks = ring + (size_t)s * 2 * kBox;
+                mbar_arrive_expect_tx(&full[s], tx);
+                tma_load_2d(ks, &tmK, &full[s], kvh * kHd, b * rows + t0 + j * kR);
+                tma_load_2d(ks + kBox, &tmV, &full[s], kvh * kHd, b * rows + t0 + j * kR);
+                issued = j + 1;
+            }
+            // the copies issued last land before the CTA can exit
+            for (int i = issued > stages ? issued - stages : 0; i < issued; ++i) {
+                const long long tw = clock64();
+                while (!mbar_try_wait(&full[i % stages], (uint32_t)(i / stages) & 1u))
+                    if (clock64() - tw > kWaitBudgetCycles) break;
+            }
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------------------------ consumers
+        const int li = lane & 7, kq = lane >> 3;          // 8 lanes per key, 4 keys per pass
+        float qv[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) qv[i] = qh[q_dim<KV>(li, i)];
+        const float rsq = rsqrtf((float)kHd);
+        const int kb = warp * (kR / 8);                   // this warp's keys in each stage
+        for (int j = 0; j < nsub; ++j) {
+            const int s = j % stages;
+            if (!warp_wait_all(&full[s], (uint32_t)(j / stages) & 1u, &abort_flag, dev_err)) {
+                m_w = -INFINITY;                          // contribute nothing after a failed copy
+                break;
+            }
+            const int rj = min(kR, n - j * kR);
+            const KV *ks = ring + (size_t)s * 2 * kBox;
+            const KV *vs = ks + kBox;
+            float sc[kPasses];
+            float mx = -INFINITY;
+#pragma unroll
+            for (int p = 0; p < kPasses; ++p) {
+                const int k = kb + 4 * p + kq;
+                float d = k < rj ? dot8<KV>(ks + (size_t)k * kHd, li, qv) : 0.f;
+                d += __shfl_xor_sync(0xffffffffu, d, 4);
+                d += __shfl_xor_sync(0xffffffffu, d, 2);
+                d += __shfl_xor_sync(0xffffffffu, d, 1);
+                sc[p] = k < rj ? d * rsq : -INFINITY;
+                mx = fmaxf(mx, sc[p]);
+            }
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+            if (mx > -INFINITY) {                         // warp-uniform: this warp has keys here
+                const float m_new = fmaxf(m_w, mx);
+                const float alpha = exp2f((m_w - m_new) * kLog2e);
+                m_w = m_new;
+                l_w *= alpha;
+                o0 *= alpha;
+                o1 *= alpha;
+#pragma unroll
+                for (int p = 0; p < kPasses; ++p) {
+                    const float e = exp2f((sc[p] - m_w) * kLog2e);     // 0 for a missing key
+                    l_w += e;                                         // per key group; summed below
+#pragma unroll
+                    for (int g = 0; g < 4; ++g) {
+                        const int k = kb + 4 * p + g;
+                        const float ek = __shfl_sync(0xffffffffu, e, 8 * g);
+                        if (k < rj) {
+                            const float2 v = ld2(vs + (size_t)k * kHd + 2 * lane);
+                            o0 = fmaf(ek, v.x, o0);
+                            o1 = fmaf(ek, v.y, o1);
+                        }
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+        }
+        // l_w holds the sum of one key group; the 8 lanes of a group agree
+        l_w += __shfl_xor_sync(0xffffffffu, l_w, 8);
+        l_w += __shfl_xor_sync(0xffffffffu, l_w, 16);
+        wo[warp][2 * lane] = o0;
+        wo[warp][2 * lane + 1] = o1;
+        if (lane == 0) {
+            wm[warp] = m_w;
+            wl[warp] = l_w;
+        }
+    }
+    __syncthreads();
+    // this CTA's (m, l, o): the warps' partials by log-sum-exp
+    float cm = -INFINITY;
+#pragma unroll
+    for (int w8 = 0; w8 < 8; ++w8) cm = fmaxf(cm, wm[w8]);
+    float cl = 0.f, co = 0.f;
+    if (tid < kHd) {
+#pragma unroll
+        for (int w8 = 0; w8 < 8; ++w8) {
+            if (wm[w8] > -INFINITY) {
+                const float f = exp2f((wm[w8] - cm) * kLog2e);
+                cl += wl[w8] * f;
+                co += wo[w8][tid] * f;
+            }
+        }
+    }
+
+    float *p0 = &part[0][0];
+    if (ns > 1) {
+        asm volatile("barrier.cluster.wait;" ::: "memory");
+        p0 = cg::this_cluster().map_shared_rank(&part[0][0], 0);
+    }
+    if (tid < kHd) p0[c * (2 + kHd) + 2 + tid] = co;
+    if (tid == 0) {
+        p0[c * (2 + kHd)] = cm;
+        p0[c * (2 + kHd) + 1] = cl;
+    }
+    if (ns > 1) {
+        asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+    } else {
+        __syncthreads();
+    }
+    if (c == 0) {
+        float gm = -INFINITY;
+        for (int r = 0; r < ns; ++r) gm = fmaxf(gm, part[r][0]);
+        float gs = 0.f;
+        for (int r = 0; r < ns; ++r)
+            if (part[r][0] > -INFINITY) gs += part[r][1] * exp2f((part[r][0] - gm) * kLog2e);
+        const float inv = 1.0f / gs;
+        if (tid < kHd) {
+            float acc = 0.f;
+            for (int r = 0; r < ns; ++r)
+                if (part[r][0] > -INFINITY) acc += part[r][2 + tid] * exp2f((part[r][0] - gm) * kLog2e);
+            out[(size_t)b * D + h * kHd + tid] = acc * inv;
+        }
+    }
+}
+
 // Two-pass form with caller-owned partials part[head][nsplit][2 + 64] (m, s, o):
 // pass 1, grid (nsplit, heads); raw scores to sc_raw[head][seqlen] when asked.
 template <typename KV>
@@ -249,6 +479,8 @@ __global__ void __launch_bounds__(kThr) cross_attn_part_kernel(float *__restrict
     __shared__ float s8[8];
     __shared__ float red[8][kHd];
     const int c = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+    pdl_trigger();
+    pdl_wait();
     const int kvh = h * nkv / nh;
     const int csz = (seqlen + nsplit - 1) / nsplit;
     const int t0 = c * csz;
@@ -287,6 +519,8 @@ __global__ void __launch_bounds__(kThr) cross_attn_reduce_kernel(float *__restri
                                                                  int nsplit, float *__restrict__ sc, int seqlen,
                                                                  int write_sc) {
     const int h = blockIdx.x, tid = threadIdx.x;
+    pdl_trigger();
+    pdl_wait();
     const float *hp = part + (size_t)h * nsplit * (2 + kHd);
     float gm = -INFINITY;
     for (int c = 0; c < nsplit; ++c) gm = fmaxf(gm, hp[c * (2 + kHd)]);
@@ -344,19 +578,57 @@ cudaError_t launch_attn_t(const void *kc, const void *vc, float *out, const floa
         if (e != cudaSuccess) return e;
         attr = true;
     }
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(ns, nh, slots);
-    cfg.blockDim = dim3(kThr);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = st;
-    cudaLaunchAttribute at[1];
-    at[0].id = cudaLaunchAttributeClusterDimension;
-    at[0].val.clusterDim.x = ns;
-    at[0].val.clusterDim.y = 1;
-    at[0].val.clusterDim.z = 1;
-    cfg.attrs = at;
-    cfg.numAttrs = ns > 1 ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, fn, tmK, tmV, out, q, sc, pos, rows, nkv, nh, ns, csz, dev_err);
+    return launch_k(fn, dim3(ns, nh, slots), kThr, smem, st, ns, tmK, tmV, out, q, sc, pos, rows, nkv, nh, ns, csz,
+                    dev_err);
+}
+
+// One wave: the largest ns (<= 8, >= 2 stages of rows per CTA) whose
+// slots x heads x ns CTAs all fit at once, with the ring sized to the shared
+// memory the resident CTAs leave (2..8 slots of 16 KB) and the fit checked against
+// the occupancy the kernel really gets at that size.
+template <typename KV>
+cudaError_t launch_attn_stream(const void *kc, const void *vc, float *out, const float *q, const uint32_t *pos,
+                               int slots, int rows, int kvd, int nkv, int nh, int *dev_err, cudaStream_t st) {
+    constexpr int kR = StreamRows<KV>::kR;
+    const size_t stage_bytes = 2 * (size_t)kR * kHd * sizeof(KV);
+    auto fn = attn_stream_kernel<KV>;
+    static int occ[kMaxStages + 1] = {0};                 // resident CTAs per SM by ring depth
+    if (!occ[kMaxStages]) {
+        cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)(128 + kMaxStages * stage_bytes));
+        if (e != cudaSuccess) return e;
+        for (int sg = 2; sg <= kMaxStages; ++sg) {
+            int nb = 0;
+            e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, fn, kThrS, 128 + sg * stage_bytes);
+            if (e != cudaSuccess) return e;
+            occ[sg] = nb > 0 ? nb : 1;
+        }
+    }
+    const int sms = num_sms();
+    const long pairs = (long)slots * nh;
+    int ns = 1, stages = 2;
+    for (int cand = 8; cand >= 1; cand /= 2) {
+        if (cand > 1 && (rows + cand - 1) / cand < 2 * kR) continue;
+        const long per_sm = (pairs * cand + sms - 1) / sms;
+        if (per_sm > 16) continue;
+        const size_t budget = (size_t)(220 * 1024) / (size_t)per_sm;
+        const size_t reserve = 8 * 1024;                 // static shared memory and alignment
+        int sg = budget > reserve ? (int)((budget - reserve) / stage_bytes) : 2;
+        sg = sg < 2 ? 2 : (sg > kMaxStages ? kMaxStages : sg);
+        if (occ[sg] >= per_sm || cand == 1) {
+            ns = cand;
+            stages = sg;
+            break;
+        }
+    }
+    const int csz = (rows + ns - 1) / ns;
+    CUtensorMap tmK, tmV;
+    const bool f16 = sizeof(KV) == 2;
+    if (!attn_map(&tmK, kc, f16, (uint64_t)slots * rows, kvd, kR) ||
+        !attn_map(&tmV, vc, f16, (uint64_t)slots * rows, kvd, kR))
+        return cudaErrorNotSupported;
+    return launch_k(fn, dim3(ns, nh, slots), kThrS, 128 + stages * stage_bytes, st, ns, tmK, tmV, out, q, pos, rows,
+                    nkv, nh, ns, csz, stages, dev_err);
 }
 
 }  // namespace
@@ -371,11 +643,9 @@ cudaError_t launch_cross_attn(float *out, const float *q, const void *kc, const 
                               int slots, int seqlen, int kvd, int nkv, int nh, int *dev_err, cudaStream_t st) {
     if (kv_f16)
         return scores ? launch_attn_t<__half, true>(kc, vc, out, q, scores, nullptr, slots, seqlen, kvd, nkv, nh, dev_err, st)
-                      : launch_attn_t<__half, false>(kc, vc, out, q, nullptr, nullptr, slots, seqlen, kvd, nkv, nh,
-                                                     dev_err, st);
+                      : launch_attn_stream<__half>(kc, vc, out, q, nullptr, slots, seqlen, kvd, nkv, nh, dev_err, st);
     return scores ? launch_attn_t<float, true>(kc, vc, out, q, scores, nullptr, slots, seqlen, kvd, nkv, nh, dev_err, st)
-                  : launch_attn_t<float, false>(kc, vc, out, q, nullptr, nullptr, slots, seqlen, kvd, nkv, nh, dev_err,
-                                                st);
+                  : launch_attn_stream<float>(kc, vc, out, q, nullptr, slots, seqlen, kvd, nkv, nh, dev_err, st);
 }
 
 cudaError_t launch_cross_attn_part(float *part, const float *q, const void *kc, const void *vc, bool kv_f16,
@@ -383,27 +653,22 @@ cudaError_t launch_cross_attn_part(float *part, const float *q, const void *kc, 
                                    cudaStream_t st) {
     const dim3 grid(nsplit, nh);
     if (kv_f16)
-        cross_attn_part_kernel<__half><<<grid, kThr, 0, st>>>(part, q, static_cast<const __half *>(kc),
-                                                              static_cast<const __half *>(vc), sc_raw, write_sc,
-                                                              seqlen, kvd, nkv, nh, nsplit);
-    else
-        cross_attn_part_kernel<float><<<grid, kThr, 0, st>>>(part, q, static_cast<const float *>(kc),
-                                                             static_cast<const float *>(vc), sc_raw, write_sc, seqlen,
-                                                             kvd, nkv, nh, nsplit);
-    return cudaGetLastError();
+        return launch_k(cross_attn_part_kernel<__half>, grid, kThr, 0, st, 1, part, q, static_cast<const __half *>(kc),
+                        static_cast<const __half *>(vc), sc_raw, write_sc, seqlen, kvd, nkv, nh, nsplit);
+    return launch_k(cross_attn_part_kernel<float>, grid, kThr, 0, st, 1, part, q, static_cast<const float *>(kc),
+                    static_cast<const float *>(vc), sc_raw, write_sc, seqlen, kvd, nkv, nh, nsplit);
 }
 
 cudaError_t launch_cross_attn_reduce(float *out, const float *part, int nsplit, float *sc, int seqlen, int write_sc,
                                      int nh, cudaStream_t st) {
-    cross_attn_reduce_kernel<<<nh, kThr, 0, st>>>(out, part, nsplit, sc, seqlen, write_sc);
-    return cudaGetLastError();
+    return launch_k(cross_attn_reduce_kernel, nh, kThr, 0, st, 1, out, part, nsplit, sc, seqlen, write_sc);
 }
 
 cudaError_t launch_self_attn(float *out, const float *q, const void *kc, const void *vc, bool kv_f16,
                              const uint32_t *pos, int slots, int kvd, int nkv, int nh, int max_tok, int *dev_err,
                              cudaStream_t st) {
-    return kv_f16 ? launch_attn_t<__half, false>(kc, vc, out, q, nullptr, pos, slots, max_tok, kvd, nkv, nh, dev_err, st)
-                  : launch_attn_t<float, false>(kc, vc, out, q, nullptr, pos, slots, max_tok, kvd, nkv, nh, dev_err, st);
+    return kv_f16 ? launch_attn_stream<__half>(kc, vc, out, q, pos, slots, max_tok, kvd, nkv, nh, dev_err, st)
+                  : launch_attn_stream<float>(kc, vc, out, q, pos, slots, max_tok, kvd, nkv, nh, dev_err, st);
 }
 
 }  // namespace madi

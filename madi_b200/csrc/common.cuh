@@ -39,6 +39,16 @@ MADI_DEV void q8_to_half2x2(uint32_t w, __half2 &lo, __half2 &hi) {
 
 MADI_DEV uint32_t h2_as_u32(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
 
+// ------------------------------------------------------ programmatic dependent launch
+// A kernel launched with programmatic stream serialization may start while the
+// kernel before it still runs.  pdl_wait() blocks until that kernel has finished
+// and its writes are visible (a no-op without the launch attribute); every kernel
+// launched that way calls it on every path before reading data another kernel
+// wrote and before it can finish, so completion stays ordered along the stream.
+// pdl_trigger() lets the next kernel of the stream start launching.
+MADI_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+MADI_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // 0.5 x (1 + erf(x / sqrt 2)), erf from A&S 7.1.26 (|eps| <= 1.5e-7) with
 // exp2(max(-z^2 log2 e, -80)): the reference's GELU formula, restated.
 // Written as 0.5 x + 0.5 |x| erf(|z|) (erf is odd, so sign(x) x = |x|).  The

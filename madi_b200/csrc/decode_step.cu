@@ -9,6 +9,7 @@
 //   gpu_emb_lookup_q8       same, tok = *tok_ptr                           (:370-383)
 //   emb_lookup_indirect     out[i] = float(emb_f16[tok*dim+i])             (:12-23)
 //   pos_embed_add_indirect  out[i] += pos_emb[*pos*dim+i]                  (:48-57)
+//                           (fused into the Q8 lookup for m slots when pos_emb is given)
 //   step_advance            *pos += 1                                      (:60-62)
 //   argmax_no_inc           tokens[*pos] = argmax(logits)                  (:64-95)
 //   argmax_conf             + conf[*pos] = 1 / sum exp(z - zmax)           (:785-821)
@@ -33,28 +34,40 @@ constexpr float kNeg = -3.4e38f;
 
 // Every index that comes from device memory (a position, a token) is checked
 // against the length the host derived for its buffer before it is used.
+// pos_emb (optional): out[s][i] = emb + pos_emb[pos[s]][i] when pos[s] < max_pos (the
+// reference's lookup followed by pos_embed_add_indirect; one f32 add, same result).
 __global__ void emb_q8_kernel(float *__restrict__ out, const int8_t *__restrict__ qs, const __half *__restrict__ scales,
                               const uint32_t *__restrict__ tokens, const uint32_t *__restrict__ pos, int dim,
-                              int rows, int m, long long tok_stride, long long tok_len) {
+                              int rows, int m, long long tok_stride, long long tok_len,
+                              const float *__restrict__ pos_emb, int max_pos) {
     const int s = blockIdx.y;                       // token slot
+    pdl_trigger();
+    pdl_wait();
     if (s >= m) return;
     const uint32_t p = pos ? pos[s] : 0u;
     const uint32_t tok = (long long)p < tok_len ? tokens[(size_t)s * tok_stride + p] : 0xffffffffu;
     const int nb = dim >> 5;
     float *o = out + (size_t)s * dim;
     if (tok >= (uint32_t)rows) {                    // out-of-range position or token: zeros, no stray read
-        for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < dim; i += gridDim.x * blockDim.x) o[i] = 0.f;
+        const float *pz = (pos_emb && p < (uint32_t)max_pos) ? pos_emb + (size_t)p * dim : nullptr;
+        for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < dim; i += gridDim.x * blockDim.x)
+            o[i] = pz ? 0.f + pz[i] : 0.f;
         return;
     }
     const int8_t *qr = qs + (size_t)tok * dim;
     const __half *sr = scales + (size_t)tok * nb;
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < dim; i += gridDim.x * blockDim.x)
-        o[i] = (float)qr[i] * __half2float(sr[i >> 5]);
+    const float *pe = (pos_emb && p < (uint32_t)max_pos) ? pos_emb + (size_t)p * dim : nullptr;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < dim; i += gridDim.x * blockDim.x) {
+        const float e = (float)qr[i] * __half2float(sr[i >> 5]);
+        o[i] = pe ? e + pe[i] : e;
+    }
 }
 
 __global__ void emb_f16_kernel(float *__restrict__ out, const __half *__restrict__ emb,
                                const uint32_t *__restrict__ tokens, const uint32_t *__restrict__ pos, int dim, int rows,
                                long long tok_len) {
+    pdl_trigger();
+    pdl_wait();
     const uint32_t p = pos[0];
     const uint32_t tok = (long long)p < tok_len ? tokens[p] : 0xffffffffu;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < dim; i += gridDim.x * blockDim.x)
@@ -63,6 +76,8 @@ __global__ void emb_f16_kernel(float *__restrict__ out, const __half *__restrict
 
 __global__ void pos_add_kernel(float *__restrict__ out, const float *__restrict__ pos_emb,
                                const uint32_t *__restrict__ pos, int dim, int max_pos) {
+    pdl_trigger();
+    pdl_wait();
     const uint32_t p = pos[0];
     if (p >= (uint32_t)max_pos) return;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < dim; i += gridDim.x * blockDim.x)
@@ -70,6 +85,8 @@ __global__ void pos_add_kernel(float *__restrict__ out, const float *__restrict_
 }
 
 __global__ void step_advance_kernel(uint32_t *pos, int m) {
+    pdl_trigger();
+    pdl_wait();
     const int s = threadIdx.x;
     if (s < m) pos[s] += 1;
 }
@@ -82,9 +99,14 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float *__restrict__ 
     __shared__ float sv[1024];
     __shared__ uint32_t si[1024];
     const int t = threadIdx.x, s = blockIdx.x;
+    pdl_trigger();
+    pdl_wait();
     const float *lg = logits + (size_t)s * V;
     float lm = -INFINITY;
     uint32_t li = 0;
+    // unrolled so that a thread's loads are in flight together; the compares still
+    // run in index order
+#pragma unroll 8
     for (int i = t; i < V; i += 1024) {
         const float v = lg[i];
         if (v > lm) { lm = v; li = (uint32_t)i; }
@@ -102,6 +124,7 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float *__restrict__ 
     if constexpr (kConf) {
         __syncthreads();
         float ls = 0.f;
+#pragma unroll 8
         for (int i = t; i < V; i += 1024) ls += expf(lg[i] - zmax);
         sv[t] = ls;
         __syncthreads();
@@ -122,18 +145,26 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float *__restrict__ 
 
 __global__ void suppress_kernel(float *__restrict__ logits, const uint32_t *__restrict__ ids, int n, int V) {
     const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    pdl_trigger();
+    pdl_wait();
     if (j >= n) return;
     const uint32_t t = ids[j];
     if (t < (uint32_t)V) logits[t] = kNeg;
 }
 
-// logit_filter_indirect (graph_helpers.metal:109-160): one CTA of 256 threads.
+// logit_filter_indirect (graph_helpers.metal:109-160): one CTA of 256 threads per
+// logits row; row r uses logits + r * V, past + r * past_stride and step_ptr[r].
 __global__ void __launch_bounds__(256) logit_filter_kernel(float *__restrict__ logits,
                                                            const uint32_t *__restrict__ past,
                                                            const uint32_t *__restrict__ step_ptr, uint32_t sample_begin,
-                                                           uint32_t no_repeat_ngram, int V, int past_len) {
+                                                           uint32_t no_repeat_ngram, int V, int past_len,
+                                                           long long past_stride) {
     const uint32_t i = threadIdx.x;
-    const uint32_t step = step_ptr[0];
+    pdl_trigger();
+    pdl_wait();
+    logits += (size_t)blockIdx.x * V;
+    past += (size_t)blockIdx.x * past_stride;
+    const uint32_t step = step_ptr[blockIdx.x];
     // the history reads below stay inside past[0 .. past_len)
     const bool hist_ok = step <= (uint32_t)past_len;
     if (i == 0 && hist_ok && step >= 3 && step >= sample_begin + 3) {
@@ -181,9 +212,12 @@ __global__ void __launch_bounds__(1024) shard_argmax_kernel(const float *__restr
     __shared__ float sv[1024];
     __shared__ uint64_t sk[1024];
     const int t = threadIdx.x, row = blockIdx.x;
+    pdl_trigger();
+    pdl_wait();
     const float *lg = logits + (size_t)row * row_stride;
     float bv = -INFINITY;
     uint64_t bk = ~0ull;
+#pragma unroll 8
     for (int i = t; i < n; i += 1024) {
         const float v = lg[i];
         const uint64_t k = tie_key(h0 + (uint32_t)i);
@@ -207,6 +241,8 @@ __global__ void __launch_bounds__(1024) shard_argmax_kernel(const float *__restr
 __global__ void merge_argmax_kernel(const float *__restrict__ vals, const uint32_t *__restrict__ idx, int world, int m,
                                     uint32_t *__restrict__ tokens) {
     const int row = blockIdx.x * blockDim.x + threadIdx.x;
+    pdl_trigger();
+    pdl_wait();
     if (row >= m) return;
     float bv = vals[row];
     uint32_t bi = idx[row];
@@ -222,59 +258,51 @@ __global__ void merge_argmax_kernel(const float *__restrict__ vals, const uint32
 
 cudaError_t launch_emb_q8(float *out, const int8_t *qs, const __half *scales, const uint32_t *tokens,
                           const uint32_t *pos, int dim, int rows, int m, long long tok_stride, long long tok_len,
-                          cudaStream_t st) {
-    emb_q8_kernel<<<dim3((dim + 255) / 256, m), 256, 0, st>>>(out, qs, scales, tokens, pos, dim, rows, m, tok_stride,
-                                                             tok_len);
-    return cudaGetLastError();
+                          const float *pos_emb, int max_pos, cudaStream_t st) {
+    return launch_k(emb_q8_kernel, dim3((dim + 255) / 256, m), 256, 0, st, 1, out, qs, scales, tokens, pos, dim, rows, m,
+                    tok_stride, tok_len, pos_emb, max_pos);
 }
 
 cudaError_t launch_emb_f16(float *out, const __half *emb, const uint32_t *tokens, const uint32_t *pos, int dim,
                            int rows, long long tok_len, cudaStream_t st) {
-    emb_f16_kernel<<<(dim + 255) / 256, 256, 0, st>>>(out, emb, tokens, pos, dim, rows, tok_len);
-    return cudaGetLastError();
+    return launch_k(emb_f16_kernel, (dim + 255) / 256, 256, 0, st, 1, out, emb, tokens, pos, dim, rows, tok_len);
 }
 
 cudaError_t launch_pos_add(float *out, const float *pos_emb, const uint32_t *pos, int dim, int max_pos,
                            cudaStream_t st) {
-    pos_add_kernel<<<(dim + 255) / 256, 256, 0, st>>>(out, pos_emb, pos, dim, max_pos);
-    return cudaGetLastError();
+    return launch_k(pos_add_kernel, (dim + 255) / 256, 256, 0, st, 1, out, pos_emb, pos, dim, max_pos);
 }
 
 cudaError_t launch_step_advance(uint32_t *pos, int m, cudaStream_t st) {
-    step_advance_kernel<<<1, 32, 0, st>>>(pos, m);
-    return cudaGetLastError();
+    return launch_k(step_advance_kernel, 1, 32, 0, st, 1, pos, m);
 }
 
 cudaError_t launch_argmax(const float *logits, uint32_t *tokens, float *conf, const uint32_t *pos, int V,
                           int max_len, int m, long long stride, cudaStream_t st) {
-    if (conf)
-        argmax_kernel<true><<<m, 1024, 0, st>>>(logits, tokens, conf, pos, V, max_len, stride);
-    else
-        argmax_kernel<false><<<m, 1024, 0, st>>>(logits, tokens, nullptr, pos, V, max_len, stride);
-    return cudaGetLastError();
+    return conf ? launch_k(argmax_kernel<true>, m, 1024, 0, st, 1, logits, tokens, conf, pos, V, max_len, stride)
+                : launch_k(argmax_kernel<false>, m, 1024, 0, st, 1, logits, tokens, static_cast<float *>(nullptr), pos,
+                           V, max_len, stride);
 }
 
 cudaError_t launch_suppress(float *logits, const uint32_t *ids, int n, int V, cudaStream_t st) {
-    if (n > 0) suppress_kernel<<<(n + 255) / 256, 256, 0, st>>>(logits, ids, n, V);
-    return cudaGetLastError();
+    return n > 0 ? launch_k(suppress_kernel, (n + 255) / 256, 256, 0, st, 1, logits, ids, n, V) : cudaSuccess;
 }
 
 cudaError_t launch_logit_filter(float *logits, const uint32_t *past, const uint32_t *step_ptr, uint32_t sample_begin,
-                                uint32_t no_repeat_ngram, int V, int past_len, cudaStream_t st) {
-    logit_filter_kernel<<<1, 256, 0, st>>>(logits, past, step_ptr, sample_begin, no_repeat_ngram, V, past_len);
-    return cudaGetLastError();
+                                uint32_t no_repeat_ngram, int V, int past_len, int rows, long long past_stride,
+                                cudaStream_t st) {
+    return launch_k(logit_filter_kernel, rows, 256, 0, st, 1, logits, past, step_ptr, sample_begin, no_repeat_ngram, V,
+                    past_len, past_stride);
 }
 
 cudaError_t launch_shard_argmax(const float *logits, long long row_stride, int n, uint32_t h0, int m, float *vals,
                                 uint32_t *idx, cudaStream_t st) {
-    shard_argmax_kernel<<<m, 1024, 0, st>>>(logits, row_stride, n, h0, vals, idx);
-    return cudaGetLastError();
+    return launch_k(shard_argmax_kernel, m, 1024, 0, st, 1, logits, row_stride, n, h0, vals, idx);
 }
 
 cudaError_t launch_merge_argmax(const float *vals, const uint32_t *idx, int world, int m, uint32_t *tokens,
                                 cudaStream_t st) {
-    merge_argmax_kernel<<<(m + 127) / 128, 128, 0, st>>>(vals, idx, world, m, tokens);
-    return cudaGetLastError();
+    return launch_k(merge_argmax_kernel, (m + 127) / 128, 128, 0, st, 1, vals, idx, world, m, tokens);
 }
 
 }  // namespace madi

@@ -9,6 +9,38 @@
 
 namespace madi {
 
+// Whether launches use programmatic dependent launch (MADI_PDL=0 turns it off).
+bool pdl_on();
+// Streaming multiprocessors of the current device.
+int num_sms();
+
+// cudaLaunchKernelEx with the programmatic-serialization attribute (when on) and
+// an optional cluster width along x.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*fn)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, int cluster_x,
+                     Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[2];
+    int na = 0;
+    at[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[na].val.programmaticStreamSerializationAllowed = pdl_on() ? 1 : 0;
+    ++na;
+    if (cluster_x > 1) {
+        at[na].id = cudaLaunchAttributeClusterDimension;
+        at[na].val.clusterDim.x = cluster_x;
+        at[na].val.clusterDim.y = 1;
+        at[na].val.clusterDim.z = 1;
+        ++na;
+    }
+    cfg.attrs = at;
+    cfg.numAttrs = na;
+    return cudaLaunchKernelEx(&cfg, fn, args...);
+}
+
 enum : int { kEpiNone = 0, kEpiBias = 1, kEpiBiasGelu = 2, kEpiBiasRes = 3 };
 // Tensor-core path only: no epilogue, f32 output (logits of a vocab head with
 // more than 8 token slots).
@@ -71,7 +103,7 @@ constexpr int kWhisperVocab = 51866;   // VOCAB of graph_helpers.metal:9 (the by
 // tok_len: entries readable per slot row of `tokens`; rows: embedding rows.
 cudaError_t launch_emb_q8(float *out, const int8_t *qs, const __half *scales, const uint32_t *tokens,
                           const uint32_t *pos, int dim, int rows, int m, long long tok_stride, long long tok_len,
-                          cudaStream_t st);
+                          const float *pos_emb, int max_pos, cudaStream_t st);
 cudaError_t launch_emb_f16(float *out, const __half *emb, const uint32_t *tokens, const uint32_t *pos, int dim,
                            int rows, long long tok_len, cudaStream_t st);
 cudaError_t launch_pos_add(float *out, const float *pos_emb, const uint32_t *pos, int dim, int max_pos, cudaStream_t st);
@@ -80,7 +112,8 @@ cudaError_t launch_argmax(const float *logits, uint32_t *tokens, float *conf, co
                           int m, long long stride, cudaStream_t st);
 cudaError_t launch_suppress(float *logits, const uint32_t *ids, int n, int V, cudaStream_t st);
 cudaError_t launch_logit_filter(float *logits, const uint32_t *past, const uint32_t *step_ptr, uint32_t sample_begin,
-                                uint32_t no_repeat_ngram, int V, int past_len, cudaStream_t st);
+                                uint32_t no_repeat_ngram, int V, int past_len, int rows, long long past_stride,
+                                cudaStream_t st);
 // ---- decoder attention (attn.cu); head_dim 64
 constexpr int kAttnMaxChunk = 256;   // keys per CTA of a cross-attention cluster (seqlen <= 8 * 256)
 constexpr int kAttnMaxTok = 512;     // self-attention keys per slot

@@ -83,7 +83,7 @@ size_t plan_smem(int M, const TilePlan &pl, bool x_f32) {
 // Launch plan.  Split K over a cluster when the units then still fit one wave at
 // two CTAs per SM (more CTAs streaming, fewer blocks per warp); otherwise one CTA
 // per unit, persistent when units outnumber the CTA slots.  Two CTAs per SM when
-// shared memory allows, else one.
+// shared memory allows, else one.  Last resort, a K split over more than a wave.
 bool make_plan(int M, int N, int K, bool x_f32, int num_sms, TilePlan *pl, int *grid) {
     if (M < 1 || M > 8 || N < 1 || K < 256 || K % 256 != 0) return false;
     const int tiles = (N + kTileRows - 1) / kTileRows;
@@ -95,8 +95,7 @@ bool make_plan(int M, int N, int K, bool x_f32, int num_sms, TilePlan *pl, int *
         *grid = tiles * cs;
         return true;
     }
-    if (K / 32 > 256) return false;                     // one scale box per unit
-    for (int per_sm = 2; per_sm >= 1; --per_sm) {
+    for (int per_sm = 2; per_sm >= 1 && K / 32 <= 256; --per_sm) {   // one scale box per unit
         const size_t budget = per_sm == 2 ? kSmemHalf : kSmemCap;
         const int clusters = tiles < per_sm * num_sms ? tiles : per_sm * num_sms;
         const int units = (tiles + clusters - 1) / clusters;   // per CTA
@@ -108,6 +107,16 @@ bool make_plan(int M, int N, int K, bool x_f32, int num_sms, TilePlan *pl, int *
         if (units > 1 && stages < 2) continue;          // a lone stage cannot overlap load and compute
         *pl = TilePlan{1, K, stages, clusters};
         *grid = clusters;
+        return true;
+    }
+    // Neither fits (an f32 x slice of a long K, e.g. 8 x 5120): split K even though
+    // the clusters then take more than one wave.
+    for (int cs = kMaxCs; cs >= 2; cs /= 2) {
+        if (K % (256 * cs) != 0) continue;
+        const TilePlan c{cs, K / cs, 1, tiles};
+        if (c.kslice / 32 > 256 || plan_smem(M, c, x_f32) > kSmemHalf) continue;
+        *pl = c;
+        *grid = tiles * cs;
         return true;
     }
     return false;

@@ -45,79 +45,109 @@ MADI_DEV void st4f(__half *p, float a, float b, float c, float d) {
 }
 
 // MT: type of MO (the projection output added to the residual); YT: type of Y.
-template <bool kRes, typename MT, typename YT>
+// kN: D / 128 when fixed at compile time (D = 1280: 10), 0 for any D.  Every
+// chunk's loads are predicated rather than cut off by a loop exit, so the row's
+// loads are all in flight at once.  kPre (with kN fixed; used for the few rows of
+// a decode step): gamma and beta, which no kernel writes, are fetched into
+// registers before waiting for the previous kernel.
+template <bool kRes, typename MT, typename YT, int kN, bool kPre>
 __global__ void __launch_bounds__(32 * kRowsPerCta) res_ln_kernel(float *__restrict__ X, const MT *__restrict__ MO,
                                                                   const float *__restrict__ bias, YT *__restrict__ Y,
                                                                   const float *__restrict__ gamma,
                                                                   const float *__restrict__ beta, int rows, int D,
                                                                   float eps) {
+    constexpr int C = kN ? kN : kMaxChunks;
+    static_assert(!kPre || kN != 0, "prefetch needs a fixed width");
+    constexpr int CG = kPre ? kN : 1;
+    const int nch = kN ? kN : (D >> 7);
     const int row = blockIdx.x * kRowsPerCta + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
+    pdl_trigger();
+    float4 g[CG], bt[CG];
+    if constexpr (kPre) {
+#pragma unroll
+        for (int c = 0; c < kN; ++c) {
+            g[c] = *reinterpret_cast<const float4 *>(gamma + (c << 7) + (lane << 2));
+            bt[c] = *reinterpret_cast<const float4 *>(beta + (c << 7) + (lane << 2));
+        }
+    }
+    pdl_wait();                // X and MO come from the kernels before this one
     if (row >= rows) return;   // whole warps only
-    const int nch = D >> 7;
     float *xr = X + (size_t)row * D;
-    float4 v[kMaxChunks];
+    float4 v[C];
     float s = 0.f;
 #pragma unroll
-    for (int c = 0; c < kMaxChunks; ++c) {
-        if (c >= nch) break;
-        const int i = (c << 7) + (lane << 2);
-        float4 x = *reinterpret_cast<const float4 *>(xr + i);
-        if constexpr (kRes) {
-            const float4 mo = ld4f(MO + (size_t)row * D + i);
-            const float4 b = *reinterpret_cast<const float4 *>(bias + i);
-            x.x = (x.x + mo.x) + b.x;
-            x.y = (x.y + mo.y) + b.y;
-            x.z = (x.z + mo.z) + b.z;
-            x.w = (x.w + mo.w) + b.w;
-            *reinterpret_cast<float4 *>(xr + i) = x;
+    for (int c = 0; c < C; ++c) {
+        if (c < nch) {
+            const int i = (c << 7) + (lane << 2);
+            float4 x = *reinterpret_cast<const float4 *>(xr + i);
+            if constexpr (kRes) {
+                const float4 mo = ld4f(MO + (size_t)row * D + i);
+                const float4 b = *reinterpret_cast<const float4 *>(bias + i);
+                x.x = (x.x + mo.x) + b.x;
+                x.y = (x.y + mo.y) + b.y;
+                x.z = (x.z + mo.z) + b.z;
+                x.w = (x.w + mo.w) + b.w;
+                *reinterpret_cast<float4 *>(xr + i) = x;
+            }
+            v[c] = x;
         }
-        v[c] = x;
-        s += (x.x + x.y) + (x.z + x.w);
     }
+#pragma unroll
+    for (int c = 0; c < C; ++c)
+        if (c < nch) s += (v[c].x + v[c].y) + (v[c].z + v[c].w);
     const float mean = warp_sum(s) / (float)D;
     float q = 0.f;
 #pragma unroll
-    for (int c = 0; c < kMaxChunks; ++c) {
-        if (c >= nch) break;
-        const float a = v[c].x - mean, b = v[c].y - mean, cc = v[c].z - mean, d = v[c].w - mean;
-        q += (a * a + b * b) + (cc * cc + d * d);
+    for (int c = 0; c < C; ++c) {
+        if (c < nch) {
+            const float a = v[c].x - mean, b = v[c].y - mean, cc = v[c].z - mean, d = v[c].w - mean;
+            q += (a * a + b * b) + (cc * cc + d * d);
+        }
     }
     const float inv = rsqrtf(warp_sum(q) / (float)D + eps);
     YT *yr = Y + (size_t)row * D;
 #pragma unroll
-    for (int c = 0; c < kMaxChunks; ++c) {
-        if (c >= nch) break;
-        const int i = (c << 7) + (lane << 2);
-        const float4 g = *reinterpret_cast<const float4 *>(gamma + i);
-        const float4 bt = *reinterpret_cast<const float4 *>(beta + i);
-        st4f(yr + i, (v[c].x - mean) * inv * g.x + bt.x, (v[c].y - mean) * inv * g.y + bt.y,
-             (v[c].z - mean) * inv * g.z + bt.z, (v[c].w - mean) * inv * g.w + bt.w);
+    for (int c = 0; c < C; ++c) {
+        if (c < nch) {
+            const int i = (c << 7) + (lane << 2);
+            float4 gg, bb;
+            if constexpr (kPre) {
+                gg = g[c];
+                bb = bt[c];
+            } else {
+                gg = *reinterpret_cast<const float4 *>(gamma + i);
+                bb = *reinterpret_cast<const float4 *>(beta + i);
+            }
+            st4f(yr + i, (v[c].x - mean) * inv * gg.x + bb.x, (v[c].y - mean) * inv * gg.y + bb.y,
+                 (v[c].z - mean) * inv * gg.z + bb.z, (v[c].w - mean) * inv * gg.w + bb.w);
+        }
     }
+}
+
+template <typename MT, typename YT>
+cudaError_t launch_ln(float *X, const MT *MO, const float *bias, YT *Y, const float *gamma, const float *beta, int rows,
+                      int D, float eps, cudaStream_t st) {
+    const int grid = (rows + kRowsPerCta - 1) / kRowsPerCta;
+    const int blk = 32 * kRowsPerCta;
+#define MADI_LN(RES, KN, PRE) \
+    launch_k(res_ln_kernel<RES, MT, YT, KN, PRE>, grid, blk, 0, st, 1, X, MO, bias, Y, gamma, beta, rows, D, eps)
+    if (D == 1280 && rows <= 64) return MO ? MADI_LN(true, 10, true) : MADI_LN(false, 10, true);
+    if (D == 1280) return MO ? MADI_LN(true, 10, false) : MADI_LN(false, 10, false);
+    return MO ? MADI_LN(true, 0, false) : MADI_LN(false, 0, false);
+#undef MADI_LN
 }
 
 }  // namespace
 
 cudaError_t launch_res_ln(float *X, const __half *MO, const float *bias, __half *Y, const float *gamma,
                           const float *beta, int rows, int D, float eps, cudaStream_t st) {
-    const int grid = (rows + kRowsPerCta - 1) / kRowsPerCta;
-    if (MO)
-        res_ln_kernel<true, __half, __half><<<grid, 32 * kRowsPerCta, 0, st>>>(X, MO, bias, Y, gamma, beta, rows, D, eps);
-    else
-        res_ln_kernel<false, __half, __half><<<grid, 32 * kRowsPerCta, 0, st>>>(X, nullptr, nullptr, Y, gamma, beta, rows,
-                                                                               D, eps);
-    return cudaGetLastError();
+    return launch_ln<__half, __half>(X, MO, bias, Y, gamma, beta, rows, D, eps, st);
 }
 
 cudaError_t launch_res_ln_f32(float *X, const float *MO, const float *bias, float *Y, const float *gamma,
                               const float *beta, int rows, int D, float eps, cudaStream_t st) {
-    const int grid = (rows + kRowsPerCta - 1) / kRowsPerCta;
-    if (MO)
-        res_ln_kernel<true, float, float><<<grid, 32 * kRowsPerCta, 0, st>>>(X, MO, bias, Y, gamma, beta, rows, D, eps);
-    else
-        res_ln_kernel<false, float, float><<<grid, 32 * kRowsPerCta, 0, st>>>(X, nullptr, nullptr, Y, gamma, beta, rows,
-                                                                             D, eps);
-    return cudaGetLastError();
+    return launch_ln<float, float>(X, MO, bias, Y, gamma, beta, rows, D, eps, st);
 }
 
 }  // namespace madi

@@ -66,6 +66,15 @@ struct State {
     std::map<std::string, std::pair<long long, double>> prof;   // name -> (instances, total ms)
 } S;
 
+}  // namespace
+
+namespace madi {
+bool pdl_on() { return S.pdl; }
+int num_sms() { return S.num_sms > 0 ? S.num_sms : 148; }
+}  // namespace madi
+
+namespace {
+
 std::mutex g_alloc_mu;
 std::map<uintptr_t, size_t> g_allocs;   // base -> size
 
@@ -289,7 +298,7 @@ int h_emb_q8_indirect(const ArgVal *a, uint32_t, cudaStream_t st) {      // (out
     cudaError_t e = launch_emb_q8((float *)a[0].p, static_cast<const int8_t *>(a[1].p),
                                   static_cast<const __half *>(a[2].p), static_cast<const uint32_t *>(a[3].p),
                                   static_cast<const uint32_t *>(a[4].p), dim, (int)std::min<size_t>(rows, 1u << 30), 1,
-                                  0, (long long)tok_len, st);
+                                  0, (long long)tok_len, nullptr, 0, st);
     return e == cudaSuccess ? MADI_OK : cuda_fail(e, "emb_lookup_indirect_q8");
 }
 int h_emb_q8_direct(const ArgVal *a, uint32_t, cudaStream_t st) {        // (out, qs, scales, tok_ptr, dim)
@@ -299,7 +308,7 @@ int h_emb_q8_direct(const ArgVal *a, uint32_t, cudaStream_t st) {        // (out
     if (!rows || bytes_after(a[0].p) < (size_t)dim * 4) return fail(MADI_EINVAL, "gpu_emb_lookup_q8: buffer extents");
     cudaError_t e = launch_emb_q8((float *)a[0].p, static_cast<const int8_t *>(a[1].p),
                                   static_cast<const __half *>(a[2].p), static_cast<const uint32_t *>(a[3].p), nullptr,
-                                  dim, (int)std::min<size_t>(rows, 1u << 30), 1, 0, 1, st);
+                                  dim, (int)std::min<size_t>(rows, 1u << 30), 1, 0, 1, nullptr, 0, st);
     return e == cudaSuccess ? MADI_OK : cuda_fail(e, "gpu_emb_lookup_q8");
 }
 int h_emb_f16_indirect(const ArgVal *a, uint32_t, cudaStream_t st) {     // (out, emb, tokens, pos_ptr, dim)
@@ -351,7 +360,7 @@ int h_logit_filter(const ArgVal *a, uint32_t, cudaStream_t st) {
     const size_t past_len = bytes_after(a[1].p) / 4;
     cudaError_t e = launch_logit_filter((float *)a[0].p, static_cast<const uint32_t *>(a[1].p),
                                         static_cast<const uint32_t *>(a[3].p), a[4].u, a[5].u, kWhisperVocab,
-                                        (int)std::min<size_t>(past_len, 1u << 30), st);
+                                        (int)std::min<size_t>(past_len, 1u << 30), 1, 0, st);
     return e == cudaSuccess ? MADI_OK : cuda_fail(e, "logit_filter_indirect");
 }
 
@@ -838,18 +847,28 @@ int madi_bias_res_ln_f16(float *x, const uint16_t *mo, const float *bias, uint16
     return res_ln_impl(x, mo, bias, y, gamma, beta, rows, d, eps, stream, "madi_bias_res_ln_f16");
 }
 
-int madi_emb_lookup_q8(const madi_q8w *emb, const uint32_t *tokens, const uint32_t *pos, int m, int64_t tok_stride,
-                       int tok_len, float *out, void *stream) {
-    if (!S.ready) return fail(MADI_ENOINIT, "madi_emb_lookup_q8: not initialised");
-    if (!emb || !emb->qs || !emb->scales || !tokens || !out) return fail(MADI_EINVAL, "madi_emb_lookup_q8: null argument");
+static int emb_impl(const madi_q8w *emb, const uint32_t *tokens, const uint32_t *pos, int m, int64_t tok_stride,
+                    int tok_len, const float *pos_emb, int max_pos, float *out, void *stream, const char *what) {
+    if (!S.ready) return fail(MADI_ENOINIT, "%s: not initialised", what);
+    if (!emb || !emb->qs || !emb->scales || !tokens || !out) return fail(MADI_EINVAL, "%s: null argument", what);
     if (emb->n <= 0 || emb->k <= 0 || emb->k % 32 || m <= 0 || m > 65535 || tok_len <= 0 ||
         (m > 1 && pos && tok_stride < tok_len))
-        return fail(MADI_EINVAL, "madi_emb_lookup_q8: bad shape (rows=%d dim=%d m=%d tok_len=%d)", emb->n, emb->k, m,
-                    tok_len);
+        return fail(MADI_EINVAL, "%s: bad shape (rows=%d dim=%d m=%d tok_len=%d)", what, emb->n, emb->k, m, tok_len);
     cudaError_t e = launch_emb_q8(out, emb->qs, reinterpret_cast<const __half *>(emb->scales), tokens, pos, emb->k,
-                                  emb->n, m, pos ? (long long)tok_stride : 1, pos ? (long long)tok_len : 1,
-                                  pick_stream(stream));
-    return e == cudaSuccess ? MADI_OK : cuda_fail(e, "madi_emb_lookup_q8");
+                                  emb->n, m, pos ? (long long)tok_stride : 1, pos ? (long long)tok_len : 1, pos_emb,
+                                  max_pos, pick_stream(stream));
+    return e == cudaSuccess ? MADI_OK : cuda_fail(e, what);
+}
+
+int madi_emb_lookup_q8(const madi_q8w *emb, const uint32_t *tokens, const uint32_t *pos, int m, int64_t tok_stride,
+                       int tok_len, float *out, void *stream) {
+    return emb_impl(emb, tokens, pos, m, tok_stride, tok_len, nullptr, 0, out, stream, "madi_emb_lookup_q8");
+}
+
+int madi_emb_pos_q8(const madi_q8w *emb, const uint32_t *tokens, const uint32_t *pos, int m, int64_t tok_stride,
+                    int tok_len, const float *pos_emb, int max_pos, float *out, void *stream) {
+    if (!pos || !pos_emb || max_pos <= 0) return fail(MADI_EINVAL, "madi_emb_pos_q8: pos / pos_emb / max_pos");
+    return emb_impl(emb, tokens, pos, m, tok_stride, tok_len, pos_emb, max_pos, out, stream, "madi_emb_pos_q8");
 }
 
 int madi_argmax_conf(const float *logits, int m, int vocab, uint32_t *tokens, float *conf, const uint32_t *pos,
@@ -866,9 +885,20 @@ int madi_logit_filter(float *logits, int vocab, const uint32_t *past, int past_l
                       uint32_t sample_begin, uint32_t no_repeat_ngram, void *stream) {
     if (!S.ready) return fail(MADI_ENOINIT, "madi_logit_filter: not initialised");
     if (!logits || !past || !step || vocab <= 0 || past_len < 0) return fail(MADI_EINVAL, "madi_logit_filter: bad argument");
-    cudaError_t e = launch_logit_filter(logits, past, step, sample_begin, no_repeat_ngram, vocab, past_len,
+    cudaError_t e = launch_logit_filter(logits, past, step, sample_begin, no_repeat_ngram, vocab, past_len, 1, 0,
                                         pick_stream(stream));
     return e == cudaSuccess ? MADI_OK : cuda_fail(e, "madi_logit_filter");
+}
+
+int madi_logit_filter_rows(float *logits, int m, int vocab, const uint32_t *past, int past_len, int64_t past_stride,
+                           const uint32_t *step, uint32_t sample_begin, uint32_t no_repeat_ngram, void *stream) {
+    if (!S.ready) return fail(MADI_ENOINIT, "madi_logit_filter_rows: not initialised");
+    if (!logits || !past || !step || vocab <= 0 || past_len < 0 || m <= 0 || m > 65535 ||
+        (m > 1 && past_stride < past_len))
+        return fail(MADI_EINVAL, "madi_logit_filter_rows: bad argument (m=%d past_len=%d)", m, past_len);
+    cudaError_t e = launch_logit_filter(logits, past, step, sample_begin, no_repeat_ngram, vocab, past_len, m,
+                                        (long long)past_stride, pick_stream(stream));
+    return e == cudaSuccess ? MADI_OK : cuda_fail(e, "madi_logit_filter_rows");
 }
 
 int madi_argmax_rows(const float *logits, int m, int vocab, uint32_t *tokens, void *stream) {

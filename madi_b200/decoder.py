@@ -128,8 +128,7 @@ class Decoder:
     def step(self, sample_begin: int = 1, no_repeat_ngram: int = 0, stream=None):
         """One greedy token for every slot; all state on the device."""
         s = dict(stream=stream)
-        greedy.emb_lookup_q8(self.emb, self.tokens, self.pos, out=self.x, **s)
-        self.x.add_(self.pos_emb.index_select(0, self.pos.long()))
+        greedy.emb_pos_q8(self.emb, self.tokens, self.pos, self.pos_emb, out=self.x, **s)
         for l, L in enumerate(self.layers):
             q8.layer_norm(self.x, *L.aln, eps=EPS, out=self.xb, **s)
             q8.qkv(L.qkv, self.xb, L.qb, L.vb, self.kc[l], self.vc[l], self.pos, q_out=self.q, **s)
@@ -145,8 +144,7 @@ class Decoder:
         q8.layer_norm(self.x, *self.ln_post, eps=EPS, out=self.xb, **s)
         q8.linear(self.emb, self.xb, out=self.logits, **s)
         greedy.step_advance(self.pos, **s)
-        for b in range(self.slots):
-            greedy.logit_filter(self.logits[b], self.tokens[b], self.pos[b:b + 1], sample_begin, no_repeat_ngram, **s)
+        greedy.logit_filter_rows(self.logits, self.tokens, self.pos, sample_begin, no_repeat_ngram, **s)
         greedy.argmax_conf(self.logits, self.tokens, self.pos, self.conf, **s)
 
     def step_bytes(self) -> int:

@@ -3,8 +3,8 @@
 position counters and the logits in device memory, a whole token step runs with
 no host round trip and replays as a CUDA graph.
 
-Thin wrappers of the C ABI (madi_emb_lookup_q8, madi_argmax_conf,
-madi_logit_filter, madi_step_advance) on torch CUDA tensors.
+Thin wrappers of the C ABI (madi_emb_lookup_q8, madi_emb_pos_q8, madi_argmax_conf,
+madi_logit_filter, madi_logit_filter_rows, madi_step_advance) on torch CUDA tensors.
 """
 import ctypes
 from typing import Optional
@@ -40,6 +40,27 @@ def emb_lookup_q8(emb: Q8Weight, tokens: torch.Tensor, pos: Optional[torch.Tenso
     return out
 
 
+def emb_pos_q8(emb: Q8Weight, tokens: torch.Tensor, pos: torch.Tensor, pos_emb: torch.Tensor,
+               out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+    """emb_lookup_q8 plus the positional embedding in one launch: tokens u32 [m][len],
+    pos u32 [m] on the device, pos_emb f32 [max_pos][dim]; row s is
+    emb(tokens[s][pos[s]]) + pos_emb[pos[s]].  Returns f32 [m][dim]."""
+    if tokens.dtype not in (torch.int32, torch.uint32) or tokens.dim() != 2 or not tokens.is_contiguous():
+        raise ValueError("tokens must be a contiguous 32-bit [m][len] tensor")
+    m, tok_len = tokens.shape
+    if pos.numel() != m:
+        raise ValueError("pos must have one entry per slot")
+    if pos_emb.dtype != torch.float32 or pos_emb.dim() != 2 or pos_emb.shape[1] != emb.k or not pos_emb.is_contiguous():
+        raise ValueError("pos_emb must be a contiguous f32 [max_pos][dim] tensor")
+    if out is None:
+        out = torch.empty((m, emb.k), dtype=torch.float32, device=tokens.device)
+    h = emb.handle()
+    rc = _lib.load().madi_emb_pos_q8(ctypes.byref(h), tokens.data_ptr(), pos.data_ptr(), m, tok_len, tok_len,
+                                     pos_emb.data_ptr(), pos_emb.shape[0], out.data_ptr(), _stream(stream))
+    _lib.check(rc, "madi_emb_pos_q8")
+    return out
+
+
 def argmax_conf(logits: torch.Tensor, tokens: torch.Tensor, pos: torch.Tensor, conf: Optional[torch.Tensor] = None,
                 stream=None) -> None:
     """tokens[s][pos[s]] = argmax(logits[s]) (and conf[s][pos[s]] = its softmax
@@ -64,6 +85,20 @@ def logit_filter(logits: torch.Tensor, past: torch.Tensor, step: torch.Tensor, s
     rc = _lib.load().madi_logit_filter(logits.data_ptr(), logits.numel(), past.data_ptr(), past.numel(),
                                        step.data_ptr(), int(sample_begin), int(no_repeat_ngram), _stream(stream))
     _lib.check(rc, "madi_logit_filter")
+
+
+def logit_filter_rows(logits: torch.Tensor, past: torch.Tensor, pos: torch.Tensor, sample_begin: int,
+                      no_repeat_ngram: int = 0, stream=None) -> None:
+    """logit_filter on every row of logits f32 [m][vocab] in one launch: row s uses
+    the history past[s] (u32 [m][len]) and the step pos[s] (device u32 [m])."""
+    if logits.dim() != 2 or logits.dtype != torch.float32 or not logits.is_contiguous():
+        raise ValueError("logits must be a contiguous f32 [m][vocab] tensor")
+    m, vocab = logits.shape
+    if past.dim() != 2 or past.shape[0] != m or not past.is_contiguous() or pos.numel() != m:
+        raise ValueError("past must be a contiguous [m][len] tensor and pos hold one step per row")
+    rc = _lib.load().madi_logit_filter_rows(logits.data_ptr(), m, vocab, past.data_ptr(), past.shape[1], past.shape[1],
+                                            pos.data_ptr(), int(sample_begin), int(no_repeat_ngram), _stream(stream))
+    _lib.check(rc, "madi_logit_filter_rows")
 
 
 def step_advance(pos: torch.Tensor, stream=None) -> None:

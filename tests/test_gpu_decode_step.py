@@ -157,6 +157,57 @@ def test_logit_filter(madi, oracle, case):
     assert np.array_equal(lg2.cpu().numpy(), want)
 
 
+def test_logit_filter_rows(madi, oracle):
+    """Every filter case as one row of a single batched launch (row s: its own
+    history row and step counter); each row bit-exact against the oracle."""
+    import torch
+    from madi_b200 import greedy
+    m = len(FILTER_CASES)
+    past = np.zeros((m, 64), np.uint32)
+    steps = np.zeros(m, np.uint32)
+    L = np.stack([_logit_rows(40 + r)[0] for r in range(m)])
+    lg = _t(L)
+    for r, (hist, step, sb, n) in enumerate(FILTER_CASES):
+        past[r, :len(hist)] = hist
+        steps[r] = step
+    # sample_begin / no_repeat_ngram are per launch: group the rows by them
+    for sb, n in sorted({(c[2], c[3]) for c in FILTER_CASES}):
+        rows = [r for r, c in enumerate(FILTER_CASES) if (c[2], c[3]) == (sb, n)]
+        sub = _t(L[rows])
+        greedy.logit_filter_rows(sub, _u32(past[rows]), _u32(steps[rows]), sb, n)
+        torch.cuda.synchronize()
+        got = sub.cpu().numpy()
+        for i, r in enumerate(rows):
+            assert np.array_equal(got[i], oracle.logit_filter(L[r], past[r], int(steps[r]), sb, n)), f"row {r}"
+    full = L.copy()
+    greedy.logit_filter_rows(lg, _u32(past), _u32(steps), 1, 0)
+    torch.cuda.synchronize()
+    got = lg.cpu().numpy()
+    for r in range(m):
+        assert np.array_equal(got[r], oracle.logit_filter(full[r], past[r], int(steps[r]), 1, 0)), f"row {r}"
+
+
+def test_emb_pos_q8(madi, oracle):
+    """Fused embedding + positional embedding for 5 slots, bit-exact against the
+    lookup followed by the f32 add; a position past max_pos adds nothing."""
+    import torch
+    from madi_b200 import greedy
+    qs, sc = _q8_table(VOCAB, 1280, 3)
+    emb = _weight(qs, sc)
+    g = np.random.default_rng(4)
+    pe = (g.standard_normal((448, 1280)) * 0.1).astype(np.float32)
+    toks = g.integers(0, VOCAB, (5, 500)).astype(np.uint32)
+    toks[2, 7] = VOCAB + 1                               # token outside the table: zero row + pe
+    pos = np.array([0, 9, 7, 447, 460], np.uint32)       # slot 4: past max_pos
+    out = greedy.emb_pos_q8(emb, _u32(toks), _u32(pos), _t(pe))
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    for s in range(5):
+        e = np.zeros(1280, np.float32) if s == 2 else oracle.emb_q8(qs, sc, toks[s, pos[s]])
+        want = e + pe[pos[s]] if pos[s] < 448 else e
+        assert np.array_equal(got[s], want.astype(np.float32)), f"slot {s}"
+
+
 def test_logit_filter_step_past_history(madi, oracle):
     """A step counter beyond the history buffer reads nothing from it: only the
     history-free bans apply."""
