@@ -20,6 +20,10 @@ Workload (N=1 is BASELINE config 1 at B=16, the largest single-GPU config):
   e2e   = the same encoder metric through the public API (madi_b200.q8.linear)
           with pinned HOST buffers: per step H2D of X and D2H of Y inside the
           timed region.
+  long_audio: 120 chunks of synthetic log-mel sharded over the
+          ranks; per batch of 8 chunks the whole encoder (conv stem, 32 Q8 layers,
+          ln_post), cross K/V, then exactly 224 greedy tokens per chunk (EOT
+          suppressed) -- chunks/s from pinned host mel to host tokens, slowest rank.
 Multi-GPU: one process per GPU (torchrun), each rank runs its own B chunks
 (weak scaling, no data-path collective on the encoder); times are the max
 over ranks.  --impl reference times the reference's CPU computation of the
@@ -60,6 +64,9 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-encoder-layer", action="store_true")
+    ap.add_argument("--no-long-audio", action="store_true")
+    ap.add_argument("--chunks", type=int, default=120, help="long-audio leg: 30 s chunks over all GPUs (config 4)")
+    ap.add_argument("--tokens", type=int, default=224, help="long-audio leg: greedy tokens per chunk")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     return ap.parse_args()
 
@@ -368,6 +375,11 @@ def main_madi(args, world, rank, local):
     if not args.no_decode:
         decode = decode_leg(args, world, rank, dev, stream, peaks)
 
+    # ---------------- long-audio batched transcription (config 4)
+    long_audio = None
+    if not args.no_long_audio:
+        long_audio = long_audio_leg(args, world, rank, dev)
+
     # ---------------- CPU baseline (rank 0, N=1 only)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -389,9 +401,72 @@ def main_madi(args, world, rank, local):
                 # 30 s chunks through one fc1 + fc2 pair per second (not the whole encoder)
                 "ffn_pair_chunks_per_s": chunks_per_s,
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "decode": decode,
-                "encoder_layer": enc_layer,
+                "encoder_layer": enc_layer, "long_audio": long_audio,
                 "clocks": clocks, "gpu_launches": 2 * K}
         print(json.dumps(line), flush=True)
+
+
+def long_audio_leg(args, world, rank, dev):
+    """`--chunks` independent 30 s chunks (synthetic log-mel, f16
+    [128][3000] each) sharded over the ranks; each rank runs the whole encoder (conv
+    stem, 32 layers, ln_post) on batches of 8 chunks, then the 4-layer greedy decoder
+    for exactly `--tokens` tokens per chunk (EOT suppressed), replicated vocab head.
+    Timed from the pinned host mel to the tokens back in host memory; one untimed
+    batch first (module load, graph capture).  chunks/s = all chunks / the slowest
+    rank's time (strong scaling: the total is fixed)."""
+    import math
+
+    import torch
+
+    from madi_b200 import pipeline
+
+    slots = 8
+    per = math.ceil(args.chunks / world)
+    lo = min(args.chunks, rank * per)
+    mine = max(0, min(args.chunks, lo + per) - lo)
+    tr = pipeline.Transcriber(slots=slots, enc_layers=32, tokens=args.tokens, seed=1, device=dev)
+    mel_h = torch.from_numpy(pipeline.synthetic_mel(max(mine, 1), first=lo)).pin_memory()
+    mel_d = torch.empty((slots,) + tuple(mel_h.shape[1:]), dtype=torch.float16, device=dev)
+    tok_h = torch.empty((max(mine, 1), args.tokens), dtype=torch.int32, pin_memory=True)
+    b0 = min(slots, mel_h.shape[0])
+    mel_d[:b0].copy_(mel_h[:b0])
+    tr.transcribe(mel_d[:b0])                       # untimed: module load, graph capture
+    torch.cuda.synchronize()
+    barrier(world)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    enc_ms, dec_ms = [], []
+    ev[0].record()
+    for i in range(0, mine, slots):
+        b = min(slots, mine - i)
+        e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        e0.record()
+        mel_d[:b].copy_(mel_h[i:i + b], non_blocking=True)
+        states = tr.encode(mel_d[:b])
+        e1.record()
+        toks = tr.decode(states)
+        tok_h[i:i + b].copy_(toks, non_blocking=True)
+        e2.record()
+        enc_ms.append((e0, e1))
+        dec_ms.append((e1, e2))
+    ev[1].record()
+    torch.cuda.synchronize()
+    ms = ev[0].elapsed_time(ev[1]) if mine else 0.0
+    ms_max = max_over_ranks(world, ms)
+    enc_avg = sum(a.elapsed_time(b) for a, b in enc_ms) / max(1, len(enc_ms))
+    dec_avg = sum(a.elapsed_time(b) for a, b in dec_ms) / max(1, len(dec_ms))
+    toks = tok_h[:mine].numpy().view("uint32")
+    tr.release()
+    del tr, mel_d
+    torch.cuda.empty_cache()
+    return {"chunks": args.chunks, "chunks_per_rank": per, "tokens_per_chunk": args.tokens, "slots": slots,
+            "chunks_per_s": args.chunks / (ms_max / 1e3), "ms_total": ms_max, "scaling": "strong",
+            "encoder_ms_per_batch": enc_avg, "decoder_ms_per_batch": dec_avg,
+            "decoder_ms_per_token_step": dec_avg / args.tokens,
+            "encoder": "conv stem (PyTorch f16 conv1d) + 32 Q8 layers + ln_post, 8 chunks per batch",
+            "decoder": "4 Q8 layers, replicated head, one CUDA graph per token step, EOT suppressed",
+            "h2d_bytes": int(mine * 128 * 3000 * 2), "d2h_bytes": int(mine * args.tokens * 4),
+            "first_tokens_rank0": toks[0, :8].tolist() if mine else [],
+            "data": "synthetic log-mel (seeded N(0,1) clipped to +-1.5), random-init Q8 weights"}
 
 
 def decode_leg(args, world, rank, dev, stream, peaks):

@@ -301,6 +301,10 @@ int madi_flash_attn_enc(const uint16_t *q, const uint16_t *k, const uint16_t *v,
 int madi_self_attn(const float *q, const void *kc, const void *vc, int kv_dtype, const uint32_t *pos, int slots,
                    int heads, int kv_heads, int kv_dim, int max_tok, float *out, void *stream);
 
+/* suppress_list (graph_helpers.metal:97-107) on m logit rows in one launch:
+ * logits[r][ids[j]] = -3.4e38 for every id < vocab (ids u32 [n], on the device). */
+int madi_suppress_rows(float *logits, int m, int vocab, const uint32_t *ids, int n, void *stream);
+
 /* Greedy token of each of m full logit rows (tokens[s], no position), the
  * reference's argmax including its tie order (graph_helpers.metal:64-95). */
 int madi_argmax_rows(const float *logits, int m, int vocab, uint32_t *tokens, void *stream);

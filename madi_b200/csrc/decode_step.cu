@@ -143,13 +143,14 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float *__restrict__ 
     }
 }
 
+// Row blockIdx.y of logits [rows][V].
 __global__ void suppress_kernel(float *__restrict__ logits, const uint32_t *__restrict__ ids, int n, int V) {
     const int j = blockIdx.x * blockDim.x + threadIdx.x;
     pdl_trigger();
     pdl_wait();
     if (j >= n) return;
     const uint32_t t = ids[j];
-    if (t < (uint32_t)V) logits[t] = kNeg;
+    if (t < (uint32_t)V) logits[(size_t)blockIdx.y * V + t] = kNeg;
 }
 
 // logit_filter_indirect (graph_helpers.metal:109-160): one CTA of 256 threads per
@@ -284,8 +285,9 @@ cudaError_t launch_argmax(const float *logits, uint32_t *tokens, float *conf, co
                            V, max_len, stride);
 }
 
-cudaError_t launch_suppress(float *logits, const uint32_t *ids, int n, int V, cudaStream_t st) {
-    return n > 0 ? launch_k(suppress_kernel, (n + 255) / 256, 256, 0, st, 1, logits, ids, n, V) : cudaSuccess;
+cudaError_t launch_suppress(float *logits, const uint32_t *ids, int n, int V, int rows, cudaStream_t st) {
+    return n > 0 ? launch_k(suppress_kernel, dim3((n + 255) / 256, rows), 256, 0, st, 1, logits, ids, n, V)
+                 : cudaSuccess;
 }
 
 cudaError_t launch_logit_filter(float *logits, const uint32_t *past, const uint32_t *step_ptr, uint32_t sample_begin,

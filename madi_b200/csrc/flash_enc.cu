@@ -214,7 +214,10 @@ __global__ void __launch_bounds__(kFaThreads, 1)
             // exp(s * scale - m') = 2^(s * scale * log2 e - m' * log2 e): one FFMA and the
             // hardware base-2 exponential per element (P is rounded to f16 after it)
             const float ml = mn * kLog2e;
-            const float alpha = (m == -INFINITY) ? 0.f : ex2_approx(fmaf(m, kLog2e, -ml));
+            // exactly 1 when the row max did not move: the O rescale below runs when any
+            // row of the warp grew (rows past the chunk end included), and it must then
+            // leave the other rows' O bit-for-bit unchanged
+            const float alpha = (m == -INFINITY) ? 0.f : (mn == m ? 1.f : ex2_approx(fmaf(m, kLog2e, -ml)));
             float bs = 0.f;
             uint32_t pp[kKT / 2];
 #pragma unroll

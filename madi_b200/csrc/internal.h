@@ -110,7 +110,7 @@ cudaError_t launch_pos_add(float *out, const float *pos_emb, const uint32_t *pos
 cudaError_t launch_step_advance(uint32_t *pos, int m, cudaStream_t st);
 cudaError_t launch_argmax(const float *logits, uint32_t *tokens, float *conf, const uint32_t *pos, int V, int max_len,
                           int m, long long stride, cudaStream_t st);
-cudaError_t launch_suppress(float *logits, const uint32_t *ids, int n, int V, cudaStream_t st);
+cudaError_t launch_suppress(float *logits, const uint32_t *ids, int n, int V, int rows, cudaStream_t st);
 cudaError_t launch_logit_filter(float *logits, const uint32_t *past, const uint32_t *step_ptr, uint32_t sample_begin,
                                 uint32_t no_repeat_ngram, int V, int past_len, int rows, long long past_stride,
                                 cudaStream_t st);

@@ -351,7 +351,8 @@ int h_suppress(const ArgVal *a, uint32_t, cudaStream_t st) {             // (log
     const uint32_t n = a[2].u;
     if (bytes_after(a[0].p) < (size_t)kWhisperVocab * 4 || bytes_after(a[1].p) < (size_t)n * 4)
         return fail(MADI_EINVAL, "suppress_list: buffer extents");
-    cudaError_t e = launch_suppress((float *)a[0].p, static_cast<const uint32_t *>(a[1].p), (int)n, kWhisperVocab, st);
+    cudaError_t e =
+        launch_suppress((float *)a[0].p, static_cast<const uint32_t *>(a[1].p), (int)n, kWhisperVocab, 1, st);
     return e == cudaSuccess ? MADI_OK : cuda_fail(e, "suppress_list");
 }
 // (logits, past_tokens, num_suppress, step_ptr, sample_begin, no_repeat_ngram)
@@ -899,6 +900,14 @@ int madi_logit_filter_rows(float *logits, int m, int vocab, const uint32_t *past
     cudaError_t e = launch_logit_filter(logits, past, step, sample_begin, no_repeat_ngram, vocab, past_len, m,
                                         (long long)past_stride, pick_stream(stream));
     return e == cudaSuccess ? MADI_OK : cuda_fail(e, "madi_logit_filter_rows");
+}
+
+int madi_suppress_rows(float *logits, int m, int vocab, const uint32_t *ids, int n, void *stream) {
+    if (!S.ready) return fail(MADI_ENOINIT, "madi_suppress_rows: not initialised");
+    if (!logits || !ids || m <= 0 || m > 65535 || vocab <= 0 || n < 0)
+        return fail(MADI_EINVAL, "madi_suppress_rows: bad argument (m=%d vocab=%d n=%d)", m, vocab, n);
+    cudaError_t e = launch_suppress(logits, ids, n, vocab, m, pick_stream(stream));
+    return e == cudaSuccess ? MADI_OK : cuda_fail(e, "madi_suppress_rows");
 }
 
 int madi_argmax_rows(const float *logits, int m, int vocab, uint32_t *tokens, void *stream) {

@@ -75,13 +75,42 @@ def host_weights(seed: int = 1) -> dict:
     return w
 
 
+def device_weights(seed: int = 1, device="cuda") -> dict:
+    """The same model drawn on the device (host_weights' distributions; for the
+    long-audio pipeline, where only the shapes and value ranges matter)."""
+    g = torch.Generator(device=device)
+    g.manual_seed(seed * 104729)
+
+    def q8w(n, k):
+        return (torch.randint(-127, 128, (n, k), dtype=torch.int8, device=device, generator=g),
+                (torch.rand((n, k // 32), device=device, generator=g) * 1.9e-3 + 1e-4).half())
+
+    def vec(n):
+        return (torch.randn(n, device=device, generator=g) * 0.02).half().float()
+
+    def ln():
+        return (1.0 + 0.1 * torch.randn(D, device=device, generator=g), 0.1 * torch.randn(D, device=device, generator=g))
+
+    w = {"layers": []}
+    for _ in range(LAYERS):
+        w["layers"].append({"aln": ln(), "caln": ln(), "mln": ln(), "qkv": q8w(3 * D, D), "qb": vec(D), "vb": vec(D),
+                            "o": q8w(D, D), "ob": vec(D), "cq": q8w(D, D), "cqb": vec(D), "ck": q8w(D, D),
+                            "cv": q8w(D, D), "cvb": vec(D), "co": q8w(D, D), "cob": vec(D), "fc1": q8w(F, D),
+                            "m0b": vec(F), "fc2": q8w(D, F), "m2b": vec(D)})
+    w["emb"] = q8w(V, D)
+    w["pos_emb"] = torch.randn((MAX_TOK, D), device=device, generator=g) * 0.1
+    w["ln_post"] = ln()
+    return w
+
+
 class Decoder:
     """Device copy of the synthetic decoder plus the per-slot decode state."""
 
     def __init__(self, w: dict, slots: int, device="cuda"):
         if not 1 <= slots <= 8:
             raise ValueError("1..8 token slots")
-        t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(device)
+        t = lambda a: (a.to(device) if isinstance(a, torch.Tensor) else
+                       torch.from_numpy(np.ascontiguousarray(a)).to(device))
         qw = lambda p: q8.Q8Weight(t(p[0]), t(p[1]))
         self.slots, self.dev = slots, device
         self.layers: List[Layer] = []
@@ -110,12 +139,17 @@ class Decoder:
 
     def set_encoder(self, enc_states: torch.Tensor, stream=None):
         """Cross K / V of every layer from the encoder states f16 [slots][1500][1280]
-        (the tcgen05 GEMM, once per audio chunk); kept f16 as the reference's decoder does."""
+        (the tcgen05 GEMM, once per audio chunk); kept f16 as the reference's decoder does.
+        The K / V buffers are reused while their shape holds, so a captured token step
+        stays valid across audio chunks."""
         S, T, _ = enc_states.shape
         flat = enc_states.reshape(S * T, D).contiguous()
         for l, L in enumerate(self.layers):
-            self.ck[l] = q8.linear(L.ck, flat, stream=stream).view(S, T, D)
-            self.cv[l] = q8.linear(L.cv, flat, bias=L.cvb, stream=stream).view(S, T, D)
+            if self.ck[l] is None or self.ck[l].shape != (S, T, D):
+                self.ck[l] = torch.empty((S, T, D), dtype=torch.float16, device=flat.device)
+                self.cv[l] = torch.empty((S, T, D), dtype=torch.float16, device=flat.device)
+            q8.linear(L.ck, flat, out=self.ck[l].view(S * T, D), stream=stream)
+            q8.linear(L.cv, flat, bias=L.cvb, out=self.cv[l].view(S * T, D), stream=stream)
 
     def reset(self, seed_token: int = 50258):
         self.tokens.zero_()
@@ -125,8 +159,9 @@ class Decoder:
         for c in self.kc + self.vc:
             c.zero_()
 
-    def step(self, sample_begin: int = 1, no_repeat_ngram: int = 0, stream=None):
-        """One greedy token for every slot; all state on the device."""
+    def step(self, sample_begin: int = 1, no_repeat_ngram: int = 0, stream=None, suppress=None):
+        """One greedy token for every slot; all state on the device.  suppress: device
+        u32 token ids banned at every step (e.g. EOT, to force a fixed length)."""
         s = dict(stream=stream)
         greedy.emb_pos_q8(self.emb, self.tokens, self.pos, self.pos_emb, out=self.x, **s)
         for l, L in enumerate(self.layers):
@@ -145,6 +180,8 @@ class Decoder:
         q8.linear(self.emb, self.xb, out=self.logits, **s)
         greedy.step_advance(self.pos, **s)
         greedy.logit_filter_rows(self.logits, self.tokens, self.pos, sample_begin, no_repeat_ngram, **s)
+        if suppress is not None:
+            greedy.suppress_rows(self.logits, suppress, **s)
         greedy.argmax_conf(self.logits, self.tokens, self.pos, self.conf, **s)
 
     def step_bytes(self) -> int:

@@ -13,7 +13,15 @@ One layer, in the reference's order (encoder.zig:235-315, encoder_ops.metal:305-
     f   = h W2^T                              Q8 GEMM (its bias + residual join the next LN)
 
 x is the f32 residual stream [chunks * 1500][1280]; weights are seeded random Q8.
+
+Encoder puts the whole large-v3-turbo encoder together (config 3): the conv stem
+(conv1d 128 -> 1280, k 3, GELU; conv1d 1280 -> 1280, k 3, stride 2, GELU) on f16
+weights as the reference keeps them (transcribe.zig:1099-1102), through PyTorch's
+convolution -- it is not a Q8 op and is < 1 % of the encoder's FLOPs -- then the
+sinusoidal positions, 32 layers as above and the final LayerNorm (ln_post), whose
+f16 output is what the decoder's cross K / V projections read.
 """
+import math
 from typing import Optional
 
 import numpy as np
@@ -23,6 +31,29 @@ from . import attn, q8, synth
 
 D, F, HEADS, SEQ = 1280, 5120, 20, 1500
 EPS = 1e-5
+
+
+def device_layer(seed: int, device="cuda") -> dict:
+    """One random-init encoder layer generated on the device (same distributions as
+    host_layer; used for the 32-layer encoder, whose 0.67 GB of Q8 weights would
+    take seconds to draw on the host)."""
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+
+    def q8w(n, k):
+        return (torch.randint(-127, 128, (n, k), dtype=torch.int8, device=device, generator=g),
+                (torch.rand((n, k // 32), device=device, generator=g) * 1.9e-3 + 1e-4).half())
+
+    def vec(n, s=0.02):
+        return (torch.randn(n, device=device, generator=g) * s).half().float()
+
+    def ln():
+        return (1.0 + 0.1 * torch.randn(D, device=device, generator=g), 0.1 * torch.randn(D, device=device, generator=g))
+
+    bqkv = vec(3 * D)
+    bqkv[D:2 * D] = 0.0
+    return {"ln1": ln(), "ln2": ln(), "qkv": q8w(3 * D, D), "bqkv": bqkv, "o": q8w(D, D), "bo": vec(D),
+            "fc1": q8w(F, D), "b1": vec(F), "fc2": q8w(D, F), "b2": vec(D)}
 
 
 def host_layer(seed: int = 1) -> dict:
@@ -41,7 +72,8 @@ def host_layer(seed: int = 1) -> dict:
 
 class EncoderLayer:
     def __init__(self, w: dict, device="cuda"):
-        t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(device)
+        t = lambda a: (a.to(device) if isinstance(a, torch.Tensor) else
+                       torch.from_numpy(np.ascontiguousarray(a)).to(device))
         qw = lambda p: q8.Q8Weight(t(p[0]), t(p[1]))
         self.ln1 = (t(w["ln1"][0]), t(w["ln1"][1]))
         self.ln2 = (t(w["ln2"][0]), t(w["ln2"][1]))
@@ -74,3 +106,56 @@ class EncoderLayer:
         linears = 2.0 * M * D * (3 * D + D + F + F)
         attention = 4.0 * SEQ * SEQ * 64 * HEADS * chunks
         return linears + attention
+
+
+def sinusoids(length: int, channels: int, max_timescale: float = 10000.0) -> torch.Tensor:
+    """Whisper's sinusoidal positions [length][channels]: sin | cos halves."""
+    inc = math.log(max_timescale) / (channels // 2 - 1)
+    inv = torch.exp(-inc * torch.arange(channels // 2, dtype=torch.float64))
+    t = torch.arange(length, dtype=torch.float64)[:, None] * inv[None, :]
+    return torch.cat([torch.sin(t), torch.cos(t)], dim=1).float()
+
+
+class Encoder:
+    """The whole encoder: conv stem, positions, `layers` encoder layers, ln_post."""
+    N_MELS, FRAMES = 128, 3000
+
+    def __init__(self, layers: int = 32, seed: int = 1, device="cuda"):
+        g = torch.Generator(device=device)
+        g.manual_seed(seed * 7919)
+        self.c1w = (torch.randn((D, self.N_MELS, 3), device=device, generator=g) / math.sqrt(3 * self.N_MELS)).half()
+        self.c1b = (torch.randn(D, device=device, generator=g) * 0.02).half()
+        self.c2w = (torch.randn((D, D, 3), device=device, generator=g) / math.sqrt(3 * D)).half()
+        self.c2b = (torch.randn(D, device=device, generator=g) * 0.02).half()
+        self.pos = sinusoids(SEQ, D).to(device)
+        self.layers = [EncoderLayer(device_layer(seed * 1000 + l, device), device) for l in range(layers)]
+        self.ln_post = (1.0 + 0.1 * torch.randn(D, device=device, generator=g), 0.1 * torch.randn(D, device=device,
+                                                                                                generator=g))
+
+    def forward(self, mel: torch.Tensor, stream=None) -> torch.Tensor:
+        """mel f16 [chunks][128][3000] -> encoder states f16 [chunks][1500][1280]."""
+        B = mel.shape[0]
+        x = torch.empty((B * SEQ, D), dtype=torch.float32, device=mel.device)     # f32 residual stream
+        for c in range(B):
+            # one chunk per convolution call: the library picks its algorithm by shape,
+            # so a chunk's stem output does not depend on how many chunks share a batch
+            x[c * SEQ:(c + 1) * SEQ] = self.stem(mel[c:c + 1])[0]
+        f, b2 = None, None
+        for L in self.layers:
+            f, b2 = L.forward(x, f, b2, stream=stream), L.b2
+        if f is None:
+            y = q8.layer_norm_f16(x, *self.ln_post, eps=EPS, stream=stream)
+        else:
+            y = q8.bias_res_ln_f16(x, f, b2, *self.ln_post, eps=EPS, stream=stream)
+        return y.view(B, SEQ, D)
+
+    def stem(self, mel: torch.Tensor) -> torch.Tensor:
+        """Conv stem and positions: mel f16 [b][128][3000] -> f32 [b][1500][1280]."""
+        import torch.nn.functional as Fn
+        h = Fn.gelu(Fn.conv1d(mel, self.c1w, self.c1b, padding=1))
+        h = Fn.gelu(Fn.conv1d(h, self.c2w, self.c2b, stride=2, padding=1))         # [b][1280][1500]
+        return h.transpose(1, 2).float() + self.pos
+
+    def flops(self, chunks: int) -> float:
+        """Algorithmic FLOPs of the layers (the stem's 17.6 GFLOP per chunk not counted)."""
+        return len(self.layers) * EncoderLayer.flops(chunks)

@@ -4,7 +4,8 @@ position counters and the logits in device memory, a whole token step runs with
 no host round trip and replays as a CUDA graph.
 
 Thin wrappers of the C ABI (madi_emb_lookup_q8, madi_emb_pos_q8, madi_argmax_conf,
-madi_logit_filter, madi_logit_filter_rows, madi_step_advance) on torch CUDA tensors.
+madi_logit_filter, madi_logit_filter_rows, madi_suppress_rows, madi_step_advance) on
+torch CUDA tensors.
 """
 import ctypes
 from typing import Optional
@@ -99,6 +100,18 @@ def logit_filter_rows(logits: torch.Tensor, past: torch.Tensor, pos: torch.Tenso
     rc = _lib.load().madi_logit_filter_rows(logits.data_ptr(), m, vocab, past.data_ptr(), past.shape[1], past.shape[1],
                                             pos.data_ptr(), int(sample_begin), int(no_repeat_ngram), _stream(stream))
     _lib.check(rc, "madi_logit_filter_rows")
+
+
+def suppress_rows(logits: torch.Tensor, ids: torch.Tensor, stream=None) -> None:
+    """suppress_list on every row of logits f32 [m][vocab]: the token ids (device
+    u32 [n]) get -3.4e38."""
+    if logits.dim() != 2 or logits.dtype != torch.float32 or not logits.is_contiguous():
+        raise ValueError("logits must be a contiguous f32 [m][vocab] tensor")
+    if ids.dtype not in (torch.int32, torch.uint32) or not ids.is_contiguous():
+        raise ValueError("ids must be a contiguous 32-bit tensor")
+    m, vocab = logits.shape
+    _lib.check(_lib.load().madi_suppress_rows(logits.data_ptr(), m, vocab, ids.data_ptr(), ids.numel(),
+                                              _stream(stream)), "madi_suppress_rows")
 
 
 def step_advance(pos: torch.Tensor, stream=None) -> None:

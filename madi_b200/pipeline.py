@@ -1,0 +1,83 @@
+"""Long-audio batched transcription on the library's kernels (config 4 shapes):
+independent 30 s chunks of log-mel -> the whole encoder (conv stem, 32 layers,
+ln_post) -> cross K / V -> the 4-layer greedy decoder with EOT suppressed, exactly
+`tokens` tokens per chunk, chunks in batches of `slots` token slots (the reference
+batches independent chunks into decoder slots the same way, transcribe.zig:2314-2321).
+
+Per batch: one eager encoder pass (about 290 launches, tcgen05 GEMMs and flash
+attention), 8 cross K / V GEMMs, then `tokens` replays of one captured CUDA graph
+of the token step.  Weights are random-init Q8 of the real shapes drawn on the
+device; the mel input is seeded Gaussian noise clipped to [-1.5, 1.5].
+
+Every result row depends only on its own chunk: the GEMMs' per-row accumulation
+order does not depend on M, attention runs per chunk / slot, and the decode
+kernels treat token slots independently, so a chunk's tokens do not depend on
+which batch it was decoded in.
+"""
+import numpy as np
+import torch
+
+from . import decoder as dec
+from . import encoder as enc
+from . import synth
+
+SOT, EOT = 50258, 50257
+
+
+def synthetic_mel(chunks: int, first: int = 0) -> np.ndarray:
+    """f16 [chunks][128][3000]: chunk c (global index first + c) is seeded Gaussian
+    noise clipped to [-1.5, 1.5], reproducible chunk by chunk."""
+    out = np.empty((chunks, enc.Encoder.N_MELS, enc.Encoder.FRAMES), np.float16)
+    for c in range(chunks):
+        g = synth.rng(4, 700001, first + c)
+        out[c] = np.clip(g.standard_normal((enc.Encoder.N_MELS, enc.Encoder.FRAMES), dtype=np.float32), -1.5, 1.5)
+    return out
+
+
+class Transcriber:
+    def __init__(self, slots: int = 8, enc_layers: int = 32, tokens: int = 224, seed: int = 1, device="cuda"):
+        if tokens < 1 or tokens + 1 > dec.MAX_TOK:
+            raise ValueError(f"1..{dec.MAX_TOK - 1} tokens per chunk")
+        self.encoder = enc.Encoder(enc_layers, seed, device)
+        self.decoder = dec.Decoder(dec.device_weights(seed, device), slots, device)
+        self.slots, self.tokens = slots, tokens
+        self.eot = torch.tensor([EOT], dtype=torch.int32, device=device)
+        self.graph = None
+
+    def _capture(self):
+        d = self.decoder
+        d.reset(SOT)
+        d.step(suppress=self.eot)               # eager first step: module load, one-time attributes
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            d.step(suppress=self.eot)
+        torch.cuda.synchronize()
+        self.graph = g
+
+    def encode(self, mel: torch.Tensor) -> torch.Tensor:
+        """mel f16 [b][128][3000] on the device -> encoder states f16 [b][1500][1280]."""
+        return self.encoder.forward(mel)
+
+    def decode(self, states: torch.Tensor) -> torch.Tensor:
+        """Greedy tokens u32-as-int32 [b][tokens] (on the device) for b <= slots chunks'
+        encoder states; unused slots decode a copy of the last chunk."""
+        b = states.shape[0]
+        if not 1 <= b <= self.slots:
+            raise ValueError(f"1..{self.slots} chunks per batch")
+        if b < self.slots:
+            states = torch.cat([states, states[-1:].expand(self.slots - b, -1, -1)], dim=0)
+        self.decoder.set_encoder(states)
+        if self.graph is None:
+            self._capture()
+        self.decoder.reset(SOT)
+        for _ in range(self.tokens):
+            self.graph.replay()
+        return self.decoder.tokens[:b, 1:1 + self.tokens]
+
+    def transcribe(self, mel: torch.Tensor) -> torch.Tensor:
+        return self.decode(self.encode(mel))
+
+    def release(self):
+        """Drops the captured token step (before the process group or the context goes)."""
+        self.graph = None

@@ -187,6 +187,21 @@ def test_logit_filter_rows(madi, oracle):
         assert np.array_equal(got[r], oracle.logit_filter(full[r], past[r], int(steps[r]), 1, 0)), f"row {r}"
 
 
+def test_suppress_rows(madi, oracle):
+    """suppress_list on 3 rows in one launch, bit-exact against the oracle's per row;
+    an id past the vocabulary is skipped."""
+    import torch
+    from madi_b200 import greedy
+    L = np.stack([_logit_rows(60 + r)[0] for r in range(3)])
+    ids = np.array([50257, 220, 99999, 0, 51865], np.uint32)
+    lg = _t(L)
+    greedy.suppress_rows(lg, _u32(ids))
+    torch.cuda.synchronize()
+    got = lg.cpu().numpy()
+    for r in range(3):
+        assert np.array_equal(got[r], oracle.suppress(L[r], ids)), f"row {r}"
+
+
 def test_emb_pos_q8(madi, oracle):
     """Fused embedding + positional embedding for 5 slots, bit-exact against the
     lookup followed by the f32 add; a position past max_pos adds nothing."""

@@ -1,0 +1,67 @@
+"""The long-audio pipeline (madi_b200/pipeline.py: conv stem, encoder layers,
+ln_post, cross K / V, greedy decoder with EOT suppressed) on a reduced depth:
+its size-independent properties, since every piece it chains is parity-tested
+on its own (encoder layer, decoder end to end, attention, decode-step helpers):
+
+* batch invariance -- a chunk's encoder states and tokens are the same whether
+  it is processed in a batch of 4, of 2 or alone (per-row GEMM accumulation does
+  not depend on M; attention and the decode kernels are per chunk / slot);
+* determinism -- the same input gives the same tokens again;
+* the forced length -- exactly `tokens` tokens, none of them EOT or a special.
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def tr(madi):
+    from madi_b200 import pipeline
+    t = pipeline.Transcriber(slots=4, enc_layers=2, tokens=6, seed=3)
+    yield t
+    t.release()
+
+
+def test_stem_and_layer_batch_invariance(madi):
+    """The stem (one convolution call per chunk) and one encoder layer (Q8 GEMMs
+    at M = 4 x 1500 vs 1500, flash attention, LNs) each give a chunk the same
+    bits in any batch."""
+    import torch
+    from madi_b200 import encoder as enc, pipeline
+    e = enc.Encoder(layers=1, seed=5)
+    mel = torch.from_numpy(pipeline.synthetic_mel(3, first=70)).cuda()
+    x3 = torch.cat([e.stem(mel[i:i + 1]) for i in range(3)]).reshape(-1, enc.D).contiguous()
+    x1 = e.stem(mel[1:2]).reshape(-1, enc.D).contiguous()
+    assert torch.equal(x3[enc.SEQ:2 * enc.SEQ], x1)
+    L = e.layers[0]
+    f3 = L.forward(x3.clone(), None, None)
+    f1 = L.forward(x1.clone(), None, None)
+    torch.cuda.synchronize()
+    assert torch.equal(f3[enc.SEQ:2 * enc.SEQ], f1), "encoder layer output depends on the batch"
+
+
+def test_batch_invariance(tr):
+    import torch
+    from madi_b200 import pipeline
+    mel = torch.from_numpy(pipeline.synthetic_mel(5, first=10)).cuda()
+    states4 = tr.encode(mel[:4])
+    states1 = torch.cat([tr.encode(mel[i:i + 1]) for i in range(4)])
+    states2 = torch.cat([tr.encode(mel[0:2]), tr.encode(mel[2:4])])
+    assert torch.equal(states4, states1) and torch.equal(states4, states2), "encoder states depend on the batch"
+    tok_batch = torch.cat([tr.decode(states4).clone(), tr.transcribe(mel[4:5]).clone()])
+    tok_single = torch.cat([tr.transcribe(mel[i:i + 1]).clone() for i in range(5)])
+    torch.cuda.synchronize()
+    assert torch.equal(tok_batch, tok_single), f"{tok_batch.tolist()} vs {tok_single.tolist()}"
+    again = tr.transcribe(mel[:4]).clone()
+    assert torch.equal(again, tok_batch[:4])
+
+
+def test_forced_length(tr):
+    import torch
+    from madi_b200 import pipeline
+    mel = torch.from_numpy(pipeline.synthetic_mel(3, first=40)).cuda()
+    toks = tr.transcribe(mel).clone().cpu().numpy().view(np.uint32)
+    assert toks.shape == (3, 6)
+    assert (toks < pipeline.EOT).all(), toks
+    assert int(tr.decoder.pos[0].item()) == 6
