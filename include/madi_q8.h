@@ -284,6 +284,25 @@ int madi_logit_filter_rows(float *logits, int m, int vocab, const uint32_t *past
 int madi_cross_attn(const float *q, const void *kc, const void *vc, int kv_dtype, int slots, int seqlen, int heads,
                     int kv_heads, int kv_dim, float *out, float *scores, void *stream);
 
+/* No counterpart in the reference.  Cross-attention of one query token over `seqlen`
+ * f16 keys in the two-pass split form (the arithmetic of flash_cross_attn_split +
+ * flash_cross_attn_reduce, in one call) for callers that cannot allocate device
+ * memory: a decode loop driven from a real-time audio callback, where cudaMalloc and
+ * cudaFree may block or synchronise the whole device, or a host application that
+ * gives this library a fixed memory budget at start-up and no allocator afterwards.
+ * The split partials, which the reference's form keeps in a buffer the caller
+ * allocates, live here in a fixed array inside the library: it allocates nothing.
+ * q f32 [heads*64]; kc, vc f16 [seqlen][kv_dim]; out f32 [heads*64]; scores f32
+ * [heads][seqlen] (normalised) or NULL; at most 256 keys per split.  Limit: heads x
+ * nsplit <= 2048 (the array holds 2048 x 66 floats, 528 KB, on every GPU that loads
+ * the library, until the process exits); larger requests return MADI_EINVAL.  The
+ * first call on a device looks up the array's device address; make that first call
+ * before any stream capture.  Every call shares the one array: calls whose kernels
+ * overlap on the GPU (different streams, or other threads) race on it. */
+int madi_cross_attn_split_static(const float *q, const uint16_t *kc, const uint16_t *vc, int seqlen,
+                                 int heads, int kv_heads, int kv_dim, int nsplit, float *out,
+                                 float *scores, void *stream);
+
 /* Encoder self-attention, bidirectional (m4_flash_enc, m4_gemm.metal:255-407) on
  * the tensor cores: for each of `chunks` sequences of `seq` rows and each head h,
  * out[t][h*64..] = softmax(Q K^T * 0.125) V over the sequence, P rounded to f16,

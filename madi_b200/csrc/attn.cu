@@ -24,6 +24,8 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include <mutex>
+
 #include "common.cuh"
 #include "internal.h"
 
@@ -662,6 +664,41 @@ cudaError_t launch_cross_attn_part(float *part, const float *q, const void *kc, 
 cudaError_t launch_cross_attn_reduce(float *out, const float *part, int nsplit, float *sc, int seqlen, int write_sc,
                                      int nh, cudaStream_t st) {
     return launch_k(cross_attn_reduce_kernel, nh, kThr, 0, st, 1, out, part, nsplit, sc, seqlen, write_sc);
+}
+
+// ---------------------------------------------------------------- fixed-scratch split form
+// Partials [heads][nsplit][2 + 64] of madi_cross_attn_split_static.  Every GPU that
+// loads the library holds this array (540 672 bytes) until the process exits; host
+// code only ever sees a stand-in for it, so kernels get the device address that
+// cudaGetSymbolAddress returns for the current device.  The split pass writes every
+// (head, split) entry it covers before the reduce pass reads it, so nothing needs
+// clearing between calls.
+static __device__ __align__(256) float g_split_part[kSplitStaticMax * (2 + kHd)];
+
+cudaError_t launch_cross_attn_split_static(float *out, const float *q, const void *kc, const void *vc, float *sc,
+                                           int seqlen, int kvd, int nkv, int nh, int nsplit, cudaStream_t st) {
+    constexpr int kMaxDevices = 64;
+    static std::mutex mu;
+    static float *addr[kMaxDevices] = {};
+    if ((long)nh * nsplit > kSplitStaticMax) return cudaErrorInvalidValue;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    float *part = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (!addr[dev]) {
+            void *p = nullptr;
+            e = cudaGetSymbolAddress(&p, g_split_part);
+            if (e != cudaSuccess) return e;
+            addr[dev] = static_cast<float *>(p);
+        }
+        part = addr[dev];
+    }
+    e = launch_cross_attn_part(part, q, kc, vc, true, sc, sc != nullptr, seqlen, kvd, nkv, nh, nsplit, st);
+    if (e != cudaSuccess) return e;
+    return launch_cross_attn_reduce(out, part, nsplit, sc, seqlen, sc != nullptr, nh, st);
 }
 
 cudaError_t launch_self_attn(float *out, const float *q, const void *kc, const void *vc, bool kv_f16,

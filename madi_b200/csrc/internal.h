@@ -125,6 +125,12 @@ cudaError_t launch_cross_attn_part(float *part, const float *q, const void *kc, 
                                    cudaStream_t st);
 cudaError_t launch_cross_attn_reduce(float *out, const float *part, int nsplit, float *sc, int seqlen, int write_sc,
                                      int nh, cudaStream_t st);
+// Split form with the partials in a fixed device array (attn.cu): heads x nsplit at
+// most kSplitStaticMax.  Looks the array's device address up on each device's
+// first call.
+constexpr int kSplitStaticMax = 2048;
+cudaError_t launch_cross_attn_split_static(float *out, const float *q, const void *kc, const void *vc, float *sc,
+                                           int seqlen, int kvd, int nkv, int nh, int nsplit, cudaStream_t st);
 cudaError_t launch_self_attn(float *out, const float *q, const void *kc, const void *vc, bool kv_f16,
                              const uint32_t *pos, int slots, int kvd, int nkv, int nh, int max_tok, int *dev_err,
                              cudaStream_t st);

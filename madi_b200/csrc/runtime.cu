@@ -949,6 +949,27 @@ int madi_cross_attn(const float *q, const void *kc, const void *vc, int kv_dtype
     return e == cudaSuccess ? MADI_OK : cuda_fail(e, "madi_cross_attn");
 }
 
+int madi_cross_attn_split_static(const float *q, const uint16_t *kc, const uint16_t *vc, int seqlen, int heads,
+                                 int kv_heads, int kv_dim, int nsplit, float *out, float *scores, void *stream) {
+    if (!S.ready) return fail(MADI_ENOINIT, "madi_cross_attn_split_static: not initialised");
+    if (!q || !kc || !vc || !out) return fail(MADI_EINVAL, "madi_cross_attn_split_static: null argument");
+    if (int rc = attn_shape_ok("madi_cross_attn_split_static", 64, (uint32_t)kv_dim, (uint32_t)kv_heads,
+                               (uint32_t)heads))
+        return rc;
+    if (seqlen <= 0 || nsplit <= 0 || (seqlen + nsplit - 1) / nsplit > kAttnMaxChunk)
+        return fail(MADI_EINVAL, "madi_cross_attn_split_static: seqlen %d over %d splits (at most %d keys per split)",
+                    seqlen, nsplit, kAttnMaxChunk);
+    if ((long)heads * nsplit > kSplitStaticMax)
+        return fail(MADI_EINVAL,
+                    "madi_cross_attn_split_static: heads x nsplit = %ld exceeds the fixed scratch of %d partials",
+                    (long)heads * nsplit, kSplitStaticMax);
+    if (!aligned(q, 16) || !aligned(kc, 16) || !aligned(vc, 16) || !aligned(out, 16) || (scores && !aligned(scores, 16)))
+        return fail(MADI_EINVAL, "madi_cross_attn_split_static: buffers must be 16-byte aligned");
+    cudaError_t e = launch_cross_attn_split_static(out, q, kc, vc, scores, seqlen, kv_dim, kv_heads, heads, nsplit,
+                                                   pick_stream(stream));
+    return e == cudaSuccess ? MADI_OK : cuda_fail(e, "madi_cross_attn_split_static");
+}
+
 int madi_flash_attn_enc(const uint16_t *q, const uint16_t *k, const uint16_t *v, int stride, uint16_t *out,
                         int out_stride, int seq, int heads, int chunks, void *stream) {
     if (!S.ready) return fail(MADI_ENOINIT, "madi_flash_attn_enc: not initialised");
