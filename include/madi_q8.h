@@ -320,6 +320,18 @@ int madi_flash_attn_enc(const uint16_t *q, const uint16_t *k, const uint16_t *v,
 int madi_self_attn(const float *q, const void *kc, const void *vc, int kv_dtype, const uint32_t *pos, int slots,
                    int heads, int kv_heads, int kv_dim, int max_tok, float *out, void *stream);
 
+/* The tail of a greedy token step for m slots in one launch, equal to madi_step_advance,
+ * madi_logit_filter_rows (history tokens[s], step = the advanced pos[s]),
+ * madi_suppress_rows (ids, may be NULL with n_suppress 0) and madi_argmax_conf in turn:
+ * pos[s] += 1; row s of logits [m][vocab] filtered in place; tokens[s][pos[s]] =
+ * its greedy token (the reference's tie order) and conf[s][pos[s]] (conf may be
+ * NULL) = 1 / sum exp(z - zmax) when pos[s] < max_len.  The confidence's f32 sum runs
+ * in another order than argmax_conf's (within 1e-5 relative).  vocab <= 57344. */
+int madi_decode_tail(float *logits, int m, int vocab, uint32_t *tokens, int64_t tok_stride,
+                     int max_len, uint32_t *pos, float *conf, uint32_t sample_begin,
+                     uint32_t no_repeat_ngram, const uint32_t *suppress, int n_suppress,
+                     void *stream);
+
 /* suppress_list (graph_helpers.metal:97-107) on m logit rows in one launch:
  * logits[r][ids[j]] = -3.4e38 for every id < vocab (ids u32 [n], on the device). */
 int madi_suppress_rows(float *logits, int m, int vocab, const uint32_t *ids, int n, void *stream);

@@ -66,6 +66,7 @@ SIGNATURES = {
     "madi_logit_filter_rows": ([P, I, I, P, I, ctypes.c_int64, P, U32, U32, P], I),
     "madi_step_advance": ([P, I, P], I),
     "madi_argmax_rows": ([P, I, I, P, P], I),
+    "madi_decode_tail": ([P, I, I, P, ctypes.c_int64, I, P, P, U32, U32, P, I, P], I),
     "madi_cross_attn_split_static": ([P, P, P, I, I, I, I, I, P, P, P], I),
     "madi_suppress_rows": ([P, I, I, P, I, P], I),
     "madi_shard_argmax": ([P, I, I, ctypes.c_int64, U32, P, P, P], I),

@@ -21,6 +21,7 @@
 // shared memory that takes the upper slot only when strictly greater -- so ties
 // resolve as the reference's do (the first index of the winning thread, the
 // winning thread being the one whose 10-bit index is smallest when bit-reversed).
+#include <cooperative_groups.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
 
@@ -29,6 +30,8 @@
 
 namespace madi {
 namespace {
+
+namespace cg = cooperative_groups;
 
 constexpr float kNeg = -3.4e38f;
 
@@ -255,6 +258,143 @@ __global__ void merge_argmax_kernel(const float *__restrict__ vals, const uint32
     tokens[row] = bi;
 }
 
+// ---- the token step's tail in one launch: step_advance, logit_filter_indirect,
+// suppress_list and argmax_conf for m slots.  One cluster of kTailCtas CTAs per slot
+// (blockIdx.y), CTA r owning logits [r * per, r * per + per): each CTA writes the
+// filter's and the suppress list's bans that fall in its range (the same -3.4e38 the
+// separate kernels write), reads its range once into registers, reduces (max,
+// tie key) -- the reference's tie order as a total order, as the column-split head
+// does -- and the cluster combines through rank 0's shared memory; the exp sum of
+// the confidence runs over the registers against the global max.  Same tokens and
+// filtered logits as the four kernels; the confidence's f32 sum runs in another
+// order.
+constexpr int kTailCtas = 8;
+constexpr int kTailThr = 256;
+constexpr int kTailPer = 28;                              // values per thread (V <= 8 * 256 * 28)
+
+__global__ void __launch_bounds__(kTailThr) decode_tail_kernel(float *__restrict__ logits, int V,
+                                                               uint32_t *__restrict__ tokens, long long stride,
+                                                               int max_len, uint32_t *__restrict__ pos,
+                                                               float *__restrict__ conf, uint32_t sample_begin,
+                                                               uint32_t no_repeat_ngram,
+                                                               const uint32_t *__restrict__ sup, int nsup) {
+    __shared__ float wv[kTailThr / 32];
+    __shared__ uint64_t wk[kTailThr / 32];
+    __shared__ float cv[kTailCtas];                       // rank 0: the CTAs' best values
+    __shared__ uint64_t ck[kTailCtas];
+    __shared__ float csum[kTailCtas];                     // rank 0: the CTAs' exp sums
+    __shared__ float gmax;                                // every CTA: the slot's max
+    __shared__ uint64_t gkey;                             // rank 0: the winner's key
+    const int r = blockIdx.x, s = blockIdx.y, tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
+    pdl_trigger();
+    pdl_wait();
+    asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
+    float *lg = logits + (size_t)s * V;
+    const uint32_t *past = tokens + (size_t)s * stride;
+    const uint32_t step = pos[s] + 1u;                    // step_advance
+    const int per = (V + kTailCtas - 1) / kTailCtas;
+    const int lo = r * per, hi = min(V, lo + per);
+    auto ban = [&](uint32_t t) {
+        if (t < (uint32_t)V && (int)t >= lo && (int)t < hi) lg[t] = kNeg;
+    };
+    // logit_filter_indirect (graph_helpers.metal:109-160) with step = the advanced position
+    const bool hist_ok = step <= (uint32_t)max_len;
+    if (tid == 0) {
+        if (hist_ok && step >= 3 && step >= sample_begin + 3) {
+            const uint32_t t1 = past[step - 1], t2 = past[step - 2], t3 = past[step - 3];
+            if (t1 == t2 && t2 == t3) ban(t1);
+        }
+        if (hist_ok && no_repeat_ngram >= 2 && step >= no_repeat_ngram && sample_begin <= step &&
+            step >= sample_begin + no_repeat_ngram) {
+            const uint32_t kWin = 16;
+            const uint32_t nn = no_repeat_ngram;
+            const uint32_t suf = step - (nn - 1);
+            const uint32_t j0 = (step > sample_begin + kWin) ? (step - kWin) : sample_begin;
+            for (uint32_t j = j0; j + nn <= step; ++j) {
+                bool match = true;
+                for (uint32_t k = 0; k + 1 < nn; ++k)
+                    if (past[j + k] != past[suf + k]) { match = false; break; }
+                if (match) ban(past[j + nn - 1]);
+            }
+        }
+        if (step < sample_begin + 4) {
+            ban(220u);
+            ban(50257u);
+        }
+    }
+    for (int t = max(lo, 50258) + tid; t < hi; t += kTailThr) lg[t] = kNeg;
+    for (int j = tid; j < nsup; j += kTailThr) ban(sup[j]);                 // suppress_list
+    __syncthreads();
+    float v[kTailPer];
+    float bv = -INFINITY;
+    uint64_t bk = ~0ull;
+#pragma unroll
+    for (int i = 0; i < kTailPer; ++i) {
+        const int t = lo + tid + i * kTailThr;
+        v[i] = t < hi ? lg[t] : -INFINITY;
+    }
+#pragma unroll
+    for (int i = 0; i < kTailPer; ++i) {
+        const int t = lo + tid + i * kTailThr;
+        if (t < hi) {
+            const uint64_t k = tie_key((uint32_t)t);
+            if (better(v[i], k, bv, bk)) { bv = v[i]; bk = k; }
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const uint64_t ok = __shfl_xor_sync(0xffffffffu, bk, o);
+        if (better(ov, ok, bv, bk)) { bv = ov; bk = ok; }
+    }
+    if (lane == 0) { wv[warp] = bv; wk[warp] = bk; }
+    __syncthreads();
+    cg::cluster_group cluster = cg::this_cluster();
+    asm volatile("barrier.cluster.wait;" ::: "memory");
+    if (tid == 0) {
+        for (int w = 1; w < kTailThr / 32; ++w)
+            if (better(wv[w], wk[w], bv, bk)) { bv = wv[w]; bk = wk[w]; }
+        *cluster.map_shared_rank(&cv[r], 0) = bv;
+        *cluster.map_shared_rank(&ck[r], 0) = bk;
+    }
+    cluster.sync();
+    if (r == 0 && tid < kTailCtas) {
+        // rank 0: the slot's max, to every CTA
+        float gv = cv[0];
+        uint64_t gk = ck[0];
+        for (int c = 1; c < kTailCtas; ++c)
+            if (better(cv[c], ck[c], gv, gk)) { gv = cv[c]; gk = ck[c]; }
+        *cluster.map_shared_rank(&gmax, tid) = gv;
+        if (tid == 0) gkey = gk;
+    }
+    cluster.sync();
+    const float zmax = gmax;
+    float ls = 0.f;
+#pragma unroll
+    for (int i = 0; i < kTailPer; ++i)
+        if (lo + tid + i * kTailThr < hi) ls += expf(v[i] - zmax);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, o);
+    if (lane == 0) wv[warp] = ls;
+    __syncthreads();
+    if (tid == 0) {
+        float cs = 0.f;
+        for (int w = 0; w < kTailThr / 32; ++w) cs += wv[w];
+        *cluster.map_shared_rank(&csum[r], 0) = cs;
+    }
+    cluster.sync();
+    if (r == 0 && tid == 0) {
+        float tot = 0.f;
+        for (int c = 0; c < kTailCtas; ++c) tot += csum[c];
+        pos[s] = step;
+        if (step < (uint32_t)max_len) {
+            tokens[(size_t)s * stride + step] = (uint32_t)gkey;
+            if (conf) conf[(size_t)s * stride + step] = 1.0f / tot;
+        }
+    }
+}
+
 }  // namespace
 
 cudaError_t launch_emb_q8(float *out, const int8_t *qs, const __half *scales, const uint32_t *tokens,
@@ -295,6 +435,15 @@ cudaError_t launch_logit_filter(float *logits, const uint32_t *past, const uint3
                                 cudaStream_t st) {
     return launch_k(logit_filter_kernel, rows, 256, 0, st, 1, logits, past, step_ptr, sample_begin, no_repeat_ngram, V,
                     past_len, past_stride);
+}
+
+int decode_tail_max_vocab() { return kTailCtas * kTailThr * kTailPer; }
+
+cudaError_t launch_decode_tail(float *logits, int m, int V, uint32_t *tokens, long long stride, int max_len,
+                               uint32_t *pos, float *conf, uint32_t sample_begin, uint32_t no_repeat_ngram,
+                               const uint32_t *sup, int nsup, cudaStream_t st) {
+    return launch_k(decode_tail_kernel, dim3(kTailCtas, m), kTailThr, 0, st, kTailCtas, logits, V, tokens, stride,
+                    max_len, pos, conf, sample_begin, no_repeat_ngram, sup, nsup);
 }
 
 cudaError_t launch_shard_argmax(const float *logits, long long row_stride, int n, uint32_t h0, int m, float *vals,

@@ -137,6 +137,12 @@ cudaError_t launch_self_attn(float *out, const float *q, const void *kc, const v
 // ---- encoder self-attention on the tensor cores (flash_enc.cu); head_dim 64
 cudaError_t launch_flash_enc(const __half *q, const __half *k, const __half *v, int stride, __half *out,
                              int out_stride, int seq, int heads, int chunks, int *dev_err, cudaStream_t st);
+// step_advance + logit_filter_indirect + suppress_list + argmax_conf for m slots in
+// one launch (V <= decode_tail_max_vocab()).
+int decode_tail_max_vocab();
+cudaError_t launch_decode_tail(float *logits, int m, int V, uint32_t *tokens, long long stride, int max_len,
+                               uint32_t *pos, float *conf, uint32_t sample_begin, uint32_t no_repeat_ngram,
+                               const uint32_t *sup, int nsup, cudaStream_t st);
 cudaError_t launch_shard_argmax(const float *logits, long long row_stride, int n, uint32_t h0, int m, float *vals,
                                 uint32_t *idx, cudaStream_t st);
 cudaError_t launch_merge_argmax(const float *vals, const uint32_t *idx, int world, int m, uint32_t *tokens,

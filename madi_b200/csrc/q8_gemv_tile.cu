@@ -35,6 +35,8 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include <type_traits>
+
 #include "common.cuh"
 #include "internal.h"
 
@@ -182,46 +184,62 @@ MADI_DEV void store_unit(const GemvArgs &p, int tile, int g8, int t, const float
     }
 }
 
+// One quad column (4 consecutive k) of all M token rows of x: load = true fetches
+// it into v, load = false converts v and stores it in fragment order.
+template <typename XT>
+MADI_DEV void stage_x_quad(const GemvArgs &p, uint8_t *xs, const XT *xrow, int kq, bool have,
+                           typename std::conditional<sizeof(XT) == 4, float4, uint2>::type (&v)[8], bool load) {
+    constexpr bool kSplit = sizeof(XT) == 4;
+    const int M = p.M, K = p.K;
+    const int kl = kq << 2;
+    if (!have) return;
+    if (load) {
+#pragma unroll
+        for (int m = 0; m < 8; ++m)
+            if (m < M) {
+                if constexpr (kSplit) v[m] = __ldcg(reinterpret_cast<const float4 *>(xrow + (size_t)m * K + kl));
+                else v[m] = __ldcg(reinterpret_cast<const uint2 *>(xrow + (size_t)m * K + kl));
+            }
+        return;
+    }
+    const int slot0 = ((kl >> 5) * 2 + ((kl & 7) >> 2)) * M * 4 + ((kl & 31) >> 3);
+#pragma unroll
+    for (int m = 0; m < 8; ++m)
+        if (m < M) {
+            if constexpr (kSplit) {
+                const float4 f = v[m];
+                const __half2 h01 = __floats2half2_rn(f.x, f.y);
+                const __half2 h23 = __floats2half2_rn(f.z, f.w);
+                const __half2 l01 = __floats2half2_rn(f.x - __low2float(h01), f.y - __high2float(h01));
+                const __half2 l23 = __floats2half2_rn(f.z - __low2float(h23), f.w - __high2float(h23));
+                reinterpret_cast<uint4 *>(xs)[slot0 + m * 4] =
+                    make_uint4(h2_as_u32(h01), h2_as_u32(h23), h2_as_u32(l01), h2_as_u32(l23));
+            } else {
+                reinterpret_cast<uint2 *>(xs)[slot0 + m * 4] = v[m];
+            }
+        }
+}
+
 // Stage the x slice [M][kb0*32, kb0*32 + KS) once in fragment order: slot
 // (lkb, s, m, t) holds x[m][(kb0 + lkb)*32 + 8t + 4s + 0..3] as f16 hi (and, for
 // f32 x, f16 lo) pairs.  Thread `tid` of `nthr` owns the quads kq = tid, tid +
-// nthr, ... and fetches that quad of all M token rows at once (one L2 round trip
-// per quad column), then converts and stores.  x may have been written by the
-// kernel this one overlaps under programmatic dependent launch, so it is read on
-// the coherent L2 path (ld.global.cg), never through the non-coherent one.
+// nthr, ... and fetches a quad of all M token rows at once; two quads' loads are
+// in flight before either is converted, so a slice of up to 2 * nthr quads costs
+// one L2 round trip.  x may have been written by the kernel this one overlaps
+// under programmatic dependent launch, so it is read on the coherent L2 path
+// (ld.global.cg), never through the non-coherent one.
 template <typename XT>
 MADI_DEV void stage_x(const GemvArgs &p, uint8_t *xs, int kb0, int KS, int tid, int nthr) {
-    constexpr bool kSplit = sizeof(XT) == 4;
-    const int M = p.M, K = p.K;
+    using V = typename std::conditional<sizeof(XT) == 4, float4, uint2>::type;
     const int qrow = KS >> 2;
     const XT *xrow = reinterpret_cast<const XT *>(p.x) + (size_t)kb0 * 32;
-    for (int kq = tid; kq < qrow; kq += nthr) {
-        const int kl = kq << 2;
-        const int slot0 = ((kl >> 5) * 2 + ((kl & 7) >> 2)) * M * 4 + ((kl & 31) >> 3);
-        if constexpr (kSplit) {
-            float4 f[8];
-#pragma unroll
-            for (int m = 0; m < 8; ++m)
-                if (m < M) f[m] = __ldcg(reinterpret_cast<const float4 *>(xrow + (size_t)m * K + kl));
-#pragma unroll
-            for (int m = 0; m < 8; ++m)
-                if (m < M) {
-                    const __half2 h01 = __floats2half2_rn(f[m].x, f[m].y);
-                    const __half2 h23 = __floats2half2_rn(f[m].z, f[m].w);
-                    const __half2 l01 = __floats2half2_rn(f[m].x - __low2float(h01), f[m].y - __high2float(h01));
-                    const __half2 l23 = __floats2half2_rn(f[m].z - __low2float(h23), f[m].w - __high2float(h23));
-                    reinterpret_cast<uint4 *>(xs)[slot0 + m * 4] =
-                        make_uint4(h2_as_u32(h01), h2_as_u32(h23), h2_as_u32(l01), h2_as_u32(l23));
-                }
-        } else {
-            uint2 u[8];
-#pragma unroll
-            for (int m = 0; m < 8; ++m)
-                if (m < M) u[m] = __ldcg(reinterpret_cast<const uint2 *>(xrow + (size_t)m * K + kl));
-#pragma unroll
-            for (int m = 0; m < 8; ++m)
-                if (m < M) reinterpret_cast<uint2 *>(xs)[slot0 + m * 4] = u[m];
-        }
+    for (int kq = tid; kq < qrow; kq += 2 * nthr) {
+        V a[8], b[8];
+        const bool hb = kq + nthr < qrow;
+        stage_x_quad<XT>(p, xs, xrow, kq, true, a, true);
+        stage_x_quad<XT>(p, xs, xrow, kq + nthr, hb, b, true);
+        stage_x_quad<XT>(p, xs, xrow, kq, true, a, false);
+        stage_x_quad<XT>(p, xs, xrow, kq + nthr, hb, b, false);
     }
 }
 

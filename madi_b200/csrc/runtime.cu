@@ -910,6 +910,21 @@ int madi_suppress_rows(float *logits, int m, int vocab, const uint32_t *ids, int
     return e == cudaSuccess ? MADI_OK : cuda_fail(e, "madi_suppress_rows");
 }
 
+int madi_decode_tail(float *logits, int m, int vocab, uint32_t *tokens, int64_t tok_stride, int max_len, uint32_t *pos,
+                     float *conf, uint32_t sample_begin, uint32_t no_repeat_ngram, const uint32_t *suppress,
+                     int n_suppress, void *stream) {
+    if (!S.ready) return fail(MADI_ENOINIT, "madi_decode_tail: not initialised");
+    if (!logits || !tokens || !pos || (n_suppress > 0 && !suppress) || n_suppress < 0)
+        return fail(MADI_EINVAL, "madi_decode_tail: null argument");
+    if (m <= 0 || m > 65535 || vocab <= 0 || vocab > decode_tail_max_vocab() || max_len <= 0 ||
+        (m > 1 && tok_stride < max_len))
+        return fail(MADI_EINVAL, "madi_decode_tail: bad shape (m=%d vocab=%d <= %d, max_len=%d)", m, vocab,
+                    decode_tail_max_vocab(), max_len);
+    cudaError_t e = launch_decode_tail(logits, m, vocab, tokens, (long long)tok_stride, max_len, pos, conf, sample_begin,
+                                       no_repeat_ngram, suppress, n_suppress, pick_stream(stream));
+    return e == cudaSuccess ? MADI_OK : cuda_fail(e, "madi_decode_tail");
+}
+
 int madi_argmax_rows(const float *logits, int m, int vocab, uint32_t *tokens, void *stream) {
     if (!S.ready) return fail(MADI_ENOINIT, "madi_argmax_rows: not initialised");
     if (!logits || !tokens || m <= 0 || vocab <= 0) return fail(MADI_EINVAL, "madi_argmax_rows: bad argument");

@@ -178,11 +178,8 @@ class Decoder:
             q8.linear(L.fc2, self.mh, bias=L.m2b, epi=q8.EPI_BIAS_RES, residual=self.x, out=self.x, **s)
         q8.layer_norm(self.x, *self.ln_post, eps=EPS, out=self.xb, **s)
         q8.linear(self.emb, self.xb, out=self.logits, **s)
-        greedy.step_advance(self.pos, **s)
-        greedy.logit_filter_rows(self.logits, self.tokens, self.pos, sample_begin, no_repeat_ngram, **s)
-        if suppress is not None:
-            greedy.suppress_rows(self.logits, suppress, **s)
-        greedy.argmax_conf(self.logits, self.tokens, self.pos, self.conf, **s)
+        greedy.decode_tail(self.logits, self.tokens, self.pos, self.conf, sample_begin, no_repeat_ngram, suppress,
+                           **s)
 
     def step_bytes(self) -> int:
         """HBM bytes one token step must read: every Q8 weight and scale once, the

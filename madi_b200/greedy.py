@@ -4,8 +4,8 @@ position counters and the logits in device memory, a whole token step runs with
 no host round trip and replays as a CUDA graph.
 
 Thin wrappers of the C ABI (madi_emb_lookup_q8, madi_emb_pos_q8, madi_argmax_conf,
-madi_logit_filter, madi_logit_filter_rows, madi_suppress_rows, madi_step_advance) on
-torch CUDA tensors.
+madi_logit_filter, madi_logit_filter_rows, madi_suppress_rows, madi_step_advance,
+madi_decode_tail) on torch CUDA tensors.
 """
 import ctypes
 from typing import Optional
@@ -112,6 +112,27 @@ def suppress_rows(logits: torch.Tensor, ids: torch.Tensor, stream=None) -> None:
     m, vocab = logits.shape
     _lib.check(_lib.load().madi_suppress_rows(logits.data_ptr(), m, vocab, ids.data_ptr(), ids.numel(),
                                               _stream(stream)), "madi_suppress_rows")
+
+
+def decode_tail(logits: torch.Tensor, tokens: torch.Tensor, pos: torch.Tensor, conf: Optional[torch.Tensor] = None,
+                sample_begin: int = 1, no_repeat_ngram: int = 0, suppress: Optional[torch.Tensor] = None,
+                stream=None) -> None:
+    """step_advance, logit_filter_rows, suppress_rows and argmax_conf in one launch:
+    pos[s] += 1, logits [m][vocab] filtered in place, tokens[s][pos[s]] (and conf) written."""
+    if logits.dim() != 2 or logits.dtype != torch.float32 or not logits.is_contiguous():
+        raise ValueError("logits must be a contiguous f32 [m][vocab] tensor")
+    m, vocab = logits.shape
+    if tokens.dim() != 2 or tokens.shape[0] != m or not tokens.is_contiguous() or pos.numel() != m:
+        raise ValueError("tokens must be a contiguous [m][max_len] tensor and pos hold one position per slot")
+    max_len = tokens.shape[1]
+    if conf is not None and (conf.shape != tokens.shape or conf.dtype != torch.float32 or not conf.is_contiguous()):
+        raise ValueError("conf must be f32 shaped like tokens")
+    nsup = 0 if suppress is None else suppress.numel()
+    rc = _lib.load().madi_decode_tail(logits.data_ptr(), m, vocab, tokens.data_ptr(), max_len, max_len,
+                                      pos.data_ptr(), None if conf is None else conf.data_ptr(), int(sample_begin),
+                                      int(no_repeat_ngram), None if suppress is None else suppress.data_ptr(), nsup,
+                                      _stream(stream))
+    _lib.check(rc, "madi_decode_tail")
 
 
 def step_advance(pos: torch.Tensor, stream=None) -> None:

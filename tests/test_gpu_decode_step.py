@@ -202,6 +202,45 @@ def test_suppress_rows(madi, oracle):
         assert np.array_equal(got[r], oracle.suppress(L[r], ids)), f"row {r}"
 
 
+def test_decode_tail_matches_the_four_kernels(madi, oracle):
+    """madi_decode_tail (one launch) against step_advance + logit_filter_rows +
+    suppress_rows + argmax_conf on the same rows: every filter case, a row whose
+    maxima tie across the cluster's CTA ranges and a row of many small-integer ties;
+    filtered logits, tokens and positions bit-exact, confidence within 1e-5."""
+    import torch
+    from madi_b200 import greedy
+    m, max_len = len(FILTER_CASES) + 2, 64
+    past = np.zeros((m, max_len), np.uint32)
+    pos = np.zeros(m, np.uint32)
+    for r, (hist, step, _, _) in enumerate(FILTER_CASES):
+        past[r, :len(hist)] = hist
+        pos[r] = step - 1                                  # advanced to `step` by the tail
+    g = np.random.default_rng(90)
+    L = np.stack([_logit_rows(80 + r)[0] for r in range(m)])
+    L[-2, [7, 26000, 40000, 51000]] = 60.0                 # a tie spread over CTA ranges
+    L[-1] = g.integers(-3, 4, VOCAB).astype(np.float32)    # thousands of ties at the max
+    past[-2:, :6] = g.integers(0, 50000, (2, 6))
+    pos[-2:] = 5
+    sup = np.array([50257, 11, 51000, 99999], np.uint32)
+    for sb, nrng in [(1, 0), (1, 3), (3, 2)]:
+        a, b = _t(L), _t(L)
+        ta, tb = _u32(past), _u32(past)
+        pa, pb = _u32(pos), _u32(pos)
+        ca = torch.full((m, max_len), -1.0, dtype=torch.float32, device="cuda")
+        cb = ca.clone()
+        greedy.decode_tail(a, ta, pa, ca, sb, nrng, _u32(sup))
+        greedy.step_advance(pb)
+        greedy.logit_filter_rows(b, tb, pb, sb, nrng)
+        greedy.suppress_rows(b, _u32(sup))
+        greedy.argmax_conf(b, tb, pb, cb)
+        torch.cuda.synchronize()
+        assert torch.equal(a, b), f"filtered logits differ (sample_begin {sb}, ngram {nrng})"
+        assert torch.equal(ta, tb) and torch.equal(pa, pb), f"tokens / positions differ ({sb}, {nrng})"
+        ca, cb = ca.cpu().numpy(), cb.cpu().numpy()
+        assert np.array_equal(ca == -1.0, cb == -1.0)
+        assert np.abs(ca - cb).max() <= 1e-5 * np.abs(cb).max()
+
+
 def test_emb_pos_q8(madi, oracle):
     """Fused embedding + positional embedding for 5 slots, bit-exact against the
     lookup followed by the f32 add; a position past max_pos adds nothing."""
