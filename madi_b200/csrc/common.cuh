@@ -97,12 +97,17 @@ MADI_DEV void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
                  "r"(bytes)
                  : "memory");
 }
+// A waiting thread may sleep up to kSuspendNs inside one try_wait (it wakes when the
+// phase completes), so a warp that waits does not keep issuing polling
+// instructions beside the warps that work; the callers' abort-flag and clock-budget
+// checks still run at least this often.
+constexpr uint32_t kSuspendNs = 1000000;
 MADI_DEV bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
-        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\tselp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendNs)
         : "memory");
     return ok != 0;
 }

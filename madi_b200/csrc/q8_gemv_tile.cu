@@ -349,7 +349,9 @@ __global__ void __launch_bounds__(kThreads, 2)
                 for (int i = 0; i < nki; ++i) {
                     const uint2 wa = *reinterpret_cast<const uint2 *>(st + off0 + i * kBoxBytes);
                     const uint2 wb = *reinterpret_cast<const uint2 *>(st + off1 + i * kBoxBytes);
-                    float bh[4] = {0.f, 0.f, 0.f, 0.f}, bl[4] = {0.f, 0.f, 0.f, 0.f};
+                    // the block's products (both k16 halves; for f32 x, hi and lo) meet in
+                    // one f32 accumulator, then take the block scale
+                    float bs[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
                     for (int sp = 0; sp < 2; ++sp) {
                         __half2 a_lo0, a_hi0, a_lo1, a_hi1;
@@ -359,19 +361,19 @@ __global__ void __launch_bounds__(kThreads, 2)
                         const int slot = xbase + i * xstep + sp * M * 4;
                         if constexpr (kSplit) {
                             const uint4 xv = gval ? reinterpret_cast<const uint4 *>(xs)[slot] : make_uint4(0u, 0u, 0u, 0u);
-                            mma16816(bh, a, xv.x, xv.y);
-                            mma16816(bl, a, xv.z, xv.w);
+                            mma16816(bs, a, xv.x, xv.y);
+                            mma16816(bs, a, xv.z, xv.w);
                         } else {
                             const uint2 xv = gval ? reinterpret_cast<const uint2 *>(xs)[slot] : make_uint2(0u, 0u);
-                            mma16816(sp == 0 ? bh : bl, a, xv.x, xv.y);
+                            mma16816(bs, a, xv.x, xv.y);
                         }
                     }
                     const float f0 = __half2float(s0p[8 * i]);
                     const float f1 = __half2float(s1p[8 * i]);
-                    acc[0] = fmaf(bh[0] + bl[0], f0, acc[0]);
-                    acc[1] = fmaf(bh[1] + bl[1], f0, acc[1]);
-                    acc[2] = fmaf(bh[2] + bl[2], f1, acc[2]);
-                    acc[3] = fmaf(bh[3] + bl[3], f1, acc[3]);
+                    acc[0] = fmaf(bs[0], f0, acc[0]);
+                    acc[1] = fmaf(bs[1], f0, acc[1]);
+                    acc[2] = fmaf(bs[2], f1, acc[2]);
+                    acc[3] = fmaf(bs[3], f1, acc[3]);
                 }
             }
             __syncwarp();
