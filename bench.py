@@ -21,7 +21,7 @@ Workload (N=1 is BASELINE config 1 at B=16, the largest single-GPU config):
           with pinned HOST buffers: per step H2D of X and D2H of Y inside the
           timed region.
   long_audio: 120 chunks of synthetic log-mel sharded over the
-          ranks; per batch of 8 chunks the whole encoder (conv stem, 32 Q8 layers,
+          ranks; per batch of <= 16 chunks the whole encoder (conv stem, 32 Q8 layers,
           ln_post), cross K/V, then exactly 224 greedy tokens per chunk (EOT
           suppressed) -- chunks/s from pinned host mel to host tokens, slowest rank.
 Multi-GPU: one process per GPU (torchrun), each rank runs its own B chunks
@@ -409,8 +409,9 @@ def main_madi(args, world, rank, local):
 def long_audio_leg(args, world, rank, dev):
     """`--chunks` independent 30 s chunks (synthetic log-mel, f16
     [128][3000] each) sharded over the ranks; each rank runs the whole encoder (conv
-    stem, 32 layers, ln_post) on batches of 8 chunks, then the 4-layer greedy decoder
-    for exactly `--tokens` tokens per chunk (EOT suppressed), replicated vocab head.
+    stem, 32 layers, ln_post) on even batches of at most 16 chunks, then the 4-layer
+    greedy decoder (one token slot per chunk) for exactly `--tokens` tokens per chunk
+    (EOT suppressed), replicated vocab head.
     Timed from the pinned host mel to the tokens back in host memory; one untimed
     batch first (module load, graph capture).  chunks/s = all chunks / the slowest
     rank's time (strong scaling: the total is fixed)."""
@@ -420,10 +421,12 @@ def long_audio_leg(args, world, rank, dev):
 
     from madi_b200 import pipeline
 
-    slots = 8
     per = math.ceil(args.chunks / world)
     lo = min(args.chunks, rank * per)
     mine = max(0, min(args.chunks, lo + per) - lo)
+    # even batches of at most 16 chunks (token slots): 120 -> 8 x 15, 15 -> 1 x 15
+    nb = max(1, math.ceil(mine / 16))
+    slots = max(1, math.ceil(mine / nb))
     tr = pipeline.Transcriber(slots=slots, enc_layers=32, tokens=args.tokens, seed=1, device=dev)
     mel_h = torch.from_numpy(pipeline.synthetic_mel(max(mine, 1), first=lo)).pin_memory()
     mel_d = torch.empty((slots,) + tuple(mel_h.shape[1:]), dtype=torch.float16, device=dev)
@@ -462,7 +465,7 @@ def long_audio_leg(args, world, rank, dev):
             "chunks_per_s": args.chunks / (ms_max / 1e3), "ms_total": ms_max, "scaling": "strong",
             "encoder_ms_per_batch": enc_avg, "decoder_ms_per_batch": dec_avg,
             "decoder_ms_per_token_step": dec_avg / args.tokens,
-            "encoder": "conv stem (PyTorch f16 conv1d) + 32 Q8 layers + ln_post, 8 chunks per batch",
+            "encoder": f"conv stem (PyTorch f16 conv1d) + 32 Q8 layers + ln_post, {slots} chunks per batch",
             "decoder": "4 Q8 layers, replicated head, one CUDA graph per token step, EOT suppressed",
             "h2d_bytes": int(mine * 128 * 3000 * 2), "d2h_bytes": int(mine * args.tokens * 4),
             "first_tokens_rank0": toks[0, :8].tolist() if mine else [],

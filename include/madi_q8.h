@@ -176,13 +176,14 @@ int   madi_num_sms(void);
  * per-projection pairs (kDeq + m4_gemm_bias / _bias_gelu / _nn, encoder.zig:262-304;
  * the gemv_q8* family, decoder.zig:155-200; the batched f16 projection,
  * decoder.zig:337-341).  One call, no dequant scratch:
- *   m > 8 : tcgen05 tensor-core GEMM, X f16, Y f16, residual f16 (Y f32 is
- *           accepted with MADI_EPI_NONE: unrounded f32 sums, e.g. the logits of
- *           a vocab head over more than 8 token slots); f16 dequantised
- *           weights, f32 accumulation.
- *   m <= 8: bandwidth-bound skinny GEMM, X f32 or f16, Y f32 or f16,
+ *   m > 16 (or 9..16 when K % 256 != 0): tcgen05 tensor-core GEMM, X f16, Y f16,
+ *           residual f16 (Y f32 is accepted with MADI_EPI_NONE: unrounded f32
+ *           sums, e.g. the logits of a vocab head over many token slots); f16
+ *           dequantised weights, f32 accumulation.
+ *   m <= 16: bandwidth-bound skinny GEMM, X f32 or f16, Y f32 or f16,
  *           residual with Y's type and may alias Y; f32 semantics
- *           (exact int8 weights, per-block f32 scale).
+ *           (exact int8 weights, per-block f32 scale).  (The reference's GEMV
+ *           family takes one token; its batched decode takes up to 8 slots.)
  * bias: f32 or f16 per bias_dtype, required unless epi == MADI_EPI_NONE.
  * x, y, residual: row-major, rows of k (x) / n (y, residual) elements, 16-byte
  * aligned base pointers.  stream: cudaStream_t or NULL (library stream). */
@@ -191,7 +192,7 @@ int madi_q8_linear(const madi_q8w *w, const void *x, int x_dtype, int m,
                    const void *residual, void *y, int y_dtype, void *stream);
 
 /* Decoder self-attention QKV projection with the KV-cache store fused
- * (gemv_q8_qkv, graph_helpers.metal:527-567) for m <= 8 token slots.
+ * (gemv_q8_qkv, graph_helpers.metal:527-567) for m <= 16 token slots.
  * w: stacked [3D][D]; x f32 [m][D].  For slot s: q_out[s][0..D) = q + qb;
  * kc[s*cache_stride + pos[s]*D + j] = k_j;  vc[...] = v_j + vb[j].
  * pos: device u32 [m] (read on the device, so a graph can replay it);

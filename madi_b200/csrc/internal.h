@@ -89,6 +89,9 @@ struct GemmArgs {
 cudaError_t launch_gemm_tc(const GemmArgs &a, int epi, int num_sms, cudaStream_t st);
 // The smallest M routed to variant (a) by madi_q8_linear.
 constexpr int kGemmMinM = 9;
+// The largest M the streaming skinny GEMM (q8_gemv_tile.cu) takes: two groups of 8
+// token rows per weight fragment.
+constexpr int kGemvMaxM = 16;
 
 // ---------------------------------------------------------------- residual + LayerNorm (res_ln.cu)
 constexpr int kLnMaxD = 2048;   // row width limit of the register-resident row kernel (D % 128 == 0)

@@ -51,8 +51,9 @@ constexpr int kTileRows = 16;
 constexpr int kMaxStages = 8;
 constexpr int kMaxCs = 4;
 constexpr int kBoxBytes = kTileRows * 256;                  // one [16][2][128 B] weight box
-constexpr size_t kRedBytes = 2 * kConsumers * 32 * 16;      // 2 units x 8 warps x 32 lanes x float4
-constexpr size_t kXredBytes = kMaxCs * 32 * 16;             // per-rank CTA sums, on rank 0
+constexpr int kMaxM = 16;                                   // token rows: 1 or 2 groups of 8 (the MMA's n)
+constexpr size_t kRedBytes = 2 * kConsumers * 32 * 16;      // per token group: 2 units x 8 warps x 32 lanes x float4
+constexpr size_t kXredBytes = kMaxCs * 32 * 16;             // per token group: per-rank CTA sums, on rank 0
 constexpr size_t kSmemCap = 227 * 1024;                     // opt-in maximum per CTA
 constexpr size_t kSmemHalf = 112 * 1024;                    // two CTAs per SM (228 KB less reserves)
 
@@ -75,8 +76,9 @@ __host__ __device__ constexpr size_t stage_bytes(int KS) {
     return ((size_t)kTileRows * KS + (size_t)kTileRows * (KS / 32) * 2 + 1023) & ~size_t(1023);
 }
 __host__ __device__ constexpr size_t x_bytes(int M, int KS, bool x_f32) { return (size_t)M * KS * (x_f32 ? 4 : 2); }
+__host__ __device__ constexpr int groups(int M) { return (M + 7) / 8; }
 __host__ __device__ constexpr size_t fixed_bytes(int M, int KS, bool x_f32) {
-    return 1024 + x_bytes(M, KS, x_f32) + kRedBytes + kXredBytes + sizeof(TileBars);
+    return 1024 + x_bytes(M, KS, x_f32) + (size_t)groups(M) * (kRedBytes + kXredBytes) + sizeof(TileBars);
 }
 size_t plan_smem(int M, const TilePlan &pl, bool x_f32) {
     return fixed_bytes(M, pl.kslice, x_f32) + (size_t)pl.stages * stage_bytes(pl.kslice);
@@ -87,7 +89,7 @@ size_t plan_smem(int M, const TilePlan &pl, bool x_f32) {
 // per unit, persistent when units outnumber the CTA slots.  Two CTAs per SM when
 // shared memory allows, else one.  Last resort, a K split over more than a wave.
 bool make_plan(int M, int N, int K, bool x_f32, int num_sms, TilePlan *pl, int *grid) {
-    if (M < 1 || M > 8 || N < 1 || K < 256 || K % 256 != 0) return false;
+    if (M < 1 || M > kMaxM || N < 1 || K < 256 || K % 256 != 0) return false;
     const int tiles = (N + kTileRows - 1) / kTileRows;
     for (int cs = kMaxCs; cs >= 2; cs /= 2) {
         if (K % (256 * cs) != 0 || (long)tiles * cs > 2L * num_sms) continue;
@@ -111,15 +113,18 @@ bool make_plan(int M, int N, int K, bool x_f32, int num_sms, TilePlan *pl, int *
         *grid = clusters;
         return true;
     }
-    // Neither fits (an f32 x slice of a long K, e.g. 8 x 5120): split K even though
-    // the clusters then take more than one wave.
-    for (int cs = kMaxCs; cs >= 2; cs /= 2) {
-        if (K % (256 * cs) != 0) continue;
-        const TilePlan c{cs, K / cs, 1, tiles};
-        if (c.kslice / 32 > 256 || plan_smem(M, c, x_f32) > kSmemHalf) continue;
-        *pl = c;
-        *grid = tiles * cs;
-        return true;
+    // Neither fits (an f32 x slice of a long K, e.g. 8 or 16 x 5120): split K even
+    // though the clusters then take more than one wave, at two CTAs per SM if the
+    // slice fits, else one.
+    for (const size_t budget : {kSmemHalf, kSmemCap}) {
+        for (int cs = kMaxCs; cs >= 2; cs /= 2) {
+            if (K % (256 * cs) != 0) continue;
+            const TilePlan c{cs, K / cs, 1, tiles};
+            if (c.kslice / 32 > 256 || plan_smem(M, c, x_f32) > budget) continue;
+            *pl = c;
+            *grid = tiles * cs;
+            return true;
+        }
     }
     return false;
 }
@@ -148,15 +153,15 @@ MADI_DEV uint32_t frag_offset(int row, int w, int t) {
     return (uint32_t)(L * 128 + ((unit ^ (L & 7)) << 4) + ((t & 1) << 3));
 }
 
-// Writes one unit's outputs: v = (row g8, tokens 2t, 2t+1), (row g8 + 8, same).
+// Writes one unit's outputs: v = (row g8, tokens tok0 + 2t, tok0 + 2t+1), (row g8 + 8, same).
 template <typename YT, int EPI, bool kQKV>
-MADI_DEV void store_unit(const GemvArgs &p, int tile, int g8, int t, const float4 &v4) {
+MADI_DEV void store_unit(const GemvArgs &p, int tile, int g8, int t, int tok0, const float4 &v4) {
     const float v[4] = {v4.x, v4.y, v4.z, v4.w};
     const int row0 = tile * kTileRows + g8;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         const int row = (i < 2) ? row0 : row0 + 8;
-        const int tok = 2 * t + (i & 1);
+        const int tok = tok0 + 2 * t + (i & 1);
         if (row >= p.N || tok >= p.M) continue;
         float y = v[i];
         if constexpr (kQKV) {
@@ -186,16 +191,16 @@ MADI_DEV void store_unit(const GemvArgs &p, int tile, int g8, int t, const float
 
 // One quad column (4 consecutive k) of all M token rows of x: load = true fetches
 // it into v, load = false converts v and stores it in fragment order.
-template <typename XT>
+template <typename XT, int kRows>
 MADI_DEV void stage_x_quad(const GemvArgs &p, uint8_t *xs, const XT *xrow, int kq, bool have,
-                           typename std::conditional<sizeof(XT) == 4, float4, uint2>::type (&v)[8], bool load) {
+                           typename std::conditional<sizeof(XT) == 4, float4, uint2>::type (&v)[kRows], bool load) {
     constexpr bool kSplit = sizeof(XT) == 4;
     const int M = p.M, K = p.K;
     const int kl = kq << 2;
     if (!have) return;
     if (load) {
 #pragma unroll
-        for (int m = 0; m < 8; ++m)
+        for (int m = 0; m < kRows; ++m)
             if (m < M) {
                 if constexpr (kSplit) v[m] = __ldcg(reinterpret_cast<const float4 *>(xrow + (size_t)m * K + kl));
                 else v[m] = __ldcg(reinterpret_cast<const uint2 *>(xrow + (size_t)m * K + kl));
@@ -204,7 +209,7 @@ MADI_DEV void stage_x_quad(const GemvArgs &p, uint8_t *xs, const XT *xrow, int k
     }
     const int slot0 = ((kl >> 5) * 2 + ((kl & 7) >> 2)) * M * 4 + ((kl & 31) >> 3);
 #pragma unroll
-    for (int m = 0; m < 8; ++m)
+    for (int m = 0; m < kRows; ++m)
         if (m < M) {
             if constexpr (kSplit) {
                 const float4 f = v[m];
@@ -228,22 +233,32 @@ MADI_DEV void stage_x_quad(const GemvArgs &p, uint8_t *xs, const XT *xrow, int k
 // one L2 round trip.  x may have been written by the kernel this one overlaps
 // under programmatic dependent launch, so it is read on the coherent L2 path
 // (ld.global.cg), never through the non-coherent one.
-template <typename XT>
+template <typename XT, int kG>
 MADI_DEV void stage_x(const GemvArgs &p, uint8_t *xs, int kb0, int KS, int tid, int nthr) {
     using V = typename std::conditional<sizeof(XT) == 4, float4, uint2>::type;
     const int qrow = KS >> 2;
     const XT *xrow = reinterpret_cast<const XT *>(p.x) + (size_t)kb0 * 32;
-    for (int kq = tid; kq < qrow; kq += 2 * nthr) {
-        V a[8], b[8];
-        const bool hb = kq + nthr < qrow;
-        stage_x_quad<XT>(p, xs, xrow, kq, true, a, true);
-        stage_x_quad<XT>(p, xs, xrow, kq + nthr, hb, b, true);
-        stage_x_quad<XT>(p, xs, xrow, kq, true, a, false);
-        stage_x_quad<XT>(p, xs, xrow, kq + nthr, hb, b, false);
+    if constexpr (kG == 1) {
+        for (int kq = tid; kq < qrow; kq += 2 * nthr) {
+            V a[8], b[8];
+            const bool hb = kq + nthr < qrow;
+            stage_x_quad<XT, 8>(p, xs, xrow, kq, true, a, true);
+            stage_x_quad<XT, 8>(p, xs, xrow, kq + nthr, hb, b, true);
+            stage_x_quad<XT, 8>(p, xs, xrow, kq, true, a, false);
+            stage_x_quad<XT, 8>(p, xs, xrow, kq + nthr, hb, b, false);
+        }
+    } else {
+        for (int kq = tid; kq < qrow; kq += nthr) {      // 16 rows: one quad's loads at a time
+            V a[16];
+            stage_x_quad<XT, 16>(p, xs, xrow, kq, true, a, true);
+            stage_x_quad<XT, 16>(p, xs, xrow, kq, true, a, false);
+        }
     }
 }
 
-template <typename XT, typename YT, int EPI, bool kQKV>
+// kG: token groups of 8 (1 for M <= 8, 2 for 9..16); each weight fragment feeds
+// one m16n8k16 MMA per group.
+template <typename XT, typename YT, int EPI, bool kQKV, int kG>
 __global__ void __launch_bounds__(kThreads, 2)
     q8_gemv_tile_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tms,
                         const GemvArgs p, const TilePlan plan, int *dev_err) {
@@ -260,8 +275,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     uint8_t *ring = smem;
     uint8_t *xs = smem + (size_t)stages * sb;
     float4 *red = reinterpret_cast<float4 *>(xs + x_bytes(M, KS, kSplit));
-    float4 *xred = red + 2 * kConsumers * 32;
-    TileBars *bars = reinterpret_cast<TileBars *>(reinterpret_cast<uint8_t *>(xred) + kXredBytes);
+    float4 *xred = red + 2 * kConsumers * 32 * kG;
+    TileBars *bars = reinterpret_cast<TileBars *>(reinterpret_cast<uint8_t *>(xred) + kG * kXredBytes);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g8 = lane >> 2, t = lane & 3;
@@ -282,8 +297,10 @@ __global__ void __launch_bounds__(kThreads, 2)
     // of the cluster is running by then.
     if (cs > 1) asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
 
-    bool have = false;            // reducer lanes of a split unit: `mine` holds the CTA sum
-    float4 mine = make_float4(0.f, 0.f, 0.f, 0.f);
+    bool have = false;            // reducer lanes of a split unit: `mine` holds the CTA sums
+    float4 mine[kG];
+#pragma unroll
+    for (int g = 0; g < kG; ++g) mine[g] = make_float4(0.f, 0.f, 0.f, 0.f);
     int mine_tile = 0;
 
     if (warp == 0) {
@@ -322,11 +339,13 @@ __global__ void __launch_bounds__(kThreads, 2)
         // ------------------------------------------------ consumers
         asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
         asm volatile("griddepcontrol.wait;" ::: "memory");
-        stage_x<XT>(p, xs, kb0, KS, (int)threadIdx.x - 32, kConsumers * 32);
+        stage_x<XT, kG>(p, xs, kb0, KS, (int)threadIdx.x - 32, kConsumers * 32);
         asm volatile("bar.sync 1, %0;" ::"r"(kConsumers * 32) : "memory");   // consumers only
 
         const int cw = warp - 1;
-        const bool gval = g8 < M;
+        bool gval[kG];
+#pragma unroll
+        for (int g = 0; g < kG; ++g) gval[g] = g8 + 8 * g < M;
         const int nki = nkbs >> 3;                          // 32-blocks per warp per unit
         const uint32_t off0 = frag_offset(g8, cw, t), off1 = frag_offset(g8 + 8, cw, t);
         const int xstep = 16 * M * 4;                       // x slots per i (8 blocks x 2 halves x M x 4)
@@ -340,7 +359,9 @@ __global__ void __launch_bounds__(kThreads, 2)
             const int s = n % stages;
             const uint32_t ph = (uint32_t)(n / stages) & 1u;
             if (alive) alive = warp_wait_all(&bars->full[s], ph, abort_flag, dev_err);
-            float acc[4] = {0.f, 0.f, 0.f, 0.f};
+            float acc[kG][4];
+#pragma unroll
+            for (int g = 0; g < kG; ++g) acc[g][0] = acc[g][1] = acc[g][2] = acc[g][3] = 0.f;
             if (alive) {
                 const uint8_t *st = ring + (size_t)s * sb;
                 const __half *sc = reinterpret_cast<const __half *>(st + (size_t)kTileRows * KS);
@@ -351,7 +372,9 @@ __global__ void __launch_bounds__(kThreads, 2)
                     const uint2 wb = *reinterpret_cast<const uint2 *>(st + off1 + i * kBoxBytes);
                     // the block's products (both k16 halves; for f32 x, hi and lo) meet in
                     // one f32 accumulator, then take the block scale
-                    float bs[4] = {0.f, 0.f, 0.f, 0.f};
+                    float bs[kG][4];
+#pragma unroll
+                    for (int g = 0; g < kG; ++g) bs[g][0] = bs[g][1] = bs[g][2] = bs[g][3] = 0.f;
 #pragma unroll
                     for (int sp = 0; sp < 2; ++sp) {
                         __half2 a_lo0, a_hi0, a_lo1, a_hi1;
@@ -359,43 +382,55 @@ __global__ void __launch_bounds__(kThreads, 2)
                         q8_to_half2x2(sp == 0 ? wb.x : wb.y, a_lo1, a_hi1);
                         const uint32_t a[4] = {h2_as_u32(a_lo0), h2_as_u32(a_lo1), h2_as_u32(a_hi0), h2_as_u32(a_hi1)};
                         const int slot = xbase + i * xstep + sp * M * 4;
-                        if constexpr (kSplit) {
-                            const uint4 xv = gval ? reinterpret_cast<const uint4 *>(xs)[slot] : make_uint4(0u, 0u, 0u, 0u);
-                            mma16816(bs, a, xv.x, xv.y);
-                            mma16816(bs, a, xv.z, xv.w);
-                        } else {
-                            const uint2 xv = gval ? reinterpret_cast<const uint2 *>(xs)[slot] : make_uint2(0u, 0u);
-                            mma16816(bs, a, xv.x, xv.y);
+#pragma unroll
+                        for (int g = 0; g < kG; ++g) {              // tokens 8g .. 8g+7: slots 32 further
+                            if constexpr (kSplit) {
+                                const uint4 xv = gval[g] ? reinterpret_cast<const uint4 *>(xs)[slot + 32 * g]
+                                                         : make_uint4(0u, 0u, 0u, 0u);
+                                mma16816(bs[g], a, xv.x, xv.y);
+                                mma16816(bs[g], a, xv.z, xv.w);
+                            } else {
+                                const uint2 xv = gval[g] ? reinterpret_cast<const uint2 *>(xs)[slot + 32 * g]
+                                                         : make_uint2(0u, 0u);
+                                mma16816(bs[g], a, xv.x, xv.y);
+                            }
                         }
                     }
                     const float f0 = __half2float(s0p[8 * i]);
                     const float f1 = __half2float(s1p[8 * i]);
-                    acc[0] = fmaf(bs[0], f0, acc[0]);
-                    acc[1] = fmaf(bs[1], f0, acc[1]);
-                    acc[2] = fmaf(bs[2], f1, acc[2]);
-                    acc[3] = fmaf(bs[3], f1, acc[3]);
+#pragma unroll
+                    for (int g = 0; g < kG; ++g) {
+                        acc[g][0] = fmaf(bs[g][0], f0, acc[g][0]);
+                        acc[g][1] = fmaf(bs[g][1], f0, acc[g][1]);
+                        acc[g][2] = fmaf(bs[g][2], f1, acc[g][2]);
+                        acc[g][3] = fmaf(bs[g][3], f1, acc[g][3]);
+                    }
                 }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&bars->empty[s]);   // stage consumed: the producer may refill it
-            float4 *rb = red + (size_t)(n & 1) * kConsumers * 32;
-            rb[cw * 32 + lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+            float4 *rb = red + (size_t)(n & 1) * kConsumers * 32 * kG;
+#pragma unroll
+            for (int g = 0; g < kG; ++g)
+                rb[(cw * kG + g) * 32 + lane] = make_float4(acc[g][0], acc[g][1], acc[g][2], acc[g][3]);
             asm volatile("bar.sync 2, %0;" ::"r"(kConsumers * 32) : "memory");
             // The reducer of unit n reads buffer n & 1 before it reaches the barrier of
             // unit n + 1, and unit n + 2 rewrites that buffer only after that barrier.
             if (cw != (n & (kConsumers - 1))) continue;
-            float4 v = rb[lane];
 #pragma unroll
-            for (int w = 1; w < kConsumers; ++w) {
-                const float4 q = rb[w * 32 + lane];
-                v.x += q.x; v.y += q.y; v.z += q.z; v.w += q.w;
+            for (int g = 0; g < kG; ++g) {
+                float4 v = rb[g * 32 + lane];
+#pragma unroll
+                for (int w = 1; w < kConsumers; ++w) {
+                    const float4 q = rb[(w * kG + g) * 32 + lane];
+                    v.x += q.x; v.y += q.y; v.z += q.z; v.w += q.w;
+                }
+                if (cs > 1) mine[g] = v;
+                else if (alive) store_unit<YT, EPI, kQKV>(p, tile, g8, t, 8 * g, v);
             }
             if (cs > 1) {
-                mine = v;
                 mine_tile = tile;
                 have = alive;
-            } else if (alive) {
-                store_unit<YT, EPI, kQKV>(p, tile, g8, t, v);
             }
         }
     }
@@ -405,16 +440,22 @@ __global__ void __launch_bounds__(kThreads, 2)
         // in rank order.  Every thread of every CTA takes part in both barriers.
         cg::cluster_group cluster = cg::this_cluster();
         asm volatile("barrier.cluster.wait;" ::: "memory");
-        if (have) cluster.map_shared_rank(xred, 0)[rank * 32 + lane] = mine;
+        if (have) {
+#pragma unroll
+            for (int g = 0; g < kG; ++g) cluster.map_shared_rank(xred, 0)[(rank * kG + g) * 32 + lane] = mine[g];
+        }
         asm volatile("barrier.cluster.arrive.release;" ::: "memory");
         asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
         if (rank == 0 && have) {
-            float4 v = xred[lane];
-            for (int r = 1; r < cs; ++r) {
-                const float4 q = xred[r * 32 + lane];
-                v.x += q.x; v.y += q.y; v.z += q.z; v.w += q.w;
+#pragma unroll
+            for (int g = 0; g < kG; ++g) {
+                float4 v = xred[g * 32 + lane];
+                for (int r = 1; r < cs; ++r) {
+                    const float4 q = xred[(r * kG + g) * 32 + lane];
+                    v.x += q.x; v.y += q.y; v.z += q.z; v.w += q.w;
+                }
+                store_unit<YT, EPI, kQKV>(p, mine_tile, g8, t, 8 * g, v);
             }
-            store_unit<YT, EPI, kQKV>(p, mine_tile, g8, t, v);
         }
     }
 }
@@ -441,10 +482,10 @@ bool make_tile_maps(const GemvArgs &a, int KS, CUtensorMap *tmq, CUtensorMap *tm
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <typename XT, typename YT, int EPI, bool kQKV>
-cudaError_t launch_tile_one(const GemvArgs &a, const CUtensorMap &tmq, const CUtensorMap &tms, const TilePlan &pl,
-                            int grid, int *dev_err, cudaStream_t st, bool pdl) {
-    auto fn = q8_gemv_tile_kernel<XT, YT, EPI, kQKV>;
+template <typename XT, typename YT, int EPI, bool kQKV, int kG>
+cudaError_t launch_tile_g(const GemvArgs &a, const CUtensorMap &tmq, const CUtensorMap &tms, const TilePlan &pl,
+                          int grid, int *dev_err, cudaStream_t st, bool pdl) {
+    auto fn = q8_gemv_tile_kernel<XT, YT, EPI, kQKV, kG>;
     static bool attr = false;
     if (!attr) {
         cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemCap);
@@ -471,6 +512,13 @@ cudaError_t launch_tile_one(const GemvArgs &a, const CUtensorMap &tmq, const CUt
     cfg.attrs = attrs;
     cfg.numAttrs = na;
     return cudaLaunchKernelEx(&cfg, fn, tmq, tms, a, pl, dev_err);
+}
+
+template <typename XT, typename YT, int EPI, bool kQKV>
+cudaError_t launch_tile_one(const GemvArgs &a, const CUtensorMap &tmq, const CUtensorMap &tms, const TilePlan &pl,
+                            int grid, int *dev_err, cudaStream_t st, bool pdl) {
+    return a.M > 8 ? launch_tile_g<XT, YT, EPI, kQKV, 2>(a, tmq, tms, pl, grid, dev_err, st, pdl)
+                   : launch_tile_g<XT, YT, EPI, kQKV, 1>(a, tmq, tms, pl, grid, dev_err, st, pdl);
 }
 
 }  // namespace

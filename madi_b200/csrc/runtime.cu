@@ -145,7 +145,13 @@ int q8_linear_impl(const madi_q8w *w, const void *x, int x_dtype, int m, const v
         return fail(MADI_EINVAL, "%s: problem too large (m=%d N=%d K=%d)", who, m, N, K);
     if (!aligned(w->qs, 16) || !aligned(w->scales, 2)) return fail(MADI_EINVAL, "%s: qs must be 16-byte aligned", who);
 
-    if (m >= kGemmMinM) {
+    // m <= 16 token rows take the streaming skinny GEMM when its tile plan fits (all
+    // K % 256 == 0 shapes of the decoder and the head); larger m, or m in 9..16 with
+    // another K, the tensor-core GEMM.
+    const bool x_al = aligned(x, x_dtype == MADI_F32 ? 16 : 8);
+    const bool tile_fits = m <= kGemvMaxM && x_al && aligned(w->scales, 16) &&
+                           gemv_tile_ok(m, N, K, x_dtype == MADI_F32, S.num_sms);
+    if (m >= kGemmMinM && !tile_fits) {
         const bool y32 = y_dtype == MADI_F32;
         if (x_dtype != MADI_F16 || (y32 && epi != MADI_EPI_NONE))
             return fail(MADI_EINVAL, "%s: the tensor-core path (m > 8) takes f16 x, and f16 y (f32 y without an "
@@ -196,12 +202,12 @@ int q8_qkv_impl(const madi_q8w *w, const float *x, int m, const float *qb, const
         return fail(MADI_EINVAL, "%s: null argument", who);
     const int D = w->k;
     if (D <= 0 || D % 32 != 0 || w->n != 3 * D) return fail(MADI_EINVAL, "%s: qkv weight must be [3D][D], D %% 32 == 0", who);
-    if (m <= 0 || m > 8) return fail(MADI_EINVAL, "%s: m=%d outside 1..8", who, m);
+    if (m <= 0 || m > kGemvMaxM) return fail(MADI_EINVAL, "%s: m=%d outside 1..%d", who, m, kGemvMaxM);
     if (!aligned(x, 16) || !aligned(w->qs, 16)) return fail(MADI_EINVAL, "%s: misaligned x or qs", who);
     const int ks = gemv_pick_ks(3 * D, D, S.num_sms);
     const bool tile_path = aligned(w->scales, 16) && gemv_tile_ok(m, 3 * D, D, true, S.num_sms);
-    if (!tile_path && gemv_smem_bytes(m, D, ks, true) > (size_t)S.max_smem_optin)
-        return fail(MADI_EINVAL, "%s: D too large", who);
+    if (!tile_path && (m > 8 || gemv_smem_bytes(m, D, ks, true) > (size_t)S.max_smem_optin))
+        return fail(MADI_EINVAL, "%s: D=%d at m=%d does not fit the decode path", who, D, m);
     GemvArgs a{};
     a.qs = w->qs;
     a.scales = reinterpret_cast<const __half *>(w->scales);

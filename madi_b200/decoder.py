@@ -10,7 +10,7 @@ One token step per slot follows the reference's decodeBlock (decoder.zig:255-330
                 x += fc2(gelu(fc1(xb) + m0b)) + m2b                 gemv_q8_bias_gelu / _bias_res
     logits = emb_q8 . LN_post(x)  (tied head);  pos += 1;  logit filter;  tokens[pos] = argmax
 
-Every operation is a library kernel (Q8 GEMVs for the projections at M = slots <= 8,
+Every operation is a library kernel (Q8 GEMVs for the projections at M = slots <= 16,
 the tcgen05 GEMM for the one-time cross K/V projection of the encoder states, the
 cluster attention kernels, the f32 LayerNorms, the decode-step helpers), all on one
 stream and capturable as one CUDA graph per token step.  Weights are seeded random
@@ -107,8 +107,8 @@ class Decoder:
     """Device copy of the synthetic decoder plus the per-slot decode state."""
 
     def __init__(self, w: dict, slots: int, device="cuda"):
-        if not 1 <= slots <= 8:
-            raise ValueError("1..8 token slots")
+        if not 1 <= slots <= 16:
+            raise ValueError("1..16 token slots")
         t = lambda a: (a.to(device) if isinstance(a, torch.Tensor) else
                        torch.from_numpy(np.ascontiguousarray(a)).to(device))
         qw = lambda p: q8.Q8Weight(t(p[0]), t(p[1]))

@@ -1,8 +1,9 @@
 """Long-audio batched transcription on the library's kernels (config 4 shapes):
 independent 30 s chunks of log-mel -> the whole encoder (conv stem, 32 layers,
 ln_post) -> cross K / V -> the 4-layer greedy decoder with EOT suppressed, exactly
-`tokens` tokens per chunk, chunks in batches of `slots` token slots (the reference
-batches independent chunks into decoder slots the same way, transcribe.zig:2314-2321).
+`tokens` tokens per chunk, chunks in batches of `slots` token slots (up to 16; the
+reference batches independent chunks into decoder slots the same way,
+transcribe.zig:2314-2321).
 
 Per batch: one eager encoder pass (about 290 launches, tcgen05 GEMMs and flash
 attention), 8 cross K / V GEMMs, then `tokens` replays of one captured CUDA graph

@@ -61,9 +61,10 @@ def _ptr(t):
 def linear(w: Q8Weight, x: torch.Tensor, bias: Optional[torch.Tensor] = None, epi: Optional[int] = None,
            residual: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
            out_dtype: Optional[torch.dtype] = None, stream=None) -> torch.Tensor:
-    """y[m][n] = epi(x @ deq(w)^T).  x [m][k] (f16; f32 also allowed for m <= 8).
+    """y[m][n] = epi(x @ deq(w)^T).  x [m][k] (f16; f32 also allowed for m <= 16).
     epi defaults to BIAS when a bias is given, BIAS_RES when a residual is given.
-    m > 8 runs the tcgen05 GEMM, m <= 8 the decode skinny GEMM."""
+    m <= 16 runs the decode skinny GEMM (when K % 256 == 0, else m <= 8), larger m
+    the tcgen05 GEMM."""
     if x.dim() != 2 or x.shape[1] != w.k:
         raise ValueError(f"x {tuple(x.shape)} vs weight k={w.k}")
     if not x.is_contiguous():

@@ -46,8 +46,9 @@ def test_config0_shape_all_epilogues(madi, oracle, epi):
     _run(madi, oracle, 1500, 1280, 1280, epi)
 
 
-@pytest.mark.parametrize("M", [9, 50, 129, 191, 192, 193, 385])
+@pytest.mark.parametrize("M", [17, 50, 129, 191, 192, 193, 385])
 def test_token_tails(madi, oracle, M):
+    # 17: the smallest M the tensor-core path takes for K % 256 == 0 (m <= 16 streams)
     _run(madi, oracle, M, 256, 256, 1, seed=M)
 
 
@@ -133,9 +134,11 @@ def test_deterministic_repeat(madi):
 
 @pytest.mark.parametrize("M,N", [(16, 6483), (64, 6483), (200, 1312), (160, 25933)])
 def test_f32_output_without_epilogue(madi, oracle, M, N):
-    """The tensor-core path with f32 y and no epilogue (a vocab-head shard over
-    more than 8 token slots): f32 accumulation written without rounding, so the
-    error against the exact result is held to 1e-4 x RMS, far inside the gate."""
+    """f32 y and no epilogue (a vocab-head shard over many token slots): f32
+    accumulation written without rounding, so the error against the exact result
+    is held to 1e-4 x RMS, far inside the gate.  Up to 16 rows the skinny GEMM
+    runs it (exact int8 weights times f32 block scales, as gemv_q8 computes); above
+    16 the tensor-core GEMM (weights dequantised to f16 first, as the encoder does)."""
     import torch
     from madi_b200 import q8
     K = 1280
@@ -145,7 +148,10 @@ def test_f32_output_without_epilogue(madi, oracle, M, N):
     y = q8.linear(W, _t(x), out_dtype=torch.float32)
     torch.cuda.synchronize()
     assert y.dtype == torch.float32
-    y_exact = oracle.linear_f16(x, qs, sc, epi=oracle.EPI_NONE)
+    if M <= 16:
+        y_exact = oracle.gemv_q8(x.astype(np.float32), qs, sc)
+    else:
+        y_exact = oracle.linear_f16(x, qs, sc, epi=oracle.EPI_NONE)
     err = np.abs(y.cpu().numpy().astype(np.float64) - y_exact).max()
     rms = np.sqrt(np.mean(y_exact ** 2))
     assert err <= 1e-4 * rms, f"M={M} N={N}: max err {err:.3e} vs rms {rms:.3e}"

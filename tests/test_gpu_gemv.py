@@ -1,4 +1,4 @@
-"""Variant (b) parity: decode GEMV / skinny GEMM (M <= 8) against the oracle.
+"""Variant (b) parity: decode GEMV / skinny GEMM (M <= 16) against the oracle.
 
 The oracle restates graph_helpers.metal's f32 GEMV family; the gate
 (tests/gate.py) is max |y - y_exact| <= 2e-3 * RMS(y_exact) with y_exact the
@@ -117,6 +117,26 @@ def test_reference_gemv_family_through_dispatch(madi, oracle):
     assert int(torch.argmax(logits).item()) == oracle.argmax(ex.astype(np.float32))
 
 
+@pytest.mark.parametrize("M", [9, 12, 16])
+@pytest.mark.parametrize("name,N,K", synth.decoder_shapes())
+def test_decoder_shapes_two_token_groups(madi, oracle, M, name, N, K):
+    """9..16 token rows: each weight fragment feeds two MMAs (tokens 0..7, 8..15),
+    with the second group partly empty below 16."""
+    epi = {"qkv": 0, "o": 0, "cq": 1, "co": 0, "fc1": 2, "fc2": 3}[name]
+    _case(madi, oracle, M, N, K, epi, seed=M * 5 + N)
+
+
+@pytest.mark.parametrize("M,N,K,epi,x_dt,y_dt", [
+    (16, 51866, 1280, 0, np.float32, np.float32),   # vocab head, persistent ring
+    (13, 40010, 1536, 3, np.float16, np.float16),   # ragged last tile, f16 in / out
+    (10, 300, 1024, 1, np.float32, np.float32),     # 4-CTA clusters split K
+    (16, 1280, 5120, 3, np.float32, np.float32),    # fc2 shape, f32 x
+    (11, 37, 2048, 2, np.float16, np.float32),
+])
+def test_two_token_group_plans(madi, oracle, M, N, K, epi, x_dt, y_dt):
+    _case(madi, oracle, M, N, K, epi, x_dt=x_dt, y_dt=y_dt, seed=N + K + 3 * M)
+
+
 def test_qkv_kv_store(madi, oracle):
     """gemv_q8_qkv: q+qb -> q_out, k -> kc[pos], v+vb -> vc[pos] (pos read on device)."""
     import torch
@@ -140,12 +160,18 @@ def test_qkv_kv_store(madi, oracle):
     _check(kc[17], k_ex[17], "k cache row")
     _check(vc[17], v_ex[17], "v cache row")
     assert torch.isnan(kc[16]).all() and torch.isnan(vc[18]).all(), "other cache rows must be untouched"
-    # batched slots: per-slot caches and positions
-    M = 5
-    xb = synth.activations(M, D, 35, np.float32)
+    # batched slots: per-slot caches and positions (5 slots, then 12: two token groups)
+    for M, posb in [(5, np.array([0, 3, 447, 10, 200], np.uint32)),
+                    (12, np.array([0, 3, 447, 10, 200, 1, 2, 5, 8, 13, 21, 34], np.uint32))]:
+        _qkv_slots(oracle, qs, sc, qb, vb, D, T, M, posb)
+
+
+def _qkv_slots(oracle, qs, sc, qb, vb, D, T, M, posb):
+    import torch
+    from madi_b200 import q8
+    xb = synth.activations(M, D, 35 + M, np.float32)
     kcb = torch.full((M, T, D), float("nan"), device="cuda")
     vcb = torch.full((M, T, D), float("nan"), device="cuda")
-    posb = np.array([0, 3, 447, 10, 200], np.uint32)
     W = q8.Q8Weight(_t(qs), _t(sc))
     qo = q8.qkv(W, _t(xb), _t(qb), _t(vb), kcb, vcb, _t(posb.astype(np.int32)))
     torch.cuda.synchronize()

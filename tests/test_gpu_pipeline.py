@@ -65,3 +65,25 @@ def test_forced_length(tr):
     assert toks.shape == (3, 6)
     assert (toks < pipeline.EOT).all(), toks
     assert int(tr.decoder.pos[0].item()) == 6
+
+
+def test_slot_count_invariance(madi):
+    """The decoder at 12 slots (two token groups per GEMV weight fragment) gives the
+    first 4 chunks the same tokens as the decoder at 4 slots."""
+    import torch
+    from madi_b200 import decoder as dec
+    w = dec.device_weights(seed=9)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(17)
+    states = torch.randn((12, dec.ENC, dec.D), device="cuda", generator=g).half()
+    got = []
+    for slots in (12, 4):
+        d = dec.Decoder(w, slots)
+        d.set_encoder(states[:slots].contiguous())
+        d.reset(50258)
+        for _ in range(6):
+            d.step()
+        torch.cuda.synchronize()
+        got.append(d.tokens[:4, :7].clone())
+        del d
+    assert torch.equal(got[0], got[1]), f"{got[0].tolist()} vs {got[1].tolist()}"
