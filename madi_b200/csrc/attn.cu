@@ -20,6 +20,7 @@
 // output.  No global scratch and one launch, with (slots x heads x ns) CTAs
 // streaming K/V in parallel.  The cross-attention K/V is the decode step's largest
 // read at 8 slots (2 x 1500 x 1280 f16 per slot per layer): the kernel is HBM-bound.
+#include <algorithm>
 #include <cooperative_groups.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
@@ -291,28 +292,35 @@ template <> MADI_DEV int q_dim<float>(int li, int i) { return i < 4 ? 4 * li + i
 
 template <typename KV> struct StreamRows { static constexpr int kR = sizeof(KV) == 2 ? 64 : 32; };
 
-template <typename KV>
+// G heads per CTA (2 when every head has its own kv head and nh is even): the K / V
+// boxes are G * 64 columns wide, so one TMA row request carries G heads' keys --
+// the stream's rate is set by the number of box rows, not by their width -- and
+// consumer warps 8/G * g .. 8/G * (g+1) - 1 serve head g.
+template <typename KV, int G>
 __global__ void __launch_bounds__(kThrS, 4) attn_stream_kernel(const __grid_constant__ CUtensorMap tmK,
                                                             const __grid_constant__ CUtensorMap tmV,
                                                             float *__restrict__ out, const float *__restrict__ q,
                                                             const uint32_t *__restrict__ pos, int rows, int nkv,
                                                             int nh, int ns, int csz, int stages, int *dev_err) {
     constexpr int kR = StreamRows<KV>::kR;
-    constexpr int kBox = kR * kHd;                        // elements per K (or V) box
-    constexpr int kPasses = kR / 32;                      // 4 keys per warp per pass, 8 warps
+    constexpr int kW = kHd * G;                           // box width (elements)
+    constexpr int kBox = kR * kW;                         // elements per K (or V) box
+    constexpr int kWarpsPerHead = 8 / G;
+    constexpr int kKeysPerWarp = kR / kWarpsPerHead;      // of each stage
+    constexpr int kPasses = kKeysPerWarp / 4;             // 4 keys per pass
     extern __shared__ uint8_t attn_smem[];
     KV *ring = reinterpret_cast<KV *>((reinterpret_cast<uintptr_t>(attn_smem) + 127) & ~uintptr_t(127));
-    __shared__ float qh[kHd];
+    __shared__ float qh[G][kHd];
     __shared__ float wm[8], wl[8];
     __shared__ float wo[8][kHd];
-    __shared__ float part[8][2 + kHd];
+    __shared__ float part[8][G][2 + kHd];
     __shared__ __align__(8) uint64_t full[kMaxStages];
     __shared__ __align__(8) uint64_t empty[kMaxStages];
     __shared__ int abort_flag;
-    const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    const int c = blockIdx.x, hp = blockIdx.y, b = blockIdx.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int D = nh * kHd;
-    const int kvh = h * nkv / nh;
+    const int kvh = hp * G * nkv / nh;                    // first kv head of the box (G > 1: nkv == nh)
     pdl_trigger();
     pdl_wait();                 // q, pos and the cache row at pos come from earlier kernels
     const int len = pos ? (pos[b] < (uint32_t)rows ? (int)pos[b] + 1 : rows) : rows;
@@ -328,7 +336,7 @@ __global__ void __launch_bounds__(kThrS, 4) attn_stream_kernel(const __grid_cons
         }
         fence_mbar_init();
     }
-    if (tid < kHd) qh[tid] = q[(size_t)b * D + h * kHd + tid];
+    if (tid < kHd * G) qh[tid / kHd][tid % kHd] = q[(size_t)b * D + hp * G * kHd + tid];
     __syncthreads();
 
     float m_w = -INFINITY, l_w = 0.f, o0 = 0.f, o1 = 0.f;
@@ -347,21 +355,22 @@ __global__ void __launch_bounds__(kThrS, 4) attn_stream_kernel(const __grid_cons
                 issued = j + 1;
             }
             // the copies issued last land before the CTA can exit
-            for (int i = issued > stages ? issued - stages : 0; i < issued; ++i) {
+            for (int i2 = issued > stages ? issued - stages : 0; i2 < issued; ++i2) {
                 const long long tw = clock64();
-                while (!mbar_try_wait(&full[i % stages], (uint32_t)(i / stages) & 1u))
+                while (!mbar_try_wait(&full[i2 % stages], (uint32_t)(i2 / stages) & 1u))
                     if (clock64() - tw > kWaitBudgetCycles) break;
             }
         }
         __syncwarp();
     } else {
         // ------------------------------------------------ consumers
+        const int g = warp / kWarpsPerHead, wl_ = warp % kWarpsPerHead;
         const int li = lane & 7, kq = lane >> 3;          // 8 lanes per key, 4 keys per pass
         float qv[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) qv[i] = qh[q_dim<KV>(li, i)];
+        for (int i2 = 0; i2 < 8; ++i2) qv[i2] = qh[g][q_dim<KV>(li, i2)];
         const float rsq = rsqrtf((float)kHd);
-        const int kb = warp * (kR / 8);                   // this warp's keys in each stage
+        const int kb = wl_ * kKeysPerWarp;                // this warp's keys in each stage
         for (int j = 0; j < nsub; ++j) {
             const int s = j % stages;
             if (!warp_wait_all(&full[s], (uint32_t)(j / stages) & 1u, &abort_flag, dev_err)) {
@@ -369,14 +378,14 @@ __global__ void __launch_bounds__(kThrS, 4) attn_stream_kernel(const __grid_cons
                 break;
             }
             const int rj = min(kR, n - j * kR);
-            const KV *ks = ring + (size_t)s * 2 * kBox;
+            const KV *ks = ring + (size_t)s * 2 * kBox + g * kHd;
             const KV *vs = ks + kBox;
             float sc[kPasses];
             float mx = -INFINITY;
 #pragma unroll
             for (int p = 0; p < kPasses; ++p) {
                 const int k = kb + 4 * p + kq;
-                float d = k < rj ? dot8<KV>(ks + (size_t)k * kHd, li, qv) : 0.f;
+                float d = k < rj ? dot8<KV>(ks + (size_t)k * kW, li, qv) : 0.f;
                 d += __shfl_xor_sync(0xffffffffu, d, 4);
                 d += __shfl_xor_sync(0xffffffffu, d, 2);
                 d += __shfl_xor_sync(0xffffffffu, d, 1);
@@ -397,11 +406,11 @@ __global__ void __launch_bounds__(kThrS, 4) attn_stream_kernel(const __grid_cons
                     const float e = exp2f((sc[p] - m_w) * kLog2e);     // 0 for a missing key
                     l_w += e;                                         // per key group; summed below
 #pragma unroll
-                    for (int g = 0; g < 4; ++g) {
-                        const int k = kb + 4 * p + g;
-                        const float ek = __shfl_sync(0xffffffffu, e, 8 * g);
+                    for (int g4 = 0; g4 < 4; ++g4) {
+                        const int k = kb + 4 * p + g4;
+                        const float ek = __shfl_sync(0xffffffffu, e, 8 * g4);
                         if (k < rj) {
-                            const float2 v = ld2(vs + (size_t)k * kHd + 2 * lane);
+                            const float2 v = ld2(vs + (size_t)k * kW + 2 * lane);
                             o0 = fmaf(ek, v.x, o0);
                             o1 = fmaf(ek, v.y, o1);
                         }
@@ -422,50 +431,52 @@ __global__ void __launch_bounds__(kThrS, 4) attn_stream_kernel(const __grid_cons
         }
     }
     __syncthreads();
-    // this CTA's (m, l, o): the warps' partials by log-sum-exp
-    float cm = -INFINITY;
+    // this CTA's (m, l, o) per head: its warps' partials by log-sum-exp
+    const int hg = tid / kHd, d = tid % kHd;              // threads 0 .. G*64-1: (head, dim)
+    float cm = -INFINITY, cl = 0.f, co = 0.f;
+    if (tid < kHd * G) {
 #pragma unroll
-    for (int w8 = 0; w8 < 8; ++w8) cm = fmaxf(cm, wm[w8]);
-    float cl = 0.f, co = 0.f;
-    if (tid < kHd) {
+        for (int w8 = 0; w8 < kWarpsPerHead; ++w8) cm = fmaxf(cm, wm[hg * kWarpsPerHead + w8]);
 #pragma unroll
-        for (int w8 = 0; w8 < 8; ++w8) {
-            if (wm[w8] > -INFINITY) {
-                const float f = exp2f((wm[w8] - cm) * kLog2e);
-                cl += wl[w8] * f;
-                co += wo[w8][tid] * f;
+        for (int w8 = 0; w8 < kWarpsPerHead; ++w8) {
+            const int w = hg * kWarpsPerHead + w8;
+            if (wm[w] > -INFINITY) {
+                const float f = exp2f((wm[w] - cm) * kLog2e);
+                cl += wl[w] * f;
+                co += wo[w][d] * f;
             }
         }
     }
 
-    float *p0 = &part[0][0];
+    float *p0 = &part[0][0][0];
     if (ns > 1) {
         asm volatile("barrier.cluster.wait;" ::: "memory");
-        p0 = cg::this_cluster().map_shared_rank(&part[0][0], 0);
+        p0 = cg::this_cluster().map_shared_rank(&part[0][0][0], 0);
     }
-    if (tid < kHd) p0[c * (2 + kHd) + 2 + tid] = co;
-    if (tid == 0) {
-        p0[c * (2 + kHd)] = cm;
-        p0[c * (2 + kHd) + 1] = cl;
+    if (tid < kHd * G) {
+        float *pc = p0 + ((size_t)c * G + hg) * (2 + kHd);
+        pc[2 + d] = co;
+        if (d == 0) {
+            pc[0] = cm;
+            pc[1] = cl;
+        }
     }
     if (ns > 1) {
         asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
     } else {
         __syncthreads();
     }
-    if (c == 0) {
+    if (c == 0 && tid < kHd * G) {
         float gm = -INFINITY;
-        for (int r = 0; r < ns; ++r) gm = fmaxf(gm, part[r][0]);
-        float gs = 0.f;
+        for (int r = 0; r < ns; ++r) gm = fmaxf(gm, part[r][hg][0]);
+        float gs = 0.f, acc = 0.f;
         for (int r = 0; r < ns; ++r)
-            if (part[r][0] > -INFINITY) gs += part[r][1] * exp2f((part[r][0] - gm) * kLog2e);
-        const float inv = 1.0f / gs;
-        if (tid < kHd) {
-            float acc = 0.f;
-            for (int r = 0; r < ns; ++r)
-                if (part[r][0] > -INFINITY) acc += part[r][2 + tid] * exp2f((part[r][0] - gm) * kLog2e);
-            out[(size_t)b * D + h * kHd + tid] = acc * inv;
-        }
+            if (part[r][hg][0] > -INFINITY) {
+                const float f = exp2f((part[r][hg][0] - gm) * kLog2e);
+                gs += part[r][hg][1] * f;
+                acc += part[r][hg][2 + d] * f;
+            }
+        out[(size_t)b * D + (hp * G + hg) * kHd + d] = acc * (1.0f / gs);
     }
 }
 
@@ -548,12 +559,12 @@ __global__ void __launch_bounds__(kThr) cross_attn_reduce_kernel(float *__restri
 
 // K / V as [slots * rows][kvd] with [csz][64] boxes (no swizzle: rows of 64
 // elements, read conflict-free by half-warps).
-bool attn_map(CUtensorMap *m, const void *base, bool f16, uint64_t total_rows, int kvd, int csz) {
+bool attn_map(CUtensorMap *m, const void *base, bool f16, uint64_t total_rows, int kvd, int csz, int width = kHd) {
     PFN_encodeTiled enc = tensor_map_encoder();
     if (!enc) return false;
     const cuuint64_t dims[2] = {(cuuint64_t)kvd, total_rows};
     const cuuint64_t strides[1] = {(cuuint64_t)kvd * (f16 ? 2 : 4)};
-    const cuuint32_t box[2] = {(cuuint32_t)kHd, (cuuint32_t)csz};
+    const cuuint32_t box[2] = {(cuuint32_t)width, (cuuint32_t)csz};
     const cuuint32_t es[2] = {1, 1};
     return enc(m, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void *>(base),
                dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
@@ -588,35 +599,39 @@ cudaError_t launch_attn_t(const void *kc, const void *vc, float *out, const floa
 // slots x heads x ns CTAs all fit at once, with the ring sized to the shared
 // memory the resident CTAs leave (2..8 slots of 16 KB) and the fit checked against
 // the occupancy the kernel really gets at that size.
-template <typename KV>
-cudaError_t launch_attn_stream(const void *kc, const void *vc, float *out, const float *q, const uint32_t *pos,
-                               int slots, int rows, int kvd, int nkv, int nh, int *dev_err, cudaStream_t st) {
+template <typename KV, int G>
+cudaError_t launch_attn_stream_g(const void *kc, const void *vc, float *out, const float *q, const uint32_t *pos,
+                                 int slots, int rows, int kvd, int nkv, int nh, int *dev_err, cudaStream_t st) {
     constexpr int kR = StreamRows<KV>::kR;
-    const size_t stage_bytes = 2 * (size_t)kR * kHd * sizeof(KV);
-    auto fn = attn_stream_kernel<KV>;
+    constexpr size_t kSmemMax = 200 * 1024;
+    const size_t stage_bytes = 2 * (size_t)kR * kHd * G * sizeof(KV);
+    auto fn = attn_stream_kernel<KV, G>;
     static int occ[kMaxStages + 1] = {0};                 // resident CTAs per SM by ring depth
-    if (!occ[kMaxStages]) {
+    if (!occ[2]) {
         cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)(128 + kMaxStages * stage_bytes));
+                                             (int)std::min(kSmemMax, 128 + kMaxStages * stage_bytes));
         if (e != cudaSuccess) return e;
         for (int sg = 2; sg <= kMaxStages; ++sg) {
             int nb = 0;
-            e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, fn, kThrS, 128 + sg * stage_bytes);
-            if (e != cudaSuccess) return e;
-            occ[sg] = nb > 0 ? nb : 1;
+            if (128 + sg * stage_bytes <= kSmemMax) {
+                e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, fn, kThrS, 128 + sg * stage_bytes);
+                if (e != cudaSuccess) return e;
+            }
+            occ[sg] = nb;
         }
     }
     const int sms = num_sms();
-    const long pairs = (long)slots * nh;
+    const long pairs = (long)slots * (nh / G);
     int ns = 1, stages = 2;
     for (int cand = 8; cand >= 1; cand /= 2) {
         if (cand > 1 && (rows + cand - 1) / cand < 2 * kR) continue;
         const long per_sm = (pairs * cand + sms - 1) / sms;
         if (per_sm > 16) continue;
         const size_t budget = (size_t)(220 * 1024) / (size_t)per_sm;
-        const size_t reserve = 8 * 1024;                 // static shared memory and alignment
+        const size_t reserve = 12 * 1024;                // static shared memory and alignment
         int sg = budget > reserve ? (int)((budget - reserve) / stage_bytes) : 2;
         sg = sg < 2 ? 2 : (sg > kMaxStages ? kMaxStages : sg);
+        while (sg > 2 && 128 + sg * stage_bytes > kSmemMax) --sg;
         if (occ[sg] >= per_sm || cand == 1) {
             ns = cand;
             stages = sg;
@@ -626,11 +641,21 @@ cudaError_t launch_attn_stream(const void *kc, const void *vc, float *out, const
     const int csz = (rows + ns - 1) / ns;
     CUtensorMap tmK, tmV;
     const bool f16 = sizeof(KV) == 2;
-    if (!attn_map(&tmK, kc, f16, (uint64_t)slots * rows, kvd, kR) ||
-        !attn_map(&tmV, vc, f16, (uint64_t)slots * rows, kvd, kR))
+    if (!attn_map(&tmK, kc, f16, (uint64_t)slots * rows, kvd, kR, kHd * G) ||
+        !attn_map(&tmV, vc, f16, (uint64_t)slots * rows, kvd, kR, kHd * G))
         return cudaErrorNotSupported;
-    return launch_k(fn, dim3(ns, nh, slots), kThrS, 128 + stages * stage_bytes, st, ns, tmK, tmV, out, q, pos, rows,
-                    nkv, nh, ns, csz, stages, dev_err);
+    return launch_k(fn, dim3(ns, nh / G, slots), kThrS, 128 + stages * stage_bytes, st, ns, tmK, tmV, out, q, pos,
+                    rows, nkv, nh, ns, csz, stages, dev_err);
+}
+
+// Two heads per CTA when each head has its own kv head (Whisper's layout), else one.
+// (Four heads per CTA measured slower: 31.5 us against 20.4 us at 8 slots x 1500 keys.)
+template <typename KV>
+cudaError_t launch_attn_stream(const void *kc, const void *vc, float *out, const float *q, const uint32_t *pos,
+                               int slots, int rows, int kvd, int nkv, int nh, int *dev_err, cudaStream_t st) {
+    if (nkv == nh && nh % 2 == 0)
+        return launch_attn_stream_g<KV, 2>(kc, vc, out, q, pos, slots, rows, kvd, nkv, nh, dev_err, st);
+    return launch_attn_stream_g<KV, 1>(kc, vc, out, q, pos, slots, rows, kvd, nkv, nh, dev_err, st);
 }
 
 }  // namespace
