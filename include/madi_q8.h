@@ -45,6 +45,10 @@ extern "C" {
 /* ---- element types ------------------------------------------------------ */
 #define MADI_F32  0
 #define MADI_F16  1
+/* Activations stored as f32 and rounded to f16 when the kernel loads them, as the
+ * reference's batched decode (decodeBlockBatched, decoder.zig:337-341) converts its
+ * f32 activations to f16 before the projection; madi_q8_linear's streaming path only. */
+#define MADI_F32_AS_F16  2
 
 /* ---- epilogues (bias / GELU / residual flags of the reference kernels) ---- */
 #define MADI_EPI_NONE       0   /* y = acc                       gemv_q8, m4_gemm_nn, logit_gemv_q8 */
@@ -180,7 +184,7 @@ int   madi_num_sms(void);
  *           residual f16 (Y f32 is accepted with MADI_EPI_NONE: unrounded f32
  *           sums, e.g. the logits of a vocab head over many token slots); f16
  *           dequantised weights, f32 accumulation.
- *   m <= 16: bandwidth-bound skinny GEMM, X f32 or f16, Y f32 or f16,
+ *   m <= 16: bandwidth-bound skinny GEMM, X f32, f16 or MADI_F32_AS_F16, Y f32 or f16,
  *           residual with Y's type and may alias Y; f32 semantics
  *           (exact int8 weights, per-block f32 scale).  (The reference's GEMV
  *           family takes one token; its batched decode takes up to 8 slots.)

@@ -22,6 +22,7 @@ MADI_EUNSUPPORTED = -8
 MADI_EBUSY = -9
 
 MADI_F32, MADI_F16 = 0, 1
+MADI_F32_AS_F16 = 2        # f32 activations rounded to f16 on load (the streaming path)
 EPI_NONE, EPI_BIAS, EPI_BIAS_GELU, EPI_BIAS_RES = 0, 1, 2, 3
 
 # every function the header declares, with its ctypes signature

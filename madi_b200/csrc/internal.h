@@ -70,8 +70,10 @@ cudaError_t launch_gemv(const GemvArgs &a, bool x_f32, bool y_f32, int epi, bool
 // x slice and one weight stage fit in shared memory, QKV included; same
 // arithmetic and epilogues as launch_gemv.  Needs 16-byte aligned qs and scales.
 bool gemv_tile_ok(int M, int N, int K, bool x_f32, int num_sms);
+// x_r16: x f32, rounded to f16 when staged (the reference's batched decode rounds its
+// activations to f16); then as f16 x.
 cudaError_t launch_gemv_tile(const GemvArgs &a, bool x_f32, bool y_f32, int epi, bool qkv, int num_sms, int *dev_err,
-                             cudaStream_t st, bool pdl);
+                             cudaStream_t st, bool pdl, bool x_r16 = false);
 
 // ---------------------------------------------------------------- variant (a)
 struct GemmArgs {

@@ -190,8 +190,9 @@ MADI_DEV void store_unit(const GemvArgs &p, int tile, int g8, int t, int tok0, c
 }
 
 // One quad column (4 consecutive k) of all M token rows of x: load = true fetches
-// it into v, load = false converts v and stores it in fragment order.
-template <typename XT, int kRows>
+// it into v, load = false converts v and stores it in fragment order.  kR16: f32 x
+// rounded to f16 when staged (stored as f16 x is).
+template <typename XT, int kRows, bool kR16>
 MADI_DEV void stage_x_quad(const GemvArgs &p, uint8_t *xs, const XT *xrow, int kq, bool have,
                            typename std::conditional<sizeof(XT) == 4, float4, uint2>::type (&v)[kRows], bool load) {
     constexpr bool kSplit = sizeof(XT) == 4;
@@ -211,7 +212,11 @@ MADI_DEV void stage_x_quad(const GemvArgs &p, uint8_t *xs, const XT *xrow, int k
 #pragma unroll
     for (int m = 0; m < kRows; ++m)
         if (m < M) {
-            if constexpr (kSplit) {
+            if constexpr (kSplit && kR16) {
+                const float4 f = v[m];
+                reinterpret_cast<uint2 *>(xs)[slot0 + m * 4] =
+                    make_uint2(h2_as_u32(__floats2half2_rn(f.x, f.y)), h2_as_u32(__floats2half2_rn(f.z, f.w)));
+            } else if constexpr (kSplit) {
                 const float4 f = v[m];
                 const __half2 h01 = __floats2half2_rn(f.x, f.y);
                 const __half2 h23 = __floats2half2_rn(f.z, f.w);
@@ -233,7 +238,7 @@ MADI_DEV void stage_x_quad(const GemvArgs &p, uint8_t *xs, const XT *xrow, int k
 // one L2 round trip.  x may have been written by the kernel this one overlaps
 // under programmatic dependent launch, so it is read on the coherent L2 path
 // (ld.global.cg), never through the non-coherent one.
-template <typename XT, int kG>
+template <typename XT, int kG, bool kR16>
 MADI_DEV void stage_x(const GemvArgs &p, uint8_t *xs, int kb0, int KS, int tid, int nthr) {
     using V = typename std::conditional<sizeof(XT) == 4, float4, uint2>::type;
     const int qrow = KS >> 2;
@@ -242,27 +247,28 @@ MADI_DEV void stage_x(const GemvArgs &p, uint8_t *xs, int kb0, int KS, int tid, 
         for (int kq = tid; kq < qrow; kq += 2 * nthr) {
             V a[8], b[8];
             const bool hb = kq + nthr < qrow;
-            stage_x_quad<XT, 8>(p, xs, xrow, kq, true, a, true);
-            stage_x_quad<XT, 8>(p, xs, xrow, kq + nthr, hb, b, true);
-            stage_x_quad<XT, 8>(p, xs, xrow, kq, true, a, false);
-            stage_x_quad<XT, 8>(p, xs, xrow, kq + nthr, hb, b, false);
+            stage_x_quad<XT, 8, kR16>(p, xs, xrow, kq, true, a, true);
+            stage_x_quad<XT, 8, kR16>(p, xs, xrow, kq + nthr, hb, b, true);
+            stage_x_quad<XT, 8, kR16>(p, xs, xrow, kq, true, a, false);
+            stage_x_quad<XT, 8, kR16>(p, xs, xrow, kq + nthr, hb, b, false);
         }
     } else {
         for (int kq = tid; kq < qrow; kq += nthr) {      // 16 rows: one quad's loads at a time
             V a[16];
-            stage_x_quad<XT, 16>(p, xs, xrow, kq, true, a, true);
-            stage_x_quad<XT, 16>(p, xs, xrow, kq, true, a, false);
+            stage_x_quad<XT, 16, kR16>(p, xs, xrow, kq, true, a, true);
+            stage_x_quad<XT, 16, kR16>(p, xs, xrow, kq, true, a, false);
         }
     }
 }
 
 // kG: token groups of 8 (1 for M <= 8, 2 for 9..16); each weight fragment feeds
 // one m16n8k16 MMA per group.
-template <typename XT, typename YT, int EPI, bool kQKV, int kG>
+// kR16: f32 x rounded to f16 when staged, then the f16 path (one MMA per group).
+template <typename XT, typename YT, int EPI, bool kQKV, int kG, bool kR16>
 __global__ void __launch_bounds__(kThreads, 2)
     q8_gemv_tile_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tms,
                         const GemvArgs p, const TilePlan plan, int *dev_err) {
-    constexpr bool kSplit = sizeof(XT) == 4;
+    constexpr bool kSplit = sizeof(XT) == 4 && !kR16;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int M = p.M, N = p.N;
@@ -339,7 +345,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         // ------------------------------------------------ consumers
         asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
         asm volatile("griddepcontrol.wait;" ::: "memory");
-        stage_x<XT, kG>(p, xs, kb0, KS, (int)threadIdx.x - 32, kConsumers * 32);
+        stage_x<XT, kG, kR16>(p, xs, kb0, KS, (int)threadIdx.x - 32, kConsumers * 32);
         asm volatile("bar.sync 1, %0;" ::"r"(kConsumers * 32) : "memory");   // consumers only
 
         const int cw = warp - 1;
@@ -482,10 +488,10 @@ bool make_tile_maps(const GemvArgs &a, int KS, CUtensorMap *tmq, CUtensorMap *tm
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <typename XT, typename YT, int EPI, bool kQKV, int kG>
+template <typename XT, typename YT, int EPI, bool kQKV, int kG, bool kR16>
 cudaError_t launch_tile_g(const GemvArgs &a, const CUtensorMap &tmq, const CUtensorMap &tms, const TilePlan &pl,
                           int grid, int *dev_err, cudaStream_t st, bool pdl) {
-    auto fn = q8_gemv_tile_kernel<XT, YT, EPI, kQKV, kG>;
+    auto fn = q8_gemv_tile_kernel<XT, YT, EPI, kQKV, kG, kR16>;
     static bool attr = false;
     if (!attr) {
         cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemCap);
@@ -495,7 +501,7 @@ cudaError_t launch_tile_g(const GemvArgs &a, const CUtensorMap &tmq, const CUten
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = plan_smem(a.M, pl, sizeof(XT) == 4);
+    cfg.dynamicSmemBytes = plan_smem(a.M, pl, sizeof(XT) == 4 && !kR16);
     cfg.stream = st;
     cudaLaunchAttribute attrs[2];
     int na = 0;
@@ -514,11 +520,11 @@ cudaError_t launch_tile_g(const GemvArgs &a, const CUtensorMap &tmq, const CUten
     return cudaLaunchKernelEx(&cfg, fn, tmq, tms, a, pl, dev_err);
 }
 
-template <typename XT, typename YT, int EPI, bool kQKV>
+template <typename XT, typename YT, int EPI, bool kQKV, bool kR16 = false>
 cudaError_t launch_tile_one(const GemvArgs &a, const CUtensorMap &tmq, const CUtensorMap &tms, const TilePlan &pl,
                             int grid, int *dev_err, cudaStream_t st, bool pdl) {
-    return a.M > 8 ? launch_tile_g<XT, YT, EPI, kQKV, 2>(a, tmq, tms, pl, grid, dev_err, st, pdl)
-                   : launch_tile_g<XT, YT, EPI, kQKV, 1>(a, tmq, tms, pl, grid, dev_err, st, pdl);
+    return a.M > 8 ? launch_tile_g<XT, YT, EPI, kQKV, 2, kR16>(a, tmq, tms, pl, grid, dev_err, st, pdl)
+                   : launch_tile_g<XT, YT, EPI, kQKV, 1, kR16>(a, tmq, tms, pl, grid, dev_err, st, pdl);
 }
 
 }  // namespace
@@ -530,10 +536,11 @@ bool gemv_tile_ok(int M, int N, int K, bool x_f32, int num_sms) {
 }
 
 cudaError_t launch_gemv_tile(const GemvArgs &a, bool x_f32, bool y_f32, int epi, bool qkv, int num_sms, int *dev_err,
-                             cudaStream_t st, bool pdl) {
+                             cudaStream_t st, bool pdl, bool x_r16) {
     TilePlan pl;
     int grid;
-    if (!make_plan(a.M, a.N, a.K, x_f32, num_sms, &pl, &grid)) return cudaErrorInvalidValue;
+    if (x_r16 && (!x_f32 || qkv)) return cudaErrorInvalidValue;
+    if (!make_plan(a.M, a.N, a.K, x_f32 && !x_r16, num_sms, &pl, &grid)) return cudaErrorInvalidValue;
     CUtensorMap tmq, tms;
     if (!make_tile_maps(a, pl.kslice, &tmq, &tms)) return cudaErrorNotSupported;
     if (qkv) return launch_tile_one<float, float, kEpiNone, true>(a, tmq, tms, pl, grid, dev_err, st, pdl);
@@ -547,6 +554,19 @@ cudaError_t launch_gemv_tile(const GemvArgs &a, bool x_f32, bool y_f32, int epi,
             return launch_tile_one<XT, YT, kEpiBiasRes, false>(a, tmq, tms, pl, grid, dev_err, st, pdl);         \
         default: return cudaErrorInvalidValue;                                                                   \
     }
+#define MADI_TILE_R16(YT)                                                                                           \
+    switch (epi) {                                                                                                  \
+        case kEpiNone: return launch_tile_one<float, YT, kEpiNone, false, true>(a, tmq, tms, pl, grid, dev_err, st, pdl); \
+        case kEpiBias: return launch_tile_one<float, YT, kEpiBias, false, true>(a, tmq, tms, pl, grid, dev_err, st, pdl); \
+        case kEpiBiasGelu:                                                                                          \
+            return launch_tile_one<float, YT, kEpiBiasGelu, false, true>(a, tmq, tms, pl, grid, dev_err, st, pdl);   \
+        case kEpiBiasRes:                                                                                           \
+            return launch_tile_one<float, YT, kEpiBiasRes, false, true>(a, tmq, tms, pl, grid, dev_err, st, pdl);    \
+        default: return cudaErrorInvalidValue;                                                                      \
+    }
+    if (x_r16 && y_f32) { MADI_TILE_R16(float) }
+    if (x_r16) { MADI_TILE_R16(__half) }
+#undef MADI_TILE_R16
     if (x_f32 && y_f32) { MADI_TILE_CASE(float, float) }
     if (x_f32 && !y_f32) { MADI_TILE_CASE(float, __half) }
     if (!x_f32 && y_f32) { MADI_TILE_CASE(__half, float) }

@@ -138,9 +138,11 @@ int q8_linear_impl(const madi_q8w *w, const void *x, int x_dtype, int m, const v
     if (epi < MADI_EPI_NONE || epi > MADI_EPI_BIAS_RES) return fail(MADI_EINVAL, "%s: bad epilogue %d", who, epi);
     if (epi != MADI_EPI_NONE && !bias) return fail(MADI_EINVAL, "%s: epilogue %d needs a bias", who, epi);
     if (epi == MADI_EPI_BIAS_RES && !residual) return fail(MADI_EINVAL, "%s: residual epilogue needs a residual", who);
-    if ((x_dtype != MADI_F32 && x_dtype != MADI_F16) || (y_dtype != MADI_F32 && y_dtype != MADI_F16) ||
-        (bias && bias_dtype != MADI_F32 && bias_dtype != MADI_F16))
+    if ((x_dtype != MADI_F32 && x_dtype != MADI_F16 && x_dtype != MADI_F32_AS_F16) ||
+        (y_dtype != MADI_F32 && y_dtype != MADI_F16) || (bias && bias_dtype != MADI_F32 && bias_dtype != MADI_F16))
         return fail(MADI_EINVAL, "%s: bad dtype", who);
+    const bool x_r16 = x_dtype == MADI_F32_AS_F16;
+    if (x_r16) x_dtype = MADI_F32;
     if ((size_t)m * (size_t)std::max(N, K) >= (1ull << 31) || (size_t)N * K >= (1ull << 40))
         return fail(MADI_EINVAL, "%s: problem too large (m=%d N=%d K=%d)", who, m, N, K);
     if (!aligned(w->qs, 16) || !aligned(w->scales, 2)) return fail(MADI_EINVAL, "%s: qs must be 16-byte aligned", who);
@@ -150,7 +152,10 @@ int q8_linear_impl(const madi_q8w *w, const void *x, int x_dtype, int m, const v
     // another K, the tensor-core GEMM.
     const bool x_al = aligned(x, x_dtype == MADI_F32 ? 16 : 8);
     const bool tile_fits = m <= kGemvMaxM && x_al && aligned(w->scales, 16) &&
-                           gemv_tile_ok(m, N, K, x_dtype == MADI_F32, S.num_sms);
+                           gemv_tile_ok(m, N, K, x_dtype == MADI_F32 && !x_r16, S.num_sms);
+    if (x_r16 && !tile_fits)
+        return fail(MADI_EINVAL, "%s: MADI_F32_AS_F16 activations need the streaming path (m <= %d, K %% 256 == 0, "
+                                 "16-byte aligned x and scales)", who, kGemvMaxM);
     if (m >= kGemmMinM && !tile_fits) {
         const bool y32 = y_dtype == MADI_F32;
         if (x_dtype != MADI_F16 || (y32 && epi != MADI_EPI_NONE))
@@ -177,7 +182,8 @@ int q8_linear_impl(const madi_q8w *w, const void *x, int x_dtype, int m, const v
     const bool xf32 = x_dtype == MADI_F32;
     if (!aligned(x, xf32 ? 16 : 8)) return fail(MADI_EINVAL, "%s: x must be %d-byte aligned", who, xf32 ? 16 : 8);
     const int ks = gemv_pick_ks(N, K, S.num_sms);
-    const bool tile_path = aligned(w->qs, 16) && aligned(w->scales, 16) && gemv_tile_ok(m, N, K, xf32, S.num_sms);
+    const bool tile_path =
+        aligned(w->qs, 16) && aligned(w->scales, 16) && gemv_tile_ok(m, N, K, xf32 && !x_r16, S.num_sms);
     if (!tile_path && gemv_smem_bytes(m, K, ks, xf32) > (size_t)S.max_smem_optin)
         return fail(MADI_EINVAL, "%s: K=%d too large for the decode path at m=%d", who, K, m);
     GemvArgs a{};
@@ -188,7 +194,8 @@ int q8_linear_impl(const madi_q8w *w, const void *x, int x_dtype, int m, const v
     a.N = N; a.K = K; a.M = m;
     a.ks = ks;
     cudaError_t e = tile_path
-                        ? launch_gemv_tile(a, xf32, y_dtype == MADI_F32, epi, false, S.num_sms, S.dev_err, st, S.pdl)
+                        ? launch_gemv_tile(a, xf32, y_dtype == MADI_F32, epi, false, S.num_sms, S.dev_err, st, S.pdl,
+                                           x_r16)
                         : launch_gemv(a, xf32, y_dtype == MADI_F32, epi, false, st, S.pdl);
     if (e == cudaErrorNotSupported) return fail(MADI_EUNSUPPORTED, "%s: cuTensorMapEncodeTiled unavailable", who);
     if (e != cudaSuccess) return cuda_fail(e, who);

@@ -106,13 +106,17 @@ def device_weights(seed: int = 1, device="cuda") -> dict:
 class Decoder:
     """Device copy of the synthetic decoder plus the per-slot decode state."""
 
-    def __init__(self, w: dict, slots: int, device="cuda"):
+    def __init__(self, w: dict, slots: int, device="cuda", act16: bool = False):
+        """act16: the projections other than the fused QKV take their f32 activations
+        rounded to f16, as the reference's batched decode (decodeBlockBatched,
+        decoder.zig:337-341) converts them; False keeps the single-token GEMV family's
+        f32 activations."""
         if not 1 <= slots <= 16:
             raise ValueError("1..16 token slots")
         t = lambda a: (a.to(device) if isinstance(a, torch.Tensor) else
                        torch.from_numpy(np.ascontiguousarray(a)).to(device))
         qw = lambda p: q8.Q8Weight(t(p[0]), t(p[1]))
-        self.slots, self.dev = slots, device
+        self.slots, self.dev, self.act16 = slots, device, act16
         self.layers: List[Layer] = []
         for L in w["layers"]:
             self.layers.append(Layer(
@@ -163,21 +167,22 @@ class Decoder:
         """One greedy token for every slot; all state on the device.  suppress: device
         u32 token ids banned at every step (e.g. EOT, to force a fixed length)."""
         s = dict(stream=stream)
+        r = dict(stream=stream, x_round16=self.act16)
         greedy.emb_pos_q8(self.emb, self.tokens, self.pos, self.pos_emb, out=self.x, **s)
         for l, L in enumerate(self.layers):
             q8.layer_norm(self.x, *L.aln, eps=EPS, out=self.xb, **s)
             q8.qkv(L.qkv, self.xb, L.qb, L.vb, self.kc[l], self.vc[l], self.pos, q_out=self.q, **s)
             attn.self_attn(self.q, self.kc[l], self.vc[l], self.pos, HEADS, out=self.ao, **s)
-            q8.linear(L.o, self.ao, out=self.mo, **s)
+            q8.linear(L.o, self.ao, out=self.mo, **r)
             q8.bias_res_ln(self.x, self.mo, L.ob, *L.caln, eps=EPS, out=self.xb, **s)
-            q8.linear(L.cq, self.xb, bias=L.cqb, out=self.q, **s)
+            q8.linear(L.cq, self.xb, bias=L.cqb, out=self.q, **r)
             attn.cross_attn(self.q, self.ck[l], self.cv[l], HEADS, out=self.ao, **s)
-            q8.linear(L.co, self.ao, out=self.mo, **s)
+            q8.linear(L.co, self.ao, out=self.mo, **r)
             q8.bias_res_ln(self.x, self.mo, L.cob, *L.mln, eps=EPS, out=self.xb, **s)
-            q8.linear(L.fc1, self.xb, bias=L.m0b, epi=q8.EPI_BIAS_GELU, out=self.mh, **s)
-            q8.linear(L.fc2, self.mh, bias=L.m2b, epi=q8.EPI_BIAS_RES, residual=self.x, out=self.x, **s)
+            q8.linear(L.fc1, self.xb, bias=L.m0b, epi=q8.EPI_BIAS_GELU, out=self.mh, **r)
+            q8.linear(L.fc2, self.mh, bias=L.m2b, epi=q8.EPI_BIAS_RES, residual=self.x, out=self.x, **r)
         q8.layer_norm(self.x, *self.ln_post, eps=EPS, out=self.xb, **s)
-        q8.linear(self.emb, self.xb, out=self.logits, **s)
+        q8.linear(self.emb, self.xb, out=self.logits, **r)
         greedy.decode_tail(self.logits, self.tokens, self.pos, self.conf, sample_begin, no_repeat_ngram, suppress,
                            **s)
 

@@ -40,7 +40,8 @@ class Transcriber:
         if tokens < 1 or tokens + 1 > dec.MAX_TOK:
             raise ValueError(f"1..{dec.MAX_TOK - 1} tokens per chunk")
         self.encoder = enc.Encoder(enc_layers, seed, device)
-        self.decoder = dec.Decoder(dec.device_weights(seed, device), slots, device)
+        # more than one slot: the reference's batched decode, f16 activations
+        self.decoder = dec.Decoder(dec.device_weights(seed, device), slots, device, act16=slots > 1)
         self.slots, self.tokens = slots, tokens
         self.eot = torch.tensor([EOT], dtype=torch.int32, device=device)
         self.graph = None

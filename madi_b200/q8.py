@@ -12,7 +12,7 @@ from typing import Optional
 import torch
 
 from . import _lib
-from ._lib import EPI_BIAS, EPI_BIAS_GELU, EPI_BIAS_RES, EPI_NONE, MADI_F16, MADI_F32  # noqa: F401
+from ._lib import EPI_BIAS, EPI_BIAS_GELU, EPI_BIAS_RES, EPI_NONE, MADI_F16, MADI_F32, MADI_F32_AS_F16  # noqa: F401
 
 _DT = {torch.float32: MADI_F32, torch.float16: MADI_F16}
 
@@ -60,8 +60,10 @@ def _ptr(t):
 
 def linear(w: Q8Weight, x: torch.Tensor, bias: Optional[torch.Tensor] = None, epi: Optional[int] = None,
            residual: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
-           out_dtype: Optional[torch.dtype] = None, stream=None) -> torch.Tensor:
+           out_dtype: Optional[torch.dtype] = None, stream=None, x_round16: bool = False) -> torch.Tensor:
     """y[m][n] = epi(x @ deq(w)^T).  x [m][k] (f16; f32 also allowed for m <= 16).
+    x_round16: f32 x is rounded to f16 as it is loaded (the reference's batched decode
+    projects f16 activations); streaming path only (m <= 16, K % 256 == 0).
     epi defaults to BIAS when a bias is given, BIAS_RES when a residual is given.
     m <= 16 runs the decode skinny GEMM (when K % 256 == 0, else m <= 8), larger m
     the tcgen05 GEMM."""
@@ -79,7 +81,8 @@ def linear(w: Q8Weight, x: torch.Tensor, bias: Optional[torch.Tensor] = None, ep
         raise TypeError("residual must have the output's dtype")
     bias_dt = _DT[bias.dtype] if bias is not None else MADI_F32
     h = w.handle()
-    rc = _lib.load().madi_q8_linear(ctypes.byref(h), x.data_ptr(), _DT[x.dtype], m, _ptr(bias), bias_dt, epi,
+    x_dt = MADI_F32_AS_F16 if (x_round16 and x.dtype == torch.float32) else _DT[x.dtype]
+    rc = _lib.load().madi_q8_linear(ctypes.byref(h), x.data_ptr(), x_dt, m, _ptr(bias), bias_dt, epi,
                                     _ptr(residual), out.data_ptr(), _DT[out.dtype], _stream(stream))
     _lib.check(rc, "madi_q8_linear")
     return out

@@ -23,9 +23,11 @@ def _t(a, dev="cuda"):
     return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
 
 
-def _oracle_decode(oracle, w, ck, cv, dec):
+def _oracle_decode(oracle, w, ck, cv, dec, act16=False):
     D, HEADS, MAX_TOK = dec.D, dec.HEADS, dec.MAX_TOK
     f32 = lambda a: np.asarray(a, np.float32)
+    # act16: the activations of every projection but the fused QKV rounded to f16
+    r = (lambda a: f32(a).astype(np.float16).astype(np.float32)) if act16 else f32
     S = ck[0].shape[0]
     tokens = np.zeros((S, MAX_TOK), np.uint32)
     tokens[:, 0] = SEED_TOKEN
@@ -44,16 +46,16 @@ def _oracle_decode(oracle, w, ck, cv, dec):
                 kc[l][b, pos[b]] = f32(full[b, D:2 * D])
                 vc[l][b, pos[b]] = f32(full[b, 2 * D:] + L["vb"])
             ao = f32(oracle.self_attn(q, kc[l], vc[l], pos, HEADS))
-            mo = f32(oracle.gemv_q8(ao, *L["o"]))
+            mo = f32(oracle.gemv_q8(r(ao), *L["o"]))
             x, xb = oracle.bias_res_ln_f32(x, mo, L["ob"], *L["caln"], dec.EPS)
-            q = f32(oracle.gemv_q8(f32(xb), *L["cq"], bias=L["cqb"], epi=oracle.EPI_BIAS))
+            q = f32(oracle.gemv_q8(r(xb), *L["cq"], bias=L["cqb"], epi=oracle.EPI_BIAS))
             ao = f32(oracle.cross_attn(q, ck[l], cv[l], HEADS)[0])
-            mo = f32(oracle.gemv_q8(ao, *L["co"]))
+            mo = f32(oracle.gemv_q8(r(ao), *L["co"]))
             x, xb = oracle.bias_res_ln_f32(x, mo, L["cob"], *L["mln"], dec.EPS)
-            mh = f32(oracle.gemv_q8(f32(xb), *L["fc1"], bias=L["m0b"], epi=oracle.EPI_BIAS_GELU))
-            x = f32(oracle.gemv_q8(mh, *L["fc2"], bias=L["m2b"], epi=oracle.EPI_BIAS_RES, res_in=x))
+            mh = f32(oracle.gemv_q8(r(xb), *L["fc1"], bias=L["m0b"], epi=oracle.EPI_BIAS_GELU))
+            x = f32(oracle.gemv_q8(r(mh), *L["fc2"], bias=L["m2b"], epi=oracle.EPI_BIAS_RES, res_in=x))
         _, xb = oracle.bias_res_ln_f32(x, None, None, *w["ln_post"], dec.EPS)
-        logits = oracle.gemv_q8(f32(xb), eq, es)
+        logits = oracle.gemv_q8(r(xb), eq, es)
         pos += 1
         for b in range(S):
             lg = oracle.logit_filter(f32(logits[b]), tokens[b], int(pos[b]), SAMPLE_BEGIN, 0)
@@ -65,11 +67,14 @@ def _oracle_decode(oracle, w, ck, cv, dec):
     return tokens, np.array(confs).reshape(STEPS, S), min(margins)
 
 
-def test_greedy_decoder_end_to_end(madi, oracle):
+@pytest.mark.parametrize("act16", [False, True])
+def test_greedy_decoder_end_to_end(madi, oracle, act16):
+    """act16=False: the single-token GEMV family's f32 activations; True: the batched
+    decode's f16 activations (every projection but the fused QKV)."""
     import torch
     from madi_b200 import decoder as dec
     w = dec.host_weights(seed=1)
-    model = dec.Decoder(w, SLOTS)
+    model = dec.Decoder(w, SLOTS, act16=act16)
     g = np.random.default_rng(5)
     enc = g.standard_normal((SLOTS, dec.ENC, dec.D)).astype(np.float16)
     model.set_encoder(_t(enc))
@@ -99,9 +104,13 @@ def test_greedy_decoder_end_to_end(madi, oracle):
     conf = model.conf[:, 1:STEPS + 1].cpu().numpy()
     del graph
 
-    want, want_conf, margin = _oracle_decode(oracle, w, ck, cv, dec)
+    want, want_conf, margin = _oracle_decode(oracle, w, ck, cv, dec, act16)
     assert margin > 1e-3, f"synthetic data too close to a tie (margin {margin:.2e})"
     assert np.array_equal(first, want[:, 1])
     assert np.array_equal(got, want[:, :STEPS + 1]), f"GPU {got.tolist()}\noracle {want[:, :STEPS + 1].tolist()}"
     assert int(model.pos[0].item()) == STEPS
-    np.testing.assert_allclose(conf.T, want_conf, rtol=1e-3)
+    # act16: the GPU rounds its f32 LayerNorm / GEMV results to f16, the oracle its f64
+    # ones; an element at an f16 rounding boundary can land one ulp apart, and such
+    # differences travel through the four layers into the logits, so the confidence
+    # (a softmax probability) gets a looser bar -- the tokens stay bit-identical
+    np.testing.assert_allclose(conf.T, want_conf, rtol=2e-2 if act16 else 1e-3)

@@ -137,6 +137,29 @@ def test_two_token_group_plans(madi, oracle, M, N, K, epi, x_dt, y_dt):
     _case(madi, oracle, M, N, K, epi, x_dt=x_dt, y_dt=y_dt, seed=N + K + 3 * M)
 
 
+@pytest.mark.parametrize("M", [1, 3, 8, 12, 16])
+@pytest.mark.parametrize("name,N,K", synth.decoder_shapes() + [("head", 51866, 1280)])
+def test_f32_rounded_to_f16_on_load(madi, oracle, M, name, N, K):
+    """MADI_F32_AS_F16: f32 x rounded to f16 as it is staged (the batched decode's f16
+    activations), then the f16 path; against the oracle on the f16-rounded x."""
+    import torch
+    from madi_b200 import q8
+    epi = {"qkv": 0, "o": 0, "cq": 1, "co": 0, "fc1": 2, "fc2": 3, "head": 0}[name]
+    qs, sc = synth.q8_weight(N, K, M + N + 5)
+    x = synth.activations(M, K, M + N + 6, dtype=np.float32) * 3.0
+    b = synth.bias(N, M + N + 7)
+    res = synth.activations(M, N, M + N + 8, dtype=np.float32) if epi == q8.EPI_BIAS_RES else None
+    out = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    if res is not None:
+        out.copy_(_t(res))
+    q8.linear(q8.Q8Weight(_t(qs), _t(sc)), _t(x), bias=_t(b) if epi else None, epi=epi,
+              residual=out if res is not None else None, out=out, x_round16=True)
+    torch.cuda.synchronize()
+    x16 = x.astype(np.float16).astype(np.float32)
+    y_exact = oracle.gemv_q8(x16, qs, sc, bias=b, epi=epi, res_in=res)
+    _check(out, y_exact, f"round16 M={M} {name}")
+
+
 def test_qkv_kv_store(madi, oracle):
     """gemv_q8_qkv: q+qb -> q_out, k -> kc[pos], v+vb -> vc[pos] (pos read on device)."""
     import torch

@@ -67,9 +67,10 @@ def test_forced_length(tr):
     assert int(tr.decoder.pos[0].item()) == 6
 
 
-def test_slot_count_invariance(madi):
+@pytest.mark.parametrize("act16", [False, True])
+def test_slot_count_invariance(madi, act16):
     """The decoder at 12 slots (two token groups per GEMV weight fragment) gives the
-    first 4 chunks the same tokens as the decoder at 4 slots."""
+    first 4 chunks the same tokens as the decoder at 4 slots (f32 or f16 activations)."""
     import torch
     from madi_b200 import decoder as dec
     w = dec.device_weights(seed=9)
@@ -78,7 +79,7 @@ def test_slot_count_invariance(madi):
     states = torch.randn((12, dec.ENC, dec.D), device="cuda", generator=g).half()
     got = []
     for slots in (12, 4):
-        d = dec.Decoder(w, slots)
+        d = dec.Decoder(w, slots, act16=act16)
         d.set_encoder(states[:slots].contiguous())
         d.reset(50258)
         for _ in range(6):
