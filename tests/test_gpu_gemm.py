@@ -82,7 +82,7 @@ def test_encoder_ffn_pair_b1(madi, oracle):
     torch.cuda.synchronize()
     h_exact = oracle.linear_f16(x, w["fc1_qs"], w["fc1_scales"], w["fc1_bias"], oracle.EPI_BIAS_GELU)
     _check(H, h_exact, "fc1")
-    # fc2 judged on the GPU's own H (isolates the kernel) and end to end
+    # fc2 checked on the GPU's own H (isolates the kernel) and end to end
     h16 = H.cpu().numpy()
     y_exact = oracle.linear_f16(h16, w["fc2_qs"], w["fc2_scales"], w["fc2_bias"], oracle.EPI_BIAS_RES, residual=x)
     _check(Y, y_exact, "fc2")
