@@ -6,7 +6,7 @@ put under a profiler (ncu -k regex:<kernel> -s <skip> -c <count> ...).
     python -m madi_b200.cases cross --m 8 --n 1500 --k 1280 --iters 6   (slots, keys, kv_dim)
     python -m madi_b200.cases self --m 8 --n 448 --k 1280 --iters 6     (slots, cache rows, kv_dim)
     python -m madi_b200.cases flash --m 8 --n 1500 --k 1280 --iters 6    (chunks, seq, heads*64)
-    python -m madi_b200.cases decoder --m 8 --n 64 --k 1280 --iters 6    (slots, tokens decoded first, d)
+    python -m madi_b200.cases decoder --m 15 --n 112 --k 1280 --iters 6  (slots, tokens decoded first, d)
 
 Inputs are seeded random tensors of the given shape (int8 weights in [-127, 127],
 f16 scales in [1e-4, 2.1e-3], N(0,1) activations); the script prints the mean
@@ -132,9 +132,10 @@ def flash_case(a, dev, g):
 def decoder_case(a, dev):
     """The synthetic 4-layer greedy decoder (madi_b200/decoder.py) with --m slots: one
     token step captured as a CUDA graph, replayed --n times untimed (the positions
-    reach n), then --iters timed replays."""
+    reach n), then --iters timed replays.  --x f16 (the default) with more than one
+    slot: the batched decode's f16-rounded activations; --x f32: f32 activations."""
     from . import decoder as dec
-    model = dec.Decoder(dec.host_weights(seed=1), a.m, device=dev)
+    model = dec.Decoder(dec.host_weights(seed=1), a.m, device=dev, act16=a.x == "f16" and a.m > 1)
     g = torch.Generator(device=dev)
     g.manual_seed(5)
     model.set_encoder(torch.randn((a.m, dec.ENC, dec.D), device=dev, generator=g).half())
