@@ -23,7 +23,8 @@ Workload (N=1 is BASELINE config 1 at B=16, the largest single-GPU config):
   long_audio: 120 chunks of synthetic log-mel sharded over the
           ranks; per batch of <= 16 chunks the whole encoder (conv stem, 32 Q8 layers,
           ln_post), cross K/V, then exactly 224 greedy tokens per chunk (EOT
-          suppressed) -- chunks/s from pinned host mel to host tokens, slowest rank.
+          suppressed), batch k+1's encoder overlapped with batch k's decoder --
+          chunks/s from pinned host mel to host tokens, slowest rank.
 Multi-GPU: one process per GPU (torchrun), each rank runs its own B chunks
 (weak scaling, no data-path collective on the encoder); times are the max
 over ranks.  --impl reference times the reference's CPU computation of the
@@ -67,6 +68,8 @@ def parse():
     ap.add_argument("--no-long-audio", action="store_true")
     ap.add_argument("--chunks", type=int, default=120, help="long-audio leg: 30 s chunks over all GPUs (config 4)")
     ap.add_argument("--tokens", type=int, default=224, help="long-audio leg: greedy tokens per chunk")
+    ap.add_argument("--no-overlap", action="store_true",
+                    help="long-audio leg: run each batch's encoder and decoder back to back on one stream")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     return ap.parse_args()
 
@@ -438,20 +441,49 @@ def long_audio_leg(args, world, rank, dev):
     barrier(world)
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
     enc_ms, dec_ms = [], []
-    ev[0].record()
-    for i in range(0, mine, slots):
-        b = min(slots, mine - i)
-        e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
-        e0.record()
-        mel_d[:b].copy_(mel_h[i:i + b], non_blocking=True)
-        states = tr.encode(mel_d[:b])
-        e1.record()
-        toks = tr.decode(states)
-        tok_h[i:i + b].copy_(toks, non_blocking=True)
-        e2.record()
+    overlap = not args.no_overlap
+    batches = [(i, min(slots, mine - i)) for i in range(0, mine, slots)]
+    cur = torch.cuda.current_stream()
+    # overlapped: batch k + 1's encoder (tensor-core GEMMs, flash attention) runs on its
+    # own stream while batch k decodes on a higher-priority stream; the decoder's
+    # latency-bound token steps leave most of the GPU idle
+    enc_s = torch.cuda.Stream(device=dev) if overlap else cur
+    dec_s = torch.cuda.Stream(device=dev, priority=-1) if overlap else cur
+    ev[0].record(cur)
+    enc_s.wait_stream(cur)
+    dec_s.wait_stream(cur)
+
+    def encode(k):
+        i, b = batches[k]
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(enc_s):
+            e0.record(enc_s)
+            mel_d[:b].copy_(mel_h[i:i + b], non_blocking=True)
+            st = tr.encode(mel_d[:b])
+            e1.record(enc_s)
         enc_ms.append((e0, e1))
+        return st, e1
+
+    nxt = encode(0) if batches else None
+    for k, (i, b) in enumerate(batches):
+        states, ready = nxt
+        e1, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(dec_s):
+            dec_s.wait_event(ready)
+            e1.record(dec_s)
+            states.record_stream(dec_s)
+            if overlap and k + 1 < len(batches):
+                # the next encoder may start once this batch's states are taken
+                nxt = encode(k + 1)
+            toks = tr.decode(states)
+            tok_h[i:i + b].copy_(toks, non_blocking=True)
+            e2.record(dec_s)
         dec_ms.append((e1, e2))
-    ev[1].record()
+        if not overlap and k + 1 < len(batches):
+            nxt = encode(k + 1)
+        del states
+    cur.wait_stream(dec_s)
+    ev[1].record(cur)
     torch.cuda.synchronize()
     ms = ev[0].elapsed_time(ev[1]) if mine else 0.0
     ms_max = max_over_ranks(world, ms)
@@ -464,6 +496,7 @@ def long_audio_leg(args, world, rank, dev):
     return {"chunks": args.chunks, "chunks_per_rank": per, "tokens_per_chunk": args.tokens, "slots": slots,
             "chunks_per_s": args.chunks / (ms_max / 1e3), "ms_total": ms_max, "scaling": "strong",
             "encoder_ms_per_batch": enc_avg, "decoder_ms_per_batch": dec_avg,
+            "overlap": "encoder of batch k+1 on its own stream beside the decoder of batch k" if overlap else None,
             "decoder_ms_per_token_step": dec_avg / args.tokens,
             "encoder": f"conv stem (PyTorch f16 conv1d) + 32 Q8 layers + ln_post, {slots} chunks per batch",
             "decoder": "4 Q8 layers, replicated head, one CUDA graph per token step, EOT suppressed",
