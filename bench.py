@@ -439,52 +439,15 @@ def long_audio_leg(args, world, rank, dev):
     tr.transcribe(mel_d[:b0])                       # untimed: module load, graph capture
     torch.cuda.synchronize()
     barrier(world)
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
-    enc_ms, dec_ms = [], []
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
     overlap = not args.no_overlap
-    batches = [(i, min(slots, mine - i)) for i in range(0, mine, slots)]
-    cur = torch.cuda.current_stream()
-    # overlapped: batch k + 1's encoder (tensor-core GEMMs, flash attention) runs on its
-    # own stream while batch k decodes on a higher-priority stream; the decoder's
-    # latency-bound token steps leave most of the GPU idle
-    enc_s = torch.cuda.Stream(device=dev) if overlap else cur
-    dec_s = torch.cuda.Stream(device=dev, priority=-1) if overlap else cur
-    ev[0].record(cur)
-    enc_s.wait_stream(cur)
-    dec_s.wait_stream(cur)
-
-    def encode(k):
-        i, b = batches[k]
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with torch.cuda.stream(enc_s):
-            e0.record(enc_s)
-            mel_d[:b].copy_(mel_h[i:i + b], non_blocking=True)
-            st = tr.encode(mel_d[:b])
-            e1.record(enc_s)
-        enc_ms.append((e0, e1))
-        return st, e1
-
-    nxt = encode(0) if batches else None
-    for k, (i, b) in enumerate(batches):
-        states, ready = nxt
-        e1, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with torch.cuda.stream(dec_s):
-            dec_s.wait_event(ready)
-            e1.record(dec_s)
-            states.record_stream(dec_s)
-            if overlap and k + 1 < len(batches):
-                # the next encoder may start once this batch's states are taken
-                nxt = encode(k + 1)
-            toks = tr.decode(states)
-            tok_h[i:i + b].copy_(toks, non_blocking=True)
-            e2.record(dec_s)
-        dec_ms.append((e1, e2))
-        if not overlap and k + 1 < len(batches):
-            nxt = encode(k + 1)
-        del states
-    cur.wait_stream(dec_s)
-    ev[1].record(cur)
+    timings = []
+    ev[0].record()
+    tr.transcribe_chunks(mel_h[:mine], tok_h[:mine], overlap=overlap, timings=timings)
+    ev[1].record()
     torch.cuda.synchronize()
+    enc_ms = [t[0] for t in timings]
+    dec_ms = [t[1] for t in timings]
     ms = ev[0].elapsed_time(ev[1]) if mine else 0.0
     ms_max = max_over_ranks(world, ms)
     enc_avg = sum(a.elapsed_time(b) for a, b in enc_ms) / max(1, len(enc_ms))

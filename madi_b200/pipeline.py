@@ -15,6 +15,8 @@ order does not depend on M, attention runs per chunk / slot, and the decode
 kernels treat token slots independently, so a chunk's tokens do not depend on
 which batch it was decoded in.
 """
+from typing import Optional
+
 import numpy as np
 import torch
 
@@ -79,6 +81,59 @@ class Transcriber:
 
     def transcribe(self, mel: torch.Tensor) -> torch.Tensor:
         return self.decode(self.encode(mel))
+
+    def transcribe_chunks(self, mel_host: torch.Tensor, tokens_host: torch.Tensor, overlap: bool = True,
+                          timings: Optional[list] = None) -> None:
+        """Every chunk of mel_host (f16 [n][128][3000], pinned host memory) to
+        tokens_host (int32 [n][tokens], pinned), in batches of `slots` chunks: the
+        mel copy and the encoder of batch k + 1 run on their own stream beside batch k's
+        decoder, which runs on a higher-priority stream (its latency-bound token steps
+        leave most of the GPU idle); overlap=False runs the phases back to back.  Returns
+        when the work is queued; synchronise before reading tokens_host.  timings, if
+        given, receives ((encoder start, end), (decoder start, end)) CUDA events per
+        batch."""
+        n = mel_host.shape[0]
+        batches = [(i, min(self.slots, n - i)) for i in range(0, n, self.slots)]
+        if not batches:
+            return
+        dev = self.encoder.pos.device
+        cur = torch.cuda.current_stream(dev)
+        enc_s = torch.cuda.Stream(device=dev) if overlap else cur
+        dec_s = torch.cuda.Stream(device=dev, priority=-1) if overlap else cur
+        enc_s.wait_stream(cur)
+        dec_s.wait_stream(cur)
+        mel_d = torch.empty((self.slots,) + tuple(mel_host.shape[1:]), dtype=torch.float16, device=dev)
+        mel_d.record_stream(enc_s)
+
+        def encode(k):
+            i, b = batches[k]
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(enc_s):
+                e0.record(enc_s)
+                mel_d[:b].copy_(mel_host[i:i + b], non_blocking=True)
+                st = self.encode(mel_d[:b])
+                e1.record(enc_s)
+            return st, (e0, e1)
+
+        nxt = encode(0)
+        for k, (i, b) in enumerate(batches):
+            states, enc_ev = nxt
+            d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(dec_s):
+                dec_s.wait_event(enc_ev[1])
+                d0.record(dec_s)
+                states.record_stream(dec_s)
+                if overlap and k + 1 < len(batches):
+                    nxt = encode(k + 1)             # its states are taken: the next encoder may start
+                toks = self.decode(states)
+                tokens_host[i:i + b].copy_(toks, non_blocking=True)
+                d1.record(dec_s)
+            if timings is not None:
+                timings.append((enc_ev, (d0, d1)))
+            if not overlap and k + 1 < len(batches):
+                nxt = encode(k + 1)
+            del states
+        cur.wait_stream(dec_s)
 
     def release(self):
         """Drops the captured token step (before the process group or the context goes)."""

@@ -88,3 +88,21 @@ def test_slot_count_invariance(madi, act16):
         got.append(d.tokens[:4, :7].clone())
         del d
     assert torch.equal(got[0], got[1]), f"{got[0].tolist()} vs {got[1].tolist()}"
+
+
+def test_transcribe_chunks_overlap(tr):
+    """transcribe_chunks (host mel in, host tokens out, batch k+1's encoder beside batch
+    k's decoder) gives the tokens transcribe() gives batch by batch, overlapped or not."""
+    import torch
+    from madi_b200 import pipeline
+    mel = pipeline.synthetic_mel(6, first=90)
+    mel_h = torch.from_numpy(mel).pin_memory()
+    got = []
+    for overlap in (True, False):
+        tok_h = torch.full((6, 6), -1, dtype=torch.int32).pin_memory()
+        tr.transcribe_chunks(mel_h, tok_h, overlap=overlap)
+        torch.cuda.synchronize()
+        got.append(tok_h.clone())
+    m = torch.from_numpy(mel).cuda()
+    want = torch.cat([tr.transcribe(m[0:4]).cpu(), tr.transcribe(m[4:6]).cpu()])
+    assert torch.equal(got[0], want) and torch.equal(got[1], want), f"{got[0].tolist()} vs {want.tolist()}"
