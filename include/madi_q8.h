@@ -197,11 +197,12 @@ int madi_q8_linear(const madi_q8w *w, const void *x, int x_dtype, int m,
 
 /* Decoder self-attention QKV projection with the KV-cache store fused
  * (gemv_q8_qkv, graph_helpers.metal:527-567) for m <= 16 token slots.
+ * x_dtype: MADI_F32, or MADI_F32_AS_F16 (x rounded to f16 on load, the batched decode).
  * w: stacked [3D][D]; x f32 [m][D].  For slot s: q_out[s][0..D) = q + qb;
  * kc[s*cache_stride + pos[s]*D + j] = k_j;  vc[...] = v_j + vb[j].
  * pos: device u32 [m] (read on the device, so a graph can replay it);
  * cache_stride: elements between slots' caches (ignored for m == 1). */
-int madi_q8_qkv(const madi_q8w *w, const float *x, int m,
+int madi_q8_qkv(const madi_q8w *w, const float *x, int x_dtype, int m,
                 const float *qb, const float *vb, float *q_out,
                 float *kc, float *vc, const uint32_t *pos, int64_t cache_stride,
                 void *stream);

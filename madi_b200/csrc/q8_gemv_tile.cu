@@ -539,11 +539,12 @@ cudaError_t launch_gemv_tile(const GemvArgs &a, bool x_f32, bool y_f32, int epi,
                              cudaStream_t st, bool pdl, bool x_r16) {
     TilePlan pl;
     int grid;
-    if (x_r16 && (!x_f32 || qkv)) return cudaErrorInvalidValue;
+    if (x_r16 && !x_f32) return cudaErrorInvalidValue;
     if (!make_plan(a.M, a.N, a.K, x_f32 && !x_r16, num_sms, &pl, &grid)) return cudaErrorInvalidValue;
     CUtensorMap tmq, tms;
     if (!make_tile_maps(a, pl.kslice, &tmq, &tms)) return cudaErrorNotSupported;
-    if (qkv) return launch_tile_one<float, float, kEpiNone, true>(a, tmq, tms, pl, grid, dev_err, st, pdl);
+    if (qkv) return x_r16 ? launch_tile_one<float, float, kEpiNone, true, true>(a, tmq, tms, pl, grid, dev_err, st, pdl)
+                          : launch_tile_one<float, float, kEpiNone, true>(a, tmq, tms, pl, grid, dev_err, st, pdl);
 #define MADI_TILE_CASE(XT, YT)                                                                                   \
     switch (epi) {                                                                                               \
         case kEpiNone: return launch_tile_one<XT, YT, kEpiNone, false>(a, tmq, tms, pl, grid, dev_err, st, pdl); \

@@ -203,7 +203,8 @@ int q8_linear_impl(const madi_q8w *w, const void *x, int x_dtype, int m, const v
 }
 
 int q8_qkv_impl(const madi_q8w *w, const float *x, int m, const float *qb, const float *vb, float *q_out, float *kc,
-                float *vc, const uint32_t *pos, long long cache_stride, cudaStream_t st, const char *who) {
+                float *vc, const uint32_t *pos, long long cache_stride, cudaStream_t st, const char *who,
+                bool x_r16 = false) {
     if (!S.ready) return fail(MADI_ENOINIT, "%s: madi_init has not succeeded", who);
     if (!w || !w->qs || !w->scales || !x || !qb || !vb || !q_out || !kc || !vc || !pos)
         return fail(MADI_EINVAL, "%s: null argument", who);
@@ -212,8 +213,8 @@ int q8_qkv_impl(const madi_q8w *w, const float *x, int m, const float *qb, const
     if (m <= 0 || m > kGemvMaxM) return fail(MADI_EINVAL, "%s: m=%d outside 1..%d", who, m, kGemvMaxM);
     if (!aligned(x, 16) || !aligned(w->qs, 16)) return fail(MADI_EINVAL, "%s: misaligned x or qs", who);
     const int ks = gemv_pick_ks(3 * D, D, S.num_sms);
-    const bool tile_path = aligned(w->scales, 16) && gemv_tile_ok(m, 3 * D, D, true, S.num_sms);
-    if (!tile_path && (m > 8 || gemv_smem_bytes(m, D, ks, true) > (size_t)S.max_smem_optin))
+    const bool tile_path = aligned(w->scales, 16) && gemv_tile_ok(m, 3 * D, D, !x_r16, S.num_sms);
+    if (!tile_path && (m > 8 || x_r16 || gemv_smem_bytes(m, D, ks, true) > (size_t)S.max_smem_optin))
         return fail(MADI_EINVAL, "%s: D=%d at m=%d does not fit the decode path", who, D, m);
     GemvArgs a{};
     a.qs = w->qs;
@@ -224,7 +225,8 @@ int q8_qkv_impl(const madi_q8w *w, const float *x, int m, const float *qb, const
     a.qb = qb; a.vb = vb; a.kc = kc; a.vc = vc; a.pos = pos;
     a.cache_stride = m > 1 ? cache_stride : 0;
     a.D = D;
-    cudaError_t e = tile_path ? launch_gemv_tile(a, true, true, MADI_EPI_NONE, true, S.num_sms, S.dev_err, st, S.pdl)
+    cudaError_t e = tile_path ? launch_gemv_tile(a, true, true, MADI_EPI_NONE, true, S.num_sms, S.dev_err, st, S.pdl,
+                                                 x_r16)
                               : launch_gemv(a, true, true, MADI_EPI_NONE, true, st, S.pdl);
     if (e == cudaErrorNotSupported) return fail(MADI_EUNSUPPORTED, "%s: cuTensorMapEncodeTiled unavailable", who);
     if (e != cudaSuccess) return cuda_fail(e, who);
@@ -795,9 +797,12 @@ int madi_q8_linear(const madi_q8w *w, const void *x, int x_dtype, int m, const v
                           "madi_q8_linear");
 }
 
-int madi_q8_qkv(const madi_q8w *w, const float *x, int m, const float *qb, const float *vb, float *q_out, float *kc,
-                float *vc, const uint32_t *pos, int64_t cache_stride, void *stream) {
-    return q8_qkv_impl(w, x, m, qb, vb, q_out, kc, vc, pos, (long long)cache_stride, pick_stream(stream), "madi_q8_qkv");
+int madi_q8_qkv(const madi_q8w *w, const float *x, int x_dtype, int m, const float *qb, const float *vb, float *q_out,
+                float *kc, float *vc, const uint32_t *pos, int64_t cache_stride, void *stream) {
+    if (x_dtype != MADI_F32 && x_dtype != MADI_F32_AS_F16)
+        return fail(MADI_EINVAL, "madi_q8_qkv: x_dtype %d (MADI_F32 or MADI_F32_AS_F16)", x_dtype);
+    return q8_qkv_impl(w, x, m, qb, vb, q_out, kc, vc, pos, (long long)cache_stride, pick_stream(stream), "madi_q8_qkv",
+                       x_dtype == MADI_F32_AS_F16);
 }
 
 int madi_q8_dequant_f16(const madi_q8w *w, uint16_t *out, void *stream) {

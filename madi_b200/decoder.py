@@ -107,10 +107,9 @@ class Decoder:
     """Device copy of the synthetic decoder plus the per-slot decode state."""
 
     def __init__(self, w: dict, slots: int, device="cuda", act16: bool = False):
-        """act16: the projections other than the fused QKV take their f32 activations
-        rounded to f16, as the reference's batched decode (decodeBlockBatched,
-        decoder.zig:337-341) converts them; False keeps the single-token GEMV family's
-        f32 activations."""
+        """act16: the projections take their f32 activations rounded to f16, as the
+        reference's batched decode (decodeBlockBatched, decoder.zig:337-341) converts
+        them; False keeps the single-token GEMV family's f32 activations."""
         if not 1 <= slots <= 16:
             raise ValueError("1..16 token slots")
         t = lambda a: (a.to(device) if isinstance(a, torch.Tensor) else
@@ -171,7 +170,7 @@ class Decoder:
         greedy.emb_pos_q8(self.emb, self.tokens, self.pos, self.pos_emb, out=self.x, **s)
         for l, L in enumerate(self.layers):
             q8.layer_norm(self.x, *L.aln, eps=EPS, out=self.xb, **s)
-            q8.qkv(L.qkv, self.xb, L.qb, L.vb, self.kc[l], self.vc[l], self.pos, q_out=self.q, **s)
+            q8.qkv(L.qkv, self.xb, L.qb, L.vb, self.kc[l], self.vc[l], self.pos, q_out=self.q, **r)
             attn.self_attn(self.q, self.kc[l], self.vc[l], self.pos, HEADS, out=self.ao, **s)
             q8.linear(L.o, self.ao, out=self.mo, **r)
             q8.bias_res_ln(self.x, self.mo, L.ob, *L.caln, eps=EPS, out=self.xb, **s)

@@ -89,15 +89,17 @@ def linear(w: Q8Weight, x: torch.Tensor, bias: Optional[torch.Tensor] = None, ep
 
 
 def qkv(w: Q8Weight, x: torch.Tensor, qb: torch.Tensor, vb: torch.Tensor, kc: torch.Tensor, vc: torch.Tensor,
-        pos: torch.Tensor, q_out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+        pos: torch.Tensor, q_out: Optional[torch.Tensor] = None, stream=None, x_round16: bool = False) -> torch.Tensor:
     """Fused decoder QKV (gemv_q8_qkv).  x f32 [m][D]; kc/vc f32 [m][max_tok][D]
-    (or [max_tok][D] for m == 1); pos u32/int32 [m] on the device."""
+    (or [max_tok][D] for m == 1); pos u32/int32 [m] on the device.  x_round16: x
+    rounded to f16 as it is loaded (the batched decode's activations)."""
     m, D = x.shape
     if q_out is None:
         q_out = torch.empty((m, D), dtype=torch.float32, device=x.device)
     stride = kc.stride(0) if kc.dim() == 3 else 0
     h = w.handle()
-    rc = _lib.load().madi_q8_qkv(ctypes.byref(h), x.data_ptr(), m, qb.data_ptr(), vb.data_ptr(), q_out.data_ptr(),
+    rc = _lib.load().madi_q8_qkv(ctypes.byref(h), x.data_ptr(), MADI_F32_AS_F16 if x_round16 else MADI_F32, m,
+                                 qb.data_ptr(), vb.data_ptr(), q_out.data_ptr(),
                                  kc.data_ptr(), vc.data_ptr(), pos.data_ptr(), stride, _stream(stream))
     _lib.check(rc, "madi_q8_qkv")
     return q_out

@@ -26,7 +26,7 @@ def _t(a, dev="cuda"):
 def _oracle_decode(oracle, w, ck, cv, dec, act16=False):
     D, HEADS, MAX_TOK = dec.D, dec.HEADS, dec.MAX_TOK
     f32 = lambda a: np.asarray(a, np.float32)
-    # act16: the activations of every projection but the fused QKV rounded to f16
+    # act16: the activations of every projection rounded to f16
     r = (lambda a: f32(a).astype(np.float16).astype(np.float32)) if act16 else f32
     S = ck[0].shape[0]
     tokens = np.zeros((S, MAX_TOK), np.uint32)
@@ -40,7 +40,7 @@ def _oracle_decode(oracle, w, ck, cv, dec, act16=False):
         x = np.stack([oracle.emb_q8(eq, es, tokens[b, pos[b]]) + w["pos_emb"][pos[b]] for b in range(S)])
         for l, L in enumerate(w["layers"]):
             _, xb = oracle.bias_res_ln_f32(x, None, None, *L["aln"], dec.EPS)
-            full = oracle.gemv_q8(f32(xb), *L["qkv"])
+            full = oracle.gemv_q8(r(xb), *L["qkv"])
             q = f32(full[:, :D] + L["qb"])
             for b in range(S):
                 kc[l][b, pos[b]] = f32(full[b, D:2 * D])
@@ -70,7 +70,7 @@ def _oracle_decode(oracle, w, ck, cv, dec, act16=False):
 @pytest.mark.parametrize("act16", [False, True])
 def test_greedy_decoder_end_to_end(madi, oracle, act16):
     """act16=False: the single-token GEMV family's f32 activations; True: the batched
-    decode's f16 activations (every projection but the fused QKV)."""
+    decode's f16 activations (every projection)."""
     import torch
     from madi_b200 import decoder as dec
     w = dec.host_weights(seed=1)

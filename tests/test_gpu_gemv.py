@@ -187,16 +187,20 @@ def test_qkv_kv_store(madi, oracle):
     for M, posb in [(5, np.array([0, 3, 447, 10, 200], np.uint32)),
                     (12, np.array([0, 3, 447, 10, 200, 1, 2, 5, 8, 13, 21, 34], np.uint32))]:
         _qkv_slots(oracle, qs, sc, qb, vb, D, T, M, posb)
+    # the batched decode's f16-rounded activations
+    _qkv_slots(oracle, qs, sc, qb, vb, D, T, 12, np.arange(12, dtype=np.uint32) * 7, round16=True)
 
 
-def _qkv_slots(oracle, qs, sc, qb, vb, D, T, M, posb):
+def _qkv_slots(oracle, qs, sc, qb, vb, D, T, M, posb, round16=False):
     import torch
     from madi_b200 import q8
     xb = synth.activations(M, D, 35 + M, np.float32)
     kcb = torch.full((M, T, D), float("nan"), device="cuda")
     vcb = torch.full((M, T, D), float("nan"), device="cuda")
     W = q8.Q8Weight(_t(qs), _t(sc))
-    qo = q8.qkv(W, _t(xb), _t(qb), _t(vb), kcb, vcb, _t(posb.astype(np.int32)))
+    qo = q8.qkv(W, _t(xb), _t(qb), _t(vb), kcb, vcb, _t(posb.astype(np.int32)), x_round16=round16)
+    if round16:
+        xb = xb.astype(np.float16).astype(np.float32)
     torch.cuda.synchronize()
     for s in range(M):
         q_ex, k_ex, v_ex = oracle.gemv_q8_qkv(xb[s:s + 1], qs, sc, qb, vb, posb[s:s + 1], T)
