@@ -63,6 +63,8 @@ def parse():
                     help="decode activations (config 2: fp16; the reference decoder's own GEMVs take f32)")
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--e2e-chunks", type=int, default=4,
+                    help="e2e leg: row chunks per step pipelined across the copy and compute streams")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-encoder-layer", action="store_true")
     ap.add_argument("--no-long-audio", action="store_true")
@@ -71,6 +73,14 @@ def parse():
     ap.add_argument("--no-overlap", action="store_true",
                     help="long-audio leg: run each batch's encoder and decoder back to back on one stream")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    # --case KIND: one op of one shape on cuda:0 (see run_case), instead of the benchmark
+    ap.add_argument("--case", choices=["gemv", "gemm", "cross", "self", "flash", "decoder"])
+    ap.add_argument("--m", type=int, default=8)
+    ap.add_argument("--n", type=int, default=1280)
+    ap.add_argument("--k", type=int, default=1280)
+    ap.add_argument("--x", choices=["f16", "f32"], default="f16")
+    ap.add_argument("--epi", choices=["none", "bias", "gelu", "res"], default="none")
+    ap.add_argument("--iters", type=int, default=6)
     return ap.parse_args()
 
 
@@ -179,56 +189,160 @@ def host_threads() -> int:
         return os.cpu_count() or 1
 
 
-def cpu_ffn_sample(rows, seconds, nthreads=None):
+class CpuFfn:
     """The reference's CPU computation of the FFN pair (f32 dequant + accumulate,
-    oracle/q8_oracle.c madi_orc_linear_f32_baseline) on `rows` frames, repeated
-    for about `seconds`.  Returns (TFLOP/s, threads, passes)."""
+    test_q8gemm.zig:59-69, with the m4_gemm epilogues) on a `rows`-frame sample of the
+    step's X, through oracle/cpu_baseline.c built for this host (-march=native).
+    Everything that is not the op -- building the library, synthesising weights
+    and activations, the once-per-run f32 dequant of the weights -- happens here,
+    before any timing."""
+
+    def __init__(self, rows, nthreads):
+        import numpy as np
+        from madi_b200 import synth
+        from oracle import cpu_baseline as cb
+        self.cb, self.rows, self.nt = cb, rows, nthreads
+        self.w = synth.ffn_weights(0)
+        self.x = synth.activations(rows, D, 1000)
+        self.wdq1 = cb.dequant_f32(self.w["fc1_qs"], self.w["fc1_scales"], nthreads)
+        self.wdq2 = cb.dequant_f32(self.w["fc2_qs"], self.w["fc2_scales"], nthreads)
+        self.h = np.empty((rows, F), np.float16)
+        self.y = np.empty((rows, D), np.float16)
+        self.flops = 2.0 * rows * F * D * 2
+        self.one_pass()                                  # warm-up: thread team, page faults
+
+    def one_pass(self):
+        cb, w = self.cb, self.w
+        cb.linear_tiled(self.x, self.wdq1, w["fc1_bias"], cb.EPI_BIAS_GELU, nthreads=self.nt, out=self.h)
+        cb.linear_tiled(self.h, self.wdq2, w["fc2_bias"], cb.EPI_BIAS_RES, residual=self.x, nthreads=self.nt,
+                        out=self.y)
+
+    def timed(self, seconds):
+        """Repeats one_pass for about `seconds`; returns (TFLOP/s, passes)."""
+        t0 = time.perf_counter()
+        n = 0
+        while True:
+            self.one_pass()
+            n += 1
+            el = time.perf_counter() - t0
+            if el >= seconds:
+                break
+        return self.flops * n / el / 1e12, n
+
+    def single_thread_faithful(self, rows, seconds):
+        """The reference's loop exactly as written (one thread, scalar, dequant inline)
+        on the first `rows` frames; TFLOP/s."""
+        cb, w = self.cb, self.w
+        x = self.x[:rows]
+        t0 = time.perf_counter()
+        n = 0
+        while True:
+            h = cb.linear_faithful(x, w["fc1_qs"], w["fc1_scales"], w["fc1_bias"], cb.EPI_BIAS_GELU)
+            cb.linear_faithful(h, w["fc2_qs"], w["fc2_scales"], w["fc2_bias"], cb.EPI_BIAS_RES, residual=x)
+            n += 1
+            el = time.perf_counter() - t0
+            if el >= seconds:
+                break
+        return 2.0 * rows * F * D * 2 * n / el / 1e12
+
+
+def cpu_decode_step(thread_counts, seconds, m=8):
+    """CPU baseline of BASELINE config 2: one decoder token step's Q8 projections
+    (4 layers x {qkv, o, cq, co, fc1, fc2} + the 51866-row head) for m token rows,
+    f32 activations, int8 weights dequantised in registers (oracle/cpu_baseline.c
+    madi_cpu_gemv_q8, the gemv_q8 family's arithmetic).  GB/s over the same
+    algorithmic bytes as the GPU decode leg (weights + scales + x + y + bias).
+    Returns ([GB/s per thread count], bytes per step)."""
     import numpy as np
     from madi_b200 import synth
-    from oracle import oracle
-    oracle.build()
-    w = synth.ffn_weights(0)
-    x = synth.activations(rows, D, 1)
-    nt = nthreads or host_threads()
-    flops = 2.0 * rows * F * D * 2
-    t0 = time.perf_counter()
-    n = 0
-    while True:
-        h = oracle.linear_f32_baseline(x, w["fc1_qs"], w["fc1_scales"], w["fc1_bias"], oracle.EPI_BIAS_GELU,
-                                       nthreads=nt)
-        oracle.linear_f32_baseline(h, w["fc2_qs"], w["fc2_scales"], w["fc2_bias"], oracle.EPI_BIAS_RES,
-                                   residual=x, nthreads=nt)
-        n += 1
-        el = time.perf_counter() - t0
-        if el >= seconds:
-            break
-    return flops * n / el / 1e12, nt, n
+    from oracle import cpu_baseline as cb
+    g = np.random.default_rng(12345)
+    shapes = [(nm, n, k) for nm, n, k in synth.decoder_shapes()] * 4 + [("head", V, D)]
+    ws = [(nm, g.integers(-127, 128, (n, k), dtype=np.int8),
+           g.uniform(1e-4, 2e-3, (n, k // 32)).astype(np.float16), (g.standard_normal(n) * 0.02).astype(np.float32))
+          for nm, n, k in shapes]
+    x = g.standard_normal((m, D)).astype(np.float32)
+    xf = g.standard_normal((m, F)).astype(np.float32)
+    ys = {nm: np.zeros((m, n), np.float32) for nm, n, _ in shapes}
+    epis = {"cq": cb.EPI_BIAS, "fc1": cb.EPI_BIAS_GELU, "fc2": cb.EPI_BIAS_RES}
+    nbytes = 0
+    for nm, qs, sc, b in ws:
+        n, k = qs.shape
+        nbytes += n * k + n * k // 16 + m * k * 4 + m * n * 4 + (n * 4 if nm in epis else 0) + \
+            (m * n * 4 if nm == "fc2" else 0)
+
+    def step(nthreads):
+        for nm, qs, sc, b in ws:
+            cb.gemv_q8(xf if nm == "fc2" else x, qs, sc, bias=b, epi=epis.get(nm, cb.EPI_NONE), y=ys[nm],
+                       nthreads=nthreads)
+    out = []
+    for nt in thread_counts:
+        step(nt)
+        t0 = time.perf_counter()
+        n = 0
+        while True:
+            step(nt)
+            n += 1
+            el = time.perf_counter() - t0
+            if el >= seconds:
+                break
+        out.append(nbytes * n / el / 1e9)
+    return out, nbytes
+
+
+def cpu_baseline_leg(args, rows=256):
+    """All three CPU figures: the FFN pair on all host threads (the value), the
+    reference's loop on one thread, and the decode step on all threads and one."""
+    from oracle import cpu_baseline as cb
+    nt = host_threads()
+    ffn = CpuFfn(rows, nt)
+    tf, n = ffn.timed(args.cpu_seconds)
+    st_rows = 16
+    st = ffn.single_thread_faithful(st_rows, 2.0)
+    (dec_all, dec_one), dec_bytes = cpu_decode_step((nt, 1), 2.0)
+    return {"value": tf, "unit": "TFLOP/s", "cores": nt, "kind": "port",
+            "sample": f"FFN pair on {rows} of {args.batch * SEQ} frames, {n} passes (~{args.cpu_seconds:.0f} s), "
+                      f"f32 dequant+accumulate as test_q8gemm.zig:59-69, weights dequantised once per run, "
+                      f"register-tiled, all {nt} threads",
+            "cpu_model": cb.cpu_model(), "build": "gcc -O3 -march=native -fopenmp (built on this host)",
+            "single_thread": {"value": st, "unit": "TFLOP/s", "cores": 1,
+                              "sample": f"FFN pair on {st_rows} frames, the reference's loop as written "
+                                        f"(scalar f32, k ascending, dequant inline)"},
+            "decode": {"unit": "GB/s", "all_threads": dec_all, "single_thread": dec_one, "bytes_per_step": dec_bytes,
+                       "sample": "config 2 token step at M=8, f32 activations: 4 layers x {qkv,o,cq,co,fc1,fc2} + "
+                                 "vocab head, int8 weights dequantised in registers (gemv_q8 arithmetic)"}}
 
 
 def run_reference(args, world, rank):
+    """The reference's CPU computation of the benchmarked op (oracle/cpu_baseline.c:
+    test_q8gemm.zig:59-69's f32 dequant + accumulate with the m4_gemm epilogues), on
+    the same 256-frame sample of the config-1 step as the GPU arm's cpu_baseline,
+    with every host thread.  Weights, activations and the once-per-run dequant are
+    prepared before the warm-up; each step is one FFN pair over the sample."""
     if rank != 0:
         return
-    from oracle import oracle
-    oracle.build()
-    rows = 96                      # bounded sample of the 24000-frame step
+    rows = 256
     nt = host_threads()
+    ffn = CpuFfn(rows, nt)
+    for _ in range(args.warmup):
+        ffn.one_pass()
     per = []
-    for i in range(args.warmup + args.steps):
+    for _ in range(args.steps):
         t0 = time.perf_counter()
-        tf, _, _ = cpu_ffn_sample(rows, 0.0, nthreads=nt)
-        if i >= args.warmup:
-            per.append(time.perf_counter() - t0)
-    flops = 2.0 * rows * F * D * 2
-    value = flops * len(per) / sum(per) / 1e12
+        ffn.one_pass()
+        per.append(time.perf_counter() - t0)
+    value = ffn.flops * len(per) / sum(per) / 1e12
     ms = 1e3 * sum(per) / len(per)
-    sample = f"FFN pair (fc1+GELU, fc2+residual) on {rows} of {args.batch * SEQ} frames per step"
+    sample = (f"FFN pair (fc1+GELU, fc2+residual) on {rows} of {args.batch * SEQ} frames per step, weights "
+              f"dequantised to f32 once per run, register-tiled, all {nt} threads")
+    from oracle import cpu_baseline as cb
     line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "impl": "reference", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": f"config1 encoder FFN pair, B={args.batch} chunks (M={args.batch * SEQ})",
                        "cpu_sample_rows": rows},
-            "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": nt, "kind": "port",
-                             "sample": sample},
+            "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": nt, "kind": "port", "sample": sample,
+                             "cpu_model": cb.cpu_model()},
             "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -345,33 +459,11 @@ def main_madi(args, world, rank, local):
         torch.cuda.empty_cache()
 
     # ---------------- e2e through the public API with host buffers
+    del H, Y
+    torch.cuda.empty_cache()
     e2e = None
     if not args.no_e2e:
-        Xh = torch.empty((M, D), dtype=torch.float16, pin_memory=True)
-        Xh.copy_(X.cpu())
-        Yh = torch.empty((M, D), dtype=torch.float16, pin_memory=True)
-        Ke = max(3, min(K, 20))
-        for _ in range(2):
-            X.copy_(Xh, non_blocking=True)
-        torch.cuda.synchronize()
-        barrier(world)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with torch.cuda.stream(stream):
-            e0.record(stream)
-            for _ in range(Ke):
-                X.copy_(Xh, non_blocking=True)
-                q8.linear(W1, X, bias=b1, epi=q8.EPI_BIAS_GELU, out=H, stream=stream)
-                q8.linear(W2, H, bias=b2, epi=q8.EPI_BIAS_RES, residual=X, out=Y, stream=stream)
-                Yh.copy_(Y, non_blocking=True)
-            e1.record(stream)
-        torch.cuda.synchronize()
-        ms_e2e = max_over_ranks(world, e0.elapsed_time(e1) / Ke)
-        e2e = {"value": 2 * gemm_flops * world / (ms_e2e / 1e3) / 1e12, "unit": "TFLOP/s",
-               "h2d_bytes_per_step": M * D * 2, "d2h_bytes_per_step": M * D * 2, "ms_per_step": ms_e2e}
-        del Xh, Yh
-
-    del H
-    torch.cuda.empty_cache()
+        e2e = e2e_leg(args, world, dev, X, W1, W2, b1, b2, gemm_flops)
 
     # ---------------- decode leg (config 2)
     decode = None
@@ -386,11 +478,7 @@ def main_madi(args, world, rank, local):
     # ---------------- CPU baseline (rank 0, N=1 only)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        rows = 256
-        tf, nt, n = cpu_ffn_sample(rows, args.cpu_seconds)
-        cpu = {"value": tf, "unit": "TFLOP/s", "cores": nt, "kind": "port",
-               "sample": f"FFN pair on {rows} of {M} frames, {n} passes (~{args.cpu_seconds:.0f} s), "
-                         f"f32 dequant+accumulate as test_q8gemm.zig:59-69"}
+        cpu = cpu_baseline_leg(args)
 
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": K,
@@ -407,6 +495,82 @@ def main_madi(args, world, rank, local):
                 "encoder_layer": enc_layer, "long_audio": long_audio,
                 "clocks": clocks, "gpu_launches": 2 * K}
         print(json.dumps(line), flush=True)
+
+
+def e2e_leg(args, world, dev, X, W1, W2, b1, b2, gemm_flops):
+    """`e2e`: the config-1 step end to end through the public API (madi_b200.q8.linear)
+    from pinned HOST X to pinned HOST Y, the copies inside the timed region.  Each
+    step's M rows are cut into `--e2e-chunks` row chunks and pipelined over three
+    streams -- H2D of chunk i+1, the two GEMMs of chunk i and D2H of chunk i-1 run at
+    once (one cudaMemcpyAsync per chunk and direction) -- with two sets of device
+    buffers alternating between steps so that step s+1's copies may start while
+    step s finishes.  Events order every reuse of a device buffer."""
+    import torch
+    from madi_b200 import q8
+    M = X.shape[0]
+    nch = max(1, min(args.e2e_chunks, M // 192))
+    bounds = [(M * c // nch, M * (c + 1) // nch) for c in range(nch)]
+    Xh = torch.empty((M, D), dtype=torch.float16, pin_memory=True)
+    Xh.copy_(X.cpu())
+    Yh = torch.empty((M, D), dtype=torch.float16, pin_memory=True)
+    sets = [dict(X=torch.empty((M, D), dtype=torch.float16, device=dev),
+                 H=torch.empty((M, F), dtype=torch.float16, device=dev),
+                 Y=torch.empty((M, D), dtype=torch.float16, device=dev)) for _ in range(2)]
+    s_in = torch.cuda.Stream(device=dev)
+    s_mm = torch.cuda.Stream(device=dev)
+    s_out = torch.cuda.Stream(device=dev)
+    ev = lambda: torch.cuda.Event()
+    comp_done = [[None] * nch for _ in range(2)]
+    out_done = [[None] * nch for _ in range(2)]
+
+    def step(si):
+        p = si % 2
+        B = sets[p]
+        for c, (r0, r1) in enumerate(bounds):
+            with torch.cuda.stream(s_in):
+                if comp_done[p][c] is not None:
+                    s_in.wait_event(comp_done[p][c])          # X rows free: step si-2 consumed them
+                B["X"][r0:r1].copy_(Xh[r0:r1], non_blocking=True)
+                e_in = ev()
+                e_in.record(s_in)
+            with torch.cuda.stream(s_mm):
+                s_mm.wait_event(e_in)
+                if out_done[p][c] is not None:
+                    s_mm.wait_event(out_done[p][c])           # Y rows free: step si-2 copied them out
+                Xc = B["X"][r0:r1]
+                q8.linear(W1, Xc, bias=b1, epi=q8.EPI_BIAS_GELU, out=B["H"][r0:r1], stream=s_mm)
+                q8.linear(W2, B["H"][r0:r1], bias=b2, epi=q8.EPI_BIAS_RES, residual=Xc, out=B["Y"][r0:r1],
+                          stream=s_mm)
+                comp_done[p][c] = ev()
+                comp_done[p][c].record(s_mm)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(comp_done[p][c])
+                Yh[r0:r1].copy_(B["Y"][r0:r1], non_blocking=True)
+                out_done[p][c] = ev()
+                out_done[p][c].record(s_out)
+
+    for si in range(3):
+        step(si)
+    torch.cuda.synchronize()
+    barrier(world)
+    Ke = max(3, min(args.steps, 20))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    cur = torch.cuda.current_stream(dev)
+    e0.record(cur)
+    for s_ in (s_in, s_mm, s_out):
+        s_.wait_event(e0)
+    for si in range(Ke):
+        step(si)
+    e1.record(s_out)
+    torch.cuda.synchronize()
+    ms_e2e = max_over_ranks(world, e0.elapsed_time(e1) / Ke)
+    ok = torch.equal(Yh[:8].to(dev), sets[(Ke - 1) % 2]["Y"][:8])
+    del sets, Xh, Yh
+    torch.cuda.empty_cache()
+    return {"value": 2 * gemm_flops * world / (ms_e2e / 1e3) / 1e12, "unit": "TFLOP/s",
+            "h2d_bytes_per_step": M * D * 2, "d2h_bytes_per_step": M * D * 2, "ms_per_step": ms_e2e,
+            "pipeline": f"{nch} row chunks per step over H2D / compute / D2H streams, two device buffer sets",
+            "host_copy_matches": bool(ok)}
 
 
 def long_audio_leg(args, world, rank, dev):
@@ -791,8 +955,174 @@ def decode_leg(args, world, rank, dev, stream, peaks):
                   "distinct weight copies per graph"}
 
 
+# ----------------------------------------------------------------------------- single-op cases (--case)
+CASE_EPIS = {"none": 0, "bias": 1, "gelu": 2, "res": 3}      # MADI_EPI_*
+
+
+def run_case(a):
+    """One library op of a given shape a few times on cuda:0 (--case), a fixed
+    workload to time or to put under a profiler (ncu -k regex:<kernel> -s <skip> -c
+    <count> ...):
+
+        python bench.py --case gemv --n 51866 --k 1280 --m 8 --x f16 --iters 6
+        python bench.py --case gemm --m 24000 --n 5120 --k 1280 --epi gelu --iters 3
+        python bench.py --case cross --m 8 --n 1500 --k 1280 --iters 6    (slots, keys, kv_dim)
+        python bench.py --case self --m 8 --n 448 --k 1280 --iters 6      (slots, cache rows, kv_dim)
+        python bench.py --case flash --m 8 --n 1500 --k 1280 --iters 6    (chunks, seq, heads*64)
+        python bench.py --case decoder --m 15 --n 112 --k 1280 --iters 6  (slots, tokens decoded first, d)
+
+    Inputs are seeded random tensors of the given shape (int8 weights in [-127, 127],
+    f16 scales in [1e-4, 2.1e-3], N(0,1) activations); prints the mean device time
+    per call from CUDA events, between an L2-evicting read of a 256 MB buffer and
+    each call."""
+    import torch
+    from madi_b200 import init, q8
+    a.kind = a.case
+    init(0)
+    dev = torch.device("cuda:0")
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234)
+    if a.kind in ("cross", "self"):
+        return attention_case(a, dev, g)
+    if a.kind == "flash":
+        return flash_case(a, dev, g)
+    if a.kind == "decoder":
+        return decoder_case(a, dev)
+    W = q8.Q8Weight(torch.randint(-127, 128, (a.n, a.k), dtype=torch.int8, device=dev, generator=g),
+                    (torch.rand((a.n, a.k // 32), device=dev, generator=g) * 2e-3 + 1e-4).half())
+    xdt = torch.float32 if a.x == "f32" else torch.float16
+    if a.kind == "gemm":
+        xdt = torch.float16
+    x = torch.randn((a.m, a.k), device=dev, generator=g).to(xdt)
+    ydt = xdt if a.kind == "gemm" else torch.float32
+    bias = torch.randn(a.n, device=dev, generator=g) * 0.02
+    epi = CASE_EPIS[a.epi]
+    y = torch.zeros((a.m, a.n), dtype=ydt, device=dev)
+    flush = torch.zeros(64 << 20, dtype=torch.int32, device=dev)
+    def call():
+        q8.linear(W, x, bias=bias if epi != q8.EPI_NONE else None, epi=epi,
+                  residual=y if epi == q8.EPI_BIAS_RES else None, out=y)
+
+    call()                      # first call: module load and one-time attributes, untimed
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(a.iters):
+        flush.sum()             # read-flush of L2 (64 MB x 4 B) between calls
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        call()
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1) * 1e3)
+    print(f"{a.kind} M={a.m} N={a.n} K={a.k} x={a.x} epi={a.epi}: mean {sum(ts) / len(ts):.2f} us, "
+          f"min {min(ts):.2f} us over {len(ts)} calls (after one untimed call)")
+
+
+def attention_case(a, dev, g):
+    """Decoder attention: --m slots, --n keys (cross) or cache rows (self), --k kv_dim
+    (heads = kv_dim / 64); f16 K/V for cross, f32 for self, as the reference keeps them."""
+    import torch
+    from madi_b200 import attn
+    heads = a.k // 64
+    kv_dt = torch.float16 if a.kind == "cross" else torch.float32
+    kc = torch.randn((a.m, a.n, a.k), device=dev, generator=g).to(kv_dt)
+    vc = torch.randn((a.m, a.n, a.k), device=dev, generator=g).to(kv_dt)
+    q = torch.randn((a.m, a.k), device=dev, generator=g) * 0.5
+    out = torch.empty_like(q)
+    pos = torch.full((a.m,), a.n - 1, dtype=torch.int32, device=dev)
+
+    def call():
+        if a.kind == "cross":
+            attn.cross_attn(q, kc, vc, heads, out=out)
+        else:
+            attn.self_attn(q, kc, vc, pos, heads, out=out)
+
+    call()
+    torch.cuda.synchronize()
+    flush = torch.zeros(64 << 20, dtype=torch.int32, device=dev)
+    ts = []
+    for _ in range(a.iters):
+        flush.sum()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        call()
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1) * 1e3)
+    print(f"{a.kind} attention slots={a.m} keys={a.n} kv_dim={a.k}: mean {sum(ts) / len(ts):.2f} us, "
+          f"min {min(ts):.2f} us over {len(ts)} calls (after one untimed call)")
+
+
+def flash_case(a, dev, g):
+    """Encoder self-attention: --m chunks, --n sequence length, --k heads * 64; q / k / v
+    as column slices of one packed [chunks * seq][3 * k] f16 QKV buffer."""
+    import torch
+    from madi_b200 import attn
+    heads = a.k // 64
+    qkv = torch.randn((a.m * a.n, 3 * a.k), device=dev, generator=g).half()
+    q, k, v = qkv[:, :a.k], qkv[:, a.k:2 * a.k], qkv[:, 2 * a.k:]
+    out = torch.empty((a.m * a.n, a.k), dtype=torch.float16, device=dev)
+    attn.flash_attn_enc(q, k, v, heads, a.n, out=out)
+    torch.cuda.synchronize()
+    flops = 4.0 * a.n * a.n * 64 * heads * a.m
+    ts = []
+    for _ in range(a.iters):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        attn.flash_attn_enc(q, k, v, heads, a.n, out=out)
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1) * 1e3)
+    print(f"flash attention chunks={a.m} seq={a.n} heads={heads}: mean {sum(ts) / len(ts):.2f} us, min {min(ts):.2f} us, "
+          f"{flops / min(ts) / 1e6:.1f} TFLOP/s at the min over {len(ts)} calls (after one untimed call)")
+
+
+def decoder_case(a, dev):
+    """The synthetic 4-layer greedy decoder (madi_b200/decoder.py) with --m slots: one
+    token step captured as a CUDA graph, replayed --n times untimed (the positions
+    reach n), then --iters timed replays.  --x f16 (the default) with more than one
+    slot: the batched decode's f16-rounded activations; --x f32: f32 activations."""
+    import torch
+    from madi_b200 import decoder as dec
+    model = dec.Decoder(dec.host_weights(seed=1), a.m, device=dev, act16=a.x == "f16" and a.m > 1)
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    model.set_encoder(torch.randn((a.m, dec.ENC, dec.D), device=dev, generator=g).half())
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    model.reset()
+    with torch.cuda.stream(s):
+        model.step()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    model.reset()
+    torch.cuda.synchronize()
+    with torch.cuda.graph(graph):
+        model.step()
+    model.reset()
+    for _ in range(a.n):
+        graph.replay()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(a.iters):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1) * 1e3)
+    del graph
+    print(f"decoder slots={a.m} from position {a.n}: mean {sum(ts) / len(ts):.2f} us, min {min(ts):.2f} us per token "
+          f"step over {len(ts)} replays")
+
+
+
 def main():
     args = parse()
+    if args.case:
+        run_case(args)
+        return 0
     if args.impl == "reference":
         world = int(os.environ.get("WORLD_SIZE", "1"))
         rank = int(os.environ.get("RANK", "0"))

@@ -196,16 +196,23 @@ int madi_q8_linear(const madi_q8w *w, const void *x, int x_dtype, int m,
                    const void *residual, void *y, int y_dtype, void *stream);
 
 /* Decoder self-attention QKV projection with the KV-cache store fused
- * (gemv_q8_qkv, graph_helpers.metal:527-567) for m <= 16 token slots.
- * x_dtype: MADI_F32, or MADI_F32_AS_F16 (x rounded to f16 on load, the batched decode).
+ * (gemv_q8_qkv, graph_helpers.metal:527-567) for m <= 16 token slots, f32 x.
  * w: stacked [3D][D]; x f32 [m][D].  For slot s: q_out[s][0..D) = q + qb;
  * kc[s*cache_stride + pos[s]*D + j] = k_j;  vc[...] = v_j + vb[j].
  * pos: device u32 [m] (read on the device, so a graph can replay it);
  * cache_stride: elements between slots' caches (ignored for m == 1). */
-int madi_q8_qkv(const madi_q8w *w, const float *x, int x_dtype, int m,
+int madi_q8_qkv(const madi_q8w *w, const float *x, int m,
                 const float *qb, const float *vb, float *q_out,
                 float *kc, float *vc, const uint32_t *pos, int64_t cache_stride,
                 void *stream);
+
+/* madi_q8_qkv with an activation type (same reference kernel): x_dtype MADI_F32, or
+ * MADI_F32_AS_F16 -- x f32 rounded to f16 as it is loaded, as the reference's batched
+ * decode (decodeBlockBatched, decoder.zig:337-341) rounds its activations. */
+int madi_q8_qkv_ex(const madi_q8w *w, const float *x, int x_dtype, int m,
+                   const float *qb, const float *vb, float *q_out,
+                   float *kc, float *vc, const uint32_t *pos, int64_t cache_stride,
+                   void *stream);
 
 /* dequant_q8_f16 (q8_gemm.metal:12-27): out f16 [K][N] = half(q*s), transposed. */
 int madi_q8_dequant_f16(const madi_q8w *w, uint16_t *out, void *stream);
@@ -301,10 +308,12 @@ int madi_cross_attn(const float *q, const void *kc, const void *vc, int kv_dtype
  * q f32 [heads*64]; kc, vc f16 [seqlen][kv_dim]; out f32 [heads*64]; scores f32
  * [heads][seqlen] (normalised) or NULL; at most 256 keys per split.  Limit: heads x
  * nsplit <= 2048 (the array holds 2048 x 66 floats, 528 KB, on every GPU that loads
- * the library, until the process exits); larger requests return MADI_EINVAL.  The
- * first call on a device looks up the array's device address; make that first call
- * before any stream capture.  Every call shares the one array: calls whose kernels
- * overlap on the GPU (different streams, or other threads) race on it. */
+ * the library, until the process exits); larger requests return MADI_EINVAL, and so
+ * does a call while another device than the one madi_init bound is current.  The
+ * first call on a device (and after its context was re-created) looks up the
+ * array's device address; make that first call before any stream capture.  Every
+ * call shares the one array: calls whose kernels overlap on the GPU (different
+ * streams, or other threads) race on it. */
 int madi_cross_attn_split_static(const float *q, const uint16_t *kc, const uint16_t *vc, int seqlen,
                                  int heads, int kv_heads, int kv_dim, int nsplit, float *out,
                                  float *scores, void *stream);

@@ -53,7 +53,8 @@ SIGNATURES = {
     "madi_dump_profile": ([ctypes.c_char_p], None),
     "madi_num_sms": ([], I),
     "madi_q8_linear": ([ctypes.POINTER(madi_q8w), P, I, I, P, I, I, P, P, I, P], I),
-    "madi_q8_qkv": ([ctypes.POINTER(madi_q8w), P, I, I, P, P, P, P, P, P, ctypes.c_int64, P], I),
+    "madi_q8_qkv": ([ctypes.POINTER(madi_q8w), P, I, P, P, P, P, P, P, ctypes.c_int64, P], I),
+    "madi_q8_qkv_ex": ([ctypes.POINTER(madi_q8w), P, I, I, P, P, P, P, P, P, ctypes.c_int64, P], I),
     "madi_q8_dequant_f16": ([ctypes.POINTER(madi_q8w), P, P], I),
     "madi_q8_quantize_f16": ([P, I, I, P, P, P], I),
     "madi_bias_res_ln_f16": ([P, P, P, P, P, P, I, I, ctypes.c_float, P], I),

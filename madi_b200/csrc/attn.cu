@@ -584,13 +584,13 @@ cudaError_t launch_attn_t(const void *kc, const void *vc, float *out, const floa
         return cudaErrorNotSupported;
     auto fn = attn_kernel<KV, kScores>;
     const size_t smem = 128 + 2 * (size_t)csz * kHd * sizeof(KV);
-    static bool attr = false;
-    if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)(128 + 2 * kAttnMaxChunk * kHd * sizeof(KV)));
-        if (e != cudaSuccess) return e;
-        attr = true;
-    }
+    static std::once_flag once;
+    static cudaError_t once_status;
+    if (cudaError_t e = run_once(once, once_status, [&] {
+            return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)(128 + 2 * kAttnMaxChunk * kHd * sizeof(KV)));
+        }))
+        return e;
     return launch_k(fn, dim3(ns, nh, slots), kThr, smem, st, ns, tmK, tmV, out, q, sc, pos, rows, nkv, nh, ns, csz,
                     dev_err);
 }
@@ -607,19 +607,23 @@ cudaError_t launch_attn_stream_g(const void *kc, const void *vc, float *out, con
     const size_t stage_bytes = 2 * (size_t)kR * kHd * G * sizeof(KV);
     auto fn = attn_stream_kernel<KV, G>;
     static int occ[kMaxStages + 1] = {0};                 // resident CTAs per SM by ring depth
-    if (!occ[2]) {
-        cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)std::min(kSmemMax, 128 + kMaxStages * stage_bytes));
-        if (e != cudaSuccess) return e;
-        for (int sg = 2; sg <= kMaxStages; ++sg) {
-            int nb = 0;
-            if (128 + sg * stage_bytes <= kSmemMax) {
-                e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, fn, kThrS, 128 + sg * stage_bytes);
-                if (e != cudaSuccess) return e;
+    static std::once_flag once;
+    static cudaError_t once_status;
+    if (cudaError_t e0 = run_once(once, once_status, [&] {
+            cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int)std::min(kSmemMax, 128 + kMaxStages * stage_bytes));
+            if (e != cudaSuccess) return e;
+            for (int sg = 2; sg <= kMaxStages; ++sg) {
+                int nb = 0;
+                if (128 + sg * stage_bytes <= kSmemMax) {
+                    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, fn, kThrS, 128 + sg * stage_bytes);
+                    if (e != cudaSuccess) return e;
+                }
+                occ[sg] = nb;
             }
-            occ[sg] = nb;
-        }
-    }
+            return cudaSuccess;
+        }))
+        return e0;
     const int sms = num_sms();
     const long pairs = (long)slots * (nh / G);
     int ns = 1, stages = 2;
@@ -700,26 +704,62 @@ cudaError_t launch_cross_attn_reduce(float *out, const float *part, int nsplit, 
 // clearing between calls.
 static __device__ __align__(256) float g_split_part[kSplitStaticMax * (2 + kHd)];
 
+// The array's address is looked up once per device and context: the entry for a
+// device is refreshed when the current context is another one (the context was
+// destroyed and created again, e.g. after cudaDeviceReset).
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_split_mu;
+struct SplitAddr {
+    CUcontext ctx = nullptr;
+    float *addr = nullptr;
+} g_split_addr[kMaxDevices];
+
+CUcontext current_context() {
+    typedef CUresult (*PFN_ctx)(CUcontext *);
+    static PFN_ctx fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &ptr, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_ctx>(ptr);
+    });
+    CUcontext c = nullptr;
+    if (!fn || fn(&c) != CUDA_SUCCESS) return nullptr;
+    return c;
+}
+}  // namespace
+
+void forget_split_static_addresses() {
+    std::lock_guard<std::mutex> lk(g_split_mu);
+    for (auto &a : g_split_addr) a = SplitAddr();
+}
+
 cudaError_t launch_cross_attn_split_static(float *out, const float *q, const void *kc, const void *vc, float *sc,
-                                           int seqlen, int kvd, int nkv, int nh, int nsplit, cudaStream_t st) {
-    constexpr int kMaxDevices = 64;
-    static std::mutex mu;
-    static float *addr[kMaxDevices] = {};
+                                           int seqlen, int kvd, int nkv, int nh, int nsplit, int device,
+                                           cudaStream_t st) {
     if ((long)nh * nsplit > kSplitStaticMax) return cudaErrorInvalidValue;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    if (dev != device || dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
     float *part = nullptr;
     {
-        std::lock_guard<std::mutex> lk(mu);
-        if (!addr[dev]) {
+        // the first call on this device (and context) makes the context current
+        // through cudaGetSymbolAddress; the context is read after it
+        std::lock_guard<std::mutex> lk(g_split_mu);
+        SplitAddr &a = g_split_addr[dev];
+        CUcontext ctx = current_context();
+        if (!a.addr || !ctx || ctx != a.ctx) {
             void *p = nullptr;
             e = cudaGetSymbolAddress(&p, g_split_part);
             if (e != cudaSuccess) return e;
-            addr[dev] = static_cast<float *>(p);
+            a.addr = static_cast<float *>(p);
+            a.ctx = current_context();
         }
-        part = addr[dev];
+        part = a.addr;
     }
     e = launch_cross_attn_part(part, q, kc, vc, true, sc, sc != nullptr, seqlen, kvd, nkv, nh, nsplit, st);
     if (e != cudaSuccess) return e;

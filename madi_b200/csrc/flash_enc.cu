@@ -310,12 +310,12 @@ cudaError_t launch_flash_enc(const __half *q, const __half *k, const __half *v, 
     if (!fa_map(&tmQ, q, rows, stride, cols) || !fa_map(&tmK, k, rows, stride, cols) ||
         !fa_map(&tmV, v, rows, stride, cols))
         return cudaErrorNotSupported;
-    static bool attr = false;
-    if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(flash_enc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kFaSmem);
-        if (e != cudaSuccess) return e;
-        attr = true;
-    }
+    static std::once_flag once;
+    static cudaError_t once_status;
+    if (cudaError_t e = run_once(once, once_status, [] {
+            return cudaFuncSetAttribute(flash_enc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kFaSmem);
+        }))
+        return e;
     const dim3 grid((seq + kQT - 1) / kQT, heads, chunks);
     flash_enc_kernel<<<grid, kFaThreads, kFaSmem, st>>>(tmQ, tmK, tmV, out, out_stride, seq, dev_err);
     return cudaGetLastError();

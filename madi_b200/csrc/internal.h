@@ -2,6 +2,7 @@
 // the kernel translation units.  Not part of the public ABI.
 #pragma once
 #include <cuda.h>
+#include <mutex>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
@@ -132,10 +133,14 @@ cudaError_t launch_cross_attn_reduce(float *out, const float *part, int nsplit, 
                                      int nh, cudaStream_t st);
 // Split form with the partials in a fixed device array (attn.cu): heads x nsplit at
 // most kSplitStaticMax.  Looks the array's device address up on each device's
-// first call.
+// first call (again when the device's context changed); cudaErrorInvalidDevice
+// unless the current device is `device` (the one the library is bound to).
 constexpr int kSplitStaticMax = 2048;
 cudaError_t launch_cross_attn_split_static(float *out, const float *q, const void *kc, const void *vc, float *sc,
-                                           int seqlen, int kvd, int nkv, int nh, int nsplit, cudaStream_t st);
+                                           int seqlen, int kvd, int nkv, int nh, int nsplit, int device,
+                                           cudaStream_t st);
+// Drops the looked-up addresses (madi_cleanup).
+void forget_split_static_addresses();
 cudaError_t launch_self_attn(float *out, const float *q, const void *kc, const void *vc, bool kv_f16,
                              const uint32_t *pos, int slots, int kvd, int nkv, int nh, int max_tok, int *dev_err,
                              cudaStream_t st);
@@ -156,6 +161,17 @@ cudaError_t launch_merge_argmax(const float *vals, const uint32_t *idx, int worl
 // ---------------------------------------------------------------- misc kernels
 cudaError_t launch_dequant_f16(const int8_t *qs, const __half *scales, int N, int K, __half *out, cudaStream_t st);
 cudaError_t launch_quantize_f16(const __half *w, int rows, int dim, int8_t *qs, __half *scales, cudaStream_t st);
+
+// One-time set-up shared by every host thread: `init` runs once per call site (per
+// template instantiation inside a template) and its status is returned to every
+// later caller; concurrent first calls wait for the one that runs it.  The library
+// binds one device per process (madi_init), so set-up that belongs to a device
+// (function attributes, occupancy queries) is done for that device.
+template <typename F>
+inline cudaError_t run_once(std::once_flag &flag, cudaError_t &status, F &&init) {
+    std::call_once(flag, [&] { status = init(); });
+    return status;
+}
 
 // Driver entry point for cuTensorMapEncodeTiled (resolved lazily through the
 // runtime, so the library needs no link-time libcuda).

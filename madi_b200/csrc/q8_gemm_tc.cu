@@ -493,12 +493,13 @@ cudaError_t launch_bt(const GemmArgs &a, const CUtensorMap &tmX, const CUtensorM
                       int ystore, int num_sms, cudaStream_t st) {
     using C = Cfg<BT>;
     auto fn = q8_gemm_tc_kernel<BT, EPI>;
-    static bool attr_set = false;   // once per instantiation: launches inside a capture stay pure launches
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem<BT, EPI>());
-        if (e != cudaSuccess) return e;
-        attr_set = true;
-    }
+    // once per instantiation: launches inside a capture stay pure launches
+    static std::once_flag once;
+    static cudaError_t once_status;
+    if (cudaError_t e = run_once(once, once_status, [&] {
+            return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem<BT, EPI>());
+        }))
+        return e;
     const int tiles = ((a.N + BN - 1) / BN) * ((a.M + BT - 1) / BT);
     const int grid = tiles < num_sms ? tiles : num_sms;
     fn<<<grid, kThreads, gemm_smem<BT, EPI>(), st>>>(tmX, tmW, tmY, a, ystore);
@@ -859,8 +860,10 @@ template <int PBT, int EPI>
 cudaError_t launch_pair(const GemmArgs &a, const CUtensorMap &tmX, const CUtensorMap &tmW, const CUtensorMap &tmY,
                         int ystore, int num_sms, cudaStream_t st) {
     auto fn = q8_gemm_pair_kernel<PBT, EPI>;
-    static int max_pairs = -1;     // once per instantiation: co-resident clusters on this device
-    if (max_pairs < 0) {
+    static int max_pairs = 1;      // once per instantiation: co-resident clusters on this device
+    static std::once_flag once;
+    static cudaError_t once_status;
+    if (cudaError_t e0 = run_once(once, once_status, [&] {
         cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pair_smem<PBT, EPI>());
         if (e != cudaSuccess) return e;
         cudaLaunchConfig_t cfg = {};
@@ -878,7 +881,9 @@ cudaError_t launch_pair(const GemmArgs &a, const CUtensorMap &tmX, const CUtenso
         e = cudaOccupancyMaxActiveClusters(&n, fn, &cfg);
         if (e != cudaSuccess) return e;
         max_pairs = n > 0 ? n : 1;
-    }
+        return cudaSuccess;
+    }))
+        return e0;
     const int tiles = ((a.N + PBN - 1) / PBN) * ((a.M + PBT - 1) / PBT);
     const int pairs = tiles < max_pairs ? tiles : max_pairs;
     fn<<<2 * pairs, kThreads, pair_smem<PBT, EPI>(), st>>>(tmX, tmW, tmY, a, ystore);
@@ -917,28 +922,26 @@ int pick_bt(int M, int N, int num_sms) {
 
 PFN_encodeTiled tensor_map_encoder() {
     static PFN_encodeTiled fn = nullptr;
-    static bool tried = false;
-    if (!tried) {
-        tried = true;
+    static std::once_flag once;
+    std::call_once(once, [] {
         void *ptr = nullptr;
         cudaDriverEntryPointQueryResult q;
         if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault, &q) ==
                 cudaSuccess &&
             q == cudaDriverEntryPointSuccess)
             fn = reinterpret_cast<PFN_encodeTiled>(ptr);
-    }
+    });
     return fn;
 }
 
 // CTA-pair kernel by default; MADI_GEMM_PAIR=0 in the environment selects the
 // one-CTA kernel (kept for comparison and for devices without cluster support).
 static bool use_pair_kernel() {
-    static int v = -1;
-    if (v < 0) {
+    static const bool v = [] {
         const char *e = getenv("MADI_GEMM_PAIR");
-        v = (e && e[0] == '0') ? 0 : 1;
-    }
-    return v == 1;
+        return !(e && e[0] == '0');
+    }();
+    return v;
 }
 cudaError_t launch_gemm_tc(const GemmArgs &a, int epi, int num_sms, cudaStream_t st) {
     const bool pair = use_pair_kernel() && num_sms >= 2;

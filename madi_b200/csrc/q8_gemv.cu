@@ -261,15 +261,19 @@ cudaError_t launch_one(const GemvArgs &a, cudaStream_t st, bool pdl) {
     // largest ever needed), so a launch inside a graph capture is only a launch
     static size_t smem_cap = 48 * 1024;
     static bool cluster_attr = false;
-    if (smem > smem_cap) {
-        cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-        smem_cap = smem;
-    }
-    if (!cluster_attr && a.ks > 8) {
-        cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-        if (e != cudaSuccess) return e;
-        cluster_attr = true;
+    static std::mutex mu;                 // host threads share the two attributes
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        if (smem > smem_cap) {
+            cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e != cudaSuccess) return e;
+            smem_cap = smem;
+        }
+        if (!cluster_attr && a.ks > 8) {
+            cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+            if (e != cudaSuccess) return e;
+            cluster_attr = true;
+        }
     }
     const int groups = (a.N + kRows - 1) / kRows;
     cudaLaunchConfig_t cfg = {};

@@ -492,12 +492,12 @@ template <typename XT, typename YT, int EPI, bool kQKV, int kG, bool kR16>
 cudaError_t launch_tile_g(const GemvArgs &a, const CUtensorMap &tmq, const CUtensorMap &tms, const TilePlan &pl,
                           int grid, int *dev_err, cudaStream_t st, bool pdl) {
     auto fn = q8_gemv_tile_kernel<XT, YT, EPI, kQKV, kG, kR16>;
-    static bool attr = false;
-    if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemCap);
-        if (e != cudaSuccess) return e;
-        attr = true;
-    }
+    static std::once_flag once;
+    static cudaError_t once_status;
+    if (cudaError_t e = run_once(once, once_status, [&] {
+            return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemCap);
+        }))
+        return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(kThreads);

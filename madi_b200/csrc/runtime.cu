@@ -107,16 +107,15 @@ bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) %
 size_t bytes_after(const void *p) {
     typedef CUresult (*PFN_range)(CUdeviceptr *, size_t *, CUdeviceptr);
     static PFN_range fn = nullptr;
-    static bool tried = false;
-    if (!tried) {
-        tried = true;
+    static std::once_flag once;
+    std::call_once(once, [] {
         void *ptr = nullptr;
         cudaDriverEntryPointQueryResult q;
         if (cudaGetDriverEntryPointByVersion("cuMemGetAddressRange", &ptr, 12000, cudaEnableDefault, &q) ==
                 cudaSuccess &&
             q == cudaDriverEntryPointSuccess)
             fn = reinterpret_cast<PFN_range>(ptr);
-    }
+    });
     CUdeviceptr base = 0;
     size_t size = 0;
     if (!fn || !p || fn(&base, &size, reinterpret_cast<CUdeviceptr>(p)) != CUDA_SUCCESS) return 0;
@@ -600,6 +599,7 @@ void madi_cleanup(void) {
         for (auto &kv : g_allocs) cudaFree(reinterpret_cast<void *>(kv.first));
         g_allocs.clear();
     }
+    forget_split_static_addresses();
     S = State();
 }
 
@@ -797,12 +797,18 @@ int madi_q8_linear(const madi_q8w *w, const void *x, int x_dtype, int m, const v
                           "madi_q8_linear");
 }
 
-int madi_q8_qkv(const madi_q8w *w, const float *x, int x_dtype, int m, const float *qb, const float *vb, float *q_out,
-                float *kc, float *vc, const uint32_t *pos, int64_t cache_stride, void *stream) {
-    if (x_dtype != MADI_F32 && x_dtype != MADI_F32_AS_F16)
-        return fail(MADI_EINVAL, "madi_q8_qkv: x_dtype %d (MADI_F32 or MADI_F32_AS_F16)", x_dtype);
+int madi_q8_qkv(const madi_q8w *w, const float *x, int m, const float *qb, const float *vb, float *q_out, float *kc,
+                float *vc, const uint32_t *pos, int64_t cache_stride, void *stream) {
     return q8_qkv_impl(w, x, m, qb, vb, q_out, kc, vc, pos, (long long)cache_stride, pick_stream(stream), "madi_q8_qkv",
-                       x_dtype == MADI_F32_AS_F16);
+                       false);
+}
+
+int madi_q8_qkv_ex(const madi_q8w *w, const float *x, int x_dtype, int m, const float *qb, const float *vb,
+                   float *q_out, float *kc, float *vc, const uint32_t *pos, int64_t cache_stride, void *stream) {
+    if (x_dtype != MADI_F32 && x_dtype != MADI_F32_AS_F16)
+        return fail(MADI_EINVAL, "madi_q8_qkv_ex: x_dtype %d (MADI_F32 or MADI_F32_AS_F16)", x_dtype);
+    return q8_qkv_impl(w, x, m, qb, vb, q_out, kc, vc, pos, (long long)cache_stride, pick_stream(stream),
+                       "madi_q8_qkv_ex", x_dtype == MADI_F32_AS_F16);
 }
 
 int madi_q8_dequant_f16(const madi_q8w *w, uint16_t *out, void *stream) {
@@ -999,7 +1005,10 @@ int madi_cross_attn_split_static(const float *q, const uint16_t *kc, const uint1
     if (!aligned(q, 16) || !aligned(kc, 16) || !aligned(vc, 16) || !aligned(out, 16) || (scores && !aligned(scores, 16)))
         return fail(MADI_EINVAL, "madi_cross_attn_split_static: buffers must be 16-byte aligned");
     cudaError_t e = launch_cross_attn_split_static(out, q, kc, vc, scores, seqlen, kv_dim, kv_heads, heads, nsplit,
-                                                   pick_stream(stream));
+                                                   S.device, pick_stream(stream));
+    if (e == cudaErrorInvalidDevice)
+        return fail(MADI_EINVAL, "madi_cross_attn_split_static: the current device is not device %d, which "
+                                 "madi_init bound", S.device);
     return e == cudaSuccess ? MADI_OK : cuda_fail(e, "madi_cross_attn_split_static");
 }
 

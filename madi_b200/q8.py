@@ -1,6 +1,6 @@
 """Typed Q8_0 linear API over torch CUDA tensors.
 
-Thin wrappers of the C ABI's typed entry points (madi_q8_linear, madi_q8_qkv,
+Thin wrappers of the C ABI's typed entry points (madi_q8_linear, madi_q8_qkv / _ex,
 madi_q8_dequant_f16, madi_q8_quantize_f16).  torch supplies device memory and
 streams only: every call runs this library's sm_100a kernels on the caller's
 current torch stream.
@@ -98,10 +98,15 @@ def qkv(w: Q8Weight, x: torch.Tensor, qb: torch.Tensor, vb: torch.Tensor, kc: to
         q_out = torch.empty((m, D), dtype=torch.float32, device=x.device)
     stride = kc.stride(0) if kc.dim() == 3 else 0
     h = w.handle()
-    rc = _lib.load().madi_q8_qkv(ctypes.byref(h), x.data_ptr(), MADI_F32_AS_F16 if x_round16 else MADI_F32, m,
-                                 qb.data_ptr(), vb.data_ptr(), q_out.data_ptr(),
-                                 kc.data_ptr(), vc.data_ptr(), pos.data_ptr(), stride, _stream(stream))
-    _lib.check(rc, "madi_q8_qkv")
+    if x_round16:
+        rc = _lib.load().madi_q8_qkv_ex(ctypes.byref(h), x.data_ptr(), MADI_F32_AS_F16, m, qb.data_ptr(),
+                                        vb.data_ptr(), q_out.data_ptr(), kc.data_ptr(), vc.data_ptr(), pos.data_ptr(),
+                                        stride, _stream(stream))
+        _lib.check(rc, "madi_q8_qkv_ex")
+    else:
+        rc = _lib.load().madi_q8_qkv(ctypes.byref(h), x.data_ptr(), m, qb.data_ptr(), vb.data_ptr(), q_out.data_ptr(),
+                                     kc.data_ptr(), vc.data_ptr(), pos.data_ptr(), stride, _stream(stream))
+        _lib.check(rc, "madi_q8_qkv")
     return q_out
 
 

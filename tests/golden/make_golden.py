@@ -11,7 +11,7 @@ bit-identical to the engine's in-load quantiser ``quantInto``
 The reference tree is only needed when (re)generating: the committed .npz is
 what the tests read.  Usage::
 
-    python tests/golden/make_golden.py [--reference-root DIR]
+    python tests/golden/make_golden.py --reference-root DIR   (or MADI_REFERENCE_ROOT=DIR)
 
 Cases (all F16, in-dim a multiple of 32 as the reference asserts):
   * ``normal``   : N(0, 0.02) weights, the Whisper projection scale, [48 x 256]
@@ -67,8 +67,12 @@ def make_cases(seed: int = 20261201):
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference-root", default=os.environ.get("MADI_REFERENCE_ROOT", "/root/reference"))
+    ap.add_argument("--reference-root", default=os.environ.get("MADI_REFERENCE_ROOT", ""),
+                    help="the companyjupiter/madi checkout (or set MADI_REFERENCE_ROOT)")
     args = ap.parse_args()
+    if not args.reference_root:
+        print("pass --reference-root (the companyjupiter/madi checkout) or set MADI_REFERENCE_ROOT", file=sys.stderr)
+        return 2
     script = os.path.join(args.reference_root, SCRIPT_REL)
     if not os.path.isfile(script):
         print(f"reference quantiser not found at {script}", file=sys.stderr)

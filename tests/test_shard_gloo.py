@@ -1,7 +1,9 @@
 """CPU: multi-rank host logic of the Q8 path with world_size-2 gloo ranks.
 
 Checks the chunk partition, the column-split vocab head's all-gather and the greedy
-merge (lowest index on ties, also across shard boundaries), and that a failing rank
+merge (ties resolved in the reference argmax's order -- the index whose lane, index
+mod 1024, is smallest bit-reversed, then the lower index -- also across shard
+boundaries), and that a failing rank
 surfaces as an error on the host instead of a hang (short process-group timeout)."""
 import datetime
 import os

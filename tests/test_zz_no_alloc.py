@@ -8,7 +8,8 @@ Called through the C ABI twice in a row -- the second call with another sequence
 length and split count, after the first left its partials in the shared array --
 and each result checked against the existing entry point madi_cross_attn on the
 same inputs, within the attention tests' bar (outputs 2e-5 x max|out|, normalised
-scores 1e-6).  A request beyond the array's limit must be refused before any launch.
+scores 1e-6).  Repeated calls must leave the device's free memory unchanged, and a
+request beyond the array's limit must be refused before any launch.
 
 This file is collected last on purpose.
 """
@@ -44,6 +45,32 @@ def test_static_scratch_matches_cross_attn(madi):
         w, o = want[0].cpu().numpy().astype(np.float64), out.cpu().numpy().astype(np.float64)
         assert np.abs(o - w).max() <= 2e-5 * np.abs(w).max(), f"seqlen {seqlen}: output differs"
         assert np.abs(sc.cpu().numpy() - want_sc[0].cpu().numpy()).max() <= 1e-6, f"seqlen {seqlen}: scores differ"
+
+
+def test_static_scratch_allocates_nothing(madi):
+    """After a first call (which looks the array's address up), further calls leave
+    the device's free memory and torch's allocator exactly as they were: the entry
+    point takes no device memory of its own."""
+    import torch
+    from madi_b200 import _lib
+    L = _lib.load()
+    stream = torch.cuda.current_stream().cuda_stream
+    q, kc, vc = (torch.from_numpy(a).cuda() for a in _inputs(1500, 20, 4))
+    out = torch.empty((20 * 64,), dtype=torch.float32, device="cuda")
+    sc = torch.empty((20, 1500), dtype=torch.float32, device="cuda")
+
+    def call():
+        _lib.check(L.madi_cross_attn_split_static(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), 1500, 20, 20, 1280, 8,
+                                                  out.data_ptr(), sc.data_ptr(), stream),
+                   "madi_cross_attn_split_static")
+    call()
+    torch.cuda.synchronize()
+    free0, alloc0 = torch.cuda.mem_get_info()[0], torch.cuda.memory_allocated()
+    for _ in range(3):
+        call()
+    torch.cuda.synchronize()
+    assert torch.cuda.memory_allocated() == alloc0
+    assert torch.cuda.mem_get_info()[0] == free0
 
 
 def test_static_scratch_limit(madi):
