@@ -578,10 +578,29 @@ def long_audio_leg(args, world, rank, dev):
     [128][3000] each) sharded over the ranks; each rank runs the whole encoder (conv
     stem, 32 layers, ln_post) on even batches of at most 16 chunks, then the 4-layer
     greedy decoder (one token slot per chunk) for exactly `--tokens` tokens per chunk
-    (EOT suppressed), replicated vocab head.
-    Timed from the pinned host mel to the tokens back in host memory; one untimed
-    batch first (module load, graph capture).  chunks/s = all chunks / the slowest
-    rank's time (strong scaling: the total is fixed)."""
+    (EOT suppressed).  At N > 1 both head layouts run: the vocab head column-split
+    over the ranks with NCCL all-gathers inside every token step (what config 4
+    prescribes; `chunks_per_s`), and the head replicated on every rank
+    (`replicated_head`).  Timed from the pinned host mel to the tokens back in host
+    memory; one untimed batch first (module load, graph capture).  chunks/s = all
+    chunks / the slowest rank's time (strong scaling: the total is fixed)."""
+    modes = ["replicated"]
+    if world > 1 and args.chunks % world == 0:
+        modes = ["split", "replicated"]
+    res = {m: long_audio_run(args, world, rank, dev, m == "split") for m in modes}
+    out = dict(res[modes[0]])
+    out["head"] = modes[0]
+    if len(modes) > 1:
+        out["replicated_head"] = {k: res["replicated"][k] for k in
+                                  ("chunks_per_s", "ms_total", "decoder_ms_per_token_step", "encoder_ms_per_batch",
+                                   "decoder_ms_per_batch")}
+        differ = 0.0 if res["split"]["_tokens"] == res["replicated"]["_tokens"] else 1.0
+        out["tokens_equal_between_head_modes"] = max_over_ranks(world, differ) == 0.0   # on every rank
+    out.pop("_tokens", None)
+    return out
+
+
+def long_audio_run(args, world, rank, dev, split):
     import math
 
     import torch
@@ -594,7 +613,8 @@ def long_audio_leg(args, world, rank, dev):
     # even batches of at most 16 chunks (token slots): 120 -> 8 x 15, 15 -> 1 x 15
     nb = max(1, math.ceil(mine / 16))
     slots = max(1, math.ceil(mine / nb))
-    tr = pipeline.Transcriber(slots=slots, enc_layers=32, tokens=args.tokens, seed=1, device=dev)
+    tr = pipeline.Transcriber(slots=slots, enc_layers=32, tokens=args.tokens, seed=1, device=dev,
+                              split=(world, rank) if split else None)
     mel_h = torch.from_numpy(pipeline.synthetic_mel(max(mine, 1), first=lo)).pin_memory()
     mel_d = torch.empty((slots,) + tuple(mel_h.shape[1:]), dtype=torch.float16, device=dev)
     tok_h = torch.empty((max(mine, 1), args.tokens), dtype=torch.int32, pin_memory=True)
@@ -618,17 +638,21 @@ def long_audio_leg(args, world, rank, dev):
     dec_avg = sum(a.elapsed_time(b) for a, b in dec_ms) / max(1, len(dec_ms))
     toks = tok_h[:mine].numpy().view("uint32")
     tr.release()
+    barrier(world)
     del tr, mel_d
     torch.cuda.empty_cache()
+    head = ("column-split over the ranks (NCCL all-gathers of the hidden states and of per-row (max, index, "
+            "exp-sum) parts in every token step)" if split else "replicated head")
     return {"chunks": args.chunks, "chunks_per_rank": per, "tokens_per_chunk": args.tokens, "slots": slots,
             "chunks_per_s": args.chunks / (ms_max / 1e3), "ms_total": ms_max, "scaling": "strong",
             "encoder_ms_per_batch": enc_avg, "decoder_ms_per_batch": dec_avg,
             "overlap": "encoder of batch k+1 on its own stream beside the decoder of batch k" if overlap else None,
             "decoder_ms_per_token_step": dec_avg / args.tokens,
             "encoder": f"conv stem (PyTorch f16 conv1d) + 32 Q8 layers + ln_post, {slots} chunks per batch",
-            "decoder": "4 Q8 layers, replicated head, one CUDA graph per token step, EOT suppressed",
+            "decoder": f"4 Q8 layers, {head}, one CUDA graph per token step, EOT suppressed",
             "h2d_bytes": int(mine * 128 * 3000 * 2), "d2h_bytes": int(mine * args.tokens * 4),
             "first_tokens_rank0": toks[0, :8].tolist() if mine else [],
+            "_tokens": toks.tobytes(),
             "data": "synthetic log-mel (seeded N(0,1) clipped to +-1.5), random-init Q8 weights"}
 
 

@@ -366,6 +366,25 @@ int madi_shard_argmax(const float *logits, int m, int n, int64_t row_stride, uin
                       void *stream);
 int madi_merge_shard_argmax(const float *vals, const uint32_t *idx, int world, int m, uint32_t *tokens, void *stream);
 
+/* madi_decode_tail over a column-split vocab head (no reference counterpart: the
+ * reference runs the head on one device).  Each rank holds logits [m][n] for the
+ * global token ids [h0, h0 + n) of a `vocab`-token vocabulary, for ALL m token
+ * rows of the job, and the same token history / positions / suppress list for
+ * them (tokens [m][tok_stride], pos [m], read only here).  madi_shard_decode_tail
+ * applies the filter and suppress bans that fall in the shard and writes, per row,
+ * part[row] = {max, global index (u32 bits), sum exp(z - max), 0} (f32 x 4,
+ * 16-byte aligned).  After an all-gather of the parts (rank-major:
+ * parts[r][row]), madi_merge_shard_tail does the rest of madi_decode_tail: pos[row]
+ * += 1, tokens[row][pos[row]] = the greedy token (the reference's tie order across
+ * shards) and conf[row][pos[row]] = 1 / sum_r part_r.sum * exp(part_r.max - max)
+ * (conf may be NULL).  Same tokens as madi_decode_tail over the gathered rows. */
+int madi_shard_decode_tail(float *logits, int m, int n, uint32_t h0, int vocab, const uint32_t *tokens,
+                           int64_t tok_stride, int max_len, const uint32_t *pos, uint32_t sample_begin,
+                           uint32_t no_repeat_ngram, const uint32_t *suppress, int n_suppress, float *part,
+                           void *stream);
+int madi_merge_shard_tail(const float *parts, int world, int m, uint32_t *tokens, int64_t tok_stride, int max_len,
+                          uint32_t *pos, float *conf, void *stream);
+
 /* step_advance (graph_helpers.metal:60-62) for m <= 32 slots: pos[s] += 1. */
 int madi_step_advance(uint32_t *pos, int m, void *stream);
 

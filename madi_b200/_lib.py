@@ -72,6 +72,8 @@ SIGNATURES = {
     "madi_cross_attn_split_static": ([P, P, P, I, I, I, I, I, P, P, P], I),
     "madi_suppress_rows": ([P, I, I, P, I, P], I),
     "madi_shard_argmax": ([P, I, I, ctypes.c_int64, U32, P, P, P], I),
+    "madi_shard_decode_tail": ([P, I, I, U32, I, P, ctypes.c_int64, I, P, U32, U32, P, I, P, P], I),
+    "madi_merge_shard_tail": ([P, I, I, P, ctypes.c_int64, I, P, P, P], I),
     "madi_merge_shard_argmax": ([P, P, I, I, P, P], I),
     "madi_cross_attn": ([P, P, P, I, I, I, I, I, I, P, P, P], I),
     "madi_self_attn": ([P, P, P, I, P, I, I, I, I, I, P, P], I),

@@ -268,16 +268,25 @@ __global__ void merge_argmax_kernel(const float *__restrict__ vals, const uint32
 // the confidence runs over the registers against the global max.  Same tokens and
 // filtered logits as the four kernels; the confidence's f32 sum runs in another
 // order.
+//
+// kShard: the same for one column shard of the vocabulary -- the row holds global
+// token ids [h0, h0 + n) of a vocabulary of V; bans apply to the ids that fall in
+// the shard.  Instead of advancing pos and writing the token, CTA 0 writes the
+// shard's (max value, global index, exp sum against the shard's max) to part[s],
+// which merge_tail_kernel combines over the shards (with the history, position and
+// suppress list every shard shares).
 constexpr int kTailCtas = 8;
 constexpr int kTailThr = 256;
-constexpr int kTailPer = 28;                              // values per thread (V <= 8 * 256 * 28)
+constexpr int kTailPer = 28;                              // values per thread (n <= 8 * 256 * 28)
 
-__global__ void __launch_bounds__(kTailThr) decode_tail_kernel(float *__restrict__ logits, int V,
+template <bool kShard>
+__global__ void __launch_bounds__(kTailThr) decode_tail_kernel(float *__restrict__ logits, int n, uint32_t h0, int V,
                                                                uint32_t *__restrict__ tokens, long long stride,
                                                                int max_len, uint32_t *__restrict__ pos,
                                                                float *__restrict__ conf, uint32_t sample_begin,
                                                                uint32_t no_repeat_ngram,
-                                                               const uint32_t *__restrict__ sup, int nsup) {
+                                                               const uint32_t *__restrict__ sup, int nsup,
+                                                               float4 *__restrict__ part) {
     __shared__ float wv[kTailThr / 32];
     __shared__ uint64_t wk[kTailThr / 32];
     __shared__ float cv[kTailCtas];                       // rank 0: the CTAs' best values
@@ -290,13 +299,16 @@ __global__ void __launch_bounds__(kTailThr) decode_tail_kernel(float *__restrict
     pdl_trigger();
     pdl_wait();
     asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
-    float *lg = logits + (size_t)s * V;
+    float *lg = logits + (size_t)s * n;
     const uint32_t *past = tokens + (size_t)s * stride;
     const uint32_t step = pos[s] + 1u;                    // step_advance
-    const int per = (V + kTailCtas - 1) / kTailCtas;
-    const int lo = r * per, hi = min(V, lo + per);
-    auto ban = [&](uint32_t t) {
-        if (t < (uint32_t)V && (int)t >= lo && (int)t < hi) lg[t] = kNeg;
+    const int per = (n + kTailCtas - 1) / kTailCtas;
+    const int lo = r * per, hi = min(n, lo + per);        // local columns of this CTA
+    auto ban = [&](uint32_t t) {                          // t: a global token id
+        if (t < (uint32_t)V && t >= h0) {
+            const uint32_t c = t - h0;
+            if ((int)c >= lo && (int)c < hi) lg[c] = kNeg;
+        }
     };
     // logit_filter_indirect (graph_helpers.metal:109-160) with step = the advanced position
     const bool hist_ok = step <= (uint32_t)max_len;
@@ -323,7 +335,9 @@ __global__ void __launch_bounds__(kTailThr) decode_tail_kernel(float *__restrict
             ban(50257u);
         }
     }
-    for (int t = max(lo, 50258) + tid; t < hi; t += kTailThr) lg[t] = kNeg;
+    // ids >= 50258 (specials): local columns from max(lo, 50258 - h0)
+    const int sp0 = 50258 > (int)h0 ? 50258 - (int)h0 : 0;
+    for (int c = max(lo, sp0) + tid; c < hi && (uint32_t)c + h0 < (uint32_t)V; c += kTailThr) lg[c] = kNeg;
     for (int j = tid; j < nsup; j += kTailThr) ban(sup[j]);                 // suppress_list
     __syncthreads();
     float v[kTailPer];
@@ -338,7 +352,7 @@ __global__ void __launch_bounds__(kTailThr) decode_tail_kernel(float *__restrict
     for (int i = 0; i < kTailPer; ++i) {
         const int t = lo + tid + i * kTailThr;
         if (t < hi) {
-            const uint64_t k = tie_key((uint32_t)t);
+            const uint64_t k = tie_key(h0 + (uint32_t)t);
             if (better(v[i], k, bv, bk)) { bv = v[i]; bk = k; }
         }
     }
@@ -387,11 +401,46 @@ __global__ void __launch_bounds__(kTailThr) decode_tail_kernel(float *__restrict
     if (r == 0 && tid == 0) {
         float tot = 0.f;
         for (int c = 0; c < kTailCtas; ++c) tot += csum[c];
-        pos[s] = step;
-        if (step < (uint32_t)max_len) {
-            tokens[(size_t)s * stride + step] = (uint32_t)gkey;
-            if (conf) conf[(size_t)s * stride + step] = 1.0f / tot;
+        if constexpr (kShard) {
+            part[s] = make_float4(zmax, __uint_as_float((uint32_t)gkey), tot, 0.f);
+        } else {
+            pos[s] = step;
+            if (step < (uint32_t)max_len) {
+                tokens[(size_t)s * stride + step] = (uint32_t)gkey;
+                if (conf) conf[(size_t)s * stride + step] = 1.0f / tot;
+            }
         }
+    }
+}
+
+// Combines the shards' (max, index, exp sum) of every row -- part[r * m + row], shard
+// (rank) major -- into the greedy token: the best (max, tie key), the confidence
+// 1 / sum_r sum_r * exp(max_r - max), then step_advance and the token / confidence
+// writes of decode_tail_kernel.  One thread per row.
+__global__ void merge_tail_kernel(const float4 *__restrict__ part, int world, int m, uint32_t *__restrict__ tokens,
+                                  long long stride, int max_len, uint32_t *__restrict__ pos, float *__restrict__ conf) {
+    const int row = blockIdx.x * blockDim.x + threadIdx.x;
+    pdl_trigger();
+    pdl_wait();
+    if (row >= m) return;
+    float bv = -INFINITY;
+    uint32_t bi = 0;
+    uint64_t bk = ~0ull;
+    for (int r = 0; r < world; ++r) {
+        const float4 p = part[(size_t)r * m + row];
+        const uint32_t i = __float_as_uint(p.y);
+        if (better(p.x, tie_key(i), bv, bk)) { bv = p.x; bi = i; bk = tie_key(i); }
+    }
+    float tot = 0.f;
+    for (int r = 0; r < world; ++r) {
+        const float4 p = part[(size_t)r * m + row];
+        if (p.z > 0.f) tot += p.z * expf(p.x - bv);
+    }
+    const uint32_t step = pos[row] + 1u;
+    pos[row] = step;
+    if (step < (uint32_t)max_len) {
+        tokens[(size_t)row * stride + step] = bi;
+        if (conf) conf[(size_t)row * stride + step] = 1.0f / tot;
     }
 }
 
@@ -442,8 +491,23 @@ int decode_tail_max_vocab() { return kTailCtas * kTailThr * kTailPer; }
 cudaError_t launch_decode_tail(float *logits, int m, int V, uint32_t *tokens, long long stride, int max_len,
                                uint32_t *pos, float *conf, uint32_t sample_begin, uint32_t no_repeat_ngram,
                                const uint32_t *sup, int nsup, cudaStream_t st) {
-    return launch_k(decode_tail_kernel, dim3(kTailCtas, m), kTailThr, 0, st, kTailCtas, logits, V, tokens, stride,
-                    max_len, pos, conf, sample_begin, no_repeat_ngram, sup, nsup);
+    return launch_k(decode_tail_kernel<false>, dim3(kTailCtas, m), kTailThr, 0, st, kTailCtas, logits, V, 0u, V,
+                    tokens, stride, max_len, pos, conf, sample_begin, no_repeat_ngram, sup, nsup,
+                    static_cast<float4 *>(nullptr));
+}
+
+cudaError_t launch_shard_tail(float *logits, int m, int n, uint32_t h0, int V, const uint32_t *tokens,
+                              long long stride, int max_len, const uint32_t *pos, uint32_t sample_begin,
+                              uint32_t no_repeat_ngram, const uint32_t *sup, int nsup, float4 *part, cudaStream_t st) {
+    return launch_k(decode_tail_kernel<true>, dim3(kTailCtas, m), kTailThr, 0, st, kTailCtas, logits, n, h0, V,
+                    const_cast<uint32_t *>(tokens), stride, max_len, const_cast<uint32_t *>(pos),
+                    static_cast<float *>(nullptr), sample_begin, no_repeat_ngram, sup, nsup, part);
+}
+
+cudaError_t launch_merge_tail(const float4 *part, int world, int m, uint32_t *tokens, long long stride, int max_len,
+                              uint32_t *pos, float *conf, cudaStream_t st) {
+    return launch_k(merge_tail_kernel, (m + 127) / 128, 128, 0, st, 1, part, world, m, tokens, stride, max_len, pos,
+                    conf);
 }
 
 cudaError_t launch_shard_argmax(const float *logits, long long row_stride, int n, uint32_t h0, int m, float *vals,

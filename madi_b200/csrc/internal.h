@@ -153,6 +153,15 @@ int decode_tail_max_vocab();
 cudaError_t launch_decode_tail(float *logits, int m, int V, uint32_t *tokens, long long stride, int max_len,
                                uint32_t *pos, float *conf, uint32_t sample_begin, uint32_t no_repeat_ngram,
                                const uint32_t *sup, int nsup, cudaStream_t st);
+// The same tail over one column shard [h0, h0 + n) of a V-token vocabulary: per row
+// the shard's (max, global index, exp sum against its max) into part[row]; then
+// the merge of the world shards' parts (rank-major) with step_advance and the
+// token / confidence writes.
+cudaError_t launch_shard_tail(float *logits, int m, int n, uint32_t h0, int V, const uint32_t *tokens,
+                              long long stride, int max_len, const uint32_t *pos, uint32_t sample_begin,
+                              uint32_t no_repeat_ngram, const uint32_t *sup, int nsup, float4 *part, cudaStream_t st);
+cudaError_t launch_merge_tail(const float4 *part, int world, int m, uint32_t *tokens, long long stride, int max_len,
+                              uint32_t *pos, float *conf, cudaStream_t st);
 cudaError_t launch_shard_argmax(const float *logits, long long row_stride, int n, uint32_t h0, int m, float *vals,
                                 uint32_t *idx, cudaStream_t st);
 cudaError_t launch_merge_argmax(const float *vals, const uint32_t *idx, int world, int m, uint32_t *tokens,

@@ -949,6 +949,35 @@ int madi_decode_tail(float *logits, int m, int vocab, uint32_t *tokens, int64_t 
     return e == cudaSuccess ? MADI_OK : cuda_fail(e, "madi_decode_tail");
 }
 
+int madi_shard_decode_tail(float *logits, int m, int n, uint32_t h0, int vocab, const uint32_t *tokens,
+                           int64_t tok_stride, int max_len, const uint32_t *pos, uint32_t sample_begin,
+                           uint32_t no_repeat_ngram, const uint32_t *suppress, int n_suppress, float *part,
+                           void *stream) {
+    if (!S.ready) return fail(MADI_ENOINIT, "madi_shard_decode_tail: not initialised");
+    if (!logits || !tokens || !pos || !part || (n_suppress > 0 && !suppress) || n_suppress < 0)
+        return fail(MADI_EINVAL, "madi_shard_decode_tail: null argument");
+    if (m <= 0 || m > 65535 || n <= 0 || n > decode_tail_max_vocab() || vocab <= 0 || (int64_t)h0 + n > vocab ||
+        max_len <= 0 || (m > 1 && tok_stride < max_len))
+        return fail(MADI_EINVAL, "madi_shard_decode_tail: bad shape (m=%d n=%d <= %d, h0=%u, vocab=%d, max_len=%d)", m,
+                    n, decode_tail_max_vocab(), h0, vocab, max_len);
+    if (!aligned(part, 16)) return fail(MADI_EINVAL, "madi_shard_decode_tail: part must be 16-byte aligned");
+    cudaError_t e = launch_shard_tail(logits, m, n, h0, vocab, tokens, (long long)tok_stride, max_len, pos, sample_begin,
+                                      no_repeat_ngram, suppress, n_suppress, reinterpret_cast<float4 *>(part),
+                                      pick_stream(stream));
+    return e == cudaSuccess ? MADI_OK : cuda_fail(e, "madi_shard_decode_tail");
+}
+
+int madi_merge_shard_tail(const float *parts, int world, int m, uint32_t *tokens, int64_t tok_stride, int max_len,
+                          uint32_t *pos, float *conf, void *stream) {
+    if (!S.ready) return fail(MADI_ENOINIT, "madi_merge_shard_tail: not initialised");
+    if (!parts || !tokens || !pos || world <= 0 || m <= 0 || max_len <= 0 || (m > 1 && tok_stride < max_len))
+        return fail(MADI_EINVAL, "madi_merge_shard_tail: bad argument (world=%d m=%d max_len=%d)", world, m, max_len);
+    if (!aligned(parts, 16)) return fail(MADI_EINVAL, "madi_merge_shard_tail: parts must be 16-byte aligned");
+    cudaError_t e = launch_merge_tail(reinterpret_cast<const float4 *>(parts), world, m, tokens, (long long)tok_stride,
+                                      max_len, pos, conf, pick_stream(stream));
+    return e == cudaSuccess ? MADI_OK : cuda_fail(e, "madi_merge_shard_tail");
+}
+
 int madi_argmax_rows(const float *logits, int m, int vocab, uint32_t *tokens, void *stream) {
     if (!S.ready) return fail(MADI_ENOINIT, "madi_argmax_rows: not initialised");
     if (!logits || !tokens || m <= 0 || vocab <= 0) return fail(MADI_EINVAL, "madi_argmax_rows: bad argument");

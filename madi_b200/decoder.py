@@ -15,14 +15,26 @@ the tcgen05 GEMM for the one-time cross K/V projection of the encoder states, th
 cluster attention kernels, the f32 LayerNorms, the decode-step helpers), all on one
 stream and capturable as one CUDA graph per token step.  Weights are seeded random
 Q8 (no checkpoint); the encoder states are seeded random f16 [1500][1280] per slot.
+
+Column-split vocab head (split=(world, rank)): one process per GPU, each running the
+layers for its own `slots` token slots, while the tied head is split by vocabulary
+rows -- rank r owns token ids [h0, h1) (shard.vocab_shard).  Per token step: an
+all-gather of every rank's final hidden states (f32 [world*slots][1280]); this
+rank's head shard over all world*slots rows (the skinny GEMM, one launch per
+source rank, so every row is computed exactly as the replicated head computes it);
+the logit filter and suppress list on the shard's columns for every row
+(madi_shard_decode_tail -- every rank keeps the token history and positions of all
+rows); an all-gather of the per-row (max, index, exp sum) parts; and the merge
+(madi_merge_shard_tail) that writes every row's token.  The exchange is a callable
+(out, inp) -> all-gather; NCCL's all_gather_into_tensor by default.
 """
 from dataclasses import dataclass
-from typing import List
+from typing import Callable, List, Optional, Tuple
 
 import numpy as np
 import torch
 
-from . import attn, greedy, q8, synth
+from . import attn, greedy, q8, shard, synth
 
 D, F, V, HEADS, LAYERS, MAX_TOK, ENC = 1280, 5120, 51866, 20, 4, 448, 1500
 EPS = 1e-5
@@ -106,12 +118,19 @@ def device_weights(seed: int = 1, device="cuda") -> dict:
 class Decoder:
     """Device copy of the synthetic decoder plus the per-slot decode state."""
 
-    def __init__(self, w: dict, slots: int, device="cuda", act16: bool = False):
+    def __init__(self, w: dict, slots: int, device="cuda", act16: bool = False,
+                 split: Optional[Tuple[int, int]] = None,
+                 exchange: Optional[Callable[[torch.Tensor, torch.Tensor], None]] = None):
         """act16: the projections take their f32 activations rounded to f16, as the
         reference's batched decode (decodeBlockBatched, decoder.zig:337-341) converts
-        them; False keeps the single-token GEMV family's f32 activations."""
+        them; False keeps the single-token GEMV family's f32 activations.
+        split: (world, rank) for the column-split vocab head (see the module
+        docstring); exchange(out, inp): all-gather of inp from every rank into out,
+        rank-major (default: torch.distributed.all_gather_into_tensor)."""
         if not 1 <= slots <= 16:
             raise ValueError("1..16 token slots")
+        if split is not None and not (split[0] >= 1 and 0 <= split[1] < split[0]):
+            raise ValueError(f"split (world, rank) = {split}")
         t = lambda a: (a.to(device) if isinstance(a, torch.Tensor) else
                        torch.from_numpy(np.ascontiguousarray(a)).to(device))
         qw = lambda p: q8.Q8Weight(t(p[0]), t(p[1]))
@@ -131,14 +150,36 @@ class Decoder:
         f32 = dict(dtype=torch.float32, device=device)
         self.x, self.xb, self.q, self.ao, self.mo = (torch.zeros((S, D), **f32) for _ in range(5))
         self.mh = torch.zeros((S, F), **f32)
-        self.logits = torch.zeros((S, V), **f32)
         self.kc = [torch.zeros((S, MAX_TOK, D), **f32) for _ in range(LAYERS)]
         self.vc = [torch.zeros((S, MAX_TOK, D), **f32) for _ in range(LAYERS)]
         self.ck = [None] * LAYERS
         self.cv = [None] * LAYERS
-        self.tokens = torch.zeros((S, MAX_TOK), dtype=torch.int32, device=device)
-        self.conf = torch.zeros((S, MAX_TOK), **f32)
-        self.pos = torch.zeros(S, dtype=torch.int32, device=device)
+        self.split = split
+        if split is None:
+            self.logits = torch.zeros((S, V), **f32)
+            self.tokens = torch.zeros((S, MAX_TOK), dtype=torch.int32, device=device)
+            self.conf = torch.zeros((S, MAX_TOK), **f32)
+            self.pos = torch.zeros(S, dtype=torch.int32, device=device)
+        else:
+            world, rank = split
+            R = world * S                                         # token rows of the whole job
+            self.h0, self.h1 = shard.vocab_shard(V, world, rank)
+            self.head = self.emb.rows(self.h0, self.h1)           # this rank's rows of the tied head
+            self.tokens_all = torch.zeros((R, MAX_TOK), dtype=torch.int32, device=device)
+            self.conf_all = torch.zeros((R, MAX_TOK), **f32)
+            self.pos_all = torch.zeros(R, dtype=torch.int32, device=device)
+            # this rank's slots: views of its rows of the job-wide state
+            self.tokens = self.tokens_all[rank * S:(rank + 1) * S]
+            self.conf = self.conf_all[rank * S:(rank + 1) * S]
+            self.pos = self.pos_all[rank * S:(rank + 1) * S]
+            self.xb_all = torch.zeros((R, D), **f32)
+            self.logits = torch.zeros((R, self.h1 - self.h0), **f32)
+            self.part = torch.zeros((R, 4), **f32)
+            self.parts = torch.zeros((world, R, 4), **f32)
+            if exchange is None:
+                import torch.distributed as dist
+                exchange = lambda out, inp: dist.all_gather_into_tensor(out, inp)   # noqa: E731
+            self.exchange = exchange
 
     def set_encoder(self, enc_states: torch.Tensor, stream=None):
         """Cross K / V of every layer from the encoder states f16 [slots][1500][1280]
@@ -155,16 +196,51 @@ class Decoder:
             q8.linear(L.cv, flat, bias=L.cvb, out=self.cv[l].view(S * T, D), stream=stream)
 
     def reset(self, seed_token: int = 50258):
-        self.tokens.zero_()
-        self.tokens[:, 0] = seed_token
-        self.conf.zero_()
-        self.pos.zero_()
+        if self.split is None:
+            tok, conf, pos = self.tokens, self.conf, self.pos
+        else:
+            tok, conf, pos = self.tokens_all, self.conf_all, self.pos_all
+        tok.zero_()
+        tok[:, 0] = seed_token
+        conf.zero_()
+        pos.zero_()
         for c in self.kc + self.vc:
             c.zero_()
 
     def step(self, sample_begin: int = 1, no_repeat_ngram: int = 0, stream=None, suppress=None):
         """One greedy token for every slot; all state on the device.  suppress: device
         u32 token ids banned at every step (e.g. EOT, to force a fixed length)."""
+        self.step_layers(stream)
+        if self.split is None:
+            r = dict(stream=stream, x_round16=self.act16)
+            q8.linear(self.emb, self.xb, out=self.logits, **r)
+            greedy.decode_tail(self.logits, self.tokens, self.pos, self.conf, sample_begin, no_repeat_ngram, suppress,
+                               stream=stream)
+            return
+        self.exchange(self.xb_all, self.xb)
+        self.step_shard_head(sample_begin, no_repeat_ngram, stream, suppress)
+        self.exchange(self.parts.view(-1, 4), self.part)
+        self.step_merge(stream)
+
+    def step_shard_head(self, sample_begin: int = 1, no_repeat_ngram: int = 0, stream=None, suppress=None):
+        """Split head, after the hidden states of all rows are in xb_all: this rank's
+        head shard for every row (one skinny-GEMM launch per source rank, at most 16
+        rows each, so a row's logits are computed exactly as by the replicated head),
+        then the shard's filter / suppress bans and its per-row parts."""
+        S = self.slots
+        for r0 in range(0, self.xb_all.shape[0], S):
+            q8.linear(self.head, self.xb_all[r0:r0 + S], out=self.logits[r0:r0 + S], stream=stream,
+                      x_round16=self.act16)
+        greedy.shard_decode_tail(self.logits, self.h0, V, self.tokens_all, self.pos_all, self.part, sample_begin,
+                                 no_repeat_ngram, suppress, stream=stream)
+
+    def step_merge(self, stream=None):
+        """Split head, after the parts of every shard are in `parts`: every row's token."""
+        greedy.merge_shard_tail(self.parts, self.tokens_all, self.pos_all, self.conf_all, stream=stream)
+
+    def step_layers(self, stream=None):
+        """Embedding, the decoder layers and the final LayerNorm for this rank's
+        slots: the head's input in xb."""
         s = dict(stream=stream)
         r = dict(stream=stream, x_round16=self.act16)
         greedy.emb_pos_q8(self.emb, self.tokens, self.pos, self.pos_emb, out=self.x, **s)
@@ -181,15 +257,13 @@ class Decoder:
             q8.linear(L.fc1, self.xb, bias=L.m0b, epi=q8.EPI_BIAS_GELU, out=self.mh, **r)
             q8.linear(L.fc2, self.mh, bias=L.m2b, epi=q8.EPI_BIAS_RES, residual=self.x, out=self.x, **r)
         q8.layer_norm(self.x, *self.ln_post, eps=EPS, out=self.xb, **s)
-        q8.linear(self.emb, self.xb, out=self.logits, **r)
-        greedy.decode_tail(self.logits, self.tokens, self.pos, self.conf, sample_begin, no_repeat_ngram, suppress,
-                           **s)
 
     def step_bytes(self) -> int:
         """HBM bytes one token step must read: every Q8 weight and scale once, the
-        self K/V rows 0..pos (counted at a full 448-row cache), the cross K/V."""
+        self K/V rows 0..pos (counted at a full 448-row cache), the cross K/V, the
+        head (this rank's shard of it when split)."""
         per_layer = (3 * D * D + 3 * D * D + 2 * F * D) * (1 + 1 / 16)
         kv_self = 2 * self.slots * MAX_TOK * D * 4
         kv_cross = 2 * self.slots * ENC * D * 2
-        head = V * D * (1 + 1 / 16)
+        head = (V if self.split is None else self.h1 - self.h0) * D * (1 + 1 / 16)
         return int(LAYERS * (per_layer + kv_self + kv_cross) + head)

@@ -5,7 +5,7 @@ no host round trip and replays as a CUDA graph.
 
 Thin wrappers of the C ABI (madi_emb_lookup_q8, madi_emb_pos_q8, madi_argmax_conf,
 madi_logit_filter, madi_logit_filter_rows, madi_suppress_rows, madi_step_advance,
-madi_decode_tail) on torch CUDA tensors.
+madi_decode_tail, madi_shard_decode_tail, madi_merge_shard_tail) on torch CUDA tensors.
 """
 import ctypes
 from typing import Optional
@@ -138,3 +138,43 @@ def decode_tail(logits: torch.Tensor, tokens: torch.Tensor, pos: torch.Tensor, c
 def step_advance(pos: torch.Tensor, stream=None) -> None:
     """pos[s] += 1 on the device."""
     _lib.check(_lib.load().madi_step_advance(pos.data_ptr(), pos.numel(), _stream(stream)), "madi_step_advance")
+
+
+def shard_decode_tail(logits: torch.Tensor, h0: int, vocab: int, tokens: torch.Tensor, pos: torch.Tensor,
+                      part: torch.Tensor, sample_begin: int = 1, no_repeat_ngram: int = 0,
+                      suppress: Optional[torch.Tensor] = None, stream=None) -> None:
+    """decode_tail over one column shard of the vocab head: logits [m][n] hold the
+    global token ids [h0, h0 + n) for all m rows of the job; tokens [m][max_len] and
+    pos [m] are the rows' shared history (read only).  Writes part [m][4] f32 =
+    (max, global index as u32 bits, exp sum against the max, 0) per row."""
+    if logits.dim() != 2 or logits.dtype != torch.float32 or not logits.is_contiguous():
+        raise ValueError("logits must be a contiguous f32 [m][n] tensor")
+    m, n = logits.shape
+    if tokens.dim() != 2 or tokens.shape[0] != m or not tokens.is_contiguous() or pos.numel() != m:
+        raise ValueError("tokens must be a contiguous [m][max_len] tensor and pos hold one position per row")
+    if part.dtype != torch.float32 or tuple(part.shape) != (m, 4) or not part.is_contiguous():
+        raise ValueError("part must be a contiguous f32 [m][4] tensor")
+    max_len = tokens.shape[1]
+    nsup = 0 if suppress is None else suppress.numel()
+    rc = _lib.load().madi_shard_decode_tail(logits.data_ptr(), m, n, int(h0), int(vocab), tokens.data_ptr(), max_len,
+                                            max_len, pos.data_ptr(), int(sample_begin), int(no_repeat_ngram),
+                                            None if suppress is None else suppress.data_ptr(), nsup, part.data_ptr(),
+                                            _stream(stream))
+    _lib.check(rc, "madi_shard_decode_tail")
+
+
+def merge_shard_tail(parts: torch.Tensor, tokens: torch.Tensor, pos: torch.Tensor,
+                     conf: Optional[torch.Tensor] = None, stream=None) -> None:
+    """The rest of decode_tail from the all-gathered shard parts [world][m][4]:
+    pos[row] += 1, tokens[row][pos[row]] and conf[row][pos[row]] written."""
+    if parts.dim() != 3 or parts.shape[2] != 4 or parts.dtype != torch.float32 or not parts.is_contiguous():
+        raise ValueError("parts must be a contiguous f32 [world][m][4] tensor")
+    world, m, _ = parts.shape
+    if tokens.dim() != 2 or tokens.shape[0] != m or not tokens.is_contiguous() or pos.numel() != m:
+        raise ValueError("tokens must be a contiguous [m][max_len] tensor and pos hold one position per row")
+    if conf is not None and (conf.shape != tokens.shape or conf.dtype != torch.float32 or not conf.is_contiguous()):
+        raise ValueError("conf must be f32 shaped like tokens")
+    max_len = tokens.shape[1]
+    rc = _lib.load().madi_merge_shard_tail(parts.data_ptr(), world, m, tokens.data_ptr(), max_len, max_len,
+                                           pos.data_ptr(), None if conf is None else conf.data_ptr(), _stream(stream))
+    _lib.check(rc, "madi_merge_shard_tail")

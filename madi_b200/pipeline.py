@@ -15,7 +15,7 @@ order does not depend on M, attention runs per chunk / slot, and the decode
 kernels treat token slots independently, so a chunk's tokens do not depend on
 which batch it was decoded in.
 """
-from typing import Optional
+from typing import Optional, Tuple
 
 import numpy as np
 import torch
@@ -38,12 +38,22 @@ def synthetic_mel(chunks: int, first: int = 0) -> np.ndarray:
 
 
 class Transcriber:
-    def __init__(self, slots: int = 8, enc_layers: int = 32, tokens: int = 224, seed: int = 1, device="cuda"):
+    def __init__(self, slots: int = 8, enc_layers: int = 32, tokens: int = 224, seed: int = 1, device="cuda",
+                 split: Optional[Tuple[int, int]] = None, act16: Optional[bool] = None):
+        """split: (world, rank) -- the decoder's vocab head column-split over the
+        ranks of the default process group (one process per GPU), its logits
+        exchanged by NCCL all-gathers inside the captured token step.  Every rank
+        must then decode the same number of batches (the collectives pair up step by
+        step).  act16: the decoder projections on f16-rounded activations (default:
+        when there is more than one slot or the head is split, as the reference's
+        batched decode)."""
         if tokens < 1 or tokens + 1 > dec.MAX_TOK:
             raise ValueError(f"1..{dec.MAX_TOK - 1} tokens per chunk")
         self.encoder = enc.Encoder(enc_layers, seed, device)
-        # more than one slot: the reference's batched decode, f16 activations
-        self.decoder = dec.Decoder(dec.device_weights(seed, device), slots, device, act16=slots > 1)
+        if act16 is None:
+            act16 = slots > 1 or split is not None
+        self.decoder = dec.Decoder(dec.device_weights(seed, device), slots, device, act16=act16, split=split)
+        self.split = split
         self.slots, self.tokens = slots, tokens
         self.eot = torch.tensor([EOT], dtype=torch.int32, device=device)
         self.graph = None
@@ -54,7 +64,8 @@ class Transcriber:
         d.step(suppress=self.eot)               # eager first step: module load, one-time attributes
         torch.cuda.synchronize()
         g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
+        # thread-local capture mode: NCCL's calls in the split head's step are legal
+        with torch.cuda.graph(g, capture_error_mode="thread_local"):
             d.step(suppress=self.eot)
         torch.cuda.synchronize()
         self.graph = g
