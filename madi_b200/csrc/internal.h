@@ -76,16 +76,6 @@ bool gemv_tile_ok(int M, int N, int K, bool x_f32, int num_sms);
 cudaError_t launch_gemv_tile(const GemvArgs &a, bool x_f32, bool y_f32, int epi, bool qkv, int num_sms, int *dev_err,
                              cudaStream_t st, bool pdl, bool x_r16 = false);
 
-// One warp per 8-row unit over the whole of K (q8_gemv_rows.cu): K % 256 == 0, K <=
-// 1280, M <= 16 (f16 or rounded f32 x) or M <= 8 (f32 x); 16-byte aligned qs,
-// scales and x.  Same arithmetic and epilogues as launch_gemv_tile.
-bool gemv_rows_ok(int M, int N, int K, bool x_f32);
-cudaError_t launch_gemv_rows(const GemvArgs &a, bool x_f32, bool y_f32, int epi, bool qkv, int num_sms,
-                             int *dev_err, cudaStream_t st, bool pdl, bool x_r16 = false);
-// Whether the streaming path takes the row-unit kernel for this shape (MADI_GEMV_ROWS
-// = 0 turns it off, 1 takes it wherever it applies).
-bool gemv_use_rows(int M, int N, int K, bool x_f32_split);
-
 // ---------------------------------------------------------------- variant (a)
 struct GemmArgs {
     const __half *x;         // [M][K] f16

@@ -192,10 +192,7 @@ int q8_linear_impl(const madi_q8w *w, const void *x, int x_dtype, int m, const v
     a.bias_f16 = bias_dtype == MADI_F16;
     a.N = N; a.K = K; a.M = m;
     a.ks = ks;
-    const bool rows_path = tile_path && aligned(x, 16) && gemv_use_rows(m, N, K, xf32 && !x_r16);
-    cudaError_t e = rows_path ? launch_gemv_rows(a, xf32, y_dtype == MADI_F32, epi, false, S.num_sms, S.dev_err, st,
-                                                 S.pdl, x_r16)
-                    : tile_path
+    cudaError_t e = tile_path
                         ? launch_gemv_tile(a, xf32, y_dtype == MADI_F32, epi, false, S.num_sms, S.dev_err, st, S.pdl,
                                            x_r16)
                         : launch_gemv(a, xf32, y_dtype == MADI_F32, epi, false, st, S.pdl);
@@ -227,12 +224,9 @@ int q8_qkv_impl(const madi_q8w *w, const float *x, int m, const float *qb, const
     a.qb = qb; a.vb = vb; a.kc = kc; a.vc = vc; a.pos = pos;
     a.cache_stride = m > 1 ? cache_stride : 0;
     a.D = D;
-    const bool rows_path = tile_path && gemv_use_rows(m, 3 * D, D, !x_r16);
-    cudaError_t e = rows_path ? launch_gemv_rows(a, true, true, MADI_EPI_NONE, true, S.num_sms, S.dev_err, st, S.pdl,
+    cudaError_t e = tile_path ? launch_gemv_tile(a, true, true, MADI_EPI_NONE, true, S.num_sms, S.dev_err, st, S.pdl,
                                                  x_r16)
-                    : tile_path ? launch_gemv_tile(a, true, true, MADI_EPI_NONE, true, S.num_sms, S.dev_err, st, S.pdl,
-                                                   x_r16)
-                                : launch_gemv(a, true, true, MADI_EPI_NONE, true, st, S.pdl);
+                              : launch_gemv(a, true, true, MADI_EPI_NONE, true, st, S.pdl);
     if (e == cudaErrorNotSupported) return fail(MADI_EUNSUPPORTED, "%s: cuTensorMapEncodeTiled unavailable", who);
     if (e != cudaSuccess) return cuda_fail(e, who);
     return MADI_OK;
