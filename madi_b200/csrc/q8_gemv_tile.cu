@@ -361,9 +361,10 @@ __global__ void __launch_bounds__(kThreads, 2)
         // is met by all 256 consumer threads each time, also after a bounded wait
         // gave up; each warp waited for a stage's previous round itself, so the
         // parity waits are unambiguous.
-        for (int n = 0, tile = cl; tile < tiles; ++n, tile += clusters) {
-            const int s = n % stages;
-            const uint32_t ph = (uint32_t)(n / stages) & 1u;
+        int s = 0;                                          // stage and parity of unit n, division-free
+        uint32_t ph = 0;
+        for (int n = 0, tile = cl; tile < tiles; ++n, tile += clusters, s = (s + 1 == stages) ? 0 : s + 1,
+                 ph ^= (s == 0) ? 1u : 0u) {
             if (alive) alive = warp_wait_all(&bars->full[s], ph, abort_flag, dev_err);
             float acc[kG][4];
 #pragma unroll

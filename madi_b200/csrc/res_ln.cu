@@ -6,7 +6,8 @@
 //   layer_norm_f16  (encoder_ops.metal:305-331): the same without the residual add.
 //   bias_res_ln / layer_norm (encoder_ops.metal:14-120, the decoder's forms): MO
 //       and Y in f32.
-//   mean = sum(X[r]) / D, inv = rsqrt(sum((X[r] - mean)^2) / D + eps) (two passes).
+//   mean = sum(X[r]) / D, inv = rsqrt(sum((X[r] - mean)^2) / D + eps) (two passes;
+//   the row arithmetic of ln_row.cuh).
 //
 // HBM-bound row kernel: one warp per row, the row held in registers (D / 128
 // float4 per lane, D <= 2048) so the residual update, both reduction passes and
@@ -18,18 +19,13 @@
 
 #include "common.cuh"
 #include "internal.h"
+#include "ln_row.cuh"
 
 namespace madi {
 namespace {
 
 constexpr int kRowsPerCta = 8;
 constexpr int kMaxChunks = kLnMaxD / 128;
-
-MADI_DEV float warp_sum(float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
-}
 
 template <typename T> MADI_DEV float4 ld4f(const T *p);
 template <> MADI_DEV float4 ld4f<float>(const float *p) { return *reinterpret_cast<const float4 *>(p); }
@@ -75,7 +71,6 @@ __global__ void __launch_bounds__(32 * kRowsPerCta) res_ln_kernel(float *__restr
     if (row >= rows) return;   // whole warps only
     float *xr = X + (size_t)row * D;
     float4 v[C];
-    float s = 0.f;
 #pragma unroll
     for (int c = 0; c < C; ++c) {
         if (c < nch) {
@@ -93,19 +88,8 @@ __global__ void __launch_bounds__(32 * kRowsPerCta) res_ln_kernel(float *__restr
             v[c] = x;
         }
     }
-#pragma unroll
-    for (int c = 0; c < C; ++c)
-        if (c < nch) s += (v[c].x + v[c].y) + (v[c].z + v[c].w);
-    const float mean = warp_sum(s) / (float)D;
-    float q = 0.f;
-#pragma unroll
-    for (int c = 0; c < C; ++c) {
-        if (c < nch) {
-            const float a = v[c].x - mean, b = v[c].y - mean, cc = v[c].z - mean, d = v[c].w - mean;
-            q += (a * a + b * b) + (cc * cc + d * d);
-        }
-    }
-    const float inv = rsqrtf(warp_sum(q) / (float)D + eps);
+    float mean, inv;
+    ln_row_stats<C>(v, nch, D, eps, mean, inv);
     YT *yr = Y + (size_t)row * D;
 #pragma unroll
     for (int c = 0; c < C; ++c) {
@@ -119,8 +103,8 @@ __global__ void __launch_bounds__(32 * kRowsPerCta) res_ln_kernel(float *__restr
                 gg = *reinterpret_cast<const float4 *>(gamma + i);
                 bb = *reinterpret_cast<const float4 *>(beta + i);
             }
-            st4f(yr + i, (v[c].x - mean) * inv * gg.x + bb.x, (v[c].y - mean) * inv * gg.y + bb.y,
-                 (v[c].z - mean) * inv * gg.z + bb.z, (v[c].w - mean) * inv * gg.w + bb.w);
+            st4f(yr + i, ln_apply(v[c].x, mean, inv, gg.x, bb.x), ln_apply(v[c].y, mean, inv, gg.y, bb.y),
+                 ln_apply(v[c].z, mean, inv, gg.z, bb.z), ln_apply(v[c].w, mean, inv, gg.w, bb.w));
         }
     }
 }
