@@ -74,7 +74,9 @@ def parse():
                     help="long-audio leg: run each batch's encoder and decoder back to back on one stream")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     # --case KIND: one op of one shape on cuda:0 (see run_case), instead of the benchmark
-    ap.add_argument("--case", choices=["gemv", "gemm", "cross", "self", "flash", "decoder"])
+    ap.add_argument("--case", choices=["gemv", "gemm", "cross", "self", "flash", "decoder", "enclayer"])
+    ap.add_argument("--unfused", action="store_true",
+                    help="--case enclayer: residual adds in separate bias_res_ln_f16 kernels")
     ap.add_argument("--m", type=int, default=8)
     ap.add_argument("--n", type=int, default=1280)
     ap.add_argument("--k", type=int, default=1280)
@@ -432,14 +434,13 @@ def main_madi(args, world, rank, local):
         gx = torch.Generator(device=dev)
         gx.manual_seed(55 + rank)
         xl = torch.randn((EB * enc_mod.SEQ, D), device=dev, generator=gx)
-        pf = (torch.randn((EB * enc_mod.SEQ, D), device=dev, generator=gx) * 0.5).half()
         with torch.cuda.stream(stream):
             for _ in range(2):
-                layer.forward(xl, pf, layer.b2, stream=stream)
+                layer.forward_fused(xl, stream=stream)
             torch.cuda.synchronize()
             gl = torch.cuda.CUDAGraph()
             with torch.cuda.graph(gl, stream=stream, capture_error_mode="thread_local"):
-                layer.forward(xl, pf, layer.b2, stream=stream)
+                layer.forward_fused(xl, stream=stream)
             gl.replay()
             torch.cuda.synchronize()
             nl = 10
@@ -452,10 +453,34 @@ def main_madi(args, world, rank, local):
         ms_layer = max_over_ranks(world, l0.elapsed_time(l1) / nl)
         fl = enc_mod.EncoderLayer.flops(EB)
         enc_layer = {"chunks_per_gpu": EB, "ms_per_layer": ms_layer, "TFLOPs": fl / (ms_layer / 1e3) / 1e12,
-                     "flops_per_layer": fl,
-                     "encoder_32_layers_chunks_per_s": EB * world / (32 * ms_layer / 1e3),
-                     "note": "derived: 32 x one measured layer; conv stem and positional embedding not included"}
-        del gl, layer, xl, pf
+                     "flops_per_layer": fl, "residual": "fused into the out-projection / fc2 epilogues"}
+        del gl, layer, xl
+        torch.cuda.empty_cache()
+        # the whole encoder, measured: synthetic log-mel of EB chunks
+        # resident in HBM -> conv stem, positions, 32 Q8 layers, ln_post; eager launches
+        # as in the pipeline, best of 3 passes after one untimed pass
+        from madi_b200 import pipeline
+        encoder = enc_mod.Encoder(32, seed=1, device=dev)
+        mel = torch.from_numpy(pipeline.synthetic_mel(EB, first=1000 * rank)).to(dev)
+        with torch.cuda.stream(stream):
+            encoder.forward(mel, stream=stream)
+            torch.cuda.synchronize()
+            best = None
+            for _ in range(3):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                encoder.forward(mel, stream=stream)
+                e1.record(stream)
+                torch.cuda.synchronize()
+                best = e0.elapsed_time(e1) if best is None else min(best, e0.elapsed_time(e1))
+        ms_enc = max_over_ranks(world, best)
+        enc_layer["encoder_32_layers"] = {"chunks_per_gpu": EB, "ms_per_batch": ms_enc,
+                                          "chunks_per_s": EB * world / (ms_enc / 1e3),
+                                          "layer_TFLOPs": encoder.flops(EB) / (ms_enc / 1e3) / 1e12,
+                                          "note": "measured: conv stem (PyTorch f16 conv1d, one call per chunk), "
+                                                  "positions, 32 Q8 layers, ln_post; TFLOP/s over the layers' "
+                                                  "FLOPs"}
+        del encoder, mel
         torch.cuda.empty_cache()
 
     # ---------------- e2e through the public API with host buffers
@@ -994,6 +1019,7 @@ def run_case(a):
         python bench.py --case self --m 8 --n 448 --k 1280 --iters 6      (slots, cache rows, kv_dim)
         python bench.py --case flash --m 8 --n 1500 --k 1280 --iters 6    (chunks, seq, heads*64)
         python bench.py --case decoder --m 15 --n 112 --k 1280 --iters 6  (slots, tokens decoded first, d)
+        python bench.py --case enclayer --m 8 --iters 6                   (chunks; --unfused: separate res-LN)
 
     Inputs are seeded random tensors of the given shape (int8 weights in [-127, 127],
     f16 scales in [1e-4, 2.1e-3], N(0,1) activations); prints the mean device time
@@ -1012,6 +1038,8 @@ def run_case(a):
         return flash_case(a, dev, g)
     if a.kind == "decoder":
         return decoder_case(a, dev)
+    if a.kind == "enclayer":
+        return enclayer_case(a, dev)
     W = q8.Q8Weight(torch.randint(-127, 128, (a.n, a.k), dtype=torch.int8, device=dev, generator=g),
                     (torch.rand((a.n, a.k // 32), device=dev, generator=g) * 2e-3 + 1e-4).half())
     xdt = torch.float32 if a.x == "f32" else torch.float16
@@ -1099,6 +1127,37 @@ def flash_case(a, dev, g):
         ts.append(e0.elapsed_time(e1) * 1e3)
     print(f"flash attention chunks={a.m} seq={a.n} heads={heads}: mean {sum(ts) / len(ts):.2f} us, min {min(ts):.2f} us, "
           f"{flops / min(ts) / 1e6:.1f} TFLOP/s at the min over {len(ts)} calls (after one untimed call)")
+
+
+def enclayer_case(a, dev):
+    """One encoder layer at --m chunks of 1500 frames: forward_fused (residual adds in
+    the GEMM epilogues) or, with --unfused, forward + bias_res_ln_f16; eager launches,
+    --iters timed passes."""
+    import torch
+    from madi_b200 import encoder as enc
+    layer = enc.EncoderLayer(enc.host_layer(seed=1), device=dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(3)
+    x = torch.randn((a.m * enc.SEQ, enc.D), device=dev, generator=g)
+    pf = (torch.randn((a.m * enc.SEQ, enc.D), device=dev, generator=g) * 0.5).half()
+
+    def run():
+        if a.unfused:
+            layer.forward(x, pf, layer.b2)
+        else:
+            layer.forward_fused(x)
+    run()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(a.iters):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        run()
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1) * 1e3)
+    print(f"encoder layer chunks={a.m} {'unfused' if a.unfused else 'fused'}: mean {sum(ts) / len(ts):.1f} us, "
+          f"min {min(ts):.1f} us over {len(ts)} passes")
 
 
 def decoder_case(a, dev):

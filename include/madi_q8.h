@@ -182,8 +182,11 @@ int   madi_num_sms(void);
  * decoder.zig:337-341).  One call, no dequant scratch:
  *   m > 16 (or 9..16 when K % 256 != 0): tcgen05 tensor-core GEMM, X f16, Y f16,
  *           residual f16 (Y f32 is accepted with MADI_EPI_NONE: unrounded f32
- *           sums, e.g. the logits of a vocab head over many token slots); f16
- *           dequantised weights, f32 accumulation.
+ *           sums, e.g. the logits of a vocab head over many token slots; and with
+ *           MADI_EPI_BIAS_RES and an f32 residual: Y = (residual + half(acc)) +
+ *           bias, the encoder's f32 residual stream updated in the epilogue -- the
+ *           add of bias_res_ln_f16, encoder_ops.metal:343-347, on the f16 projection
+ *           output; residual may be Y); f16 dequantised weights, f32 accumulation.
  *   m <= 16: bandwidth-bound skinny GEMM, X f32, f16 or MADI_F32_AS_F16, Y f32 or f16,
  *           residual with Y's type and may alias Y; f32 semantics
  *           (exact int8 weights, per-block f32 scale).  (The reference's GEMV

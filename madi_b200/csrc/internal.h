@@ -46,6 +46,11 @@ enum : int { kEpiNone = 0, kEpiBias = 1, kEpiBiasGelu = 2, kEpiBiasRes = 3 };
 // Tensor-core path only: no epilogue, f32 output (logits of a vocab head with
 // more than 8 token slots).
 constexpr int kEpiNoneF32 = 4;
+// Tensor-core path only: the encoder's f32 residual stream updated in place,
+// y[m][n] = (r[m][n] + float(half(acc))) + bias[n] with r, y f32 (r may be y) --
+// the residual add of bias_res_ln_f16 (encoder_ops.metal:343-347) on the f16
+// projection output the reference's GEMM writes, moved into the GEMM's epilogue.
+constexpr int kEpiResF32 = 5;
 
 // ---------------------------------------------------------------- variant (b)
 struct GemvArgs {
@@ -82,8 +87,8 @@ struct GemmArgs {
     const int8_t *qs;        // [N][K]
     const __half *scales;    // [N][K/32]
     const void *bias;        // [N] f32 or f16
-    const __half *residual;  // [M][N] f16
-    __half *y;               // [M][N] f16 (f32 for kEpiNoneF32)
+    const void *residual;    // [M][N] f16 (f32 for kEpiResF32)
+    __half *y;               // [M][N] f16 (f32 for kEpiNoneF32 / kEpiResF32)
     int M, N, K;
     int bias_f16;
     int *dev_err;            // device error word (bounded-wait expiry)

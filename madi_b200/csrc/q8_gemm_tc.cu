@@ -119,11 +119,27 @@ MADI_DEV void epilogue_chunk(const GemmArgs &p, const uint32_t (&v)[32], int mb,
             if (mb + i < p.M) yf[base + (size_t)i * N] = __uint_as_float(v[i]);
         return;
     }
+    if constexpr (EPI == kEpiResF32) {
+        // x += half(acc) + bias in the reference's order ((x + mo) + bias); the
+        // residual reads of the chunk are issued together before the stores
+        float *yf = reinterpret_cast<float *>(p.y);
+        const float *rf = reinterpret_cast<const float *>(p.residual);
+        const int nr = p.M - mb < 32 ? p.M - mb : 32;
+        float r[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) r[i] = i < nr ? rf[base + (size_t)i * N] : 0.f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            const float mo = __half2float(__float2half_rn(__uint_as_float(v[i])));
+            if (i < nr) yf[base + (size_t)i * N] = __fadd_rn(__fadd_rn(r[i], mo), bias);
+        }
+        return;
+    }
     if (mb + 32 <= p.M) {
         float res[32];
         if constexpr (EPI == kEpiBiasRes) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) res[i] = __half2float(p.residual[base + (size_t)i * N]);
+            for (int i = 0; i < 32; ++i) res[i] = __half2float(static_cast<const __half *>(p.residual)[base + (size_t)i * N]);
         }
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
@@ -140,7 +156,8 @@ MADI_DEV void epilogue_chunk(const GemmArgs &p, const uint32_t (&v)[32], int mb,
                 float y = __uint_as_float(v[i]);
                 if constexpr (EPI == kEpiBias) y += bias;
                 if constexpr (EPI == kEpiBiasGelu) y = gelu_erf(y + bias);
-                if constexpr (EPI == kEpiBiasRes) y = y + bias + __half2float(p.residual[base + (size_t)i * N]);
+                if constexpr (EPI == kEpiBiasRes)
+                    y = y + bias + __half2float(static_cast<const __half *>(p.residual)[base + (size_t)i * N]);
                 p.y[base + (size_t)i * N] = __float2half_rn(y);
             }
         }
@@ -158,7 +175,8 @@ MADI_DEV void epilogue_chunk_stage(const GemmArgs &p, const uint32_t (&v)[32], i
         const size_t base = (size_t)mb * p.N + n;
 #pragma unroll
         for (int i = 0; i < 32; ++i)
-            res[i] = (nok && mb + i < p.M) ? __half2float(p.residual[base + (size_t)i * p.N]) : 0.f;
+            res[i] = (nok && mb + i < p.M) ? __half2float(static_cast<const __half *>(p.residual)[base + (size_t)i * p.N])
+                                           : 0.f;
     }
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
@@ -174,7 +192,7 @@ MADI_DEV void epilogue_chunk_stage(const GemmArgs &p, const uint32_t (&v)[32], i
 // read.  The residual epilogue keeps direct stores and the smaller shared-memory
 // footprint: measured faster for fc2, whose scale reads profit from the larger
 // L1 left beside it.
-template <int EPI> constexpr bool kStagedY = EPI != kEpiBiasRes && EPI != kEpiNoneF32;
+template <int EPI> constexpr bool kStagedY = EPI != kEpiBiasRes && EPI != kEpiNoneF32 && EPI != kEpiResF32;
 template <int BT, int EPI> constexpr size_t gemm_smem() {
     return Cfg<BT>::SMEM_BASE + (kStagedY<EPI> ? Y_STAGE_BYTES : 0);
 }
@@ -445,7 +463,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int n = n0 + r;
             const bool nok = n < N;
             float bias = 0.f;
-            if constexpr (EPI != kEpiNone && EPI != kEpiNoneF32) {
+            if constexpr (EPI != kEpiNone && EPI != kEpiNoneF32) {      // kEpiResF32 has a bias
                 if (nok)
                     bias = p.bias_f16 ? __half2float(reinterpret_cast<const __half *>(p.bias)[n])
                                       : reinterpret_cast<const float *>(p.bias)[n];
@@ -813,7 +831,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const int n = n0 + r;
             const bool nok = n < N;
             float bias = 0.f;
-            if constexpr (EPI != kEpiNone && EPI != kEpiNoneF32) {
+            if constexpr (EPI != kEpiNone && EPI != kEpiNoneF32) {      // kEpiResF32 has a bias
                 if (nok)
                     bias = p.bias_f16 ? __half2float(reinterpret_cast<const __half *>(p.bias)[n])
                                       : reinterpret_cast<const float *>(p.bias)[n];
@@ -956,7 +974,7 @@ cudaError_t launch_gemm_tc(const GemmArgs &a, int epi, int num_sms, cudaStream_t
     // Output through staged TMA stores when the row pitch allows a tensor map
     // (N * 2 bytes a multiple of 16); otherwise the epilogue stores directly.
     CUtensorMap tmY;
-    int ystore = epi != kEpiNoneF32 && a.N % 8 == 0 && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0 &&
+    int ystore = epi != kEpiNoneF32 && epi != kEpiResF32 && a.N % 8 == 0 && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0 &&
                  make_map(&tmY, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.y, (uint64_t)a.N, (uint64_t)a.M,
                           (uint64_t)a.N * 2, BN, Y_ROWS, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (!ystore) memset(&tmY, 0, sizeof(tmY));
@@ -967,6 +985,7 @@ cudaError_t launch_gemm_tc(const GemmArgs &a, int epi, int num_sms, cudaStream_t
             case kEpiBiasGelu: return launch_pair<kPairTokens, kEpiBiasGelu>(a, tmX, tmW, tmY, ystore, num_sms, st);
             case kEpiBiasRes: return launch_pair<kPairTokens, kEpiBiasRes>(a, tmX, tmW, tmY, ystore, num_sms, st);
             case kEpiNoneF32: return launch_pair<kPairTokens, kEpiNoneF32>(a, tmX, tmW, tmY, 0, num_sms, st);
+            case kEpiResF32: return launch_pair<kPairTokens, kEpiResF32>(a, tmX, tmW, tmY, 0, num_sms, st);
             default: return cudaErrorInvalidValue;
         }
     }
@@ -977,6 +996,7 @@ cudaError_t launch_gemm_tc(const GemmArgs &a, int epi, int num_sms, cudaStream_t
         case kEpiBiasGelu: return launch_bt<BT, kEpiBiasGelu>(a, tmX, tmW, tmY, ystore, num_sms, st); \
         case kEpiBiasRes: return launch_bt<BT, kEpiBiasRes>(a, tmX, tmW, tmY, ystore, num_sms, st);   \
         case kEpiNoneF32: return launch_bt<BT, kEpiNoneF32>(a, tmX, tmW, tmY, 0, num_sms, st);       \
+        case kEpiResF32: return launch_bt<BT, kEpiResF32>(a, tmX, tmW, tmY, 0, num_sms, st);         \
         default: return cudaErrorInvalidValue;                                                    \
     }
     if (bt == 192) { MADI_GEMM_EPI(192) }

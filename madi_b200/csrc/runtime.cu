@@ -157,11 +157,11 @@ int q8_linear_impl(const madi_q8w *w, const void *x, int x_dtype, int m, const v
                                  "16-byte aligned x and scales)", who, kGemvMaxM);
     if (m >= kGemmMinM && !tile_fits) {
         const bool y32 = y_dtype == MADI_F32;
-        if (x_dtype != MADI_F16 || (y32 && epi != MADI_EPI_NONE))
+        if (x_dtype != MADI_F16 || (y32 && epi != MADI_EPI_NONE && epi != MADI_EPI_BIAS_RES))
             return fail(MADI_EINVAL, "%s: the tensor-core path (m > 8) takes f16 x, and f16 y (f32 y without an "
-                                     "epilogue)", who);
+                                     "epilogue, or with the f32 residual stream)", who);
         if (!aligned(x, 16)) return fail(MADI_EINVAL, "%s: x must be 16-byte aligned", who);
-        if (!aligned(y, y32 ? 4 : 2) || (residual && !aligned(residual, 2)))
+        if (!aligned(y, y32 ? 4 : 2) || (residual && !aligned(residual, y32 ? 4 : 2)))
             return fail(MADI_EINVAL, "%s: misaligned y", who);
         GemmArgs a{};
         a.x = static_cast<const __half *>(x);
@@ -169,11 +169,12 @@ int q8_linear_impl(const madi_q8w *w, const void *x, int x_dtype, int m, const v
         a.scales = reinterpret_cast<const __half *>(w->scales);
         a.bias = bias;
         a.bias_f16 = bias_dtype == MADI_F16;
-        a.residual = static_cast<const __half *>(residual);
+        a.residual = residual;
         a.y = static_cast<__half *>(y);
         a.M = m; a.N = N; a.K = K;
         a.dev_err = S.dev_err;
-        cudaError_t e = launch_gemm_tc(a, y32 ? kEpiNoneF32 : epi, S.num_sms, st);
+        cudaError_t e = launch_gemm_tc(a, y32 ? (epi == MADI_EPI_BIAS_RES ? kEpiResF32 : kEpiNoneF32) : epi, S.num_sms,
+                                       st);
         if (e == cudaErrorNotSupported) return fail(MADI_EUNSUPPORTED, "%s: cuTensorMapEncodeTiled unavailable", who);
         if (e != cudaSuccess) return cuda_fail(e, who);
         return MADI_OK;

@@ -14,6 +14,13 @@ One layer, in the reference's order (encoder.zig:235-315, encoder_ops.metal:305-
 
 x is the f32 residual stream [chunks * 1500][1280]; weights are seeded random Q8.
 
+forward_fused runs the same layer with the residual adds inside the GEMMs (the
+bias_res_ln fusion of the reference's encoder_ops.metal:305-364): the out-projection
+and fc2 epilogues update x in place, x += half(acc) + bias in f32 -- the f16
+projection output the reference writes, added in its order -- so no f16 projection
+output goes through memory and each LayerNorm is a plain one (layer_norm_f16).  The
+residual stream and every LayerNorm output are bit-identical to forward's.
+
 Encoder puts the whole large-v3-turbo encoder together (config 3): the conv stem
 (conv1d 128 -> 1280, k 3, GELU; conv1d 1280 -> 1280, k 3, stride 2, GELU) on f16
 weights as the reference keeps them (transcribe.zig:1099-1102), through PyTorch's
@@ -99,6 +106,18 @@ class EncoderLayer:
         h = q8.linear(self.fc1, y2, bias=self.b1, epi=q8.EPI_BIAS_GELU, **s)
         return q8.linear(self.fc2, h, **s)
 
+    def forward_fused(self, x: torch.Tensor, seq: int = SEQ, stream=None) -> None:
+        """x f32 [chunks * seq][1280], the residual stream with the previous layer's
+        fc2 output and bias already added; updated in place to include this layer's."""
+        s = dict(stream=stream)
+        y = q8.layer_norm_f16(x, *self.ln1, eps=EPS, **s)
+        qkv = q8.linear(self.qkv, y, bias=self.bqkv, **s)
+        a = attn.flash_attn_enc(qkv[:, :D], qkv[:, D:2 * D], qkv[:, 2 * D:], HEADS, seq, **s)
+        q8.linear(self.o, a, bias=self.bo, epi=q8.EPI_BIAS_RES, residual=x, out=x, **s)
+        y2 = q8.layer_norm_f16(x, *self.ln2, eps=EPS, **s)
+        h = q8.linear(self.fc1, y2, bias=self.b1, epi=q8.EPI_BIAS_GELU, **s)
+        q8.linear(self.fc2, h, bias=self.b2, epi=q8.EPI_BIAS_RES, residual=x, out=x, **s)
+
     @staticmethod
     def flops(chunks: int) -> float:
         """Algorithmic FLOPs of one layer: the four projections and the attention."""
@@ -120,7 +139,11 @@ class Encoder:
     """The whole encoder: conv stem, positions, `layers` encoder layers, ln_post."""
     N_MELS, FRAMES = 128, 3000
 
-    def __init__(self, layers: int = 32, seed: int = 1, device="cuda"):
+    def __init__(self, layers: int = 32, seed: int = 1, device="cuda", fuse_res: bool = True):
+        """fuse_res: the residual adds inside the out-projection / fc2 GEMMs
+        (EncoderLayer.forward_fused); False runs the separate bias_res_ln_f16 kernels
+        (the same results, bit for bit)."""
+        self.fuse_res = fuse_res
         g = torch.Generator(device=device)
         g.manual_seed(seed * 7919)
         self.c1w = (torch.randn((D, self.N_MELS, 3), device=device, generator=g) / math.sqrt(3 * self.N_MELS)).half()
@@ -140,6 +163,10 @@ class Encoder:
             # one chunk per convolution call: the library picks its algorithm by shape,
             # so a chunk's stem output does not depend on how many chunks share a batch
             x[c * SEQ:(c + 1) * SEQ] = self.stem(mel[c:c + 1])[0]
+        if self.fuse_res:
+            for L in self.layers:
+                L.forward_fused(x, stream=stream)
+            return q8.layer_norm_f16(x, *self.ln_post, eps=EPS, stream=stream).view(B, SEQ, D)
         f, b2 = None, None
         for L in self.layers:
             f, b2 = L.forward(x, f, b2, stream=stream), L.b2

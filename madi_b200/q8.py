@@ -66,7 +66,9 @@ def linear(w: Q8Weight, x: torch.Tensor, bias: Optional[torch.Tensor] = None, ep
     projects f16 activations); streaming path only (m <= 16, K % 256 == 0).
     epi defaults to BIAS when a bias is given, BIAS_RES when a residual is given.
     m <= 16 runs the decode skinny GEMM (when K % 256 == 0, else m <= 8), larger m
-    the tcgen05 GEMM."""
+    the tcgen05 GEMM.  On the tcgen05 GEMM, BIAS_RES with f32 out and residual is the
+    encoder's residual stream: out = (residual + half(acc)) + bias (residual may be
+    out, updated in place)."""
     if x.dim() != 2 or x.shape[1] != w.k:
         raise ValueError(f"x {tuple(x.shape)} vs weight k={w.k}")
     if not x.is_contiguous():

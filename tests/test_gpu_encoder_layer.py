@@ -48,3 +48,30 @@ def test_encoder_layer_composition(madi, oracle):
     fr = f.float().cpu().numpy()
     rms = np.sqrt(np.mean(f_exact ** 2))
     assert np.abs(fr - f_exact).max() <= 1e-2 * rms, f"fc2 output: {np.abs(fr - f_exact).max() / rms:.3e} x RMS"
+
+
+def test_fused_residual_layer_equals_separate_kernels(madi):
+    """forward_fused (residual adds in the out-projection / fc2 epilogues, plain
+    LayerNorms) against forward + bias_res_ln_f16: the residual stream and the
+    LayerNorm outputs bit for bit, over two chained layers and ln_post; and the
+    whole Encoder (stem, 2 layers, ln_post) the same in both modes."""
+    import torch
+    from madi_b200 import encoder as enc, pipeline, q8
+    seq, chunks, D = 300, 2, enc.D
+    L1, L2 = enc.EncoderLayer(enc.host_layer(seed=4)), enc.EncoderLayer(enc.host_layer(seed=5))
+    g = np.random.default_rng(9)
+    x = g.standard_normal((chunks * seq, D)).astype(np.float32)
+    xa, xb = _t(x), _t(x)
+    f1 = L1.forward(xa, None, None, seq=seq)
+    f2 = L2.forward(xa, f1, L1.b2, seq=seq)
+    ya = q8.bias_res_ln_f16(xa, f2, L2.b2, *L1.ln1, eps=enc.EPS)
+    L1.forward_fused(xb, seq=seq)
+    L2.forward_fused(xb, seq=seq)
+    yb = q8.layer_norm_f16(xb, *L1.ln1, eps=enc.EPS)
+    torch.cuda.synchronize()
+    assert torch.equal(xa, xb), "residual stream differs"
+    assert torch.equal(ya, yb), "LayerNorm output differs"
+    mel = torch.from_numpy(pipeline.synthetic_mel(1, first=3)).cuda()
+    outs = [enc.Encoder(layers=2, seed=6, fuse_res=f).forward(mel) for f in (True, False)]
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1]), "encoder states differ between the fused and separate forms"

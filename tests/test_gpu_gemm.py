@@ -155,3 +155,33 @@ def test_f32_output_without_epilogue(madi, oracle, M, N):
     err = np.abs(y.cpu().numpy().astype(np.float64) - y_exact).max()
     rms = np.sqrt(np.mean(y_exact ** 2))
     assert err <= 1e-4 * rms, f"M={M} N={N}: max err {err:.3e} vs rms {rms:.3e}"
+
+
+@pytest.mark.parametrize("M,N,K", [(1500, 1280, 1280), (3000, 1280, 5120), (333, 160, 96)])
+def test_f32_residual_stream_epilogue(madi, oracle, M, N, K):
+    """f32 out + BIAS_RES + f32 residual on the tensor-core path: the encoder's residual
+    stream x += half(acc) + bias in place (the add of bias_res_ln_f16 moved into the
+    GEMM).  x must equal (x + f16(acc)) + bias with the f16 rounding of the projection
+    as the only approximation: max error beyond the half-ulp of the f16 projection
+    <= 2e-3 x RMS(acc), under the shared gate's rule."""
+    import torch
+    from madi_b200 import q8
+    from tests.gate import half_ulp16
+    qs, sc = synth.q8_weight(N, K, M + K)
+    a = synth.activations(M, K, M + 1)
+    b = synth.bias(N, 4)
+    x0 = np.random.default_rng(M).standard_normal((M, N)).astype(np.float32)
+    X = _t(x0)
+    q8.linear(q8.Q8Weight(_t(qs), _t(sc)), _t(a), bias=_t(b), epi=q8.EPI_BIAS_RES, residual=X, out=X)
+    torch.cuda.synchronize()
+    acc = oracle.linear_f16(a, qs, sc)
+    want = x0.astype(np.float64) + acc + b.astype(np.float64)
+    got = X.cpu().numpy().astype(np.float64)
+    excess = np.maximum(np.abs(got - want) - half_ulp16(acc) - 1e-6 * np.abs(want), 0.0)
+    rms = np.sqrt(np.mean(acc ** 2))
+    assert excess.max() <= 2e-3 * rms, f"excess {excess.max() / rms:.3e} x RMS"
+    # the add itself is exact f32 arithmetic on the f16-rounded projection of the GPU
+    y16 = q8.linear(q8.Q8Weight(_t(qs), _t(sc)), _t(a))
+    torch.cuda.synchronize()
+    ref = (torch.from_numpy(x0) + y16.float().cpu()) + torch.from_numpy(b.astype(np.float32))
+    assert torch.equal(X.cpu(), ref), "x != (x + f16 projection) + bias in f32"
