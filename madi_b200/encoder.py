@@ -156,32 +156,42 @@ class Encoder:
                                                                                                 generator=g))
 
     def forward(self, mel: torch.Tensor, stream=None) -> torch.Tensor:
-        """mel f16 [chunks][128][3000] -> encoder states f16 [chunks][1500][1280]."""
+        """mel f16 [chunks][128][frames] -> encoder states f16 [chunks][frames / 2][1280];
+        frames = 3000 for a 30 s chunk (shorter even lengths for tests)."""
         B = mel.shape[0]
-        x = torch.empty((B * SEQ, D), dtype=torch.float32, device=mel.device)     # f32 residual stream
+        x = self.stem_all(mel)
+        return self.layers_forward(x, mel.shape[2] // 2, stream=stream).view(B, mel.shape[2] // 2, D)
+
+    def stem_all(self, mel: torch.Tensor) -> torch.Tensor:
+        """The stem of every chunk: f32 residual stream [chunks * frames / 2][1280]."""
+        B, seq = mel.shape[0], mel.shape[2] // 2
+        x = torch.empty((B * seq, D), dtype=torch.float32, device=mel.device)
         for c in range(B):
             # one chunk per convolution call: the library picks its algorithm by shape,
             # so a chunk's stem output does not depend on how many chunks share a batch
-            x[c * SEQ:(c + 1) * SEQ] = self.stem(mel[c:c + 1])[0]
+            x[c * seq:(c + 1) * seq] = self.stem(mel[c:c + 1])[0]
+        return x
+
+    def layers_forward(self, x: torch.Tensor, seq: int, stream=None) -> torch.Tensor:
+        """Every layer and ln_post on the residual stream x (updated in place) of
+        chunks of `seq` frames; returns the f16 encoder states [rows][1280]."""
         if self.fuse_res:
             for L in self.layers:
-                L.forward_fused(x, stream=stream)
-            return q8.layer_norm_f16(x, *self.ln_post, eps=EPS, stream=stream).view(B, SEQ, D)
+                L.forward_fused(x, seq=seq, stream=stream)
+            return q8.layer_norm_f16(x, *self.ln_post, eps=EPS, stream=stream)
         f, b2 = None, None
         for L in self.layers:
-            f, b2 = L.forward(x, f, b2, stream=stream), L.b2
+            f, b2 = L.forward(x, f, b2, seq=seq, stream=stream), L.b2
         if f is None:
-            y = q8.layer_norm_f16(x, *self.ln_post, eps=EPS, stream=stream)
-        else:
-            y = q8.bias_res_ln_f16(x, f, b2, *self.ln_post, eps=EPS, stream=stream)
-        return y.view(B, SEQ, D)
+            return q8.layer_norm_f16(x, *self.ln_post, eps=EPS, stream=stream)
+        return q8.bias_res_ln_f16(x, f, b2, *self.ln_post, eps=EPS, stream=stream)
 
     def stem(self, mel: torch.Tensor) -> torch.Tensor:
-        """Conv stem and positions: mel f16 [b][128][3000] -> f32 [b][1500][1280]."""
+        """Conv stem and positions: mel f16 [b][128][frames] -> f32 [b][frames / 2][1280]."""
         import torch.nn.functional as Fn
         h = Fn.gelu(Fn.conv1d(mel, self.c1w, self.c1b, padding=1))
-        h = Fn.gelu(Fn.conv1d(h, self.c2w, self.c2b, stride=2, padding=1))         # [b][1280][1500]
-        return h.transpose(1, 2).float() + self.pos
+        h = Fn.gelu(Fn.conv1d(h, self.c2w, self.c2b, stride=2, padding=1))         # [b][1280][frames / 2]
+        return h.transpose(1, 2).float() + self.pos[:h.shape[2]]
 
     def flops(self, chunks: int) -> float:
         """Algorithmic FLOPs of the layers (the stem's 17.6 GFLOP per chunk not counted)."""

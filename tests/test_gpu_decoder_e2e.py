@@ -23,7 +23,7 @@ def _t(a, dev="cuda"):
     return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
 
 
-def _oracle_decode(oracle, w, ck, cv, dec, act16=False):
+def _oracle_decode(oracle, w, ck, cv, dec, act16=False, steps=STEPS):
     D, HEADS, MAX_TOK = dec.D, dec.HEADS, dec.MAX_TOK
     f32 = lambda a: np.asarray(a, np.float32)
     # act16: the activations of every projection rounded to f16
@@ -36,7 +36,7 @@ def _oracle_decode(oracle, w, ck, cv, dec, act16=False):
     vc = [np.zeros((S, MAX_TOK, D), np.float32) for _ in w["layers"]]
     eq, es = w["emb"]
     margins, confs = [], []
-    for _ in range(STEPS):
+    for _ in range(steps):
         x = np.stack([oracle.emb_q8(eq, es, tokens[b, pos[b]]) + w["pos_emb"][pos[b]] for b in range(S)])
         for l, L in enumerate(w["layers"]):
             _, xb = oracle.bias_res_ln_f32(x, None, None, *L["aln"], dec.EPS)
@@ -64,7 +64,7 @@ def _oracle_decode(oracle, w, ck, cv, dec, act16=False):
             margins.append((top2[1] - top2[0]) / np.sqrt(np.mean(logits[b] ** 2)))
             tokens[b, pos[b]] = tok
             confs.append(conf)
-    return tokens, np.array(confs).reshape(STEPS, S), min(margins)
+    return tokens, np.array(confs).reshape(steps, S), np.array(margins).reshape(steps, S)
 
 
 @pytest.mark.parametrize("act16", [False, True])
@@ -104,7 +104,8 @@ def test_greedy_decoder_end_to_end(madi, oracle, act16):
     conf = model.conf[:, 1:STEPS + 1].cpu().numpy()
     del graph
 
-    want, want_conf, margin = _oracle_decode(oracle, w, ck, cv, dec, act16)
+    want, want_conf, margins = _oracle_decode(oracle, w, ck, cv, dec, act16)
+    margin = margins.min()
     assert margin > 1e-3, f"synthetic data too close to a tie (margin {margin:.2e})"
     assert np.array_equal(first, want[:, 1])
     assert np.array_equal(got, want[:, :STEPS + 1]), f"GPU {got.tolist()}\noracle {want[:, :STEPS + 1].tolist()}"
@@ -114,3 +115,56 @@ def test_greedy_decoder_end_to_end(madi, oracle, act16):
     # differences travel through the four layers into the logits, so the confidence
     # (a softmax probability) gets a looser bar -- the tokens stay bit-identical
     np.testing.assert_allclose(conf.T, want_conf, rtol=2e-2 if act16 else 1e-3)
+
+
+LONG_STEPS, LONG_SLOTS, DECISIVE = 40, 4, 5e-3
+
+
+def test_greedy_decoder_long_stream(madi, oracle):
+    """The batched decode of the long-audio configuration (f16 activations) for 4
+    slots over 40 greedy tokens, one CUDA graph per token step, against the oracle's
+    loop.  Each slot's stream is compared token by token for as long as the oracle's
+    top-2 margin stays decisive (> 5e-3 x the logits' RMS, well above the f16
+    rounding differences the two can carry); a step below that ends the comparison of
+    that slot (from there the two could take different tokens legitimately, and the
+    histories would differ).  At least half of all decisions must be compared."""
+    import torch
+    from madi_b200 import decoder as dec
+    w = dec.host_weights(seed=4)
+    model = dec.Decoder(w, LONG_SLOTS, act16=True)
+    g = np.random.default_rng(12)
+    enc = g.standard_normal((LONG_SLOTS, dec.ENC, dec.D)).astype(np.float16)
+    model.set_encoder(_t(enc))
+    torch.cuda.synchronize()
+    ck = [c.cpu().numpy() for c in model.ck]
+    cv = [c.cpu().numpy() for c in model.cv]
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    model.reset(SEED_TOKEN)
+    with torch.cuda.stream(s):
+        model.step(SAMPLE_BEGIN)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    model.reset(SEED_TOKEN)
+    torch.cuda.synchronize()
+    with torch.cuda.graph(graph):
+        model.step(SAMPLE_BEGIN)
+    model.reset(SEED_TOKEN)
+    torch.cuda.synchronize()
+    for _ in range(LONG_STEPS):
+        graph.replay()
+    torch.cuda.synchronize()
+    got = model.tokens[:, :LONG_STEPS + 1].cpu().numpy().view(np.uint32)
+    del graph
+    want, _, margins = _oracle_decode(oracle, w, ck, cv, dec, True, steps=LONG_STEPS)
+    compared = 0
+    for b in range(LONG_SLOTS):
+        for t in range(LONG_STEPS):
+            if margins[t, b] <= DECISIVE:
+                break
+            assert got[b, t + 1] == want[b, t + 1], f"slot {b} step {t}: GPU {got[b, :t + 2].tolist()} " \
+                                                    f"oracle {want[b, :t + 2].tolist()}"
+            compared += 1
+    print(f"long stream: {compared} of {LONG_SLOTS * LONG_STEPS} decisions compared")
+    assert compared >= LONG_SLOTS * LONG_STEPS // 2, f"only {compared} decisive decisions"
