@@ -39,27 +39,48 @@ def synthetic_mel(chunks: int, first: int = 0) -> np.ndarray:
 
 class Transcriber:
     def __init__(self, slots: int = 8, enc_layers: int = 32, tokens: int = 224, seed: int = 1, device="cuda",
-                 split: Optional[Tuple[int, int]] = None, act16: Optional[bool] = None):
+                 split: Optional[Tuple[int, int]] = None, act16: Optional[bool] = None,
+                 decoders: Optional[int] = None):
         """split: (world, rank) -- the decoder's vocab head column-split over the
         ranks of the default process group (one process per GPU), its logits
         exchanged by NCCL all-gathers inside the captured token step.  Every rank
         must then decode the same number of batches (the collectives pair up step by
         step).  act16: the decoder projections on f16-rounded activations (default:
         when there is more than one slot or the head is split, as the reference's
-        batched decode)."""
+        batched decode).  decoders: how many batches transcribe_chunks decodes at
+        once, each decoder (sharing the weights, with its own KV caches and token-step
+        graph) on its own stream -- the token step is latency-bound, so several
+        batches' steps overlap on the GPU (default 4).  With the split head each
+        decoder exchanges over a process group of its own (a communicator per
+        decoder), so the collectives of different decoders never interleave on one
+        communicator; every rank creates the groups in the same order."""
         if tokens < 1 or tokens + 1 > dec.MAX_TOK:
             raise ValueError(f"1..{dec.MAX_TOK - 1} tokens per chunk")
         self.encoder = enc.Encoder(enc_layers, seed, device)
         if act16 is None:
             act16 = slots > 1 or split is not None
-        self.decoder = dec.Decoder(dec.device_weights(seed, device), slots, device, act16=act16, split=split)
+        if decoders is None:
+            decoders = 4
+        if decoders < 1:
+            raise ValueError("decoders >= 1")
+        w = dec.device_weights(seed, device)
+        exchanges = [None] * decoders
+        self.groups = []
+        if split is not None and split[0] > 1:
+            import torch.distributed as dist
+            self.groups = [dist.new_group() for _ in range(decoders)]
+            exchanges = [(lambda g: (lambda out, inp: dist.all_gather_into_tensor(out, inp, group=g)))(g)
+                         for g in self.groups]
+        self.decoders = [dec.Decoder(w, slots, device, act16=act16, split=split, exchange=exchanges[i])
+                         for i in range(decoders)]
+        self.decoder = self.decoders[0]
         self.split = split
         self.slots, self.tokens = slots, tokens
         self.eot = torch.tensor([EOT], dtype=torch.int32, device=device)
-        self.graph = None
+        self.graphs = [None] * decoders
 
-    def _capture(self):
-        d = self.decoder
+    def _capture(self, i: int = 0):
+        d = self.decoders[i]
         d.reset(SOT)
         d.step(suppress=self.eot)               # eager first step: module load, one-time attributes
         torch.cuda.synchronize()
@@ -68,51 +89,67 @@ class Transcriber:
         with torch.cuda.graph(g, capture_error_mode="thread_local"):
             d.step(suppress=self.eot)
         torch.cuda.synchronize()
-        self.graph = g
+        self.graphs[i] = g
 
     def encode(self, mel: torch.Tensor) -> torch.Tensor:
         """mel f16 [b][128][3000] on the device -> encoder states f16 [b][1500][1280]."""
         return self.encoder.forward(mel)
 
-    def decode(self, states: torch.Tensor) -> torch.Tensor:
+    def decode(self, states: torch.Tensor, i: int = 0) -> torch.Tensor:
         """Greedy tokens u32-as-int32 [b][tokens] (on the device) for b <= slots chunks'
-        encoder states; unused slots decode a copy of the last chunk."""
+        encoder states, on decoder i; unused slots decode a copy of the last chunk."""
         b = states.shape[0]
         if not 1 <= b <= self.slots:
             raise ValueError(f"1..{self.slots} chunks per batch")
         if b < self.slots:
             states = torch.cat([states, states[-1:].expand(self.slots - b, -1, -1)], dim=0)
-        self.decoder.set_encoder(states)
-        if self.graph is None:
-            self._capture()
-        self.decoder.reset(SOT)
+        d = self.decoders[i]
+        d.set_encoder(states)
+        if self.graphs[i] is None:
+            self._capture(i)
+        d.reset(SOT)
+        g = self.graphs[i]
         for _ in range(self.tokens):
-            self.graph.replay()
-        return self.decoder.tokens[:b, 1:1 + self.tokens]
+            g.replay()
+        return d.tokens[:b, 1:1 + self.tokens]
 
     def transcribe(self, mel: torch.Tensor) -> torch.Tensor:
         return self.decode(self.encode(mel))
 
+    def prepare(self):
+        """Captures every decoder's token step (module load, graphs) ahead of timing;
+        a decoder that has not seen encoder states yet gets zeros (its cross K / V
+        buffers must exist before its step is captured)."""
+        dev = self.encoder.pos.device
+        for i, d in enumerate(self.decoders):
+            if self.graphs[i] is None:
+                if d.ck[0] is None:
+                    d.set_encoder(torch.zeros((self.slots, dec.ENC, dec.D), dtype=torch.float16, device=dev))
+                self._capture(i)
+
     def transcribe_chunks(self, mel_host: torch.Tensor, tokens_host: torch.Tensor, overlap: bool = True,
                           timings: Optional[list] = None) -> None:
         """Every chunk of mel_host (f16 [n][128][3000], pinned host memory) to
-        tokens_host (int32 [n][tokens], pinned), in batches of `slots` chunks: the
-        mel copy and the encoder of batch k + 1 run on their own stream beside batch k's
-        decoder, which runs on a higher-priority stream (its latency-bound token steps
-        leave most of the GPU idle); overlap=False runs the phases back to back.  Returns
-        when the work is queued; synchronise before reading tokens_host.  timings, if
-        given, receives ((encoder start, end), (decoder start, end)) CUDA events per
-        batch."""
+        tokens_host (int32 [n][tokens], pinned), in batches of `slots` chunks.  The mel
+        copies and the encoder run in order on their own stream, ahead of the
+        decoders; batch k is decoded by decoder k mod D on that decoder's
+        higher-priority stream (its latency-bound token steps leave most of the GPU
+        idle, so the decoders and the encoder overlap); overlap=False runs every phase
+        back to back on one stream with one decoder.  Returns when the work is queued;
+        synchronise before reading tokens_host.  timings, if given, receives ((encoder
+        start, end), (decoder start, end)) CUDA events per batch."""
         n = mel_host.shape[0]
         batches = [(i, min(self.slots, n - i)) for i in range(0, n, self.slots)]
         if not batches:
             return
         dev = self.encoder.pos.device
         cur = torch.cuda.current_stream(dev)
+        nd = len(self.decoders) if overlap else 1
         enc_s = torch.cuda.Stream(device=dev) if overlap else cur
-        dec_s = torch.cuda.Stream(device=dev, priority=-1) if overlap else cur
+        dec_s = [torch.cuda.Stream(device=dev, priority=-1) for _ in range(nd)] if overlap else [cur]
         enc_s.wait_stream(cur)
-        dec_s.wait_stream(cur)
+        for s in dec_s:
+            s.wait_stream(cur)
         mel_d = torch.empty((self.slots,) + tuple(mel_host.shape[1:]), dtype=torch.float16, device=dev)
         mel_d.record_stream(enc_s)
 
@@ -129,23 +166,33 @@ class Transcriber:
         nxt = encode(0)
         for k, (i, b) in enumerate(batches):
             states, enc_ev = nxt
+            d = k % nd
+            s = dec_s[d]
             d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            with torch.cuda.stream(dec_s):
-                dec_s.wait_event(enc_ev[1])
-                d0.record(dec_s)
-                states.record_stream(dec_s)
-                if overlap and k + 1 < len(batches):
-                    nxt = encode(k + 1)             # its states are taken: the next encoder may start
-                toks = self.decode(states)
+            if overlap and k + 1 < len(batches):
+                nxt = encode(k + 1)                 # queued on the encoder stream, ahead of the decoders
+            with torch.cuda.stream(s):
+                s.wait_event(enc_ev[1])
+                d0.record(s)
+                states.record_stream(s)
+                toks = self.decode(states, d)
                 tokens_host[i:i + b].copy_(toks, non_blocking=True)
-                d1.record(dec_s)
+                d1.record(s)
             if timings is not None:
                 timings.append((enc_ev, (d0, d1)))
             if not overlap and k + 1 < len(batches):
                 nxt = encode(k + 1)
             del states
-        cur.wait_stream(dec_s)
+        for s in dec_s:
+            cur.wait_stream(s)
 
     def release(self):
-        """Drops the captured token step (before the process group or the context goes)."""
-        self.graph = None
+        """Drops the captured token steps and the decoders' process groups (before the
+        default process group or the context goes)."""
+        self.graphs = [None] * len(self.decoders)
+        if self.groups:
+            import torch.distributed as dist
+            torch.cuda.synchronize()
+            for g in self.groups:
+                dist.destroy_process_group(g)
+            self.groups = []
