@@ -317,6 +317,28 @@ def cpu_baseline_leg(args, rows=256):
                                  "vocab head, int8 weights dequantised in registers (gemv_q8 arithmetic)"}}
 
 
+def parity_sample(sample, w):
+    """The timed step's own outputs on a row sample against the oracle (the checker,
+    beside the CPU baseline): fc1 on the sampled X rows, fc2 on the GPU's H rows with
+    the X residual.  Reports the raw max |err| / RMS and the error beyond the final f16
+    half-ulp (tests/gate.py), whose bar is 2e-3."""
+    import numpy as np
+    from oracle import oracle
+    from tests.gate import check
+    x, h, y, rows = sample
+    oracle.build()
+    ex1, raw1 = check(h.astype(np.float64), oracle.linear_f16(x, w["fc1_qs"], w["fc1_scales"], w["fc1_bias"],
+                                                              oracle.EPI_BIAS_GELU), "bench fc1", f16_out=True)
+    ex2, raw2 = check(y.astype(np.float64), oracle.linear_f16(h, w["fc2_qs"], w["fc2_scales"], w["fc2_bias"],
+                                                              oracle.EPI_BIAS_RES, residual=x), "bench fc2",
+                      f16_out=True)
+    return {"rows": int(len(rows)), "gate": 2e-3,
+            "fc1": {"raw_max_err_over_rms": raw1, "excess_over_rms": ex1},
+            "fc2": {"raw_max_err_over_rms": raw2, "excess_over_rms": ex2},
+            "note": "the timed step's last H / Y rows (first, last, tile edges, random) vs the oracle's f64 result; "
+                    "excess = error beyond the final f16 half-ulp"}
+
+
 def run_reference(args, world, rank):
     """The reference's CPU computation of the benchmarked op (oracle/cpu_baseline.c:
     test_q8gemm.zig:59-69's f32 dequant + accumulate with the m4_gemm epilogues), on
@@ -486,6 +508,10 @@ def main_madi(args, world, rank, local):
         torch.cuda.empty_cache()
 
     # ---------------- e2e through the public API with host buffers
+    # rows of the timed step's last outputs, kept for the oracle check beside the CPU baseline
+    prows = np.unique(np.concatenate([[0, 191, 192, M // 2, M - 1],
+                                      np.random.default_rng(7).choice(M, 59, replace=False)]))
+    psample = (X[prows].cpu().numpy(), H[prows].cpu().numpy(), Y[prows].cpu().numpy(), prows)
     del H, Y
     torch.cuda.empty_cache()
     e2e = None
@@ -503,9 +529,10 @@ def main_madi(args, world, rank, local):
         long_audio = long_audio_leg(args, world, rank, dev)
 
     # ---------------- CPU baseline (rank 0, N=1 only)
-    cpu = None
+    cpu, parity = None, None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline_leg(args)
+        parity = parity_sample(psample, w)
 
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": K,
@@ -518,7 +545,7 @@ def main_madi(args, world, rank, local):
                            "weights": "random-init Q8_0 (block-32 int8 + f16 scales)"},
                 # 30 s chunks through one fc1 + fc2 pair per second (not the whole encoder)
                 "ffn_pair_chunks_per_s": chunks_per_s,
-                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "decode": decode,
+                "roofline": roofline, "cpu_baseline": cpu, "parity": parity, "e2e": e2e, "decode": decode,
                 "encoder_layer": enc_layer, "long_audio": long_audio,
                 "clocks": clocks, "gpu_launches": 2 * K}
         print(json.dumps(line), flush=True)

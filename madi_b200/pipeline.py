@@ -6,8 +6,9 @@ reference batches independent chunks into decoder slots the same way,
 transcribe.zig:2314-2321).
 
 Per batch: one eager encoder pass (about 290 launches, tcgen05 GEMMs and flash
-attention), 8 cross K / V GEMMs, then `tokens` replays of one captured CUDA graph
-of the token step.  Weights are random-init Q8 of the real shapes drawn on the
+attention), 8 cross K / V GEMMs, then `tokens` / 8 replays of one captured CUDA graph
+of 8 token steps (one step per replay when 8 does not divide `tokens`).  Several
+batches decode at once, one decoder per stream.  Weights are random-init Q8 of the real shapes drawn on the
 device; the mel input is seeded Gaussian noise clipped to [-1.5, 1.5].
 
 Every result row depends only on its own chunk: the GEMMs' per-row accumulation
@@ -78,6 +79,9 @@ class Transcriber:
         self.slots, self.tokens = slots, tokens
         self.eot = torch.tensor([EOT], dtype=torch.int32, device=device)
         self.graphs = [None] * decoders
+        # token steps per graph: 8 when they divide the tokens (the reference's DBATCH,
+        # transcribe.zig:2564), so a batch is tokens / 8 graph launches
+        self.steps_per_graph = 8 if tokens % 8 == 0 else 1
 
     def _capture(self, i: int = 0):
         d = self.decoders[i]
@@ -87,7 +91,8 @@ class Transcriber:
         g = torch.cuda.CUDAGraph()
         # thread-local capture mode: NCCL's calls in the split head's step are legal
         with torch.cuda.graph(g, capture_error_mode="thread_local"):
-            d.step(suppress=self.eot)
+            for _ in range(self.steps_per_graph):
+                d.step(suppress=self.eot)
         torch.cuda.synchronize()
         self.graphs[i] = g
 
@@ -109,7 +114,7 @@ class Transcriber:
             self._capture(i)
         d.reset(SOT)
         g = self.graphs[i]
-        for _ in range(self.tokens):
+        for _ in range(self.tokens // self.steps_per_graph):
             g.replay()
         return d.tokens[:b, 1:1 + self.tokens]
 

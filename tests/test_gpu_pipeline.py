@@ -106,3 +106,23 @@ def test_transcribe_chunks_overlap(tr):
     m = torch.from_numpy(mel).cuda()
     want = torch.cat([tr.transcribe(m[0:4]).cpu(), tr.transcribe(m[4:6]).cpu()])
     assert torch.equal(got[0], want) and torch.equal(got[1], want), f"{got[0].tolist()} vs {want.tolist()}"
+
+
+def test_eight_step_graph_equals_eager_steps(madi):
+    """With tokens a multiple of 8 the token step is captured eight times in one graph
+    (the reference's DBATCH); replaying it gives the tokens of 16 eager steps."""
+    import torch
+    from madi_b200 import pipeline
+    t = pipeline.Transcriber(slots=2, enc_layers=1, tokens=16, seed=4, decoders=1)
+    assert t.steps_per_graph == 8
+    mel = torch.from_numpy(pipeline.synthetic_mel(2, first=30)).cuda()
+    states = t.encode(mel)
+    got = t.decode(states).clone()
+    d = t.decoders[0]
+    d.reset(pipeline.SOT)
+    for _ in range(16):
+        d.step(suppress=t.eot)
+    torch.cuda.synchronize()
+    assert torch.equal(got, d.tokens[:2, 1:17])
+    assert int(d.pos[0].item()) == 16
+    t.release()
