@@ -121,17 +121,20 @@ MADI_DEV void epilogue_chunk(const GemmArgs &p, const uint32_t (&v)[32], int mb,
     }
     if constexpr (EPI == kEpiResF32) {
         // x += half(acc) + bias in the reference's order ((x + mo) + bias); the
-        // residual reads of the chunk are issued together before the stores
+        // residual reads of each half chunk are issued together before its stores
         float *yf = reinterpret_cast<float *>(p.y);
         const float *rf = reinterpret_cast<const float *>(p.residual);
         const int nr = p.M - mb < 32 ? p.M - mb : 32;
-        float r[32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) r[i] = i < nr ? rf[base + (size_t)i * N] : 0.f;
+        for (int hh = 0; hh < 32; hh += 16) {
+            float r[16];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-            const float mo = __half2float(__float2half_rn(__uint_as_float(v[i])));
-            if (i < nr) yf[base + (size_t)i * N] = __fadd_rn(__fadd_rn(r[i], mo), bias);
+            for (int i = 0; i < 16; ++i) r[i] = hh + i < nr ? rf[base + (size_t)(hh + i) * N] : 0.f;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const float mo = __half2float(__float2half_rn(__uint_as_float(v[hh + i])));
+                if (hh + i < nr) yf[base + (size_t)(hh + i) * N] = __fadd_rn(__fadd_rn(r[i], mo), bias);
+            }
         }
         return;
     }
@@ -554,9 +557,11 @@ constexpr int PBN = 2 * BN;       // weight rows per pair tile (MMA M)
 
 // PBT tokens per pair tile (MMA N; each CTA stages PBT / 2 of them).  The A
 // ring takes the tensor-memory columns the two accumulators leave: 4 stages at
-// PBT = 192.  Narrower tiles (deeper A rings: 6 stages at 160, 8 at 128) were
-// measured slower, 941 and 830 TFLOP/s against 1035 on the encoder FFN pair.
+// PBT = 192 and two at 224.  Narrower tiles (deeper A rings: 6 stages at 160, 8 at
+// 128) were measured slower, 941 and 830 TFLOP/s against 1035 on the encoder FFN
+// pair; 224 measured 1047 against 1025 at 192 there (fc1 3.8 % faster).
 constexpr int kPairTokens = 192;
+constexpr int kPairTokensWide = 224;     // the wider tile, chosen per shape by pair_tokens()
 template <int PBT> struct PCfg {
     static constexpr int PHALF = PBT / 2;
     static constexpr int X_STAGE = PHALF * BK * 2;   // f16 bytes of one CTA's X half
@@ -604,7 +609,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const int num_tiles = n_tiles * ((M + PBT - 1) / PBT);
     const int KT = (K + BK - 1) / BK;
     const int nkb = K / 32;
-    const bool pairs = (KT & 1) == 0;
+    // pair mode issues two K stages per MMA-thread step; it needs two pairs of TMEM A
+    // stages so the dequant of one pair overlaps the MMAs of the other
+    const bool pairs = (KT & 1) == 0 && A_STAGES >= 4;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -961,9 +968,50 @@ static bool use_pair_kernel() {
     }();
     return v;
 }
+// Tokens per CTA-pair tile, 192 or 224.  A K stage costs about 2 (192 + tokens)
+// cycles of the pair (measured over 128-224 token tiles), so the wider tile does
+// 7 % more work per cycle; its 448 accumulator columns leave two TMEM A stages, so
+// the MMA thread takes one K stage at a time.  The tile with the lower
+// waves x (192 + tokens) wins, 192 on ties: 224 for the encoder FFN pair at 16
+// chunks (fc1 30 waves against 34), 192 for shapes that fit one wave.
+// MADI_GEMM_PBT=192 or 224 in the environment forces one (for comparisons).
+static int pair_tokens(int M, int N, int num_sms) {
+    static const int forced = [] {
+        const char *e = getenv("MADI_GEMM_PBT");
+        const int v = e ? atoi(e) : 0;
+        return v == 192 || v == 224 ? v : 0;
+    }();
+    if (forced) return forced;
+    const long pairs = num_sms / 2 > 0 ? num_sms / 2 : 1;
+    const long n_tiles = (N + PBN - 1) / PBN;
+    long best_cost = -1;
+    int best = kPairTokens;
+    for (int pbt : {kPairTokens, kPairTokensWide}) {
+        const long waves = (n_tiles * ((M + pbt - 1) / pbt) + pairs - 1) / pairs;
+        const long cost = waves * (192 + pbt);
+        if (best_cost < 0 || cost < best_cost) { best_cost = cost; best = pbt; }
+    }
+    return best;
+}
+
+template <int PBT>
+static cudaError_t launch_pair_epi(const GemmArgs &a, int epi, const CUtensorMap &tmX, const CUtensorMap &tmW,
+                                   const CUtensorMap &tmY, int ystore, int num_sms, cudaStream_t st) {
+    switch (epi) {
+        case kEpiNone: return launch_pair<PBT, kEpiNone>(a, tmX, tmW, tmY, ystore, num_sms, st);
+        case kEpiBias: return launch_pair<PBT, kEpiBias>(a, tmX, tmW, tmY, ystore, num_sms, st);
+        case kEpiBiasGelu: return launch_pair<PBT, kEpiBiasGelu>(a, tmX, tmW, tmY, ystore, num_sms, st);
+        case kEpiBiasRes: return launch_pair<PBT, kEpiBiasRes>(a, tmX, tmW, tmY, ystore, num_sms, st);
+        case kEpiNoneF32: return launch_pair<PBT, kEpiNoneF32>(a, tmX, tmW, tmY, 0, num_sms, st);
+        case kEpiResF32: return launch_pair<PBT, kEpiResF32>(a, tmX, tmW, tmY, 0, num_sms, st);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
 cudaError_t launch_gemm_tc(const GemmArgs &a, int epi, int num_sms, cudaStream_t st) {
     const bool pair = use_pair_kernel() && num_sms >= 2;
-    const int bt = pair ? kPairTokens / 2 : pick_bt(a.M, a.N, num_sms);   // X box rows
+    const int pbt = pair ? pair_tokens(a.M, a.N, num_sms) : 0;
+    const int bt = pair ? pbt / 2 : pick_bt(a.M, a.N, num_sms);   // X box rows
     CUtensorMap tmX, tmW;
     if (!make_map(&tmX, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.x, (uint64_t)a.K, (uint64_t)a.M, (uint64_t)a.K * 2, BK,
                   (uint32_t)bt, CU_TENSOR_MAP_SWIZZLE_128B))
@@ -978,17 +1026,9 @@ cudaError_t launch_gemm_tc(const GemmArgs &a, int epi, int num_sms, cudaStream_t
                  make_map(&tmY, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.y, (uint64_t)a.N, (uint64_t)a.M,
                           (uint64_t)a.N * 2, BN, Y_ROWS, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (!ystore) memset(&tmY, 0, sizeof(tmY));
-    if (pair) {
-        switch (epi) {
-            case kEpiNone: return launch_pair<kPairTokens, kEpiNone>(a, tmX, tmW, tmY, ystore, num_sms, st);
-            case kEpiBias: return launch_pair<kPairTokens, kEpiBias>(a, tmX, tmW, tmY, ystore, num_sms, st);
-            case kEpiBiasGelu: return launch_pair<kPairTokens, kEpiBiasGelu>(a, tmX, tmW, tmY, ystore, num_sms, st);
-            case kEpiBiasRes: return launch_pair<kPairTokens, kEpiBiasRes>(a, tmX, tmW, tmY, ystore, num_sms, st);
-            case kEpiNoneF32: return launch_pair<kPairTokens, kEpiNoneF32>(a, tmX, tmW, tmY, 0, num_sms, st);
-            case kEpiResF32: return launch_pair<kPairTokens, kEpiResF32>(a, tmX, tmW, tmY, 0, num_sms, st);
-            default: return cudaErrorInvalidValue;
-        }
-    }
+    if (pair)
+        return pbt == kPairTokensWide ? launch_pair_epi<kPairTokensWide>(a, epi, tmX, tmW, tmY, ystore, num_sms, st)
+                          : launch_pair_epi<kPairTokens>(a, epi, tmX, tmW, tmY, ystore, num_sms, st);
 #define MADI_GEMM_EPI(BT)                                                                         \
     switch (epi) {                                                                                \
         case kEpiNone: return launch_bt<BT, kEpiNone>(a, tmX, tmW, tmY, ystore, num_sms, st);     \

@@ -64,6 +64,15 @@ def test_odd_k_blocks(madi, oracle, K):
     _run(madi, oracle, 300, 256, K, 1, seed=K)
 
 
+@pytest.mark.parametrize("epi", [0, 1, 2, 3])
+@pytest.mark.parametrize("K", [320, 288])
+def test_wide_pair_tile_ragged_waves(madi, oracle, epi, K):
+    # M = 3001, N = 2560: 140 tiles of 224 tokens (two waves of 74 pairs, the last
+    # tile 89 tokens) cost less than 160 tiles of 192 (three waves), so the launcher
+    # picks the 224-token pair tile; K = 288 leaves the last stage half filled
+    _run(madi, oracle, 3001, 2560, K, epi, seed=K + epi)
+
+
 def test_bias_f16(madi, oracle):
     _run(madi, oracle, 257, 384, 320, 2, bias_f16=True)
 
