@@ -78,6 +78,49 @@ MADI_DEV float gelu_erf(float xv) {
     return fmaf(fabsf(h), erf_abs, h);
 }
 
+// Packed f32x2 arithmetic (sm_100): two IEEE f32 operations per instruction,
+// each lane rounded exactly as the scalar operation.
+MADI_DEV void fma2(float &d0, float &d1, float a0, float a1, float b0, float b1, float c0, float c1) {
+    asm("{\n\t.reg .b64 a, b, c, d;\n\tmov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\tmov.b64 c, {%6, %7};\n\t"
+        "fma.rn.f32x2 d, a, b, c;\n\tmov.b64 {%0, %1}, d;\n\t}"
+        : "=f"(d0), "=f"(d1)
+        : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+MADI_DEV void mul2(float &d0, float &d1, float a0, float a1, float b0, float b1) {
+    asm("{\n\t.reg .b64 a, b, d;\n\tmov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\t"
+        "mul.rn.f32x2 d, a, b;\n\tmov.b64 {%0, %1}, d;\n\t}"
+        : "=f"(d0), "=f"(d1)
+        : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+MADI_DEV void add2(float &d0, float &d1, float a0, float a1, float b0, float b1) {
+    asm("{\n\t.reg .b64 a, b, d;\n\tmov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\t"
+        "add.rn.f32x2 d, a, b;\n\tmov.b64 {%0, %1}, d;\n\t}"
+        : "=f"(d0), "=f"(d1)
+        : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
+// gelu_erf of two values with packed arithmetic, bit-identical to gelu_erf on
+// each: the same operations in the same order.  The polynomial runs on negated
+// coefficients, giving -poly exactly (round-to-nearest is symmetric), so
+// 1 - poly * ex is one FMA without a separate negation.
+MADI_DEV void gelu_erf2(float &y0, float &y1, float x0, float x1) {
+    float az0, az1, d0, d1, np0, np1, s0, s1, e0, e1, h0, h1;
+    mul2(az0, az1, fabsf(x0), fabsf(x1), 0.7071067811865476f, 0.7071067811865476f);
+    fma2(d0, d1, az0, az1, 0.3275911f, 0.3275911f, 1.0f, 1.0f);
+    const float t0 = rcp_approx(d0), t1 = rcp_approx(d1);
+    fma2(np0, np1, -1.061405429f, -1.061405429f, t0, t1, 1.453152027f, 1.453152027f);
+    fma2(np0, np1, np0, np1, t0, t1, -1.421413741f, -1.421413741f);
+    fma2(np0, np1, np0, np1, t0, t1, 0.284496736f, 0.284496736f);
+    fma2(np0, np1, np0, np1, t0, t1, -0.254829592f, -0.254829592f);
+    mul2(np0, np1, np0, np1, t0, t1);
+    mul2(s0, s1, az0, az1, az0, az1);
+    mul2(s0, s1, s0, s1, -1.4426950408889634f, -1.4426950408889634f);
+    const float ex0 = ex2_approx(fmaxf(s0, -80.0f)), ex1 = ex2_approx(fmaxf(s1, -80.0f));
+    fma2(e0, e1, np0, np1, ex0, ex1, 1.0f, 1.0f);
+    mul2(h0, h1, 0.5f, 0.5f, x0, x1);
+    fma2(y0, y1, fabsf(h0), fabsf(h1), e0, e1, h0, h1);
+}
+
 // ------------------------------------------------------------------ shared / mbarrier
 
 MADI_DEV uint32_t smem_u32(const void *p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }

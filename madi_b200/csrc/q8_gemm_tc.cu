@@ -181,13 +181,23 @@ MADI_DEV void epilogue_chunk_stage(const GemmArgs &p, const uint32_t (&v)[32], i
             res[i] = (nok && mb + i < p.M) ? __half2float(static_cast<const __half *>(p.residual)[base + (size_t)i * p.N])
                                            : 0.f;
     }
+    if constexpr (EPI == kEpiBiasGelu) {
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-        float y = __uint_as_float(v[i]);
-        if constexpr (EPI == kEpiBias) y += bias;
-        if constexpr (EPI == kEpiBiasGelu) y = gelu_erf(y + bias);
-        if constexpr (EPI == kEpiBiasRes) y = y + bias + res[i];
-        col[i * BN] = __float2half_rn(y);
+        for (int i = 0; i < 32; i += 2) {
+            float a0, a1, y0, y1;
+            add2(a0, a1, __uint_as_float(v[i]), __uint_as_float(v[i + 1]), bias, bias);
+            gelu_erf2(y0, y1, a0, a1);
+            col[i * BN] = __float2half_rn(y0);
+            col[(i + 1) * BN] = __float2half_rn(y1);
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            float y = __uint_as_float(v[i]);
+            if constexpr (EPI == kEpiBias) y += bias;
+            if constexpr (EPI == kEpiBiasRes) y = y + bias + res[i];
+            col[i * BN] = __float2half_rn(y);
+        }
     }
 }
 
