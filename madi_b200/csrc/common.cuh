@@ -518,6 +518,16 @@ MADI_DEV void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
         : "memory");
 }
 
+// 32 lanes x 16 consecutive 32-bit columns.
+MADI_DEV void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+        "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
+
 // Shared-memory matrix descriptor for a K-major operand stored in the
 // 128-byte swizzle layout that TMA's SWIZZLE_128B writes: rows of 128 bytes,
 // 8-row groups 1024 bytes apart (SBO), LBO unused (1), descriptor version 1.

@@ -7,18 +7,26 @@
 //   q / k / v: f16 rows of `stride` elements, head h at columns h*64..h*64+63;
 //   `chunks` independent sequences of `seq` rows each, back to back.
 //
-// One CTA per (128-query tile, head, chunk); 256 threads:
-//   warp 0   TMA producer: the Q tile, then K / V tiles of 128 keys through a
-//            2-stage ring (SWIZZLE_128B boxes [128 rows][64 dims]);
-//   warp 1   MMA issuer + TMEM owner: S_j = Q K_j^T (M = 128 queries, N = 128 keys,
-//            K = 64 dims, both operands K-major in shared memory) into one of two
-//            TMEM S buffers, issued one tile ahead so the tensor cores compute
-//            S_{j+1} while the softmax of tile j runs; then O += P_j V_j (TS form:
-//            P from TMEM as A, V from shared memory as an N-contiguous B operand);
-//   warps 4-7 softmax (thread = query row = TMEM lane): read the S row from TMEM,
-//            update the running max / sum, write P as f16 pairs back over S, and
-//            rescale O in TMEM by alpha before P_j V_j is issued; finally O / l.
-// TMEM columns: S0 [0, 128), S1 [128, 256), O [256, 320).  Every wait is bounded.
+// One CTA per (two 128-query tiles A and B, head, chunk); 384 threads:
+//   warp 0     TMA producer: the two Q tiles, then K / V tiles of 128 keys through a
+//              3-stage ring (SWIZZLE_128B boxes [128 rows][64 dims]) shared by both;
+//   warp 1     MMA issuer + TMEM owner.  Per key tile j and query tile x in (A, B):
+//              once the softmax of x has published P_x(j), S_x(j+1) = Q_x K_{j+1}^T
+//              (M = 128 queries, N = 128 keys, K = 64 dims, both operands K-major in
+//              shared memory), then O_x += P_x(j) V_j (TS form: P from TMEM as A, V an
+//              N-contiguous shared-memory B operand);
+//   warps 4-7  softmax of tile A, warps 8-11 softmax of tile B (thread = query row =
+//              TMEM lane): the row max over S in 32-column passes, then the
+//              exponentials written as f16 pairs into the tile's P columns, O rescaled
+//              in TMEM by alpha when a row maximum moved; finally O / l.
+// Two softmax warpgroups keep the special-function unit and the tensor cores busy
+// while the other group waits for its MMAs; a tcgen05.mma of M = 128 costs the
+// tensor pipe ~115-125 cycles whatever N (64..256), so the 12 MMAs of a query x key
+// tile (S at N = 128, PV at N = 64) are the floor this layout is built around.
+// TMEM columns of tile x: S [256x, 256x + 128), P [256x + 128, +64), O [256x + 192,
+// +64).  P has its own columns, so S_x(j+1) can be computed while PV_x(j) still reads
+// P_x(j); the softmax waits for PV_x(j) before it overwrites P_x.  Every wait is
+// bounded.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
@@ -29,15 +37,17 @@
 namespace madi {
 namespace {
 
-constexpr int kQT = 128;                 // queries per CTA
+constexpr int kQT = 128;                 // queries per tile
 constexpr int kKT = 128;                 // keys per tile
 constexpr int kHD = 64;                  // head dim
-constexpr int kNS = 3;                   // K / V ring stages (2 measured 16 % slower: the next tile's loads waited for PV)
+constexpr int kNS = 3;                   // K / V ring stages (2 measured 16 % slower: loads waited for PV)
 constexpr int kTile = kQT * kHD * 2;     // bytes of one [128][64] f16 tile
-constexpr int kFaThreads = 256;
-constexpr int kSmWarp0 = 4;              // warps 4..7: softmax
+constexpr int kFaThreads = 384;
+constexpr int kSmWarp0 = 4;              // warps 4..7: softmax of tile A; 8..11: tile B
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kOCol = 256;
+constexpr uint32_t kTileCols = 256;      // TMEM columns per query tile
+constexpr uint32_t kPCol = 128;          // P columns within a tile's block
+constexpr uint32_t kOCol = 192;          // O columns within a tile's block
 constexpr float kScale = 0.125f;
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -45,18 +55,17 @@ struct __align__(8) FaBars {
     uint64_t q_full;
     uint64_t kv_full[kNS];
     uint64_t kv_empty[kNS];
-    uint64_t s_full[2];
-    uint64_t s_free[2];
-    uint64_t p_ready[2];
-    uint64_t o_done;
+    uint64_t s_full[2];     // per query tile: S_x(j) computed
+    uint64_t p_ready[2];    // per query tile: P_x(j) written, O_x rescaled (128 arrivals)
+    uint64_t o_done[2];     // per query tile: PV_x(j) complete
     uint64_t drain;
     uint32_t tmem_base;
     int abort;
 };
 
-// The CTA allocates all 512 TMEM columns, so it asks for more than half of the
-// SM's shared memory: a second CTA never lands on the SM to wait in tcgen05.alloc.
-constexpr size_t kFaSmemUsed = 1024 + (size_t)(1 + 2 * kNS) * kTile + sizeof(FaBars) + 64;
+// Two Q tiles and the K / V ring; more than half of the SM's shared memory, so a
+// second CTA (which would wait in tcgen05.alloc for the 512 TMEM columns) never lands.
+constexpr size_t kFaSmemUsed = 1024 + (size_t)(2 + 2 * kNS) * kTile + sizeof(FaBars) + 64;
 constexpr size_t kFaSmem = kFaSmemUsed > 120 * 1024 ? kFaSmemUsed : 120 * 1024;
 
 // PV: A = P (TMEM, K-major), B = V (shared memory, N-contiguous: bit 16 transposes B).
@@ -91,13 +100,13 @@ __global__ void __launch_bounds__(kFaThreads, 1)
                      int *dev_err) {
     extern __shared__ uint8_t fa_smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(fa_smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t *qs = smem;
-    uint8_t *ks = qs + kTile;                    // kNS tiles
+    uint8_t *qs = smem;                          // 2 tiles: A, B
+    uint8_t *ks = qs + 2 * kTile;                // kNS tiles
     uint8_t *vs = ks + kNS * kTile;              // kNS tiles
     FaBars *bars = reinterpret_cast<FaBars *>(vs + kNS * kTile);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int q0 = blockIdx.x * kQT, h = blockIdx.y, chunk = blockIdx.z;
+    const int q0 = blockIdx.x * 2 * kQT, h = blockIdx.y, chunk = blockIdx.z;
     const int row0 = chunk * seq;                // first row of this chunk
     const int nkv = (seq + kKT - 1) / kKT;
 
@@ -107,12 +116,11 @@ __global__ void __launch_bounds__(kFaThreads, 1)
             mbar_init(&bars->kv_full[s], 1);
             mbar_init(&bars->kv_empty[s], 1);
         }
-        for (int b = 0; b < 2; ++b) {
-            mbar_init(&bars->s_full[b], 1);
-            mbar_init(&bars->s_free[b], 1);
-            mbar_init(&bars->p_ready[b], 128);
+        for (int x = 0; x < 2; ++x) {
+            mbar_init(&bars->s_full[x], 1);
+            mbar_init(&bars->p_ready[x], 128);
+            mbar_init(&bars->o_done[x], 1);
         }
-        mbar_init(&bars->o_done, 1);
         mbar_init(&bars->drain, 1);
         bars->abort = 0;
         fence_mbar_init();
@@ -133,8 +141,11 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     if (warp == 0) {
         // ------------------------------------------------ TMA producer
         if (lane == 0) {
-            mbar_arrive_expect_tx(&bars->q_full, kTile);
+            // tile B may lie past the chunk (its rows are then the next chunk's, or past
+            // the tensor and zero-filled); its outputs are not stored
+            mbar_arrive_expect_tx(&bars->q_full, 2 * kTile);
             tma_load_2d(qs, &tmQ, &bars->q_full, h * kHD, row0 + q0);
+            tma_load_2d(qs + kTile, &tmQ, &bars->q_full, h * kHD, row0 + q0 + kQT);
             int issued = 0;
             for (int j = 0; j < nkv; ++j) {
                 const int s = j % kNS;
@@ -158,30 +169,33 @@ __global__ void __launch_bounds__(kFaThreads, 1)
             const uint64_t vd0 = smem_desc_sw128(smem_u32(vs));
             constexpr uint64_t kTileU = kTile >> 4;          // descriptor units per tile
             bool ok = mbar_wait(&bars->q_full, 0, abort_flag, dev_err);
-            auto issue_s = [&](int j) -> bool {
-                const int s = j % kNS, b = j & 1;
-                if (!mbar_wait(&bars->kv_full[s], (j / kNS) & 1, abort_flag, dev_err)) return false;
-                if (j >= 2 && !mbar_wait(&bars->s_free[b], ((j - 2) >> 1) & 1, abort_flag, dev_err)) return false;
+            // S_x(j) = Q_x K_j^T; the K / V stage of tile j is waited for before S_A(j)
+            auto issue_s = [&](int x, int j) -> bool {
+                const int s = j % kNS;
+                if (x == 0 && !mbar_wait(&bars->kv_full[s], (j / kNS) & 1, abort_flag, dev_err)) return false;
                 tc_fence_after();
 #pragma unroll
                 for (int k = 0; k < kHD / 16; ++k)       // K = 64 dims: 4 MMAs, descriptors +32 bytes each
-                    mma_ss(tmem + b * kKT, qd + 2 * k, kd0 + s * kTileU + 2 * k, kIdescS, k != 0);
-                umma_commit(&bars->s_full[b]);
+                    mma_ss(tmem + x * kTileCols, qd + x * kTileU + 2 * k, kd0 + s * kTileU + 2 * k, kIdescS, k != 0);
+                umma_commit(&bars->s_full[x]);
                 return true;
             };
-            if (ok) ok = issue_s(0);
+            if (ok) ok = issue_s(0, 0) && issue_s(1, 0);
             for (int j = 0; ok && j < nkv; ++j) {
-                const int s = j % kNS, b = j & 1;
-                if (j + 1 < nkv && !issue_s(j + 1)) { ok = false; break; }
-                if (!mbar_wait(&bars->p_ready[b], (j >> 1) & 1, abort_flag, dev_err)) { ok = false; break; }
-                tc_fence_after();
-                // O += P_j V_j: K = 128 keys in 8 steps; P columns +8 (16 f16), V rows +16 = 2048 bytes
+                const int s = j % kNS;
+                for (int x = 0; ok && x < 2; ++x) {
+                    if (!mbar_wait(&bars->p_ready[x], j & 1, abort_flag, dev_err)) { ok = false; break; }
+                    tc_fence_after();
+                    // the next S first, so the softmax of x can start on it while PV_x(j) runs
+                    if (j + 1 < nkv && !issue_s(x, j + 1)) { ok = false; break; }
+                    // O_x += P_x(j) V_j: K = 128 keys in 8 steps; P columns +8 (16 f16), V rows +16 = 2048 bytes
+                    const uint32_t tb = tmem + x * kTileCols;
 #pragma unroll
-                for (int k = 0; k < kKT / 16; ++k)
-                    mma_ts(tmem + kOCol, tmem + b * kKT + 8 * k, vd0 + s * kTileU + 128 * k, kIdescPV, (j | k) != 0);
-                umma_commit(&bars->kv_empty[s]);
-                umma_commit(&bars->s_free[b]);
-                umma_commit(&bars->o_done);
+                    for (int k = 0; k < kKT / 16; ++k)
+                        mma_ts(tb + kOCol, tb + kPCol + 8 * k, vd0 + s * kTileU + 128 * k, kIdescPV, (j | k) != 0);
+                    umma_commit(&bars->o_done[x]);
+                }
+                if (ok) umma_commit(&bars->kv_empty[s]);
             }
             umma_commit(&bars->drain);
             mbar_wait_drain_fa(&bars->drain, 0);
@@ -189,42 +203,41 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         __syncwarp();
     } else if (warp >= kSmWarp0) {
         // ------------------------------------------------ softmax, one query row per thread
+        const int x = (warp - kSmWarp0) >> 2;      // query tile of this warpgroup
         const int qw = warp & 3;
         const uint32_t lane_addr = (uint32_t)(qw * 32) << 16;
+        const uint32_t tb = tmem + lane_addr + x * kTileCols;
         const int qrow = qw * 32 + lane;         // row of the tile
         float m = -INFINITY, l = 0.f;
         bool alive = true;
         for (int j = 0; j < nkv && alive; ++j) {
-            const int b = j & 1;
-            alive = warp_wait_all(&bars->s_full[b], (j >> 1) & 1, abort_flag, dev_err);
+            alive = warp_wait_all(&bars->s_full[x], j & 1, abort_flag, dev_err);
             if (!alive) break;
             tc_fence_after();
             const int kcur = min(seq - j * kKT, kKT);   // valid keys of this tile
-            const uint32_t sa = tmem + lane_addr + b * kKT;
-            uint32_t sv[kKT];
-#pragma unroll
-            for (int c = 0; c < kKT / 32; ++c) tmem_ld32(sa + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&sv[32 * c]));
-            tmem_wait_ld();
-            // row max of the raw scores (scale > 0 commutes with max); keys >= kcur masked.
-            // A full tile (every tile but a chunk's last) takes the max over eight
-            // independent partial maxima -- max is exact in any order -- instead of one
-            // 128-long dependency chain, with no per-key mask.
             const bool full = kcur == kKT;
-            float mxr = -INFINITY;
-            if (full) {
-                float mx[8];
+            // row max of the raw scores (scale > 0 commutes with max), 32 columns per
+            // pass; keys >= kcur masked.  A full tile (every tile but a chunk's last)
+            // keeps eight partial maxima (max is exact in any order) and no per-key mask.
+            float mx[8];
 #pragma unroll
-                for (int k = 0; k < 8; ++k) mx[k] = __uint_as_float(sv[k]);
+            for (int k = 0; k < 8; ++k) mx[k] = -INFINITY;
 #pragma unroll
-                for (int i = 8; i < kKT; i += 8)
+            for (int c = 0; c < kKT / 32; ++c) {
+                uint32_t sv[32];
+                tmem_ld32(tb + 32 * c, sv);
+                tmem_wait_ld();
+                if (full) {
 #pragma unroll
-                    for (int k = 0; k < 8; ++k) mx[k] = fmaxf(mx[k], __uint_as_float(sv[i + k]));
-                mxr = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
-            } else {
+                    for (int i = 0; i < 32; ++i) mx[i & 7] = fmaxf(mx[i & 7], __uint_as_float(sv[i]));
+                } else {
 #pragma unroll
-                for (int i = 0; i < kKT; ++i)
-                    if (i < kcur) mxr = fmaxf(mxr, __uint_as_float(sv[i]));
+                    for (int i = 0; i < 32; ++i)
+                        if (32 * c + i < kcur) mx[i & 7] = fmaxf(mx[i & 7], __uint_as_float(sv[i]));
+                }
             }
+            const float mxr =
+                fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
             const float mn = fmaxf(m, mxr * kScale);
             // exp(s * scale - m') = 2^(s * scale * log2 e - m' * log2 e): one FFMA and the
             // hardware base-2 exponential per element (P is rounded to f16 after it)
@@ -233,75 +246,74 @@ __global__ void __launch_bounds__(kFaThreads, 1)
             // row of the warp grew (rows past the chunk end included), and it must then
             // leave the other rows' O bit-for-bit unchanged
             const float alpha = (m == -INFINITY) ? 0.f : (mn == m ? 1.f : ex2_approx(fmaf(m, kLog2e, -ml)));
+            // P_x(j - 1) must have been read by PV_x(j - 1) before P_x(j) overwrites it;
+            // that also makes O_x complete for the rescale below
+            if (j > 0) {
+                alive = warp_wait_all(&bars->o_done[x], (j - 1) & 1, abort_flag, dev_err);
+                if (!alive) break;
+                tc_fence_after();
+            }
             // row sum of the unrounded P over four partial sums (shorter dependency chains)
             float bq[4] = {0.f, 0.f, 0.f, 0.f};
-            uint32_t pp[kKT / 2];
-            if (full) {
 #pragma unroll
-                for (int i = 0; i < kKT; i += 2) {
-                    const float e0 = ex2_approx(fmaf(__uint_as_float(sv[i]), kScale * kLog2e, -ml));
-                    const float e1 = ex2_approx(fmaf(__uint_as_float(sv[i + 1]), kScale * kLog2e, -ml));
+            for (int c = 0; c < kKT / 32; ++c) {
+                uint32_t sv[32];
+                tmem_ld32(tb + 32 * c, sv);
+                tmem_wait_ld();
+                uint32_t pp[16];
+#pragma unroll
+                for (int i = 0; i < 32; i += 2) {
+                    const int key = 32 * c + i;
+                    const float e0 =
+                        (full || key < kcur) ? ex2_approx(fmaf(__uint_as_float(sv[i]), kScale * kLog2e, -ml)) : 0.f;
+                    const float e1 =
+                        (full || key + 1 < kcur) ? ex2_approx(fmaf(__uint_as_float(sv[i + 1]), kScale * kLog2e, -ml)) : 0.f;
                     bq[(i >> 1) & 3] += e0 + e1;
                     pp[i >> 1] = h2_as_u32(__floats2half2_rn(e0, e1));
                 }
-            } else {
-#pragma unroll
-                for (int i = 0; i < kKT; i += 2) {
-                    const float e0 = i < kcur ? ex2_approx(fmaf(__uint_as_float(sv[i]), kScale * kLog2e, -ml)) : 0.f;
-                    const float e1 = i + 1 < kcur ? ex2_approx(fmaf(__uint_as_float(sv[i + 1]), kScale * kLog2e, -ml)) : 0.f;
-                    bq[(i >> 1) & 3] += e0 + e1;
-                    pp[i >> 1] = h2_as_u32(__floats2half2_rn(e0, e1));
-                }
+                tmem_st16(tb + kPCol + 16 * c, pp);
             }
             const float bs = (bq[0] + bq[1]) + (bq[2] + bq[3]);
             l = l * alpha + bs;
             const bool grew = mn != m;
             m = mn;
-            // P_j over the first 64 columns of S_j (f16 pairs, K-major for the TS MMA)
-            tmem_st32(sa, *reinterpret_cast<uint32_t(*)[32]>(&pp[0]));
-            tmem_st32(sa + 32, *reinterpret_cast<uint32_t(*)[32]>(&pp[32]));
-            if (j > 0) {
-                // O *= alpha, once P_{j-1} V_{j-1} has landed in TMEM; skipped when no
-                // row of the warp has a new maximum (alpha == 1 for all of them)
-                alive = warp_wait_all(&bars->o_done, (j - 1) & 1, abort_flag, dev_err);
-                if (!alive) break;
-            }
             if (j > 0 && __any_sync(0xffffffffu, grew)) {
-                tc_fence_after();
-                const uint32_t oa = tmem + lane_addr + kOCol;
-                uint32_t ov[kHD];
-                tmem_ld32(oa, *reinterpret_cast<uint32_t(*)[32]>(&ov[0]));
-                tmem_ld32(oa + 32, *reinterpret_cast<uint32_t(*)[32]>(&ov[32]));
-                tmem_wait_ld();
+                // O *= alpha; skipped when no row of the warp has a new maximum
+                uint32_t ov[32];
 #pragma unroll
-                for (int i = 0; i < kHD; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
-                tmem_st32(oa, *reinterpret_cast<uint32_t(*)[32]>(&ov[0]));
-                tmem_st32(oa + 32, *reinterpret_cast<uint32_t(*)[32]>(&ov[32]));
+                for (int c = 0; c < kHD / 32; ++c) {
+                    tmem_ld32(tb + kOCol + 32 * c, ov);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
+                    tmem_st32(tb + kOCol + 32 * c, ov);
+                }
             }
             tmem_wait_st();
             tc_fence_before();
-            mbar_arrive(&bars->p_ready[b]);
+            mbar_arrive(&bars->p_ready[x]);
         }
-        if (alive) alive = warp_wait_all(&bars->o_done, (nkv - 1) & 1, abort_flag, dev_err);
+        if (alive) alive = warp_wait_all(&bars->o_done[x], (nkv - 1) & 1, abort_flag, dev_err);
         if (alive) {
             tc_fence_after();
-            const uint32_t oa = tmem + lane_addr + kOCol;
-            uint32_t ov[kHD];
-            tmem_ld32(oa, *reinterpret_cast<uint32_t(*)[32]>(&ov[0]));
-            tmem_ld32(oa + 32, *reinterpret_cast<uint32_t(*)[32]>(&ov[32]));
-            tmem_wait_ld();
-            const int q = q0 + qrow;
-            if (q < seq) {
-                const float inv = 1.0f / (l + 1e-6f);
-                __half *orow = out + (size_t)(row0 + q) * out_stride + h * kHD;
+            const int q = q0 + x * kQT + qrow;
+            const float inv = 1.0f / (l + 1e-6f);
+            __half *orow = out + (size_t)(row0 + q) * out_stride + h * kHD;
 #pragma unroll
-                for (int c = 0; c < kHD / 8; ++c) {
-                    uint4 w;
-                    w.x = h2_as_u32(__floats2half2_rn(__uint_as_float(ov[8 * c]) * inv, __uint_as_float(ov[8 * c + 1]) * inv));
-                    w.y = h2_as_u32(__floats2half2_rn(__uint_as_float(ov[8 * c + 2]) * inv, __uint_as_float(ov[8 * c + 3]) * inv));
-                    w.z = h2_as_u32(__floats2half2_rn(__uint_as_float(ov[8 * c + 4]) * inv, __uint_as_float(ov[8 * c + 5]) * inv));
-                    w.w = h2_as_u32(__floats2half2_rn(__uint_as_float(ov[8 * c + 6]) * inv, __uint_as_float(ov[8 * c + 7]) * inv));
-                    *reinterpret_cast<uint4 *>(orow + 8 * c) = w;
+            for (int c = 0; c < kHD / 32; ++c) {
+                uint32_t ov[32];
+                tmem_ld32(tb + kOCol + 32 * c, ov);
+                tmem_wait_ld();
+                if (q < seq) {
+#pragma unroll
+                    for (int g = 0; g < 4; ++g) {
+                        uint4 w;
+                        w.x = h2_as_u32(__floats2half2_rn(__uint_as_float(ov[8 * g]) * inv, __uint_as_float(ov[8 * g + 1]) * inv));
+                        w.y = h2_as_u32(__floats2half2_rn(__uint_as_float(ov[8 * g + 2]) * inv, __uint_as_float(ov[8 * g + 3]) * inv));
+                        w.z = h2_as_u32(__floats2half2_rn(__uint_as_float(ov[8 * g + 4]) * inv, __uint_as_float(ov[8 * g + 5]) * inv));
+                        w.w = h2_as_u32(__floats2half2_rn(__uint_as_float(ov[8 * g + 6]) * inv, __uint_as_float(ov[8 * g + 7]) * inv));
+                        *reinterpret_cast<uint4 *>(orow + 32 * c + 8 * g) = w;
+                    }
                 }
             }
         }
@@ -343,7 +355,7 @@ cudaError_t launch_flash_enc(const __half *q, const __half *k, const __half *v, 
             return cudaFuncSetAttribute(flash_enc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kFaSmem);
         }))
         return e;
-    const dim3 grid((seq + kQT - 1) / kQT, heads, chunks);
+    const dim3 grid((seq + 2 * kQT - 1) / (2 * kQT), heads, chunks);
     flash_enc_kernel<<<grid, kFaThreads, kFaSmem, st>>>(tmQ, tmK, tmV, out, out_stride, seq, dev_err);
     return cudaGetLastError();
 }
