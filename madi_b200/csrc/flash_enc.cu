@@ -11,10 +11,10 @@
 //   warp 0     TMA producer: the two Q tiles, then K / V tiles of 128 keys through a
 //              3-stage ring (SWIZZLE_128B boxes [128 rows][64 dims]) shared by both;
 //   warp 1     MMA issuer + TMEM owner.  Per key tile j and query tile x in (A, B):
-//              once the softmax of x has published P_x(j), S_x(j+1) = Q_x K_{j+1}^T
+//              once the softmax of x has read S_x(j) (s_free), S_x(j+1) = Q_x K_{j+1}^T
 //              (M = 128 queries, N = 128 keys, K = 64 dims, both operands K-major in
-//              shared memory), then O_x += P_x(j) V_j (TS form: P from TMEM as A, V an
-//              N-contiguous shared-memory B operand);
+//              shared memory); once it has published P_x(j) (p_ready), O_x += P_x(j) V_j
+//              (TS form: P from TMEM as A, V an N-contiguous shared-memory B operand);
 //   warps 4-7  softmax of tile A, warps 8-11 softmax of tile B (thread = query row =
 //              TMEM lane): the row max over S in 32-column passes, then the
 //              exponentials written as f16 pairs into the tile's P columns, O rescaled
@@ -56,6 +56,7 @@ struct __align__(8) FaBars {
     uint64_t kv_full[kNS];
     uint64_t kv_empty[kNS];
     uint64_t s_full[2];     // per query tile: S_x(j) computed
+    uint64_t s_free[2];     // per query tile: S_x(j) read by the softmax (128 arrivals)
     uint64_t p_ready[2];    // per query tile: P_x(j) written, O_x rescaled (128 arrivals)
     uint64_t o_done[2];     // per query tile: PV_x(j) complete
     uint64_t drain;
@@ -118,6 +119,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         }
         for (int x = 0; x < 2; ++x) {
             mbar_init(&bars->s_full[x], 1);
+            mbar_init(&bars->s_free[x], 128);
             mbar_init(&bars->p_ready[x], 128);
             mbar_init(&bars->o_done[x], 1);
         }
@@ -184,10 +186,16 @@ __global__ void __launch_bounds__(kFaThreads, 1)
             for (int j = 0; ok && j < nkv; ++j) {
                 const int s = j % kNS;
                 for (int x = 0; ok && x < 2; ++x) {
+                    // the next S as soon as the softmax has read S_x(j) (it still computes
+                    // the last exponentials and the rescale), then PV_x(j) once P_x(j) is out
+                    if (j + 1 < nkv) {
+                        if (!mbar_wait(&bars->s_free[x], j & 1, abort_flag, dev_err) || !issue_s(x, j + 1)) {
+                            ok = false;
+                            break;
+                        }
+                    }
                     if (!mbar_wait(&bars->p_ready[x], j & 1, abort_flag, dev_err)) { ok = false; break; }
                     tc_fence_after();
-                    // the next S first, so the softmax of x can start on it while PV_x(j) runs
-                    if (j + 1 < nkv && !issue_s(x, j + 1)) { ok = false; break; }
                     // O_x += P_x(j) V_j: K = 128 keys in 8 steps; P columns +8 (16 f16), V rows +16 = 2048 bytes
                     const uint32_t tb = tmem + x * kTileCols;
 #pragma unroll
@@ -219,22 +227,27 @@ __global__ void __launch_bounds__(kFaThreads, 1)
             // row max of the raw scores (scale > 0 commutes with max), 32 columns per
             // pass; keys >= kcur masked.  A full tile (every tile but a chunk's last)
             // keeps eight partial maxima (max is exact in any order) and no per-key mask.
+            // Loads run one chunk ahead of the arithmetic (tcgen05.wait::ld waits for all
+            // of this thread's loads, so chunk c + 1 is in flight while chunk c is used).
             float mx[8];
 #pragma unroll
             for (int k = 0; k < 8; ++k) mx[k] = -INFINITY;
+            uint32_t sv[2][32];
+            tmem_ld32(tb, sv[0]);
+            tmem_wait_ld();
 #pragma unroll
             for (int c = 0; c < kKT / 32; ++c) {
-                uint32_t sv[32];
-                tmem_ld32(tb + 32 * c, sv);
-                tmem_wait_ld();
+                if (c + 1 < kKT / 32) tmem_ld32(tb + 32 * (c + 1), sv[(c + 1) & 1]);
+                const uint32_t (&cv)[32] = sv[c & 1];
                 if (full) {
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) mx[i & 7] = fmaxf(mx[i & 7], __uint_as_float(sv[i]));
+                    for (int i = 0; i < 32; ++i) mx[i & 7] = fmaxf(mx[i & 7], __uint_as_float(cv[i]));
                 } else {
 #pragma unroll
                     for (int i = 0; i < 32; ++i)
-                        if (32 * c + i < kcur) mx[i & 7] = fmaxf(mx[i & 7], __uint_as_float(sv[i]));
+                        if (32 * c + i < kcur) mx[i & 7] = fmaxf(mx[i & 7], __uint_as_float(cv[i]));
                 }
+                if (c + 1 < kKT / 32) tmem_wait_ld();
             }
             const float mxr =
                 fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
@@ -255,23 +268,33 @@ __global__ void __launch_bounds__(kFaThreads, 1)
             }
             // row sum of the unrounded P over four partial sums (shorter dependency chains)
             float bq[4] = {0.f, 0.f, 0.f, 0.f};
+            tmem_ld32(tb, sv[0]);
+            tmem_wait_ld();
 #pragma unroll
             for (int c = 0; c < kKT / 32; ++c) {
-                uint32_t sv[32];
-                tmem_ld32(tb + 32 * c, sv);
-                tmem_wait_ld();
+                if (c + 1 < kKT / 32) tmem_ld32(tb + 32 * (c + 1), sv[(c + 1) & 1]);
+                const uint32_t (&cv)[32] = sv[c & 1];
                 uint32_t pp[16];
 #pragma unroll
                 for (int i = 0; i < 32; i += 2) {
                     const int key = 32 * c + i;
                     const float e0 =
-                        (full || key < kcur) ? ex2_approx(fmaf(__uint_as_float(sv[i]), kScale * kLog2e, -ml)) : 0.f;
+                        (full || key < kcur) ? ex2_approx(fmaf(__uint_as_float(cv[i]), kScale * kLog2e, -ml)) : 0.f;
                     const float e1 =
-                        (full || key + 1 < kcur) ? ex2_approx(fmaf(__uint_as_float(sv[i + 1]), kScale * kLog2e, -ml)) : 0.f;
+                        (full || key + 1 < kcur) ? ex2_approx(fmaf(__uint_as_float(cv[i + 1]), kScale * kLog2e, -ml)) : 0.f;
                     bq[(i >> 1) & 3] += e0 + e1;
                     pp[i >> 1] = h2_as_u32(__floats2half2_rn(e0, e1));
                 }
                 tmem_st16(tb + kPCol + 16 * c, pp);
+                if (c + 1 < kKT / 32) {
+                    tmem_wait_ld();
+                    if (c + 2 == kKT / 32) {
+                        // the last chunk of S_x(j) is in registers: the MMA thread may
+                        // overwrite S_x with S_x(j + 1)
+                        tc_fence_before();
+                        mbar_arrive(&bars->s_free[x]);
+                    }
+                }
             }
             const float bs = (bq[0] + bq[1]) + (bq[2] + bq[3]);
             l = l * alpha + bs;
