@@ -558,7 +558,10 @@ def e2e_leg(args, world, dev, X, W1, W2, b1, b2, gemm_flops):
     streams -- H2D of chunk i+1, the two GEMMs of chunk i and D2H of chunk i-1 run at
     once (one cudaMemcpyAsync per chunk and direction) -- with two sets of device
     buffers alternating between steps so that step s+1's copies may start while
-    step s finishes.  Events order every reuse of a device buffer."""
+    step s finishes.  Events order every reuse of a device buffer.  The same pipeline
+    without the GEMMs is timed first: `copies_only_ms_per_step` is the box's host <->
+    device bound for the step (pinned-copy bandwidth differs between boxes), and
+    `frac_of_copy_bound` how close the end-to-end step comes to it."""
     import torch
     from madi_b200 import q8
     M = X.shape[0]
@@ -577,7 +580,7 @@ def e2e_leg(args, world, dev, X, W1, W2, b1, b2, gemm_flops):
     comp_done = [[None] * nch for _ in range(2)]
     out_done = [[None] * nch for _ in range(2)]
 
-    def step(si):
+    def step(si, compute=True):
         p = si % 2
         B = sets[p]
         for c, (r0, r1) in enumerate(bounds):
@@ -592,9 +595,10 @@ def e2e_leg(args, world, dev, X, W1, W2, b1, b2, gemm_flops):
                 if out_done[p][c] is not None:
                     s_mm.wait_event(out_done[p][c])           # Y rows free: step si-2 copied them out
                 Xc = B["X"][r0:r1]
-                q8.linear(W1, Xc, bias=b1, epi=q8.EPI_BIAS_GELU, out=B["H"][r0:r1], stream=s_mm)
-                q8.linear(W2, B["H"][r0:r1], bias=b2, epi=q8.EPI_BIAS_RES, residual=Xc, out=B["Y"][r0:r1],
-                          stream=s_mm)
+                if compute:
+                    q8.linear(W1, Xc, bias=b1, epi=q8.EPI_BIAS_GELU, out=B["H"][r0:r1], stream=s_mm)
+                    q8.linear(W2, B["H"][r0:r1], bias=b2, epi=q8.EPI_BIAS_RES, residual=Xc, out=B["Y"][r0:r1],
+                              stream=s_mm)
                 comp_done[p][c] = ev()
                 comp_done[p][c].record(s_mm)
             with torch.cuda.stream(s_out):
@@ -603,27 +607,34 @@ def e2e_leg(args, world, dev, X, W1, W2, b1, b2, gemm_flops):
                 out_done[p][c] = ev()
                 out_done[p][c].record(s_out)
 
-    for si in range(3):
-        step(si)
-    torch.cuda.synchronize()
-    barrier(world)
     Ke = max(3, min(args.steps, 20))
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     cur = torch.cuda.current_stream(dev)
-    e0.record(cur)
-    for s_ in (s_in, s_mm, s_out):
-        s_.wait_event(e0)
-    for si in range(Ke):
-        step(si)
-    e1.record(s_out)
-    torch.cuda.synchronize()
-    ms_e2e = max_over_ranks(world, e0.elapsed_time(e1) / Ke)
+
+    def timed(compute):
+        for si in range(3):
+            step(si, compute)
+        torch.cuda.synchronize()
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(cur)
+        for s_ in (s_in, s_mm, s_out):
+            s_.wait_event(e0)
+        for si in range(Ke):
+            step(si, compute)
+        e1.record(s_out)
+        torch.cuda.synchronize()
+        return max_over_ranks(world, e0.elapsed_time(e1) / Ke)
+
+    # the same copies alone (no GEMMs): this box's host <-> device bound for the step
+    ms_copy = timed(False)
+    ms_e2e = timed(True)
     ok = torch.equal(Yh[:8].to(dev), sets[(Ke - 1) % 2]["Y"][:8])
     del sets, Xh, Yh
     torch.cuda.empty_cache()
     return {"value": 2 * gemm_flops * world / (ms_e2e / 1e3) / 1e12, "unit": "TFLOP/s",
             "h2d_bytes_per_step": M * D * 2, "d2h_bytes_per_step": M * D * 2, "ms_per_step": ms_e2e,
             "pipeline": f"{nch} row chunks per step over H2D / compute / D2H streams, two device buffer sets",
+            "copies_only_ms_per_step": ms_copy, "frac_of_copy_bound": ms_copy / ms_e2e,
             "host_copy_matches": bool(ok)}
 
 
