@@ -248,47 +248,51 @@ __global__ void __launch_bounds__(kThr) attn_kernel(const __grid_constant__ CUte
 // K / V, 32 for f32: 16 KB of K and V per stage): a producer warp keeps a ring of
 // `stages` TMA slots in flight ([kR][64] K and V boxes), and each of the 8
 // consumer warps runs its own online softmax over its kR / 8 keys of every stage
-// -- running max m_w, sum l_w and the partial output over the 64 dims (2 per
-// lane), rescaled by exp2((m_old - m_new) log2 e) when m_w grows -- with no
-// block-wide barrier per stage.  8 lanes form a key's score (4 keys per pass).
+// -- running max m_w, sum l_w and the partial output, rescaled by
+// exp2((m_old - m_new) log2 e) when m_w grows -- with no block-wide barrier per
+// stage.  A group of 8 lanes forms a key's score (4 keys per pass), each lane over
+// 8 dims with packed f32x2 FMAs, and the same lane then accumulates p * v for its
+// key over the same 8 dims (one 16-byte V load, no shuffle); the four groups'
+// outputs are added after the stream.
 // At the end the warps' (m, l, o) and then the cluster's CTAs are recombined by
 // log-sum-exp, as flash_cross_attn_reduce does.
 constexpr int kMaxStages = 8;
 constexpr int kThrS = 288;                                 // 8 consumer warps + 1 producer warp
 
-template <typename KV>
-MADI_DEV float dot8(const KV *kr, int li, const float (&qv)[8]);
-template <>
-MADI_DEV float dot8<__half>(const __half *kr, int li, const float (&qv)[8]) {
-    const uint4 u = *reinterpret_cast<const uint4 *>(kr + 8 * li);           // dims 8li .. 8li+7
+// The eight dims of a row that lane li of a key group handles (dim_of(li, i), i < 8):
+// for f16 rows 8li .. 8li+7, for f32 rows 4li .. 4li+3 and 32+4li .. 32+4li+3, so
+// that the 8 lanes of a group read 128 contiguous bytes per 16-byte load.
+template <typename KV> MADI_DEV int dim_of(int li, int i);
+template <> MADI_DEV int dim_of<__half>(int li, int i) { return 8 * li + i; }
+template <> MADI_DEV int dim_of<float>(int li, int i) { return i < 4 ? 4 * li + i : 32 + 4 * li + (i - 4); }
+// Those eight elements of a K or V row, as f32.
+template <typename KV> MADI_DEV void ld8(const KV *r, int li, float (&f)[8]);
+template <> MADI_DEV void ld8<__half>(const __half *r, int li, float (&f)[8]) {
+    const uint4 u = *reinterpret_cast<const uint4 *>(r + 8 * li);
     const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-    float d = 0.f;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-        const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&w[i]));
-        d = fmaf(qv[2 * i], f.x, d);
-        d = fmaf(qv[2 * i + 1], f.y, d);
+        const float2 v = __half22float2(*reinterpret_cast<const __half2 *>(&w[i]));
+        f[2 * i] = v.x;
+        f[2 * i + 1] = v.y;
     }
-    return d;
 }
-template <>
-MADI_DEV float dot8<float>(const float *kr, int li, const float (&qv)[8]) {
-    const float4 a = *reinterpret_cast<const float4 *>(kr + 4 * li);         // dims 4li .. 4li+3
-    const float4 b = *reinterpret_cast<const float4 *>(kr + 32 + 4 * li);    // dims 32+4li .. 32+4li+3
-    float d = qv[0] * a.x;
-    d = fmaf(qv[1], a.y, d);
-    d = fmaf(qv[2], a.z, d);
-    d = fmaf(qv[3], a.w, d);
-    d = fmaf(qv[4], b.x, d);
-    d = fmaf(qv[5], b.y, d);
-    d = fmaf(qv[6], b.z, d);
-    d = fmaf(qv[7], b.w, d);
-    return d;
+template <> MADI_DEV void ld8<float>(const float *r, int li, float (&f)[8]) {
+    const float4 a = *reinterpret_cast<const float4 *>(r + 4 * li);
+    const float4 b = *reinterpret_cast<const float4 *>(r + 32 + 4 * li);
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+    f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
 }
-// The q dims lane li multiplies in dot8.
-template <typename KV> MADI_DEV int q_dim(int li, int i);
-template <> MADI_DEV int q_dim<__half>(int li, int i) { return 8 * li + i; }
-template <> MADI_DEV int q_dim<float>(int li, int i) { return i < 4 ? 4 * li + i : 32 + 4 * li + (i - 4); }
+// This lane's part of q . k over its eight dims, in two interleaved f32 partial sums
+// (packed f32x2 FMAs).
+template <typename KV> MADI_DEV float dot8(const KV *kr, int li, const float (&qv)[8]) {
+    float k[8];
+    ld8<KV>(kr, li, k);
+    float d0 = 0.f, d1 = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) fma2(d0, d1, qv[2 * i], qv[2 * i + 1], k[2 * i], k[2 * i + 1], d0, d1);
+    return d0 + d1;
+}
 
 template <typename KV> struct StreamRows { static constexpr int kR = sizeof(KV) == 2 ? 64 : 32; };
 
@@ -339,7 +343,10 @@ __global__ void __launch_bounds__(kThrS, 4) attn_stream_kernel(const __grid_cons
     if (tid < kHd * G) qh[tid / kHd][tid % kHd] = q[(size_t)b * D + hp * G * kHd + tid];
     __syncthreads();
 
-    float m_w = -INFINITY, l_w = 0.f, o0 = 0.f, o1 = 0.f;
+    // consumer state: running max / sum of this warp and, per lane, its eight output
+    // dims accumulated over the keys of the lane's group kq (summed over the four
+    // groups after the stream)
+    float m_w = -INFINITY, l_w = 0.f, o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     if (warp == 8) {
         // ------------------------------------------------ producer
         if (lane == 0) {
@@ -368,7 +375,7 @@ __global__ void __launch_bounds__(kThrS, 4) attn_stream_kernel(const __grid_cons
         const int li = lane & 7, kq = lane >> 3;          // 8 lanes per key, 4 keys per pass
         float qv[8];
 #pragma unroll
-        for (int i2 = 0; i2 < 8; ++i2) qv[i2] = qh[g][q_dim<KV>(li, i2)];
+        for (int i2 = 0; i2 < 8; ++i2) qv[i2] = qh[g][dim_of<KV>(li, i2)];
         const float rsq = rsqrtf((float)kHd);
         const int kb = wl_ * kKeysPerWarp;                // this warp's keys in each stage
         for (int j = 0; j < nsub; ++j) {
@@ -399,32 +406,36 @@ __global__ void __launch_bounds__(kThrS, 4) attn_stream_kernel(const __grid_cons
                 const float alpha = exp2f((m_w - m_new) * kLog2e);
                 m_w = m_new;
                 l_w *= alpha;
-                o0 *= alpha;
-                o1 *= alpha;
+#pragma unroll
+                for (int i2 = 0; i2 < 8; i2 += 2) mul2(o[i2], o[i2 + 1], o[i2], o[i2 + 1], alpha, alpha);
 #pragma unroll
                 for (int p = 0; p < kPasses; ++p) {
+                    const int k = kb + 4 * p + kq;          // this lane's key (the 8 lanes of kq agree on e)
                     const float e = exp2f((sc[p] - m_w) * kLog2e);     // 0 for a missing key
                     l_w += e;                                         // per key group; summed below
+                    if (k < rj) {
+                        float v[8];
+                        ld8<KV>(vs + (size_t)k * kW, li, v);
 #pragma unroll
-                    for (int g4 = 0; g4 < 4; ++g4) {
-                        const int k = kb + 4 * p + g4;
-                        const float ek = __shfl_sync(0xffffffffu, e, 8 * g4);
-                        if (k < rj) {
-                            const float2 v = ld2(vs + (size_t)k * kW + 2 * lane);
-                            o0 = fmaf(ek, v.x, o0);
-                            o1 = fmaf(ek, v.y, o1);
-                        }
+                        for (int i2 = 0; i2 < 8; i2 += 2) fma2(o[i2], o[i2 + 1], e, e, v[i2], v[i2 + 1], o[i2], o[i2 + 1]);
                     }
                 }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
         }
-        // l_w holds the sum of one key group; the 8 lanes of a group agree
+        // l_w and o hold the sums over one key group; the four groups are added
         l_w += __shfl_xor_sync(0xffffffffu, l_w, 8);
         l_w += __shfl_xor_sync(0xffffffffu, l_w, 16);
-        wo[warp][2 * lane] = o0;
-        wo[warp][2 * lane + 1] = o1;
+#pragma unroll
+        for (int i2 = 0; i2 < 8; ++i2) {
+            o[i2] += __shfl_xor_sync(0xffffffffu, o[i2], 8);
+            o[i2] += __shfl_xor_sync(0xffffffffu, o[i2], 16);
+        }
+        if (kq == 0) {
+#pragma unroll
+            for (int i2 = 0; i2 < 8; ++i2) wo[warp][dim_of<KV>(li, i2)] = o[i2];
+        }
         if (lane == 0) {
             wm[warp] = m_w;
             wl[warp] = l_w;
