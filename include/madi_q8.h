@@ -209,10 +209,11 @@ int madi_q8_qkv(const madi_q8w *w, const float *x, int m,
                 float *kc, float *vc, const uint32_t *pos, int64_t cache_stride,
                 void *stream);
 
-/* madi_q8_qkv with an activation type (same reference kernel): x_dtype MADI_F32, or
+/* madi_q8_qkv with an activation type (same reference kernel): x_dtype MADI_F32;
  * MADI_F32_AS_F16 -- x f32 rounded to f16 as it is loaded, as the reference's batched
- * decode (decodeBlockBatched, decoder.zig:337-341) rounds its activations. */
-int madi_q8_qkv_ex(const madi_q8w *w, const float *x, int x_dtype, int m,
+ * decode (decodeBlockBatched, decoder.zig:337-341) rounds its activations; or MADI_F16
+ * -- x already f16 [m][D] (e.g. from madi_layer_norm_y16), the same values. */
+int madi_q8_qkv_ex(const madi_q8w *w, const void *x, int x_dtype, int m,
                    const float *qb, const float *vb, float *q_out,
                    float *kc, float *vc, const uint32_t *pos, int64_t cache_stride,
                    void *stream);
@@ -251,6 +252,16 @@ int madi_bias_res_ln(float *x, const float *mo, const float *bias, float *y, con
                      int rows, int d, float eps, void *stream);
 int madi_layer_norm(const float *x, float *y, const float *gamma, const float *beta, int rows, int d, float eps,
                     void *stream);
+
+/* The same two with y written as f16 (round to nearest): the LayerNorm and the
+ * f32 -> f16 conversion the reference's batched decode applies to a projection's
+ * input (decodeBlockBatched, decoder.zig:337-341) in one pass -- bit-equal to
+ * madi_bias_res_ln / madi_layer_norm followed by that rounding.  No single
+ * reference kernel; y rows 8-byte aligned. */
+int madi_bias_res_ln_y16(float *x, const float *mo, const float *bias, uint16_t *y, const float *gamma,
+                         const float *beta, int rows, int d, float eps, void *stream);
+int madi_layer_norm_y16(const float *x, uint16_t *y, const float *gamma, const float *beta, int rows, int d,
+                        float eps, void *stream);
 
 /* ======================= GPU-resident greedy decode step ==================== */
 

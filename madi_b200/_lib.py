@@ -61,6 +61,8 @@ SIGNATURES = {
     "madi_layer_norm_f16": ([P, P, P, P, I, I, ctypes.c_float, P], I),
     "madi_bias_res_ln": ([P, P, P, P, P, P, I, I, ctypes.c_float, P], I),
     "madi_layer_norm": ([P, P, P, P, I, I, ctypes.c_float, P], I),
+    "madi_bias_res_ln_y16": ([P, P, P, P, P, P, I, I, ctypes.c_float, P], I),
+    "madi_layer_norm_y16": ([P, P, P, P, I, I, ctypes.c_float, P], I),
     "madi_emb_lookup_q8": ([ctypes.POINTER(madi_q8w), P, P, I, ctypes.c_int64, I, P, P], I),
     "madi_emb_pos_q8": ([ctypes.POINTER(madi_q8w), P, P, I, ctypes.c_int64, I, P, I, P, P], I),
     "madi_argmax_conf": ([P, I, I, P, P, P, I, ctypes.c_int64, P], I),

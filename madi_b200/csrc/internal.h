@@ -108,6 +108,9 @@ cudaError_t launch_res_ln(float *X, const __half *MO, const float *bias, __half 
                           const float *beta, int rows, int D, float eps, cudaStream_t st);
 cudaError_t launch_res_ln_f32(float *X, const float *MO, const float *bias, float *Y, const float *gamma,
                               const float *beta, int rows, int D, float eps, cudaStream_t st);
+// MO f32, Y f16 (round to nearest): the decoder's forms feeding f16-activation projections.
+cudaError_t launch_res_ln_f32_y16(float *X, const float *MO, const float *bias, __half *Y, const float *gamma,
+                                  const float *beta, int rows, int D, float eps, cudaStream_t st);
 
 // ---------------------------------------------------------------- decode-step primitives (decode_step.cu)
 constexpr int kWhisperVocab = 51866;   // VOCAB of graph_helpers.metal:9 (the by-name kernels assume it)

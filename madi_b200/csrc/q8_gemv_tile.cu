@@ -544,8 +544,11 @@ cudaError_t launch_gemv_tile(const GemvArgs &a, bool x_f32, bool y_f32, int epi,
     if (!make_plan(a.M, a.N, a.K, x_f32 && !x_r16, num_sms, &pl, &grid)) return cudaErrorInvalidValue;
     CUtensorMap tmq, tms;
     if (!make_tile_maps(a, pl.kslice, &tmq, &tms)) return cudaErrorNotSupported;
-    if (qkv) return x_r16 ? launch_tile_one<float, float, kEpiNone, true, true>(a, tmq, tms, pl, grid, dev_err, st, pdl)
-                          : launch_tile_one<float, float, kEpiNone, true>(a, tmq, tms, pl, grid, dev_err, st, pdl);
+    if (qkv) {
+        if (!x_f32) return launch_tile_one<__half, float, kEpiNone, true>(a, tmq, tms, pl, grid, dev_err, st, pdl);
+        return x_r16 ? launch_tile_one<float, float, kEpiNone, true, true>(a, tmq, tms, pl, grid, dev_err, st, pdl)
+                     : launch_tile_one<float, float, kEpiNone, true>(a, tmq, tms, pl, grid, dev_err, st, pdl);
+    }
 #define MADI_TILE_CASE(XT, YT)                                                                                   \
     switch (epi) {                                                                                               \
         case kEpiNone: return launch_tile_one<XT, YT, kEpiNone, false>(a, tmq, tms, pl, grid, dev_err, st, pdl); \

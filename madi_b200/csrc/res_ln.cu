@@ -5,7 +5,7 @@
 //       Y[r][i]  = half((X[r][i] - mean) * inv * gamma[i] + beta[i])
 //   layer_norm_f16  (encoder_ops.metal:305-331): the same without the residual add.
 //   bias_res_ln / layer_norm (encoder_ops.metal:14-120, the decoder's forms): MO
-//       and Y in f32.
+//       and Y in f32; or MO f32 and Y f16 (the decoder with f16 activations).
 //   mean = sum(X[r]) / D, inv = rsqrt(sum((X[r] - mean)^2) / D + eps) (two passes;
 //   the row arithmetic of ln_row.cuh).
 //
@@ -127,6 +127,11 @@ cudaError_t launch_ln(float *X, const MT *MO, const float *bias, YT *Y, const fl
 cudaError_t launch_res_ln(float *X, const __half *MO, const float *bias, __half *Y, const float *gamma,
                           const float *beta, int rows, int D, float eps, cudaStream_t st) {
     return launch_ln<__half, __half>(X, MO, bias, Y, gamma, beta, rows, D, eps, st);
+}
+
+cudaError_t launch_res_ln_f32_y16(float *X, const float *MO, const float *bias, __half *Y, const float *gamma,
+                                  const float *beta, int rows, int D, float eps, cudaStream_t st) {
+    return launch_ln<float, __half>(X, MO, bias, Y, gamma, beta, rows, D, eps, st);
 }
 
 cudaError_t launch_res_ln_f32(float *X, const float *MO, const float *bias, float *Y, const float *gamma,

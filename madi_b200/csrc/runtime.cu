@@ -202,9 +202,11 @@ int q8_linear_impl(const madi_q8w *w, const void *x, int x_dtype, int m, const v
     return MADI_OK;
 }
 
-int q8_qkv_impl(const madi_q8w *w, const float *x, int m, const float *qb, const float *vb, float *q_out, float *kc,
+// x_dtype: MADI_F32, MADI_F32_AS_F16 (f32 rounded to f16 as it is loaded) or MADI_F16.
+int q8_qkv_impl(const madi_q8w *w, const void *x, int m, const float *qb, const float *vb, float *q_out, float *kc,
                 float *vc, const uint32_t *pos, long long cache_stride, cudaStream_t st, const char *who,
-                bool x_r16 = false) {
+                int x_dtype = MADI_F32) {
+    const bool x_r16 = x_dtype == MADI_F32_AS_F16, x_f32 = x_dtype != MADI_F16;
     if (!S.ready) return fail(MADI_ENOINIT, "%s: madi_init has not succeeded", who);
     if (!w || !w->qs || !w->scales || !x || !qb || !vb || !q_out || !kc || !vc || !pos)
         return fail(MADI_EINVAL, "%s: null argument", who);
@@ -213,8 +215,8 @@ int q8_qkv_impl(const madi_q8w *w, const float *x, int m, const float *qb, const
     if (m <= 0 || m > kGemvMaxM) return fail(MADI_EINVAL, "%s: m=%d outside 1..%d", who, m, kGemvMaxM);
     if (!aligned(x, 16) || !aligned(w->qs, 16)) return fail(MADI_EINVAL, "%s: misaligned x or qs", who);
     const int ks = gemv_pick_ks(3 * D, D, S.num_sms);
-    const bool tile_path = aligned(w->scales, 16) && gemv_tile_ok(m, 3 * D, D, !x_r16, S.num_sms);
-    if (!tile_path && (m > 8 || x_r16 || gemv_smem_bytes(m, D, ks, true) > (size_t)S.max_smem_optin))
+    const bool tile_path = aligned(w->scales, 16) && gemv_tile_ok(m, 3 * D, D, x_f32 && !x_r16, S.num_sms);
+    if (!tile_path && (m > 8 || !x_f32 || x_r16 || gemv_smem_bytes(m, D, ks, true) > (size_t)S.max_smem_optin))
         return fail(MADI_EINVAL, "%s: D=%d at m=%d does not fit the decode path", who, D, m);
     GemvArgs a{};
     a.qs = w->qs;
@@ -225,7 +227,7 @@ int q8_qkv_impl(const madi_q8w *w, const float *x, int m, const float *qb, const
     a.qb = qb; a.vb = vb; a.kc = kc; a.vc = vc; a.pos = pos;
     a.cache_stride = m > 1 ? cache_stride : 0;
     a.D = D;
-    cudaError_t e = tile_path ? launch_gemv_tile(a, true, true, MADI_EPI_NONE, true, S.num_sms, S.dev_err, st, S.pdl,
+    cudaError_t e = tile_path ? launch_gemv_tile(a, x_f32, true, MADI_EPI_NONE, true, S.num_sms, S.dev_err, st, S.pdl,
                                                  x_r16)
                               : launch_gemv(a, true, true, MADI_EPI_NONE, true, st, S.pdl);
     if (e == cudaErrorNotSupported) return fail(MADI_EUNSUPPORTED, "%s: cuTensorMapEncodeTiled unavailable", who);
@@ -801,15 +803,15 @@ int madi_q8_linear(const madi_q8w *w, const void *x, int x_dtype, int m, const v
 int madi_q8_qkv(const madi_q8w *w, const float *x, int m, const float *qb, const float *vb, float *q_out, float *kc,
                 float *vc, const uint32_t *pos, int64_t cache_stride, void *stream) {
     return q8_qkv_impl(w, x, m, qb, vb, q_out, kc, vc, pos, (long long)cache_stride, pick_stream(stream), "madi_q8_qkv",
-                       false);
+                       MADI_F32);
 }
 
-int madi_q8_qkv_ex(const madi_q8w *w, const float *x, int x_dtype, int m, const float *qb, const float *vb,
+int madi_q8_qkv_ex(const madi_q8w *w, const void *x, int x_dtype, int m, const float *qb, const float *vb,
                    float *q_out, float *kc, float *vc, const uint32_t *pos, int64_t cache_stride, void *stream) {
-    if (x_dtype != MADI_F32 && x_dtype != MADI_F32_AS_F16)
-        return fail(MADI_EINVAL, "madi_q8_qkv_ex: x_dtype %d (MADI_F32 or MADI_F32_AS_F16)", x_dtype);
+    if (x_dtype != MADI_F32 && x_dtype != MADI_F32_AS_F16 && x_dtype != MADI_F16)
+        return fail(MADI_EINVAL, "madi_q8_qkv_ex: x_dtype %d (MADI_F32, MADI_F16 or MADI_F32_AS_F16)", x_dtype);
     return q8_qkv_impl(w, x, m, qb, vb, q_out, kc, vc, pos, (long long)cache_stride, pick_stream(stream),
-                       "madi_q8_qkv_ex", x_dtype == MADI_F32_AS_F16);
+                       "madi_q8_qkv_ex", x_dtype);
 }
 
 int madi_q8_dequant_f16(const madi_q8w *w, uint16_t *out, void *stream) {
@@ -832,25 +834,29 @@ int madi_q8_quantize_f16(const uint16_t *w, int rows, int dim, int8_t *qs, uint1
 }
 
 namespace {
-// f32 = false: MO and Y f16 (the encoder's *_f16 forms); true: MO and Y f32 (the decoder's).
+// Operand types: kLnF16 MO and Y f16 (the encoder's *_f16 forms); kLnF32 MO and Y f32
+// (the decoder's); kLnF32Y16 MO f32, Y f16 (the decoder's, feeding f16 activations).
+enum LnTypes { kLnF16 = 0, kLnF32 = 1, kLnF32Y16 = 2 };
 int res_ln_impl(float *x, const void *mo, const float *bias, void *y, const float *gamma, const float *beta, int rows,
-                int d, float eps, void *stream, const char *who, bool f32 = false) {
+                int d, float eps, void *stream, const char *who, int types = kLnF16) {
     if (!S.ready) return fail(MADI_ENOINIT, "%s: not initialised", who);
     if (!x || !y || !gamma || !beta || (mo && !bias)) return fail(MADI_EINVAL, "%s: null argument", who);
     if (rows < 0 || d < 128 || d > kLnMaxD || d % 128)
         return fail(MADI_EINVAL, "%s: rows=%d, D=%d (need 128 <= D <= %d, D %% 128 == 0)", who, rows, d, kLnMaxD);
     if (!(eps >= 0.f) || eps > 1.f) return fail(MADI_EINVAL, "%s: eps=%g", who, (double)eps);
-    const size_t ya = f32 ? 16 : 8;
-    if (!aligned(x, 16) || !aligned(gamma, 16) || !aligned(beta, 16) || !aligned(y, ya) || (mo && !aligned(mo, ya)) ||
+    const size_t ya = types == kLnF32 ? 16 : 8, ma = types == kLnF16 ? 8 : 16;
+    if (!aligned(x, 16) || !aligned(gamma, 16) || !aligned(beta, 16) || !aligned(y, ya) || (mo && !aligned(mo, ma)) ||
         (bias && !aligned(bias, 16)))
         return fail(MADI_EINVAL, "%s: misaligned buffer (f32 rows 16-byte, f16 rows 8-byte aligned)", who);
     if ((size_t)rows * (size_t)d >= (1ull << 31)) return fail(MADI_EINVAL, "%s: too large", who);
     if (rows == 0) return MADI_OK;
     cudaError_t e =
-        f32 ? launch_res_ln_f32(x, static_cast<const float *>(mo), bias, static_cast<float *>(y), gamma, beta, rows, d,
-                                eps, pick_stream(stream))
-            : launch_res_ln(x, static_cast<const __half *>(mo), bias, static_cast<__half *>(y), gamma, beta, rows, d,
-                            eps, pick_stream(stream));
+        types == kLnF32    ? launch_res_ln_f32(x, static_cast<const float *>(mo), bias, static_cast<float *>(y), gamma,
+                                               beta, rows, d, eps, pick_stream(stream))
+        : types == kLnF32Y16 ? launch_res_ln_f32_y16(x, static_cast<const float *>(mo), bias, static_cast<__half *>(y),
+                                                   gamma, beta, rows, d, eps, pick_stream(stream))
+                           : launch_res_ln(x, static_cast<const __half *>(mo), bias, static_cast<__half *>(y), gamma,
+                                           beta, rows, d, eps, pick_stream(stream));
     return e == cudaSuccess ? MADI_OK : cuda_fail(e, who);
 }
 }  // namespace
@@ -858,13 +864,25 @@ int res_ln_impl(float *x, const void *mo, const float *bias, void *y, const floa
 int madi_bias_res_ln(float *x, const float *mo, const float *bias, float *y, const float *gamma, const float *beta,
                      int rows, int d, float eps, void *stream) {
     if (!mo) return fail(MADI_EINVAL, "madi_bias_res_ln: null MO");
-    return res_ln_impl(x, mo, bias, y, gamma, beta, rows, d, eps, stream, "madi_bias_res_ln", true);
+    return res_ln_impl(x, mo, bias, y, gamma, beta, rows, d, eps, stream, "madi_bias_res_ln", kLnF32);
 }
 
 int madi_layer_norm(const float *x, float *y, const float *gamma, const float *beta, int rows, int d, float eps,
                     void *stream) {
     return res_ln_impl(const_cast<float *>(x), nullptr, nullptr, y, gamma, beta, rows, d, eps, stream, "madi_layer_norm",
-                       true);
+                       kLnF32);
+}
+
+int madi_bias_res_ln_y16(float *x, const float *mo, const float *bias, uint16_t *y, const float *gamma,
+                         const float *beta, int rows, int d, float eps, void *stream) {
+    if (!mo) return fail(MADI_EINVAL, "madi_bias_res_ln_y16: null MO");
+    return res_ln_impl(x, mo, bias, y, gamma, beta, rows, d, eps, stream, "madi_bias_res_ln_y16", kLnF32Y16);
+}
+
+int madi_layer_norm_y16(const float *x, uint16_t *y, const float *gamma, const float *beta, int rows, int d, float eps,
+                        void *stream) {
+    return res_ln_impl(const_cast<float *>(x), nullptr, nullptr, y, gamma, beta, rows, d, eps, stream,
+                       "madi_layer_norm_y16", kLnF32Y16);
 }
 
 int madi_bias_res_ln_f16(float *x, const uint16_t *mo, const float *bias, uint16_t *y, const float *gamma,

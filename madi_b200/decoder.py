@@ -123,7 +123,9 @@ class Decoder:
                  exchange: Optional[Callable[[torch.Tensor, torch.Tensor], None]] = None):
         """act16: the projections take their f32 activations rounded to f16, as the
         reference's batched decode (decodeBlockBatched, decoder.zig:337-341) converts
-        them; False keeps the single-token GEMV family's f32 activations.
+        them; False keeps the single-token GEMV family's f32 activations.  With act16
+        the LayerNorms and fc1 write their outputs as f16 (the same rounding, done by
+        the producer), so the projections stage half the activation bytes.
         split: (world, rank) for the column-split vocab head (see the module
         docstring); exchange(out, inp): all-gather of inp from every rank into out,
         rank-major (default: torch.distributed.all_gather_into_tensor)."""
@@ -148,8 +150,10 @@ class Decoder:
         self.ln_post = (t(w["ln_post"][0]), t(w["ln_post"][1]))
         S = slots
         f32 = dict(dtype=torch.float32, device=device)
-        self.x, self.xb, self.q, self.ao, self.mo = (torch.zeros((S, D), **f32) for _ in range(5))
-        self.mh = torch.zeros((S, F), **f32)
+        act = dict(dtype=torch.float16 if act16 else torch.float32, device=device)   # projection inputs
+        self.x, self.q, self.ao, self.mo = (torch.zeros((S, D), **f32) for _ in range(4))
+        self.xb = torch.zeros((S, D), **act)
+        self.mh = torch.zeros((S, F), **act)
         self.kc = [torch.zeros((S, MAX_TOK, D), **f32) for _ in range(LAYERS)]
         self.vc = [torch.zeros((S, MAX_TOK, D), **f32) for _ in range(LAYERS)]
         self.ck = [None] * LAYERS
@@ -172,7 +176,7 @@ class Decoder:
             self.tokens = self.tokens_all[rank * S:(rank + 1) * S]
             self.conf = self.conf_all[rank * S:(rank + 1) * S]
             self.pos = self.pos_all[rank * S:(rank + 1) * S]
-            self.xb_all = torch.zeros((R, D), **f32)
+            self.xb_all = torch.zeros((R, D), **act)
             self.logits = torch.zeros((R, self.h1 - self.h0), **f32)
             self.part = torch.zeros((R, 4), **f32)
             self.parts = torch.zeros((world, R, 4), **f32)

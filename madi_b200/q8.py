@@ -92,16 +92,17 @@ def linear(w: Q8Weight, x: torch.Tensor, bias: Optional[torch.Tensor] = None, ep
 
 def qkv(w: Q8Weight, x: torch.Tensor, qb: torch.Tensor, vb: torch.Tensor, kc: torch.Tensor, vc: torch.Tensor,
         pos: torch.Tensor, q_out: Optional[torch.Tensor] = None, stream=None, x_round16: bool = False) -> torch.Tensor:
-    """Fused decoder QKV (gemv_q8_qkv).  x f32 [m][D]; kc/vc f32 [m][max_tok][D]
-    (or [max_tok][D] for m == 1); pos u32/int32 [m] on the device.  x_round16: x
+    """Fused decoder QKV (gemv_q8_qkv).  x f32 or f16 [m][D]; kc/vc f32 [m][max_tok][D]
+    (or [max_tok][D] for m == 1); pos u32/int32 [m] on the device.  x_round16: f32 x
     rounded to f16 as it is loaded (the batched decode's activations)."""
     m, D = x.shape
     if q_out is None:
         q_out = torch.empty((m, D), dtype=torch.float32, device=x.device)
     stride = kc.stride(0) if kc.dim() == 3 else 0
     h = w.handle()
-    if x_round16:
-        rc = _lib.load().madi_q8_qkv_ex(ctypes.byref(h), x.data_ptr(), MADI_F32_AS_F16, m, qb.data_ptr(),
+    if x_round16 or x.dtype == torch.float16:
+        dt = MADI_F16 if x.dtype == torch.float16 else MADI_F32_AS_F16
+        rc = _lib.load().madi_q8_qkv_ex(ctypes.byref(h), x.data_ptr(), dt, m, qb.data_ptr(),
                                         vb.data_ptr(), q_out.data_ptr(), kc.data_ptr(), vc.data_ptr(), pos.data_ptr(),
                                         stride, _stream(stream))
         _lib.check(rc, "madi_q8_qkv_ex")
@@ -186,30 +187,39 @@ def layer_norm_f16(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, eps
     return out
 
 
+def _ln_out(out, rows, d, x):
+    if out is None:
+        return torch.empty((rows, d), dtype=torch.float32, device=x.device)
+    if out.shape != (rows, d) or out.dtype not in (torch.float32, torch.float16) or not out.is_contiguous():
+        raise ValueError("out must be a contiguous f32 or f16 tensor shaped like x")
+    return out
+
+
 def bias_res_ln(x: torch.Tensor, mo: torch.Tensor, bias: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor,
                 eps: float = 1e-5, out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
     """bias_res_ln (encoder_ops.metal:69-120), the decoder's f32 form: x (updated in
-    place) += mo + bias; returns LayerNorm(x) * gamma + beta as f32."""
+    place) += mo + bias; returns LayerNorm(x) * gamma + beta as f32 -- or, given an f16
+    `out`, rounded to f16 (madi_bias_res_ln_y16)."""
     rows, d = _ln_check(x, gamma, beta)
     if mo.dtype != torch.float32 or mo.shape != x.shape or not mo.is_contiguous():
         raise ValueError("mo must be a contiguous f32 tensor shaped like x")
     if bias.dtype != torch.float32 or bias.shape != (d,):
         raise ValueError("bias must be f32 [d]")
-    if out is None:
-        out = torch.empty((rows, d), dtype=torch.float32, device=x.device)
-    rc = _lib.load().madi_bias_res_ln(x.data_ptr(), mo.data_ptr(), bias.data_ptr(), out.data_ptr(), gamma.data_ptr(),
-                                      beta.data_ptr(), rows, d, float(eps), _stream(stream))
+    out = _ln_out(out, rows, d, x)
+    fn = _lib.load().madi_bias_res_ln_y16 if out.dtype == torch.float16 else _lib.load().madi_bias_res_ln
+    rc = fn(x.data_ptr(), mo.data_ptr(), bias.data_ptr(), out.data_ptr(), gamma.data_ptr(), beta.data_ptr(), rows, d,
+            float(eps), _stream(stream))
     _lib.check(rc, "madi_bias_res_ln")
     return out
 
 
 def layer_norm(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, eps: float = 1e-5,
                out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
-    """layer_norm (encoder_ops.metal:14-67): f32 LayerNorm(x) * gamma + beta."""
+    """layer_norm (encoder_ops.metal:14-67): f32 LayerNorm(x) * gamma + beta -- or,
+    given an f16 `out`, rounded to f16 (madi_layer_norm_y16)."""
     rows, d = _ln_check(x, gamma, beta)
-    if out is None:
-        out = torch.empty((rows, d), dtype=torch.float32, device=x.device)
-    rc = _lib.load().madi_layer_norm(x.data_ptr(), out.data_ptr(), gamma.data_ptr(), beta.data_ptr(), rows, d,
-                                     float(eps), _stream(stream))
+    out = _ln_out(out, rows, d, x)
+    fn = _lib.load().madi_layer_norm_y16 if out.dtype == torch.float16 else _lib.load().madi_layer_norm
+    rc = fn(x.data_ptr(), out.data_ptr(), gamma.data_ptr(), beta.data_ptr(), rows, d, float(eps), _stream(stream))
     _lib.check(rc, "madi_layer_norm")
     return out
