@@ -458,27 +458,39 @@ def main_madi(args, world, rank, local):
         gx = torch.Generator(device=dev)
         gx.manual_seed(55 + rank)
         xl = torch.randn((EB * enc_mod.SEQ, D), device=dev, generator=gx)
-        with torch.cuda.stream(stream):
-            for _ in range(2):
-                layer.forward_fused(xl, stream=stream)
-            torch.cuda.synchronize()
-            gl = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(gl, stream=stream, capture_error_mode="thread_local"):
-                layer.forward_fused(xl, stream=stream)
-            gl.replay()
-            torch.cuda.synchronize()
-            nl = 10
-            l0, l1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            l0.record(stream)
-            for _ in range(nl):
+        f_in = (torch.randn((EB * enc_mod.SEQ, D), device=dev, generator=gx) * 0.1).half()
+
+        def time_layer(body):
+            """One layer captured as a CUDA graph, 10 timed replays (same kernels every time)."""
+            with torch.cuda.stream(stream):
+                for _ in range(2):
+                    body()
+                torch.cuda.synchronize()
+                gl = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gl, stream=stream, capture_error_mode="thread_local"):
+                    body()
                 gl.replay()
-            l1.record(stream)
-            torch.cuda.synchronize()
-        ms_layer = max_over_ranks(world, l0.elapsed_time(l1) / nl)
+                torch.cuda.synchronize()
+                nl = 10
+                l0, l1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                l0.record(stream)
+                for _ in range(nl):
+                    gl.replay()
+                l1.record(stream)
+                torch.cuda.synchronize()
+            del gl
+            return max_over_ranks(world, l0.elapsed_time(l1) / nl)
+
+        # the encoder's default form: separate bias_res_ln_f16 kernels (the previous
+        # layer's fc2 output and bias join the first LayerNorm); and the fused form
+        # (residual adds in the out-projection / fc2 epilogues), bit-identical
+        ms_layer = time_layer(lambda: layer.forward(xl, f_in, layer.b2, stream=stream))
+        ms_fused = time_layer(lambda: layer.forward_fused(xl, stream=stream))
         fl = enc_mod.EncoderLayer.flops(EB)
         enc_layer = {"chunks_per_gpu": EB, "ms_per_layer": ms_layer, "TFLOPs": fl / (ms_layer / 1e3) / 1e12,
-                     "flops_per_layer": fl, "residual": "fused into the out-projection / fc2 epilogues"}
-        del gl, layer, xl
+                     "flops_per_layer": fl, "residual": "separate bias_res_ln_f16 kernels (the encoder's default)",
+                     "ms_per_layer_fused_residual": ms_fused}
+        del layer, xl, f_in
         torch.cuda.empty_cache()
         # the whole encoder (BASELINE config 3), measured: synthetic log-mel of EB chunks
         # resident in HBM -> conv stem, positions, 32 Q8 layers, ln_post; eager launches
