@@ -328,8 +328,11 @@ __global__ void __launch_bounds__(kThrS, 4) attn_stream_kernel(const __grid_cons
     pdl_trigger();
     pdl_wait();                 // q, pos and the cache row at pos come from earlier kernels
     const int len = pos ? (pos[b] < (uint32_t)rows ? (int)pos[b] + 1 : rows) : rows;
-    const int t0 = c * csz;
-    const int n = t0 < len ? min(csz, len - t0) : 0;
+    // Self-attention (pos given) splits the slot's actual keys 0..pos over the cluster,
+    // not the cache's rows: every CTA streams its share of a short cache, none idles.
+    const int cz = pos ? (len + ns - 1) / ns : csz;
+    const int t0 = c * cz;
+    const int n = t0 < len ? min(cz, len - t0) : 0;
     const int nsub = (n + kR - 1) / kR;
     if (ns > 1) asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
     if (tid == 0) {
