@@ -63,8 +63,9 @@ def parse():
                     help="decode activations (config 2: fp16; the reference decoder's own GEMVs take f32)")
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--e2e-chunks", type=int, default=4,
-                    help="e2e leg: row chunks per step pipelined across the copy and compute streams")
+    ap.add_argument("--e2e-chunks", type=int, default=2,
+                    help="e2e leg: row chunks per step pipelined across the copy and compute streams "
+                         "(2 measured best: 1 overlaps the two copy directions worse, 3-6 add GEMM tails)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-encoder-layer", action="store_true")
     ap.add_argument("--no-long-audio", action="store_true")
