@@ -494,8 +494,9 @@ def main_madi(args, world, rank, local):
         del layer, xl, f_in
         torch.cuda.empty_cache()
         # the whole encoder, measured: synthetic log-mel of EB chunks
-        # resident in HBM -> conv stem, positions, 32 Q8 layers, ln_post; eager launches
-        # as in the pipeline, best of 3 passes after one untimed pass
+        # resident in HBM -> conv stem, positions, 32 Q8 layers, ln_post; Encoder.forward
+        # as the pipeline calls it (one CUDA graph per batch shape, captured in the
+        # untimed pass), best of 3 passes after one untimed pass
         from madi_b200 import pipeline
         encoder = enc_mod.Encoder(32, seed=1, device=dev)
         mel = torch.from_numpy(pipeline.synthetic_mel(EB, first=1000 * rank)).to(dev)
@@ -515,8 +516,8 @@ def main_madi(args, world, rank, local):
                                           "chunks_per_s": EB * world / (ms_enc / 1e3),
                                           "layer_TFLOPs": encoder.flops(EB) / (ms_enc / 1e3) / 1e12,
                                           "note": "measured: conv stem (PyTorch f16 conv1d, one call per chunk), "
-                                                  "positions, 32 Q8 layers, ln_post; TFLOP/s over the layers' "
-                                                  "FLOPs"}
+                                                  "positions, 32 Q8 layers, ln_post, replayed as one CUDA graph "
+                                                  "(Encoder.forward); TFLOP/s over the layers' FLOPs"}
         del encoder, mel
         torch.cuda.empty_cache()
 

@@ -5,8 +5,8 @@ ln_post) -> cross K / V -> the 4-layer greedy decoder with EOT suppressed, exact
 reference batches independent chunks into decoder slots the same way,
 transcribe.zig:2314-2321).
 
-Per batch: one eager encoder pass (about 290 launches, tcgen05 GEMMs and flash
-attention), 8 cross K / V GEMMs, then `tokens` / 8 replays of one captured CUDA graph
+Per batch: one encoder pass (about 290 kernels -- tcgen05 GEMMs and flash attention --
+replayed as one CUDA graph per batch shape), 8 cross K / V GEMMs, then `tokens` / 8 replays of one captured CUDA graph
 of 8 token steps (one step per replay when 8 does not divide `tokens`).  Several
 batches decode at once, one decoder per stream.  Weights are random-init Q8 of the real shapes drawn on the
 device; the mel input is seeded Gaussian noise clipped to [-1.5, 1.5].
