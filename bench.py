@@ -515,7 +515,7 @@ def main_madi(args, world, rank, local):
         enc_layer["encoder_32_layers"] = {"chunks_per_gpu": EB, "ms_per_batch": ms_enc,
                                           "chunks_per_s": EB * world / (ms_enc / 1e3),
                                           "layer_TFLOPs": encoder.flops(EB) / (ms_enc / 1e3) / 1e12,
-                                          "note": "measured: conv stem (PyTorch f16 conv1d, one call per chunk), "
+                                          "note": "measured: conv stem (f16 im2col GEMMs, one chunk per call), "
                                                   "positions, 32 Q8 layers, ln_post, replayed as one CUDA graph "
                                                   "(Encoder.forward); TFLOP/s over the layers' FLOPs"}
         del encoder, mel
@@ -730,7 +730,7 @@ def long_audio_run(args, world, rank, dev, split):
             "overlap": (f"encoder on its own stream ahead of {ndec} decoder(s), each decoding every "
                         f"{ndec}-th batch on its own stream") if overlap else None,
             "decoder_ms_per_token_step": dec_avg / args.tokens,
-            "encoder": f"conv stem (PyTorch f16 conv1d) + 32 Q8 layers + ln_post, {slots} chunks per batch",
+            "encoder": f"conv stem (f16 im2col GEMMs) + 32 Q8 layers + ln_post, {slots} chunks per batch",
             "decoder": f"4 Q8 layers, {head}, one CUDA graph per token step, EOT suppressed",
             "h2d_bytes": int(mine * 128 * 3000 * 2), "d2h_bytes": int(mine * args.tokens * 4),
             "first_tokens_rank0": toks[0, :8].tolist() if mine else [],

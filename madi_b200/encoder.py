@@ -25,8 +25,9 @@ residual traffic costs the out-projection more than the separate LayerNorm does.
 
 Encoder puts the whole large-v3-turbo encoder together (config 3): the conv stem
 (conv1d 128 -> 1280, k 3, GELU; conv1d 1280 -> 1280, k 3, stride 2, GELU) on f16
-weights as the reference keeps them (transcribe.zig:1099-1102), through PyTorch's
-convolution -- it is not a Q8 op and is < 1 % of the encoder's FLOPs -- then the
+weights as the reference keeps them (transcribe.zig:1099-1102), as im2col + cuBLAS f16
+GEMMs (f32 accumulate), one chunk per call -- it is not a Q8 op and is < 1 % of the
+encoder's FLOPs -- then the
 sinusoidal positions, 32 layers as above and the final LayerNorm (ln_post), whose
 f16 output is what the decoder's cross K / V projections read.
 """
@@ -160,6 +161,9 @@ class Encoder:
         self.c1b = (torch.randn(D, device=device, generator=g) * 0.02).half()
         self.c2w = (torch.randn((D, D, 3), device=device, generator=g) / math.sqrt(3 * D)).half()
         self.c2b = (torch.randn(D, device=device, generator=g) * 0.02).half()
+        # the convolutions as GEMMs over (tap, channel): w1t [3 * 128][1280], w2t [3 * 1280][1280]
+        self.w1t = self.c1w.permute(2, 1, 0).reshape(3 * self.N_MELS, D).contiguous()
+        self.w2t = self.c2w.permute(2, 1, 0).reshape(3 * D, D).contiguous()
         self.pos = sinusoids(SEQ, D).to(device)
         self.layers = [EncoderLayer(device_layer(seed * 1000 + l, device), device) for l in range(layers)]
         self.ln_post = (1.0 + 0.1 * torch.randn(D, device=device, generator=g), 0.1 * torch.randn(D, device=device,
@@ -225,11 +229,21 @@ class Encoder:
         return q8.bias_res_ln_f16(x, f, b2, *self.ln_post, eps=EPS, stream=stream)
 
     def stem(self, mel: torch.Tensor) -> torch.Tensor:
-        """Conv stem and positions: mel f16 [b][128][frames] -> f32 [b][frames / 2][1280]."""
+        """Conv stem and positions: mel f16 [1][128][frames] -> f32 [1][frames / 2][1280].
+        conv1d(128 -> 1280, k 3, pad 1) and conv1d(1280 -> 1280, k 3, stride 2, pad 1),
+        each + bias and GELU, as GEMMs of the tap-stacked input rows (im2col) with the
+        tap-major weights: out[t] = sum_k in[s t + k - 1] W_k^T (f16 in, f32 accumulate,
+        bias in the GEMM epilogue, one rounding to f16), then the positions in f32."""
         import torch.nn.functional as Fn
-        h = Fn.gelu(Fn.conv1d(mel, self.c1w, self.c1b, padding=1))
-        h = Fn.gelu(Fn.conv1d(h, self.c2w, self.c2b, stride=2, padding=1))         # [b][1280][frames / 2]
-        return h.transpose(1, 2).float() + self.pos[:h.shape[2]]
+        T = mel.shape[2]
+        S = T // 2
+        xp = Fn.pad(mel[0].t(), (0, 0, 1, 1))                                     # [T + 2][128]
+        cols = torch.cat([xp[k:k + T] for k in range(3)], dim=1)                 # [T][384]
+        h = Fn.gelu(torch.addmm(self.c1b, cols, self.w1t))                       # [T][1280]
+        hp = Fn.pad(h, (0, 0, 1, 1))                                              # [T + 2][1280]
+        cols = torch.cat([hp[k:k + 2 * S:2] for k in range(3)], dim=1)           # [S][3840]
+        h = Fn.gelu(torch.addmm(self.c2b, cols, self.w2t))                       # [S][1280]
+        return (h.float() + self.pos[:S])[None]
 
     def flops(self, chunks: int) -> float:
         """Algorithmic FLOPs of the layers (the stem's 17.6 GFLOP per chunk not counted)."""

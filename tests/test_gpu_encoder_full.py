@@ -7,7 +7,7 @@ The chain follows the reference's encoder (encoder.zig:235-315, encoder_ops.meta
 305-364) with its f16 rounding points: LN1 -> f16; QKV GEMM + bias -> f16; attention
 -> f16; out-projection -> f16, added to the f32 residual with its bias; LN2 -> f16;
 fc1 + bias + GELU -> f16; fc2 -> f16, added with its bias; after 32 layers ln_post.
-The conv stem is PyTorch's convolution (not a Q8 op): the oracle starts from the
+The conv stem is f16 GEMMs through cuBLAS (not a Q8 op): the oracle starts from the
 GPU's stem output.  Rounding points in series let the GPU and the oracle land an f16
 ulp apart at any of them, and the residual stream carries that through 32 layers, so
 the bars are on the whole output: max |err| <= 5e-2 x RMS and RMS(err) <= 5e-3 x RMS
