@@ -53,7 +53,8 @@ constexpr int kMaxCs = 4;
 constexpr int kBoxBytes = kTileRows * 256;                  // one [16][2][128 B] weight box
 constexpr int kMaxM = 16;                                   // token rows: 1 or 2 groups of 8 (the MMA's n)
 constexpr size_t kRedBytes = 2 * kConsumers * 32 * 16;      // per token group: 2 units x 8 warps x 32 lanes x float4
-constexpr size_t kXredBytes = kMaxCs * 32 * 16;             // per token group: per-rank CTA sums, on rank 0
+constexpr size_t kXredBytes = kMaxCs * 32 * 16;             // per token group and unit: per-rank CTA sums, on rank 0
+constexpr int kSplitUnits = 2;                              // units per CTA of a K-split plan, at most
 constexpr size_t kSmemCap = 227 * 1024;                     // opt-in maximum per CTA
 constexpr size_t kSmemHalf = 112 * 1024;                    // two CTAs per SM (228 KB less reserves)
 
@@ -78,7 +79,8 @@ __host__ __device__ constexpr size_t stage_bytes(int KS) {
 __host__ __device__ constexpr size_t x_bytes(int M, int KS, bool x_f32) { return (size_t)M * KS * (x_f32 ? 4 : 2); }
 __host__ __device__ constexpr int groups(int M) { return (M + 7) / 8; }
 __host__ __device__ constexpr size_t fixed_bytes(int M, int KS, bool x_f32) {
-    return 1024 + x_bytes(M, KS, x_f32) + (size_t)groups(M) * (kRedBytes + kXredBytes) + sizeof(TileBars);
+    return 1024 + x_bytes(M, KS, x_f32) + (size_t)groups(M) * (kRedBytes + kSplitUnits * kXredBytes) +
+           sizeof(TileBars);
 }
 size_t plan_smem(int M, const TilePlan &pl, bool x_f32) {
     return fixed_bytes(M, pl.kslice, x_f32) + (size_t)pl.stages * stage_bytes(pl.kslice);
@@ -97,6 +99,18 @@ bool make_plan(int M, int N, int K, bool x_f32, int num_sms, TilePlan *pl, int *
         if (c.kslice / 32 > 256 || plan_smem(M, c, x_f32) > kSmemHalf) continue;
         *pl = c;
         *grid = tiles * cs;
+        return true;
+    }
+    // K split with two units per CTA (the second unit's weights load while the first
+    // is computed) when one unit per CTA needs more than a wave and the wider x slice
+    // of a one-unit split does not fit two CTAs per SM (16 token rows, K = 5120).
+    for (int cs = kMaxCs; cs >= 2; cs /= 2) {
+        const int clusters = (tiles + kSplitUnits - 1) / kSplitUnits;
+        if (K % (256 * cs) != 0 || (long)clusters * cs > 2L * num_sms) continue;
+        const TilePlan c{cs, K / cs, kSplitUnits, clusters};
+        if (c.kslice / 32 > 256 || plan_smem(M, c, x_f32) > kSmemHalf) continue;
+        *pl = c;
+        *grid = clusters * cs;
         return true;
     }
     for (int per_sm = 2; per_sm >= 1 && K / 32 <= 256; --per_sm) {   // one scale box per unit
@@ -282,7 +296,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     uint8_t *xs = smem + (size_t)stages * sb;
     float4 *red = reinterpret_cast<float4 *>(xs + x_bytes(M, KS, kSplit));
     float4 *xred = red + 2 * kConsumers * 32 * kG;
-    TileBars *bars = reinterpret_cast<TileBars *>(reinterpret_cast<uint8_t *>(xred) + kG * kXredBytes);
+    TileBars *bars = reinterpret_cast<TileBars *>(reinterpret_cast<uint8_t *>(xred) + kG * kSplitUnits * kXredBytes);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g8 = lane >> 2, t = lane & 3;
@@ -303,11 +317,14 @@ __global__ void __launch_bounds__(kThreads, 2)
     // of the cluster is running by then.
     if (cs > 1) asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
 
-    bool have = false;            // reducer lanes of a split unit: `mine` holds the CTA sums
+    // Reducer lanes of a split unit: `mine` holds the CTA sums of unit `mine_unit`.  A
+    // CTA's units are reduced by different warps (unit n by warp n), so a thread holds
+    // the sums of one unit at most.
+    bool have = false;
     float4 mine[kG];
 #pragma unroll
     for (int g = 0; g < kG; ++g) mine[g] = make_float4(0.f, 0.f, 0.f, 0.f);
-    int mine_tile = 0;
+    int mine_tile = 0, mine_unit = 0;
 
     if (warp == 0) {
         // ------------------------------------------------ producer: one stage = one unit
@@ -437,28 +454,31 @@ __global__ void __launch_bounds__(kThreads, 2)
             }
             if (cs > 1) {
                 mine_tile = tile;
+                mine_unit = n;
                 have = alive;
             }
         }
     }
 
     if (cs > 1) {
-        // One unit per cluster: ranks push their CTA sums into rank 0, which adds them
-        // in rank order.  Every thread of every CTA takes part in both barriers.
+        // At most kSplitUnits units per cluster: ranks push their CTA sums into rank 0
+        // (a slot per unit and rank), which adds them in rank order.  Every thread of
+        // every CTA takes part in both barriers.
         cg::cluster_group cluster = cg::this_cluster();
         asm volatile("barrier.cluster.wait;" ::: "memory");
         if (have) {
 #pragma unroll
-            for (int g = 0; g < kG; ++g) cluster.map_shared_rank(xred, 0)[(rank * kG + g) * 32 + lane] = mine[g];
+            for (int g = 0; g < kG; ++g)
+                cluster.map_shared_rank(xred, 0)[((mine_unit * cs + rank) * kG + g) * 32 + lane] = mine[g];
         }
         asm volatile("barrier.cluster.arrive.release;" ::: "memory");
         asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
         if (rank == 0 && have) {
 #pragma unroll
             for (int g = 0; g < kG; ++g) {
-                float4 v = xred[g * 32 + lane];
+                float4 v = xred[(mine_unit * cs * kG + g) * 32 + lane];
                 for (int r = 1; r < cs; ++r) {
-                    const float4 q = xred[(r * kG + g) * 32 + lane];
+                    const float4 q = xred[((mine_unit * cs + r) * kG + g) * 32 + lane];
                     v.x += q.x; v.y += q.y; v.z += q.z; v.w += q.w;
                 }
                 store_unit<YT, EPI, kQKV>(p, mine_tile, g8, t, 8 * g, v);

@@ -132,6 +132,9 @@ def test_decoder_shapes_two_token_groups(madi, oracle, M, name, N, K):
     (10, 300, 1024, 1, np.float32, np.float32),     # 4-CTA clusters split K
     (16, 1280, 5120, 3, np.float32, np.float32),    # fc2 shape, f32 x
     (11, 37, 2048, 2, np.float16, np.float32),
+    (15, 1280, 5120, 3, np.float16, np.float32),    # fc2, f16 activations: 4-CTA clusters, two units each
+    (12, 1270, 5120, 0, np.float16, np.float16),    # the same plan, last tile ragged
+    (16, 1264, 4096, 1, np.float16, np.float32),    # 79 tiles: the last cluster has one unit
 ])
 def test_two_token_group_plans(madi, oracle, M, N, K, epi, x_dt, y_dt):
     _case(madi, oracle, M, N, K, epi, x_dt=x_dt, y_dt=y_dt, seed=N + K + 3 * M)
