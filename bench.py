@@ -73,6 +73,9 @@ def parse():
     ap.add_argument("--tokens", type=int, default=224, help="long-audio leg: greedy tokens per chunk")
     ap.add_argument("--decoders", type=int, default=None,
                     help="long-audio leg: batches decoded at once, one decoder per stream (default 4)")
+    ap.add_argument("--exchange", choices=["nccl", "p2p", "auto"], default="auto",
+                    help="long-audio leg, split head: the all-gathers through NCCL, through the library's "
+                         "peer-memory exchange over NVLink (ranks on distinct GPUs), or p2p when possible")
     ap.add_argument("--no-overlap", action="store_true",
                     help="long-audio leg: run each batch's encoder and decoder back to back on one stream")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -695,7 +698,9 @@ def long_audio_run(args, world, rank, dev, split):
     nb = max(1, math.ceil(mine / 16))
     slots = max(1, math.ceil(mine / nb))
     tr = pipeline.Transcriber(slots=slots, enc_layers=32, tokens=args.tokens, seed=1, device=dev,
-                              split=(world, rank) if split else None, decoders=args.decoders)
+                              split=(world, rank) if split else None, decoders=args.decoders,
+                              exchange=args.exchange)
+    xname = tr.exchange
     mel_h = torch.from_numpy(pipeline.synthetic_mel(max(mine, 1), first=lo)).pin_memory()
     mel_d = torch.empty((slots,) + tuple(mel_h.shape[1:]), dtype=torch.float16, device=dev)
     tok_h = torch.empty((max(mine, 1), args.tokens), dtype=torch.int32, pin_memory=True)
@@ -724,8 +729,9 @@ def long_audio_run(args, world, rank, dev, split):
     barrier(world)
     del tr, mel_d
     torch.cuda.empty_cache()
-    head = ("column-split over the ranks (NCCL all-gathers of the hidden states and of per-row (max, index, "
-            "exp-sum) parts in every token step)" if split else "replicated head")
+    via = ("the library's peer-memory exchange over NVLink" if xname == "p2p" else "NCCL")
+    head = (f"column-split over the ranks (all-gathers of the hidden states and of per-row (max, index, "
+            f"exp-sum) parts in every token step, through {via})" if split else "replicated head")
     return {"chunks": args.chunks, "chunks_per_rank": per, "tokens_per_chunk": args.tokens, "slots": slots,
             "chunks_per_s": args.chunks / (ms_max / 1e3), "ms_total": ms_max, "scaling": "strong",
             "encoder_ms_per_batch": enc_avg, "decoder_ms_per_batch": dec_avg,

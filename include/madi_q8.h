@@ -402,6 +402,27 @@ int madi_merge_shard_tail(const float *parts, int world, int m, uint32_t *tokens
 /* step_advance (graph_helpers.metal:60-62) for m <= 32 slots: pos[s] += 1. */
 int madi_step_advance(uint32_t *pos, int m, void *stream);
 
+/* ======================= rank-to-rank all-gather over NVLink ================= */
+/* The column-split head's two exchanges per token step (hidden-state rows, per-row
+ * parts) without a collective library.  No reference counterpart: the reference
+ * runs one GPU; this replaces the all-gather the multi-GPU split head needs.
+ * Every rank creates one object (ranks on DISTINCT GPUs of one node), hands its
+ * 64-byte IPC handle to every peer (any host channel), and maps every peer's handle;
+ * then every rank calls madi_xchg_allgather in the same order.  Each call stores this
+ * rank's `bytes` of src into every rank's buffer over peer memory, raises a sequence
+ * flag there, waits (bounded: MADI_EDEVICE at the next madi_sync on expiry) for every
+ * peer's flag, and writes all ranks' rows, rank-major, to dst (world x bytes).  One
+ * kernel per call, capturable in a CUDA graph.  bytes: a multiple of 16, <= cap. */
+typedef struct madi_xchg madi_xchg;
+int madi_xchg_create(int world, int rank, size_t cap_bytes, madi_xchg **out);
+int madi_xchg_handle(const madi_xchg *x, void *handle64);
+int madi_xchg_open(madi_xchg *x, int peer, const void *handle64);
+int madi_xchg_allgather(madi_xchg *x, const void *src, size_t bytes, void *dst, void *stream);
+/* Teardown in two steps: every rank unmaps its peers' buffers, the ranks meet (host
+ * barrier), then every rank frees its own (destroy also unmaps what is still mapped). */
+int madi_xchg_unmap(madi_xchg *x);
+int madi_xchg_destroy(madi_xchg *x);
+
 #ifdef __cplusplus
 }
 #endif

@@ -62,6 +62,12 @@ SIGNATURES = {
     "madi_bias_res_ln": ([P, P, P, P, P, P, I, I, ctypes.c_float, P], I),
     "madi_layer_norm": ([P, P, P, P, I, I, ctypes.c_float, P], I),
     "madi_bias_res_ln_y16": ([P, P, P, P, P, P, I, I, ctypes.c_float, P], I),
+    "madi_xchg_create": ([I, I, SZ, ctypes.POINTER(P)], I),
+    "madi_xchg_handle": ([P, P], I),
+    "madi_xchg_open": ([P, I, P], I),
+    "madi_xchg_allgather": ([P, P, SZ, P, P], I),
+    "madi_xchg_unmap": ([P], I),
+    "madi_xchg_destroy": ([P], I),
     "madi_layer_norm_y16": ([P, P, P, P, I, I, ctypes.c_float, P], I),
     "madi_emb_lookup_q8": ([ctypes.POINTER(madi_q8w), P, P, I, ctypes.c_int64, I, P, P], I),
     "madi_emb_pos_q8": ([ctypes.POINTER(madi_q8w), P, P, I, ctypes.c_int64, I, P, I, P, P], I),

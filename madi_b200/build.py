@@ -17,7 +17,7 @@ ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 BUILD = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "libmadi_q8.so")
-SOURCES = ["runtime.cu", "q8_gemv.cu", "q8_gemv_tile.cu", "q8_gemm_tc.cu", "q8_misc.cu", "res_ln.cu", "decode_step.cu", "attn.cu", "flash_enc.cu"]
+SOURCES = ["runtime.cu", "q8_gemv.cu", "q8_gemv_tile.cu", "q8_gemm_tc.cu", "q8_misc.cu", "res_ln.cu", "decode_step.cu", "attn.cu", "flash_enc.cu", "xchg.cu"]
 HEADERS = ["common.cuh", "internal.h"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

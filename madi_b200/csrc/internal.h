@@ -101,6 +101,15 @@ constexpr int kGemmMinM = 9;
 // token rows per weight fragment.
 constexpr int kGemvMaxM = 16;
 
+// ---------------------------------------------------------------- rank-to-rank all-gather (xchg.cu)
+constexpr int kXchgMaxWorld = 8;
+// Bytes of one rank's exchange buffer: 256-byte header (flags, call counter), then
+// data[2][world][cap].
+size_t xchg_buffer_bytes(int world, size_t cap);
+// bases[r]: rank r's buffer as this rank maps it (bases[rank] its own).
+cudaError_t launch_xchg_allgather(uint8_t *const *bases, int world, int rank, size_t cap, const void *src,
+                                  size_t bytes, void *dst, int *dev_err, cudaStream_t st);
+
 // ---------------------------------------------------------------- residual + LayerNorm (res_ln.cu)
 constexpr int kLnMaxD = 2048;   // row width limit of the register-resident row kernel (D % 128 == 0)
 // MO == nullptr: layer_norm_f16; else bias_res_ln_f16 (X updated in place).

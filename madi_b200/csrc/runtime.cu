@@ -1105,4 +1105,97 @@ int madi_layer_norm_f16(const float *x, uint16_t *y, const float *gamma, const f
                        "madi_layer_norm_f16");
 }
 
+
+/* ---- rank-to-rank all-gather over NVLink (xchg.cu) ---- */
+struct madi_xchg {
+    int world = 0, rank = 0;
+    size_t cap = 0;
+    uint8_t *own = nullptr;
+    uint8_t *bases[kXchgMaxWorld] = {};
+    bool opened[kXchgMaxWorld] = {};
+};
+
+int madi_xchg_create(int world, int rank, size_t cap_bytes, madi_xchg **out) {
+    if (!S.ready) return fail(MADI_ENOINIT, "madi_xchg_create: not initialised");
+    if (!out) return fail(MADI_EINVAL, "madi_xchg_create: null out");
+    *out = nullptr;
+    if (world < 1 || world > kXchgMaxWorld || rank < 0 || rank >= world)
+        return fail(MADI_EINVAL, "madi_xchg_create: world %d, rank %d (1 <= world <= %d)", world, rank,
+                    kXchgMaxWorld);
+    if (cap_bytes == 0 || cap_bytes % 16 || cap_bytes > (64u << 20))
+        return fail(MADI_EINVAL, "madi_xchg_create: cap %zu (a multiple of 16, at most 64 MiB)", cap_bytes);
+    madi_xchg *x = new madi_xchg;
+    x->world = world;
+    x->rank = rank;
+    x->cap = cap_bytes;
+    const size_t n = xchg_buffer_bytes(world, cap_bytes);
+    cudaError_t e = cudaMalloc(&x->own, n);
+    if (e == cudaSuccess) e = cudaMemset(x->own, 0, n);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();          // zeroed before any peer maps it
+    if (e != cudaSuccess) {
+        if (x->own) cudaFree(x->own);
+        delete x;
+        return cuda_fail(e, "madi_xchg_create");
+    }
+    x->bases[rank] = x->own;
+    x->opened[rank] = true;
+    *out = x;
+    return MADI_OK;
+}
+
+int madi_xchg_handle(const madi_xchg *x, void *handle64) {
+    if (!x || !handle64) return fail(MADI_EINVAL, "madi_xchg_handle: null argument");
+    cudaIpcMemHandle_t h;
+    const cudaError_t e = cudaIpcGetMemHandle(&h, x->own);
+    if (e != cudaSuccess) return cuda_fail(e, "madi_xchg_handle");
+    memcpy(handle64, &h, sizeof(h));
+    return MADI_OK;
+}
+
+int madi_xchg_open(madi_xchg *x, int peer, const void *handle64) {
+    if (!x || !handle64) return fail(MADI_EINVAL, "madi_xchg_open: null argument");
+    if (peer < 0 || peer >= x->world || peer == x->rank || x->opened[peer])
+        return fail(MADI_EINVAL, "madi_xchg_open: peer %d (world %d, rank %d)", peer, x->world, x->rank);
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle64, sizeof(h));
+    void *p = nullptr;
+    const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return cuda_fail(e, "madi_xchg_open");
+    x->bases[peer] = static_cast<uint8_t *>(p);
+    x->opened[peer] = true;
+    return MADI_OK;
+}
+
+int madi_xchg_allgather(madi_xchg *x, const void *src, size_t bytes, void *dst, void *stream) {
+    if (!S.ready) return fail(MADI_ENOINIT, "madi_xchg_allgather: not initialised");
+    if (!x || !src || !dst) return fail(MADI_EINVAL, "madi_xchg_allgather: null argument");
+    for (int r = 0; r < x->world; ++r)
+        if (!x->opened[r]) return fail(MADI_EINVAL, "madi_xchg_allgather: rank %d's buffer is not mapped", r);
+    if (bytes == 0 || bytes % 16 || bytes > x->cap)
+        return fail(MADI_EINVAL, "madi_xchg_allgather: %zu bytes (a multiple of 16, at most %zu)", bytes, x->cap);
+    if (!aligned(src, 16) || !aligned(dst, 16)) return fail(MADI_EINVAL, "madi_xchg_allgather: misaligned buffer");
+    const cudaError_t e =
+        launch_xchg_allgather(x->bases, x->world, x->rank, x->cap, src, bytes, dst, S.dev_err, pick_stream(stream));
+    return e == cudaSuccess ? MADI_OK : cuda_fail(e, "madi_xchg_allgather");
+}
+
+int madi_xchg_unmap(madi_xchg *x) {
+    if (!x) return MADI_OK;
+    for (int r = 0; r < x->world; ++r)
+        if (r != x->rank && x->opened[r]) {
+            cudaIpcCloseMemHandle(x->bases[r]);
+            x->opened[r] = false;
+            x->bases[r] = nullptr;
+        }
+    return MADI_OK;
+}
+
+int madi_xchg_destroy(madi_xchg *x) {
+    if (!x) return MADI_OK;
+    madi_xchg_unmap(x);
+    if (x->own) cudaFree(x->own);
+    delete x;
+    return MADI_OK;
+}
+
 }  // extern "C"

@@ -41,10 +41,10 @@ def synthetic_mel(chunks: int, first: int = 0) -> np.ndarray:
 class Transcriber:
     def __init__(self, slots: int = 8, enc_layers: int = 32, tokens: int = 224, seed: int = 1, device="cuda",
                  split: Optional[Tuple[int, int]] = None, act16: Optional[bool] = None,
-                 decoders: Optional[int] = None):
+                 decoders: Optional[int] = None, exchange: str = "auto"):
         """split: (world, rank) -- the decoder's vocab head column-split over the
         ranks of the default process group (one process per GPU), its logits
-        exchanged by NCCL all-gathers inside the captured token step.  Every rank
+        exchanged by all-gathers inside the captured token step (see `exchange`).  Every rank
         must then decode the same number of batches (the collectives pair up step by
         step).  act16: the decoder projections on f16-rounded activations (default:
         when there is more than one slot or the head is split, as the reference's
@@ -54,7 +54,11 @@ class Transcriber:
         batches' steps overlap on the GPU (default 4).  With the split head each
         decoder exchanges over a process group of its own (a communicator per
         decoder), so the collectives of different decoders never interleave on one
-        communicator; every rank creates the groups in the same order."""
+        communicator; every rank creates the groups in the same order.
+        exchange: how the split head's all-gathers travel -- "nccl" (torch.distributed
+        all_gather_into_tensor), "p2p" (madi_b200.p2p.PeerExchange: one kernel storing
+        into the peers' memory over NVLink; ranks on distinct GPUs), or "auto" (the
+        default: p2p when the ranks sit on distinct GPUs, else nccl)."""
         if tokens < 1 or tokens + 1 > dec.MAX_TOK:
             raise ValueError(f"1..{dec.MAX_TOK - 1} tokens per chunk")
         self.encoder = enc.Encoder(enc_layers, seed, device)
@@ -67,11 +71,26 @@ class Transcriber:
         w = dec.device_weights(seed, device)
         exchanges = [None] * decoders
         self.groups = []
+        self.peers = []
+        self.exchange = None
         if split is not None and split[0] > 1:
             import torch.distributed as dist
-            self.groups = [dist.new_group() for _ in range(decoders)]
-            exchanges = [(lambda g: (lambda out, inp: dist.all_gather_into_tensor(out, inp, group=g)))(g)
-                         for g in self.groups]
+            from . import p2p
+            if exchange not in ("nccl", "p2p", "auto"):
+                raise ValueError(f"exchange {exchange!r}: nccl, p2p or auto")
+            dev = torch.device(device)
+            if exchange == "auto":
+                exchange = "p2p" if p2p.PeerExchange.usable(split[0], dev) else "nccl"
+            if exchange == "p2p":
+                # the larger of the two exchanges: a rank's hidden-state rows (f32 at most)
+                cap = slots * dec.D * 4
+                self.peers = [p2p.PeerExchange(split[0], split[1], cap, dev) for _ in range(decoders)]
+                exchanges = list(self.peers)
+            else:
+                self.groups = [dist.new_group() for _ in range(decoders)]
+                exchanges = [(lambda g: (lambda out, inp: dist.all_gather_into_tensor(out, inp, group=g)))(g)
+                             for g in self.groups]
+            self.exchange = exchange
         self.decoders = [dec.Decoder(w, slots, device, act16=act16, split=split, exchange=exchanges[i])
                          for i in range(decoders)]
         self.decoder = self.decoders[0]
@@ -195,6 +214,9 @@ class Transcriber:
         """Drops the captured token steps and the decoders' process groups (before the
         default process group or the context goes)."""
         self.graphs = [None] * len(self.decoders)
+        for p in self.peers:
+            p.close()
+        self.peers = []
         if self.groups:
             import torch.distributed as dist
             torch.cuda.synchronize()
