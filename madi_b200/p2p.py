@@ -69,6 +69,7 @@ class PeerExchange:
         """Collective: every rank unmaps its peers' buffers, the ranks meet, then each
         frees its own (no buffer is freed while a peer still maps it)."""
         import torch.distributed as dist
+        group = group if group is not None else self.group
         if self._x:
             torch.cuda.synchronize()
             _lib.load().madi_xchg_unmap(self._x)
