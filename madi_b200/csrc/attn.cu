@@ -609,10 +609,12 @@ cudaError_t launch_attn_t(const void *kc, const void *vc, float *out, const floa
                     dev_err);
 }
 
-// One wave: the largest ns (<= 8, >= 2 stages of rows per CTA) whose
+// One wave: the largest power-of-two ns (<= 8, >= 2 stages of rows per CTA) whose
 // slots x heads x ns CTAs all fit at once, with the ring sized to the shared
 // memory the resident CTAs leave (2..8 slots of 16 KB) and the fit checked against
-// the occupancy the kernel really gets at that size.
+// the occupancy the kernel really gets at that size; then another cluster size when
+// it balances the SMs better (below).  MADI_ATTN_NS=1..8 in the environment forces
+// the cluster size (for comparisons).
 template <typename KV, int G>
 cudaError_t launch_attn_stream_g(const void *kc, const void *vc, float *out, const float *q, const uint32_t *pos,
                                  int slots, int rows, int kvd, int nkv, int nh, int *dev_err, cudaStream_t st) {
@@ -640,20 +642,62 @@ cudaError_t launch_attn_stream_g(const void *kc, const void *vc, float *out, con
         return e0;
     const int sms = num_sms();
     const long pairs = (long)slots * (nh / G);
-    int ns = 1, stages = 2;
-    for (int cand = 8; cand >= 1; cand /= 2) {
-        if (cand > 1 && (rows + cand - 1) / cand < 2 * kR) continue;
-        const long per_sm = (pairs * cand + sms - 1) / sms;
-        if (per_sm > 16) continue;
+    static const int forced_ns = [] {
+        const char *e = getenv("MADI_ATTN_NS");
+        const int v = e ? atoi(e) : 0;
+        return v >= 1 && v <= 8 ? v : 0;
+    }();
+    auto ring_depth = [&](long per_sm) {
         const size_t budget = (size_t)(220 * 1024) / (size_t)per_sm;
         const size_t reserve = 12 * 1024;                // static shared memory and alignment
         int sg = budget > reserve ? (int)((budget - reserve) / stage_bytes) : 2;
         sg = sg < 2 ? 2 : (sg > kMaxStages ? kMaxStages : sg);
         while (sg > 2 && 128 + sg * stage_bytes > kSmemMax) --sg;
-        if (occ[sg] >= per_sm || cand == 1) {
-            ns = cand;
-            stages = sg;
-            break;
+        return sg;
+    };
+    // Work on the busiest SM: resident CTAs x kR-row stages per CTA.
+    auto busiest = [&](int cand, long per_sm) { return per_sm * (((rows + cand - 1) / cand + kR - 1) / kR); };
+    int ns = 1, stages = 2;
+    if (forced_ns) {
+        ns = forced_ns;
+        const long per_sm = (pairs * ns + sms - 1) / sms;
+        stages = ring_depth(per_sm > 16 ? 16 : per_sm);
+    } else {
+        long best = -1;
+        for (int cand = 8; cand >= 1; cand /= 2) {
+            if (cand > 1 && (rows + cand - 1) / cand < 2 * kR) continue;
+            const long per_sm = (pairs * cand + sms - 1) / sms;
+            if (per_sm > 16) continue;
+            const int sg = ring_depth(per_sm);
+            if (occ[sg] >= per_sm || cand == 1) {
+                ns = cand;
+                stages = sg;
+                best = busiest(cand, per_sm);
+                break;
+            }
+        }
+        // Cross-attention (every slot attends all `rows` keys): another cluster size (3,
+        // 5 or 6 CTAs too) that also fits one wave with a ring of at least 3 stages
+        // replaces it when it leaves less work on the busiest SM:
+        // 8 slots x 10 head pairs give 320 CTAs at ns = 4, so 24 SMs hold a third CTA
+        // and set the time; ns = 5 spreads 400 shorter CTAs.  Measured on a B200 (1500
+        // f16 keys, min over 40 calls): 8 slots 22.4 -> 20.4 us, 2 slots 14.2 us at
+        // ns = 6 (the same as 8), 15 slots unchanged at ns = 2.  Not taken: two-stage
+        // rings (15 slots at ns = 3, 450 CTAs: 32.8 us against 30.6) and clusters of 7,
+        // which pack into the GPCs worse than their per-SM occupancy says (2 and 4
+        // slots: 20.3-20.5 us against 14.2-16.2 at 6 or 8).
+        for (int cand = 8; cand >= 1 && best >= 0 && !pos; --cand) {
+            if (cand == 7 || (cand > 1 && (rows + cand - 1) / cand < 2 * kR)) continue;
+            const long per_sm = (pairs * cand + sms - 1) / sms;
+            if (per_sm > 16) continue;
+            const int sg = ring_depth(per_sm);
+            if (sg < 3 || occ[sg] < per_sm) continue;
+            const long c = busiest(cand, per_sm);
+            if (c < best) {
+                best = c;
+                ns = cand;
+                stages = sg;
+            }
         }
     }
     const int csz = (rows + ns - 1) / ns;

@@ -6,8 +6,9 @@ on one).
 1. Many all-gathers of different sizes and contents, eager and replayed from a CUDA
    graph, each equal byte for byte to NCCL's all_gather_into_tensor of the same data.
 2. The column-split head with the peer exchange inside the captured token step:
-   every rank's job-wide tokens equal those of one replicated decoder holding all
-   slots (as tests/test_gpu_split_nccl.py checks for the NCCL exchange)."""
+   every rank's job-wide tokens equal those of replicated decoders of the ranks'
+   own shape, one per rank's slots, concatenated in rank order (as
+   tests/test_gpu_split_nccl.py checks for the NCCL exchange)."""
 import datetime
 import os
 import socket
@@ -102,13 +103,18 @@ def _worker(rank, WORLD, port, q):
         del g
         xd.close()
         if rank == 0:
-            ref = dec.Decoder(w, R, act16=True)
-            ref.set_encoder(states)
-            ref.reset(50258)
-            for _ in range(STEPS):
-                ref.step(suppress=eot)
+            # replicated decoders of the ranks' own shape (the attention's launch plan
+            # depends on the slot count), one per rank's slice of the slots
+            want = []
+            for r2 in range(WORLD):
+                ref = dec.Decoder(w, SLOTS, act16=True)
+                ref.set_encoder(states[r2 * SLOTS:(r2 + 1) * SLOTS].contiguous())
+                ref.reset(50258)
+                for _ in range(STEPS):
+                    ref.step(suppress=eot)
+                want.append(ref.tokens[:, :STEPS + 1])
             torch.cuda.synchronize()
-            out["ref"] = ref.tokens[:, :STEPS + 1].cpu().numpy()
+            out["ref"] = torch.cat(want).cpu().numpy()
         from madi_b200 import backend
         backend.sync(10000)                              # raises if a bounded wait expired
         q.put((rank, out))

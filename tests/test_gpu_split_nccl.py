@@ -1,9 +1,10 @@
 """The column-split vocab head over NCCL, one process per GPU (needs 2 GPUs; skipped
 on a one-GPU box).  Each rank runs the decoder for its own 2 token slots with
 Decoder(split=(2, rank)) -- hidden-state and part all-gathers inside the token step --
-captured as one CUDA graph and replayed; rank 0 also runs one replicated decoder
-holding all 4 slots.  Every rank's job-wide tokens must equal the replicated
-decoder's, and its own slots' tokens their rows of it."""
+captured as one CUDA graph and replayed; rank 0 also runs replicated decoders of
+the same shape, one per rank's 2 slots.  Every rank's job-wide tokens must equal the
+replicated decoders' (concatenated in rank order), and its own slots' tokens their
+rows of it."""
 import datetime
 import os
 import socket
@@ -58,13 +59,18 @@ def _worker(rank, port, q):
                "pos_all": d.pos_all.cpu().numpy()}
         del g
         if rank == 0:
-            ref = dec.Decoder(w, R, act16=True)
-            ref.set_encoder(states)
-            ref.reset(50258)
-            for _ in range(STEPS):
-                ref.step(suppress=eot)
+            # replicated decoders of the ranks' own shape (the attention's launch plan
+            # depends on the slot count), one per rank's slice of the slots
+            want = []
+            for r2 in range(WORLD):
+                ref = dec.Decoder(w, SLOTS, act16=True)
+                ref.set_encoder(states[r2 * SLOTS:(r2 + 1) * SLOTS].contiguous())
+                ref.reset(50258)
+                for _ in range(STEPS):
+                    ref.step(suppress=eot)
+                want.append(ref.tokens[:, :STEPS + 1])
             torch.cuda.synchronize()
-            out["ref"] = ref.tokens[:, :STEPS + 1].cpu().numpy()
+            out["ref"] = torch.cat(want).cpu().numpy()
         q.put((rank, out))
     except Exception as e:                               # reported to the parent, not hung
         q.put((rank, repr(e)))
