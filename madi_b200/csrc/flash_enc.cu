@@ -20,9 +20,11 @@
 //              exponentials written as f16 pairs into the tile's P columns, O rescaled
 //              in TMEM by alpha when a row maximum moved; finally O / l.
 // Two softmax warpgroups keep the special-function unit and the tensor cores busy
-// while the other group waits for its MMAs; a tcgen05.mma of M = 128 costs the
-// tensor pipe ~115-125 cycles whatever N (64..256), so the 12 MMAs of a query x key
-// tile (S at N = 128, PV at N = 64) are the floor this layout is built around.
+// while the other group waits for its MMAs.  Back to back, an M = 128, K = 16
+// tcgen05.mma takes N / 2 cycles for N >= 128, but one issuing thread starts them no
+// faster than ~60 cycles apart, so the PV MMAs (N = 64) run at half the pipe's rate;
+// one issuer per query tile measured slower all the same (the tiles' chains fall
+// into step), so one thread issues for both tiles.
 // TMEM columns of tile x: S [256x, 256x + 128), P [256x + 128, +64), O [256x + 192,
 // +64).  P has its own columns, so S_x(j+1) can be computed while PV_x(j) still reads
 // P_x(j); the softmax waits for PV_x(j) before it overwrites P_x.  Every wait is
