@@ -82,6 +82,12 @@ MADI_DEV void mbar_wait_drain_fa(uint64_t *bar, uint32_t parity) {
         if (clock64() - t0 > kWaitBudgetCycles) return;
 }
 
+// max(a, b, c) in one instruction (exact, like fmaxf on finite values).
+MADI_DEV float max3f(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
 MADI_DEV void mma_ss(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
@@ -243,7 +249,8 @@ __global__ void __launch_bounds__(kFaThreads, 1)
                 const uint32_t (&cv)[32] = sv[c & 1];
                 if (full) {
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) mx[i & 7] = fmaxf(mx[i & 7], __uint_as_float(cv[i]));
+                    for (int i = 0; i < 32; i += 2)    // three-input max: two scores per instruction
+                        mx[(i >> 1) & 7] = max3f(mx[(i >> 1) & 7], __uint_as_float(cv[i]), __uint_as_float(cv[i + 1]));
                 } else {
 #pragma unroll
                     for (int i = 0; i < 32; ++i)
@@ -268,8 +275,9 @@ __global__ void __launch_bounds__(kFaThreads, 1)
                 if (!alive) break;
                 tc_fence_after();
             }
-            // row sum of the unrounded P over four partial sums (shorter dependency chains)
-            float bq[4] = {0.f, 0.f, 0.f, 0.f};
+            // row sum of the unrounded P over eight partial sums (even and odd keys of four
+            // interleaved groups: shorter dependency chains, packed adds)
+            float bq[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
             tmem_ld32(tb, sv[0]);
             tmem_wait_ld();
 #pragma unroll
@@ -280,11 +288,20 @@ __global__ void __launch_bounds__(kFaThreads, 1)
 #pragma unroll
                 for (int i = 0; i < 32; i += 2) {
                     const int key = 32 * c + i;
-                    const float e0 =
-                        (full || key < kcur) ? ex2_approx(fmaf(__uint_as_float(cv[i]), kScale * kLog2e, -ml)) : 0.f;
-                    const float e1 =
-                        (full || key + 1 < kcur) ? ex2_approx(fmaf(__uint_as_float(cv[i + 1]), kScale * kLog2e, -ml)) : 0.f;
-                    bq[(i >> 1) & 3] += e0 + e1;
+                    const int g = (i >> 1) & 3;
+                    float e0, e1;
+                    if (full) {
+                        // both exponents in one packed FMA (each lane rounded as fmaf)
+                        float a0, a1;
+                        fma2(a0, a1, __uint_as_float(cv[i]), __uint_as_float(cv[i + 1]), kScale * kLog2e,
+                             kScale * kLog2e, -ml, -ml);
+                        e0 = ex2_approx(a0);
+                        e1 = ex2_approx(a1);
+                    } else {
+                        e0 = key < kcur ? ex2_approx(fmaf(__uint_as_float(cv[i]), kScale * kLog2e, -ml)) : 0.f;
+                        e1 = key + 1 < kcur ? ex2_approx(fmaf(__uint_as_float(cv[i + 1]), kScale * kLog2e, -ml)) : 0.f;
+                    }
+                    add2(bq[2 * g], bq[2 * g + 1], bq[2 * g], bq[2 * g + 1], e0, e1);
                     pp[i >> 1] = h2_as_u32(__floats2half2_rn(e0, e1));
                 }
                 tmem_st16(tb + kPCol + 16 * c, pp);
@@ -298,7 +315,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
                     }
                 }
             }
-            const float bs = (bq[0] + bq[1]) + (bq[2] + bq[3]);
+            const float bs = ((bq[0] + bq[1]) + (bq[2] + bq[3])) + ((bq[4] + bq[5]) + (bq[6] + bq[7]));
             l = l * alpha + bs;
             const bool grew = mn != m;
             m = mn;
@@ -310,7 +327,12 @@ __global__ void __launch_bounds__(kFaThreads, 1)
                     tmem_ld32(tb + kOCol + 32 * c, ov);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
+                    for (int i = 0; i < 32; i += 2) {
+                        float o0, o1;
+                        mul2(o0, o1, __uint_as_float(ov[i]), __uint_as_float(ov[i + 1]), alpha, alpha);
+                        ov[i] = __float_as_uint(o0);
+                        ov[i + 1] = __float_as_uint(o1);
+                    }
                     tmem_st32(tb + kOCol + 32 * c, ov);
                 }
             }
