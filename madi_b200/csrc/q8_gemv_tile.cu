@@ -266,8 +266,19 @@ MADI_DEV void stage_x(const GemvArgs &p, uint8_t *xs, int kb0, int KS, int tid, 
             stage_x_quad<XT, 8, kR16>(p, xs, xrow, kq, true, a, false);
             stage_x_quad<XT, 8, kR16>(p, xs, xrow, kq + nthr, hb, b, false);
         }
+    } else if constexpr (sizeof(XT) == 2) {
+        // 16 rows of f16 x: two quads' loads (32 x 8 bytes) in flight before either is
+        // stored, as for 8 rows -- a K = 1280 slice then costs one L2 round trip
+        for (int kq = tid; kq < qrow; kq += 2 * nthr) {
+            V a[16], b[16];
+            const bool hb = kq + nthr < qrow;
+            stage_x_quad<XT, 16, kR16>(p, xs, xrow, kq, true, a, true);
+            stage_x_quad<XT, 16, kR16>(p, xs, xrow, kq + nthr, hb, b, true);
+            stage_x_quad<XT, 16, kR16>(p, xs, xrow, kq, true, a, false);
+            stage_x_quad<XT, 16, kR16>(p, xs, xrow, kq + nthr, hb, b, false);
+        }
     } else {
-        for (int kq = tid; kq < qrow; kq += nthr) {      // 16 rows: one quad's loads at a time
+        for (int kq = tid; kq < qrow; kq += nthr) {      // 16 rows of f32: one quad's loads at a time
             V a[16];
             stage_x_quad<XT, 16, kR16>(p, xs, xrow, kq, true, a, true);
             stage_x_quad<XT, 16, kR16>(p, xs, xrow, kq, true, a, false);
